@@ -1,0 +1,451 @@
+"""Benchmark of the hot path: the FP4 MoE layer decode step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one MoE layer decode for one token per GPU: router over 256
+bf16-valued logits -> top-8 of 256 HBM-resident FP4 experts (2048x4096 w1/w3,
+4096x2048 w2, 1x32 E8M0 scales) + the FP8 shared expert (128x128 E8M0) ->
+SwiGLU -> weighted k-order combine, hidden 4096. Every step routes a fresh
+token (seeded logits), and L2 is flushed (256 MiB write) before each timed step,
+so each step streams its ~132 MB of expert weights from HBM.
+
+value  = tokens/s over all ranks, device time (CUDA events, max over ranks).
+e2e    = the same through the public C ABI (dsv4cu_moe_decode) from pinned host
+         buffers: H2D of x + logits and D2H of the output inside the timed region.
+roofline: the dominant kernel (w1/w3 + SwiGLU) timed live with CUDA events on
+         its stream; algorithmic bytes = weight bytes of the 9 experts' w1/w3
+         plus activations in/out; peak = MEASURED_PEAKS.json hbm_gbs.
+cpu_baseline: the reference's own CPU kernels (oracle/_ref, dsv4_route +
+         9 x dsv4_expert_forward + the k-order combine) on the host's cores.
+--impl reference: times that reference CPU path as the reference arm.
+N > 1: every rank runs an independent replica of the layer on its own token
+         ("replicas"; the expert-parallel NCCL path is not used by this bench).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "deepseek-v4-in-c_b200")
+ORACLE = os.path.join(ROOT, "oracle")
+sys.path[:0] = [PKG]
+
+HIDDEN, INTER, N_EXPERTS, TOPK = 4096, 2048, 256, 8
+ROUTE_SCALE, LIMIT = 1.5, 10.0
+METRIC = "decode tok/s per GPU (FP4 MoE layer decode step, batch 1)"
+FP4_MAT = INTER * HIDDEN // 2 + INTER * HIDDEN // 32        # 4,456,448 B (W + S)
+FP8_MAT = INTER * HIDDEN + (INTER // 128) * (HIDDEN // 128)  # 8,389,120 B
+STEP_BYTES = TOPK * 3 * FP4_MAT + 3 * FP8_MAT + HIDDEN * 4 * 2 + N_EXPERTS * 4
+PHASE1_BYTES = TOPK * 2 * FP4_MAT + 2 * FP8_MAT + HIDDEN * 4 + (TOPK + 1) * INTER * 4
+WORKLOAD = ("config2: FP4 MoE decode step, 256 experts (w1/w3 2048x4096, w2 4096x2048, e2m1 + "
+            "1x32 E8M0), top-8 + 1 FP8 shared expert (128x128 E8M0), hidden 4096, batch 1 per GPU")
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--experts", type=int, default=256,
+                    help="routed experts resident in HBM (256 = config 2; smaller only for ncu captures)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic():
+    """dram bytes per launch of the dominant kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "moe_gate_up_config2.json")) as f:
+            return json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+        self.path = os.path.join("/tmp", f"dsv4cu_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self):
+        if not self.p:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        self.p.wait()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------- our arm
+def build_layer(dev, torch, n_experts=N_EXPERTS):
+    """n_experts FP4 routed experts + 1 FP8 shared expert, N(0, 0.02) quantized on device."""
+    import dsv4cu
+    keep = []
+    src = torch.empty(INTER * HIDDEN, dtype=torch.float32, device="cuda")
+
+    def mat(fmt, rows, cols, seed):
+        dev.fill_normal(src, seed, 0.0, 0.02)
+        if fmt == 3:
+            W = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
+            S = torch.empty(rows * cols // 32, dtype=torch.uint8, device="cuda")
+            dev.quantize_fp4(W, S, src, rows, cols)
+            q = dsv4cu.QMat(W.data_ptr(), S.data_ptr(), 3, rows, cols, 1, 32)
+        else:
+            W = torch.empty(rows * cols, dtype=torch.uint8, device="cuda")
+            S = torch.empty((rows // 128) * (cols // 128), dtype=torch.uint8, device="cuda")
+            dev.quantize_fp8(W, S, src, rows, cols)
+            q = dsv4cu.QMat(W.data_ptr(), S.data_ptr(), 2, rows, cols, 128, 128)
+        keep.extend([W, S])
+        return q
+
+    experts = []
+    for e in range(n_experts):
+        experts.append(dsv4cu.Expert(mat(3, INTER, HIDDEN, 10 * e + 1), mat(3, INTER, HIDDEN, 10 * e + 2),
+                                     mat(3, HIDDEN, INTER, 10 * e + 3)))
+    shared = dsv4cu.Expert(mat(2, INTER, HIDDEN, 7001), mat(2, INTER, HIDDEN, 7002), mat(2, HIDDEN, INTER, 7003))
+    arr = (dsv4cu.Expert * n_experts)(*experts)
+    experts_dev = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
+    torch.cuda.synchronize()
+    return experts_dev, shared, keep
+
+
+def step_inputs(n, seed):
+    """Per-step token: x ~ N(0,1) and router logits ~ N(0,1), both bf16-valued."""
+    sys.path.insert(0, PKG)
+    import pack
+    rng = np.random.default_rng(seed)
+    x = pack.bf16_round(rng.standard_normal((n, HIDDEN)).astype(np.float32))
+    lg = pack.bf16_round(rng.standard_normal((n, N_EXPERTS)).astype(np.float32))
+    return x, lg
+
+
+def run_ours(args, rank, local_rank, world):
+    import torch
+    import dsv4cu
+    torch.cuda.set_device(local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        pg = tdist
+    dev = dsv4cu.Device(local_rank)
+    NE = args.experts
+    experts_dev, shared, keep = build_layer(dev, torch, NE)
+    n_steps = args.warmup + args.steps
+    xs, lgs = step_inputs(n_steps, 1000 + rank)
+    lgs = np.ascontiguousarray(lgs[:, :NE])
+    dx = torch.from_numpy(xs).cuda()
+    dl = torch.from_numpy(lgs).cuda()
+    out = torch.empty((1, HIDDEN), dtype=torch.float32, device="cuda")
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")   # 256 MiB > L2
+    st = torch.cuda.current_stream()
+
+    def step(i, ev=None):
+        if ev is None:
+            dev.moe_decode(out, dx[i:i + 1], dl[i:i + 1], experts_dev, NE, shared, TOPK, ROUTE_SCALE,
+                           HIDDEN, INTER, LIMIT, 1)
+        else:
+            evp = (dsv4cu.C.c_void_p * 4)(*[e.cuda_event for e in ev])
+            dsv4cu.check(dev.L.dsv4cu_moe_decode_ev(dev.ctx, out.data_ptr(), dx[i:i + 1].data_ptr(),
+                                                   dl[i:i + 1].data_ptr(), None, None, None,
+                                                   experts_dev.data_ptr(), NE,
+                                                   dsv4cu.C.addressof(shared), TOPK, ROUTE_SCALE, HIDDEN,
+                                                   INTER, LIMIT, 1, None, None, st.cuda_stream, evp),
+                         "moe_decode_ev")
+
+    for i in range(args.warmup):
+        flush.zero_()
+        step(i)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if pg:
+            pg.barrier()
+
+    # ---- headline: device time per step, L2 flushed before each step
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = Clocks(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    wall0 = time.perf_counter()
+    for k in range(args.steps):
+        flush.zero_()
+        starts[k].record()
+        step(args.warmup + k)
+        ends[k].record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    barrier()
+    clk = clocks.stop()
+    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(ms)
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    total_ms = t.item()
+
+    # ---- roofline: the three kernels timed live on the launch stream
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for e in evs:                      # create the driver events before handing them out
+        for ev in e:
+            ev.record()
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        flush.zero_()
+        step(args.warmup + k, evs[k])
+    torch.cuda.synchronize()
+    ph = np.array([[e[i].elapsed_time(e[i + 1]) for i in range(3)] for e in evs])
+    ph_ms = ph.mean(axis=0)
+
+    # ---- e2e through the public API from pinned host buffers
+    hx = torch.from_numpy(xs).pin_memory()
+    hl = torch.from_numpy(lgs).pin_memory()
+    hout = torch.empty((args.steps, HIDDEN), dtype=torch.float32).pin_memory()
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    gx = torch.empty((1, HIDDEN), dtype=torch.float32, device="cuda")
+    gl = torch.empty((1, NE), dtype=torch.float32, device="cuda")
+    barrier()
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        i = args.warmup + k
+        flush.zero_()
+        e_s[k].record()
+        gx.copy_(hx[i:i + 1], non_blocking=True)
+        gl.copy_(hl[i:i + 1], non_blocking=True)
+        dev.moe_decode(out, gx, gl, experts_dev, NE, shared, TOPK, ROUTE_SCALE, HIDDEN, INTER,
+                       LIMIT, 1)
+        hout[k].copy_(out[0], non_blocking=True)
+        e_e[k].record()
+    torch.cuda.synchronize()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    e2e_ms = t.item()
+
+    peak, peak_kind = load_peaks()
+    achieved = PHASE1_BYTES / (ph_ms[1] * 1e-3) / 1e9
+    res = {
+        "metric": METRIC,
+        "value": round(world * args.steps / (total_ms * 1e-3), 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e2m1/e4m3 weights x f16 activation split -> f32 accumulate",
+        "data": "synthetic: weights N(0,0.02) quantized on device, x/logits N(0,1) bf16-valued, seeded",
+        "config": {"workload": WORKLOAD, "global_batch": world, "parallelism": f"replicas x{world}",
+                   "l2": "flushed before every timed step (256 MiB write, untimed)",
+                   "algorithmic_bytes_per_step": STEP_BYTES,
+                   "step_hbm_gbs": round(STEP_BYTES / (total_ms / args.steps * 1e-3) / 1e9, 1),
+                   "wall_s_timed_loop": round(wall, 4)},
+        "roofline": {"bound": "hbm", "kernel": "moe_gate_up_kernel (w1/w3 + SwiGLU of 9 experts)",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": load_traffic(),
+                     "algorithmic_bytes": PHASE1_BYTES,
+                     "kernel_ms": {"prologue": round(ph_ms[0], 5), "gate_up": round(ph_ms[1], 5),
+                                   "down_combine": round(ph_ms[2], 5)},
+                     "down_combine_gbs": round((STEP_BYTES - PHASE1_BYTES) / (ph_ms[2] * 1e-3) / 1e9, 1)},
+        "e2e": {"value": round(world * args.steps / (e2e_ms * 1e-3), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": (HIDDEN + NE) * 4, "d2h_bytes_per_step": HIDDEN * 4,
+                "api": "dsv4cu_moe_decode (include/dsv4cu.h)"},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clk,
+    }
+    if NE != N_EXPERTS:
+        res["config"]["workload"] += f" [REDUCED: {NE} routed experts resident; not a bench value]"
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    dev.close()
+    del keep
+    return res if rank == 0 else None
+
+
+# --------------------------------------------------- reference (CPU) path
+def reference_layer(pool=12, seed=5):
+    """Host copies of the layer in the reference pack layout. Routed expert e
+    uses pool entry e % pool (distinct byte buffers, same distribution)."""
+    sys.path.insert(0, ORACLE)
+    import oracle
+    import pack
+    rng = np.random.default_rng(seed)
+    base1 = (rng.standard_normal((INTER, HIDDEN), dtype=np.float32) * np.float32(0.02))
+    base2 = (rng.standard_normal((HIDDEN, INTER), dtype=np.float32) * np.float32(0.02))
+    W1, S1 = pack.quantize_fp4(base1)
+    W2, S2 = pack.quantize_fp4(base2)
+    keep, experts = [], []
+    for p in range(pool):
+        mats = []
+        for (W, S, rows, cols) in ((W1, S1, INTER, HIDDEN), (W1, S1, INTER, HIDDEN), (W2, S2, HIDDEN, INTER)):
+            flip = rng.integers(0, 256, W.shape, dtype=np.uint8) & np.uint8(0x88)   # random sign flips
+            Wp = np.ascontiguousarray(np.roll(W ^ flip, p * 7 + len(mats), axis=0))
+            Sp = np.ascontiguousarray(np.roll(S, p * 7 + len(mats), axis=0))
+            keep += [Wp, Sp]
+            mats.append(oracle.qmat(Wp, Sp, 3, rows, cols, 1, 32))
+        experts.append(mats)
+    sh = []
+    for rows, cols in ((INTER, HIDDEN), (INTER, HIDDEN), (HIDDEN, INTER)):
+        W, S = pack.quantize_fp8((rng.standard_normal((rows, cols), dtype=np.float32) * np.float32(0.02)))
+        keep += [W, S]
+        sh.append(oracle.qmat(W, S, 2, rows, cols, 128, 128))
+    return experts, sh, keep
+
+
+def reference_step(ref, experts, shared, x, logits):
+    """dsv4_layer_moe (src/70_decode/dsv4_layer.c:48-117) from the logits on,
+    through the reference's own dsv4_route and dsv4_expert_forward."""
+    idx, wts, _, _ = ref.route(logits, TOPK, ROUTE_SCALE)
+    out = np.zeros(HIDDEN, np.float32)
+    accs = [ref.expert_forward(x, experts[e % len(experts)], INTER, LIMIT) for e in idx]
+    sh = ref.expert_forward(x, shared, INTER, LIMIT)
+    for k in range(TOPK):
+        out += np.float32(wts[k]) * accs[k]
+    out += sh
+    return out
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(seconds):
+    """The reference CPU path on this host's cores for a bounded sample."""
+    sys.path.insert(0, ORACLE)
+    os.environ.setdefault("OMP_NUM_THREADS", str(cpu_threads()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import oracle
+    kind = "reference" if oracle.RefLib.available() else "port"
+    if kind == "reference":
+        ref = oracle.RefLib()
+    else:
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "port",
+                "sample": "oracle/_ref not built on this host; restatement not timed"}
+    experts, shared, keep = reference_layer()
+    xs, lgs = step_inputs(64, 77)
+    reference_step(ref, experts, shared, xs[0], lgs[0])   # warm-up
+    n, t0 = 0, time.perf_counter()
+    while n < 64 and (time.perf_counter() - t0 < seconds or n < 3):
+        reference_step(ref, experts, shared, xs[n], lgs[n])
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "tok/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "kind": kind, "sample": f"{n} decode steps of config 2 (router + 8 routed FP4 + FP8 shared "
+            f"experts + combine), {dt:.2f} s, OMP_PROC_BIND=close; routed experts drawn from a pool of 12 "
+            f"distinct host buffers"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    sys.path.insert(0, ORACLE)
+    os.environ.setdefault("OMP_NUM_THREADS", str(cpu_threads()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import oracle
+    if not oracle.RefLib.available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libdsv4ref.so was not built (reference tree "
+                "absent at build time)"}
+    ref = oracle.RefLib()
+    experts, shared, keep = reference_layer()
+    xs, lgs = step_inputs(args.warmup + args.steps, 2000)
+    for i in range(args.warmup):
+        reference_step(ref, experts, shared, xs[i], lgs[i])
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        reference_step(ref, experts, shared, xs[args.warmup + k], lgs[args.warmup + k])
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    sample = (f"{args.steps} decode steps of config 2 through the reference's dsv4_route + dsv4_expert_forward "
+              f"(src/10_compute, AVX2+OpenMP), {cores} threads; routed experts from a pool of 12 host buffers")
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e2m1/e4m3 weights x f32 (AVX2 FMA)", "data": "synthetic, seeded",
+            "config": {"workload": WORKLOAD, "global_batch": 1, "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": cores, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    rank, local_rank, world = dist_env()
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+    else:
+        res = run_ours(args, rank, local_rank, world)
+    if res is not None and rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

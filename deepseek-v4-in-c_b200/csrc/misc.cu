@@ -1,0 +1,218 @@
+// misc.cu - router, SwiGLU, index offset, weight quantizers, synthetic fill.
+#include <math.h>
+
+#include "common.cuh"
+#include "ctx.h"
+#include "router.cuh"
+
+namespace dsv4cu {
+
+__global__ void route_kernel(int *idx, float *wts, float *scores, float *orig, const float *logits,
+                             const float *bias, const int64_t *tid2eid, const int *token_ids, int n_experts,
+                             int topk, float route_scale, int nt)
+{
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= nt) return;
+    route_token_warp(logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0, n_experts,
+                     topk, route_scale, idx + (size_t)t * topk, wts + (size_t)t * topk,
+                     scores ? scores + (size_t)t * n_experts : nullptr,
+                     orig ? orig + (size_t)t * n_experts : nullptr);
+}
+
+// SwiGLU exactly as dsv4_swiglu (src/10_compute/dsv4_ops.c:61-79).
+__global__ void swiglu_kernel(float *y, const float *gate, const float *up, int n, float limit)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float u = up[i], g = gate[i];
+    if (limit > 0.0f) {
+        if (u > limit) u = limit;
+        if (u < -limit) u = -limit;
+        if (g > limit) g = limit;
+    }
+    y[i] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+__global__ void offset_kernel(int *idxs, int n, int offset)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n && idxs[i] >= 0) idxs[i] += offset;
+}
+
+// E8M0 exponent of the smallest power of two s with amax / s <= qmax, where
+// qmax = qf * 2^qe (448 = 0.875 * 2^9, 6 = 0.75 * 2^3). With amax = f 2^E,
+// f in [0.5, 1): e = E - qe + (f > qf). Exact; no division is rounded.
+__device__ __forceinline__ int e8m0_exponent(float amax, float qf, int qe)
+{
+    if (!(amax > 0.0f) || !isfinite(amax)) return 0;
+    int E;
+    const float f = frexpf(amax, &E);
+    int e = E - qe + (f > qf ? 1 : 0);
+    return max(-127, min(127, e));
+}
+
+// FP8: one CTA per 128x128 block.
+__global__ void __launch_bounds__(256) quant_fp8_kernel(uint8_t *w, uint8_t *s, const float *src, int rows,
+                                                        int cols)
+{
+    const int br = blockIdx.y, bc = blockIdx.x, s_cols = (cols + 127) / 128;
+    const int r0 = br * 128, c0 = bc * 128;
+    __shared__ float red[8];
+    float a = 0.0f;
+    for (int i = threadIdx.x; i < 128 * 128; i += 256) {
+        const int r = r0 + (i >> 7), c = c0 + (i & 127);
+        if (r < rows && c < cols) {
+            const float v = fabsf(src[(size_t)r * cols + c]);
+            if (isfinite(v)) a = fmaxf(a, v);
+        }
+    }
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 16));
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 8));
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 4));
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 2));
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 1));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+    __syncthreads();
+    float amax = 0.0f;
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, red[i]);
+    const int e = e8m0_exponent(amax, 0.875f, 9);
+    if (threadIdx.x == 0) s[(size_t)br * s_cols + bc] = (uint8_t)(127 + e);
+    for (int i = threadIdx.x; i < 128 * 64; i += 256) {
+        const int r = r0 + (i >> 6), c = c0 + 2 * (i & 63);
+        if (r >= rows || c >= cols) continue;
+        const float v0 = ldexpf(src[(size_t)r * cols + c], -e);
+        const float v1 = (c + 1 < cols) ? ldexpf(src[(size_t)r * cols + c + 1], -e) : 0.0f;
+        uint16_t two;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(two) : "f"(v1), "f"(v0));
+        w[(size_t)r * cols + c] = (uint8_t)(two & 0xFF);
+        if (c + 1 < cols) w[(size_t)r * cols + c + 1] = (uint8_t)(two >> 8);
+    }
+}
+
+// FP4: one warp per 1x32 block; lane = element.
+__global__ void quant_fp4_kernel(uint8_t *w, uint8_t *s, const float *src, int rows, int cols)
+{
+    const long gw = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31, nb = cols / 32;
+    if (gw >= (long)rows * nb) return;
+    const int r = (int)(gw / nb), b = (int)(gw - (long)r * nb), c = b * 32 + lane;
+    const float v = src[(size_t)r * cols + c];
+    float a = isfinite(v) ? fabsf(v) : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+    const int e = e8m0_exponent(a, 0.75f, 3);
+    if (lane == 0) s[(size_t)r * nb + b] = (uint8_t)(127 + e);
+    const float vs = ldexpf(v, -e);
+    const float other = __shfl_down_sync(0xFFFFFFFFu, vs, 1);
+    if ((lane & 1) == 0) {
+        uint16_t packed;
+        // first operand -> high nibble: the odd element; second -> low nibble.
+        asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}"
+            : "=h"(packed) : "f"(other), "f"(vs));
+        w[(size_t)r * (cols / 2) + (c >> 1)] = (uint8_t)packed;
+    }
+}
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Box-Muller on two 24-bit uniforms drawn from (seed, pair index).
+__global__ void fill_normal_kernel(float *dst, size_t n, uint64_t seed, float mean, float stdv)
+{
+    const size_t pair = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (2 * pair >= n) return;
+    const uint64_t h = splitmix64(seed * 0x9E3779B97F4A7C15ull ^ splitmix64(pair));
+    const float u1 = ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = ((float)(uint32_t)((h >> 16) & 0xFFFFFFu) + 0.5f) * (1.0f / 16777216.0f);
+    const float r = sqrtf(-2.0f * logf(u1));
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    dst[2 * pair] = mean + stdv * r * cs;
+    if (2 * pair + 1 < n) dst[2 * pair + 1] = mean + stdv * r * sn;
+}
+
+__global__ void round_bf16_kernel(float *x, size_t n)
+{
+    const size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    if (i < n) x[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
+}
+
+}  // namespace dsv4cu
+
+using namespace dsv4cu;
+
+extern "C" int dsv4cu_route(int *idx, float *wts, float *scores, float *orig, const float *logits,
+                            const float *bias, const int64_t *tid2eid, const int *token_ids, int n_experts,
+                            int topk, float route_scale, int nt, void *stream)
+{
+    if (!idx || !wts || !logits) return dsv4cu_set_error(DSV4CU_ERR_ARG, "route: NULL argument");
+    if (topk < 1 || topk > 16 || n_experts < 1 || n_experts > 32 * RMAX_PER_LANE)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "route: topk %d / n_experts %d out of range", topk, n_experts);
+    if (!tid2eid && topk > n_experts) return dsv4cu_set_error(DSV4CU_ERR_ARG, "route: topk > n_experts");
+    if (tid2eid && !token_ids) return dsv4cu_set_error(DSV4CU_ERR_ARG, "route: hash routing needs token_ids");
+    if (nt <= 0) return DSV4CU_OK;
+    route_kernel<<<(nt + 3) / 4, 128, 0, (cudaStream_t)stream>>>(idx, wts, scores, orig, logits, bias, tid2eid,
+                                                                  token_ids, n_experts, topk, route_scale, nt);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_swiglu(float *y, const float *gate, const float *up, int n, float limit, void *stream)
+{
+    if (n <= 0) return DSV4CU_OK;
+    if (!y || !gate || !up) return dsv4cu_set_error(DSV4CU_ERR_ARG, "swiglu: NULL argument");
+    swiglu_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(y, gate, up, n, limit);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_indexer_offset(int *idxs, int n, int offset, void *stream)
+{
+    if (n <= 0) return DSV4CU_OK;
+    offset_kernel<<<(n + 255) / 256, 256, 0, (cudaStream_t)stream>>>(idxs, n, offset);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_quantize_fp8(uint8_t *w, uint8_t *s, const float *src, int rows, int cols, void *stream)
+{
+    if (!w || !s || !src || rows <= 0 || cols <= 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "quantize_fp8: bad args");
+    dim3 grid((cols + 127) / 128, (rows + 127) / 128);
+    quant_fp8_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(w, s, src, rows, cols);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_quantize_fp4(uint8_t *w, uint8_t *s, const float *src, int rows, int cols, void *stream)
+{
+    if (!w || !s || !src || rows <= 0 || cols <= 0 || cols % 32)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "quantize_fp4: bad args (cols must be a multiple of 32)");
+    const long warps = (long)rows * (cols / 32);
+    quant_fp4_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, (cudaStream_t)stream>>>(w, s, src, rows, cols);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_fill_normal(float *dst, size_t n, uint64_t seed, float mean, float stdv, void *stream)
+{
+    if (!dst) return dsv4cu_set_error(DSV4CU_ERR_ARG, "fill_normal: NULL");
+    if (!n) return DSV4CU_OK;
+    const size_t pairs = (n + 1) / 2;
+    fill_normal_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, (cudaStream_t)stream>>>(dst, n, seed, mean, stdv);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_round_bf16(float *x, size_t n, void *stream)
+{
+    if (!x) return dsv4cu_set_error(DSV4CU_ERR_ARG, "round_bf16: NULL");
+    if (!n) return DSV4CU_OK;
+    round_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, n);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}

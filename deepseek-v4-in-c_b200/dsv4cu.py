@@ -1,0 +1,311 @@
+"""Python binding of libdsv4cu.so (the B200 hot-path library) via ctypes.
+
+Two surfaces, mirroring the C ABI:
+
+* ``HostAPI``: the reference engine's own operator entry points (``dsv4_mmq_n``,
+  ``fp8_n``, ``dsv4_route``, ``dsv4_topk`` ...) over host numpy arrays, exactly as
+  the reference's C host code calls them (include/dsv4_compat.h).
+* ``Device``: the native ``dsv4cu_*`` entry points over device memory (torch
+  CUDA tensors are used only as device allocations) on a CUDA stream
+  (include/dsv4cu.h).
+
+There is no fallback: if the shared library is missing or fails to load, every
+entry point raises. Build it with ``make -C deepseek-v4-in-c_b200``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdsv4cu.so")
+
+WF32, WBF16, WFP8, WFP4 = 0, 1, 2, 3
+
+
+class DSV4CUError(RuntimeError):
+    pass
+
+
+class QMat(C.Structure):
+    """DSV4QMat / dsv4cu_qmat (src/00_base/dsv4_weights.h:34-40)."""
+    _fields_ = [("w", C.c_void_p), ("s", C.c_void_p), ("wdt", C.c_int),
+                ("rows", C.c_int), ("cols", C.c_int),
+                ("blk_r", C.c_int), ("blk_c", C.c_int)]
+
+
+class Expert(C.Structure):
+    """DSV4ExpertW / dsv4cu_expert: {w1, w3, w2} (src/00_base/dsv4_weights.h:101-104)."""
+    _fields_ = [("w1", QMat), ("w3", QMat), ("w2", QMat)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load libdsv4cu.so once; raise if it is absent (no fallback path exists)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise DSV4CUError(f"{LIB_PATH} is missing; build with make -C {HERE}")
+        L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
+        vp, i, f, sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
+        sig = {
+            "dsv4cu_last_error": (C.c_char_p, []),
+            "dsv4cu_ctx_create": (i, [C.POINTER(vp), i]),
+            "dsv4cu_ctx_destroy": (None, [vp]),
+            "dsv4cu_ctx_reserve": (i, [vp, sz]),
+            "dsv4cu_ctx_workspace_bytes": (sz, [vp]),
+            "dsv4cu_mmq_workspace": (sz, [vp, i]),
+            "dsv4cu_mmq": (i, [vp, vp, vp, vp, i, vp]),
+            "dsv4cu_route": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, i, f, i, vp]),
+            "dsv4cu_swiglu": (i, [vp, vp, vp, i, f, vp]),
+            "dsv4cu_moe_decode": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, vp, i, f, i, i, f, i,
+                                      vp, vp, vp]),
+            "dsv4cu_moe_decode_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, vp, i, f, i, i, f, i,
+                                         vp, vp, vp, vp]),
+            "dsv4cu_indexer_score": (i, [vp, vp, vp, vp, i, i, i, vp]),
+            "dsv4cu_indexer_score_fp8": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]),
+            "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
+            "dsv4cu_sparse_attn": (i, [vp, vp, vp, vp, i, vp, vp, i, i, i, f, vp]),
+            "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
+            "dsv4cu_quantize_fp8": (i, [vp, vp, vp, i, i, vp]),
+            "dsv4cu_quantize_fp4": (i, [vp, vp, vp, i, i, vp]),
+            "dsv4cu_fill_normal": (i, [vp, sz, C.c_uint64, f, f, vp]),
+            "dsv4cu_round_bf16": (i, [vp, sz, vp]),
+            # host-pointer reference ABI
+            "dsv4_mmq_n": (None, [vp, vp, vp, i]),
+            "dsv4_mmq": (None, [vp, vp, vp]),
+            "bf16_n": (None, [vp, vp, vp, i, i, i]),
+            "fp8_n": (None, [vp, vp, vp, vp, i, i, i, i, i]),
+            "fp4_n": (None, [vp, vp, vp, vp, i, i, i, i, i]),
+            "dsv4_swiglu": (None, [vp, vp, vp, i, f]),
+            "dsv4_route": (None, [vp, vp, vp, vp, vp, vp, i, i, i, f]),
+            "dsv4_expert_forward": (None, [vp, vp, vp, vp, vp, vp, i, f]),
+            "dsv4_sparse_attn": (None, [vp, vp, vp, vp, vp, i, i, i, f, vp]),
+            "dsv4_window_idxs": (i, [vp, i, i]),
+            "dsv4_indexer_score": (None, [vp, vp, vp, vp, i, i, i]),
+            "dsv4_topk": (i, [vp, vp, i, i]),
+            "dsv4_indexer_offset": (None, [vp, i, i]),
+            "dsv4_prefill_vk_init": (i, [C.POINTER(vp), vp, vp, vp]),
+            "dsv4_prefill_vk_free": (None, [vp]),
+            "dsv4_prefill_vk_gemm": (i, [vp, vp, vp, vp, i]),
+            "dsv4_prefill_vk_expert_fused": (i, [vp, vp, vp, vp, vp, vp, i, i, f, vp, vp]),
+            "dsv4cu_host_forget": (None, [vp]),
+            "dsv4cu_host_forget_all": (None, []),
+            "dsv4cu_host_registry_count": (sz, []),
+            "dsv4cu_host_registry_bytes": (sz, []),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().dsv4cu_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str = "dsv4cu") -> None:
+    if rc != 0:
+        raise DSV4CUError(f"{what}: status {rc}: {last_error()}")
+
+
+def _p(a):
+    """Host pointer of a numpy array (or None)."""
+    return None if a is None else a.ctypes.data
+
+
+# ------------------------------------------------------------------ host ABI
+class HostAPI:
+    """The reference's operator entry points over host arrays."""
+
+    def __init__(self):
+        self.L = lib()
+
+    def mmq(self, x: np.ndarray, m: QMat) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.shape[0] if x.ndim == 2 else 1
+        y = np.zeros((nt, m.rows), np.float32)
+        self.L.dsv4_mmq_n(_p(y), _p(x), C.byref(m), nt)
+        return y
+
+    def fp8_n(self, x, W, S, rows, cols, blk_r, blk_c):
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.shape[0] if x.ndim == 2 else 1
+        y = np.zeros((nt, rows), np.float32)
+        self.L.fp8_n(_p(y), _p(x), _p(W), _p(S), cols, rows, blk_r, blk_c, nt)
+        return y
+
+    def fp4_n(self, x, W, S, rows, cols, blk_r, blk_c):
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.shape[0] if x.ndim == 2 else 1
+        y = np.zeros((nt, rows), np.float32)
+        self.L.fp4_n(_p(y), _p(x), _p(W), _p(S), cols, rows, blk_r, blk_c, nt)
+        return y
+
+    def bf16_n(self, x, W, rows, cols):
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.shape[0] if x.ndim == 2 else 1
+        y = np.zeros((nt, rows), np.float32)
+        self.L.bf16_n(_p(y), _p(x), _p(W), cols, rows, nt)
+        return y
+
+    def route(self, logits, topk, route_scale, bias=None, tid2eid=None, token_id=0):
+        ne = logits.shape[0]
+        scores = np.ascontiguousarray(logits, np.float32).copy()
+        orig = np.zeros(ne, np.float32)
+        idx = np.zeros(topk, np.int32)
+        wts = np.zeros(topk, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        t = None if tid2eid is None else np.ascontiguousarray(tid2eid, np.int64)
+        self.L.dsv4_route(_p(idx), _p(wts), _p(scores), _p(orig), _p(b), _p(t), token_id, ne,
+                          topk, route_scale)
+        return idx, wts, scores, orig
+
+    def swiglu(self, gate, up, limit):
+        g = np.ascontiguousarray(gate, np.float32)
+        u = np.ascontiguousarray(up, np.float32)
+        y = np.zeros_like(g)
+        self.L.dsv4_swiglu(_p(y), _p(g), _p(u), g.size, limit)
+        return y
+
+    def expert_forward(self, x, w3: list, inter, limit):
+        e = Expert(*w3)
+        out = np.zeros(w3[2].rows, np.float32)
+        scr = np.zeros(3 * inter, np.float32)
+        self.L.dsv4_expert_forward(_p(out), _p(np.ascontiguousarray(x, np.float32)), C.addressof(e),
+                                   _p(scr), _p(scr[inter:]), _p(scr[2 * inter:]), inter, limit)
+        return out, scr[:inter].copy(), scr[inter:2 * inter].copy(), scr[2 * inter:].copy()
+
+    def indexer_score(self, q, kv, weights):
+        h, d = q.shape
+        n = kv.shape[0]
+        out = np.zeros(n, np.float32)
+        self.L.dsv4_indexer_score(_p(out), _p(np.ascontiguousarray(q, np.float32)),
+                                  _p(np.ascontiguousarray(kv, np.float32)),
+                                  _p(np.ascontiguousarray(weights, np.float32)), h, d, n)
+        return out
+
+    def topk(self, scores, k):
+        s = np.ascontiguousarray(scores, np.float32)
+        out = np.full(max(1, min(k, s.size)), -7, np.int32)
+        r = self.L.dsv4_topk(_p(out), _p(s), s.size, k)
+        return out[:max(r, 0)], r
+
+    def indexer_offset(self, idxs, offset):
+        a = np.ascontiguousarray(idxs, np.int32).copy()
+        self.L.dsv4_indexer_offset(_p(a), a.size, offset)
+        return a
+
+    def window_idxs(self, pos, win):
+        out = np.zeros(max(win, 1), np.int32)
+        n = self.L.dsv4_window_idxs(_p(out), pos, win)
+        return out[:win], n
+
+    def sparse_attn(self, q, kv, sink, idxs, scale):
+        h, d = q.shape
+        o = np.zeros((h, d), np.float32)
+        scr = np.zeros(h * max(1, len(idxs)), np.float32)
+        self.L.dsv4_sparse_attn(_p(o), _p(np.ascontiguousarray(q, np.float32)),
+                                _p(np.ascontiguousarray(kv, np.float32)),
+                                _p(np.ascontiguousarray(sink, np.float32)),
+                                _p(np.ascontiguousarray(idxs, np.int32)), h, d, len(idxs), scale,
+                                _p(scr))
+        return o
+
+    def forget_all(self):
+        self.L.dsv4cu_host_forget_all()
+
+
+# ---------------------------------------------------------------- device ABI
+class Device:
+    """The native dsv4cu_* entry points on one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        import torch
+        self.torch = torch
+        self.L = lib()
+        self.device = device
+        h = C.c_void_p()
+        torch.cuda.set_device(device)
+        check(self.L.dsv4cu_ctx_create(C.byref(h), device), "ctx_create")
+        self.ctx = h
+
+    def close(self):
+        if self.ctx:
+            self.L.dsv4cu_ctx_destroy(self.ctx)
+            self.ctx = None
+
+    def stream(self):
+        return self.torch.cuda.current_stream(self.device).cuda_stream
+
+    @staticmethod
+    def ptr(t):
+        return None if t is None else t.data_ptr()
+
+    def qmat(self, w, s, wdt, rows, cols, blk_r=0, blk_c=0) -> QMat:
+        return QMat(self.ptr(w), self.ptr(s), wdt, rows, cols, blk_r, blk_c)
+
+    def mmq(self, y, x, m: QMat, nt: int):
+        check(self.L.dsv4cu_mmq(self.ctx, self.ptr(y), self.ptr(x), C.byref(m), nt, self.stream()),
+              "dsv4cu_mmq")
+
+    def route(self, idx, wts, scores, orig, logits, topk, route_scale, nt, bias=None,
+              tid2eid=None, token_ids=None):
+        ne = logits.shape[-1]
+        check(self.L.dsv4cu_route(self.ptr(idx), self.ptr(wts), self.ptr(scores), self.ptr(orig),
+                                  self.ptr(logits), self.ptr(bias), self.ptr(tid2eid),
+                                  self.ptr(token_ids), ne, topk, route_scale, nt, self.stream()),
+              "dsv4cu_route")
+
+    def moe_decode(self, out, x, logits, experts_dev, n_experts, shared: Expert | None, topk,
+                   route_scale, hidden, inter, limit, nt, idx_out=None, wts_out=None, bias=None,
+                   tid2eid=None, token_ids=None, stream=None):
+        check(self.L.dsv4cu_moe_decode(self.ctx, self.ptr(out), self.ptr(x), self.ptr(logits),
+                                       self.ptr(bias), self.ptr(tid2eid), self.ptr(token_ids),
+                                       self.ptr(experts_dev), n_experts,
+                                       None if shared is None else C.addressof(shared), topk,
+                                       route_scale, hidden, inter, limit, nt, self.ptr(idx_out),
+                                       self.ptr(wts_out),
+                                       self.stream() if stream is None else stream),
+              "dsv4cu_moe_decode")
+
+    def indexer_score(self, out, q, kv, w, n_heads, head_dim, n_pos):
+        check(self.L.dsv4cu_indexer_score(self.ptr(out), self.ptr(q), self.ptr(kv), self.ptr(w),
+                                          n_heads, head_dim, n_pos, self.stream()),
+              "dsv4cu_indexer_score")
+
+    def indexer_score_fp8(self, out, q8, qs, k8, ks, w, n_heads, head_dim, n_pos, k_stride):
+        check(self.L.dsv4cu_indexer_score_fp8(self.ptr(out), self.ptr(q8), self.ptr(qs),
+                                              self.ptr(k8), self.ptr(ks), self.ptr(w), n_heads,
+                                              head_dim, n_pos, k_stride, self.stream()),
+              "dsv4cu_indexer_score_fp8")
+
+    def topk(self, idx, scores, n, k):
+        check(self.L.dsv4cu_topk(self.ctx, self.ptr(idx), self.ptr(scores), n, k, self.stream()),
+              "dsv4cu_topk")
+
+    def sparse_attn(self, o, q, kv, kv_bf16, sink, idxs, h, d, topk, scale):
+        check(self.L.dsv4cu_sparse_attn(self.ctx, self.ptr(o), self.ptr(q), self.ptr(kv), kv_bf16,
+                                        self.ptr(sink), self.ptr(idxs), h, d, topk, scale,
+                                        self.stream()), "dsv4cu_sparse_attn")
+
+    def quantize_fp8(self, w, s, src, rows, cols):
+        check(self.L.dsv4cu_quantize_fp8(self.ptr(w), self.ptr(s), self.ptr(src), rows, cols,
+                                         self.stream()), "quantize_fp8")
+
+    def quantize_fp4(self, w, s, src, rows, cols):
+        check(self.L.dsv4cu_quantize_fp4(self.ptr(w), self.ptr(s), self.ptr(src), rows, cols,
+                                         self.stream()), "quantize_fp4")
+
+    def fill_normal(self, dst, seed, mean, std):
+        check(self.L.dsv4cu_fill_normal(self.ptr(dst), dst.numel(), seed, mean, std,
+                                        self.stream()), "fill_normal")
+
+    def round_bf16(self, x):
+        check(self.L.dsv4cu_round_bf16(self.ptr(x), x.numel(), self.stream()), "round_bf16")

@@ -1,0 +1,183 @@
+/* dsv4cu.h - native C ABI of the B200 (sm_100a) library for the quantized
+ * matmul / MoE / sparse-attention-indexer hot path of deepseek-v4-in-c.
+ *
+ * Two layers are exported from libdsv4cu.so:
+ *
+ *   1. dsv4_compat.h: the reference's own operator entry points (dsv4_mmq_n,
+ *      fp8_n, dsv4_route, dsv4_topk, ...) with HOST pointers, so the reference
+ *      engine links against this library unchanged.
+ *   2. This header: device-pointer entry points (prefix dsv4cu_) that take a
+ *      cudaStream_t and return a status. Every call here is asynchronous on the
+ *      given stream unless stated; no call aborts the process.
+ *
+ * Plain C types only: pointers, ints, floats. A "stream" is a cudaStream_t
+ * passed as void*. All pointers are device pointers unless marked (host).
+ */
+#ifndef DSV4CU_H
+#define DSV4CU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+enum {
+    DSV4CU_OK = 0,
+    DSV4CU_ERR_ARG = -1,          /* invalid argument or shape               */
+    DSV4CU_ERR_UNSUPPORTED = -2,  /* format/geometry this build does not cover */
+    DSV4CU_ERR_CUDA = -3,         /* a CUDA runtime call or launch failed     */
+    DSV4CU_ERR_NOMEM = -4,        /* device allocation failed                 */
+    DSV4CU_ERR_TIMEOUT = -5,      /* a bounded device wait expired            */
+    DSV4CU_ERR_COMM = -6          /* collective / peer exchange failed        */
+};
+
+/* Weight storage tags; same values as the reference enum
+ * (src/00_base/dsv4.h:81). */
+enum { DSV4CU_WF32 = 0, DSV4CU_WBF16 = 1, DSV4CU_WFP8 = 2, DSV4CU_WFP4 = 3 };
+
+/* Packed matrix. Member order and types are those of the reference
+ * DSV4QMat (src/00_base/dsv4_weights.h:34-40); here w and s are DEVICE
+ * pointers. FP8: w [rows][cols] e4m3, s [ceil(rows/blk_r)][ceil(cols/blk_c)]
+ * E8M0. FP4: w [rows][cols/2] (low nibble = even column), s likewise.
+ * BF16: w [rows][cols] u16, s unused. */
+typedef struct {
+    const void *w;
+    const void *s;
+    int         wdt;
+    int         rows, cols;
+    int         blk_r, blk_c;
+} dsv4cu_qmat;
+
+/* One expert: same member order as the reference DSV4ExpertW
+ * (src/00_base/dsv4_weights.h:101-104): w1 (gate) and w3 (up) are
+ * [inter][hidden], w2 (down) is [hidden][inter]. */
+typedef struct {
+    dsv4cu_qmat w1, w3, w2;
+} dsv4cu_expert;
+
+/* Last error message of the calling thread (static storage, never NULL). */
+const char *dsv4cu_last_error(void);
+int dsv4cu_set_error(int code, const char *fmt, ...);
+
+/* Library context: owns a device workspace (grown on demand, or reserved up
+ * front with dsv4cu_ctx_reserve so later calls allocate nothing). One context
+ * per device; not shared between threads without external locking. */
+typedef struct dsv4cu_ctx dsv4cu_ctx;
+int  dsv4cu_ctx_create(dsv4cu_ctx **out, int device);
+void dsv4cu_ctx_destroy(dsv4cu_ctx *ctx);
+int  dsv4cu_ctx_reserve(dsv4cu_ctx *ctx, size_t bytes);
+size_t dsv4cu_ctx_workspace_bytes(const dsv4cu_ctx *ctx);
+
+/* Workspace bytes a dsv4cu_mmq call of this shape needs. */
+size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt);
+
+/* y[t*rows + o] = sum_c x[t*cols + c] * W[o][c], t < nt, fp32 in and out.
+ * Replaces dsv4_mmq_n (src/10_compute/dsv4_matmul.h:40) on device memory.
+ * Every geometry the reference accepts is covered: fast tensor-core paths for
+ * FP8 with blk_c % 16 == 0, FP4 with blk_c % 32 == 0 and BF16, and an exact
+ * per-element path for every other block geometry. */
+int dsv4cu_mmq(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
+               int nt, void *stream);
+
+/* Router for nt tokens; replaces dsv4_route (src/10_compute/dsv4_kernels.h:24).
+ * logits [nt][n_experts] (read), scores/orig [nt][n_experts] (written: biased
+ * selection scores and sqrt(softplus) scores, either may be NULL), idx/wts
+ * [nt][topk]. bias [n_experts] or NULL; tid2eid [vocab][topk] int64 or NULL
+ * (hash routing, token_ids [nt] then required). topk <= 16. */
+int dsv4cu_route(int *idx, float *wts, float *scores, float *orig,
+                 const float *logits, const float *bias, const int64_t *tid2eid,
+                 const int *token_ids, int n_experts, int topk,
+                 float route_scale, int nt, void *stream);
+
+/* y = silu(min(gate, limit)) * clamp(up, -limit, limit), n elements;
+ * replaces dsv4_swiglu (src/10_compute/dsv4_kernels.h:22). */
+int dsv4cu_swiglu(float *y, const float *gate, const float *up, int n,
+                  float limit, void *stream);
+
+/* One MoE layer decode step for nt tokens (the reference dsv4_layer_moe,
+ * src/70_decode/dsv4_layer.c:48-117, from the router logits on): route, the
+ * routed experts' w1/w3 -> SwiGLU -> w2, the weighted sum in k order, plus the
+ * shared expert added unweighted. experts: DEVICE array of n_experts
+ * descriptors (their w/s are device pointers). shared: HOST pointer to one
+ * descriptor, or NULL. x [nt][hidden], logits [nt][n_experts],
+ * out [nt][hidden]. idx_out/wts_out [nt][topk] may be NULL. nt <= 64.
+ * Routed descriptors are validated on the device; one with a wrong shape or
+ * an unsupported format (FP4 with blk_c % 32, FP8 with blk_c % 16 required)
+ * is skipped rather than read. */
+int dsv4cu_moe_decode(dsv4cu_ctx *ctx, float *out, const float *x,
+                      const float *logits, const float *bias,
+                      const int64_t *tid2eid, const int *token_ids,
+                      const dsv4cu_expert *experts, int n_experts,
+                      const dsv4cu_expert *shared, int topk, float route_scale,
+                      int hidden, int inter, float limit, int nt,
+                      int *idx_out, float *wts_out, void *stream);
+
+/* dsv4cu_moe_decode with CUDA events (cudaEvent_t) recorded around its three
+ * launches: events[0] before the router/bucketing prologue, [1] after it,
+ * [2] after the w1/w3 + SwiGLU kernel, [3] after the w2 + combine kernel.
+ * events may be NULL. Used to time each kernel live on the launching stream. */
+int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, float *out, const float *x,
+                         const float *logits, const float *bias,
+                         const int64_t *tid2eid, const int *token_ids,
+                         const dsv4cu_expert *experts, int n_experts,
+                         const dsv4cu_expert *shared, int topk, float route_scale,
+                         int hidden, int inter, float limit, int nt,
+                         int *idx_out, float *wts_out, void *stream, void **events);
+
+/* Indexer score with fp32 inputs, bit-identical to dsv4_indexer_score
+ * (src/10_compute/dsv4_indexer.c:66-90): out[t] = (float)(sum_h relu(q_h.k_t)
+ * * w_h) * d^-1/2 h^-1/2, with the reference's double reduction tree. */
+int dsv4cu_indexer_score(float *out, const float *q, const float *kv,
+                         const float *weights, int n_heads, int head_dim,
+                         int n_pos, void *stream);
+
+/* The same score from FP8 inputs: q8 [n_heads][head_dim] e4m3 with one fp32
+ * scale per head, k8 [n_pos][k_stride] e4m3 (first head_dim bytes used) with
+ * one fp32 scale per position. Bit-identical to dsv4_indexer_score applied to
+ * the dequantized values q8*q_scale and k8*k_scale. */
+int dsv4cu_indexer_score_fp8(float *out, const uint8_t *q8, const float *q_scale,
+                             const uint8_t *k8, const float *k_scale,
+                             const float *weights, int n_heads, int head_dim,
+                             int n_pos, int k_stride, void *stream);
+
+/* Top-k indices of scores[n], descending, ties to the lower index, k clamped
+ * to n; replaces dsv4_topk (src/10_compute/dsv4_topk.c:76-112) without its
+ * k <= 1024 bound. Writes min(k, n) indices. */
+int dsv4cu_topk(dsv4cu_ctx *ctx, int *idx, const float *scores, int n, int k,
+                void *stream);
+
+/* Sparse attention with sinks over gathered rows; replaces dsv4_sparse_attn
+ * (src/10_compute/dsv4_attn.c:60-107). q/o [h][d] fp32; kv [n][d] fp32
+ * (kv_bf16 = 0) or bf16 (kv_bf16 = 1); idxs [topk] with -1 = masked. */
+int dsv4cu_sparse_attn(dsv4cu_ctx *ctx, float *o, const float *q, const void *kv,
+                       int kv_bf16, const float *sink, const int *idxs, int h,
+                       int d, int topk, float scale, void *stream);
+
+/* Add offset to every idxs[i] >= 0 (dsv4_indexer_offset,
+ * src/10_compute/dsv4_indexer.c:92-96). */
+int dsv4cu_indexer_offset(int *idxs, int n, int offset, void *stream);
+
+/* --------------------------------------------------- weight packing utility
+ * Quantize fp32 [rows][cols] to the reference pack layouts: FP8 e4m3 with one
+ * E8M0 scale per 128x128 block, or FP4 e2m1 with one E8M0 scale per 1x32
+ * block. Scale = 2^ceil(log2(amax / qmax)) (qmax 448 or 6), values rounded to
+ * nearest-even and saturated. */
+int dsv4cu_quantize_fp8(uint8_t *w, uint8_t *s, const float *src, int rows,
+                        int cols, void *stream);
+int dsv4cu_quantize_fp4(uint8_t *w, uint8_t *s, const float *src, int rows,
+                        int cols, void *stream);
+/* Deterministic N(mean, std) fill from (seed, element index), for synthetic
+ * weights and activations. */
+int dsv4cu_fill_normal(float *dst, size_t n, uint64_t seed, float mean,
+                       float std, void *stream);
+/* Round fp32 values to the nearest bf16 value in place (kept as fp32). */
+int dsv4cu_round_bf16(float *x, size_t n, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSV4CU_H */

@@ -1,0 +1,244 @@
+"""CPU checkers for the CUDA library: TEST INFRASTRUCTURE ONLY.
+
+Two checkers, both plain C, loaded with ctypes:
+
+* ``Oracle`` wraps ``oracle/liboracle.so``: this repository's C restatement of
+  the reference algorithms (``oracle/dsv4_oracle.c``; every function cites the
+  reference lines it restates).
+* ``RefLib`` wraps ``oracle/_ref/libdsv4ref.so``: the reference's own CPU kernels
+  compiled from its sources by ``oracle/Makefile``. It exists only where the
+  reference tree was available at build time; callers must tolerate its absence.
+
+Only tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline legs may use
+this module. The product library never imports it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_SO = os.path.join(HERE, "_ref", "libdsv4ref.so")
+REF_TREE = os.environ.get("DSV4_REFERENCE_TREE", "/root/reference")
+
+WF32, WBF16, WFP8, WFP4 = 0, 1, 2, 3
+
+
+class QMat(C.Structure):
+    """Same layout as the reference DSV4QMat (src/00_base/dsv4_weights.h:34-40)."""
+    _fields_ = [("w", C.c_void_p), ("s", C.c_void_p), ("wdt", C.c_int),
+                ("rows", C.c_int), ("cols", C.c_int),
+                ("blk_r", C.c_int), ("blk_c", C.c_int)]
+
+
+def build(with_ref: bool | None = None) -> None:
+    """Compile the restatement (always) and the reference library (when the
+    reference tree is present). Builds the checkers; does not run them."""
+    subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
+    if with_ref is None:
+        with_ref = os.path.isdir(os.path.join(REF_TREE, "src", "10_compute"))
+    if with_ref:
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True)
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def qmat(w: np.ndarray, s, wdt: int, rows: int, cols: int, blk_r=0, blk_c=0) -> QMat:
+    return QMat(w.ctypes.data, None if s is None else s.ctypes.data, wdt, rows, cols,
+                blk_r, blk_c)
+
+
+class _Common:
+    """Calls shared by the restatement and the reference library (same ABI
+    shapes; the restatement prefixes its symbols with ``orc_``)."""
+
+    def __init__(self, lib, prefix):
+        self.lib = lib
+        self.pf = prefix
+        f = self.fn
+        f("indexer_score").restype = None
+        f("topk").restype = C.c_int
+        f("sparse_attn").restype = None
+        f("route").restype = None
+        f("swiglu").restype = None
+
+    def fn(self, name):
+        return getattr(self.lib, self.pf + name)
+
+    def route(self, logits, topk, route_scale, bias=None, tid2eid=None, token_id=0):
+        ne = logits.shape[0]
+        scores = np.ascontiguousarray(logits, dtype=np.float32).copy()
+        orig = np.zeros(ne, np.float32)
+        idx = np.zeros(topk, np.int32)
+        wts = np.zeros(topk, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        t = None if tid2eid is None else np.ascontiguousarray(tid2eid, np.int64)
+        self.fn("route")(_p(idx), _p(wts), _p(scores), _p(orig), _p(b), _p(t),
+                         C.c_int(token_id), C.c_int(ne), C.c_int(topk),
+                         C.c_float(route_scale))
+        return idx, wts, scores, orig
+
+    def swiglu(self, gate, up, limit):
+        y = np.zeros_like(gate, dtype=np.float32)
+        self.fn("swiglu")(_p(y), _p(np.ascontiguousarray(gate, np.float32)),
+                          _p(np.ascontiguousarray(up, np.float32)), C.c_int(gate.size),
+                          C.c_float(limit))
+        return y
+
+    def indexer_score(self, q, kv, weights):
+        h, d = q.shape
+        n = kv.shape[0]
+        out = np.zeros(n, np.float32)
+        self.fn("indexer_score")(_p(out), _p(np.ascontiguousarray(q, np.float32)),
+                                 _p(np.ascontiguousarray(kv, np.float32)),
+                                 _p(np.ascontiguousarray(weights, np.float32)),
+                                 C.c_int(h), C.c_int(d), C.c_int(n))
+        return out
+
+    def topk(self, scores, k):
+        scores = np.ascontiguousarray(scores, np.float32)
+        out = np.full(max(1, min(k, scores.size)), -7, np.int32)
+        r = self.fn("topk")(_p(out), _p(scores), C.c_int(scores.size), C.c_int(k))
+        return out[:max(r, 0)]
+
+
+class Oracle(_Common):
+    def __init__(self, path: str = ORACLE_SO):
+        if not os.path.exists(path):
+            build(with_ref=False)
+        lib = C.CDLL(path)
+        super().__init__(lib, "orc_")
+        lib.orc_e8m0.restype = C.c_float
+        lib.orc_e8m0.argtypes = [C.c_uint8]
+        lib.orc_e4m3.restype = C.c_float
+        lib.orc_e4m3.argtypes = [C.c_uint8]
+        lib.orc_e2m1.restype = C.c_float
+        lib.orc_e2m1.argtypes = [C.c_uint8]
+        lib.orc_fp4_at.restype = C.c_float
+        lib.orc_fp4_at.argtypes = [C.c_void_p, C.c_int64]
+        lib.orc_mmq_n.restype = C.c_int
+        lib.orc_dot_f32d.restype = C.c_double
+        lib.orc_window_idxs.restype = C.c_int
+        lib.orc_expert_buckets.restype = C.c_int
+
+    def mmq(self, x, m: QMat, nt=None):
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.shape[0] if x.ndim == 2 else 1
+        y = np.zeros((nt, m.rows), np.float32)
+        r = self.lib.orc_mmq_n(_p(y), _p(x), C.byref(m), C.c_int(nt))
+        if r != 0:
+            raise ValueError(f"oracle: unknown weight format {m.wdt}")
+        return y
+
+    def expert_forward(self, x, w3: list, inter: int, limit: float):
+        arr = (QMat * 3)(*w3)
+        out = np.zeros(w3[2].rows, np.float32)
+        self.lib.orc_expert_forward(_p(out), _p(np.ascontiguousarray(x, np.float32)), arr,
+                                    C.c_int(inter), C.c_float(limit))
+        return out
+
+    def moe_decode(self, x, logits, experts: list, shared: list, topk, route_scale,
+                   hidden, inter, limit, bias=None, tid2eid=None, token_id=0):
+        ne = len(experts)
+        arr = (QMat * (3 * ne))(*[q for e in experts for q in e])
+        sh = (QMat * 3)(*shared)
+        out = np.zeros(hidden, np.float32)
+        idx = np.zeros(topk, np.int32)
+        wts = np.zeros(topk, np.float32)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        t = None if tid2eid is None else np.ascontiguousarray(tid2eid, np.int64)
+        self.lib.orc_moe_decode(_p(out), _p(idx), _p(wts),
+                                _p(np.ascontiguousarray(x, np.float32)),
+                                _p(np.ascontiguousarray(logits, np.float32)), _p(b), _p(t),
+                                C.c_int(token_id), arr, sh, C.c_int(ne), C.c_int(topk),
+                                C.c_float(route_scale), C.c_int(hidden), C.c_int(inter),
+                                C.c_float(limit))
+        return out, idx, wts
+
+    def sparse_attn(self, q, kv, sink, idxs, scale):
+        h, d = q.shape
+        o = np.zeros((h, d), np.float32)
+        self.lib.orc_sparse_attn(_p(o), _p(np.ascontiguousarray(q, np.float32)),
+                                 _p(np.ascontiguousarray(kv, np.float32)),
+                                 _p(np.ascontiguousarray(sink, np.float32)),
+                                 _p(np.ascontiguousarray(idxs, np.int32)), C.c_int(h),
+                                 C.c_int(d), C.c_int(len(idxs)), C.c_float(scale))
+        return o
+
+    def window_idxs(self, pos, win):
+        out = np.zeros(win, np.int32)
+        n = self.lib.orc_window_idxs(_p(out), C.c_int(pos), C.c_int(win))
+        return out, n
+
+    def indexer_offset(self, idxs, offset):
+        a = np.ascontiguousarray(idxs, np.int32).copy()
+        self.lib.orc_indexer_offset(_p(a), C.c_int(a.size), C.c_int(offset))
+        return a
+
+    def expert_buckets(self, topk_idx, n_experts):
+        ti = np.ascontiguousarray(topk_idx, np.int32)
+        n, topk = ti.shape
+        count = np.zeros(n_experts, np.int32)
+        off = np.zeros(n_experts + 1, np.int32)
+        tok = np.zeros(n * topk, np.int32)
+        ks = np.zeros(n * topk, np.int32)
+        d = self.lib.orc_expert_buckets(_p(count), _p(off), _p(tok), _p(ks), _p(ti),
+                                        C.c_int(n), C.c_int(topk), C.c_int(n_experts))
+        return count, off, tok, ks, d
+
+
+class RefLib(_Common):
+    """The reference's own kernels (oracle/_ref/libdsv4ref.so)."""
+
+    def __init__(self, path: str = REF_SO):
+        lib = C.CDLL(path)
+        super().__init__(lib, "dsv4_")
+        lib.dsv4_cfg_init.restype = None
+
+    @staticmethod
+    def available(path: str = REF_SO) -> bool:
+        return os.path.exists(path)
+
+    def mmq(self, x, m: QMat):
+        x = np.ascontiguousarray(x, np.float32)
+        nt = x.shape[0] if x.ndim == 2 else 1
+        y = np.zeros((nt, m.rows), np.float32)
+        self.lib.dsv4_mmq_n(_p(y), _p(x), C.byref(m), C.c_int(nt))
+        return y
+
+    def matmul_fp8_exact(self, x, m: QMat):
+        """tests/unit/ref_kernels.c:53-76, the exact-table FP8 reference."""
+        y = np.zeros(m.rows, np.float32)
+        self.lib.dsv4_matmul_fp8_f32(_p(y), _p(np.ascontiguousarray(x, np.float32)),
+                                     C.c_void_p(m.w), C.c_void_p(m.s), C.c_int(m.cols),
+                                     C.c_int(m.rows), C.c_int(m.blk_r), C.c_int(m.blk_c))
+        return y
+
+    def expert_forward(self, x, w3: list, inter: int, limit: float):
+        """src/10_compute/dsv4_ops.c:85-93 through the reference's own matmuls.
+        DSV4ExpertW is {w1, w3, w2} (src/00_base/dsv4_weights.h:101-104)."""
+        arr = (QMat * 3)(*w3)
+        out = np.zeros(w3[2].rows, np.float32)
+        scratch = np.zeros(inter * 3, np.float32)
+        self.lib.dsv4_expert_forward(_p(out), _p(np.ascontiguousarray(x, np.float32)), arr,
+                                     _p(scratch), _p(scratch[inter:]), _p(scratch[2 * inter:]),
+                                     C.c_int(inter), C.c_float(limit))
+        return out
+
+    def sparse_attn(self, q, kv, sink, idxs, scale):
+        h, d = q.shape
+        o = np.zeros((h, d), np.float32)
+        scratch = np.zeros(h * max(1, len(idxs)), np.float32)
+        self.lib.dsv4_sparse_attn(_p(o), _p(np.ascontiguousarray(q, np.float32)),
+                                  _p(np.ascontiguousarray(kv, np.float32)),
+                                  _p(np.ascontiguousarray(sink, np.float32)),
+                                  _p(np.ascontiguousarray(idxs, np.int32)), C.c_int(h),
+                                  C.c_int(d), C.c_int(len(idxs)), C.c_float(scale),
+                                  _p(scratch))
+        return o

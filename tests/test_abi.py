@@ -1,0 +1,71 @@
+"""The C-ABI library loads and exports every entry point include/*.h declares.
+
+CPU only: nothing here launches a kernel.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import PKG, ROOT
+
+HEADERS = [os.path.join(ROOT, "include", h) for h in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if h.endswith(".h")]
+LIB = os.path.join(PKG, "libdsv4cu.so")
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        src = re.sub(r"//[^\n]*", "", src)
+        for m in re.finditer(r"^[A-Za-z_][\w\s\*]*?\b([A-Za-z_]\w*)\s*\(", src, flags=re.M):
+            name = m.group(1)
+            line = src[m.start():src.find("\n", m.start())]
+            if line.lstrip().startswith(("typedef", "#", "return", "if", "enum", "struct")):
+                continue
+            names.add(name)
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def built_lib():
+    if not os.path.exists(LIB):
+        subprocess.run(["make", "-s", "-C", PKG], check=True)
+    return LIB
+
+
+def test_headers_declare_the_reference_entry_points():
+    names = set(declared_functions())
+    # src/10_compute/dsv4_matmul.h:40-52, dsv4_kernels.h, 80_prefill/dsv4_prefill_vk.h:31-49
+    for ref in ("dsv4_mmq_n", "dsv4_mmq", "bf16_n", "fp8_n", "fp4_n", "dsv4_route", "dsv4_swiglu",
+                "dsv4_expert_forward", "dsv4_indexer_score", "dsv4_topk", "dsv4_indexer_offset",
+                "dsv4_sparse_attn", "dsv4_window_idxs", "dsv4_prefill_vk_init",
+                "dsv4_prefill_vk_free", "dsv4_prefill_vk_gemm", "dsv4_prefill_vk_expert_fused"):
+        assert ref in names, ref
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    lib = ctypes.CDLL(built_lib)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_no_cxx_types_in_headers():
+    for h in HEADERS:
+        src = open(h).read()
+        for bad in ("torch", "std::", "at::Tensor", "c10::"):
+            assert bad not in src, (h, bad)
+
+
+def test_binding_raises_without_library(tmp_path, monkeypatch):
+    import dsv4cu
+    monkeypatch.setattr(dsv4cu, "LIB_PATH", str(tmp_path / "missing.so"))
+    monkeypatch.setattr(dsv4cu, "_lib", None)
+    with pytest.raises(dsv4cu.DSV4CUError):
+        dsv4cu.lib()

@@ -1,0 +1,189 @@
+"""Sparse-attention indexer on the B200: FP8 / fp32 scores bit-identical to the
+reference, top-k indices identical (ties to the lower index), sparse attention
+within tolerance; config 4 at full size (32768 keys, 64 heads x 128, top-2048).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import kat
+import pack
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def quant_rows(a):
+    """e4m3 codes with one power-of-two fp32 scale per row."""
+    amax = np.abs(a).max(axis=1)
+    f, E = np.frexp(amax)
+    e = E - 9 + (f > 0.875)
+    sc = np.ldexp(np.ones_like(amax), e).astype(np.float32)
+    v = np.ldexp(a, -e[:, None]).astype(np.float32)
+    codes = pack._rne_grid(v, pack._E4M3_POS).astype(np.uint8)
+    codes = np.where(np.signbit(v), codes | 0x80, codes).astype(np.uint8)
+    return codes, sc
+
+
+def dev_score(dev, q, kv, w):
+    t = __import__("torch")
+    h, d = q.shape
+    n = kv.shape[0]
+    out = t.empty(n, dtype=t.float32, device="cuda")
+    dev.indexer_score(out, t.from_numpy(q).cuda(), t.from_numpy(kv).cuda(), t.from_numpy(w).cuda(), h, d, n)
+    t.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def dev_score8(dev, q8, qs, k8, ks, w, stride=None):
+    t = __import__("torch")
+    h, d = q8.shape
+    n = k8.shape[0]
+    stride = stride or k8.shape[1]
+    out = t.empty(n, dtype=t.float32, device="cuda")
+    dev.indexer_score_fp8(out, t.from_numpy(q8).cuda(), t.from_numpy(qs).cuda(), t.from_numpy(k8).cuda(),
+                          t.from_numpy(ks).cuda(), t.from_numpy(w).cuda(), h, d, n, stride)
+    t.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def dev_topk(dev, s, k):
+    t = __import__("torch")
+    kk = max(0, min(k, s.size))
+    out = t.full((max(kk, 1),), -7, dtype=t.int32, device="cuda")
+    dev.topk(out, t.from_numpy(np.ascontiguousarray(s, np.float32)).cuda(), s.size, k)
+    t.cuda.synchronize()
+    return out.cpu().numpy()[:kk]
+
+
+def bits(a):
+    return np.asarray(a, np.float32).view(np.uint32)
+
+
+def test_indexer_golden_bitexact(dev, host):
+    g = dict(golden("indexer.npz"))
+    assert np.array_equal(bits(dev_score(dev, g["q"], g["kv"], g["w"])), bits(g["score"]))
+    assert np.array_equal(bits(dev_score8(dev, g["q8"], g["qsc"], g["k8"], g["ksc"], g["w"])), bits(g["score8"]))
+    assert np.array_equal(bits(dev_score(dev, g["q3"], g["k3"], g["w3"])), bits(g["score3"]))
+    assert np.array_equal(bits(host.indexer_score(g["q"], g["kv"], g["w"])), bits(g["score"]))
+
+
+def test_indexer_kat(host):
+    out = host.indexer_score(np.array([[1, 0], [0, 0]], np.float32), np.array([[1, 0], [-1, 0]], np.float32),
+                             np.array([1, 1], np.float32))
+    assert out[0] > 0 and out[1] == 0.0
+    out = host.indexer_score(np.eye(2, dtype=np.float32), np.eye(2, dtype=np.float32), np.array([1, 4], np.float32))
+    assert abs(out[1] / out[0] - 4) < 1e-4
+
+
+@pytest.mark.parametrize("h,d,n", [(64, 128, 4097), (3, 7, 50), (8, 48, 31), (1, 16, 1), (64, 256, 33)])
+def test_indexer_random_bitexact(dev, orc, h, d, n):
+    rng = np.random.default_rng(h * d + n)
+    q = rng.standard_normal((h, d)).astype(np.float32)
+    kv = rng.standard_normal((n, d)).astype(np.float32)
+    w = rng.standard_normal(h).astype(np.float32)
+    assert np.array_equal(bits(dev_score(dev, q, kv, w)), bits(orc.indexer_score(q, kv, w)))
+
+
+def test_config4_full_fp8_score_topk(dev, orc):
+    """32768 FP8 keys (per-token pow2 scale), 64 heads x 128, top-2048."""
+    rng = np.random.default_rng(7)
+    k8, ks = quant_rows(rng.standard_normal((32768, 128)).astype(np.float32))
+    q8, qs = quant_rows(rng.standard_normal((64, 128)).astype(np.float32))
+    w = rng.standard_normal(64).astype(np.float32)
+    got = dev_score8(dev, q8, qs, k8, ks, w)
+    kf = (pack.E4M3[k8] * ks[:, None]).astype(np.float32)
+    qf = (pack.E4M3[q8] * qs[:, None]).astype(np.float32)
+    want = orc.indexer_score(qf, kf, w)
+    assert np.array_equal(bits(got), bits(want))
+    idx = dev_topk(dev, got, 2048)
+    assert np.array_equal(idx, orc.topk(want, 2048))
+
+
+def test_topk_golden_and_kat(dev, host):
+    g = dict(golden("topk.npz"))
+    for key in g:
+        if key.endswith("_scores"):
+            base = key[:-len("_scores")]
+            k = int(base.split("_k")[1])
+            assert np.array_equal(dev_topk(dev, g[key], k), g[base + "_idx"]), base
+    s = np.array([1, 5, 5, 2, 0, 5], np.float32)
+    idx, r = host.topk(s, 4)
+    assert idx.tolist() == [1, 2, 5, 3] and r == 4
+    idx, r = host.topk(s, 10)
+    assert r == 6 and idx.tolist() == [1, 2, 5, 3, 0, 4]
+    assert host.topk(s, 0)[1] == 0 and host.topk(s, -3)[1] == -3
+
+
+@pytest.mark.parametrize("n,k", [(32768, 2048), (32768, 512), (1, 1), (5, 5), (100000, 1024),
+                                 (3000, 8192), (65536, 8192)])
+def test_topk_random_with_ties(dev, orc, n, k):
+    rng = np.random.default_rng(n + k)
+    s = (rng.integers(-300, 300, n) * 0.125).astype(np.float32)   # many exact ties
+    s[rng.integers(0, n, max(1, n // 50))] = -0.0
+    s[rng.integers(0, n, max(1, n // 50))] = 0.0
+    assert np.array_equal(dev_topk(dev, s, k), orc.topk(s, k))
+
+
+def test_topk_all_equal_and_extremes(dev, orc):
+    s = np.zeros(5000, np.float32)
+    assert np.array_equal(dev_topk(dev, s, 2048), np.arange(2048))
+    s = np.array([np.inf, -np.inf, 3e38, -3e38, 1e-45, -1e-45, 0.0, -0.0], np.float32)
+    assert np.array_equal(dev_topk(dev, s, 8), orc.topk(s, 8))
+
+
+def test_offset_and_window(host):
+    assert host.indexer_offset([0, 3, -1, 7, -1], 128).tolist() == [128, 131, -1, 135, -1]
+    for pos, win, want, n in kat.window_kat():
+        got, cnt = host.window_idxs(pos, win)
+        assert got.tolist() == want and cnt == n
+
+
+# ----------------------------------------------------------------- attention
+ATT_TOL = 1e-5
+
+
+def att_err(got, want):
+    return float(np.abs(got.astype(np.float64) - want).max()) / max(float(np.abs(want).max()), 1e-30)
+
+
+@pytest.mark.parametrize("case", kat.attn_kat(), ids=lambda c: c[0])
+def test_attn_kat(host, case):
+    name, q, kv, sink, idxs, scale, check = case
+    # the device kernel needs head dims that are multiples of 4: pad with zeros
+    d = q.shape[1]
+    pad = (-d) % 4
+    qp = np.pad(q, ((0, 0), (0, pad)))
+    kvp = np.pad(kv, ((0, 0), (0, pad)))
+    o = host.sparse_attn(qp, kvp, sink, idxs, scale)[:, :d]
+    assert check(o), (name, o)
+
+
+def test_attn_golden(host):
+    g = dict(golden("attn.npz"))
+    o = host.sparse_attn(g["q"], g["kv"], g["sink"], g["idx"], np.float32(1 / np.sqrt(64)))
+    assert att_err(o, g["o"]) <= ATT_TOL
+
+
+@pytest.mark.parametrize("bf16", [0, 1])
+def test_attn_config4_full(dev, orc, bf16):
+    """64 heads, d = 512, 2048 indexer rows + a 128-slot window with masked slots."""
+    t = __import__("torch")
+    rng = np.random.default_rng(5 + bf16)
+    H, D, N, T = 64, 512, 32768, 2176
+    kv = pack.bf16_round(rng.standard_normal((N, D)).astype(np.float32))
+    q = pack.bf16_round(rng.standard_normal((H, D)).astype(np.float32))
+    sink = rng.standard_normal(H).astype(np.float32)
+    idx = rng.choice(N, T, replace=False).astype(np.int32)
+    idx[2048 + 100:] = -1
+    scale = np.float32(1 / np.sqrt(D))
+    o = t.empty((H, D), dtype=t.float32, device="cuda")
+    kvd = t.from_numpy(kv).cuda()
+    if bf16:
+        kvd = kvd.to(t.bfloat16)
+    dev.sparse_attn(o, t.from_numpy(q).cuda(), kvd, bf16, t.from_numpy(sink).cuda(), t.from_numpy(idx).cuda(),
+                    H, D, T, float(scale))
+    t.cuda.synchronize()
+    want = orc.sparse_attn(q, kv, sink, idx, scale)
+    assert att_err(o.cpu().numpy(), want) <= ATT_TOL

@@ -1,0 +1,224 @@
+"""Packed matmul on the B200 against the reference (golden vectors, known
+answers) and the CPU oracle, through both C-ABI layers.
+
+Tolerance (the BASELINE contract for matmul outputs): max|y - y_ref| /
+max|y_ref| <= 1e-3. The kernels are far tighter in practice (exact products,
+fp32 accumulation), so the L2 relative error is also held to 1e-5.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+import kat
+import oracle
+import pack
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+MAX_REL = 1e-3
+L2_REL = 1e-5
+
+
+def rel_err(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    den = max(float(np.abs(want).max()), 1e-30)
+    return float(np.abs(got - want).max()) / den
+
+
+def l2_rel(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return math.sqrt(float(((got - want) ** 2).sum()) / max(float((want ** 2).sum()), 1e-300))
+
+
+def assert_close(got, want, what=""):
+    assert rel_err(got, want) <= MAX_REL, (what, rel_err(got, want))
+    assert l2_rel(got, want) <= L2_REL, (what, l2_rel(got, want))
+
+
+@pytest.fixture(autouse=True)
+def _fresh_registry(host):
+    host.forget_all()
+    yield
+    host.forget_all()
+
+
+@pytest.mark.parametrize("case", kat.matmul_cases(), ids=lambda c: c[0])
+def test_matmul_known_answers(host, orc, case):
+    import dsv4cu
+    name, wdt, W, S, rows, cols, br, bc, x, y, chk = case
+    m = dsv4cu.QMat(W.ctypes.data, None if S is None else S.ctypes.data, wdt, rows, cols, br, bc)
+    got = host.mmq(x, m)
+    if chk == "exact":
+        assert np.array_equal(got, y), (got, y)
+    elif chk == "absmag":
+        assert np.array_equal(np.abs(got), y)
+    elif chk == "all_codes":
+        want = pack.E4M3
+        nan = np.isnan(want)
+        assert np.all(np.isnan(got[0][nan]))
+        assert np.array_equal(got[0][~nan], want[~nan] + 0.0)
+    else:
+        want = orc.mmq(x, oracle.qmat(W, S, wdt, rows, cols, br, bc))
+        if chk == "nan_row0":
+            assert np.isnan(got[0][0])
+            assert not np.any(np.isnan(got[0][1:]))
+            assert_close(got[0][1:], want[0][1:], name)
+        else:
+            assert_close(got, want, name)
+
+
+def test_matmul_reference_golden(host):
+    import dsv4cu
+    g = dict(golden("matmul.npz"))
+    for tag, wdt, br, bc in (("fp8", 2, 128, 128), ("fp8g", 2, 128, 100), ("fp4", 3, 1, 32),
+                             ("fp4t", 3, 1, 32), ("bf16", 1, 0, 0)):
+        W, x = g[f"{tag}_W"], g[f"{tag}_x"]
+        S = g.get(f"{tag}_S")
+        m = dsv4cu.QMat(W.ctypes.data, None if S is None else S.ctypes.data, wdt, W.shape[0],
+                        x.shape[1], br, bc)
+        assert_close(host.mmq(x, m), g[f"{tag}_y"], tag)
+
+
+SHAPES = [
+    # (wdt, rows, cols, blk_r, blk_c, nt)
+    (2, 7168, 7168, 128, 128, 1),
+    (2, 1024, 4096, 128, 128, 1),     # wq_a
+    (2, 512, 4096, 128, 128, 3),      # wkv, small batch
+    (2, 4096, 8192, 128, 128, 2),     # wo_b
+    (2, 129, 320, 128, 128, 5),       # ragged rows, K not a multiple of 128
+    (2, 200, 256, 64, 32, 1),         # other block grid, fast path
+    (2, 33, 100, 16, 20, 2),          # generic path (blk_c % 16 != 0)
+    (3, 2048, 4096, 1, 32, 1),        # routed w1/w3
+    (3, 4096, 2048, 1, 32, 4),        # routed w2, batch
+    (3, 77, 160, 1, 32, 7),           # tail blocks, odd rows, nt not a tile multiple
+    (3, 40, 96, 2, 64, 2),            # two-row scale blocks, 64-wide
+    (3, 9, 72, 1, 24, 1),             # generic path (blk_c % 32 != 0)
+    (1, 256, 4096, 0, 0, 1),          # router gate
+    (1, 64, 4096, 0, 0, 2),           # indexer weights_proj
+    (1, 19, 36, 0, 0, 3),             # bf16 generic (cols % 8 != 0)
+]
+
+
+def make_weights(rng, wdt, rows, cols, br, bc):
+    if wdt == 2:
+        W = rng.integers(0, 256, (rows, cols), dtype=np.uint8)
+        W = np.where((W & 0x7F) == 0x7F, W & 0xFE, W).astype(np.uint8)
+        S = rng.integers(112, 132, (-(-rows // br)) * (-(-cols // bc)), dtype=np.uint8)
+    elif wdt == 3:
+        W = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+        S = rng.integers(112, 132, (-(-rows // br)) * (-(-cols // bc)), dtype=np.uint8)
+    else:
+        W = pack.bf16_bits((rng.standard_normal((rows, cols)) * 0.05).astype(np.float32))
+        S = None
+    return W, S
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "w%d_%dx%d_b%dx%d_nt%d" % s)
+def test_matmul_vs_oracle(host, dev, orc, shape):
+    import torch
+    import dsv4cu
+    wdt, rows, cols, br, bc, nt = shape
+    rng = np.random.default_rng(rows * 31 + cols + nt)
+    W, S = make_weights(rng, wdt, rows, cols, br, bc)
+    x = pack.bf16_round(rng.standard_normal((nt, cols)).astype(np.float32))
+    want = orc.mmq(x, oracle.qmat(W, S, wdt, rows, cols, br, bc))
+    # host-pointer reference ABI
+    m = dsv4cu.QMat(W.ctypes.data, None if S is None else S.ctypes.data, wdt, rows, cols, br, bc)
+    got = host.mmq(x, m)
+    assert_close(got, want, shape)
+    # native device ABI gives the same bits
+    dW = torch.from_numpy(W).cuda()
+    dS = None if S is None else torch.from_numpy(S).cuda()
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((nt, rows), dtype=torch.float32, device="cuda")
+    dev.mmq(dy, dx, dev.qmat(dW, dS, wdt, rows, cols, br, bc), nt)
+    torch.cuda.synchronize()
+    assert np.array_equal(dy.cpu().numpy().view(np.uint32), got.view(np.uint32))
+
+
+def test_matmul_fp32_activations(host, orc):
+    """Arbitrary fp32 (not bf16-valued) activations stay within the contract."""
+    import dsv4cu
+    rng = np.random.default_rng(5)
+    W, S = make_weights(rng, 2, 512, 2048, 128, 128)
+    x = (rng.standard_normal((2, 2048)) * np.exp(rng.uniform(-6, 6, (2, 2048)))).astype(np.float32)
+    m = dsv4cu.QMat(W.ctypes.data, S.ctypes.data, 2, 512, 2048, 128, 128)
+    assert_close(host.mmq(x, m), orc.mmq(x, oracle.qmat(W, S, 2, 512, 2048, 128, 128)))
+
+
+def test_batched_equals_single_token_calls_bitwise(host):
+    """test_matmul.c:690-793: a batch row is the same arithmetic as a 1-token
+    call; NT > 128 also crosses the reference's tile size."""
+    import dsv4cu
+    rng = np.random.default_rng(9)
+    for wdt, br, bc in ((2, 128, 128), (3, 1, 32), (1, 0, 0)):
+        W, S = make_weights(rng, wdt, 130, 256, br, bc)
+        x = rng.standard_normal((130, 256)).astype(np.float32)
+        m = dsv4cu.QMat(W.ctypes.data, None if S is None else S.ctypes.data, wdt, 130, 256, br, bc)
+        batched = host.mmq(x, m)
+        singles = np.stack([host.mmq(x[t:t + 1], m)[0] for t in range(0, 130, 13)])
+        assert np.array_equal(batched[::13].view(np.uint32), singles.view(np.uint32)), wdt
+
+
+def test_deterministic_and_cache_refresh(host):
+    import dsv4cu
+    rng = np.random.default_rng(3)
+    W, S = make_weights(rng, 3, 1024, 2048, 1, 32)
+    x = rng.standard_normal((1, 2048)).astype(np.float32)
+    m = dsv4cu.QMat(W.ctypes.data, S.ctypes.data, 3, 1024, 2048, 1, 32)
+    a = host.mmq(x, m)
+    b = host.mmq(x, m)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    # refill the same host buffer with another expert: the mirror must notice
+    W[:] = rng.integers(0, 256, W.shape, dtype=np.uint8)
+    c = host.mmq(x, m)
+    assert not np.array_equal(a, c)
+    d = oracle.Oracle().mmq(x, oracle.qmat(W, S, 3, 1024, 2048, 1, 32))
+    assert_close(c, d)
+
+
+def test_fp8_n_fp4_n_bf16_n_entry_points(host, orc):
+    rng = np.random.default_rng(4)
+    W8, S8 = make_weights(rng, 2, 256, 512, 128, 128)
+    W4, S4 = make_weights(rng, 3, 256, 512, 1, 32)
+    Wb, _ = make_weights(rng, 1, 64, 512, 0, 0)
+    x = rng.standard_normal((2, 512)).astype(np.float32)
+    assert_close(host.fp8_n(x, W8, S8, 256, 512, 128, 128), orc.mmq(x, oracle.qmat(W8, S8, 2, 256, 512, 128, 128)))
+    assert_close(host.fp4_n(x, W4, S4, 256, 512, 1, 32), orc.mmq(x, oracle.qmat(W4, S4, 3, 256, 512, 1, 32)))
+    assert_close(host.bf16_n(x, Wb, 64, 512), orc.mmq(x, oracle.qmat(Wb, None, 1, 64, 512)))
+
+
+def test_prefill_seam(host, orc):
+    """dsv4_prefill_vk_* keep their 0 / -1 contract and the GEMM / expert math."""
+    import ctypes as C
+    import dsv4cu
+    L = dsv4cu.lib()
+    v = C.c_void_p()
+    assert L.dsv4_prefill_vk_init(C.byref(v), None, None, None) == 0
+    rng = np.random.default_rng(12)
+    W, S = make_weights(rng, 2, 256, 512, 128, 128)
+    x = rng.standard_normal((17, 512)).astype(np.float32)
+    y = np.zeros((17, 256), np.float32)
+    m = dsv4cu.QMat(W.ctypes.data, S.ctypes.data, 2, 256, 512, 128, 128)
+    assert L.dsv4_prefill_vk_gemm(v, y.ctypes.data, x.ctypes.data, C.byref(m), 17) == 0
+    assert_close(y, orc.mmq(x, oracle.qmat(W, S, 2, 256, 512, 128, 128)))
+    g = dict(golden("expert.npz"))
+    mats = [dsv4cu.QMat(g[f"fp4_{n}_W"].ctypes.data, g[f"fp4_{n}_S"].ctypes.data, 3, r, c, 1, 32)
+            for n, r, c in (("w1", 256, 512), ("w3", 256, 512), ("w2", 512, 256))]
+    xe = np.repeat(g["fp4_x"][None], 3, 0)
+    ye = np.zeros((3, 512), np.float32)
+    calls = []
+    FILL = C.CFUNCTYPE(C.c_int, C.c_void_p)
+    fill = FILL(lambda ctx: (calls.append(1), 0)[1])
+    assert L.dsv4_prefill_vk_expert_fused(v, ye.ctypes.data, xe.ctypes.data, C.byref(mats[0]),
+                                          C.byref(mats[1]), C.byref(mats[2]), 3, 256,
+                                          C.c_float(10.0), fill, None) == 0
+    for t in range(3):
+        assert_close(ye[t], g["fp4_out"], "expert_fused")
+    L.dsv4_prefill_vk_free(v)
