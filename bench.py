@@ -158,10 +158,9 @@ def build_layer(dev, torch, n_experts=N_EXPERTS):
         experts.append(dsv4cu.Expert(mat(3, INTER, HIDDEN, 10 * e + 1), mat(3, INTER, HIDDEN, 10 * e + 2),
                                      mat(3, HIDDEN, INTER, 10 * e + 3)))
     shared = dsv4cu.Expert(mat(2, INTER, HIDDEN, 7001), mat(2, INTER, HIDDEN, 7002), mat(2, HIDDEN, INTER, 7003))
-    arr = (dsv4cu.Expert * n_experts)(*experts)
-    experts_dev = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
     torch.cuda.synchronize()
-    return experts_dev, shared, keep
+    layer = dev.moe_create(experts, shared, HIDDEN, INTER)
+    return layer, keep
 
 
 def step_inputs(n, seed):
@@ -186,7 +185,7 @@ def run_ours(args, rank, local_rank, world):
         pg = tdist
     dev = dsv4cu.Device(local_rank)
     NE = args.experts
-    experts_dev, shared, keep = build_layer(dev, torch, NE)
+    layer, keep = build_layer(dev, torch, NE)
     n_steps = args.warmup + args.steps
     xs, lgs = step_inputs(n_steps, 1000 + rank)
     lgs = np.ascontiguousarray(lgs[:, :NE])
@@ -197,17 +196,7 @@ def run_ours(args, rank, local_rank, world):
     st = torch.cuda.current_stream()
 
     def step(i, ev=None):
-        if ev is None:
-            dev.moe_decode(out, dx[i:i + 1], dl[i:i + 1], experts_dev, NE, shared, TOPK, ROUTE_SCALE,
-                           HIDDEN, INTER, LIMIT, 1)
-        else:
-            evp = (dsv4cu.C.c_void_p * 4)(*[e.cuda_event for e in ev])
-            dsv4cu.check(dev.L.dsv4cu_moe_decode_ev(dev.ctx, out.data_ptr(), dx[i:i + 1].data_ptr(),
-                                                   dl[i:i + 1].data_ptr(), None, None, None,
-                                                   experts_dev.data_ptr(), NE,
-                                                   dsv4cu.C.addressof(shared), TOPK, ROUTE_SCALE, HIDDEN,
-                                                   INTER, LIMIT, 1, None, None, st.cuda_stream, evp),
-                         "moe_decode_ev")
+        dev.moe_decode(layer, out, dx[i:i + 1], dl[i:i + 1], TOPK, ROUTE_SCALE, LIMIT, 1, events=ev)
 
     for i in range(args.warmup):
         flush.zero_()
@@ -271,8 +260,7 @@ def run_ours(args, rank, local_rank, world):
         e_s[k].record()
         gx.copy_(hx[i:i + 1], non_blocking=True)
         gl.copy_(hl[i:i + 1], non_blocking=True)
-        dev.moe_decode(out, gx, gl, experts_dev, NE, shared, TOPK, ROUTE_SCALE, HIDDEN, INTER,
-                       LIMIT, 1)
+        dev.moe_decode(layer, out, gx, gl, TOPK, ROUTE_SCALE, LIMIT, 1)
         hout[k].copy_(out[0], non_blocking=True)
         e_e[k].record()
     torch.cuda.synchronize()
@@ -322,6 +310,7 @@ def run_ours(args, rank, local_rank, world):
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+    dev.moe_destroy(layer)
     dev.close()
     del keep
     return res if rank == 0 else None

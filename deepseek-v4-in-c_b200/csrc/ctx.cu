@@ -7,6 +7,10 @@
 #include "common.cuh"
 #include "ctx.h"
 
+namespace dsv4cu {
+const float *router_table_get();
+}
+
 static thread_local char g_err[512] = "no error";
 
 extern "C" const char *dsv4cu_last_error(void) { return g_err; }
@@ -39,13 +43,21 @@ extern "C" int dsv4cu_ctx_create(dsv4cu_ctx **out, int device)
     c->sm_count = p.multiProcessorCount;
     // Counters for the last-block reductions must start at zero and are
     // returned to zero by the block that consumes them.
-    e = cudaMalloc(&c->counters, DSV4CU_MAX_COUNTERS * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(c->counters, 0, DSV4CU_MAX_COUNTERS * sizeof(int));
+    e = cudaMalloc(&c->counters, (DSV4CU_MAX_COUNTERS + 64) * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c->counters, 0, (DSV4CU_MAX_COUNTERS + 64) * sizeof(int));
+    c->status = c->counters + DSV4CU_MAX_COUNTERS;
     if (e != cudaSuccess) {
         if (c->counters) cudaFree(c->counters);
         free(c);
         cudaSetDevice(prev);
         return dsv4cu_set_error(DSV4CU_ERR_NOMEM, "ctx_create: %s", cudaGetErrorString(e));
+    }
+    // Build the router's bf16 score table now, so no later call has to.
+    if (!dsv4cu::router_table_get()) {
+        cudaFree(c->counters);
+        free(c);
+        cudaSetDevice(prev);
+        return dsv4cu_set_error(DSV4CU_ERR_CUDA, "ctx_create: router table setup failed");
     }
     cudaSetDevice(prev);
     *out = c;
@@ -83,6 +95,18 @@ extern "C" int dsv4cu_ctx_reserve(dsv4cu_ctx *c, size_t bytes)
 extern "C" size_t dsv4cu_ctx_workspace_bytes(const dsv4cu_ctx *c)
 {
     return c ? c->ws_bytes : 0;
+}
+
+extern "C" int dsv4cu_ctx_status(dsv4cu_ctx *c, void *stream, int *code)
+{
+    if (!c || !code) return dsv4cu_set_error(DSV4CU_ERR_ARG, "ctx_status: NULL argument");
+    DSV4CU_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
+    DSV4CU_CUDA_TRY(cudaMemcpy(code, c->status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (*code) {
+        DSV4CU_CUDA_TRY(cudaMemset(c->status, 0, sizeof(int)));
+        return dsv4cu_set_error(DSV4CU_ERR_TIMEOUT, "a bounded device wait timed out (code 0x%x)", *code);
+    }
+    return DSV4CU_OK;
 }
 
 int dsv4cu_ws_get(dsv4cu_ctx *c, size_t bytes, void **out)

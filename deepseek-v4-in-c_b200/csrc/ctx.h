@@ -14,6 +14,7 @@ struct dsv4cu_ctx {
     void  *ws;          // device workspace
     size_t ws_bytes;
     int   *counters;    // [DSV4CU_MAX_COUNTERS], zero between calls
+    int   *status;      // device word: first bounded-wait timeout code, 0 = none
 };
 
 // Returns a workspace of at least `bytes` (grows the buffer if needed).

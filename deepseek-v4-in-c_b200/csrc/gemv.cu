@@ -9,11 +9,14 @@
 //     ragged K), one thread per output in the scalar double arithmetic of the
 //     reference's own scalar reference (tests/unit/test_matmul.c:54-176).
 #include <stdio.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "ctx.h"
 #include "gemv_core.cuh"
 #include "gemv.h"
+#include "tma_gemv.cuh"
+#include "tmap.h"
 
 namespace dsv4cu {
 
@@ -66,72 +69,67 @@ __global__ void xprep_kernel(const float *__restrict__ x, int cols, int ldx_in, 
 }
 
 // ------------------------------------------------------------- fast GEMV
-// grid (row groups of 16, ks K-slices); block NW warps splitting the CTA's
-// K-slice. Partial sums are combined in a fixed order, so results are
-// deterministic: warps through shared memory, K-slices (ks > 1) by the last
-// CTA of a row group, which reads every slice's partial in slice order.
-template <int FMT, int NT, int DEPTH>
-__global__ void __launch_bounds__(256) gemv_kernel(MatArgs m, XArgs x, int nt, float *__restrict__ y,
-                                                   int ks, float *__restrict__ part,
-                                                   int *__restrict__ counters)
-{
-    __shared__ float red[8][NT][16];
-    __shared__ int last;
-    const int rg = blockIdx.x, kz = blockIdx.y;
-    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ns = (m.row_bytes + 63) >> 6;
-    const int cb = (int)((long)kz * ns / ks), ce = (int)((long)(kz + 1) * ns / ks);
-    const int wb = cb + (int)((long)warp * (ce - cb) / nw);
-    const int we = cb + (int)((long)(warp + 1) * (ce - cb) / nw);
+// TMA-staged (tma_gemv.cuh): a CTA of 8 consumer warps + 1 producer covers R
+// rows x the full K as 8 streams of 16 rows x one of P = 8 / (R/16) K-parts;
+// the K-parts meet in shared memory in a fixed order, so results are
+// deterministic and no cross-CTA reduction is needed. R is chosen so the grid
+// fills about three CTAs per SM in a single wave.
+constexpr int GEMV_STAGES = 2, GEMV_THREADS = 288;
+using GemvSmem = TmaSmem<GEMV_STAGES>;
 
+template <int FMT, int NT>
+__global__ void __launch_bounds__(GEMV_THREADS, 3) gemv_tma_kernel(MatArgs m, const __grid_constant__ CUtensorMap tw,
+                                                                  const __grid_constant__ CUtensorMap ts, int staged,
+                                                                  XArgs x, int nt, int R, float *__restrict__ y,
+                                                                  int *__restrict__ err)
+{
+    extern __shared__ __align__(128) unsigned char dsmem[];
+    __shared__ Stream streams[8];
+    __shared__ float red[8][NT][16];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int P = 8 / (R >> 4);
+    const int row0 = blockIdx.x * R;
+    // K-part length: whole 256-byte stages (stage-aligned part starts)
+    const int L = (((m.row_bytes + P - 1) / P + TMA_SB - 1) / TMA_SB) * TMA_SB;
+    if (threadIdx.x < 8) {
+        Stream st;
+        st.m = m;
+        st.tw = &tw;
+        st.ts = staged ? &ts : nullptr;
+        st.row0 = row0 + (threadIdx.x / P) * 16;
+        st.kb0 = (threadIdx.x % P) * L;
+        streams[threadIdx.x] = st;
+    }
+    __syncthreads();
     for (int t0 = 0; t0 < nt; t0 += NT) {
-        float acc[NT][2];
-#pragma unroll
-        for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0f;
         XArgs xt = x;
         xt.xh += (size_t)t0 * x.ldx;
         xt.xl += (size_t)t0 * x.ldx;
         xt.xs += (size_t)t0 * (x.ldx >> 5);
-        gemv_tile16<FMT, NT, DEPTH>(m, rg * 16, wb, we, xt, nt - t0, acc);
+        float acc[NT][2];
 #pragma unroll
-        for (int t = 0; t < NT; t++) {
-            const float s0 = quad_sum(acc[t][0]), s1 = quad_sum(acc[t][1]);
-            if ((lane & 3) == 0) {
-                red[warp][t][lane >> 2] = s0;
-                red[warp][t][(lane >> 2) + 8] = s1;
+        for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0f;
+        tma_gemv_streams<FMT, NT, GEMV_STAGES>(dsmem, streams, L, xt, nt - t0, acc, err);
+        if (warp < 8) {
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                const float s0 = quad_sum(acc[t][0]), s1 = quad_sum(acc[t][1]);
+                if ((lane & 3) == 0) {
+                    red[warp][t][lane >> 2] = s0;
+                    red[warp][t][(lane >> 2) + 8] = s1;
+                }
             }
         }
         __syncthreads();
-        if (threadIdx.x < NT * 16) {
-            const int t = threadIdx.x >> 4, r = threadIdx.x & 15, row = rg * 16 + r;
-            float s = 0.0f;
-            for (int w = 0; w < nw; w++) s += red[w][t][r];
-            if (row < m.rows && t0 + t < nt) {
-                if (ks == 1) y[(size_t)(t0 + t) * m.rows + row] = s;
-                else part[((size_t)kz * nt + t0 + t) * m.rows + row] = s;
-            }
+        // rows of stream group w / P, K-parts summed in order
+        for (int i = threadIdx.x; i < NT * R; i += blockDim.x) {
+            const int t = i / R, r = i - t * R, grp = r >> 4, rr = r & 15, row = row0 + r;
+            float v = 0.0f;
+            for (int p = 0; p < P; p++) v += red[grp * P + p][t][rr];
+            if (row < m.rows && t0 + t < nt) y[(size_t)(t0 + t) * m.rows + row] = v;
         }
         __syncthreads();
     }
-    if (ks == 1) return;
-
-    // Last CTA of this row group sums the ks slices in order.
-    __threadfence();
-    if (threadIdx.x == 0) {
-        const int prev = atomicAdd(&counters[rg], 1);
-        last = (prev == ks - 1);
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    for (int i = threadIdx.x; i < nt * 16; i += blockDim.x) {
-        const int t = i >> 4, row = rg * 16 + (i & 15);
-        if (row >= m.rows) continue;
-        float s = 0.0f;
-        for (int z = 0; z < ks; z++) s += __ldcg(part + ((size_t)z * nt + t) * m.rows + row);
-        y[(size_t)t * m.rows + row] = s;
-    }
-    if (threadIdx.x == 0) counters[rg] = 0;
 }
 
 // ----------------------------------------------------------- generic path
@@ -211,38 +209,43 @@ int xprep_launch(const float *x, int cols, int ldx_in, int nt, int ldx, bool bf1
     return DSV4CU_OK;
 }
 
-template <int FMT>
-static int launch_fast(const MatArgs &m, const XArgs &x, int nt, float *y, int ks, float *part,
-                       int *counters, cudaStream_t st)
+// Rows per CTA: the smallest of 16/32/64/128 whose grid still fits in one
+// wave of three CTAs per SM (a second partial wave would double the tail).
+static int choose_rows(const MatArgs &m, int sm_count)
 {
-    const int rg = (m.rows + 15) / 16;
-    dim3 grid(rg, ks), block(256);
-    if (nt == 1)
-        gemv_kernel<FMT, 1, 2><<<grid, block, 0, st>>>(m, x, nt, y, ks, part, counters);
-    else if (nt == 2)
-        gemv_kernel<FMT, 2, 2><<<grid, block, 0, st>>>(m, x, nt, y, ks, part, counters);
-    else
-        gemv_kernel<FMT, 4, 2><<<grid, block, 0, st>>>(m, x, nt, y, ks, part, counters);
-    DSV4CU_LAUNCH_CHECK();
-    return DSV4CU_OK;
+    const int slots = 3 * sm_count;
+    for (int R = 16; R <= 128; R <<= 1)
+        if ((m.rows + R - 1) / R <= slots) return R;
+    return 128;
 }
 
-// Split-K factor: enough warps for ~32 per SM, at least 2 segments per warp.
-static int choose_ks(const MatArgs &m, int sm_count)
+template <int FMT>
+static int launch_fast(const dsv4cu_qmat *q, const MatArgs &m, const XArgs &x, int nt, float *y, int sm_count,
+                       int *err, cudaStream_t st)
 {
-    const int rg = (m.rows + 15) / 16, ns = (m.row_bytes + 63) / 64;
-    int ks = (sm_count * 32) / (rg * 8);
-    const int maxks = ns / 16;   // >= 2 segments per warp of 8
-    if (ks > maxks) ks = maxks;
-    if (ks < 1) ks = 1;
-    if (ks > 64) ks = 64;
-    return ks;
+    CUtensorMap tw, ts;
+    memset(&ts, 0, sizeof ts);
+    int staged = 0;
+    int r = tmap_encode(q, &tw, &ts, &staged);
+    if (r) return r;
+    const int R = choose_rows(m, sm_count);
+    const int grid = (m.rows + R - 1) / R;
+    const int smem = GemvSmem::BYTES;
+    if (nt == 1) {
+        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(gemv_tma_kernel<FMT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        gemv_tma_kernel<FMT, 1><<<grid, GEMV_THREADS, smem, st>>>(m, tw, ts, staged, x, nt, R, y, err);
+    } else {
+        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(gemv_tma_kernel<FMT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        gemv_tma_kernel<FMT, 4><<<grid, GEMV_THREADS, smem, st>>>(m, tw, ts, staged, x, nt, R, y, err);
+    }
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
 }
 
 // The fast path issues 16-byte weight loads: it needs a 16-byte aligned base.
 static bool fast_ok(const dsv4cu_qmat *q)
 {
-    return fast_geometry(q->wdt, q->cols, q->blk_r, q->blk_c) && ((uintptr_t)q->w & 15u) == 0;
+    return fast_geometry(q->wdt, q->cols, q->blk_r, q->blk_c) && tmap_weights_ok(q);
 }
 
 size_t mmq_workspace(const dsv4cu_qmat *q, int nt, int sm_count)
@@ -251,9 +254,6 @@ size_t mmq_workspace(const dsv4cu_qmat *q, int nt, int sm_count)
     if (!fast_ok(q)) return 0;
     const size_t ldx = (size_t)((q->cols + 31) / 32) * 32;
     size_t b = dsv4cu_align256(nt * ldx * 2) * 2 + dsv4cu_align256(nt * (ldx / 32) * 4);
-    const MatArgs m = mat_args(q);
-    const int ks = choose_ks(m, sm_count);
-    if (ks > 1) b += dsv4cu_align256((size_t)ks * nt * q->rows * 4);
     return b;
 }
 
@@ -283,16 +283,15 @@ int mmq_run(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *q, int
     float *xs = (float *)p;
     xa.xs = xs;
     p += dsv4cu_align256((size_t)nt * (ldx / 32) * 4);
-    float *part = (float *)p;
+    (void)counters;
+    int *err = ctx->status;
     int r = xprep_launch(x, q->cols, q->cols, nt, ldx, q->wdt == DSV4CU_WBF16, xh, xl, xs, st);
     if (r) return r;
-    const int ks = choose_ks(m, ctx ? ctx->sm_count : 148);
-    if (ks > 1 && (m.rows + 15) / 16 > DSV4CU_MAX_COUNTERS)
-        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "mmq: too many row groups");
+    const int sms = ctx ? ctx->sm_count : 148;
     switch (q->wdt) {
-    case DSV4CU_WFP8: return launch_fast<DSV4CU_WFP8>(m, xa, nt, y, ks, part, counters, st);
-    case DSV4CU_WFP4: return launch_fast<DSV4CU_WFP4>(m, xa, nt, y, ks, part, counters, st);
-    default: return launch_fast<DSV4CU_WBF16>(m, xa, nt, y, ks, part, counters, st);
+    case DSV4CU_WFP8: return launch_fast<DSV4CU_WFP8>(q, m, xa, nt, y, sms, err, st);
+    case DSV4CU_WFP4: return launch_fast<DSV4CU_WFP4>(q, m, xa, nt, y, sms, err, st);
+    default: return launch_fast<DSV4CU_WBF16>(q, m, xa, nt, y, sms, err, st);
     }
 }
 

@@ -1,19 +1,54 @@
 // misc.cu - router, SwiGLU, index offset, weight quantizers, synthetic fill.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "ctx.h"
 #include "router.cuh"
+#include <string.h>
 
 namespace dsv4cu {
 
-__global__ void route_kernel(int *idx, float *wts, float *scores, float *orig, const float *logits,
+// sqrtf(softplus(x)) for every bf16 bit pattern x (src/10_compute/dsv4_ops.c:43-46,
+// :123), filled from the host C library once per device.
+__device__ float g_router_bf16[65536];
+
+const float *router_table_get()
+{
+    static std::mutex mu;
+    static bool ready[256];
+    static float host[65536];
+    static bool host_ready = false;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return nullptr;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!host_ready) {
+        for (uint32_t u = 0; u < 65536u; u++) {
+            const uint32_t b = u << 16;
+            float x;
+            memcpy(&x, &b, 4);
+            const float sp = (x > 20.0f) ? x : log1pf(expf(x));
+            host[u] = sqrtf(sp);
+        }
+        host_ready = true;
+    }
+    if (!ready[dev]) {
+        if (cudaMemcpyToSymbol(g_router_bf16, host, sizeof host) != cudaSuccess) return nullptr;
+        ready[dev] = true;
+    }
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_router_bf16) != cudaSuccess) return nullptr;
+    return (const float *)p;
+}
+
+__global__ void route_kernel(const float *tab, int *idx, float *wts, float *scores, float *orig, const float *logits,
                              const float *bias, const int64_t *tid2eid, const int *token_ids, int n_experts,
                              int topk, float route_scale, int nt)
 {
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= nt) return;
-    route_token_warp(logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0, n_experts,
+    route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0, n_experts,
                      topk, route_scale, idx + (size_t)t * topk, wts + (size_t)t * topk,
                      scores ? scores + (size_t)t * n_experts : nullptr,
                      orig ? orig + (size_t)t * n_experts : nullptr);
@@ -156,7 +191,9 @@ extern "C" int dsv4cu_route(int *idx, float *wts, float *scores, float *orig, co
     if (!tid2eid && topk > n_experts) return dsv4cu_set_error(DSV4CU_ERR_ARG, "route: topk > n_experts");
     if (tid2eid && !token_ids) return dsv4cu_set_error(DSV4CU_ERR_ARG, "route: hash routing needs token_ids");
     if (nt <= 0) return DSV4CU_OK;
-    route_kernel<<<(nt + 3) / 4, 128, 0, (cudaStream_t)stream>>>(idx, wts, scores, orig, logits, bias, tid2eid,
+    const float *tab = router_table_get();
+    if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "route: router table setup failed");
+    route_kernel<<<(nt + 3) / 4, 128, 0, (cudaStream_t)stream>>>(tab, idx, wts, scores, orig, logits, bias, tid2eid,
                                                                   token_ids, n_experts, topk, route_scale, nt);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;

@@ -17,13 +17,22 @@
 //             vectors -> per-pair partial rows. The last CTA of a row slice sums
 //             the pairs of every token in k order, then adds the shared expert.
 // Every weight byte of the touched experts is read exactly once per step.
+//
+// The experts are prepared once (dsv4cu_moe_create): descriptors validated and
+// copied to the device, and one TMA tensor map per weight matrix (and per FP4
+// scale grid) encoded, so the phase kernels stream weights with tensor-map TMA.
 #include <stdio.h>
+#include <string.h>
+
+#include <vector>
 
 #include "common.cuh"
 #include "ctx.h"
 #include "gemv.h"
 #include "gemv_core.cuh"
 #include "router.cuh"
+#include "tma_gemv.cuh"
+#include "tmap.h"
 
 namespace dsv4cu {
 
@@ -35,7 +44,7 @@ struct MoeWs {
     float *xs;            // [nt][hidden/32]
     int *idx;             // [nt][topk]
     float *wts;           // [nt][topk]
-    int *meta;            // [0] n_buckets, [1] error flag
+    int *meta;            // [0] n_buckets, [1] bad-route flag
     int *b_expert;        // [nbmax]
     int *b_off;           // [nbmax + 2]
     int *b_tok;           // [npairs] token of each bucket slot (shared slots at the end)
@@ -47,7 +56,7 @@ struct MoeWs {
 
 // ------------------------------------------------------------- prologue
 __global__ void __launch_bounds__(1024) moe_prologue_kernel(
-    const float *__restrict__ x, const float *__restrict__ logits, const float *__restrict__ bias,
+    const float *__restrict__ tab, const float *__restrict__ x, const float *__restrict__ logits, const float *__restrict__ bias,
     const int64_t *__restrict__ tid2eid, const int *__restrict__ token_ids, int n_experts, int topk,
     float route_scale, int hidden, int nt, int has_shared, MoeWs ws, int *__restrict__ idx_out,
     float *__restrict__ wts_out)
@@ -81,7 +90,7 @@ __global__ void __launch_bounds__(1024) moe_prologue_kernel(
 
     // CTA 0: routing, one warp per token.
     for (int t = warp; t < nt; t += nwarps) {
-        route_token_warp(logits + (size_t)t * n_experts, bias, tid2eid,
+        route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid,
                          token_ids ? token_ids[t] : 0, n_experts, topk, route_scale,
                          ws.idx + t * topk, ws.wts + t * topk, nullptr, nullptr);
     }
@@ -137,45 +146,44 @@ __global__ void __launch_bounds__(1024) moe_prologue_kernel(
         }
 }
 
-// Resolve bucket b of this launch: expert descriptor, first slot, slot count.
-DSV4CU_DEV bool mat_ok(const dsv4cu_qmat &q, int rows, int cols)
-{
-    if (q.rows != rows || q.cols != cols || !q.w || !q.s || q.blk_r <= 0 || q.blk_c <= 0) return false;
-    if ((uintptr_t)q.w & 15u) return false;   // 16-byte weight loads
-    if (q.wdt == DSV4CU_WFP4) return q.blk_c % 32 == 0;
-    if (q.wdt == DSV4CU_WFP8) return q.blk_c % 16 == 0;
-    return false;
-}
 
-DSV4CU_DEV bool expert_ok(const dsv4cu_expert &e, int hidden, int inter)
-{
-    return mat_ok(e.w1, inter, hidden) && mat_ok(e.w3, inter, hidden) && mat_ok(e.w2, hidden, inter) &&
-           e.w1.wdt == e.w3.wdt;
-}
+// --------------------------------------------------------- prepared layer
+// Device view of a prepared layer: expert e (e == n_experts is the shared
+// expert) has matrices m = 0 (w1), 1 (w3), 2 (w2); maps[6e + 2m] is the weight
+// map, maps[6e + 2m + 1] the FP4 scale map, valid when staged[3e + m].
+struct MoeDev {
+    const dsv4cu_expert *experts;   // [n_experts + 1], shared last
+    const CUtensorMap *maps;
+    const int *staged;
+    int n_experts, has_shared;
+};
 
-DSV4CU_DEV bool moe_bucket(const MoeWs &ws, int b, int nbmax, const dsv4cu_expert *experts,
-                           const dsv4cu_expert &shared, int has_shared, int hidden, int inter,
-                           const dsv4cu_expert *&ex, int &s0, int &cnt)
+}  // namespace dsv4cu
+
+struct dsv4cu_moe {
+    int n_experts, hidden, inter, has_shared, device;
+    void *dev_block;                // experts + maps + staged, one allocation
+    dsv4cu::MoeDev view;
+};
+
+namespace dsv4cu {
+
+// Resolve bucket b of this launch: expert index (n_experts = shared), first
+// slot and slot count.
+DSV4CU_DEV bool moe_bucket(const MoeWs &ws, const MoeDev &L, int b, int nbmax, int &e, int &s0, int &cnt)
 {
     const int nb = ws.meta[0];
     if (b == nbmax) {            // the shared-expert bucket is always the last one
-        if (!has_shared) return false;
-        ex = &shared;
+        if (!L.has_shared) return false;
+        e = L.n_experts;
         s0 = ws.b_off[nb];
         cnt = ws.b_off[nb + 1] - s0;
         return cnt > 0;
     }
     if (b >= nb) return false;
-    ex = experts + ws.b_expert[b];
+    e = ws.b_expert[b];
     s0 = ws.b_off[b];
     cnt = ws.b_off[b + 1] - s0;
-    // Routed descriptors live in device memory and are checked here: a
-    // descriptor whose shape or format this kernel cannot read is skipped and
-    // flagged (meta[1] bit 1), never read out of shape.
-    if (!expert_ok(*ex, hidden, inter)) {
-        atomicOr(ws.meta + 1, 2);
-        return false;
-    }
     return true;
 }
 
@@ -193,168 +201,166 @@ DSV4CU_DEV MatArgs mat_of(const dsv4cu_qmat &q)
     return m;
 }
 
-template <int FMT, int NT>
-DSV4CU_DEV void moe_gate_up_body(const dsv4cu_expert &ex, int row0, const XArgs &xa, int nvalid,
-                                 float (*red)[2][2][4][16], int warp)
+DSV4CU_DEV Stream moe_stream(const MoeDev &L, int e, int mat, int row0, int kb0)
 {
-    // warp -> (matrix w1|w3, 16-row half, K half)
-    const int mat = (warp >> 2) & 1, rs = (warp >> 1) & 1, kh = warp & 1;
-    const MatArgs m = mat_of(mat ? ex.w3 : ex.w1);
-    const int ns = (m.row_bytes + 63) >> 6;
-    const int sb = kh * ns / 2, se = (kh + 1) * ns / 2;
-    float acc[NT][2];
-#pragma unroll
-    for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0f;
-    gemv_tile16<FMT, NT, 2>(m, row0 + rs * 16, sb, se, xa, nvalid, acc);
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int t = 0; t < NT; t++) {
-        const float s0 = quad_sum(acc[t][0]), s1 = quad_sum(acc[t][1]);
-        if ((lane & 3) == 0) {
-            red[mat][rs][kh][t][lane >> 2] = s0;
-            red[mat][rs][kh][t][(lane >> 2) + 8] = s1;
-        }
-    }
+    const dsv4cu_expert &ex = L.experts[e];
+    Stream st;
+    st.m = mat_of(mat == 0 ? ex.w1 : (mat == 1 ? ex.w3 : ex.w2));
+    st.tw = L.maps + 6 * e + 2 * mat;
+    st.ts = L.staged[3 * e + mat] ? L.maps + 6 * e + 2 * mat + 1 : nullptr;
+    st.row0 = row0;
+    st.kb0 = kb0;
+    return st;
 }
 
-// grid (inter/32, nbmax + 1), block 256 (8 warps).
-__global__ void __launch_bounds__(256) moe_gate_up_kernel(MoeWs ws, const dsv4cu_expert *__restrict__ experts,
-                                                          dsv4cu_expert shared, int has_shared, int nbmax,
-                                                          int hidden, int inter, float limit)
+// ---------------------------------------------------------------- phases
+// Both phases run on a 1-D grid of CTAs of 8 consumer warps + 1 TMA producer
+// warp (tma_gemv.cuh), sized for three CTAs per SM so the whole grid of a
+// decode step is resident in one wave. A CTA owns a row block of one bucket's
+// matrix; the block is sized by the weight format so every CTA streams the
+// same bytes: FP4 rows are half the bytes of FP8 rows, so FP4 blocks are twice
+// as tall, and the 8 warps cover them as 16-row x full-K streams (tall block)
+// or 16-row x K-half streams (short block).
+constexpr int P1_ROWS_FP4 = 64, P1_ROWS_FP8 = 32;    // phase 1: rows of w1 (and of w3) per CTA
+constexpr int P2_ROWS_FP4 = 128, P2_ROWS_FP8 = 64;   // phase 2: w2 rows per CTA
+constexpr int MOE_STAGES = 2;
+using MoeSmem = TmaSmem<MOE_STAGES>;
+constexpr int MOE_THREADS = 288;
+
+// CTA id -> (bucket, first row, rows) over the routed buckets then the shared one.
+DSV4CU_DEV bool moe_cta_work(int cta, int nbmax, int rows_total, int rows_routed, int rows_shared,
+                             int &bucket, int &row0, int &nrows)
 {
-    __shared__ float red[2][2][2][4][16];   // [mat][row half][K half][token][row]
-    __shared__ float mid[4][32];
-    const dsv4cu_expert *ex;
-    int s0, cnt;
-    if (!moe_bucket(ws, blockIdx.y, nbmax, experts, shared, has_shared, hidden, inter, ex, s0, cnt)) return;
+    const int per_routed = rows_total / rows_routed;
+    if (cta < nbmax * per_routed) {
+        bucket = cta / per_routed;
+        row0 = (cta - bucket * per_routed) * rows_routed;
+        nrows = rows_routed;
+        return true;
+    }
+    cta -= nbmax * per_routed;
+    if (cta >= rows_total / rows_shared) return false;
+    bucket = nbmax;
+    row0 = cta * rows_shared;
+    nrows = rows_shared;
+    return true;
+}
+
+template <int NT>
+DSV4CU_DEV void moe_run_streams(int fmt, unsigned char *dsmem, const Stream *streams, int L, const XArgs &xa, int nv,
+                                float (&acc)[NT][2], int *err)
+{
+    if (fmt == DSV4CU_WFP4)
+        tma_gemv_streams<DSV4CU_WFP4, NT, MOE_STAGES>(dsmem, streams, L, xa, nv, acc, err);
+    else
+        tma_gemv_streams<DSV4CU_WFP8, NT, MOE_STAGES>(dsmem, streams, L, xa, nv, acc, err);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(MOE_THREADS, NT == 1 ? 3 : 2)
+    moe_gate_up_kernel(MoeWs ws, MoeDev Ld, int nbmax, int hidden, int inter, float limit, int *status)
+{
+    extern __shared__ __align__(128) unsigned char dsmem[];
+    __shared__ Stream streams[8];
+    __shared__ float red[2][4][2][NT][16];   // [mat][row group][K part][token][row]
+    __shared__ float mid[NT][64];
+    int bucket, row0, rows;
+    if (!moe_cta_work(blockIdx.x, nbmax, inter, P1_ROWS_FP4, P1_ROWS_FP8, bucket, row0, rows)) return;
+    int e, s0, cnt;
+    if (!moe_bucket(ws, Ld, bucket, nbmax, e, s0, cnt)) return;
+    const int fmt = Ld.experts[e].w1.wdt;
+    // A bucket of the other format than its grid slot was laid out for covers
+    // the slot in blocks of its own height.
+    const int want = min(rows, (fmt == DSV4CU_WFP4) ? P1_ROWS_FP4 : P1_ROWS_FP8);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row0 = blockIdx.x * 32;
-    const int fmt = ex->w1.wdt;
+    int *err = status;
 
-    for (int c0 = 0; c0 < cnt; c0 += 4) {
-        const int nv = min(4, cnt - c0);
-        XArgs xa;
-        xa.xh = ws.xh;
-        xa.xl = ws.xl;
-        xa.xs = ws.xs;
-        xa.ldx = hidden;
-        xa.tok = ws.b_tok + s0 + c0;
-        if (fmt == DSV4CU_WFP4) {
-            if (nv == 1) moe_gate_up_body<DSV4CU_WFP4, 1>(*ex, row0, xa, nv, red, warp);
-            else moe_gate_up_body<DSV4CU_WFP4, 4>(*ex, row0, xa, nv, red, warp);
-        } else {
-            if (nv == 1) moe_gate_up_body<DSV4CU_WFP8, 1>(*ex, row0, xa, nv, red, warp);
-            else moe_gate_up_body<DSV4CU_WFP8, 4>(*ex, row0, xa, nv, red, warp);
+    for (int r0 = row0; r0 < row0 + rows; r0 += want) {
+        const int nrow = want;                        // 64 (full-K streams) or 32 (K halves)
+        const int nk = nrow == 64 ? 1 : 2;
+        if (threadIdx.x < 8) {
+            const int w = threadIdx.x, mat = w >> 2;
+            const int rg = nk == 1 ? (w & 3) : ((w >> 1) & 1), kp = nk == 1 ? 0 : (w & 1);
+            const int rb = Ld.experts[e].w1.wdt == DSV4CU_WFP4 ? hidden / 2 : hidden;
+            streams[w] = moe_stream(Ld, e, mat, r0 + rg * 16, kp * (rb / nk));
         }
         __syncthreads();
-        // SwiGLU (dsv4_ops.c:61-79): up clamped both ways, gate from above only.
-        if (threadIdx.x < nv * 32) {
-            const int t = threadIdx.x >> 5, r = threadIdx.x & 31, rs = r >> 4, rr = r & 15;
-            const float g0 = red[0][rs][0][t][rr] + red[0][rs][1][t][rr];
-            const float u0 = red[1][rs][0][t][rr] + red[1][rs][1][t][rr];
-            float g = g0, u = u0;
-            if (limit > 0.0f) {
-                u = fminf(fmaxf(u, -limit), limit);
-                g = fminf(g, limit);
-            }
-            mid[t][r] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-        }
-        __syncthreads();
-        // mid -> f16 hi/lo operand for phase 2; one warp per token, lane = row.
-        if (warp < nv) {
-            const int t = warp, slot = s0 + c0 + t;
-            const float v = mid[t][lane];
-            float a = isfinite(v) ? fabsf(v) : 0.0f;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
-            int P = 0;
-            if (a > 0.0f) {
-                int e;
-                frexpf(a, &e);
-                P = min(125, max(-125, 15 - e));
-            }
-            const float vs = ldexpf(v, P);
-            const __half hh = __float2half_rn(vs);
-            const float hf = __half2float(hh);
-            const __half lh = isfinite(hf) ? __float2half_rn(vs - hf) : __float2half_rn(0.0f);
-            ws.mh[(size_t)slot * inter + row0 + lane] = __half_as_ushort(hh);
-            ws.ml[(size_t)slot * inter + row0 + lane] = __half_as_ushort(lh);
-            if (lane == 0) ws.mxs[(size_t)slot * (inter >> 5) + (row0 >> 5)] = ldexpf(1.0f, -P);
-        }
-        __syncthreads();
-    }
-}
-
-template <int FMT, int NT>
-DSV4CU_DEV void moe_down_body(const dsv4cu_qmat &q, int row0, const XArgs &xa, int nvalid,
-                              float (*red)[4][16], int warp, int nw)
-{
-    const MatArgs m = mat_of(q);
-    const int ns = (m.row_bytes + 63) >> 6;
-    const int sb = warp * ns / nw, se = (warp + 1) * ns / nw;
-    float acc[NT][2];
-#pragma unroll
-    for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0f;
-    gemv_tile16<FMT, NT, 2>(m, row0, sb, se, xa, nvalid, acc);
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int t = 0; t < NT; t++) {
-        const float s0 = quad_sum(acc[t][0]), s1 = quad_sum(acc[t][1]);
-        if ((lane & 3) == 0) {
-            red[warp][t][lane >> 2] = s0;
-            red[warp][t][(lane >> 2) + 8] = s1;
-        }
-    }
-}
-
-// grid (hidden/16, nbmax + 1), block 128 (4 warps splitting K).
-__global__ void __launch_bounds__(128) moe_down_kernel(MoeWs ws, const dsv4cu_expert *__restrict__ experts,
-                                                       dsv4cu_expert shared, int has_shared, int nbmax,
-                                                       int hidden, int inter, int nt, int topk,
-                                                       float *__restrict__ out, int *__restrict__ counters)
-{
-    __shared__ float red[4][4][16];
-    __shared__ int last;
-    const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const int row0 = blockIdx.x * 16;
-    const dsv4cu_expert *ex;
-    int s0, cnt;
-    if (moe_bucket(ws, blockIdx.y, nbmax, experts, shared, has_shared, hidden, inter, ex, s0, cnt)) {
-        const int fmt = ex->w2.wdt;
-        for (int c0 = 0; c0 < cnt; c0 += 4) {
-            const int nv = min(4, cnt - c0);
+        const int L = streams[0].m.row_bytes / nk;
+        for (int c0 = 0; c0 < cnt; c0 += NT) {
+            const int nv = min(NT, cnt - c0);
             XArgs xa;
-            xa.xh = ws.mh + (size_t)(s0 + c0) * inter;
-            xa.xl = ws.ml + (size_t)(s0 + c0) * inter;
-            xa.xs = ws.mxs + (size_t)(s0 + c0) * (inter >> 5);
-            xa.ldx = inter;
-            xa.tok = nullptr;
-            if (fmt == DSV4CU_WFP4) {
-                if (nv == 1) moe_down_body<DSV4CU_WFP4, 1>(ex->w2, row0, xa, nv, red, warp, nw);
-                else moe_down_body<DSV4CU_WFP4, 4>(ex->w2, row0, xa, nv, red, warp, nw);
-            } else {
-                if (nv == 1) moe_down_body<DSV4CU_WFP8, 1>(ex->w2, row0, xa, nv, red, warp, nw);
-                else moe_down_body<DSV4CU_WFP8, 4>(ex->w2, row0, xa, nv, red, warp, nw);
+            xa.xh = ws.xh;
+            xa.xl = ws.xl;
+            xa.xs = ws.xs;
+            xa.ldx = hidden;
+            xa.tok = ws.b_tok + s0 + c0;
+            float acc[NT][2];
+#pragma unroll
+            for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0f;
+            moe_run_streams<NT>(fmt, dsmem, streams, L, xa, nv, acc, err);
+            if (warp < 8) {
+                const int mat = warp >> 2;
+                const int rg = nk == 1 ? (warp & 3) : ((warp >> 1) & 1), kp = nk == 1 ? 0 : (warp & 1);
+#pragma unroll
+                for (int t = 0; t < NT; t++) {
+                    const float v0 = quad_sum(acc[t][0]), v1 = quad_sum(acc[t][1]);
+                    if ((lane & 3) == 0) {
+                        red[mat][rg][kp][t][lane >> 2] = v0;
+                        red[mat][rg][kp][t][(lane >> 2) + 8] = v1;
+                    }
+                }
             }
             __syncthreads();
-            if (threadIdx.x < nv * 16) {
-                const int t = threadIdx.x >> 4, r = threadIdx.x & 15;
-                float s = 0.0f;
-                for (int w = 0; w < nw; w++) s += red[w][t][r];
-                ws.ypart[(size_t)(s0 + c0 + t) * hidden + row0 + r] = s;
+            // SwiGLU (dsv4_ops.c:61-79): up clamped both ways, gate from above only.
+            if (threadIdx.x < nv * nrow) {
+                const int t = threadIdx.x / nrow, r = threadIdx.x - t * nrow, rg = r >> 4, rr = r & 15;
+                float g = red[0][rg][0][t][rr], u = red[1][rg][0][t][rr];
+                if (nk == 2) {
+                    g += red[0][rg][1][t][rr];
+                    u += red[1][rg][1][t][rr];
+                }
+                if (limit > 0.0f) {
+                    u = fminf(fmaxf(u, -limit), limit);
+                    g = fminf(g, limit);
+                }
+                mid[t][r] = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+            }
+            __syncthreads();
+            // mid -> f16 hi/lo operand for phase 2: one warp per (token, 32 rows).
+            if (warp < nv * (nrow >> 5)) {
+                const int t = warp / (nrow >> 5), half = warp - t * (nrow >> 5), slot = s0 + c0 + t;
+                const int rr = half * 32 + lane, row = r0 + rr;
+                const float v = mid[t][rr];
+                float a = isfinite(v) ? fabsf(v) : 0.0f;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+                int P = 0;
+                if (a > 0.0f) {
+                    int ex2;
+                    frexpf(a, &ex2);
+                    P = min(125, max(-125, 15 - ex2));
+                }
+                const float vs = ldexpf(v, P);
+                const __half hh = __float2half_rn(vs);
+                const float hf = __half2float(hh);
+                const __half lh = isfinite(hf) ? __float2half_rn(vs - hf) : __float2half_rn(0.0f);
+                ws.mh[(size_t)slot * inter + row] = __half_as_ushort(hh);
+                ws.ml[(size_t)slot * inter + row] = __half_as_ushort(lh);
+                if (lane == 0) ws.mxs[(size_t)slot * (inter >> 5) + (row >> 5)] = ldexpf(1.0f, -P);
             }
             __syncthreads();
         }
     }
-    // The last CTA of this 16-row slice combines, in k order, then the shared expert.
-    __threadfence();
-    if (threadIdx.x == 0) last = (atomicAdd(&counters[blockIdx.x], 1) == (int)gridDim.y - 1);
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
+}
+
+// Combine of one 64-row slice of the output: the routed pairs of every token
+// IN k ORDER (dsv4_layer.c:109-113), then the shared expert unweighted (:115).
+DSV4CU_DEV void moe_combine_slice(const MoeWs &ws, int row0, int nt, int topk, int hidden, int has_shared,
+                                  float *__restrict__ out)
+{
     const int nb = ws.meta[0];
-    for (int i = threadIdx.x; i < nt * 16; i += blockDim.x) {
-        const int t = i >> 4, row = row0 + (i & 15);
+    for (int i = threadIdx.x; i < nt * 64; i += blockDim.x) {
+        const int t = i >> 6, row = row0 + (i & 63);
         float o = 0.0f;
         for (int k = 0; k < topk; k++) {
             const int slot = __ldcg(ws.pos + t * topk + k);
@@ -366,7 +372,86 @@ __global__ void __launch_bounds__(128) moe_down_kernel(MoeWs ws, const dsv4cu_ex
             o = __fadd_rn(o, __ldcg(ws.ypart + (size_t)(__ldcg(ws.b_off + nb) + t) * hidden + row));
         out[(size_t)t * hidden + row] = o;
     }
-    if (threadIdx.x == 0) counters[blockIdx.x] = 0;
+}
+
+// counters[s] counts the CTAs that have written 64-row slice s; the last of
+// the (nbmax + has_shared) contributions combines the slice and resets it.
+template <int NT>
+__global__ void __launch_bounds__(MOE_THREADS, NT == 1 ? 3 : 2)
+    moe_down_kernel(MoeWs ws, MoeDev Ld, int nbmax, int hidden, int inter, int nt, int topk,
+                    float *__restrict__ out, int *__restrict__ counters, int *status)
+{
+    extern __shared__ __align__(128) unsigned char dsmem[];
+    __shared__ Stream streams[8];
+    __shared__ float red[8][2][NT][16];
+    __shared__ int last[2];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int bucket, row0, rows;
+    if (!moe_cta_work(blockIdx.x, nbmax, hidden, P2_ROWS_FP4, P2_ROWS_FP8, bucket, row0, rows)) return;
+    int e, s0, cnt;
+    int *err = status;
+    if (moe_bucket(ws, Ld, bucket, nbmax, e, s0, cnt)) {
+        const int fmt = Ld.experts[e].w2.wdt;
+        const int want = min(rows, (fmt == DSV4CU_WFP4) ? P2_ROWS_FP4 : P2_ROWS_FP8);
+        for (int r0 = row0; r0 < row0 + rows; r0 += want) {
+            const int nrow = want;                    // 128 (full-K streams) or 64 (K halves)
+            const int nk = nrow == 128 ? 1 : 2;
+            if (threadIdx.x < 8) {
+                const int w = threadIdx.x;
+                const int rg = nk == 1 ? w : (w >> 1), kp = nk == 1 ? 0 : (w & 1);
+                const int rb = fmt == DSV4CU_WFP4 ? inter / 2 : inter;
+                streams[w] = moe_stream(Ld, e, 2, r0 + rg * 16, kp * (rb / nk));
+            }
+            __syncthreads();
+            const int L = streams[0].m.row_bytes / nk;
+            for (int c0 = 0; c0 < cnt; c0 += NT) {
+                const int nv = min(NT, cnt - c0);
+                XArgs xa;
+                xa.xh = ws.mh + (size_t)(s0 + c0) * inter;
+                xa.xl = ws.ml + (size_t)(s0 + c0) * inter;
+                xa.xs = ws.mxs + (size_t)(s0 + c0) * (inter >> 5);
+                xa.ldx = inter;
+                xa.tok = nullptr;
+                float acc[NT][2];
+#pragma unroll
+                for (int t = 0; t < NT; t++) acc[t][0] = acc[t][1] = 0.0f;
+                moe_run_streams<NT>(fmt, dsmem, streams, L, xa, nv, acc, err);
+                if (warp < 8) {
+                    const int rg = nk == 1 ? warp : (warp >> 1), kp = nk == 1 ? 0 : (warp & 1);
+#pragma unroll
+                    for (int t = 0; t < NT; t++) {
+                        const float v0 = quad_sum(acc[t][0]), v1 = quad_sum(acc[t][1]);
+                        if ((lane & 3) == 0) {
+                            red[rg][kp][t][lane >> 2] = v0;
+                            red[rg][kp][t][(lane >> 2) + 8] = v1;
+                        }
+                    }
+                }
+                __syncthreads();
+                for (int i = threadIdx.x; i < nv * nrow; i += blockDim.x) {
+                    const int t = i / nrow, r = i - t * nrow, rg = r >> 4, rr = r & 15;
+                    float v = red[rg][0][t][rr];
+                    if (nk == 2) v += red[rg][1][t][rr];
+                    ws.ypart[(size_t)(s0 + c0 + t) * hidden + r0 + r] = v;
+                }
+                __syncthreads();
+            }
+        }
+    }
+    // Every CTA (idle ones included) reports each 64-row slice it covers.
+    __threadfence();
+    const int nslice = rows >> 6;
+    if (threadIdx.x < nslice) {
+        const int sl = (row0 >> 6) + threadIdx.x;
+        last[threadIdx.x] = (atomicAdd(&counters[sl], 1) == nbmax + Ld.has_shared - 1);
+    }
+    __syncthreads();
+    for (int i = 0; i < nslice; i++) {
+        if (!last[i]) continue;
+        __threadfence();
+        moe_combine_slice(ws, row0 + i * 64, nt, topk, hidden, Ld.has_shared, out);
+        if (threadIdx.x == 0) counters[(row0 >> 6) + i] = 0;
+    }
 }
 
 static size_t moe_ws_layout(int nt, int topk, int n_experts, int hidden, int inter, int has_shared,
@@ -399,62 +484,76 @@ static size_t moe_ws_layout(int nt, int topk, int n_experts, int hidden, int int
     return off;
 }
 
-int moe_decode_run(float *out, const float *x, const float *logits, const float *bias,
-                   const int64_t *tid2eid, const int *token_ids, const dsv4cu_expert *experts,
-                   int n_experts, const dsv4cu_expert *shared, int topk, float route_scale, int hidden,
-                   int inter, float limit, int nt, int *idx_out, float *wts_out, void *wsp,
-                   int *counters, cudaStream_t st, cudaEvent_t *ev = nullptr)
-{
-    const int has_shared = shared != nullptr;
-    MoeWs ws;
-    moe_ws_layout(nt, topk, n_experts, hidden, inter, has_shared, (char *)wsp, &ws);
-    const int nbmax = min(nt * topk, n_experts);
-    const int xblocks = min(64, max(1, nt * (hidden / 32) / 32));
-    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
-    moe_prologue_kernel<<<1 + xblocks, 1024, 0, st>>>(x, logits, bias, tid2eid, token_ids, n_experts,
-                                                      topk, route_scale, hidden, nt, has_shared, ws,
-                                                      idx_out, wts_out);
-    DSV4CU_LAUNCH_CHECK();
-    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
-    dsv4cu_expert sh{};
-    if (has_shared) sh = *shared;
-    moe_gate_up_kernel<<<dim3(inter / 32, nbmax + 1), 256, 0, st>>>(ws, experts, sh, has_shared, nbmax,
-                                                                    hidden, inter, limit);
-    DSV4CU_LAUNCH_CHECK();
-    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
-    moe_down_kernel<<<dim3(hidden / 16, nbmax + 1), 128, 0, st>>>(ws, experts, sh, has_shared, nbmax,
-                                                                  hidden, inter, nt, topk, out, counters);
-    DSV4CU_LAUNCH_CHECK();
-    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
-    return DSV4CU_OK;
-}
-
 size_t moe_decode_workspace(int nt, int topk, int n_experts, int hidden, int inter, int has_shared)
 {
     return moe_ws_layout(nt, topk, n_experts, hidden, inter, has_shared, nullptr, nullptr);
 }
 
-static bool moe_mat_ok(const dsv4cu_qmat &q, int rows, int cols)
+int moe_decode_run(const dsv4cu_moe *layer, float *out, const float *x, const float *logits, const float *bias,
+                   const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
+                   int *idx_out, float *wts_out, void *wsp, int *counters, int *status, cudaStream_t st,
+                   cudaEvent_t *ev)
 {
-    if (q.rows != rows || q.cols != cols || !q.w || !q.s || ((uintptr_t)q.w & 15u)) return false;
-    if (q.wdt == DSV4CU_WFP4) return q.blk_c > 0 && q.blk_c % 32 == 0 && q.blk_r > 0;
-    if (q.wdt == DSV4CU_WFP8) return q.blk_c > 0 && q.blk_c % 16 == 0 && q.blk_r > 0;
-    return false;
+    const int n_experts = layer->n_experts, hidden = layer->hidden, inter = layer->inter;
+    const int has_shared = layer->has_shared;
+    MoeWs ws;
+    moe_ws_layout(nt, topk, n_experts, hidden, inter, has_shared, (char *)wsp, &ws);
+    const int nbmax = min(nt * topk, n_experts);
+    const int xblocks = min(64, max(1, nt * (hidden / 32) / 32));
+    const float *tab = router_table_get();
+    if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_decode: router table setup failed");
+    const int smem = MoeSmem::BYTES;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
+    moe_prologue_kernel<<<1 + xblocks, 1024, 0, st>>>(tab, x, logits, bias, tid2eid, token_ids, n_experts,
+                                                      topk, route_scale, hidden, nt, has_shared, ws,
+                                                      idx_out, wts_out);
+    DSV4CU_LAUNCH_CHECK();
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
+    const int g1 = nbmax * (inter / P1_ROWS_FP4) + (has_shared ? inter / P1_ROWS_FP8 : 0);
+    const int g2 = nbmax * (hidden / P2_ROWS_FP4) + (has_shared ? hidden / P2_ROWS_FP8 : 0);
+    if (nt == 1) {
+        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(moe_gate_up_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        moe_gate_up_kernel<1><<<g1, MOE_THREADS, smem, st>>>(ws, layer->view, nbmax, hidden, inter, limit, status);
+    } else {
+        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(moe_gate_up_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        moe_gate_up_kernel<4><<<g1, MOE_THREADS, smem, st>>>(ws, layer->view, nbmax, hidden, inter, limit, status);
+    }
+    DSV4CU_LAUNCH_CHECK();
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
+    if (nt == 1) {
+        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(moe_down_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        moe_down_kernel<1><<<g2, MOE_THREADS, smem, st>>>(ws, layer->view, nbmax, hidden, inter, nt, topk, out,
+                                                          counters, status);
+    } else {
+        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(moe_down_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        moe_down_kernel<4><<<g2, MOE_THREADS, smem, st>>>(ws, layer->view, nbmax, hidden, inter, nt, topk, out,
+                                                          counters, status);
+    }
+    DSV4CU_LAUNCH_CHECK();
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
+    return DSV4CU_OK;
 }
 
-int moe_decode_check(const dsv4cu_expert *shared, int n_experts, int topk, int hidden, int inter, int nt)
+// Host-side validation of one expert: shapes, a format the kernels stream,
+// and a TMA-streamable weight layout.
+static int expert_check(const dsv4cu_expert &e, int hidden, int inter, const char *what)
 {
-    if (nt < 1 || nt > MOE_MAX_NT) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: nt %d not in 1..%d", nt, MOE_MAX_NT);
-    if (topk < 1 || topk > MOE_MAX_TOPK) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: topk %d", topk);
-    if (n_experts < topk || n_experts > 32 * RMAX_PER_LANE) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: n_experts %d", n_experts);
-    if (hidden % 32 || inter % 32 || hidden <= 0 || inter <= 0)
-        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: hidden/inter must be multiples of 32");
-    if (hidden / 16 > DSV4CU_MAX_COUNTERS) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: hidden too large");
-    if (shared) {
-        if (!moe_mat_ok(shared->w1, inter, hidden) || !moe_mat_ok(shared->w3, inter, hidden) ||
-            !moe_mat_ok(shared->w2, hidden, inter) || shared->w1.wdt != shared->w3.wdt)
-            return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: shared expert shapes/formats");
+    const dsv4cu_qmat *ms[3] = {&e.w1, &e.w3, &e.w2};
+    const int rows[3] = {inter, inter, hidden}, cols[3] = {hidden, hidden, inter};
+    for (int i = 0; i < 3; i++) {
+        const dsv4cu_qmat &q = *ms[i];
+        if (q.rows != rows[i] || q.cols != cols[i] || !q.w || !q.s)
+            return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_create: %s matrix %d shape %dx%d, want %dx%d", what, i,
+                                    q.rows, q.cols, rows[i], cols[i]);
+        const bool fmt_ok = (q.wdt == DSV4CU_WFP4 && q.blk_c > 0 && q.blk_c % 32 == 0 && q.blk_r > 0) ||
+                            (q.wdt == DSV4CU_WFP8 && q.blk_c > 0 && q.blk_c % 16 == 0 && q.blk_r > 0);
+        if (!fmt_ok)
+            return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_create: %s matrix %d format %d blk %dx%d", what, i,
+                                    q.wdt, q.blk_r, q.blk_c);
+        if (!tmap_weights_ok(&q))
+            return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_create: %s matrix %d not 16-byte aligned", what, i);
     }
+    if (e.w1.wdt != e.w3.wdt) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_create: %s w1/w3 formats differ", what);
     return DSV4CU_OK;
 }
 
@@ -462,31 +561,106 @@ int moe_decode_check(const dsv4cu_expert *shared, int n_experts, int topk, int h
 
 using namespace dsv4cu;
 
-extern "C" int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, float *out, const float *x, const float *logits,
-                                    const float *bias, const int64_t *tid2eid, const int *token_ids,
-                                    const dsv4cu_expert *experts, int n_experts, const dsv4cu_expert *shared,
-                                    int topk, float route_scale, int hidden, int inter, float limit, int nt,
-                                    int *idx_out, float *wts_out, void *stream, void **events)
+extern "C" int dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts, int n_experts,
+                                 const dsv4cu_expert *shared, int hidden, int inter)
 {
-    if (!ctx || !out || !x || !logits || !experts) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: NULL argument");
-    if ((idx_out == nullptr) != (wts_out == nullptr)) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: idx_out and wts_out go together");
-    if (tid2eid && !token_ids) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: hash routing needs token_ids");
-    int r = moe_decode_check(shared, n_experts, topk, hidden, inter, nt);
-    if (r) return r;
-    void *ws = nullptr;
-    r = dsv4cu_ws_get(ctx, moe_decode_workspace(nt, topk, n_experts, hidden, inter, shared != nullptr), &ws);
-    if (r) return r;
-    return moe_decode_run(out, x, logits, bias, tid2eid, token_ids, experts, n_experts, shared, topk,
-                          route_scale, hidden, inter, limit, nt, idx_out, wts_out, ws, ctx->counters,
-                          (cudaStream_t)stream, (cudaEvent_t *)events);
+    if (!out || !experts) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_create: NULL argument");
+    *out = nullptr;
+    if (n_experts < 1 || n_experts > 32 * RMAX_PER_LANE)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_create: n_experts %d", n_experts);
+    if (hidden % 128 || inter % 128 || hidden <= 0 || inter <= 0)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_create: hidden and inter must be multiples of 128");
+    if (hidden / 64 > DSV4CU_MAX_COUNTERS) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_create: hidden too large");
+    for (int e = 0; e < n_experts; e++) {
+        char what[32];
+        snprintf(what, sizeof what, "expert %d", e);
+        int r = expert_check(experts[e], hidden, inter, what);
+        if (r) return r;
+    }
+    if (shared) {
+        int r = expert_check(*shared, hidden, inter, "shared expert");
+        if (r) return r;
+    }
+    const int ne1 = n_experts + 1;
+    std::vector<dsv4cu_expert> hexp(experts, experts + n_experts);
+    hexp.push_back(shared ? *shared : experts[0]);
+    std::vector<CUtensorMap> maps((size_t)6 * ne1);
+    std::vector<int> staged((size_t)3 * ne1, 0);
+    memset(maps.data(), 0, maps.size() * sizeof(CUtensorMap));
+    for (int e = 0; e < ne1; e++) {
+        const dsv4cu_qmat *ms[3] = {&hexp[e].w1, &hexp[e].w3, &hexp[e].w2};
+        for (int m = 0; m < 3; m++) {
+            int r = tmap_encode(ms[m], &maps[6 * e + 2 * m], &maps[6 * e + 2 * m + 1], &staged[3 * e + m]);
+            if (r) return r;
+        }
+    }
+    const size_t b_exp = dsv4cu_align256(hexp.size() * sizeof(dsv4cu_expert));
+    const size_t b_map = dsv4cu_align256(maps.size() * sizeof(CUtensorMap));
+    const size_t b_stg = dsv4cu_align256(staged.size() * sizeof(int));
+    void *blk = nullptr;
+    cudaError_t ce = cudaMalloc(&blk, b_exp + b_map + b_stg);
+    if (ce != cudaSuccess) return dsv4cu_set_error(DSV4CU_ERR_NOMEM, "moe_create: %s", cudaGetErrorString(ce));
+    char *p = (char *)blk;
+    ce = cudaMemcpy(p, hexp.data(), hexp.size() * sizeof(dsv4cu_expert), cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(p + b_exp, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+    if (ce == cudaSuccess) ce = cudaMemcpy(p + b_exp + b_map, staged.data(), staged.size() * sizeof(int), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+        cudaFree(blk);
+        return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_create: %s", cudaGetErrorString(ce));
+    }
+    dsv4cu_moe *L = new dsv4cu_moe;
+    L->n_experts = n_experts;
+    L->hidden = hidden;
+    L->inter = inter;
+    L->has_shared = shared != nullptr;
+    cudaGetDevice(&L->device);
+    L->dev_block = blk;
+    L->view.experts = (const dsv4cu_expert *)p;
+    L->view.maps = (const CUtensorMap *)(p + b_exp);
+    L->view.staged = (const int *)(p + b_exp + b_map);
+    L->view.n_experts = n_experts;
+    L->view.has_shared = L->has_shared;
+    *out = L;
+    return DSV4CU_OK;
 }
 
-extern "C" int dsv4cu_moe_decode(dsv4cu_ctx *ctx, float *out, const float *x, const float *logits,
-                                 const float *bias, const int64_t *tid2eid, const int *token_ids,
-                                 const dsv4cu_expert *experts, int n_experts, const dsv4cu_expert *shared,
-                                 int topk, float route_scale, int hidden, int inter, float limit, int nt,
+extern "C" void dsv4cu_moe_destroy(dsv4cu_moe *L)
+{
+    if (!L) return;
+    cudaFree(L->dev_block);
+    delete L;
+}
+
+extern "C" size_t dsv4cu_moe_workspace(const dsv4cu_moe *L, int topk, int nt)
+{
+    return L ? moe_decode_workspace(nt, topk, L->n_experts, L->hidden, L->inter, L->has_shared) : 0;
+}
+
+extern "C" int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
+                                    const float *logits, const float *bias, const int64_t *tid2eid,
+                                    const int *token_ids, int topk, float route_scale, float limit, int nt,
+                                    int *idx_out, float *wts_out, void *stream, void **events)
+{
+    if (!ctx || !layer || !out || !x || !logits) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: NULL argument");
+    if ((idx_out == nullptr) != (wts_out == nullptr))
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: idx_out and wts_out go together");
+    if (tid2eid && !token_ids) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: hash routing needs token_ids");
+    if (nt < 1 || nt > MOE_MAX_NT) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: nt %d not in 1..%d", nt, MOE_MAX_NT);
+    if (topk < 1 || topk > MOE_MAX_TOPK || topk > layer->n_experts)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: topk %d", topk);
+    void *ws = nullptr;
+    int r = dsv4cu_ws_get(ctx, moe_decode_workspace(nt, topk, layer->n_experts, layer->hidden, layer->inter,
+                                                    layer->has_shared), &ws);
+    if (r) return r;
+    return moe_decode_run(layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt, idx_out,
+                          wts_out, ws, ctx->counters, ctx->status, (cudaStream_t)stream, (cudaEvent_t *)events);
+}
+
+extern "C" int dsv4cu_moe_decode(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
+                                 const float *logits, const float *bias, const int64_t *tid2eid,
+                                 const int *token_ids, int topk, float route_scale, float limit, int nt,
                                  int *idx_out, float *wts_out, void *stream)
 {
-    return dsv4cu_moe_decode_ev(ctx, out, x, logits, bias, tid2eid, token_ids, experts, n_experts, shared,
-                                topk, route_scale, hidden, inter, limit, nt, idx_out, wts_out, stream, nullptr);
+    return dsv4cu_moe_decode_ev(ctx, layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt,
+                                idx_out, wts_out, stream, nullptr);
 }

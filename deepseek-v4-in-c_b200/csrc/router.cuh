@@ -7,16 +7,28 @@
 //               argmax: strict '>' over e in increasing order, so ties go to
 //               the lower index and a NaN wins only as the first untaken entry
 //   wts[k]    = orig[idx[k]] * (float)(1 / double sum) * route_scale
-// expf and log1pf are evaluated in double and rounded once to float (the
-// correctly rounded value, which is what glibc returns outside rare hard
-// cases); sqrtf is IEEE-exact on both sides.
+// The score of a bf16-valued logit (every logit the configs feed: the router
+// input is bf16) is read from a 65536-entry table built once per device by
+// the host side of this library with the host C library's expf / log1pf /
+// sqrtf - the calls the reference makes - so it is the reference's value bit
+// for bit. glibc's log1pf is not correctly rounded (it differs from the
+// correctly rounded result on ~0.6% of bf16 inputs), so no device evaluation
+// can promise that. Any other fp32 logit is evaluated in double and rounded
+// once per function, which is the correctly rounded value and differs from
+// glibc by at most one ulp on those rare inputs.
 #pragma once
 #include "common.cuh"
 
 namespace dsv4cu {
 
-DSV4CU_DEV float router_score(float x)
+// Device address of the bf16 score table on the current device, building it
+// on first use (host computation + one copy). Returns nullptr on failure.
+const float *router_table_get();
+
+DSV4CU_DEV float router_score(float x, const float *__restrict__ tab)
 {
+    const uint32_t u = __float_as_uint(x);
+    if (tab && (u & 0xFFFFu) == 0u) return __ldg(tab + (u >> 16));
     float sp;
     if (x > 20.0f) {
         sp = x;
@@ -30,8 +42,8 @@ DSV4CU_DEV float router_score(float x)
 // One warp routes one token. n_experts <= 32 * RMAX_PER_LANE.
 constexpr int RMAX_PER_LANE = 16;
 
-DSV4CU_DEV void route_token_warp(const float *__restrict__ logits, const float *__restrict__ bias,
-                                 const int64_t *__restrict__ tid2eid, int token_id,
+DSV4CU_DEV void route_token_warp(const float *__restrict__ tab, const float *__restrict__ logits,
+                                 const float *__restrict__ bias, const int64_t *__restrict__ tid2eid, int token_id,
                                  int n_experts, int topk, float route_scale,
                                  int *__restrict__ idx_out, float *__restrict__ wts_out,
                                  float *__restrict__ scores_out, float *__restrict__ orig_out)
@@ -44,7 +56,7 @@ DSV4CU_DEV void route_token_warp(const float *__restrict__ logits, const float *
         const int e = lane + 32 * j;
         float o = 0.0f, s = 0.0f;
         if (e < n_experts) {
-            o = router_score(logits[e]);
+            o = router_score(logits[e], tab);
             s = bias ? __fadd_rn(o, bias[e]) : o;
             if (orig_out) orig_out[e] = o;
             if (scores_out) scores_out[e] = s;

@@ -58,14 +58,16 @@ def lib() -> C.CDLL:
             "dsv4cu_ctx_destroy": (None, [vp]),
             "dsv4cu_ctx_reserve": (i, [vp, sz]),
             "dsv4cu_ctx_workspace_bytes": (sz, [vp]),
+            "dsv4cu_ctx_status": (i, [vp, vp, C.POINTER(i)]),
             "dsv4cu_mmq_workspace": (sz, [vp, i]),
             "dsv4cu_mmq": (i, [vp, vp, vp, vp, i, vp]),
             "dsv4cu_route": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, i, f, i, vp]),
             "dsv4cu_swiglu": (i, [vp, vp, vp, i, f, vp]),
-            "dsv4cu_moe_decode": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, vp, i, f, i, i, f, i,
-                                      vp, vp, vp]),
-            "dsv4cu_moe_decode_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, vp, i, f, i, i, f, i,
-                                         vp, vp, vp, vp]),
+            "dsv4cu_moe_create": (i, [C.POINTER(vp), vp, i, vp, i, i]),
+            "dsv4cu_moe_destroy": (None, [vp]),
+            "dsv4cu_moe_workspace": (sz, [vp, i, i]),
+            "dsv4cu_moe_decode": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp]),
+            "dsv4cu_moe_decode_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp, vp]),
             "dsv4cu_indexer_score": (i, [vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_indexer_score_fp8": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]),
             "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
@@ -244,6 +246,11 @@ class Device:
     def stream(self):
         return self.torch.cuda.current_stream(self.device).cuda_stream
 
+    def check_status(self):
+        """Raise if a kernel of this context hit a bounded-wait timeout."""
+        code = C.c_int(0)
+        check(self.L.dsv4cu_ctx_status(self.ctx, self.stream(), C.byref(code)), "device status")
+
     @staticmethod
     def ptr(t):
         return None if t is None else t.data_ptr()
@@ -263,17 +270,29 @@ class Device:
                                   self.ptr(token_ids), ne, topk, route_scale, nt, self.stream()),
               "dsv4cu_route")
 
-    def moe_decode(self, out, x, logits, experts_dev, n_experts, shared: Expert | None, topk,
-                   route_scale, hidden, inter, limit, nt, idx_out=None, wts_out=None, bias=None,
-                   tid2eid=None, token_ids=None, stream=None):
-        check(self.L.dsv4cu_moe_decode(self.ctx, self.ptr(out), self.ptr(x), self.ptr(logits),
-                                       self.ptr(bias), self.ptr(tid2eid), self.ptr(token_ids),
-                                       self.ptr(experts_dev), n_experts,
-                                       None if shared is None else C.addressof(shared), topk,
-                                       route_scale, hidden, inter, limit, nt, self.ptr(idx_out),
-                                       self.ptr(wts_out),
-                                       self.stream() if stream is None else stream),
-              "dsv4cu_moe_decode")
+    def moe_create(self, experts: list, shared: Expert | None, hidden: int, inter: int):
+        """Prepare a MoE layer (dsv4cu_moe_create); returns an opaque handle."""
+        arr = (Expert * len(experts))(*experts)
+        h = C.c_void_p()
+        check(self.L.dsv4cu_moe_create(C.byref(h), C.addressof(arr), len(experts),
+                                       None if shared is None else C.addressof(shared), hidden, inter),
+              "dsv4cu_moe_create")
+        return h
+
+    def moe_destroy(self, layer):
+        self.L.dsv4cu_moe_destroy(layer)
+
+    def moe_decode(self, layer, out, x, logits, topk, route_scale, limit, nt, idx_out=None, wts_out=None,
+                   bias=None, tid2eid=None, token_ids=None, stream=None, events=None):
+        st = self.stream() if stream is None else stream
+        args = (self.ctx, layer, self.ptr(out), self.ptr(x), self.ptr(logits), self.ptr(bias),
+                self.ptr(tid2eid), self.ptr(token_ids), topk, route_scale, limit, nt, self.ptr(idx_out),
+                self.ptr(wts_out), st)
+        if events is None:
+            check(self.L.dsv4cu_moe_decode(*args), "dsv4cu_moe_decode")
+        else:
+            evp = (C.c_void_p * 4)(*[e.cuda_event for e in events])
+            check(self.L.dsv4cu_moe_decode_ev(*args, evp), "dsv4cu_moe_decode_ev")
 
     def indexer_score(self, out, q, kv, w, n_heads, head_dim, n_pos):
         check(self.L.dsv4cu_indexer_score(self.ptr(out), self.ptr(q), self.ptr(kv), self.ptr(w),

@@ -70,6 +70,10 @@ int  dsv4cu_ctx_create(dsv4cu_ctx **out, int device);
 void dsv4cu_ctx_destroy(dsv4cu_ctx *ctx);
 int  dsv4cu_ctx_reserve(dsv4cu_ctx *ctx, size_t bytes);
 size_t dsv4cu_ctx_workspace_bytes(const dsv4cu_ctx *ctx);
+/* Synchronise `stream` and report whether any kernel of this context hit a
+ * bounded-wait timeout since the last check (*code = 0: none; the call then
+ * returns DSV4CU_ERR_TIMEOUT and clears the word). */
+int  dsv4cu_ctx_status(dsv4cu_ctx *ctx, void *stream, int *code);
 
 /* Workspace bytes a dsv4cu_mmq call of this shape needs. */
 size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt);
@@ -97,35 +101,42 @@ int dsv4cu_route(int *idx, float *wts, float *scores, float *orig,
 int dsv4cu_swiglu(float *y, const float *gate, const float *up, int n,
                   float limit, void *stream);
 
+/* A prepared MoE layer: the routed experts and the optional shared expert of
+ * one layer, resident in HBM, validated once and given one TMA tensor map per
+ * weight matrix. experts: HOST array of n_experts descriptors whose w/s are
+ * device pointers (kept by reference: the weights must outlive the layer);
+ * shared: HOST pointer to one descriptor or NULL. w1/w3 are [inter][hidden],
+ * w2 [hidden][inter]; FP4 (blk_c % 32 == 0) or FP8 (blk_c % 16 == 0), 16-byte
+ * aligned weights; hidden and inter multiples of 128. */
+typedef struct dsv4cu_moe dsv4cu_moe;
+int  dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts, int n_experts,
+                       const dsv4cu_expert *shared, int hidden, int inter);
+void dsv4cu_moe_destroy(dsv4cu_moe *layer);
+/* Workspace bytes one dsv4cu_moe_decode of this layer needs. */
+size_t dsv4cu_moe_workspace(const dsv4cu_moe *layer, int topk, int nt);
+
 /* One MoE layer decode step for nt tokens (the reference dsv4_layer_moe,
  * src/70_decode/dsv4_layer.c:48-117, from the router logits on): route, the
  * routed experts' w1/w3 -> SwiGLU -> w2, the weighted sum in k order, plus the
- * shared expert added unweighted. experts: DEVICE array of n_experts
- * descriptors (their w/s are device pointers). shared: HOST pointer to one
- * descriptor, or NULL. x [nt][hidden], logits [nt][n_experts],
- * out [nt][hidden]. idx_out/wts_out [nt][topk] may be NULL. nt <= 64.
- * Routed descriptors are validated on the device; one with a wrong shape or
- * an unsupported format (FP4 with blk_c % 32, FP8 with blk_c % 16 required)
- * is skipped rather than read. */
-int dsv4cu_moe_decode(dsv4cu_ctx *ctx, float *out, const float *x,
-                      const float *logits, const float *bias,
-                      const int64_t *tid2eid, const int *token_ids,
-                      const dsv4cu_expert *experts, int n_experts,
-                      const dsv4cu_expert *shared, int topk, float route_scale,
-                      int hidden, int inter, float limit, int nt,
-                      int *idx_out, float *wts_out, void *stream);
+ * shared expert added unweighted. x [nt][hidden], logits [nt][n_experts],
+ * out [nt][hidden]; bias [n_experts] or NULL; tid2eid [vocab][topk] int64 or
+ * NULL (hash routing, token_ids [nt] then required). idx_out/wts_out
+ * [nt][topk] may be NULL. nt <= 64, topk <= 16. */
+int dsv4cu_moe_decode(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
+                      const float *x, const float *logits, const float *bias,
+                      const int64_t *tid2eid, const int *token_ids, int topk,
+                      float route_scale, float limit, int nt, int *idx_out,
+                      float *wts_out, void *stream);
 
 /* dsv4cu_moe_decode with CUDA events (cudaEvent_t) recorded around its three
  * launches: events[0] before the router/bucketing prologue, [1] after it,
  * [2] after the w1/w3 + SwiGLU kernel, [3] after the w2 + combine kernel.
  * events may be NULL. Used to time each kernel live on the launching stream. */
-int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, float *out, const float *x,
-                         const float *logits, const float *bias,
-                         const int64_t *tid2eid, const int *token_ids,
-                         const dsv4cu_expert *experts, int n_experts,
-                         const dsv4cu_expert *shared, int topk, float route_scale,
-                         int hidden, int inter, float limit, int nt,
-                         int *idx_out, float *wts_out, void *stream, void **events);
+int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
+                         const float *x, const float *logits, const float *bias,
+                         const int64_t *tid2eid, const int *token_ids, int topk,
+                         float route_scale, float limit, int nt, int *idx_out,
+                         float *wts_out, void *stream, void **events);
 
 /* Indexer score with fp32 inputs, bit-identical to dsv4_indexer_score
  * (src/10_compute/dsv4_indexer.c:66-90): out[t] = (float)(sum_h relu(q_h.k_t)

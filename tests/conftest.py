@@ -52,7 +52,16 @@ def dev():
     import dsv4cu
     d = dsv4cu.Device(0)
     yield d
+    d.check_status()
     d.close()
+
+
+@pytest.fixture(autouse=True)
+def _device_status(request):
+    """After every GPU test: no kernel may have hit a bounded-wait timeout."""
+    yield
+    if "dev" in request.fixturenames:
+        request.getfixturevalue("dev").check_status()
 
 
 @pytest.fixture(scope="session")
