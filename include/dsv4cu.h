@@ -167,6 +167,23 @@ int dsv4cu_sparse_attn(dsv4cu_ctx *ctx, float *o, const float *q, const void *kv
                        int kv_bf16, const float *sink, const int *idxs, int h,
                        int d, int topk, float scale, void *stream);
 
+/* dsv4cu_sparse_attn without a context and without any allocation. No
+ * counterpart in the reference (whose dsv4_sparse_attn takes a caller scratch
+ * buffer on the host). For callers that must not allocate device memory while
+ * they call in (during stream capture, inside an allocator callback, or with
+ * all free HBM handed to KV/expert pools). The per-chunk partials live in one
+ * 12 MiB array built into the library (per device): shapes whose partials need
+ * more ((ceil(topk/32) * h * (d + 2)) * 4 bytes, rounded) return
+ * DSV4CU_ERR_UNSUPPORTED; h = 64, d = 576, topk = 2176 fits. All calls on a
+ * device share that array and leave their contents in it (nothing needs to
+ * start at zero); calls that overlap in time on one device race, so serialise
+ * them on one stream. The first call on each device looks up the array's
+ * address and may load the library's module there: make it before any stream
+ * capture begins. */
+int dsv4cu_sparse_attn_noalloc(float *o, const float *q, const void *kv,
+                               int kv_bf16, const float *sink, const int *idxs,
+                               int h, int d, int topk, float scale, void *stream);
+
 /* Add offset to every idxs[i] >= 0 (dsv4_indexer_offset,
  * src/10_compute/dsv4_indexer.c:92-96). */
 int dsv4cu_indexer_offset(int *idxs, int n, int offset, void *stream);
