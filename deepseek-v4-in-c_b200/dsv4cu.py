@@ -68,6 +68,10 @@ def lib() -> C.CDLL:
             "dsv4cu_moe_workspace": (sz, [vp, i, i]),
             "dsv4cu_moe_decode": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp]),
             "dsv4cu_moe_decode_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp, vp]),
+            "dsv4cu_mat_create": (i, [C.POINTER(vp), vp, vp]),
+            "dsv4cu_mat_destroy": (None, [vp]),
+            "dsv4cu_mat_workspace": (sz, [vp, i, i]),
+            "dsv4cu_mat_gemm": (i, [vp, vp, vp, vp, i, i, vp]),
             "dsv4cu_indexer_score": (i, [vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_indexer_score_fp8": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]),
             "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
@@ -261,6 +265,19 @@ class Device:
     def mmq(self, y, x, m: QMat, nt: int):
         check(self.L.dsv4cu_mmq(self.ctx, self.ptr(y), self.ptr(x), C.byref(m), nt, self.stream()),
               "dsv4cu_mmq")
+
+    def mat_create(self, m: QMat):
+        """Prepare a packed matrix for the tensor-core GEMM (dsv4cu_mat_create)."""
+        h = C.c_void_p()
+        check(self.L.dsv4cu_mat_create(C.byref(h), C.byref(m), self.stream()), "dsv4cu_mat_create")
+        return h
+
+    def mat_destroy(self, h):
+        self.L.dsv4cu_mat_destroy(h)
+
+    def mat_gemm(self, h, y, x, nt: int, terms: int = 3):
+        check(self.L.dsv4cu_mat_gemm(self.ctx, h, self.ptr(y), self.ptr(x), nt, terms, self.stream()),
+              "dsv4cu_mat_gemm")
 
     def route(self, idx, wts, scores, orig, logits, topk, route_scale, nt, bias=None,
               tid2eid=None, token_ids=None):

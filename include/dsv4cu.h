@@ -86,6 +86,27 @@ size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt);
 int dsv4cu_mmq(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
                int nt, void *stream);
 
+/* ------------------------------------------- tensor-core (tcgen05) GEMM
+ * A packed matrix prepared once for the block-scaled tensor-core GEMM: the
+ * library keeps its TMA descriptor and a copy of its scale factors in the
+ * tensor core's block layout (rows/128 x cols/128 x 512 bytes); the weights
+ * stay where they are and must outlive the object. Needs FP4 (weights 32-byte
+ * aligned) or FP8 (16-byte aligned), cols % 128 == 0, blk_c % 32 == 0.
+ * Replaces the per-tile GEMM of the prefill seam
+ * (src/80_prefill/dsv4_prefill_vk_gemm.c:63-137) and dsv4_mmq_n for large nt. */
+typedef struct dsv4cu_mat dsv4cu_mat;
+int    dsv4cu_mat_create(dsv4cu_mat **out, const dsv4cu_qmat *m, void *stream);
+void   dsv4cu_mat_destroy(dsv4cu_mat *m);
+size_t dsv4cu_mat_workspace(const dsv4cu_mat *m, int nt, int terms);
+
+/* y[t*rows + o] = sum_c x[t*cols + c] * W[o][c] on the tensor cores
+ * (tcgen05.mma kind::mxf8f6f4 with E8M0 block scales). Each fp32 activation
+ * is split exactly into `terms` (1..4) e4m3 values with their own per-32
+ * E8M0 scales; terms = 3 keeps max|y - y_ref| / max|y_ref| well below 1e-3,
+ * terms = 4 is within about 1e-5, terms = 1 is the plain MXFP8 product. */
+int dsv4cu_mat_gemm(dsv4cu_ctx *ctx, const dsv4cu_mat *m, float *y, const float *x,
+                    int nt, int terms, void *stream);
+
 /* Router for nt tokens; replaces dsv4_route (src/10_compute/dsv4_kernels.h:24).
  * logits [nt][n_experts] (read), scores/orig [nt][n_experts] (written: biased
  * selection scores and sqrt(softplus) scores, either may be NULL), idx/wts
