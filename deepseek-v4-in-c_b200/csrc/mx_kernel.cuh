@@ -1,0 +1,327 @@
+// mx_kernel.cuh - the persistent tcgen05 block-scaled GEMM kernel template.
+//
+// One kernel body serves every packed-weight product of the library: a
+// problem policy P says how many tiles there are, where each tile's operands
+// live and what its epilogue does with the fp32 results.
+//
+// A tile is 128 weight rows (the MMA's M) x NB activation columns (N). The
+// A operand is a packed matrix in the reference pack layout (FP4 e2m1 or FP8
+// e4m3), loaded by TMA from a tensor map in 128-row x 128-element boxes with
+// 128-byte swizzle; FP4 boxes use the TMA type that spreads 16 values over 16
+// shared-memory bytes, the operand form kind::mxf8f6f4 reads. The B operand
+// is the activation written as e4m3 terms (mx_split_term): NB rows of a term
+// buffer, same box shape. Scale factors come as prepared 512-byte blocks (one
+// per 128 rows x 128 K) by 1-D bulk copy and reach TMEM through tcgen05.cp.
+//
+// Roles (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      producer: KB consecutive 128-wide K chunks per stage (A, B
+//               and both scale blocks per chunk) into a STAGES-deep ring;
+//   warp 1      TMEM owner and single-thread MMA issuer: per chunk two
+//               scale copies and four K = 32 MMAs, then the stage goes back
+//               to the producer (tcgen05.commit); after a tile's last stage
+//               the accumulator goes to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld (TMEM lane = tile row), the terms of a
+//               token summed, then P::store per value and P::finish per tile.
+// Two accumulators in TMEM (when they fit) let tile i's epilogue overlap tile
+// i+1's MMAs. Waits are bounded by 2 s of %globaltimer: a timeout records an
+// error code, the roles stop, in-flight copies and MMAs drain, TMEM is freed.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "tma_gemv.cuh"
+#include "umma.cuh"
+
+namespace dsv4cu {
+
+// Operands of one tile, as the policy describes them.
+struct MxTile {
+    const CUtensorMap *ta;   // A tensor map (global or parameter memory)
+    const uint8_t *sfa;      // A scale blocks of this row tile: [kc][512]
+    const uint8_t *sfb;      // B scale blocks of this column tile: [kc][NBB][512]
+    uint32_t idesc;          // MMA instruction descriptor (formats, M, N)
+    uint32_t a_tx;           // global bytes of one A box
+    int a_row;               // first weight row
+    int b_row;               // first row of the B term buffer
+    int kc;                  // 128-wide K chunks
+    int id0, id1, id2;       // problem-specific tile coordinates
+};
+
+constexpr int MX_THREADS = 192;
+constexpr int MX_SMEM_BUDGET = 227 * 1024 - 2048;
+
+template <int NB, int KB>
+struct MxCfg {
+    static constexpr int NBB = (NB + 127) / 128;          // 128-column scale blocks of B
+    static constexpr int A_BOX = 128 * 128;
+    static constexpr int B_BOX = NB * 128;
+    static constexpr int SFA_BOX = 512;
+    static constexpr int SFB_BOX = NBB * 512;
+    // Stage: [A x KB][B x KB][SFA x KB][SFB x KB].
+    static constexpr int OFF_B = KB * A_BOX;
+    static constexpr int OFF_SFA = OFF_B + KB * B_BOX;
+    static constexpr int OFF_SFB = OFF_SFA + KB * SFA_BOX;
+    static constexpr int STAGE = ((OFF_SFB + KB * SFB_BOX + 1023) / 1024) * 1024;
+    static constexpr int STAGES = (MX_SMEM_BUDGET / STAGE) < 16 ? (MX_SMEM_BUDGET / STAGE) : 16;
+    static constexpr int SMEM = STAGES * STAGE + 1024;
+    static constexpr int SF_SLOTS = 2 * KB < 4 ? 4 : 2 * KB;
+    static constexpr int SFB_COLS = 4 * NBB;
+    static constexpr int SF_COLS = SF_SLOTS * (4 + SFB_COLS);
+    static constexpr int ACC_BUFS = (2 * NB + SF_COLS <= 512) ? 2 : 1;
+    static constexpr int SFA_COL = ACC_BUFS * NB;
+    static constexpr int SFB_COL = SFA_COL + 4 * SF_SLOTS;
+    static constexpr int USED = SFB_COL + SFB_COLS * SF_SLOTS;
+    static constexpr int TMEM_COLS = USED <= 32 ? 32 : USED <= 64 ? 64 : USED <= 128 ? 128 : USED <= 256 ? 256 : 512;
+    static_assert(NB == 8 || NB == 16 || (NB % 32 == 0 && NB >= 32 && NB <= 256), "NB: 8, 16 or 32..256 by 32");
+    static_assert(KB == 1 || KB == 2 || KB == 4, "KB: 1, 2 or 4");
+    static_assert(STAGES >= 2, "at least two stages");
+    static_assert(USED <= 512, "TMEM budget");
+};
+
+enum { MXE_EMPTY = 21, MXE_FULL = 22, MXE_ACC_EMPTY = 23, MXE_ACC_FULL = 24, MXE_DRAIN = 25 };
+
+DSV4CU_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Named barrier of the four epilogue warps.
+DSV4CU_DEV void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Term j of the exact e4m3 split of one 32-wide block (one value per lane,
+// whole warp): returns the e4m3 byte and sets *sbyte to the block's E8M0
+// scale byte. r_0 = v; s_j = smallest power of two with max|r_j| <= 448 s_j;
+// q_j = RNE_e4m3(r_j / s_j); r_{j+1} = r_j - q_j s_j (exact). Non-finite
+// inputs stay out of the block maximum: NaN stays NaN, infinities saturate.
+DSV4CU_DEV uint8_t mx_split_term(float v, int term, uint8_t *sbyte)
+{
+    float r = v;
+    for (int j = 0;; j++) {
+        float a = isfinite(r) ? fabsf(r) : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+        int e = 0;
+        if (a > 0.0f) {
+            int E;
+            const float f = frexpf(a, &E);
+            e = max(-127, min(127, E - 9 + (f > 0.875f ? 1 : 0)));
+        }
+        uint16_t two;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(two) : "f"(0.0f), "f"(ldexpf(r, -e)));
+        const uint8_t q = (uint8_t)(two & 0xFF);
+        if (j == term) {
+            *sbyte = (uint8_t)(127 + e);
+            return q;
+        }
+        r = r - ldexpf(e4m3_to_f32(q), e);
+    }
+}
+
+// Byte offset of column n's scale for K block kb inside a [NBB][512] group.
+DSV4CU_DEV int mx_sfb_offset(int n, int kb)
+{
+    return (n >> 7) * 512 + (n & 31) * 16 + ((n & 127) >> 5) * 4 + kb;
+}
+
+template <int NB, int KB, class P>
+__global__ void __launch_bounds__(MX_THREADS, 1)
+    mx_kernel(const __grid_constant__ CUtensorMap tb, const __grid_constant__ typename P::Params p)
+{
+    using C = MxCfg<NB, KB>;
+    constexpr int STAGES = C::STAGES;
+    extern __shared__ uint8_t mx_smem_raw[];
+    __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accf[2], acce[2], drain;
+    __shared__ uint32_t tmem_holder;
+    __shared__ volatile int abort_flag;
+    __shared__ int epi_word;     // policy scratch word (epilogue warps only)
+
+    uint8_t *smem = (uint8_t *)(((uintptr_t)mx_smem_raw + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = P::ntiles(p);
+    int *err = P::err(p);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&acce[b], 4);
+        }
+        mbar_init(&drain, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        umma::tmem_alloc(&tmem_holder, C::TMEM_COLS);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before();
+    __syncthreads();
+    umma::fence_after();
+    const uint32_t tmem = tmem_holder;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int it = 0;
+            for (int t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x) {
+                const MxTile T = P::tile(p, t);
+                const uint32_t tx = KB * (T.a_tx + C::B_BOX + C::SFA_BOX + C::SFB_BOX);
+                const int nst = T.kc / KB;
+                for (int c = 0; c < nst; c++, it++) {
+                    const int s = it % STAGES, r = it / STAGES;
+                    if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, err, MXE_EMPTY)) {
+                        abort_flag = 1;
+                        break;
+                    }
+                    uint8_t *st = smem + s * C::STAGE;
+                    mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+                    for (int b = 0; b < KB; b++) {
+                        const int kc = c * KB + b;
+                        tma_load_2d(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s]);
+                        tma_load_2d(st + C::OFF_B + b * C::B_BOX, &tb, kc * 128, T.b_row, &full[s]);
+                        bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
+                                  &full[s]);
+                        bulk_load(st + C::OFF_SFB + b * C::SFB_BOX, T.sfb + (size_t)kc * C::SFB_BOX, C::SFB_BOX,
+                                  &full[s]);
+                    }
+                }
+            }
+            // Every issued copy lands before the CTA can exit.
+            for (int j = max(0, it - STAGES); j < it; j++)
+                mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, 0);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int it = 0, tcount = 0;
+            for (int t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x, tcount++) {
+                const MxTile T = P::tile(p, t);
+                const int nst = T.kc / KB;
+                const int ab = tcount % C::ACC_BUFS, use = tcount / C::ACC_BUFS;
+                if (use > 0 && !mbar_wait(&acce[ab], (use - 1) & 1, err, MXE_ACC_EMPTY)) {
+                    abort_flag = 1;
+                    break;
+                }
+                umma::fence_after();
+                const uint32_t dacc = tmem + ab * NB;
+                bool ok = true;
+                for (int c = 0; c < nst; c++, it++) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1, err, MXE_FULL)) {
+                        ok = false;
+                        break;
+                    }
+                    umma::fence_after();
+                    const uint8_t *st = smem + s * C::STAGE;
+#pragma unroll
+                    for (int b = 0; b < KB; b++) {
+                        const int slot = (it * KB + b) % C::SF_SLOTS;
+                        const uint32_t tsfa = tmem + C::SFA_COL + 4 * slot;
+                        const uint32_t tsfb = tmem + C::SFB_COL + C::SFB_COLS * slot;
+                        umma::cp_sf(tsfa, umma::desc_sf(st + C::OFF_SFA + b * C::SFA_BOX));
+#pragma unroll
+                        for (int j = 0; j < C::NBB; j++)
+                            umma::cp_sf(tsfb + 4 * j, umma::desc_sf(st + C::OFF_SFB + b * C::SFB_BOX + 512 * j));
+                        const uint8_t *sa = st + b * C::A_BOX, *sb = st + C::OFF_B + b * C::B_BOX;
+#pragma unroll
+                        for (int k = 0; k < 4; k++) {
+                            const uint32_t id = T.idesc | ((uint32_t)k << 4) | ((uint32_t)k << 29);
+                            umma::mma_mx(dacc, umma::desc_sw128(sa + 32 * k), umma::desc_sw128(sb + 32 * k), id,
+                                         (c | b | k) ? 1u : 0u, tsfa | ((uint32_t)k << 30),
+                                         tsfb | ((uint32_t)k << 30));
+                        }
+                    }
+                    umma::commit(&empty[s]);
+                }
+                if (!ok) {
+                    abort_flag = 1;
+                    break;
+                }
+                umma::commit(&accf[ab]);
+            }
+            // Every MMA / copy this thread issued completes before TMEM is freed.
+            umma::commit(&drain);
+            mbar_wait(&drain, 0, err, MXE_DRAIN);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue
+        const int q = warp & 3;             // the TMEM lane quarter this warp may read
+        const int row_l = q * 32 + lane;
+        const int terms = P::terms(p), tpt = P::tpt(p);
+        int tcount = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, tcount++) {
+            const int ab = tcount % C::ACC_BUFS, use = tcount / C::ACC_BUFS;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&accf[ab], use & 1, err, MXE_ACC_FULL);
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            if (!ok) abort_flag = 1;
+            epi_sync();
+            if (abort_flag) break;      // every epilogue warp leaves at the same tile
+            umma::fence_after();
+            const MxTile T = P::tile(p, t);
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * NB;
+            if constexpr (NB <= 16) {
+                // Narrow tiles: all NB columns at once, then per token.
+                float v[NB];
+#pragma unroll
+                for (int c8 = 0; c8 < NB; c8 += 8) {
+                    float w[8];
+                    umma::ld_x8(tbase + c8, w);
+#pragma unroll
+                    for (int i = 0; i < 8; i++) v[c8 + i] = w[i];
+                }
+                for (int tl = 0; tl < tpt; tl++) {
+                    float a = 0.0f;
+#pragma unroll
+                    for (int c = 0; c < NB; c++)
+                        if (c % tpt == tl && c / tpt < terms) a += v[c];
+                    P::store(p, T, row_l, tl, a);
+                }
+            } else {
+                for (int tb = 0; tb < tpt; tb += 8) {
+                    float acc[8];
+                    umma::ld_x8(tbase + tb, acc);
+                    for (int j = 1; j < terms; j++) {
+                        float v[8];
+                        umma::ld_x8(tbase + j * tpt + tb, v);
+#pragma unroll
+                        for (int i = 0; i < 8; i++) acc[i] += v[i];
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; i++) P::store(p, T, row_l, tb + i, acc[i]);
+                }
+            }
+            // The accumulator is free once every epilogue warp has read it.
+            umma::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[ab]);
+            P::finish(p, T, row_l, &epi_word);
+        }
+    }
+
+    umma::fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        umma::fence_after();
+        umma::tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// Dynamic shared memory of mx_kernel<NB, KB, P> (set once per device).
+template <int NB, int KB, class P>
+static int mx_kernel_prepare()
+{
+    DSV4CU_CUDA_TRY(cudaFuncSetAttribute(mx_kernel<NB, KB, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         MxCfg<NB, KB>::SMEM));
+    return DSV4CU_OK;
+}
+
+}  // namespace dsv4cu

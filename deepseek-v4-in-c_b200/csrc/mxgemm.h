@@ -1,4 +1,5 @@
-// mxgemm.h - the tcgen05 block-scaled GEMM (mxgemm.cu) for other translation units.
+// mxgemm.h - host side of the tcgen05 block-scaled GEMM shared by mxgemm.cu
+// (dense products) and moe_mx.cu (the MoE layer).
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -7,33 +8,35 @@
 
 namespace dsv4cu {
 
-// A packed matrix prepared for the tensor-core path: its TMA map and its
-// scale factors rearranged into the TMEM block layout (owned).
+// A packed matrix prepared for the tensor-core path: its TMA map (128 x 128
+// element boxes, 128-byte swizzle) and its scale factors rearranged into the
+// TMEM block layout: [tiles_m][kc][512] bytes, byte (m % 32) * 16 + (m / 32)
+// * 4 + kb of block (row tile, K chunk) = scale of row m, K block kb.
 struct MxMat {
     dsv4cu_qmat q;
     CUtensorMap ta;
-    uint8_t *sfa;      // [tiles_m][kc][512]
+    uint8_t *sfa;
     int fp4, kc, tiles_m;
+    int owns_sfa;
 };
 
-struct MxArgs {
-    const uint8_t *sfa;   // weight scale blocks [tiles_m][kc][512]
-    const uint8_t *sfb;   // activation scale blocks [tiles_n][kc][NB/128 rounded up][512]
-    int kc;               // K / 128
-    int tiles_m, tiles_n;
-    int rows, nt, tpt, terms;
-    float *y;
-    int ldy;
-    uint32_t idesc;       // instruction descriptor, scale ids 0
-    uint32_t a_tx;        // global bytes of one A box
-    int *err;
+// Column tiling of one launch: NB B columns per tile = terms x tpt tokens
+// (rounded), KB 128-wide K chunks per pipeline stage.
+struct MxTiling {
+    int NB, tpt, tiles_n, KB;
 };
 
 bool mx_supported(const dsv4cu_qmat *q);
-int mx_prepare(MxMat *m, const dsv4cu_qmat *q, cudaStream_t st);
+size_t mx_sfa_bytes(const dsv4cu_qmat *q);
+// sfa_buf: caller-owned block of mx_sfa_bytes(q) device bytes, or NULL to
+// allocate one owned by the MxMat.
+int mx_prepare(MxMat *m, const dsv4cu_qmat *q, uint8_t *sfa_buf, cudaStream_t st);
 void mx_release(MxMat *m);
+int mx_encode_kmajor(CUtensorMap *map, const void *base, bool fp4, uint64_t inner, uint64_t outer,
+                     uint64_t row_bytes, uint32_t box_rows);
+MxTiling mx_tiling(int nt, int terms, int nb_req, int kb_req, int kc);
 size_t mx_workspace(const MxMat *m, int nt, int terms);
-int mx_gemm(const MxMat *m, float *y, const float *x, int nt, int terms, void *ws, int sms, int *err,
-            cudaStream_t st);
+int mx_gemm(const MxMat *m, float *y, const float *x, int nt, int terms, int nb_req, int kb_req, void *ws, int sms,
+            int *err, cudaStream_t st);
 
 }  // namespace dsv4cu

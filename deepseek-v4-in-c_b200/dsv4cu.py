@@ -72,6 +72,7 @@ def lib() -> C.CDLL:
             "dsv4cu_mat_destroy": (None, [vp]),
             "dsv4cu_mat_workspace": (sz, [vp, i, i]),
             "dsv4cu_mat_gemm": (i, [vp, vp, vp, vp, i, i, vp]),
+            "dsv4cu_mat_gemm_cfg": (i, [vp, vp, vp, vp, i, i, i, i, vp]),
             "dsv4cu_indexer_score": (i, [vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_indexer_score_fp8": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]),
             "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
@@ -275,9 +276,13 @@ class Device:
     def mat_destroy(self, h):
         self.L.dsv4cu_mat_destroy(h)
 
-    def mat_gemm(self, h, y, x, nt: int, terms: int = 3):
-        check(self.L.dsv4cu_mat_gemm(self.ctx, h, self.ptr(y), self.ptr(x), nt, terms, self.stream()),
-              "dsv4cu_mat_gemm")
+    def mat_gemm(self, h, y, x, nt: int, terms: int = 3, nb: int = 0, kb: int = 0):
+        if nb or kb:
+            check(self.L.dsv4cu_mat_gemm_cfg(self.ctx, h, self.ptr(y), self.ptr(x), nt, terms, nb, kb,
+                                             self.stream()), "dsv4cu_mat_gemm_cfg")
+        else:
+            check(self.L.dsv4cu_mat_gemm(self.ctx, h, self.ptr(y), self.ptr(x), nt, terms, self.stream()),
+                  "dsv4cu_mat_gemm")
 
     def route(self, idx, wts, scores, orig, logits, topk, route_scale, nt, bias=None,
               tid2eid=None, token_ids=None):

@@ -107,6 +107,14 @@ size_t dsv4cu_mat_workspace(const dsv4cu_mat *m, int nt, int terms);
 int dsv4cu_mat_gemm(dsv4cu_ctx *ctx, const dsv4cu_mat *m, float *y, const float *x,
                     int nt, int terms, void *stream);
 
+/* dsv4cu_mat_gemm with an explicit tile configuration: nb B columns per tile
+ * (8, 16, 32, 64, 128, 192 or 256; terms x tokens per tile) and kb 128-wide K
+ * chunks per pipeline stage (1, 2 or 4; lowered until it divides cols/128).
+ * 0 = choose automatically. Built pairs: nb 8/16 with kb 1/2/4, nb 32/64
+ * with kb 1/2, nb 128/192/256 with kb 1. */
+int dsv4cu_mat_gemm_cfg(dsv4cu_ctx *ctx, const dsv4cu_mat *m, float *y, const float *x,
+                        int nt, int terms, int nb, int kb, void *stream);
+
 /* Router for nt tokens; replaces dsv4_route (src/10_compute/dsv4_kernels.h:24).
  * logits [nt][n_experts] (read), scores/orig [nt][n_experts] (written: biased
  * selection scores and sqrt(softplus) scores, either may be NULL), idx/wts

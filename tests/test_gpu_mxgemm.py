@@ -91,3 +91,26 @@ def test_mx_wide_terms4(dev, orc):
     """256-column tiles (4 terms x 64 tokens)."""
     got, want = _run(dev, orc, 3, 512, 1024, 70, 4, seed=9)
     assert rel_err(got, want) <= 1e-4
+
+
+@pytest.mark.parametrize("cfg", [(8, 1), (8, 2), (8, 4), (16, 4), (32, 2), (64, 1), (128, 1), (192, 1), (256, 1)],
+                         ids=lambda c: f"nb{c[0]}-kb{c[1]}")
+def test_mx_tile_configs(dev, orc, cfg):
+    """Every built tile configuration gives the same products (explicit-config entry point)."""
+    import oracle
+    t = __import__("torch")
+    nb, kb = cfg
+    rows, cols = 384, 1024
+    W, S, Wd, Sd, q = _upload_qmat(dev, 3, rows, cols, 11)
+    nt = {8: 2, 16: 4}.get(nb, 5)
+    x = np.random.default_rng(12).standard_normal((nt, cols)).astype(np.float32)
+    h = dev.mat_create(q)
+    try:
+        y = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+        dev.mat_gemm(h, y, t.from_numpy(x).cuda(), nt, 4, nb, kb)
+        t.cuda.synchronize()
+        got = y.cpu().numpy()
+    finally:
+        dev.mat_destroy(h)
+    want = orc.mmq(x, oracle.qmat(W, S, 3, rows, cols, 1, 32))
+    assert rel_err(got, want) <= 1e-4
