@@ -30,6 +30,7 @@
 #include "ctx.h"
 #include "gemv.h"
 #include "gemv_core.cuh"
+#include "moe.h"
 #include "router.cuh"
 #include "tma_gemv.cuh"
 #include "tmap.h"
@@ -88,12 +89,13 @@ __global__ void __launch_bounds__(1024) moe_prologue_kernel(
         return;
     }
 
-    // CTA 0: routing, one warp per token.
-    for (int t = warp; t < nt; t += nwarps) {
-        route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid,
-                         token_ids ? token_ids[t] : 0, n_experts, topk, route_scale,
-                         ws.idx + t * topk, ws.wts + t * topk, nullptr, nullptr);
-    }
+    // CTA 0: routing, one warp per token (eight routing warps).
+    __shared__ float rsc[8][2][32 * RMAX_PER_LANE];
+    if (warp < 8)
+        for (int t = warp; t < nt; t += 8)
+            route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0,
+                             n_experts, topk, route_scale, ws.idx + t * topk, ws.wts + t * topk, nullptr, nullptr,
+                             rsc[warp][0], rsc[warp][1]);
     __syncthreads();
 
     // Bucket the pairs by expert. counts[e] then an exclusive scan over experts
@@ -147,24 +149,7 @@ __global__ void __launch_bounds__(1024) moe_prologue_kernel(
 }
 
 
-// --------------------------------------------------------- prepared layer
-// Device view of a prepared layer: expert e (e == n_experts is the shared
-// expert) has matrices m = 0 (w1), 1 (w3), 2 (w2); maps[6e + 2m] is the weight
-// map, maps[6e + 2m + 1] the FP4 scale map, valid when staged[3e + m].
-struct MoeDev {
-    const dsv4cu_expert *experts;   // [n_experts + 1], shared last
-    const CUtensorMap *maps;
-    const int *staged;
-    int n_experts, has_shared;
-};
-
 }  // namespace dsv4cu
-
-struct dsv4cu_moe {
-    int n_experts, hidden, inter, has_shared, device;
-    void *dev_block;                // experts + maps + staged, one allocation
-    dsv4cu::MoeDev view;
-};
 
 namespace dsv4cu {
 
@@ -620,6 +605,14 @@ extern "C" int dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts,
     L->view.staged = (const int *)(p + b_exp + b_map);
     L->view.n_experts = n_experts;
     L->view.has_shared = L->has_shared;
+    L->mx_ok = 0;
+    L->mx_block = nullptr;
+    const int r = moe_mx_prepare(L, hexp.data());
+    if (r && r != DSV4CU_ERR_UNSUPPORTED) {
+        cudaFree(blk);
+        delete L;
+        return r;
+    }
     *out = L;
     return DSV4CU_OK;
 }
@@ -627,13 +620,17 @@ extern "C" int dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts,
 extern "C" void dsv4cu_moe_destroy(dsv4cu_moe *L)
 {
     if (!L) return;
+    moe_mx_release(L);
     cudaFree(L->dev_block);
     delete L;
 }
 
 extern "C" size_t dsv4cu_moe_workspace(const dsv4cu_moe *L, int topk, int nt)
 {
-    return L ? moe_decode_workspace(nt, topk, L->n_experts, L->hidden, L->inter, L->has_shared) : 0;
+    if (!L) return 0;
+    const size_t a = moe_decode_workspace(nt, topk, L->n_experts, L->hidden, L->inter, L->has_shared);
+    const size_t b = L->mx_ok ? moe_mx_workspace(L, topk, nt) : 0;
+    return a > b ? a : b;
 }
 
 extern "C" int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
@@ -649,6 +646,13 @@ extern "C" int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, fl
     if (topk < 1 || topk > MOE_MAX_TOPK || topk > layer->n_experts)
         return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: topk %d", topk);
     void *ws = nullptr;
+    if (layer->mx_ok) {
+        int r = dsv4cu_ws_get(ctx, moe_mx_workspace(layer, topk, nt), &ws);
+        if (r) return r;
+        return moe_mx_decode(layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt, idx_out,
+                             wts_out, ws, ctx->counters, ctx->status, ctx->sm_count, (cudaStream_t)stream,
+                             (cudaEvent_t *)events);
+    }
     int r = dsv4cu_ws_get(ctx, moe_decode_workspace(nt, topk, layer->n_experts, layer->hidden, layer->inter,
                                                     layer->has_shared), &ws);
     if (r) return r;

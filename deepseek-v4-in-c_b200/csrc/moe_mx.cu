@@ -1,0 +1,666 @@
+// moe_mx.cu - one MoE layer decode step on the tcgen05 block-scaled GEMM.
+//
+// Reference: dsv4_layer_moe (src/70_decode/dsv4_layer.c:48-117) from the router
+// logits on, with dsv4_route (dsv4_ops.c:117-156), dsv4_expert_forward
+// (dsv4_ops.c:85-93), dsv4_swiglu (dsv4_ops.c:61-79) and the k-order combine
+// (dsv4_layer.c:109-116).
+//
+// Four launches, stream-ordered:
+//   route    one CTA: every token routed (one warp per token), the (token, k)
+//            pairs bucketed by expert in ascending expert order with tokens
+//            ascending inside a bucket (the layout of union_prepare,
+//            src/80_prefill/dsv4_prefill_union.c:30-52), the shared expert's
+//            bucket last; then the column tiles: every bucket cut into tiles of
+//            tpt slots (tile i: expert, first slot, slot count).
+//   split    each column tile's tokens written as e4m3 terms (mx_split_term)
+//            into the gate/up B operand.
+//   gate/up  mx_kernel over (column tile, w1 | w3, 128-row tile): the fp32
+//            results go to a per-slot gate/up buffer; of the two tiles of a
+//            (column tile, row tile) pair the one that finishes second applies
+//            SwiGLU to the 128 rows and writes them as e4m3 terms straight
+//            into the down projection's B operand.
+//   down     mx_kernel over (column tile, 128-row tile of w2): per-slot partial
+//            rows; the last tile of each 128-row slice sums, for every token,
+//            its pairs in k order with the routing weights and adds the shared
+//            expert unweighted.
+// Every weight byte of the touched experts is read once per step per column
+// tile (one column tile per expert at batch 1).
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "ctx.h"
+#include "moe.h"
+#include "mx_kernel.cuh"
+#include "mxgemm.h"
+#include "router.cuh"
+
+namespace dsv4cu {
+
+constexpr int MX_TERMS = 4;         // activation terms (results within ~1e-6 of fp32)
+constexpr int MXMOE_MAX_NT = 64;
+constexpr int MXMOE_MAX_TOPK = 16;
+
+// Workspace of one step.
+struct MxMoeWs {
+    int *idx;            // [nt][topk]
+    float *wts;          // [nt][topk]
+    int *pos;            // [nt][topk] bucket slot of pair (t, k), -1 = dropped
+    int *meta;           // [0] routed buckets, [1] bad-route flag, [2] column tiles
+    int *b_expert;       // [nbmax]
+    int *b_off;          // [nbmax + 2]
+    int *b_tok;          // [npairs] token of each slot (shared slots last)
+    int *c_slot0, *c_cnt, *c_expert;   // [max_tiles] column tiles
+    uint8_t *xq1, *sfb1; // gate/up B operand and its scale blocks
+    uint8_t *xq2, *sfb2; // down B operand and its scale blocks
+    float *gu;           // [npairs][2][inter]
+    float *ypart;        // [npairs][hidden]
+};
+
+struct MxMoeShape {
+    int nt, topk, n_experts, hidden, inter, has_shared;
+    int NB, tpt, KB, nbb, max_tiles, npairs, nbmax;
+};
+
+static MxMoeShape mxmoe_shape(const dsv4cu_moe *L, int topk, int nt)
+{
+    MxMoeShape s;
+    s.nt = nt;
+    s.topk = topk;
+    s.n_experts = L->n_experts;
+    s.hidden = L->hidden;
+    s.inter = L->inter;
+    s.has_shared = L->has_shared;
+    // A bucket never holds more than nt slots: size the column tile for that.
+    if (nt <= 2) { s.NB = 8; s.KB = 4; }
+    else if (nt <= 4) { s.NB = 16; s.KB = 4; }
+    else { s.NB = 32; s.KB = 2; }
+    s.tpt = s.NB <= 16 ? s.NB / MX_TERMS : (s.NB / MX_TERMS) / 8 * 8;
+    s.nbb = (s.NB + 127) / 128;
+    s.npairs = nt * topk + (s.has_shared ? nt : 0);
+    s.nbmax = min(nt * topk, s.n_experts);
+    // sum over buckets of ceil(cnt / tpt) <= slots / tpt + buckets
+    s.max_tiles = (nt * topk) / s.tpt + s.nbmax + (s.has_shared ? nt / s.tpt + 1 : 0) + 1;
+    return s;
+}
+
+static size_t mxmoe_layout(const MxMoeShape &s, char *base, MxMoeWs *w)
+{
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char *p = base ? base + off : nullptr;
+        off += dsv4cu_align256(bytes);
+        return p;
+    };
+    MxMoeWs t;
+    t.idx = (int *)take((size_t)s.nt * s.topk * 4);
+    t.wts = (float *)take((size_t)s.nt * s.topk * 4);
+    t.pos = (int *)take((size_t)s.nt * s.topk * 4);
+    t.meta = (int *)take(64);
+    t.b_expert = (int *)take((size_t)s.nbmax * 4 + 4);
+    t.b_off = (int *)take(((size_t)s.nbmax + 2) * 4);
+    t.b_tok = (int *)take((size_t)s.npairs * 4);
+    t.c_slot0 = (int *)take((size_t)s.max_tiles * 4);
+    t.c_cnt = (int *)take((size_t)s.max_tiles * 4);
+    t.c_expert = (int *)take((size_t)s.max_tiles * 4);
+    t.xq1 = (uint8_t *)take((size_t)s.max_tiles * s.NB * s.hidden);
+    t.sfb1 = (uint8_t *)take((size_t)s.max_tiles * (s.hidden / 128) * s.nbb * 512);
+    t.xq2 = (uint8_t *)take((size_t)s.max_tiles * s.NB * s.inter);
+    t.sfb2 = (uint8_t *)take((size_t)s.max_tiles * (s.inter / 128) * s.nbb * 512);
+    t.gu = (float *)take((size_t)s.npairs * 2 * s.inter * 4);
+    t.ypart = (float *)take((size_t)s.npairs * s.hidden * 4);
+    if (w) *w = t;
+    return off;
+}
+
+// ------------------------------------------------------------ prep kernel
+// Exclusive prefix sum of a[0..n) in shared memory by one warp (n <= 32 * 32);
+// returns the total to every lane.
+DSV4CU_DEV int warp_scan_excl(int *a, int n)
+{
+    const int lane = threadIdx.x & 31, seg = (n + 31) >> 5;
+    const int b0 = min(n, lane * seg), b1 = min(n, b0 + seg);
+    int loc = 0;
+    for (int i = b0; i < b1; i++) loc += a[i];
+    int inc = loc;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += v;
+    }
+    int run = inc - loc;
+    for (int i = b0; i < b1; i++) {
+        const int v = a[i];
+        a[i] = run;
+        run += v;
+    }
+    return __shfl_sync(0xFFFFFFFFu, inc, 31);
+}
+
+constexpr int PREP_MAX_PAIRS = MXMOE_MAX_NT * MXMOE_MAX_TOPK;            // 1024
+constexpr int PREP_MAX_SLOTS = PREP_MAX_PAIRS + MXMOE_MAX_NT;
+constexpr int PREP_MAX_EXPERTS = 32 * RMAX_PER_LANE;                      // 512
+constexpr int PREP_MAX_TILES = PREP_MAX_PAIRS / 2 + PREP_MAX_EXPERTS + MXMOE_MAX_NT + 2;
+constexpr int PREP_ROUTE_WARPS = 16;
+
+// Every CTA routes all nt tokens (one warp per token), buckets the (token, k)
+// pairs by expert in ascending expert order with tokens ascending inside a
+// bucket (the layout of union_prepare, src/80_prefill/dsv4_prefill_union.c:
+// 30-52), shared expert's bucket last, and cuts the buckets into column tiles
+// of tpt slots - all in shared memory, identically in every CTA. CTA 0
+// publishes the tables; then all CTAs write their share of the gate/up B
+// operand: one warp per (column tile, column, 32-wide K block).
+__global__ void __launch_bounds__(1024) mxmoe_prep_kernel(
+    const float *__restrict__ tab, const float *__restrict__ x, const float *__restrict__ logits,
+    const float *__restrict__ bias, const int64_t *__restrict__ tid2eid, const int *__restrict__ token_ids,
+    int n_experts, int topk, float route_scale, int nt, int hidden, int has_shared, int terms, int tpt, int NB,
+    MxMoeWs ws, int *__restrict__ idx_out, float *__restrict__ wts_out)
+{
+    __shared__ int s_idx[PREP_MAX_PAIRS];
+    __shared__ float s_wts[PREP_MAX_PAIRS];
+    __shared__ int s_pos[PREP_MAX_PAIRS];
+    __shared__ int s_cnt[PREP_MAX_EXPERTS + 2], s_off[PREP_MAX_EXPERTS + 2], s_bid[PREP_MAX_EXPERTS + 2];
+    __shared__ int s_bexp[PREP_MAX_EXPERTS + 2], s_boff[PREP_MAX_EXPERTS + 3], s_btiles[PREP_MAX_EXPERTS + 2];
+    __shared__ int s_btok[PREP_MAX_SLOTS];
+    __shared__ int s_tslot[PREP_MAX_TILES], s_tcnt[PREP_MAX_TILES], s_texp[PREP_MAX_TILES];
+    __shared__ int s_nb, s_ntiles, s_bad;
+    extern __shared__ float s_route[];      // [route_warps][2][n_experts]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    const int npairs = nt * topk;
+    const int rw = min(nt, PREP_ROUTE_WARPS);
+
+    if (warp < rw)
+        for (int t = warp; t < nt; t += rw)
+            route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0,
+                             n_experts, topk, route_scale, s_idx + t * topk, s_wts + t * topk, nullptr, nullptr,
+                             s_route + (size_t)warp * 2 * n_experts, s_route + ((size_t)warp * 2 + 1) * n_experts);
+    for (int e = threadIdx.x; e <= n_experts; e += blockDim.x) s_cnt[e] = 0;
+    if (threadIdx.x == 0) s_bad = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < npairs; p += blockDim.x) {
+        const int e = s_idx[p];
+        if (e < 0 || e >= n_experts) atomicOr(&s_bad, 1);
+        else atomicAdd(&s_cnt[e], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // Slot offsets per expert, bucket index per expert (experts with pairs).
+        for (int e = lane; e < n_experts; e += 32) {
+            s_off[e] = s_cnt[e];
+            s_bid[e] = s_cnt[e] > 0;
+        }
+        __syncwarp();
+        const int routed = warp_scan_excl(s_off, n_experts);
+        const int nb = warp_scan_excl(s_bid, n_experts);
+        __syncwarp();
+        for (int e = lane; e < n_experts; e += 32)
+            if (s_cnt[e]) {
+                s_bexp[s_bid[e]] = e;
+                s_boff[s_bid[e]] = s_off[e];
+            }
+        if (lane == 0) {
+            s_nb = nb;
+            s_boff[nb] = routed;
+            s_boff[nb + 1] = routed + (has_shared ? nt : 0);
+        }
+        // Rank of each pair inside its bucket: pairs are in (t, k) order, so a
+        // running count per expert over 32-pair chunks keeps tokens ascending.
+        for (int e = lane; e < n_experts; e += 32) s_cnt[e] = 0;
+        __syncwarp();
+        for (int c0 = 0; c0 < npairs; c0 += 32) {
+            const int p = c0 + lane;
+            const int e = p < npairs ? s_idx[p] : -1;
+            const bool ok = e >= 0 && e < n_experts;
+            const unsigned same = __match_any_sync(0xFFFFFFFFu, ok ? e : -1);
+            const int before = __popc(same & ((1u << lane) - 1u));
+            const int base = ok ? s_cnt[e] : 0;
+            __syncwarp();
+            if (ok) {
+                const int slot = s_off[e] + base + before;
+                s_pos[p] = slot;
+                s_btok[slot] = p / topk;
+                if (before == __popc(same) - 1) s_cnt[e] = base + before + 1;   // last lane of the group
+            } else if (p < npairs) {
+                s_pos[p] = -1;
+            }
+            __syncwarp();
+        }
+        if (has_shared)
+            for (int t = lane; t < nt; t += 32) s_btok[routed + t] = t;
+        // Column tiles per bucket (shared expert's bucket last), then offsets.
+        __syncwarp();
+        const int nbk = s_nb + (has_shared ? 1 : 0);
+        for (int b = lane; b < nbk; b += 32) s_btiles[b] = (s_boff[b + 1] - s_boff[b] + tpt - 1) / tpt;
+        __syncwarp();
+        const int ntiles = warp_scan_excl(s_btiles, nbk);
+        __syncwarp();
+        for (int b = lane; b < nbk; b += 32) {
+            const int s0 = s_boff[b], c = s_boff[b + 1] - s0, e = b < s_nb ? s_bexp[b] : n_experts;
+            for (int j = 0, n = s_btiles[b]; j < c; j += tpt, n++) {
+                s_tslot[n] = s0 + j;
+                s_tcnt[n] = min(tpt, c - j);
+                s_texp[n] = e;
+            }
+        }
+        if (lane == 0) s_ntiles = ntiles;
+    }
+    __syncthreads();
+    const int nb = s_nb, ntiles = s_ntiles, nslots = npairs + (has_shared ? nt : 0);
+
+    if (blockIdx.x == 0) {
+        for (int p = threadIdx.x; p < npairs; p += blockDim.x) {
+            ws.idx[p] = s_idx[p];
+            ws.wts[p] = s_wts[p];
+            ws.pos[p] = s_pos[p];
+            if (idx_out) {
+                idx_out[p] = s_idx[p];
+                wts_out[p] = s_wts[p];
+            }
+        }
+        for (int i = threadIdx.x; i < nslots; i += blockDim.x) ws.b_tok[i] = s_btok[i];
+        for (int b = threadIdx.x; b < nb; b += blockDim.x) ws.b_expert[b] = s_bexp[b];
+        for (int b = threadIdx.x; b < nb + 2; b += blockDim.x) ws.b_off[b] = s_boff[b];
+        for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
+            ws.c_slot0[i] = s_tslot[i];
+            ws.c_cnt[i] = s_tcnt[i];
+            ws.c_expert[i] = s_texp[i];
+        }
+        if (threadIdx.x == 0) {
+            ws.meta[0] = nb;
+            ws.meta[1] = s_bad;
+            ws.meta[2] = ntiles;
+        }
+    }
+
+    // Gate/up B operand: one warp per (column tile, slot, 32-wide K block)
+    // writes all terms of that slot. Columns past the tile's slots are left as
+    // they are: they only feed accumulator columns that are never read.
+    const int nblk = hidden >> 5, nbb = (NB + 127) / 128;
+    const long tasks = (long)ntiles * tpt * nblk;
+    for (long task = (long)blockIdx.x * nwarps + warp; task < tasks; task += (long)gridDim.x * nwarps) {
+        const int it = (int)(task / nblk), blk = (int)(task - (long)it * nblk);
+        const int i = it / tpt, tl = it - i * tpt;
+        if (tl >= s_tcnt[i]) continue;
+        const int tok = s_btok[s_tslot[i] + tl];
+        uint8_t q[4], sb[4];
+        mx_split_all(x[(size_t)tok * hidden + blk * 32 + lane], terms, q, sb);
+        for (int j = 0; j < terms; j++) {
+            const int n = j * tpt + tl;
+            ws.xq1[((size_t)i * NB + n) * hidden + blk * 32 + lane] = q[j];
+            if (lane == 0)
+                ws.sfb1[((size_t)i * (hidden >> 7) + (blk >> 2)) * nbb * 512 + mx_sfb_offset(n, blk & 3)] = sb[j];
+        }
+    }
+}
+
+// ------------------------------------------------------------ policies
+struct MxMoeCommon {
+    MoeMxDev L;
+    MxMoeWs ws;
+    int nb, nbb, tpt, terms, hidden, inter;
+    int *counters;
+    int *err;
+};
+
+DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc, const uint8_t *sfb)
+{
+    MxTile T;
+    const int fp4 = c.L.fp4[m];
+    T.ta = c.L.maps + m;
+    T.sfa = c.L.sfa[m] + (size_t)rt * kc * 512;
+    T.sfb = sfb + (size_t)i * kc * c.nbb * 512;
+    T.idesc = umma::idesc_mx(fp4 ? umma::FMT_E2M1 : umma::FMT_E4M3, umma::FMT_E4M3, 128, c.nb);
+    T.a_tx = fp4 ? 128 * 64 : 128 * 128;
+    T.a_row = rt * 128;
+    T.b_row = i * c.nb;
+    T.kc = kc;
+    return T;
+}
+
+struct MoeGateUp {
+    struct Params {
+        MxMoeCommon c;
+        float limit;
+    };
+    DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * 2 * (p.c.inter >> 7); }
+    DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
+    DSV4CU_DEV static int terms(const Params &p) { return p.c.terms; }
+    DSV4CU_DEV static int tpt(const Params &p) { return p.c.tpt; }
+    DSV4CU_DEV static MxTile tile(const Params &p, int t)
+    {
+        const int RT = p.c.inter >> 7;
+        const int i = t / (2 * RT), rem = t - i * 2 * RT, mat = rem / RT, rt = rem - mat * RT;
+        MxTile T = mxmoe_tile(p.c, i, 3 * p.c.ws.c_expert[i] + mat, rt, p.c.hidden >> 7, p.c.ws.sfb1);
+        T.id0 = i;
+        T.id1 = mat;
+        T.id2 = rt;
+        return T;
+    }
+    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v)
+    {
+        if (tl < p.c.tpt && tl < p.c.ws.c_cnt[T.id0]) {
+            const int slot = p.c.ws.c_slot0[T.id0] + tl;
+            p.c.ws.gu[((size_t)slot * 2 + T.id1) * p.c.inter + T.id2 * 128 + row_l] = v;
+        }
+    }
+    // The second tile of a (column tile, row tile) pair applies SwiGLU
+    // (dsv4_ops.c:61-79: up clamped both ways, gate from above only) and writes
+    // the 128 mid values of each slot as e4m3 terms for the down projection.
+    DSV4CU_DEV static void finish(const Params &p, const MxTile &T, int row_l, int *word)
+    {
+        const int RT = p.c.inter >> 7;
+        int *ctr = p.c.counters + T.id0 * RT + T.id2;
+        __threadfence();
+        epi_sync();
+        if (row_l == 0) *word = atomicAdd(ctr, 1);
+        epi_sync();
+        const int first = (*word == 0);
+        epi_sync();                       // every thread has read *word
+        if (first) return;
+        if (row_l == 0) *ctr = 0;         // both tiles are done: ready for the next step
+        __threadfence();
+        const int i = T.id0, ii = T.id2 * 128 + row_l, kb = row_l >> 5;
+        const int cnt = p.c.ws.c_cnt[i], slot0 = p.c.ws.c_slot0[i];
+        const int kc2 = p.c.inter >> 7;
+        for (int tl = 0; tl < cnt; tl++) {
+            const size_t base = (size_t)(slot0 + tl) * 2 * p.c.inter;
+            float g = __ldcg(p.c.ws.gu + base + ii), u = __ldcg(p.c.ws.gu + base + p.c.inter + ii);
+            if (p.limit > 0.0f) {
+                u = fminf(fmaxf(u, -p.limit), p.limit);
+                g = fminf(g, p.limit);
+            }
+            const float mid = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+            uint8_t q[4], sb[4];
+            mx_split_all(mid, p.c.terms, q, sb);
+            for (int j = 0; j < p.c.terms; j++) {
+                const int n = j * p.c.tpt + tl;
+                p.c.ws.xq2[((size_t)i * p.c.nb + n) * p.c.inter + ii] = q[j];
+                if ((row_l & 31) == 0)
+                    p.c.ws.sfb2[((size_t)i * kc2 + T.id2) * p.c.nbb * 512 + mx_sfb_offset(n, kb)] = sb[j];
+            }
+        }
+    }
+};
+
+struct MoeDown {
+    struct Params {
+        MxMoeCommon c;
+        int nt, topk, has_shared;
+        float *out;
+    };
+    DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * (p.c.hidden >> 7); }
+    DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
+    DSV4CU_DEV static int terms(const Params &p) { return p.c.terms; }
+    DSV4CU_DEV static int tpt(const Params &p) { return p.c.tpt; }
+    DSV4CU_DEV static MxTile tile(const Params &p, int t)
+    {
+        const int RT = p.c.hidden >> 7;
+        const int i = t / RT, rt = t - i * RT;
+        MxTile T = mxmoe_tile(p.c, i, 3 * p.c.ws.c_expert[i] + 2, rt, p.c.inter >> 7, p.c.ws.sfb2);
+        T.id0 = i;
+        T.id1 = 0;
+        T.id2 = rt;
+        return T;
+    }
+    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v)
+    {
+        if (tl < p.c.tpt && tl < p.c.ws.c_cnt[T.id0]) {
+            const int slot = p.c.ws.c_slot0[T.id0] + tl;
+            p.c.ws.ypart[(size_t)slot * p.c.hidden + T.id2 * 128 + row_l] = v;
+        }
+    }
+    // The last column tile to finish a 128-row slice combines it: per token
+    // the routed pairs IN k ORDER (dsv4_layer.c:109-113), then the shared
+    // expert unweighted (:115).
+    DSV4CU_DEV static void finish(const Params &p, const MxTile &T, int row_l, int *word)
+    {
+        int *ctr = p.c.counters + T.id2;
+        const int ntiles = p.c.ws.meta[2];
+        __threadfence();
+        epi_sync();
+        if (row_l == 0) *word = atomicAdd(ctr, 1);
+        epi_sync();
+        const int last = (*word == ntiles - 1);
+        epi_sync();
+        if (!last) return;
+        if (row_l == 0) *ctr = 0;
+        __threadfence();
+        const int row = T.id2 * 128 + row_l, nb = p.c.ws.meta[0];
+        for (int t = 0; t < p.nt; t++) {
+            float o = 0.0f;
+            for (int k = 0; k < p.topk; k++) {
+                const int slot = __ldcg(p.c.ws.pos + t * p.topk + k);
+                if (slot < 0) continue;
+                o = __fadd_rn(o, __fmul_rn(__ldcg(p.c.ws.wts + t * p.topk + k),
+                                           __ldcg(p.c.ws.ypart + (size_t)slot * p.c.hidden + row)));
+            }
+            if (p.has_shared)
+                o = __fadd_rn(o, __ldcg(p.c.ws.ypart + (size_t)(__ldcg(p.c.ws.b_off + nb) + t) * p.c.hidden + row));
+            p.out[(size_t)t * p.c.hidden + row] = o;
+        }
+    }
+};
+
+// ------------------------------------------------------------ host side
+template <int NB, int KB, class P>
+static int mxmoe_launch(const CUtensorMap &tb, const typename P::Params &p, int grid, cudaStream_t st)
+{
+    int r = mx_kernel_prepare<NB, KB, P>();
+    if (r) return r;
+    mx_kernel<NB, KB, P><<<grid, MX_THREADS, MxCfg<NB, KB>::SMEM, st>>>(tb, p);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+template <class P>
+static int mxmoe_dispatch(int NB, int KB, const CUtensorMap &tb, const typename P::Params &p, int grid,
+                          cudaStream_t st)
+{
+    switch (NB * 8 + KB) {
+    case 8 * 8 + 4: return mxmoe_launch<8, 4, P>(tb, p, grid, st);
+    case 8 * 8 + 2: return mxmoe_launch<8, 2, P>(tb, p, grid, st);
+    case 16 * 8 + 4: return mxmoe_launch<16, 4, P>(tb, p, grid, st);
+    case 16 * 8 + 2: return mxmoe_launch<16, 2, P>(tb, p, grid, st);
+    case 8 * 8 + 1: return mxmoe_launch<8, 1, P>(tb, p, grid, st);
+    case 16 * 8 + 1: return mxmoe_launch<16, 1, P>(tb, p, grid, st);
+    case 32 * 8 + 2: return mxmoe_launch<32, 2, P>(tb, p, grid, st);
+    case 32 * 8 + 1: return mxmoe_launch<32, 1, P>(tb, p, grid, st);
+    default: return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe: no kernel for %d columns x %d chunks", NB, KB);
+    }
+}
+
+// The B-operand maps of a step depend only on the workspace address and the
+// shape: encoded once and reused (the encode is a driver call per map).
+static int cached_bmap(CUtensorMap *out, const void *base, uint64_t inner, uint64_t outer, uint32_t box)
+{
+    struct Entry {
+        const void *base;
+        uint64_t inner, outer;
+        uint32_t box;
+        int device;
+        CUtensorMap map;
+    };
+    static std::mutex mu;
+    static Entry cache[16];
+    static int next = 0;
+    int dev = 0;
+    DSV4CU_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    for (const Entry &e : cache)
+        if (e.base == base && e.inner == inner && e.outer == outer && e.box == box && e.device == dev) {
+            *out = e.map;
+            return DSV4CU_OK;
+        }
+    Entry &e = cache[next];
+    int r = mx_encode_kmajor(&e.map, base, false, inner, outer, inner, box);
+    if (r) {
+        e.base = nullptr;
+        return r;
+    }
+    e.base = base;
+    e.inner = inner;
+    e.outer = outer;
+    e.box = box;
+    e.device = dev;
+    next = (next + 1) % 16;
+    *out = e.map;
+    return DSV4CU_OK;
+}
+
+size_t moe_mx_workspace(const dsv4cu_moe *L, int topk, int nt)
+{
+    return mxmoe_layout(mxmoe_shape(L, topk, nt), nullptr, nullptr);
+}
+
+int moe_mx_prepare(dsv4cu_moe *L, const dsv4cu_expert *hexp)
+{
+    L->mx_ok = 0;
+    L->mx_block = nullptr;
+    const int nm = 3 * (L->n_experts + 1);
+    std::vector<const dsv4cu_qmat *> qs(nm);
+    for (int e = 0; e <= L->n_experts; e++) {
+        qs[3 * e] = &hexp[e].w1;
+        qs[3 * e + 1] = &hexp[e].w3;
+        qs[3 * e + 2] = &hexp[e].w2;
+    }
+    size_t sf_total = 0;
+    for (int m = 0; m < nm; m++) {
+        if (!mx_supported(qs[m])) return DSV4CU_ERR_UNSUPPORTED;   // the CUDA-core path serves this layer
+        sf_total += dsv4cu_align256(mx_sfa_bytes(qs[m]));
+    }
+    // One block: [maps][pointer table][fp4 flags][scale blocks].
+    const size_t b_map = dsv4cu_align256((size_t)nm * sizeof(CUtensorMap));
+    const size_t b_ptr = dsv4cu_align256((size_t)nm * sizeof(void *));
+    const size_t b_fmt = dsv4cu_align256((size_t)nm * sizeof(int));
+    char *blk = nullptr;
+    cudaError_t ce = cudaMalloc((void **)&blk, b_map + b_ptr + b_fmt + sf_total);
+    if (ce != cudaSuccess) return dsv4cu_set_error(DSV4CU_ERR_NOMEM, "moe_create: %s", cudaGetErrorString(ce));
+    std::vector<CUtensorMap> maps(nm);
+    std::vector<const uint8_t *> ptrs(nm);
+    std::vector<int> fp4(nm);
+    char *sf = blk + b_map + b_ptr + b_fmt;
+    int r = DSV4CU_OK;
+    for (int m = 0; m < nm && !r; m++) {
+        MxMat mm;
+        r = mx_prepare(&mm, qs[m], (uint8_t *)sf, 0);
+        if (r) break;
+        maps[m] = mm.ta;
+        ptrs[m] = (const uint8_t *)sf;
+        fp4[m] = mm.fp4;
+        sf += dsv4cu_align256(mx_sfa_bytes(qs[m]));
+    }
+    if (!r) {
+        ce = cudaMemcpy(blk, maps.data(), nm * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+        if (ce == cudaSuccess) ce = cudaMemcpy(blk + b_map, ptrs.data(), nm * sizeof(void *), cudaMemcpyHostToDevice);
+        if (ce == cudaSuccess)
+            ce = cudaMemcpy(blk + b_map + b_ptr, fp4.data(), nm * sizeof(int), cudaMemcpyHostToDevice);
+        if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+        if (ce != cudaSuccess) r = dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_create: %s", cudaGetErrorString(ce));
+    }
+    if (r) {
+        cudaFree(blk);
+        return r == DSV4CU_ERR_UNSUPPORTED ? DSV4CU_ERR_CUDA : r;
+    }
+    L->mx_block = blk;
+    L->mx.maps = (const CUtensorMap *)blk;
+    L->mx.sfa = (const uint8_t *const *)(blk + b_map);
+    L->mx.fp4 = (const int *)(blk + b_map + b_ptr);
+    L->mx_ok = 1;
+    return DSV4CU_OK;
+}
+
+void moe_mx_release(dsv4cu_moe *L)
+{
+    if (L && L->mx_block) cudaFree(L->mx_block);
+    if (L) {
+        L->mx_block = nullptr;
+        L->mx_ok = 0;
+    }
+}
+
+int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *logits, const float *bias,
+                  const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
+                  int *idx_out, float *wts_out, void *wsp, int *counters, int *status, int sms, cudaStream_t st,
+                  cudaEvent_t *ev)
+{
+    if (nt > MXMOE_MAX_NT || topk > MXMOE_MAX_TOPK || L->n_experts > PREP_MAX_EXPERTS)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: nt %d / topk %d / experts %d beyond 64 / 16 / 512",
+                                nt, topk, L->n_experts);
+    const MxMoeShape s = mxmoe_shape(L, topk, nt);
+    MxMoeWs ws;
+    mxmoe_layout(s, (char *)wsp, &ws);
+    const int RT = s.inter / 128, RTH = s.hidden / 128;
+    if ((size_t)s.max_tiles * RT + RTH > DSV4CU_MAX_COUNTERS)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: too many tiles for the counter table");
+    const float *tab = router_table_get();
+    if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_decode: router table setup failed");
+
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
+    {
+        // Every SM takes part in the split; each CTA repeats the (cheap) routing.
+        const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 32);
+        const int grid = (int)min((long)sms, max(1L, (tasks + 31) / 32));
+        const int rw = min(nt, PREP_ROUTE_WARPS);
+        const size_t dsm = (size_t)rw * 2 * s.n_experts * sizeof(float);
+        static volatile int prep_attr[64];
+        int dev = 0;
+        DSV4CU_CUDA_TRY(cudaGetDevice(&dev));
+        if (dev < 0 || dev >= 64 || !prep_attr[dev]) {
+            DSV4CU_CUDA_TRY(cudaFuncSetAttribute(mxmoe_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)(PREP_ROUTE_WARPS * 2 * PREP_MAX_EXPERTS * sizeof(float))));
+            if (dev >= 0 && dev < 64) prep_attr[dev] = 1;
+        }
+        mxmoe_prep_kernel<<<grid, 1024, dsm, st>>>(tab, x, logits, bias, tid2eid, token_ids, s.n_experts, topk,
+                                                 route_scale, nt, s.hidden, s.has_shared, MX_TERMS, s.tpt, s.NB, ws,
+                                                 idx_out, wts_out);
+        DSV4CU_LAUNCH_CHECK();
+    }
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
+
+    MxMoeCommon c;
+    c.L = L->mx;
+    c.ws = ws;
+    c.nb = s.NB;
+    c.nbb = s.nbb;
+    c.tpt = s.tpt;
+    c.terms = MX_TERMS;
+    c.hidden = s.hidden;
+    c.inter = s.inter;
+    c.err = status;
+    // Persistent grids: the tile count is known only on the device.
+    const int g1 = min(sms, s.max_tiles * 2 * RT), g2 = min(sms, s.max_tiles * RTH);
+
+    CUtensorMap tb1, tb2;
+    int r = cached_bmap(&tb1, ws.xq1, (uint64_t)s.hidden, (uint64_t)s.max_tiles * s.NB, (uint32_t)s.NB);
+    if (!r) r = cached_bmap(&tb2, ws.xq2, (uint64_t)s.inter, (uint64_t)s.max_tiles * s.NB, (uint32_t)s.NB);
+    if (r) return r;
+
+    MoeGateUp::Params pg;
+    pg.c = c;
+    pg.c.counters = counters;
+    pg.limit = limit;
+    int kb1 = s.KB;
+    while (kb1 > 1 && (s.hidden / 128) % kb1) kb1 >>= 1;
+    r = mxmoe_dispatch<MoeGateUp>(s.NB, kb1, tb1, pg, g1, st);
+    if (r) return r;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
+
+    MoeDown::Params pd;
+    pd.c = c;
+    pd.c.counters = counters + (size_t)s.max_tiles * RT;
+    pd.nt = nt;
+    pd.topk = topk;
+    pd.has_shared = s.has_shared;
+    pd.out = out;
+    int kb2 = s.KB;
+    while (kb2 > 1 && (s.inter / 128) % kb2) kb2 >>= 1;
+    r = mxmoe_dispatch<MoeDown>(s.NB, kb2, tb2, pd, g2, st);
+    if (r) return r;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
+    return DSV4CU_OK;
+}
+
+}  // namespace dsv4cu

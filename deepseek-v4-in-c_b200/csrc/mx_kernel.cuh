@@ -120,6 +120,30 @@ DSV4CU_DEV uint8_t mx_split_term(float v, int term, uint8_t *sbyte)
     }
 }
 
+// All terms 0..terms-1 of the same split in one pass (terms <= 4).
+DSV4CU_DEV void mx_split_all(float v, int terms, uint8_t (&q)[4], uint8_t (&sb)[4])
+{
+    float r = v;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        if (j >= terms) break;
+        float a = isfinite(r) ? fabsf(r) : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+        int e = 0;
+        if (a > 0.0f) {
+            int E;
+            const float f = frexpf(a, &E);
+            e = max(-127, min(127, E - 9 + (f > 0.875f ? 1 : 0)));
+        }
+        uint16_t two;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(two) : "f"(0.0f), "f"(ldexpf(r, -e)));
+        q[j] = (uint8_t)(two & 0xFF);
+        sb[j] = (uint8_t)(127 + e);
+        r = r - ldexpf(e4m3_to_f32(q[j]), e);
+    }
+}
+
 // Byte offset of column n's scale for K block kb inside a [NBB][512] group.
 DSV4CU_DEV int mx_sfb_offset(int n, int kb)
 {
@@ -315,12 +339,17 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     }
 }
 
-// Dynamic shared memory of mx_kernel<NB, KB, P> (set once per device).
+// Dynamic shared memory of mx_kernel<NB, KB, P>, set once per device.
 template <int NB, int KB, class P>
 static int mx_kernel_prepare()
 {
+    static volatile int done[64];
+    int dev = 0;
+    DSV4CU_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && done[dev]) return DSV4CU_OK;
     DSV4CU_CUDA_TRY(cudaFuncSetAttribute(mx_kernel<NB, KB, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          MxCfg<NB, KB>::SMEM));
+    if (dev >= 0 && dev < 64) done[dev] = 1;
     return DSV4CU_OK;
 }
 

@@ -25,10 +25,10 @@ namespace dsv4cu {
 // on first use (host computation + one copy). Returns nullptr on failure.
 const float *router_table_get();
 
-DSV4CU_DEV float router_score(float x, const float *__restrict__ tab)
+// sqrtf(softplus(x)) evaluated in double and rounded once per function; kept
+// out of line so the common table path stays a few instructions long.
+static __device__ __noinline__ float router_score_slow(float x)
 {
-    const uint32_t u = __float_as_uint(x);
-    if (tab && (u & 0xFFFFu) == 0u) return __ldg(tab + (u >> 16));
     float sp;
     if (x > 20.0f) {
         sp = x;
@@ -39,89 +39,90 @@ DSV4CU_DEV float router_score(float x, const float *__restrict__ tab)
     return __fsqrt_rn(sp);
 }
 
-// One warp routes one token. n_experts <= 32 * RMAX_PER_LANE.
+DSV4CU_DEV float router_score(float x, const float *__restrict__ tab)
+{
+    const uint32_t u = __float_as_uint(x);
+    if (tab && (u & 0xFFFFu) == 0u) return __ldg(tab + (u >> 16));
+    return router_score_slow(x);
+}
+
+// One warp routes one token. n_experts <= 32 * RMAX_PER_LANE. sv / ov: this
+// warp's scratch of n_experts floats each (shared or global memory) for the
+// biased and unbiased scores. The loops stay rolled: the router runs once per
+// token right after the weight streams of the previous layer have cycled the
+// L2, so its code is fetched cold and its length is its cost.
 constexpr int RMAX_PER_LANE = 16;
 
 DSV4CU_DEV void route_token_warp(const float *__restrict__ tab, const float *__restrict__ logits,
                                  const float *__restrict__ bias, const int64_t *__restrict__ tid2eid, int token_id,
                                  int n_experts, int topk, float route_scale,
                                  int *__restrict__ idx_out, float *__restrict__ wts_out,
-                                 float *__restrict__ scores_out, float *__restrict__ orig_out)
+                                 float *__restrict__ scores_out, float *__restrict__ orig_out,
+                                 float *sv, float *ov)
 {
     const int lane = threadIdx.x & 31;
-    float sv[RMAX_PER_LANE], ov[RMAX_PER_LANE];
-    unsigned taken = 0u;   // bit j: expert lane + 32 j already selected
-#pragma unroll
-    for (int j = 0; j < RMAX_PER_LANE; j++) {
-        const int e = lane + 32 * j;
-        float o = 0.0f, s = 0.0f;
-        if (e < n_experts) {
-            o = router_score(logits[e], tab);
-            s = bias ? __fadd_rn(o, bias[e]) : o;
-            if (orig_out) orig_out[e] = o;
-            if (scores_out) scores_out[e] = s;
-        }
-        ov[j] = o;
-        sv[j] = s;
+#pragma unroll 1
+    for (int e = lane; e < n_experts; e += 32) {
+        const float o = router_score(logits[e], tab);
+        const float s = bias ? __fadd_rn(o, bias[e]) : o;
+        ov[e] = o;
+        sv[e] = s;
+        if (orig_out) orig_out[e] = o;
+        if (scores_out) scores_out[e] = s;
     }
-    int sel[16];
+    __syncwarp();
+    unsigned taken = 0u;    // bit j: expert lane + 32 j already selected
+    int my_sel = 0;         // lane k < topk keeps selection k
+#pragma unroll 1
     for (int k = 0; k < topk; k++) {
+        int best;
         if (tid2eid) {
-            sel[k] = (int)tid2eid[(int64_t)token_id * topk + k];
-            continue;
-        }
-        // First untaken index (its NaN score, if any, sticks like the scan's).
-        int first = 0x7FFFFFFF;
-        float bv = 0.0f;
-        int bi = 0x7FFFFFFF;
-#pragma unroll
-        for (int j = 0; j < RMAX_PER_LANE; j++) {
-            const int e = lane + 32 * j;
-            if (e >= n_experts || (taken >> j) & 1u) continue;
-            if (e < first) first = e;
-            const float v = sv[j];
-            if (isnan(v)) continue;
-            if (bi == 0x7FFFFFFF || v > bv) { bv = v; bi = e; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-            const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-            const int f2 = __shfl_xor_sync(0xFFFFFFFFu, first, o);
-            first = min(first, f2);
-            if (i2 != 0x7FFFFFFF && (bi == 0x7FFFFFFF || v2 > bv || (v2 == bv && i2 < bi))) {
-                bv = v2;
-                bi = i2;
+            best = (int)tid2eid[(int64_t)token_id * topk + k];
+        } else {
+            // The reference scan: best = first untaken expert, then strict '>'
+            // over the untaken ones in increasing order. So ties go to the lower
+            // index, a NaN score is skipped, and a NaN first candidate stays.
+            int first = 0x7FFFFFFF, bi = 0x7FFFFFFF;
+            float bv = 0.0f;
+#pragma unroll 1
+            for (int j = 0; j < RMAX_PER_LANE; j++) {
+                const int e = lane + 32 * j;
+                if (e >= n_experts) break;
+                if ((taken >> j) & 1u) continue;
+                first = min(first, e);
+                const float v = sv[e];
+                if (isnan(v)) continue;
+                if (bi == 0x7FFFFFFF || v > bv) {
+                    bv = v;
+                    bi = e;
+                }
             }
-        }
-        // The scan starts from the first untaken expert: a NaN there is kept.
-        const int fl = first & 31, fj = first >> 5;
-        float fsv = 0.0f;
 #pragma unroll
-        for (int j = 0; j < RMAX_PER_LANE; j++) if (j == fj) fsv = sv[j];
-        fsv = __shfl_sync(0xFFFFFFFFu, fsv, fl);
-        const int best = (first != 0x7FFFFFFF && (isnan(fsv) || bi == 0x7FFFFFFF)) ? first : bi;
-        sel[k] = best;
-        if ((best & 31) == lane) taken |= 1u << (best >> 5);
+            for (int o = 16; o > 0; o >>= 1) {
+                const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+                const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+                first = min(first, __shfl_xor_sync(0xFFFFFFFFu, first, o));
+                if (i2 != 0x7FFFFFFF && (bi == 0x7FFFFFFF || v2 > bv || (v2 == bv && i2 < bi))) {
+                    bv = v2;
+                    bi = i2;
+                }
+            }
+            const bool first_nan = first != 0x7FFFFFFF && isnan(sv[first]);
+            best = (first != 0x7FFFFFFF && (first_nan || bi == 0x7FFFFFFF)) ? first : bi;
+        }
+        if ((best & 31) == lane && best >= 0 && best < 32 * RMAX_PER_LANE) taken |= 1u << (best >> 5);
+        if (lane == k) my_sel = best;
     }
     // Weights from the unbiased scores; double sum in k order.
+    const bool in_range = my_sel >= 0 && my_sel < n_experts;
+    const float my_w = (lane < topk && in_range) ? ov[my_sel] : 0.0f;
     double sum = 0.0;
-    float w[16];
-    for (int k = 0; k < topk; k++) {
-        const int e = sel[k];
-        float o = 0.0f;
-#pragma unroll
-        for (int j = 0; j < RMAX_PER_LANE; j++) if (j == (e >> 5)) o = ov[j];
-        o = __shfl_sync(0xFFFFFFFFu, o, e & 31);
-        w[k] = o;
-        sum = __dadd_rn(sum, (double)o);
-    }
+#pragma unroll 1
+    for (int k = 0; k < topk; k++) sum = __dadd_rn(sum, (double)__shfl_sync(0xFFFFFFFFu, my_w, k));
     const float inv = (sum != 0.0) ? (float)__drcp_rn(sum) : 0.0f;
-    if (lane == 0) {
-        for (int k = 0; k < topk; k++) {
-            idx_out[k] = sel[k];
-            wts_out[k] = __fmul_rn(__fmul_rn(w[k], inv), route_scale);
-        }
+    if (lane < topk) {
+        idx_out[lane] = my_sel;
+        wts_out[lane] = __fmul_rn(__fmul_rn(my_w, inv), route_scale);
     }
 }
 
