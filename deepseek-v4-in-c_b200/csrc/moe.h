@@ -35,6 +35,7 @@ struct dsv4cu_moe {
     dsv4cu::MoeDev view;
     // Tensor-core path (mx_ok == 0 when a matrix does not qualify).
     int mx_ok;
+    int sms;                        // SM count of the layer's device (sizes the tensor-core work split)
     void *mx_block;                 // maps + scale blocks + pointer table, one allocation
     dsv4cu::MoeMxDev mx;
 };

@@ -5,26 +5,23 @@
 // (dsv4_ops.c:85-93), dsv4_swiglu (dsv4_ops.c:61-79) and the k-order combine
 // (dsv4_layer.c:109-116).
 //
-// Four launches, stream-ordered:
-//   route    one CTA: every token routed (one warp per token), the (token, k)
-//            pairs bucketed by expert in ascending expert order with tokens
+// Five launches, stream-ordered:
+//   prep     every CTA routes the tokens (one warp per token) and buckets the
+//            (token, k) pairs by expert in ascending expert order with tokens
 //            ascending inside a bucket (the layout of union_prepare,
 //            src/80_prefill/dsv4_prefill_union.c:30-52), the shared expert's
-//            bucket last; then the column tiles: every bucket cut into tiles of
-//            tpt slots (tile i: expert, first slot, slot count).
-//   split    each column tile's tokens written as e4m3 terms (mx_split_term)
-//            into the gate/up B operand.
-//   gate/up  mx_kernel over (column tile, w1 | w3, 128-row tile): the fp32
-//            results go to a per-slot gate/up buffer; of the two tiles of a
-//            (column tile, row tile) pair the one that finishes second applies
-//            SwiGLU to the 128 rows and writes them as e4m3 terms straight
-//            into the down projection's B operand.
-//   down     mx_kernel over (column tile, 128-row tile of w2): per-slot partial
-//            rows; the last tile of each 128-row slice sums, for every token,
-//            its pairs in k order with the routing weights and adds the shared
-//            expert unweighted.
+//            bucket last, and cuts the buckets into column tiles of tpt slots;
+//            CTA 0 publishes the tables, all CTAs write the gate/up B operand
+//            (the slots' tokens as e4m3 terms).
+//   gate/up  mx_kernel over (column tile, 128-row tile, w1 | w3): per-slot
+//            gate and up rows.
+//   swiglu   SwiGLU of every slot written as e4m3 terms: the down B operand.
+//   down     mx_kernel over (column tile, 128-row tile of w2): per-slot rows.
+//   combine  per token the routed pairs in k order with the routing weights,
+//            plus the shared expert unweighted.
 // Every weight byte of the touched experts is read once per step per column
-// tile (one column tile per expert at batch 1).
+// tile (one column tile per expert at batch 1). No step depends on the order
+// in which CTAs finish: the results are the same on every run.
 #include <stdio.h>
 #include <string.h>
 
@@ -56,8 +53,8 @@ struct MxMoeWs {
     int *c_slot0, *c_cnt, *c_expert;   // [max_tiles] column tiles
     uint8_t *xq1, *sfb1; // gate/up B operand and its scale blocks
     uint8_t *xq2, *sfb2; // down B operand and its scale blocks
-    float *gu;           // [npairs][2][inter]
-    float *ypart;        // [npairs][hidden]
+    float *gu;           // [npairs][2][inter] gate (w1) and up (w3) rows of each slot
+    float *ypart;        // [npairs][hidden] down projection of each slot
 };
 
 struct MxMoeShape {
@@ -65,7 +62,7 @@ struct MxMoeShape {
     int NB, tpt, KB, nbb, max_tiles, npairs, nbmax;
 };
 
-static MxMoeShape mxmoe_shape(const dsv4cu_moe *L, int topk, int nt)
+static MxMoeShape mxmoe_shape(const dsv4cu_moe *L, int topk, int nt, int sms)
 {
     MxMoeShape s;
     s.nt = nt;
@@ -84,6 +81,7 @@ static MxMoeShape mxmoe_shape(const dsv4cu_moe *L, int topk, int nt)
     s.nbmax = min(nt * topk, s.n_experts);
     // sum over buckets of ceil(cnt / tpt) <= slots / tpt + buckets
     s.max_tiles = (nt * topk) / s.tpt + s.nbmax + (s.has_shared ? nt / s.tpt + 1 : 0) + 1;
+    (void)sms;
     return s;
 }
 
@@ -301,7 +299,6 @@ struct MxMoeCommon {
     MoeMxDev L;
     MxMoeWs ws;
     int nb, nbb, tpt, terms, hidden, inter;
-    int *counters;
     int *err;
 };
 
@@ -316,14 +313,16 @@ DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc,
     T.a_tx = fp4 ? 128 * 64 : 128 * 128;
     T.a_row = rt * 128;
     T.b_row = i * c.nb;
+    T.k0 = 0;
     T.kc = kc;
     return T;
 }
 
+// Gate/up tiles, t = (i * RT + rt) * 2 + mat: column tile i, 128-row tile rt
+// of w1 (mat 0) or w3 (mat 1). Results go to the per-slot gate/up rows.
 struct MoeGateUp {
     struct Params {
         MxMoeCommon c;
-        float limit;
     };
     DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * 2 * (p.c.inter >> 7); }
     DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
@@ -332,11 +331,12 @@ struct MoeGateUp {
     DSV4CU_DEV static MxTile tile(const Params &p, int t)
     {
         const int RT = p.c.inter >> 7;
-        const int i = t / (2 * RT), rem = t - i * 2 * RT, mat = rem / RT, rt = rem - mat * RT;
+        const int mat = t & 1, pr = t >> 1, i = pr / RT, rt = pr - i * RT;
         MxTile T = mxmoe_tile(p.c, i, 3 * p.c.ws.c_expert[i] + mat, rt, p.c.hidden >> 7, p.c.ws.sfb1);
         T.id0 = i;
         T.id1 = mat;
         T.id2 = rt;
+        T.id3 = 0;
         return T;
     }
     DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v)
@@ -346,50 +346,14 @@ struct MoeGateUp {
             p.c.ws.gu[((size_t)slot * 2 + T.id1) * p.c.inter + T.id2 * 128 + row_l] = v;
         }
     }
-    // The second tile of a (column tile, row tile) pair applies SwiGLU
-    // (dsv4_ops.c:61-79: up clamped both ways, gate from above only) and writes
-    // the 128 mid values of each slot as e4m3 terms for the down projection.
-    DSV4CU_DEV static void finish(const Params &p, const MxTile &T, int row_l, int *word)
-    {
-        const int RT = p.c.inter >> 7;
-        int *ctr = p.c.counters + T.id0 * RT + T.id2;
-        __threadfence();
-        epi_sync();
-        if (row_l == 0) *word = atomicAdd(ctr, 1);
-        epi_sync();
-        const int first = (*word == 0);
-        epi_sync();                       // every thread has read *word
-        if (first) return;
-        if (row_l == 0) *ctr = 0;         // both tiles are done: ready for the next step
-        __threadfence();
-        const int i = T.id0, ii = T.id2 * 128 + row_l, kb = row_l >> 5;
-        const int cnt = p.c.ws.c_cnt[i], slot0 = p.c.ws.c_slot0[i];
-        const int kc2 = p.c.inter >> 7;
-        for (int tl = 0; tl < cnt; tl++) {
-            const size_t base = (size_t)(slot0 + tl) * 2 * p.c.inter;
-            float g = __ldcg(p.c.ws.gu + base + ii), u = __ldcg(p.c.ws.gu + base + p.c.inter + ii);
-            if (p.limit > 0.0f) {
-                u = fminf(fmaxf(u, -p.limit), p.limit);
-                g = fminf(g, p.limit);
-            }
-            const float mid = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-            uint8_t q[4], sb[4];
-            mx_split_all(mid, p.c.terms, q, sb);
-            for (int j = 0; j < p.c.terms; j++) {
-                const int n = j * p.c.tpt + tl;
-                p.c.ws.xq2[((size_t)i * p.c.nb + n) * p.c.inter + ii] = q[j];
-                if ((row_l & 31) == 0)
-                    p.c.ws.sfb2[((size_t)i * kc2 + T.id2) * p.c.nbb * 512 + mx_sfb_offset(n, kb)] = sb[j];
-            }
-        }
-    }
+    DSV4CU_DEV static void finish(const Params &, const MxTile &, int, int *) {}
+    DSV4CU_DEV static void finish_all(const Params &, int, int, int *) {}
 };
 
+// Down tiles, t = i * RTH + rt. Results go to the per-slot output rows.
 struct MoeDown {
     struct Params {
         MxMoeCommon c;
-        int nt, topk, has_shared;
-        float *out;
     };
     DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * (p.c.hidden >> 7); }
     DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
@@ -397,12 +361,13 @@ struct MoeDown {
     DSV4CU_DEV static int tpt(const Params &p) { return p.c.tpt; }
     DSV4CU_DEV static MxTile tile(const Params &p, int t)
     {
-        const int RT = p.c.hidden >> 7;
-        const int i = t / RT, rt = t - i * RT;
+        const int RTH = p.c.hidden >> 7;
+        const int i = t / RTH, rt = t - i * RTH;
         MxTile T = mxmoe_tile(p.c, i, 3 * p.c.ws.c_expert[i] + 2, rt, p.c.inter >> 7, p.c.ws.sfb2);
         T.id0 = i;
         T.id1 = 0;
         T.id2 = rt;
+        T.id3 = 0;
         return T;
     }
     DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v)
@@ -412,37 +377,62 @@ struct MoeDown {
             p.c.ws.ypart[(size_t)slot * p.c.hidden + T.id2 * 128 + row_l] = v;
         }
     }
-    // The last column tile to finish a 128-row slice combines it: per token
-    // the routed pairs IN k ORDER (dsv4_layer.c:109-113), then the shared
-    // expert unweighted (:115).
-    DSV4CU_DEV static void finish(const Params &p, const MxTile &T, int row_l, int *word)
-    {
-        int *ctr = p.c.counters + T.id2;
-        const int ntiles = p.c.ws.meta[2];
-        __threadfence();
-        epi_sync();
-        if (row_l == 0) *word = atomicAdd(ctr, 1);
-        epi_sync();
-        const int last = (*word == ntiles - 1);
-        epi_sync();
-        if (!last) return;
-        if (row_l == 0) *ctr = 0;
-        __threadfence();
-        const int row = T.id2 * 128 + row_l, nb = p.c.ws.meta[0];
-        for (int t = 0; t < p.nt; t++) {
-            float o = 0.0f;
-            for (int k = 0; k < p.topk; k++) {
-                const int slot = __ldcg(p.c.ws.pos + t * p.topk + k);
-                if (slot < 0) continue;
-                o = __fadd_rn(o, __fmul_rn(__ldcg(p.c.ws.wts + t * p.topk + k),
-                                           __ldcg(p.c.ws.ypart + (size_t)slot * p.c.hidden + row)));
-            }
-            if (p.has_shared)
-                o = __fadd_rn(o, __ldcg(p.c.ws.ypart + (size_t)(__ldcg(p.c.ws.b_off + nb) + t) * p.c.hidden + row));
-            p.out[(size_t)t * p.c.hidden + row] = o;
-        }
-    }
+    DSV4CU_DEV static void finish(const Params &, const MxTile &, int, int *) {}
+    DSV4CU_DEV static void finish_all(const Params &, int, int, int *) {}
 };
+
+// SwiGLU (dsv4_ops.c:61-79: up clamped both ways, gate from above only) of
+// every slot, written as e4m3 terms (mx_split_all) into the down projection's
+// B operand: one warp per (column tile, slot, 32-row block of inter).
+__global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter, int terms, int tpt, int NB,
+                                                           float limit, int max_items)
+{
+    const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    const int nblk = inter >> 5, ntiles = ws.meta[2];
+    if (gw >= max_items) return;
+    const int it = gw / nblk, blk = gw - it * nblk, i = it / tpt, tl = it - i * tpt;
+    if (i >= ntiles || tl >= ws.c_cnt[i]) return;
+    const int slot = ws.c_slot0[i] + tl, ii = blk * 32 + lane;
+    float g = ws.gu[(size_t)slot * 2 * inter + ii], u = ws.gu[((size_t)slot * 2 + 1) * inter + ii];
+    if (limit > 0.0f) {
+        u = fminf(fmaxf(u, -limit), limit);
+        g = fminf(g, limit);
+    }
+    const float mid = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+    uint8_t q[4], sb[4];
+    mx_split_all(mid, terms, q, sb);
+    const int nbb = (NB + 127) / 128;
+    for (int j = 0; j < terms; j++) {
+        const int n = j * tpt + tl;
+        ws.xq2[((size_t)i * NB + n) * inter + ii] = q[j];
+        if (lane == 0) ws.sfb2[((size_t)i * (inter >> 7) + (blk >> 2)) * nbb * 512 + mx_sfb_offset(n, blk & 3)] = sb[j];
+    }
+}
+
+// Output rows: per token the routed pairs IN k ORDER with the routing
+// weights (dsv4_layer.c:109-113), then the shared expert unweighted (:115).
+__global__ void __launch_bounds__(256) mxmoe_combine_kernel(MxMoeWs ws, int nt, int topk, int hidden,
+                                                            int has_shared, float *__restrict__ out)
+{
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)nt * hidden) return;
+    const int t = (int)(i / hidden), row = (int)(i - (long)t * hidden);
+    int slot[MXMOE_MAX_TOPK];
+    float w[MXMOE_MAX_TOPK], y[MXMOE_MAX_TOPK];
+#pragma unroll
+    for (int k = 0; k < MXMOE_MAX_TOPK; k++) {
+        slot[k] = k < topk ? ws.pos[t * topk + k] : -1;
+        w[k] = k < topk ? ws.wts[t * topk + k] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < MXMOE_MAX_TOPK; k++) y[k] = slot[k] >= 0 ? ws.ypart[(size_t)slot[k] * hidden + row] : 0.0f;
+    float o = 0.0f;
+#pragma unroll
+    for (int k = 0; k < MXMOE_MAX_TOPK; k++)
+        if (slot[k] >= 0) o = __fadd_rn(o, __fmul_rn(w[k], y[k]));
+    if (has_shared) o = __fadd_rn(o, ws.ypart[(size_t)(ws.b_off[ws.meta[0]] + t) * hidden + row]);
+    out[i] = o;
+}
 
 // ------------------------------------------------------------ host side
 template <int NB, int KB, class P>
@@ -512,13 +502,15 @@ static int cached_bmap(CUtensorMap *out, const void *base, uint64_t inner, uint6
 
 size_t moe_mx_workspace(const dsv4cu_moe *L, int topk, int nt)
 {
-    return mxmoe_layout(mxmoe_shape(L, topk, nt), nullptr, nullptr);
+    return mxmoe_layout(mxmoe_shape(L, topk, nt, L->sms), nullptr, nullptr);
 }
 
 int moe_mx_prepare(dsv4cu_moe *L, const dsv4cu_expert *hexp)
 {
     L->mx_ok = 0;
     L->mx_block = nullptr;
+    L->sms = 148;
+    cudaDeviceGetAttribute(&L->sms, cudaDevAttrMultiProcessorCount, L->device);
     const int nm = 3 * (L->n_experts + 1);
     std::vector<const dsv4cu_qmat *> qs(nm);
     for (int e = 0; e <= L->n_experts; e++) {
@@ -589,12 +581,11 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     if (nt > MXMOE_MAX_NT || topk > MXMOE_MAX_TOPK || L->n_experts > PREP_MAX_EXPERTS)
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: nt %d / topk %d / experts %d beyond 64 / 16 / 512",
                                 nt, topk, L->n_experts);
-    const MxMoeShape s = mxmoe_shape(L, topk, nt);
+    const MxMoeShape s = mxmoe_shape(L, topk, nt, L->sms);
     MxMoeWs ws;
     mxmoe_layout(s, (char *)wsp, &ws);
     const int RT = s.inter / 128, RTH = s.hidden / 128;
-    if ((size_t)s.max_tiles * RT + RTH > DSV4CU_MAX_COUNTERS)
-        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: too many tiles for the counter table");
+    (void)counters;
     const float *tab = router_table_get();
     if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_decode: router table setup failed");
 
@@ -640,25 +631,27 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
 
     MoeGateUp::Params pg;
     pg.c = c;
-    pg.c.counters = counters;
-    pg.limit = limit;
     int kb1 = s.KB;
     while (kb1 > 1 && (s.hidden / 128) % kb1) kb1 >>= 1;
     r = mxmoe_dispatch<MoeGateUp>(s.NB, kb1, tb1, pg, g1, st);
     if (r) return r;
+    {
+        const int items = s.max_tiles * s.tpt * (s.inter / 32);
+        mxmoe_swiglu_kernel<<<(items * 32 + 255) / 256, 256, 0, st>>>(ws, s.inter, MX_TERMS, s.tpt, s.NB, limit,
+                                                                       items);
+        DSV4CU_LAUNCH_CHECK();
+    }
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
 
     MoeDown::Params pd;
     pd.c = c;
-    pd.c.counters = counters + (size_t)s.max_tiles * RT;
-    pd.nt = nt;
-    pd.topk = topk;
-    pd.has_shared = s.has_shared;
-    pd.out = out;
     int kb2 = s.KB;
     while (kb2 > 1 && (s.inter / 128) % kb2) kb2 >>= 1;
     r = mxmoe_dispatch<MoeDown>(s.NB, kb2, tb2, pd, g2, st);
     if (r) return r;
+    mxmoe_combine_kernel<<<(unsigned)(((long)nt * s.hidden + 255) / 256), 256, 0, st>>>(ws, nt, topk, s.hidden,
+                                                                                      s.has_shared, out);
+    DSV4CU_LAUNCH_CHECK();
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
     return DSV4CU_OK;
 }

@@ -21,7 +21,8 @@
 //               to the producer (tcgen05.commit); after a tile's last stage
 //               the accumulator goes to the epilogue;
 //   warps 2-5   epilogue: tcgen05.ld (TMEM lane = tile row), the terms of a
-//               token summed, then P::store per value and P::finish per tile.
+//               token summed, then P::store per value and P::finish per tile;
+//               after the CTA's last tile P::finish_all (cross-CTA reductions).
 // Two accumulators in TMEM (when they fit) let tile i's epilogue overlap tile
 // i+1's MMAs. Waits are bounded by 2 s of %globaltimer: a timeout records an
 // error code, the roles stop, in-flight copies and MMAs drain, TMEM is freed.
@@ -44,12 +45,16 @@ struct MxTile {
     uint32_t a_tx;           // global bytes of one A box
     int a_row;               // first weight row
     int b_row;               // first row of the B term buffer
-    int kc;                  // 128-wide K chunks
-    int id0, id1, id2;       // problem-specific tile coordinates
+    int k0;                  // first 128-wide K chunk (a K segment of a split tile)
+    int kc;                  // 128-wide K chunks of this tile
+    int id0, id1, id2, id3;  // problem-specific tile coordinates
 };
 
 constexpr int MX_THREADS = 192;
-constexpr int MX_SMEM_BUDGET = 227 * 1024 - 2048;
+constexpr int MX_TCACHE = 32;
+// Dynamic shared memory for the stage ring: 227 KB less the 1 KB alignment
+// slack and 4 KB for the kernel's static shared variables.
+constexpr int MX_SMEM_BUDGET = 227 * 1024 - 1024 - 4096;
 
 template <int NB, int KB>
 struct MxCfg {
@@ -160,7 +165,10 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accf[2], acce[2], drain;
     __shared__ uint32_t tmem_holder;
     __shared__ volatile int abort_flag;
-    __shared__ int epi_word;     // policy scratch word (epilogue warps only)
+    __shared__ int epi_words[64];    // policy scratch (epilogue warps only)
+    // Descriptors of this CTA's first MX_TCACHE tiles, resolved once up front
+    // (a policy's tile() may chase table entries in global memory).
+    __shared__ MxTile tcache[MX_TCACHE];
 
     uint8_t *smem = (uint8_t *)(((uintptr_t)mx_smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -184,17 +192,30 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         umma::tmem_alloc(&tmem_holder, C::TMEM_COLS);
         umma::tmem_relinquish();
     }
+    if (warp >= 2) {
+        const int j = threadIdx.x - 64, t = blockIdx.x + j * gridDim.x;
+        if (j < MX_TCACHE && t < ntiles) {
+            const MxTile T = P::tile(p, t);
+            tcache[j] = T;
+            // A tile switch usually changes matrices: have the TMA unit fetch
+            // the descriptor now rather than on the tile's first load.
+            asm volatile("prefetch.tensormap [%0];" ::"l"(T.ta) : "memory");
+        }
+    }
     umma::fence_before();
     __syncthreads();
+    // k-th tile of this CTA (tile index t).
+    auto tile_of = [&](int t, int k) -> MxTile { return k < MX_TCACHE ? tcache[k] : P::tile(p, t); };
     umma::fence_after();
     const uint32_t tmem = tmem_holder;
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            int it = 0;
-            for (int t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x) {
-                const MxTile T = P::tile(p, t);
+            int it = 0, k = 0;
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&tb) : "memory");
+            for (int t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x, k++) {
+                const MxTile T = tile_of(t, k);
                 const uint32_t tx = KB * (T.a_tx + C::B_BOX + C::SFA_BOX + C::SFB_BOX);
                 const int nst = T.kc / KB;
                 for (int c = 0; c < nst; c++, it++) {
@@ -207,7 +228,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
                     mbar_arrive_expect_tx(&full[s], tx);
 #pragma unroll
                     for (int b = 0; b < KB; b++) {
-                        const int kc = c * KB + b;
+                        const int kc = T.k0 + c * KB + b;
                         tma_load_2d(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s]);
                         tma_load_2d(st + C::OFF_B + b * C::B_BOX, &tb, kc * 128, T.b_row, &full[s]);
                         bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
@@ -226,7 +247,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         if (lane == 0) {
             int it = 0, tcount = 0;
             for (int t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x, tcount++) {
-                const MxTile T = P::tile(p, t);
+                const MxTile T = tile_of(t, tcount);
                 const int nst = T.kc / KB;
                 const int ab = tcount % C::ACC_BUFS, use = tcount / C::ACC_BUFS;
                 if (use > 0 && !mbar_wait(&acce[ab], (use - 1) & 1, err, MXE_ACC_EMPTY)) {
@@ -290,7 +311,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
             epi_sync();
             if (abort_flag) break;      // every epilogue warp leaves at the same tile
             umma::fence_after();
-            const MxTile T = P::tile(p, t);
+            const MxTile T = tile_of(t, tcount);
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * NB;
             if constexpr (NB <= 16) {
                 // Narrow tiles: all NB columns at once, then per token.
@@ -327,8 +348,9 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
             umma::fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[ab]);
-            P::finish(p, T, row_l, &epi_word);
+            P::finish(p, T, row_l, epi_words);
         }
+        if (!abort_flag) P::finish_all(p, row_l, ntiles, epi_words);
     }
 
     umma::fence_before();

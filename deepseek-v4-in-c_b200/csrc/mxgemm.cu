@@ -95,6 +95,7 @@ struct DenseMx {
         T.a_tx = p.a_tx;
         T.a_row = tm * 128;
         T.b_row = tn * p.nb;
+        T.k0 = 0;
         T.kc = p.kc;
         T.id0 = tm;
         T.id1 = tn;
@@ -107,6 +108,7 @@ struct DenseMx {
         if (tl < p.tpt && row < p.rows && tok < p.nt) p.y[(size_t)tok * p.ldy + row] = v;
     }
     DSV4CU_DEV static void finish(const Params &, const MxTile &, int, int *) {}
+    DSV4CU_DEV static void finish_all(const Params &, int, int, int *) {}
 };
 
 // ------------------------------------------------------------ host side
