@@ -11,6 +11,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <utility>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -151,3 +152,32 @@ DSV4CU_DEV uint32_t float_order_key(float f)
     } while (0)
 
 extern "C" int dsv4cu_set_error(int code, const char *fmt, ...);
+
+namespace dsv4cu {
+
+// Programmatic dependent launch (sm_90+): a kernel launched with
+// launch_pdl may start while the previous kernel on the stream is still
+// running; it must call pdl_wait() before it reads anything that kernel
+// writes. pdl_trigger() lets the next kernel start launching once every CTA
+// of this grid has executed it (or exited).
+DSV4CU_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+DSV4CU_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                     Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace dsv4cu

@@ -46,15 +46,12 @@ __global__ void route_kernel(const float *tab, int *idx, float *wts, float *scor
                              const float *bias, const int64_t *tid2eid, const int *token_ids, int n_experts,
                              int topk, float route_scale, int nt)
 {
-    extern __shared__ float route_scratch[];   // [warps][2][n_experts]
-    const int w = threadIdx.x >> 5;
-    const int t = blockIdx.x * (blockDim.x >> 5) + w;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= nt) return;
-    float *sv = route_scratch + (size_t)w * 2 * n_experts;
     route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0, n_experts,
                      topk, route_scale, idx + (size_t)t * topk, wts + (size_t)t * topk,
                      scores ? scores + (size_t)t * n_experts : nullptr,
-                     orig ? orig + (size_t)t * n_experts : nullptr, sv, sv + n_experts);
+                     orig ? orig + (size_t)t * n_experts : nullptr);
 }
 
 // SwiGLU exactly as dsv4_swiglu (src/10_compute/dsv4_ops.c:61-79).
@@ -196,7 +193,7 @@ extern "C" int dsv4cu_route(int *idx, float *wts, float *scores, float *orig, co
     if (nt <= 0) return DSV4CU_OK;
     const float *tab = router_table_get();
     if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "route: router table setup failed");
-    route_kernel<<<(nt + 3) / 4, 128, (size_t)4 * 2 * n_experts * sizeof(float), (cudaStream_t)stream>>>(tab, idx, wts, scores, orig, logits, bias, tid2eid,
+    route_kernel<<<(nt + 3) / 4, 128, 0, (cudaStream_t)stream>>>(tab, idx, wts, scores, orig, logits, bias, tid2eid,
                                                                   token_ids, n_experts, topk, route_scale, nt);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;

@@ -89,13 +89,10 @@ __global__ void __launch_bounds__(1024) moe_prologue_kernel(
         return;
     }
 
-    // CTA 0: routing, one warp per token (eight routing warps).
-    __shared__ float rsc[8][2][32 * RMAX_PER_LANE];
-    if (warp < 8)
-        for (int t = warp; t < nt; t += 8)
-            route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0,
-                             n_experts, topk, route_scale, ws.idx + t * topk, ws.wts + t * topk, nullptr, nullptr,
-                             rsc[warp][0], rsc[warp][1]);
+    // CTA 0: routing, one warp per token.
+    for (int t = warp; t < nt; t += nwarps)
+        route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0,
+                         n_experts, topk, route_scale, ws.idx + t * topk, ws.wts + t * topk, nullptr, nullptr);
     __syncthreads();
 
     // Bucket the pairs by expert. counts[e] then an exclusive scan over experts

@@ -142,7 +142,6 @@ constexpr int PREP_MAX_PAIRS = MXMOE_MAX_NT * MXMOE_MAX_TOPK;            // 1024
 constexpr int PREP_MAX_SLOTS = PREP_MAX_PAIRS + MXMOE_MAX_NT;
 constexpr int PREP_MAX_EXPERTS = 32 * RMAX_PER_LANE;                      // 512
 constexpr int PREP_MAX_TILES = PREP_MAX_PAIRS / 2 + PREP_MAX_EXPERTS + MXMOE_MAX_NT + 2;
-constexpr int PREP_ROUTE_WARPS = 16;
 
 // Every CTA routes all nt tokens (one warp per token), buckets the (token, k)
 // pairs by expert in ascending expert order with tokens ascending inside a
@@ -160,21 +159,125 @@ __global__ void __launch_bounds__(1024) mxmoe_prep_kernel(
     __shared__ int s_idx[PREP_MAX_PAIRS];
     __shared__ float s_wts[PREP_MAX_PAIRS];
     __shared__ int s_pos[PREP_MAX_PAIRS];
-    __shared__ int s_cnt[PREP_MAX_EXPERTS + 2], s_off[PREP_MAX_EXPERTS + 2], s_bid[PREP_MAX_EXPERTS + 2];
-    __shared__ int s_bexp[PREP_MAX_EXPERTS + 2], s_boff[PREP_MAX_EXPERTS + 3], s_btiles[PREP_MAX_EXPERTS + 2];
+    // Scratch: router scores first (2 x 1024 floats), then per-expert tables.
+    __shared__ int s_scratch[2048];
+    __shared__ int s_cnt[PREP_MAX_EXPERTS + 2];
+    __shared__ int s_bexp[PREP_MAX_EXPERTS + 2], s_boff[PREP_MAX_EXPERTS + 3];
     __shared__ int s_btok[PREP_MAX_SLOTS];
     __shared__ int s_tslot[PREP_MAX_TILES], s_tcnt[PREP_MAX_TILES], s_texp[PREP_MAX_TILES];
+    __shared__ int s_sorted[32];
     __shared__ int s_nb, s_ntiles, s_bad;
-    extern __shared__ float s_route[];      // [route_warps][2][n_experts]
+    int *s_off = s_scratch, *s_bid = s_scratch + 514, *s_btiles = s_scratch + 1028;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const int npairs = nt * topk;
-    const int rw = min(nt, PREP_ROUTE_WARPS);
+    pdl_wait();       // x and the logits come from the previous kernel
+    pdl_trigger();
 
-    if (warp < rw)
-        for (int t = warp; t < nt; t += rw)
+    // ---- routing (dsv4_route, src/10_compute/dsv4_ops.c:117-156)
+    bool warp_route = tid2eid != nullptr || nt * n_experts > (int)blockDim.x;
+    if (!warp_route) {
+        // Small batches: one thread per (token, expert). Without NaN scores,
+        // repeated arg-max with strict '>' in increasing index order selects
+        // exactly the experts of rank < topk under (score desc, index asc),
+        // in that rank order.
+        float *r_s = (float *)s_scratch, *r_o = (float *)s_scratch + 1024;
+        const int t = threadIdx.x / n_experts, e = threadIdx.x - t * n_experts;
+        const bool act = t < nt;
+        bool nan = false;
+        if (act) {
+            const float o = router_score(logits[(size_t)t * n_experts + e], tab);
+            const float sv = bias ? __fadd_rn(o, bias[e]) : o;
+            r_o[threadIdx.x] = o;
+            r_s[threadIdx.x] = sv;
+            nan = isnan(sv);
+        }
+        warp_route = __syncthreads_or(nan);
+        if (!warp_route) {
+            if (act) {
+                const float v = r_s[threadIdx.x], *row = r_s + t * n_experts;
+                int r = 0;
+                for (int q = 0; q < n_experts; q++) {
+                    const float w = row[q];
+                    r += (w > v) || (w == v && q < e);
+                }
+                if (r < topk) s_idx[t * topk + r] = e;
+            }
+            __syncthreads();
+            if ((int)threadIdx.x < nt) {
+                // Weights from the unbiased scores; double sum in k order.
+                const int tt = threadIdx.x;
+                double sum = 0.0;
+                for (int k = 0; k < topk; k++) sum = __dadd_rn(sum, (double)r_o[tt * n_experts + s_idx[tt * topk + k]]);
+                const float inv = (sum != 0.0) ? (float)__drcp_rn(sum) : 0.0f;
+                for (int k = 0; k < topk; k++)
+                    s_wts[tt * topk + k] =
+                        __fmul_rn(__fmul_rn(r_o[tt * n_experts + s_idx[tt * topk + k]], inv), route_scale);
+            }
+        }
+        __syncthreads();
+    }
+    if (warp_route) {
+        // Hash layers, NaN scores, larger batches: one warp per token.
+        for (int t = warp; t < nt; t += nwarps)
             route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0,
-                             n_experts, topk, route_scale, s_idx + t * topk, s_wts + t * topk, nullptr, nullptr,
-                             s_route + (size_t)warp * 2 * n_experts, s_route + ((size_t)warp * 2 + 1) * n_experts);
+                             n_experts, topk, route_scale, s_idx + t * topk, s_wts + t * topk, nullptr, nullptr);
+        __syncthreads();
+    }
+
+    // ---- buckets and column tiles
+    if (npairs <= 32) {
+        // One warp sorts the pairs by (expert, pair index): slot = rank.
+        if (warp == 0) {
+            const int p = lane;
+            const bool live = p < npairs;
+            const int e0 = live ? s_idx[p] : -1;
+            const bool ok = live && e0 >= 0 && e0 < n_experts;
+            const int key = ok ? e0 : 0x7FFFFFFF;
+            int rank = 0;
+            for (int q = 0; q < 32; q++) {
+                const int kq = __shfl_sync(0xFFFFFFFFu, key, q);
+                rank += (q < npairs) && (kq < key || (kq == key && q < p));
+            }
+            const int routed = __popc(__ballot_sync(0xFFFFFFFFu, ok));
+            const bool bad = __any_sync(0xFFFFFFFFu, live && !ok);
+            if (ok) {
+                s_pos[p] = rank;
+                s_btok[rank] = p / topk;
+                s_sorted[rank] = e0;
+            } else if (live) {
+                s_pos[p] = -1;
+            }
+            __syncwarp();
+            const int el = lane < routed ? s_sorted[lane] : -1;
+            const bool head = lane < routed && (lane == 0 || s_sorted[lane - 1] != el);
+            const unsigned hm = __ballot_sync(0xFFFFFFFFu, head);
+            const int nb = __popc(hm);
+            if (head) {
+                const int bi = __popc(hm & ((1u << lane) - 1u));
+                s_bexp[bi] = el;
+                s_boff[bi] = lane;
+            }
+            if (has_shared)
+                for (int t = lane; t < nt; t += 32) s_btok[routed + t] = t;
+            __syncwarp();
+            if (lane == 0) {
+                s_nb = nb;
+                s_bad = bad;
+                s_boff[nb] = routed;
+                s_boff[nb + 1] = routed + (has_shared ? nt : 0);
+                int n = 0;
+                for (int b = 0; b < nb + (has_shared ? 1 : 0); b++) {
+                    const int s0 = s_boff[b], c = s_boff[b + 1] - s0, e = b < nb ? s_bexp[b] : n_experts;
+                    for (int j = 0; j < c && n < PREP_MAX_TILES; j += tpt, n++) {
+                        s_tslot[n] = s0 + j;
+                        s_tcnt[n] = min(tpt, c - j);
+                        s_texp[n] = e;
+                    }
+                }
+                s_ntiles = n;
+            }
+        }
+    } else {
     for (int e = threadIdx.x; e <= n_experts; e += blockDim.x) s_cnt[e] = 0;
     if (threadIdx.x == 0) s_bad = 0;
     __syncthreads();
@@ -244,6 +347,7 @@ __global__ void __launch_bounds__(1024) mxmoe_prep_kernel(
             }
         }
         if (lane == 0) s_ntiles = ntiles;
+    }
     }
     __syncthreads();
     const int nb = s_nb, ntiles = s_ntiles, nslots = npairs + (has_shared ? nt : 0);
@@ -387,6 +491,8 @@ struct MoeDown {
 __global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter, int terms, int tpt, int NB,
                                                            float limit, int max_items)
 {
+    pdl_wait();
+    pdl_trigger();
     const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     const int nblk = inter >> 5, ntiles = ws.meta[2];
     if (gw >= max_items) return;
@@ -414,6 +520,8 @@ __global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter
 __global__ void __launch_bounds__(256) mxmoe_combine_kernel(MxMoeWs ws, int nt, int topk, int hidden,
                                                             int has_shared, float *__restrict__ out)
 {
+    pdl_wait();
+    pdl_trigger();
     const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
     if (i >= (long)nt * hidden) return;
     const int t = (int)(i / hidden), row = (int)(i - (long)t * hidden);
@@ -440,8 +548,7 @@ static int mxmoe_launch(const CUtensorMap &tb, const typename P::Params &p, int 
 {
     int r = mx_kernel_prepare<NB, KB, P>();
     if (r) return r;
-    mx_kernel<NB, KB, P><<<grid, MX_THREADS, MxCfg<NB, KB>::SMEM, st>>>(tb, p);
-    DSV4CU_LAUNCH_CHECK();
+    DSV4CU_CUDA_TRY(launch_pdl(mx_kernel<NB, KB, P>, dim3(grid), dim3(MX_THREADS), MxCfg<NB, KB>::SMEM, st, tb, p));
     return DSV4CU_OK;
 }
 
@@ -594,20 +701,9 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
         // Every SM takes part in the split; each CTA repeats the (cheap) routing.
         const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 32);
         const int grid = (int)min((long)sms, max(1L, (tasks + 31) / 32));
-        const int rw = min(nt, PREP_ROUTE_WARPS);
-        const size_t dsm = (size_t)rw * 2 * s.n_experts * sizeof(float);
-        static volatile int prep_attr[64];
-        int dev = 0;
-        DSV4CU_CUDA_TRY(cudaGetDevice(&dev));
-        if (dev < 0 || dev >= 64 || !prep_attr[dev]) {
-            DSV4CU_CUDA_TRY(cudaFuncSetAttribute(mxmoe_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)(PREP_ROUTE_WARPS * 2 * PREP_MAX_EXPERTS * sizeof(float))));
-            if (dev >= 0 && dev < 64) prep_attr[dev] = 1;
-        }
-        mxmoe_prep_kernel<<<grid, 1024, dsm, st>>>(tab, x, logits, bias, tid2eid, token_ids, s.n_experts, topk,
-                                                 route_scale, nt, s.hidden, s.has_shared, MX_TERMS, s.tpt, s.NB, ws,
-                                                 idx_out, wts_out);
-        DSV4CU_LAUNCH_CHECK();
+        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_prep_kernel, dim3(grid), dim3(1024), 0, st, tab, x, logits, bias, tid2eid,
+                                   token_ids, s.n_experts, topk, route_scale, nt, s.hidden, s.has_shared, MX_TERMS,
+                                   s.tpt, s.NB, ws, idx_out, wts_out));
     }
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
 
@@ -637,9 +733,8 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     if (r) return r;
     {
         const int items = s.max_tiles * s.tpt * (s.inter / 32);
-        mxmoe_swiglu_kernel<<<(items * 32 + 255) / 256, 256, 0, st>>>(ws, s.inter, MX_TERMS, s.tpt, s.NB, limit,
-                                                                       items);
-        DSV4CU_LAUNCH_CHECK();
+        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_swiglu_kernel, dim3((items * 32 + 255) / 256), dim3(256), 0, st, ws, s.inter,
+                                   MX_TERMS, s.tpt, s.NB, limit, items));
     }
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
 
@@ -649,9 +744,8 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     while (kb2 > 1 && (s.inter / 128) % kb2) kb2 >>= 1;
     r = mxmoe_dispatch<MoeDown>(s.NB, kb2, tb2, pd, g2, st);
     if (r) return r;
-    mxmoe_combine_kernel<<<(unsigned)(((long)nt * s.hidden + 255) / 256), 256, 0, st>>>(ws, nt, topk, s.hidden,
-                                                                                      s.has_shared, out);
-    DSV4CU_LAUNCH_CHECK();
+    DSV4CU_CUDA_TRY(launch_pdl(mxmoe_combine_kernel, dim3((unsigned)(((long)nt * s.hidden + 255) / 256)), dim3(256), 0,
+                               st, ws, nt, topk, s.hidden, s.has_shared, out));
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
     return DSV4CU_OK;
 }

@@ -172,7 +172,6 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 
     uint8_t *smem = (uint8_t *)(((uintptr_t)mx_smem_raw + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = P::ntiles(p);
     int *err = P::err(p);
 
     if (threadIdx.x == 0) {
@@ -192,6 +191,10 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         umma::tmem_alloc(&tmem_holder, C::TMEM_COLS);
         umma::tmem_relinquish();
     }
+    // Set-up above overlaps the previous kernel; its outputs are read below.
+    pdl_wait();
+    pdl_trigger();
+    const int ntiles = P::ntiles(p);
     if (warp >= 2) {
         const int j = threadIdx.x - 64, t = blockIdx.x + j * gridDim.x;
         if (j < MX_TCACHE && t < ntiles) {

@@ -46,33 +46,54 @@ DSV4CU_DEV float router_score(float x, const float *__restrict__ tab)
     return router_score_slow(x);
 }
 
-// One warp routes one token. n_experts <= 32 * RMAX_PER_LANE. sv / ov: this
-// warp's scratch of n_experts floats each (shared or global memory) for the
-// biased and unbiased scores. The loops stay rolled: the router runs once per
-// token right after the weight streams of the previous layer have cycled the
-// L2, so its code is fetched cold and its length is its cost.
+// One warp routes one token; n_experts <= 32 * RMAX_PER_LANE. Expert
+// lane + 32 j is held by lane `lane` in slot j. All logit and table loads are
+// issued before any use (the router runs right after the previous layer's
+// weight streams have cycled the L2, so each load is a DRAM round trip), and
+// each selection round is two warp reductions (redux.sync) of an
+// order-preserving key.
 constexpr int RMAX_PER_LANE = 16;
+
+DSV4CU_DEV uint32_t route_key(float v)
+{
+    const uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);   // -0 ties with +0, as '>' does
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
 
 DSV4CU_DEV void route_token_warp(const float *__restrict__ tab, const float *__restrict__ logits,
                                  const float *__restrict__ bias, const int64_t *__restrict__ tid2eid, int token_id,
                                  int n_experts, int topk, float route_scale,
                                  int *__restrict__ idx_out, float *__restrict__ wts_out,
-                                 float *__restrict__ scores_out, float *__restrict__ orig_out,
-                                 float *sv, float *ov)
+                                 float *__restrict__ scores_out, float *__restrict__ orig_out)
 {
     const int lane = threadIdx.x & 31;
-#pragma unroll 1
-    for (int e = lane; e < n_experts; e += 32) {
-        const float o = router_score(logits[e], tab);
-        const float s = bias ? __fadd_rn(o, bias[e]) : o;
-        ov[e] = o;
-        sv[e] = s;
-        if (orig_out) orig_out[e] = o;
-        if (scores_out) scores_out[e] = s;
+    float ov[RMAX_PER_LANE], sv[RMAX_PER_LANE];
+#pragma unroll
+    for (int j = 0; j < RMAX_PER_LANE; j++) {
+        const int e = lane + 32 * j;
+        ov[j] = e < n_experts ? logits[e] : 0.0f;
+        sv[j] = (bias && e < n_experts) ? bias[e] : 0.0f;
     }
-    __syncwarp();
+    bool fast[RMAX_PER_LANE];
+#pragma unroll
+    for (int j = 0; j < RMAX_PER_LANE; j++) {
+        const uint32_t u = __float_as_uint(ov[j]);
+        fast[j] = tab && (u & 0xFFFFu) == 0u;
+        if (lane + 32 * j < n_experts && fast[j]) ov[j] = __ldg(tab + (u >> 16));
+    }
+#pragma unroll
+    for (int j = 0; j < RMAX_PER_LANE; j++) {
+        const int e = lane + 32 * j;
+        if (e >= n_experts) continue;
+        if (!fast[j]) ov[j] = router_score_slow(ov[j]);
+        sv[j] = bias ? __fadd_rn(ov[j], sv[j]) : ov[j];
+        if (orig_out) orig_out[e] = ov[j];
+        if (scores_out) scores_out[e] = sv[j];
+    }
     unsigned taken = 0u;    // bit j: expert lane + 32 j already selected
     int my_sel = 0;         // lane k < topk keeps selection k
+    float my_w = 0.0f;
+    double sum = 0.0;
 #pragma unroll 1
     for (int k = 0; k < topk; k++) {
         int best;
@@ -82,43 +103,46 @@ DSV4CU_DEV void route_token_warp(const float *__restrict__ tab, const float *__r
             // The reference scan: best = first untaken expert, then strict '>'
             // over the untaken ones in increasing order. So ties go to the lower
             // index, a NaN score is skipped, and a NaN first candidate stays.
-            int first = 0x7FFFFFFF, bi = 0x7FFFFFFF;
-            float bv = 0.0f;
-#pragma unroll 1
+            uint32_t bkey = 0u, first = 0xFFFFFFFFu, bi = 0xFFFFFFFFu;
+#pragma unroll
             for (int j = 0; j < RMAX_PER_LANE; j++) {
                 const int e = lane + 32 * j;
-                if (e >= n_experts) break;
-                if ((taken >> j) & 1u) continue;
-                first = min(first, e);
-                const float v = sv[e];
-                if (isnan(v)) continue;
-                if (bi == 0x7FFFFFFF || v > bv) {
-                    bv = v;
-                    bi = e;
+                if (e >= n_experts || ((taken >> j) & 1u)) continue;
+                first = min(first, (uint32_t)e);
+                if (isnan(sv[j])) continue;
+                const uint32_t kv = route_key(sv[j]);
+                if (bi == 0xFFFFFFFFu || kv > bkey) {
+                    bkey = kv;
+                    bi = (uint32_t)e;
                 }
             }
+            const uint32_t kmax = __reduce_max_sync(0xFFFFFFFFu, bi != 0xFFFFFFFFu ? bkey : 0u);
+            const uint32_t any = __ballot_sync(0xFFFFFFFFu, bi != 0xFFFFFFFFu);
+            const uint32_t wbi = __reduce_min_sync(0xFFFFFFFFu, (bi != 0xFFFFFFFFu && bkey == kmax) ? bi : 0xFFFFFFFFu);
+            const uint32_t wfirst = __reduce_min_sync(0xFFFFFFFFu, first);
+            // NaN at the first untaken expert: read from its owner lane.
+            float fsv = 0.0f;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float v2 = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-                const int i2 = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-                first = min(first, __shfl_xor_sync(0xFFFFFFFFu, first, o));
-                if (i2 != 0x7FFFFFFF && (bi == 0x7FFFFFFF || v2 > bv || (v2 == bv && i2 < bi))) {
-                    bv = v2;
-                    bi = i2;
-                }
-            }
-            const bool first_nan = first != 0x7FFFFFFF && isnan(sv[first]);
-            best = (first != 0x7FFFFFFF && (first_nan || bi == 0x7FFFFFFF)) ? first : bi;
+            for (int j = 0; j < RMAX_PER_LANE; j++)
+                if ((uint32_t)j == (wfirst >> 5)) fsv = sv[j];
+            fsv = __shfl_sync(0xFFFFFFFFu, fsv, wfirst & 31);
+            best = (wfirst != 0xFFFFFFFFu && (isnan(fsv) || !any)) ? (int)wfirst : (int)wbi;
         }
-        if ((best & 31) == lane && best >= 0 && best < 32 * RMAX_PER_LANE) taken |= 1u << (best >> 5);
-        if (lane == k) my_sel = best;
+        // Weight: the unbiased score of the selection, from its owner lane.
+        float o = 0.0f;
+        const bool in_range = best >= 0 && best < n_experts;
+#pragma unroll
+        for (int j = 0; j < RMAX_PER_LANE; j++)
+            if (in_range && j == (best >> 5)) o = ov[j];
+        o = __shfl_sync(0xFFFFFFFFu, o, in_range ? (best & 31) : 0);
+        if (!in_range) o = 0.0f;
+        sum = __dadd_rn(sum, (double)o);     // double sum in k order
+        if (in_range && (best & 31) == lane) taken |= 1u << (best >> 5);
+        if (lane == k) {
+            my_sel = best;
+            my_w = o;
+        }
     }
-    // Weights from the unbiased scores; double sum in k order.
-    const bool in_range = my_sel >= 0 && my_sel < n_experts;
-    const float my_w = (lane < topk && in_range) ? ov[my_sel] : 0.0f;
-    double sum = 0.0;
-#pragma unroll 1
-    for (int k = 0; k < topk; k++) sum = __dadd_rn(sum, (double)__shfl_sync(0xFFFFFFFFu, my_w, k));
     const float inv = (sum != 0.0) ? (float)__drcp_rn(sum) : 0.0f;
     if (lane < topk) {
         idx_out[lane] = my_sel;

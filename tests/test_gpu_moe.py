@@ -234,3 +234,30 @@ def test_swiglu_and_expert_forward_host_abi(host, orc):
         want = orc.swiglu(gate, up, lim)
         assert np.allclose(got, want, rtol=1e-6, atol=1e-30)
     assert got.dtype == np.float32
+
+
+def test_moe_batch40_nan_and_ties(dev, orc):
+    """40 tokens over 32 experts (one warp per token routes, 160 pairs bucket by
+    per-expert counts), then the small-batch path with a NaN score and a row of
+    equal scores (ties go to the lower index; a NaN is never preferred unless it
+    is the first candidate)."""
+    fx = MoeFixture(dev, 32, 512, 256, shared_fmt=2, seed=40)
+    rng = np.random.default_rng(40)
+    x = pack.bf16_round(rng.standard_normal((40, 512)).astype(np.float32))
+    logits = pack.bf16_round(rng.standard_normal((40, 32)).astype(np.float32))
+    out, idx, wts = run(dev, fx, x, logits, 4, 1.5, 10.0)
+    for t in range(40):
+        want, widx, wwts = fx.oracle_out(orc, x[t], logits[t], 4, 1.5, 10.0)
+        assert np.array_equal(idx[t], widx), t
+        assert np.array_equal(wts[t].view(np.uint32), wwts.view(np.uint32)), t
+        assert rel_err(out[t], want) <= 1e-5, (t, rel_err(out[t], want))
+    x2 = x[:2].copy()
+    lg2 = logits[:2].copy()
+    lg2[0, 5] = np.nan
+    lg2[1, :] = np.float32(0.5)
+    out, idx, wts = run(dev, fx, x2, lg2, 4, 1.5, 10.0)
+    for t in range(2):
+        want, widx, wwts = fx.oracle_out(orc, x2[t], lg2[t], 4, 1.5, 10.0)
+        assert np.array_equal(idx[t], widx), (t, idx[t], widx)
+        assert np.array_equal(wts[t].view(np.uint32), wwts.view(np.uint32)), t
+        assert rel_err(out[t], want) <= 1e-5
