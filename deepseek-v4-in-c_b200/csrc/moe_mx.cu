@@ -731,12 +731,12 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     while (kb1 > 1 && (s.hidden / 128) % kb1) kb1 >>= 1;
     r = mxmoe_dispatch<MoeGateUp>(s.NB, kb1, tb1, pg, g1, st);
     if (r) return r;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
     {
         const int items = s.max_tiles * s.tpt * (s.inter / 32);
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_swiglu_kernel, dim3((items * 32 + 255) / 256), dim3(256), 0, st, ws, s.inter,
                                    MX_TERMS, s.tpt, s.NB, limit, items));
     }
-    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
 
     MoeDown::Params pd;
     pd.c = c;
