@@ -665,3 +665,30 @@ extern "C" int dsv4cu_moe_decode(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float
     return dsv4cu_moe_decode_ev(ctx, layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt,
                                 idx_out, wts_out, stream, nullptr);
 }
+
+extern "C" size_t dsv4cu_moe_prefill_workspace(const dsv4cu_moe *L, int topk, int nt, int terms)
+{
+    return (L && L->mx_ok) ? moe_mx_prefill_workspace(L, topk, nt, terms) : 0;
+}
+
+extern "C" int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
+                                  const float *logits, const float *bias, const int64_t *tid2eid,
+                                  const int *token_ids, int topk, float route_scale, float limit, int nt, int terms,
+                                  int *idx_out, float *wts_out, void *stream)
+{
+    if (!ctx || !layer || !out || !x || !logits) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: NULL argument");
+    if ((idx_out == nullptr) != (wts_out == nullptr))
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: idx_out and wts_out go together");
+    if (tid2eid && !token_ids) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: hash routing needs token_ids");
+    if (nt < 1) return nt == 0 ? DSV4CU_OK : dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: nt %d", nt);
+    if (topk < 1 || topk > MOE_MAX_TOPK || topk > layer->n_experts)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: topk %d", topk);
+    if (!layer->mx_ok)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED,
+                                "moe_prefill: the layer's matrices do not qualify for the tensor-core path");
+    void *ws = nullptr;
+    int r = dsv4cu_ws_get(ctx, moe_mx_prefill_workspace(layer, topk, nt, terms), &ws);
+    if (r) return r;
+    return moe_mx_prefill(layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt, terms,
+                          idx_out, wts_out, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream);
+}

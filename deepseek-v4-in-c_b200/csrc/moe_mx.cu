@@ -565,6 +565,8 @@ static int mxmoe_dispatch(int NB, int KB, const CUtensorMap &tb, const typename 
     case 16 * 8 + 1: return mxmoe_launch<16, 1, P>(tb, p, grid, st);
     case 32 * 8 + 2: return mxmoe_launch<32, 2, P>(tb, p, grid, st);
     case 32 * 8 + 1: return mxmoe_launch<32, 1, P>(tb, p, grid, st);
+    case 192 * 8 + 1: return mxmoe_launch<192, 1, P>(tb, p, grid, st);
+    case 256 * 8 + 1: return mxmoe_launch<256, 1, P>(tb, p, grid, st);
     default: return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe: no kernel for %d columns x %d chunks", NB, KB);
     }
 }
@@ -680,40 +682,19 @@ void moe_mx_release(dsv4cu_moe *L)
     }
 }
 
-int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *logits, const float *bias,
-                  const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
-                  int *idx_out, float *wts_out, void *wsp, int *counters, int *status, int sms, cudaStream_t st,
-                  cudaEvent_t *ev)
+// The four launches after the B operand of gate/up is in place: gate/up,
+// SwiGLU split, down, combine.
+static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &ws, int terms, float limit,
+                       float *out, int *status, int sms, cudaStream_t st, cudaEvent_t *ev)
 {
-    if (nt > MXMOE_MAX_NT || topk > MXMOE_MAX_TOPK || L->n_experts > PREP_MAX_EXPERTS)
-        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: nt %d / topk %d / experts %d beyond 64 / 16 / 512",
-                                nt, topk, L->n_experts);
-    const MxMoeShape s = mxmoe_shape(L, topk, nt, L->sms);
-    MxMoeWs ws;
-    mxmoe_layout(s, (char *)wsp, &ws);
-    const int RT = s.inter / 128, RTH = s.hidden / 128;
-    (void)counters;
-    const float *tab = router_table_get();
-    if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_decode: router table setup failed");
-
-    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
-    {
-        // Every SM takes part in the split; each CTA repeats the (cheap) routing.
-        const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 32);
-        const int grid = (int)min((long)sms, max(1L, (tasks + 31) / 32));
-        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_prep_kernel, dim3(grid), dim3(1024), 0, st, tab, x, logits, bias, tid2eid,
-                                   token_ids, s.n_experts, topk, route_scale, nt, s.hidden, s.has_shared, MX_TERMS,
-                                   s.tpt, s.NB, ws, idx_out, wts_out));
-    }
-    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
-
+    const int RT = s.inter / 128, RTH = s.hidden / 128, nt = s.nt, topk = s.topk;
     MxMoeCommon c;
     c.L = L->mx;
     c.ws = ws;
     c.nb = s.NB;
     c.nbb = s.nbb;
     c.tpt = s.tpt;
-    c.terms = MX_TERMS;
+    c.terms = terms;
     c.hidden = s.hidden;
     c.inter = s.inter;
     c.err = status;
@@ -735,7 +716,7 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     {
         const int items = s.max_tiles * s.tpt * (s.inter / 32);
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_swiglu_kernel, dim3((items * 32 + 255) / 256), dim3(256), 0, st, ws, s.inter,
-                                   MX_TERMS, s.tpt, s.NB, limit, items));
+                                   terms, s.tpt, s.NB, limit, items));
     }
 
     MoeDown::Params pd;
@@ -748,6 +729,293 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
                                st, ws, nt, topk, s.hidden, s.has_shared, out));
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
     return DSV4CU_OK;
+}
+
+int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *logits, const float *bias,
+                  const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
+                  int *idx_out, float *wts_out, void *wsp, int *counters, int *status, int sms, cudaStream_t st,
+                  cudaEvent_t *ev)
+{
+    if (nt > MXMOE_MAX_NT || topk > MXMOE_MAX_TOPK || L->n_experts > PREP_MAX_EXPERTS)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode: nt %d / topk %d / experts %d beyond 64 / 16 / 512",
+                                nt, topk, L->n_experts);
+    const MxMoeShape s = mxmoe_shape(L, topk, nt, L->sms);
+    MxMoeWs ws;
+    mxmoe_layout(s, (char *)wsp, &ws);
+    (void)counters;
+    const float *tab = router_table_get();
+    if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_decode: router table setup failed");
+
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
+    {
+        // Every SM takes part in the split; each CTA repeats the (cheap) routing.
+        const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 32);
+        const int grid = (int)min((long)sms, max(1L, (tasks + 31) / 32));
+        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_prep_kernel, dim3(grid), dim3(1024), 0, st, tab, x, logits, bias, tid2eid,
+                                   token_ids, s.n_experts, topk, route_scale, nt, s.hidden, s.has_shared, MX_TERMS,
+                                   s.tpt, s.NB, ws, idx_out, wts_out));
+    }
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
+
+    return mxmoe_gemms(L, s, ws, MX_TERMS, limit, out, status, sms, st, ev);
+}
+
+
+// ============================================================ prefill
+// The MoE layer over many tokens (the reference's prefill union path:
+// union_prepare, src/80_prefill/dsv4_prefill_union.c:30-66, bucketing as in
+// dsv4_prefill_expert_bucket, src/80_prefill/dsv4_prefill_experts.c:23-77,
+// k-order combine, src/80_prefill/dsv4_prefill_union_run.c:109-121, shared
+// expert over every token, src/80_prefill/dsv4_prefill_moe.c:40-59). The GEMM,
+// SwiGLU and combine launches are those of the decode step with wide column
+// tiles; routing and bucketing run as separate grid-wide kernels:
+//   route    one warp per token;
+//   count    per chunk of PF_CHUNK pairs, a per-expert histogram;
+//   offsets  one CTA: per expert the chunk offsets and total, the bucket
+//            offsets (ascending expert order), the column tiles;
+//   scatter  per chunk, pairs ranked in (token, k) order inside their expert,
+//            so a bucket holds its tokens ascending - a stable counting sort.
+constexpr int PF_CHUNK = 1024;
+constexpr int PF_MAX_NT = 16384;
+
+struct PfWs {
+    int *chunk_cnt;      // [nchunks][n_experts]: counts, then exclusive offsets inside each expert
+    int *e_off;          // [n_experts + 1]
+};
+
+__global__ void __launch_bounds__(256) mxpf_route_kernel(const float *__restrict__ tab,
+                                                         const float *__restrict__ logits,
+                                                         const float *__restrict__ bias,
+                                                         const int64_t *__restrict__ tid2eid,
+                                                         const int *__restrict__ token_ids, int n_experts, int topk,
+                                                         float route_scale, int nt, MxMoeWs ws,
+                                                         int *__restrict__ idx_out, float *__restrict__ wts_out)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int t = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5);
+    if (t >= nt) return;
+    route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0, n_experts,
+                     topk, route_scale, ws.idx + (size_t)t * topk, ws.wts + (size_t)t * topk, nullptr, nullptr);
+    __syncwarp();
+    if ((threadIdx.x & 31) < topk && idx_out) {
+        const int k = threadIdx.x & 31;
+        idx_out[(size_t)t * topk + k] = ws.idx[(size_t)t * topk + k];
+        wts_out[(size_t)t * topk + k] = ws.wts[(size_t)t * topk + k];
+    }
+}
+
+__global__ void __launch_bounds__(1024) mxpf_count_kernel(MxMoeWs ws, PfWs pf, int npairs, int n_experts)
+{
+    __shared__ int h[PREP_MAX_EXPERTS];
+    pdl_wait();
+    pdl_trigger();
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) h[e] = 0;
+    __syncthreads();
+    const int p = blockIdx.x * PF_CHUNK + threadIdx.x;
+    if (threadIdx.x < PF_CHUNK && p < npairs) {
+        const int e = ws.idx[p];
+        if (e >= 0 && e < n_experts) atomicAdd(&h[e], 1);
+        else atomicOr(ws.meta + 1, 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) pf.chunk_cnt[(size_t)blockIdx.x * n_experts + e] = h[e];
+}
+
+__global__ void __launch_bounds__(1024) mxpf_offsets_kernel(MxMoeWs ws, PfWs pf, int nchunks, int n_experts, int nt,
+                                                            int has_shared, int tpt, int max_tiles)
+{
+    __shared__ int tot[PREP_MAX_EXPERTS + 2], bid[PREP_MAX_EXPERTS + 2], ntl[PREP_MAX_EXPERTS + 2];
+    __shared__ int s_nb, s_routed;
+    pdl_wait();
+    pdl_trigger();
+    // Per expert: exclusive offsets over the chunks, and the total.
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) {
+        int run = 0;
+        for (int c = 0; c < nchunks; c++) {
+            int *q = pf.chunk_cnt + (size_t)c * n_experts + e;
+            const int v = *q;
+            *q = run;
+            run += v;
+        }
+        tot[e] = run;
+        bid[e] = run > 0;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        int *off = ntl;      // scratch: expert offsets
+        for (int e = threadIdx.x; e < n_experts; e += 32) off[e] = tot[e];
+        __syncwarp();
+        const int routed = warp_scan_excl(off, n_experts);
+        const int nb = warp_scan_excl(bid, n_experts);
+        __syncwarp();
+        for (int e = threadIdx.x; e < n_experts; e += 32) {
+            pf.e_off[e] = off[e];
+            if (tot[e]) {
+                ws.b_expert[bid[e]] = e;
+                ws.b_off[bid[e]] = off[e];
+            }
+        }
+        if (threadIdx.x == 0) {
+            pf.e_off[n_experts] = routed;
+            ws.b_off[nb] = routed;
+            ws.b_off[nb + 1] = routed + (has_shared ? nt : 0);
+            ws.meta[0] = nb;
+            s_nb = nb;
+            s_routed = routed;
+        }
+    }
+    __syncthreads();
+    const int nb = s_nb, nbk = nb + (has_shared ? 1 : 0);
+    // Column tiles: per bucket ceil(count / tpt), then offsets.
+    for (int b = threadIdx.x; b < nbk; b += blockDim.x) {
+        const int c = b < nb ? tot[ws.b_expert[b]] : nt;
+        ntl[b] = (c + tpt - 1) / tpt;
+    }
+    __syncthreads();
+    __shared__ int s_ntiles;
+    if (threadIdx.x < 32) {
+        const int n = warp_scan_excl(ntl, nbk);
+        if (threadIdx.x == 0) s_ntiles = min(n, max_tiles);
+    }
+    __syncthreads();
+    for (int b = threadIdx.x; b < nbk; b += blockDim.x) {
+        const int e = b < nb ? ws.b_expert[b] : n_experts;
+        const int s0 = b < nb ? ws.b_off[b] : s_routed, c = b < nb ? tot[e] : nt;
+        for (int j = 0, n = ntl[b]; j < c && n < max_tiles; j += tpt, n++) {
+            ws.c_slot0[n] = s0 + j;
+            ws.c_cnt[n] = min(tpt, c - j);
+            ws.c_expert[n] = b < nb ? e : n_experts;
+        }
+    }
+    if (threadIdx.x == 0) ws.meta[2] = s_ntiles;
+}
+
+__global__ void __launch_bounds__(1024) mxpf_scatter_kernel(MxMoeWs ws, PfWs pf, int npairs, int n_experts, int topk,
+                                                            int nt, int has_shared)
+{
+    __shared__ int run[PREP_MAX_EXPERTS];
+    pdl_wait();
+    pdl_trigger();
+    const int c = blockIdx.x, lane = threadIdx.x & 31;
+    if (threadIdx.x < 32) {
+        for (int e = lane; e < n_experts; e += 32)
+            run[e] = pf.e_off[e] + pf.chunk_cnt[(size_t)c * n_experts + e];
+        __syncwarp();
+        for (int c0 = 0; c0 < PF_CHUNK; c0 += 32) {
+            const int p = c * PF_CHUNK + c0 + lane;
+            const int e = p < npairs ? ws.idx[p] : -1;
+            const bool ok = e >= 0 && e < n_experts;
+            const unsigned same = __match_any_sync(0xFFFFFFFFu, ok ? e : -1);
+            const int before = __popc(same & ((1u << lane) - 1u));
+            const int base = ok ? run[e] : 0;
+            __syncwarp();
+            if (ok) {
+                const int slot = base + before;
+                ws.pos[p] = slot;
+                ws.b_tok[slot] = p / topk;
+                if (before == __popc(same) - 1) run[e] = base + before + 1;
+            } else if (p < npairs) {
+                ws.pos[p] = -1;
+            }
+            __syncwarp();
+        }
+    }
+    if (has_shared && c == 0)
+        for (int t = threadIdx.x; t < nt; t += blockDim.x) ws.b_tok[pf.e_off[n_experts] + t] = t;
+}
+
+// Gate/up B operand of the prefill: one warp per (column tile, slot, 32-wide
+// K block), all terms of that slot.
+__global__ void __launch_bounds__(256) mxpf_split_kernel(const float *__restrict__ x, int hidden, MxMoeWs ws,
+                                                         int terms, int tpt, int NB, long max_tasks)
+{
+    pdl_wait();
+    pdl_trigger();
+    const long task = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31, nblk = hidden >> 5;
+    if (task >= max_tasks) return;
+    const int it = (int)(task / nblk), blk = (int)(task - (long)it * nblk);
+    const int i = it / tpt, tl = it - i * tpt;
+    if (i >= ws.meta[2] || tl >= ws.c_cnt[i]) return;
+    const int tok = ws.b_tok[ws.c_slot0[i] + tl];
+    uint8_t q[4], sb[4];
+    mx_split_all(x[(size_t)tok * hidden + blk * 32 + lane], terms, q, sb);
+    const int nbb = (NB + 127) / 128;
+    for (int j = 0; j < terms; j++) {
+        const int n = j * tpt + tl;
+        ws.xq1[((size_t)i * NB + n) * hidden + blk * 32 + lane] = q[j];
+        if (lane == 0) ws.sfb1[((size_t)i * (hidden >> 7) + (blk >> 2)) * nbb * 512 + mx_sfb_offset(n, blk & 3)] = sb[j];
+    }
+}
+
+static MxMoeShape mxpf_shape(const dsv4cu_moe *L, int topk, int nt, int terms)
+{
+    MxMoeShape s;
+    s.nt = nt;
+    s.topk = topk;
+    s.n_experts = L->n_experts;
+    s.hidden = L->hidden;
+    s.inter = L->inter;
+    s.has_shared = L->has_shared;
+    s.NB = terms == 3 ? 192 : 256;
+    s.KB = 1;
+    s.tpt = (s.NB / terms) / 8 * 8;
+    s.nbb = (s.NB + 127) / 128;
+    s.npairs = nt * topk + (s.has_shared ? nt : 0);
+    s.nbmax = min(nt * topk, s.n_experts);
+    s.max_tiles = (nt * topk) / s.tpt + s.nbmax + (s.has_shared ? nt / s.tpt + 1 : 0) + 1;
+    return s;
+}
+
+static size_t mxpf_layout(const MxMoeShape &s, char *base, MxMoeWs *w, PfWs *pf)
+{
+    size_t off = mxmoe_layout(s, base, w);
+    const int nchunks = (s.nt * s.topk + PF_CHUNK - 1) / PF_CHUNK;
+    auto take = [&](size_t bytes) {
+        char *p = base ? base + off : nullptr;
+        off += dsv4cu_align256(bytes);
+        return p;
+    };
+    PfWs t;
+    t.chunk_cnt = (int *)take((size_t)nchunks * s.n_experts * 4);
+    t.e_off = (int *)take(((size_t)s.n_experts + 1) * 4);
+    if (pf) *pf = t;
+    return off;
+}
+
+size_t moe_mx_prefill_workspace(const dsv4cu_moe *L, int topk, int nt, int terms)
+{
+    return mxpf_layout(mxpf_shape(L, topk, nt, terms), nullptr, nullptr, nullptr);
+}
+
+int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float *logits, const float *bias,
+                   const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
+                   int terms, int *idx_out, float *wts_out, void *wsp, int *status, int sms, cudaStream_t st)
+{
+    if (nt > PF_MAX_NT || topk > MXMOE_MAX_TOPK || L->n_experts > PREP_MAX_EXPERTS)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_prefill: nt %d / topk %d / experts %d beyond %d / 16 / 512",
+                                nt, topk, L->n_experts, PF_MAX_NT);
+    if (terms != 3 && terms != 4) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: terms must be 3 or 4");
+    const MxMoeShape s = mxpf_shape(L, topk, nt, terms);
+    MxMoeWs ws;
+    PfWs pf;
+    mxpf_layout(s, (char *)wsp, &ws, &pf);
+    const float *tab = router_table_get();
+    if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_prefill: router table setup failed");
+    const int npairs = nt * topk, nchunks = (npairs + PF_CHUNK - 1) / PF_CHUNK;
+    DSV4CU_CUDA_TRY(cudaMemsetAsync(ws.meta, 0, 64, st));
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_route_kernel, dim3((nt * 32 + 255) / 256), dim3(256), 0, st, tab, logits, bias,
+                               tid2eid, token_ids, s.n_experts, topk, route_scale, nt, ws, idx_out, wts_out));
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_count_kernel, dim3(nchunks), dim3(1024), 0, st, ws, pf, npairs, s.n_experts));
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_offsets_kernel, dim3(1), dim3(1024), 0, st, ws, pf, nchunks, s.n_experts, nt,
+                               s.has_shared, s.tpt, s.max_tiles));
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_scatter_kernel, dim3(nchunks), dim3(1024), 0, st, ws, pf, npairs, s.n_experts, topk,
+                               nt, s.has_shared));
+    const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 32);
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_split_kernel, dim3((unsigned)((tasks * 32 + 255) / 256)), dim3(256), 0, st, x,
+                               s.hidden, ws, terms, s.tpt, s.NB, tasks));
+    return mxmoe_gemms(L, s, ws, terms, limit, out, status, sms, st, nullptr);
 }
 
 }  // namespace dsv4cu

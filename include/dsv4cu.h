@@ -183,6 +183,21 @@ int dsv4cu_indexer_score_fp8(float *out, const uint8_t *q8, const float *q_scale
                              const float *weights, int n_heads, int head_dim,
                              int n_pos, int k_stride, void *stream);
 
+/* The MoE layer over nt tokens at once (prefill, up to 16384 tokens): the
+ * reference's prefill union path (src/80_prefill/dsv4_prefill_union.c:30-66,
+ * dsv4_prefill_experts.c:23-77, dsv4_prefill_union_run.c:109-121, shared
+ * expert dsv4_prefill_moe.c:40-59) with the same arguments as
+ * dsv4cu_moe_decode. Tokens are bucketed by expert (tokens ascending inside a
+ * bucket) and every bucket runs as tcgen05 block-scaled GEMMs; the fp32
+ * activations enter the tensor core as `terms` (3 or 4) exact e4m3 terms
+ * (3: max-rel error ~1e-5, 4: ~1e-6). Needs a layer whose matrices all
+ * qualify for the tensor-core path (FP4/FP8, dims multiples of 128). */
+size_t dsv4cu_moe_prefill_workspace(const dsv4cu_moe *layer, int topk, int nt, int terms);
+int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
+                       const float *logits, const float *bias, const int64_t *tid2eid,
+                       const int *token_ids, int topk, float route_scale, float limit,
+                       int nt, int terms, int *idx_out, float *wts_out, void *stream);
+
 /* Top-k indices of scores[n], descending, ties to the lower index, k clamped
  * to n; replaces dsv4_topk (src/10_compute/dsv4_topk.c:76-112) without its
  * k <= 1024 bound. Writes min(k, n) indices. */

@@ -261,3 +261,84 @@ def test_moe_batch40_nan_and_ties(dev, orc):
         assert np.array_equal(idx[t], widx), (t, idx[t], widx)
         assert np.array_equal(wts[t].view(np.uint32), wwts.view(np.uint32)), t
         assert rel_err(out[t], want) <= 1e-5
+
+
+def _oracle_batch(fx, orc, x, logits, topk, scale, limit):
+    """Oracle MoE output of every token; all experts copied to the host once."""
+    cache = [fx.host_expert(d) for d in fx.experts_host]
+    experts = [c[0] for c in cache]
+    shared, keep = fx.host_expert(fx.shared)
+    outs, idxs, wtss = [], [], []
+    for t in range(x.shape[0]):
+        o, i, w = orc.moe_decode(x[t], logits[t], experts, shared, topk, scale, fx.H, fx.I, limit, None, None, 0)
+        outs.append(o)
+        idxs.append(i)
+        wtss.append(w)
+    del cache, keep
+    return np.stack(outs), np.stack(idxs), np.stack(wtss)
+
+
+def _prefill(dev, fx, x, logits, topk, scale, limit, terms):
+    t = fx.torch
+    nt = x.shape[0]
+    out = t.empty((nt, fx.H), dtype=t.float32, device="cuda")
+    idx = t.empty((nt, topk), dtype=t.int32, device="cuda")
+    wts = t.empty((nt, topk), dtype=t.float32, device="cuda")
+    dev.moe_prefill(fx.layer, out, t.from_numpy(x).cuda(), t.from_numpy(logits).cuda(), topk, scale, limit, nt,
+                    terms, idx, wts)
+    t.cuda.synchronize()
+    return out.cpu().numpy(), idx.cpu().numpy(), wts.cpu().numpy()
+
+
+@pytest.mark.parametrize("terms,bound", [(3, 1e-4), (4, 1e-5)])
+def test_moe_prefill_small_vs_oracle(dev, orc, terms, bound):
+    """300 tokens over 16 experts (top-4): buckets of about 75 tokens, several
+    192/256-column tiles per expert plus the shared expert over all tokens."""
+    fx = MoeFixture(dev, 16, 512, 256, shared_fmt=2, seed=300 + terms)
+    rng = np.random.default_rng(300 + terms)
+    x = pack.bf16_round(rng.standard_normal((300, 512)).astype(np.float32))
+    logits = pack.bf16_round(rng.standard_normal((300, 16)).astype(np.float32))
+    out, idx, wts = _prefill(dev, fx, x, logits, 4, 1.5, 10.0, terms)
+    want, widx, wwts = _oracle_batch(fx, orc, x, logits, 4, 1.5, 10.0)
+    assert np.array_equal(idx, widx)
+    assert np.array_equal(wts.view(np.uint32), wwts.view(np.uint32))
+    errs = [rel_err(out[t], want[t]) for t in range(300)]
+    print(f"prefill terms={terms}: max-rel over tokens {max(errs):.3e}")
+    assert max(errs) <= bound, max(errs)
+    fx.close()
+
+
+def test_moe_prefill_matches_decode(dev):
+    """The prefill path and the decode step agree on the same tokens."""
+    t = __import__("torch")
+    fx = MoeFixture(dev, 16, 512, 256, shared_fmt=2, seed=77)
+    rng = np.random.default_rng(77)
+    x = pack.bf16_round(rng.standard_normal((48, 512)).astype(np.float32))
+    logits = pack.bf16_round(rng.standard_normal((48, 16)).astype(np.float32))
+    outp, idxp, wtsp = _prefill(dev, fx, x, logits, 4, 1.5, 10.0, 4)
+    outd, idxd, wtsd = run(dev, fx, x, logits, 4, 1.5, 10.0)
+    assert np.array_equal(idxp, idxd)
+    assert np.array_equal(wtsp.view(np.uint32), wtsd.view(np.uint32))
+    assert max(rel_err(outp[i], outd[i].astype(np.float64)) for i in range(48)) <= 1e-5
+    fx.close()
+
+
+def test_moe_prefill_config3_sampled(dev, orc):
+    """BASELINE config 3 shape: 4096 tokens, 256 FP4 experts (top-8), FP8 shared
+    expert; every routing result checked, outputs of 12 sampled tokens against
+    the oracle (the oracle is scalar double: the full batch would take minutes)."""
+    fx = MoeFixture(dev, 256, 4096, 2048, shared_fmt=2, seed=4096)
+    rng = np.random.default_rng(4096)
+    nt = 4096
+    x = pack.bf16_round(rng.standard_normal((nt, 4096)).astype(np.float32))
+    logits = pack.bf16_round(rng.random((nt, 256)).astype(np.float32))   # uniform(0,1), bf16-valued
+    out, idx, wts = _prefill(dev, fx, x, logits, 8, 1.5, 10.0, 3)
+    for t_ in range(nt):
+        i_, w_, _, _ = orc.route(logits[t_], 8, 1.5, None, None, 0)
+        assert np.array_equal(idx[t_], i_), t_
+        assert np.array_equal(wts[t_].view(np.uint32), w_.view(np.uint32)), t_
+    sample = rng.choice(nt, 12, replace=False)
+    for t_ in sample:
+        want, _, _ = fx.oracle_out(orc, x[t_], logits[t_], 8, 1.5, 10.0)
+        assert rel_err(out[t_], want) <= 1e-4, (t_, rel_err(out[t_], want))
+    fx.close()
