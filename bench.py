@@ -59,6 +59,9 @@ def parse():
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts resident in HBM (256 = config 2; smaller only for ncu captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode = config 2 (the headline); prefill = config 3 (MoE layer over 4096 tokens + "
+                         "FP8 QKV projection)")
     return ap.parse_args()
 
 
@@ -425,10 +428,249 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# --------------------------------------------------- config 3: prefill
+PF_TOKENS, QKV_OUT = 4096, 6144
+PF_METRIC = "prefill tok/s per GPU (FP4 MoE layer over 4096 tokens + FP8 QKV 4096->6144)"
+PF_WORKLOAD = ("config3: 4096 tokens, hidden 4096, MoE top-8 of 256 FP4 experts (w1/w3 2048x4096, w2 4096x2048, "
+               "1x32 E8M0) + FP8 shared expert, uniform(0,1) bf16-valued router logits; FP8 QKV 6144x4096 "
+               "(128x128 E8M0)")
+PF_TERMS = 3
+
+
+def pf_flops():
+    """Useful FLOPs of one step: routed + shared expert GEMMs and the QKV projection."""
+    rows = PF_TOKENS * TOPK + PF_TOKENS
+    moe = rows * 2.0 * (2 * INTER * HIDDEN + HIDDEN * INTER)
+    gate_up = rows * 2.0 * 2 * INTER * HIDDEN
+    qkv = 2.0 * PF_TOKENS * HIDDEN * QKV_OUT
+    return moe + qkv, gate_up
+
+
+def load_bf16_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def pf_inputs(seed):
+    sys.path.insert(0, PKG)
+    import pack
+    rng = np.random.default_rng(seed)
+    x = pack.bf16_round(rng.standard_normal((PF_TOKENS, HIDDEN)).astype(np.float32))
+    lg = pack.bf16_round(rng.random((PF_TOKENS, N_EXPERTS)).astype(np.float32))
+    return x, lg
+
+
+def run_prefill(args, rank, local_rank, world):
+    import torch
+    import dsv4cu
+    torch.cuda.set_device(local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        pg = tdist
+    dev = dsv4cu.Device(local_rank)
+    layer, keep = build_layer(dev, torch, N_EXPERTS)
+    src = torch.empty(QKV_OUT * HIDDEN, dtype=torch.float32, device="cuda")
+    dev.fill_normal(src, 9001, 0.0, 0.02)
+    Wq = torch.empty(QKV_OUT * HIDDEN, dtype=torch.uint8, device="cuda")
+    Sq = torch.empty((QKV_OUT // 128) * (HIDDEN // 128), dtype=torch.uint8, device="cuda")
+    dev.quantize_fp8(Wq, Sq, src, QKV_OUT, HIDDEN)
+    del src
+    qkv = dev.mat_create(dsv4cu.QMat(Wq.data_ptr(), Sq.data_ptr(), 2, QKV_OUT, HIDDEN, 128, 128))
+    x, lg = pf_inputs(3000 + rank)
+    dx, dl = torch.from_numpy(x).cuda(), torch.from_numpy(lg).cuda()
+    out = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32, device="cuda")
+    yq = torch.empty((PF_TOKENS, QKV_OUT), dtype=torch.float32, device="cuda")
+
+    def step(ev=None):
+        dev.moe_prefill(layer, out, dx, dl, TOPK, ROUTE_SCALE, LIMIT, PF_TOKENS, PF_TERMS, events=ev)
+        dev.mat_gemm(qkv, yq, dx, PF_TOKENS, PF_TERMS)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = Clocks(local_rank)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for k in range(args.steps):
+        starts[k].record()
+        step()
+        ends[k].record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    total_ms = t.item()
+    # the dominant kernel (gate/up GEMM) live on its stream
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for e in evs:
+        for ev in e:
+            ev.record()
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        step(evs[k])
+    torch.cuda.synchronize()
+    gu_ms = float(np.mean([e[1].elapsed_time(e[2]) for e in evs]))
+    moe_ms = float(np.mean([e[0].elapsed_time(e[3]) for e in evs]))
+    # e2e through the public API from pinned host buffers
+    hx, hl = torch.from_numpy(x).pin_memory(), torch.from_numpy(lg).pin_memory()
+    hout = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32).pin_memory()
+    hyq = torch.empty((PF_TOKENS, QKV_OUT), dtype=torch.float32).pin_memory()
+    gx, gl = torch.empty_like(dx), torch.empty_like(dl)
+    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        e_s[k].record()
+        gx.copy_(hx, non_blocking=True)
+        gl.copy_(hl, non_blocking=True)
+        dev.moe_prefill(layer, out, gx, gl, TOPK, ROUTE_SCALE, LIMIT, PF_TOKENS, PF_TERMS)
+        dev.mat_gemm(qkv, yq, gx, PF_TOKENS, PF_TERMS)
+        hout.copy_(out, non_blocking=True)
+        hyq.copy_(yq, non_blocking=True)
+        e_e[k].record()
+    torch.cuda.synchronize()
+    e2e_ms = sum(s_.elapsed_time(e_) for s_, e_ in zip(e_s, e_e))
+    dev.check_status()
+    useful, gate_up = pf_flops()
+    bf16, kind = load_bf16_peak()
+    peak = 2.0 * bf16
+    issued = gate_up * PF_TERMS / (gu_ms * 1e-3) / 1e12
+    ms = total_ms / args.steps
+    res = {
+        "metric": PF_METRIC, "value": round(world * PF_TOKENS / (ms * 1e-3), 1), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"e2m1/e4m3 weights x e4m3 activation terms ({PF_TERMS}, exact split) -> f32 "
+                 "(tcgen05 kind::mxf8f6f4)",
+        "data": "synthetic: weights N(0,0.02) quantized on device, x N(0,1) and logits uniform(0,1) bf16-valued, "
+                "seeded",
+        "config": {"workload": PF_WORKLOAD, "global_batch": PF_TOKENS * world, "seq_len": PF_TOKENS,
+                   "parallelism": f"replicas x{world}",
+                   "l2": "inputs larger than L2 (3.4 GB of experts + 0.1 GB QKV weights per step)",
+                   "useful_tflop_per_step": round(useful / 1e12, 4),
+                   "moe_ms": round(moe_ms, 4), "useful_tflops": round(useful / (ms * 1e-3) / 1e12, 1)},
+        "roofline": {"bound": "tensor", "kernel": "mx_kernel<192,1,MoeGateUp> (tcgen05 gate/up GEMM of 36864 rows)",
+                     "achieved": round(issued, 1), "peak": round(peak, 1),
+                     "peak_source": f"2 x {kind} bf16 dense (FP8-rate MMA; no measured FP8 figure)",
+                     "unit": "TFLOP/s", "frac": round(issued / peak, 4), "traffic": None,
+                     "achieved_is": f"issued MMA work ({PF_TERMS} activation terms); useful = achieved / {PF_TERMS}",
+                     "kernel_ms": round(gu_ms, 4)},
+        "e2e": {"value": round(world * PF_TOKENS / (e2e_ms / args.steps * 1e-3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": int(x.nbytes + lg.nbytes), "d2h_bytes_per_step": int(hout.numel() * 4 + hyq.numel() * 4),
+                "api": "dsv4cu_moe_prefill + dsv4cu_mat_gemm (include/dsv4cu.h)"},
+        "gpu_launches": 14 * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_prefill_baseline(args.cpu_seconds)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    dev.mat_destroy(qkv)
+    dev.moe_destroy(layer)
+    dev.close()
+    del keep
+    return res if rank == 0 else None
+
+
+def cpu_prefill_sample(ref, experts, qkv_host, x, tokens=128):
+    """One expert bucket of `tokens` tokens (w1, w3, SwiGLU, w2 through the
+    reference's dsv4_mmq_n and dsv4_swiglu) and the QKV rows of the same
+    tokens; returns (expert seconds, qkv seconds)."""
+    xb = np.ascontiguousarray(x[:tokens])
+    t0 = time.perf_counter()
+    g = ref.mmq(xb, experts[0][0])
+    u = ref.mmq(xb, experts[0][1])
+    mid = np.empty_like(g)
+    for i in range(tokens):
+        mid[i] = ref.swiglu(g[i], u[i], LIMIT)
+    ref.mmq(np.ascontiguousarray(mid), experts[0][2])
+    t1 = time.perf_counter()
+    ref.mmq(xb, qkv_host)
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1
+
+
+def cpu_prefill_setup():
+    sys.path.insert(0, ORACLE)
+    os.environ.setdefault("OMP_NUM_THREADS", str(cpu_threads()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import oracle
+    import pack
+    if not oracle.RefLib.available():
+        return None
+    ref = oracle.RefLib()
+    experts, shared, keep = reference_layer(pool=1)
+    rng = np.random.default_rng(9)
+    Wq, Sq = pack.quantize_fp8((rng.standard_normal((QKV_OUT, HIDDEN), dtype=np.float32) * np.float32(0.02)))
+    keep += [Wq, Sq]
+    qkv = oracle.qmat(Wq, Sq, 2, QKV_OUT, HIDDEN, 128, 128)
+    x, _ = pf_inputs(11)
+    return ref, experts, qkv, x, keep
+
+
+def cpu_prefill_rate(ref, experts, qkv, x):
+    te, tq = cpu_prefill_sample(ref, experts, qkv, x)
+    # every token runs 8 routed + 1 shared expert passes and its QKV row
+    return 128.0 / ((TOPK + 1) * te + tq), te, tq
+
+
+def cpu_prefill_baseline(seconds):
+    st = cpu_prefill_setup()
+    if st is None:
+        return {"value": None, "unit": "tok/s", "cores": 0, "kind": "port",
+                "sample": "oracle/_ref not built on this host"}
+    ref, experts, qkv, x, keep = st
+    rate, te, tq = cpu_prefill_rate(ref, experts, qkv, x)
+    return {"value": round(rate, 3), "unit": "tok/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "kind": "reference",
+            "sample": f"one expert bucket of 128 tokens (dsv4_mmq_n w1, w3, dsv4_swiglu, w2: {te:.2f} s) and the "
+                      f"FP8 QKV rows of those tokens ({tq:.2f} s), scaled to 9 expert passes per token"}
+
+
+def run_prefill_reference(args, rank, world):
+    if rank != 0:
+        return None
+    st = cpu_prefill_setup()
+    if st is None:
+        return {"impl": "reference", "unavailable": "oracle/_ref/libdsv4ref.so was not built"}
+    ref, experts, qkv, x, keep = st
+    for _ in range(min(args.warmup, 1)):
+        cpu_prefill_rate(ref, experts, qkv, x)
+    rates = [cpu_prefill_rate(ref, experts, qkv, x)[0] for _ in range(max(1, min(args.steps, 3)))]
+    v = float(np.median(rates))
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    sample = (f"{len(rates)} samples: one 128-token expert bucket (dsv4_mmq_n w1/w3/w2 + dsv4_swiglu) and its FP8 "
+              f"QKV rows, scaled to 9 expert passes per token, {cores} threads")
+    return {"impl": "reference", "metric": PF_METRIC, "value": round(v, 3), "unit": "tok/s", "n_gpus": world,
+            "steps": len(rates), "warmup": args.warmup, "ms_per_step": round(PF_TOKENS / v * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e2m1/e4m3 weights x f32 (AVX2 FMA)", "data": "synthetic, seeded",
+            "config": {"workload": PF_WORKLOAD, "global_batch": PF_TOKENS, "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": cores, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def main():
     args = parse()
     rank, local_rank, world = dist_env()
-    if args.impl == "reference":
+    if args.workload == "prefill":
+        res = (run_prefill_reference(args, rank, world) if args.impl == "reference"
+               else run_prefill(args, rank, local_rank, world))
+    elif args.impl == "reference":
         res = run_reference(args, rank, world)
     else:
         res = run_ours(args, rank, local_rank, world)

@@ -55,6 +55,7 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
 size_t moe_mx_prefill_workspace(const dsv4cu_moe *L, int topk, int nt, int terms);
 int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float *logits, const float *bias,
                    const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
-                   int terms, int *idx_out, float *wts_out, void *ws, int *status, int sms, cudaStream_t st);
+                   int terms, int *idx_out, float *wts_out, void *ws, int *status, int sms, cudaStream_t st,
+                   cudaEvent_t *ev);
 
 }  // namespace dsv4cu

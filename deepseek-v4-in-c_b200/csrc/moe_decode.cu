@@ -671,10 +671,10 @@ extern "C" size_t dsv4cu_moe_prefill_workspace(const dsv4cu_moe *L, int topk, in
     return (L && L->mx_ok) ? moe_mx_prefill_workspace(L, topk, nt, terms) : 0;
 }
 
-extern "C" int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
-                                  const float *logits, const float *bias, const int64_t *tid2eid,
-                                  const int *token_ids, int topk, float route_scale, float limit, int nt, int terms,
-                                  int *idx_out, float *wts_out, void *stream)
+extern "C" int dsv4cu_moe_prefill_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
+                                     const float *logits, const float *bias, const int64_t *tid2eid,
+                                     const int *token_ids, int topk, float route_scale, float limit, int nt,
+                                     int terms, int *idx_out, float *wts_out, void *stream, void **events)
 {
     if (!ctx || !layer || !out || !x || !logits) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: NULL argument");
     if ((idx_out == nullptr) != (wts_out == nullptr))
@@ -690,5 +690,15 @@ extern "C" int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, floa
     int r = dsv4cu_ws_get(ctx, moe_mx_prefill_workspace(layer, topk, nt, terms), &ws);
     if (r) return r;
     return moe_mx_prefill(layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt, terms,
-                          idx_out, wts_out, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream);
+                          idx_out, wts_out, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream,
+                          (cudaEvent_t *)events);
+}
+
+extern "C" int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
+                                  const float *logits, const float *bias, const int64_t *tid2eid,
+                                  const int *token_ids, int topk, float route_scale, float limit, int nt, int terms,
+                                  int *idx_out, float *wts_out, void *stream)
+{
+    return dsv4cu_moe_prefill_ev(ctx, layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt,
+                                 terms, idx_out, wts_out, stream, nullptr);
 }

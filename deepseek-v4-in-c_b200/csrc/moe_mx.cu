@@ -143,6 +143,31 @@ constexpr int PREP_MAX_SLOTS = PREP_MAX_PAIRS + MXMOE_MAX_NT;
 constexpr int PREP_MAX_EXPERTS = 32 * RMAX_PER_LANE;                      // 512
 constexpr int PREP_MAX_TILES = PREP_MAX_PAIRS / 2 + PREP_MAX_EXPERTS + MXMOE_MAX_NT + 2;
 
+// One 128-wide chunk c of a source row of length K, split into `terms`
+// e4m3 terms, written as columns j * tpt + tl of column tile i of a B operand
+// (rows [tile][NB][K], scale blocks [tile][K / 128][NBB][512]). Whole warp.
+DSV4CU_DEV void mxmoe_split_row_chunk(const float *__restrict__ src, int K, int c, int i, int tl, int terms, int tpt,
+                                      int NB, int nbb, uint8_t *__restrict__ xq, uint8_t *__restrict__ sfb)
+{
+    const int lane = threadIdx.x & 31;
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) v[k] = src[c * 128 + 4 * lane + k];
+    uint32_t q[4];
+    uint8_t sb[4];
+    mx_split128(v, terms, q, sb);
+    uint8_t *row[4], *sf[4];
+    int step[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int n = j * tpt + tl;
+        row[j] = xq + ((size_t)i * NB + n) * K + c * 128;
+        sf[j] = sfb + ((size_t)i * (K >> 7) + c) * nbb * 512 + mx_sfb_offset(n, 0);
+        step[j] = 1;
+    }
+    mx_store128(q, sb, terms, row, sf, step);
+}
+
 // Every CTA routes all nt tokens (one warp per token), buckets the (token, k)
 // pairs by expert in ascending expert order with tokens ascending inside a
 // bucket (the layout of union_prepare, src/80_prefill/dsv4_prefill_union.c:
@@ -377,24 +402,17 @@ __global__ void __launch_bounds__(1024) mxmoe_prep_kernel(
         }
     }
 
-    // Gate/up B operand: one warp per (column tile, slot, 32-wide K block)
-    // writes all terms of that slot. Columns past the tile's slots are left as
+    // Gate/up B operand: one warp per (column tile, slot, 128-wide K chunk)
+    // writes all terms of that chunk. Columns past the tile's slots are left as
     // they are: they only feed accumulator columns that are never read.
-    const int nblk = hidden >> 5, nbb = (NB + 127) / 128;
-    const long tasks = (long)ntiles * tpt * nblk;
+    const int kc = hidden >> 7, nbb = (NB + 127) / 128;
+    const long tasks = (long)ntiles * tpt * kc;
     for (long task = (long)blockIdx.x * nwarps + warp; task < tasks; task += (long)gridDim.x * nwarps) {
-        const int it = (int)(task / nblk), blk = (int)(task - (long)it * nblk);
+        const int it = (int)(task / kc), c = (int)(task - (long)it * kc);
         const int i = it / tpt, tl = it - i * tpt;
         if (tl >= s_tcnt[i]) continue;
         const int tok = s_btok[s_tslot[i] + tl];
-        uint8_t q[4], sb[4];
-        mx_split_all(x[(size_t)tok * hidden + blk * 32 + lane], terms, q, sb);
-        for (int j = 0; j < terms; j++) {
-            const int n = j * tpt + tl;
-            ws.xq1[((size_t)i * NB + n) * hidden + blk * 32 + lane] = q[j];
-            if (lane == 0)
-                ws.sfb1[((size_t)i * (hidden >> 7) + (blk >> 2)) * nbb * 512 + mx_sfb_offset(n, blk & 3)] = sb[j];
-        }
+        mxmoe_split_row_chunk(x + (size_t)tok * hidden, hidden, c, i, tl, terms, tpt, NB, nbb, ws.xq1, ws.sfb1);
     }
 }
 
@@ -486,33 +504,44 @@ struct MoeDown {
 };
 
 // SwiGLU (dsv4_ops.c:61-79: up clamped both ways, gate from above only) of
-// every slot, written as e4m3 terms (mx_split_all) into the down projection's
-// B operand: one warp per (column tile, slot, 32-row block of inter).
+// every slot, split into e4m3 terms (mx_split128) for the down projection's B
+// operand: one warp per (column tile, slot, 128-wide chunk of inter).
 __global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter, int terms, int tpt, int NB,
                                                            float limit, int max_items)
 {
     pdl_wait();
     pdl_trigger();
     const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-    const int nblk = inter >> 5, ntiles = ws.meta[2];
+    const int kc = inter >> 7, ntiles = ws.meta[2];
     if (gw >= max_items) return;
-    const int it = gw / nblk, blk = gw - it * nblk, i = it / tpt, tl = it - i * tpt;
+    const int it = gw / kc, c = gw - it * kc, i = it / tpt, tl = it - i * tpt;
     if (i >= ntiles || tl >= ws.c_cnt[i]) return;
-    const int slot = ws.c_slot0[i] + tl, ii = blk * 32 + lane;
-    float g = ws.gu[(size_t)slot * 2 * inter + ii], u = ws.gu[((size_t)slot * 2 + 1) * inter + ii];
-    if (limit > 0.0f) {
-        u = fminf(fmaxf(u, -limit), limit);
-        g = fminf(g, limit);
+    const int slot = ws.c_slot0[i] + tl;
+    const float *g = ws.gu + (size_t)slot * 2 * inter + c * 128 + 4 * lane, *u = g + inter;
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        float gg = g[k], uu = u[k];
+        if (limit > 0.0f) {
+            uu = fminf(fmaxf(uu, -limit), limit);
+            gg = fminf(gg, limit);
+        }
+        v[k] = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.0f, expf(-gg))), uu);
     }
-    const float mid = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-    uint8_t q[4], sb[4];
-    mx_split_all(mid, terms, q, sb);
+    uint32_t q[4];
+    uint8_t sb[4];
+    mx_split128(v, terms, q, sb);
     const int nbb = (NB + 127) / 128;
-    for (int j = 0; j < terms; j++) {
+    uint8_t *row[4], *sf[4];
+    int step[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
         const int n = j * tpt + tl;
-        ws.xq2[((size_t)i * NB + n) * inter + ii] = q[j];
-        if (lane == 0) ws.sfb2[((size_t)i * (inter >> 7) + (blk >> 2)) * nbb * 512 + mx_sfb_offset(n, blk & 3)] = sb[j];
+        row[j] = ws.xq2 + ((size_t)i * NB + n) * inter + c * 128;
+        sf[j] = ws.sfb2 + ((size_t)i * kc + c) * nbb * 512 + mx_sfb_offset(n, 0);
+        step[j] = 1;
     }
+    mx_store128(q, sb, terms, row, sf, step);
 }
 
 // Output rows: per token the routed pairs IN k ORDER with the routing
@@ -522,24 +551,45 @@ __global__ void __launch_bounds__(256) mxmoe_combine_kernel(MxMoeWs ws, int nt, 
 {
     pdl_wait();
     pdl_trigger();
+    // Four consecutive output rows per thread (16-byte loads of the slot rows).
     const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-    if (i >= (long)nt * hidden) return;
-    const int t = (int)(i / hidden), row = (int)(i - (long)t * hidden);
-    int slot[MXMOE_MAX_TOPK];
-    float w[MXMOE_MAX_TOPK], y[MXMOE_MAX_TOPK];
+    const int h4 = hidden >> 2;
+    if (i >= (long)nt * h4) return;
+    const int t = (int)(i / h4), row = (int)(i - (long)t * h4) * 4;
+    int slot[MXMOE_MAX_TOPK + 1];
+    float w[MXMOE_MAX_TOPK];
 #pragma unroll
     for (int k = 0; k < MXMOE_MAX_TOPK; k++) {
         slot[k] = k < topk ? ws.pos[t * topk + k] : -1;
         w[k] = k < topk ? ws.wts[t * topk + k] : 0.0f;
     }
+    slot[MXMOE_MAX_TOPK] = has_shared ? ws.b_off[ws.meta[0]] + t : -1;
+    float4 y[MXMOE_MAX_TOPK + 1];
 #pragma unroll
-    for (int k = 0; k < MXMOE_MAX_TOPK; k++) y[k] = slot[k] >= 0 ? ws.ypart[(size_t)slot[k] * hidden + row] : 0.0f;
-    float o = 0.0f;
+    for (int k = 0; k <= MXMOE_MAX_TOPK; k++)
+        y[k] = slot[k] >= 0 ? *reinterpret_cast<const float4 *>(ws.ypart + (size_t)slot[k] * hidden + row)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    float o0 = 0.0f, o1 = 0.0f, o2 = 0.0f, o3 = 0.0f;
 #pragma unroll
     for (int k = 0; k < MXMOE_MAX_TOPK; k++)
-        if (slot[k] >= 0) o = __fadd_rn(o, __fmul_rn(w[k], y[k]));
-    if (has_shared) o = __fadd_rn(o, ws.ypart[(size_t)(ws.b_off[ws.meta[0]] + t) * hidden + row]);
-    out[i] = o;
+        if (slot[k] >= 0) {
+            o0 = __fadd_rn(o0, __fmul_rn(w[k], y[k].x));
+            o1 = __fadd_rn(o1, __fmul_rn(w[k], y[k].y));
+            o2 = __fadd_rn(o2, __fmul_rn(w[k], y[k].z));
+            o3 = __fadd_rn(o3, __fmul_rn(w[k], y[k].w));
+        }
+    if (has_shared) {
+        const float4 sh = y[MXMOE_MAX_TOPK];
+        o0 = __fadd_rn(o0, sh.x);
+        o1 = __fadd_rn(o1, sh.y);
+        o2 = __fadd_rn(o2, sh.z);
+        o3 = __fadd_rn(o3, sh.w);
+    }
+    float *o = out + (size_t)t * hidden + row;
+    o[0] = o0;
+    o[1] = o1;
+    o[2] = o2;
+    o[3] = o3;
 }
 
 // ------------------------------------------------------------ host side
@@ -714,7 +764,7 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     if (r) return r;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
     {
-        const int items = s.max_tiles * s.tpt * (s.inter / 32);
+        const int items = s.max_tiles * s.tpt * (s.inter / 128);
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_swiglu_kernel, dim3((items * 32 + 255) / 256), dim3(256), 0, st, ws, s.inter,
                                    terms, s.tpt, s.NB, limit, items));
     }
@@ -725,7 +775,7 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     while (kb2 > 1 && (s.inter / 128) % kb2) kb2 >>= 1;
     r = mxmoe_dispatch<MoeDown>(s.NB, kb2, tb2, pd, g2, st);
     if (r) return r;
-    DSV4CU_CUDA_TRY(launch_pdl(mxmoe_combine_kernel, dim3((unsigned)(((long)nt * s.hidden + 255) / 256)), dim3(256), 0,
+    DSV4CU_CUDA_TRY(launch_pdl(mxmoe_combine_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)), dim3(256), 0,
                                st, ws, nt, topk, s.hidden, s.has_shared, out));
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
     return DSV4CU_OK;
@@ -749,7 +799,7 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
     {
         // Every SM takes part in the split; each CTA repeats the (cheap) routing.
-        const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 32);
+        const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 128);
         const int grid = (int)min((long)sms, max(1L, (tasks + 31) / 32));
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_prep_kernel, dim3(grid), dim3(1024), 0, st, tab, x, logits, bias, tid2eid,
                                    token_ids, s.n_experts, topk, route_scale, nt, s.hidden, s.has_shared, MX_TERMS,
@@ -925,28 +975,22 @@ __global__ void __launch_bounds__(1024) mxpf_scatter_kernel(MxMoeWs ws, PfWs pf,
         for (int t = threadIdx.x; t < nt; t += blockDim.x) ws.b_tok[pf.e_off[n_experts] + t] = t;
 }
 
-// Gate/up B operand of the prefill: one warp per (column tile, slot, 32-wide
-// K block), all terms of that slot.
+// Gate/up B operand of the prefill: one warp per (column tile, slot, 128-wide
+// K chunk), all terms of that chunk.
 __global__ void __launch_bounds__(256) mxpf_split_kernel(const float *__restrict__ x, int hidden, MxMoeWs ws,
                                                          int terms, int tpt, int NB, long max_tasks)
 {
     pdl_wait();
     pdl_trigger();
     const long task = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31, nblk = hidden >> 5;
+    const int kc = hidden >> 7;
     if (task >= max_tasks) return;
-    const int it = (int)(task / nblk), blk = (int)(task - (long)it * nblk);
+    const int it = (int)(task / kc), c = (int)(task - (long)it * kc);
     const int i = it / tpt, tl = it - i * tpt;
     if (i >= ws.meta[2] || tl >= ws.c_cnt[i]) return;
     const int tok = ws.b_tok[ws.c_slot0[i] + tl];
-    uint8_t q[4], sb[4];
-    mx_split_all(x[(size_t)tok * hidden + blk * 32 + lane], terms, q, sb);
-    const int nbb = (NB + 127) / 128;
-    for (int j = 0; j < terms; j++) {
-        const int n = j * tpt + tl;
-        ws.xq1[((size_t)i * NB + n) * hidden + blk * 32 + lane] = q[j];
-        if (lane == 0) ws.sfb1[((size_t)i * (hidden >> 7) + (blk >> 2)) * nbb * 512 + mx_sfb_offset(n, blk & 3)] = sb[j];
-    }
+    mxmoe_split_row_chunk(x + (size_t)tok * hidden, hidden, c, i, tl, terms, tpt, NB, (NB + 127) / 128, ws.xq1,
+                          ws.sfb1);
 }
 
 static MxMoeShape mxpf_shape(const dsv4cu_moe *L, int topk, int nt, int terms)
@@ -991,7 +1035,8 @@ size_t moe_mx_prefill_workspace(const dsv4cu_moe *L, int topk, int nt, int terms
 
 int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float *logits, const float *bias,
                    const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
-                   int terms, int *idx_out, float *wts_out, void *wsp, int *status, int sms, cudaStream_t st)
+                   int terms, int *idx_out, float *wts_out, void *wsp, int *status, int sms, cudaStream_t st,
+                   cudaEvent_t *ev)
 {
     if (nt > PF_MAX_NT || topk > MXMOE_MAX_TOPK || L->n_experts > PREP_MAX_EXPERTS)
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_prefill: nt %d / topk %d / experts %d beyond %d / 16 / 512",
@@ -1004,6 +1049,7 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
     const float *tab = router_table_get();
     if (!tab) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "moe_prefill: router table setup failed");
     const int npairs = nt * topk, nchunks = (npairs + PF_CHUNK - 1) / PF_CHUNK;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
     DSV4CU_CUDA_TRY(cudaMemsetAsync(ws.meta, 0, 64, st));
     DSV4CU_CUDA_TRY(launch_pdl(mxpf_route_kernel, dim3((nt * 32 + 255) / 256), dim3(256), 0, st, tab, logits, bias,
                                tid2eid, token_ids, s.n_experts, topk, route_scale, nt, ws, idx_out, wts_out));
@@ -1012,10 +1058,11 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
                                s.has_shared, s.tpt, s.max_tiles));
     DSV4CU_CUDA_TRY(launch_pdl(mxpf_scatter_kernel, dim3(nchunks), dim3(1024), 0, st, ws, pf, npairs, s.n_experts, topk,
                                nt, s.has_shared));
-    const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 32);
+    const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 128);
     DSV4CU_CUDA_TRY(launch_pdl(mxpf_split_kernel, dim3((unsigned)((tasks * 32 + 255) / 256)), dim3(256), 0, st, x,
                                s.hidden, ws, terms, s.tpt, s.NB, tasks));
-    return mxmoe_gemms(L, s, ws, terms, limit, out, status, sms, st, nullptr);
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
+    return mxmoe_gemms(L, s, ws, terms, limit, out, status, sms, st, ev);
 }
 
 }  // namespace dsv4cu

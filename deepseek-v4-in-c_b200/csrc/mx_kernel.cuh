@@ -9,7 +9,7 @@
 // e4m3), loaded by TMA from a tensor map in 128-row x 128-element boxes with
 // 128-byte swizzle; FP4 boxes use the TMA type that spreads 16 values over 16
 // shared-memory bytes, the operand form kind::mxf8f6f4 reads. The B operand
-// is the activation written as e4m3 terms (mx_split_term): NB rows of a term
+// is the activation written as e4m3 terms (mx_split128): NB rows of a term
 // buffer, same box shape. Scale factors come as prepared 512-byte blocks (one
 // per 128 rows x 128 K) by 1-D bulk copy and reach TMEM through tcgen05.cp.
 //
@@ -96,56 +96,67 @@ DSV4CU_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *
 // Named barrier of the four epilogue warps.
 DSV4CU_DEV void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Term j of the exact e4m3 split of one 32-wide block (one value per lane,
-// whole warp): returns the e4m3 byte and sets *sbyte to the block's E8M0
-// scale byte. r_0 = v; s_j = smallest power of two with max|r_j| <= 448 s_j;
-// q_j = RNE_e4m3(r_j / s_j); r_{j+1} = r_j - q_j s_j (exact). Non-finite
-// inputs stay out of the block maximum: NaN stays NaN, infinities saturate.
-DSV4CU_DEV uint8_t mx_split_term(float v, int term, uint8_t *sbyte)
+// Exact split of 128 consecutive fp32 values (one 128-wide K chunk; lane l
+// holds values 4l .. 4l+3, so lanes 8b .. 8b+7 hold 32-block b) into `terms`
+// (<= 4) e4m3 terms with one E8M0 scale per 32-block and term:
+//   s_0   = the smallest power of two with max|x| <= 448 s_0 over the block,
+//   s_j   = s_0 * 2^(-4j),
+//   q_j   = RNE_e4m3(r_j / s_j),   r_0 = x,   r_{j+1} = r_j - q_j s_j (exact).
+// |r_j| <= 448 s_j holds for every j (after a term the residual is at most
+// half an e4m3 step, 16 s_j = 256 s_{j+1}), so no term saturates, and the
+// remaining error is at most 16 s_{T-1}: about 2^(-4T) of the block maximum.
+// q[j] returns this lane's 4 bytes of term j (byte i = value 4l + i);
+// sb[j] the block's scale byte. Non-finite values stay out of the block
+// maximum: NaN stays NaN, infinities saturate. Whole warp.
+DSV4CU_DEV void mx_split128(const float (&v)[4], int terms, uint32_t (&q)[4], uint8_t (&sb)[4])
 {
-    float r = v;
-    for (int j = 0;; j++) {
-        float a = isfinite(r) ? fabsf(r) : 0.0f;
+    float a = 0.0f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
-        int e = 0;
-        if (a > 0.0f) {
-            int E;
-            const float f = frexpf(a, &E);
-            e = max(-127, min(127, E - 9 + (f > 0.875f ? 1 : 0)));
-        }
-        uint16_t two;
-        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(two) : "f"(0.0f), "f"(ldexpf(r, -e)));
-        const uint8_t q = (uint8_t)(two & 0xFF);
-        if (j == term) {
-            *sbyte = (uint8_t)(127 + e);
-            return q;
-        }
-        r = r - ldexpf(e4m3_to_f32(q), e);
+    for (int i = 0; i < 4; i++) a = fmaxf(a, isfinite(v[i]) ? fabsf(v[i]) : 0.0f);
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 1));
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 2));
+    a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 4));
+    int e0 = 0;
+    if (a > 0.0f) {
+        int E;
+        const float f = frexpf(a, &E);
+        e0 = max(-127, min(127, E - 9 + (f > 0.875f ? 1 : 0)));
     }
-}
-
-// All terms 0..terms-1 of the same split in one pass (terms <= 4).
-DSV4CU_DEV void mx_split_all(float v, int terms, uint8_t (&q)[4], uint8_t (&sb)[4])
-{
-    float r = v;
+    float r[4] = {v[0], v[1], v[2], v[3]};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
         if (j >= terms) break;
-        float a = isfinite(r) ? fabsf(r) : 0.0f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
-        int e = 0;
-        if (a > 0.0f) {
-            int E;
-            const float f = frexpf(a, &E);
-            e = max(-127, min(127, E - 9 + (f > 0.875f ? 1 : 0)));
-        }
-        uint16_t two;
-        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(two) : "f"(0.0f), "f"(ldexpf(r, -e)));
-        q[j] = (uint8_t)(two & 0xFF);
+        const int e = max(-127, e0 - 4 * j);
+        const float inv = ldexpf(1.0f, -e), sc = ldexpf(1.0f, e);
+        uint16_t lo, hi;
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(r[1] * inv), "f"(r[0] * inv));
+        asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(r[3] * inv), "f"(r[2] * inv));
+        q[j] = (uint32_t)lo | ((uint32_t)hi << 16);
         sb[j] = (uint8_t)(127 + e);
-        r = r - ldexpf(e4m3_to_f32(q[j]), e);
+        uint32_t h01, h23;
+        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h01) : "h"(lo));
+        asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h23) : "h"(hi));
+        const float2 f01 = __half22float2(*reinterpret_cast<const __half2 *>(&h01));
+        const float2 f23 = __half22float2(*reinterpret_cast<const __half2 *>(&h23));
+        r[0] = r[0] - f01.x * sc;
+        r[1] = r[1] - f01.y * sc;
+        r[2] = r[2] - f23.x * sc;
+        r[3] = r[3] - f23.y * sc;
+    }
+}
+
+// Writes the terms of one 128-value chunk: term j goes to row_j[j] (bytes
+// 4l .. 4l+3 of the chunk from lane l) and its scale to sf_j[j][kb] with kb =
+// lane / 8 (the lane that starts each 32-block writes it).
+DSV4CU_DEV void mx_store128(const uint32_t (&q)[4], const uint8_t (&sb)[4], int terms, uint8_t *const (&row)[4],
+                            uint8_t *const (&sf)[4], const int (&sf_step)[4])
+{
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        if (j >= terms) break;
+        *reinterpret_cast<uint32_t *>(row[j] + 4 * lane) = q[j];
+        if ((lane & 7) == 0) sf[j][(lane >> 3) * sf_step[j]] = sb[j];
     }
 }
 

@@ -8,7 +8,7 @@
 //
 // Activations. The MMA's B operand is e4m3 with one E8M0 scale per 32 values
 // and per column. An fp32 activation x is written as a sum of T e4m3 terms
-// (mx_split_term): each term is its own B column with its own scales and the
+// (mx_split128): each term is its own B column with its own scales and the
 // epilogue sums a token's T columns. The remaining error per element is
 // below 2^(-4T) of its block's magnitude: T = 3 keeps matmul results within
 // the 1e-3 bar with margin, T = 4 is close to fp32, T = 1 is plain MXFP8.
@@ -48,24 +48,35 @@ __global__ void sfa_blocks_kernel(uint8_t *__restrict__ out, const uint8_t *__re
     ((uint32_t *)out)[(size_t)blk * 128 + m0 * 4 + m1] = v;
 }
 
-// Activation split for the dense problem: one warp per (B column, 32-wide K
-// block), lane = element. Column n of column tile tn holds term (n % NB) /
-// tpt of token tn * tpt + (n % NB) % tpt; unused columns are zero.
-__global__ void xsplit_kernel(const float *__restrict__ x, int nt, int K, int ldx, int terms, int tpt, int NB,
-                              int tiles_n, uint8_t *__restrict__ xq, uint8_t *__restrict__ sfb)
+// Activation split for the dense problem: one warp per (token, 128-wide K
+// chunk). Column n of column tile tn holds term n / tpt of token tn * tpt +
+// n % tpt; columns past terms x tpt only feed accumulator columns that are
+// never read.
+__global__ void __launch_bounds__(256) xsplit_kernel(const float *__restrict__ x, int nt, int K, int ldx, int terms,
+                                                     int tpt, int NB, uint8_t *__restrict__ xq,
+                                                     uint8_t *__restrict__ sfb)
 {
     const long gw = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31, nblk = K >> 5;
-    if (gw >= (long)tiles_n * NB * nblk) return;
-    const int n = (int)(gw / nblk), blk = (int)(gw - (long)n * nblk);
-    const int tn = n / NB, nl = n - tn * NB, term = nl / tpt, tl = nl - term * tpt, tok = tn * tpt + tl;
-    uint8_t q = 0, sbyte = 0;
-    if (term < terms && tok < nt) q = mx_split_term(x[(size_t)tok * ldx + blk * 32 + lane], term, &sbyte);
-    xq[(size_t)n * K + blk * 32 + lane] = q;
-    if (lane == 0) {
-        const int nbb = (NB + 127) / 128;
-        sfb[((size_t)tn * (K >> 7) + (blk >> 2)) * nbb * 512 + mx_sfb_offset(nl, blk & 3)] = sbyte;
+    const int lane = threadIdx.x & 31, kc = K >> 7;
+    if (gw >= (long)nt * kc) return;
+    const int tok = (int)(gw / kc), c = (int)(gw - (long)tok * kc);
+    const int tn = tok / tpt, tl = tok - tn * tpt, nbb = (NB + 127) / 128;
+    float v[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = x[(size_t)tok * ldx + c * 128 + 4 * lane + i];
+    uint32_t q[4];
+    uint8_t sb[4];
+    mx_split128(v, terms, q, sb);
+    uint8_t *row[4], *sf[4];
+    int step[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int n = j * tpt + tl;
+        row[j] = xq + ((size_t)tn * NB + n) * K + c * 128;
+        sf[j] = sfb + ((size_t)tn * kc + c) * nbb * 512 + mx_sfb_offset(n, 0);
+        step[j] = 1;
     }
+    mx_store128(q, sb, terms, row, sf, step);
 }
 
 // ------------------------------------------------------------ dense policy
@@ -249,9 +260,9 @@ int mx_gemm(const MxMat *m, float *y, const float *x, int nt, int terms, int nb_
     uint8_t *xq = (uint8_t *)ws;
     uint8_t *sfb = xq + dsv4cu_align256((size_t)t.tiles_n * t.NB * K);
     {
-        const long warps = (long)t.tiles_n * t.NB * (K / 32);
-        xsplit_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(x, nt, K, K, terms, t.tpt, t.NB,
-                                                                           t.tiles_n, xq, sfb);
+        const long warps = (long)nt * (K / 128);
+        xsplit_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(x, nt, K, K, terms, t.tpt, t.NB, xq,
+                                                                           sfb);
         DSV4CU_LAUNCH_CHECK();
     }
     CUtensorMap tb;

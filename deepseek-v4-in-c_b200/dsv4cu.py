@@ -69,6 +69,7 @@ def lib() -> C.CDLL:
             "dsv4cu_moe_decode": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp]),
             "dsv4cu_moe_prefill_workspace": (sz, [vp, i, i, i]),
             "dsv4cu_moe_prefill": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, i, vp, vp, vp]),
+            "dsv4cu_moe_prefill_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, i, vp, vp, vp, vp]),
             "dsv4cu_moe_decode_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp, vp]),
             "dsv4cu_mat_create": (i, [C.POINTER(vp), vp, vp]),
             "dsv4cu_mat_destroy": (None, [vp]),
@@ -307,11 +308,15 @@ class Device:
         self.L.dsv4cu_moe_destroy(layer)
 
     def moe_prefill(self, layer, out, x, logits, topk, route_scale, limit, nt, terms=3, idx_out=None,
-                    wts_out=None, bias=None, tid2eid=None, token_ids=None):
-        check(self.L.dsv4cu_moe_prefill(self.ctx, layer, self.ptr(out), self.ptr(x), self.ptr(logits),
-                                        self.ptr(bias), self.ptr(tid2eid), self.ptr(token_ids), topk, route_scale,
-                                        limit, nt, terms, self.ptr(idx_out), self.ptr(wts_out), self.stream()),
-              "dsv4cu_moe_prefill")
+                    wts_out=None, bias=None, tid2eid=None, token_ids=None, events=None):
+        args = (self.ctx, layer, self.ptr(out), self.ptr(x), self.ptr(logits), self.ptr(bias), self.ptr(tid2eid),
+                self.ptr(token_ids), topk, route_scale, limit, nt, terms, self.ptr(idx_out), self.ptr(wts_out),
+                self.stream())
+        if events is None:
+            check(self.L.dsv4cu_moe_prefill(*args), "dsv4cu_moe_prefill")
+        else:
+            evp = (C.c_void_p * 4)(*[e.cuda_event for e in events])
+            check(self.L.dsv4cu_moe_prefill_ev(*args, evp), "dsv4cu_moe_prefill_ev")
 
     def moe_decode(self, layer, out, x, logits, topk, route_scale, limit, nt, idx_out=None, wts_out=None,
                    bias=None, tid2eid=None, token_ids=None, stream=None, events=None):

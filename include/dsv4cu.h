@@ -197,6 +197,14 @@ int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, con
                        const float *logits, const float *bias, const int64_t *tid2eid,
                        const int *token_ids, int topk, float route_scale, float limit,
                        int nt, int terms, int *idx_out, float *wts_out, void *stream);
+/* dsv4cu_moe_prefill recording 4 cudaEvent_t (events, may be NULL) on the
+ * stream: before routing, before the first GEMM, after the gate/up GEMM and
+ * after the last launch. */
+int dsv4cu_moe_prefill_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
+                          const float *logits, const float *bias, const int64_t *tid2eid,
+                          const int *token_ids, int topk, float route_scale, float limit,
+                          int nt, int terms, int *idx_out, float *wts_out, void *stream,
+                          void **events);
 
 /* Top-k indices of scores[n], descending, ties to the lower index, k clamped
  * to n; replaces dsv4_topk (src/10_compute/dsv4_topk.c:76-112) without its
