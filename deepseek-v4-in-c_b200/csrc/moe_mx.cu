@@ -505,43 +505,44 @@ struct MoeDown {
 
 // SwiGLU (dsv4_ops.c:61-79: up clamped both ways, gate from above only) of
 // every slot, split into e4m3 terms (mx_split128) for the down projection's B
-// operand: one warp per (column tile, slot, 128-wide chunk of inter).
+// operand: one warp per (column tile, slot, group of cpt 128-wide chunks).
 __global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter, int terms, int tpt, int NB,
-                                                           float limit, int max_items)
+                                                           float limit, int cpt, int max_items)
 {
     pdl_wait();
     pdl_trigger();
     const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
-    const int kc = inter >> 7, ntiles = ws.meta[2];
+    const int kc = inter >> 7, ntiles = ws.meta[2], groups = kc / cpt;
     if (gw >= max_items) return;
-    const int it = gw / kc, c = gw - it * kc, i = it / tpt, tl = it - i * tpt;
+    const int it = gw / groups, grp = gw - it * groups, i = it / tpt, tl = it - i * tpt;
     if (i >= ntiles || tl >= ws.c_cnt[i]) return;
-    const int slot = ws.c_slot0[i] + tl;
-    const float *g = ws.gu + (size_t)slot * 2 * inter + c * 128 + 4 * lane, *u = g + inter;
-    float v[4];
+    const int slot = ws.c_slot0[i] + tl, nbb = (NB + 127) / 128;
+    for (int c = grp * cpt; c < (grp + 1) * cpt; c++) {
+        const float *g = ws.gu + (size_t)slot * 2 * inter + c * 128 + 4 * lane, *u = g + inter;
+        float v[4];
 #pragma unroll
-    for (int k = 0; k < 4; k++) {
-        float gg = g[k], uu = u[k];
-        if (limit > 0.0f) {
-            uu = fminf(fmaxf(uu, -limit), limit);
-            gg = fminf(gg, limit);
+        for (int k = 0; k < 4; k++) {
+            float gg = g[k], uu = u[k];
+            if (limit > 0.0f) {
+                uu = fminf(fmaxf(uu, -limit), limit);
+                gg = fminf(gg, limit);
+            }
+            v[k] = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.0f, expf(-gg))), uu);
         }
-        v[k] = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.0f, expf(-gg))), uu);
-    }
-    uint32_t q[4];
-    uint8_t sb[4];
-    mx_split128(v, terms, q, sb);
-    const int nbb = (NB + 127) / 128;
-    uint8_t *row[4], *sf[4];
-    int step[4];
+        uint32_t q[4];
+        uint8_t sb[4];
+        mx_split128(v, terms, q, sb);
+        uint8_t *row[4], *sf[4];
+        int step[4];
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const int n = j * tpt + tl;
-        row[j] = ws.xq2 + ((size_t)i * NB + n) * inter + c * 128;
-        sf[j] = ws.sfb2 + ((size_t)i * kc + c) * nbb * 512 + mx_sfb_offset(n, 0);
-        step[j] = 1;
+        for (int j = 0; j < 4; j++) {
+            const int n = j * tpt + tl;
+            row[j] = ws.xq2 + ((size_t)i * NB + n) * inter + c * 128;
+            sf[j] = ws.sfb2 + ((size_t)i * kc + c) * nbb * 512 + mx_sfb_offset(n, 0);
+            step[j] = 1;
+        }
+        mx_store128(q, sb, terms, row, sf, step);
     }
-    mx_store128(q, sb, terms, row, sf, step);
 }
 
 // Output rows: per token the routed pairs IN k ORDER with the routing
@@ -764,9 +765,11 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     if (r) return r;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
     {
-        const int items = s.max_tiles * s.tpt * (s.inter / 128);
+        // Few slots (decode): one chunk per warp; many (prefill): whole rows.
+        const int cpt = s.npairs > 1024 ? s.inter / 128 : 1;
+        const int items = s.max_tiles * s.tpt * (s.inter / 128 / cpt);
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_swiglu_kernel, dim3((items * 32 + 255) / 256), dim3(256), 0, st, ws, s.inter,
-                                   terms, s.tpt, s.NB, limit, items));
+                                   terms, s.tpt, s.NB, limit, cpt, items));
     }
 
     MoeDown::Params pd;
@@ -975,22 +978,20 @@ __global__ void __launch_bounds__(1024) mxpf_scatter_kernel(MxMoeWs ws, PfWs pf,
         for (int t = threadIdx.x; t < nt; t += blockDim.x) ws.b_tok[pf.e_off[n_experts] + t] = t;
 }
 
-// Gate/up B operand of the prefill: one warp per (column tile, slot, 128-wide
-// K chunk), all terms of that chunk.
+// Gate/up B operand of the prefill: one warp per (column tile, slot) walks
+// the token's row chunk by chunk (the table lookups are paid once per row).
 __global__ void __launch_bounds__(256) mxpf_split_kernel(const float *__restrict__ x, int hidden, MxMoeWs ws,
                                                          int terms, int tpt, int NB, long max_tasks)
 {
     pdl_wait();
     pdl_trigger();
     const long task = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
-    const int kc = hidden >> 7;
     if (task >= max_tasks) return;
-    const int it = (int)(task / kc), c = (int)(task - (long)it * kc);
-    const int i = it / tpt, tl = it - i * tpt;
+    const int i = (int)(task / tpt), tl = (int)(task - (long)i * tpt);
     if (i >= ws.meta[2] || tl >= ws.c_cnt[i]) return;
-    const int tok = ws.b_tok[ws.c_slot0[i] + tl];
-    mxmoe_split_row_chunk(x + (size_t)tok * hidden, hidden, c, i, tl, terms, tpt, NB, (NB + 127) / 128, ws.xq1,
-                          ws.sfb1);
+    const int tok = ws.b_tok[ws.c_slot0[i] + tl], nbb = (NB + 127) / 128;
+    for (int c = 0; c < (hidden >> 7); c++)
+        mxmoe_split_row_chunk(x + (size_t)tok * hidden, hidden, c, i, tl, terms, tpt, NB, nbb, ws.xq1, ws.sfb1);
 }
 
 static MxMoeShape mxpf_shape(const dsv4cu_moe *L, int topk, int nt, int terms)
@@ -1058,7 +1059,7 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
                                s.has_shared, s.tpt, s.max_tiles));
     DSV4CU_CUDA_TRY(launch_pdl(mxpf_scatter_kernel, dim3(nchunks), dim3(1024), 0, st, ws, pf, npairs, s.n_experts, topk,
                                nt, s.has_shared));
-    const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 128);
+    const long tasks = (long)s.max_tiles * s.tpt;
     DSV4CU_CUDA_TRY(launch_pdl(mxpf_split_kernel, dim3((unsigned)((tasks * 32 + 255) / 256)), dim3(256), 0, st, x,
                                s.hidden, ws, terms, s.tpt, s.NB, tasks));
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
