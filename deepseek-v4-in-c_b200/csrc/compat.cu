@@ -18,6 +18,7 @@
 #include "../../include/dsv4_compat.h"
 #include "common.cuh"
 #include "ctx.h"
+#include "mxgemm.h"
 
 namespace {
 
@@ -40,6 +41,9 @@ struct HostState {
     cudaStream_t st = nullptr;
     std::map<uintptr_t, RegEntry> reg;   // keyed by host start address
     size_t reg_bytes = 0;
+    // Tensor-core preparations (TMA map + scale blocks) of mirrored
+    // matrices, keyed by the device weight address.
+    std::map<uintptr_t, dsv4cu::MxMat> mx;
     DevBuf buf[8];
 };
 
@@ -143,6 +147,17 @@ void reg_drop(std::map<uintptr_t, RegEntry>::iterator it)
 {
     HostState &s = S();
     cudaStreamSynchronize(s.st);
+    // Tensor-core preparations that read the dropped mirror go with it.
+    const uintptr_t a = (uintptr_t)it->second.dev, b = a + it->second.bytes;
+    for (auto jt = s.mx.begin(); jt != s.mx.end();) {
+        const uintptr_t w = (uintptr_t)jt->second.q.w, sc = (uintptr_t)jt->second.q.s;
+        if ((w >= a && w < b) || (sc >= a && sc < b)) {
+            dsv4cu::mx_release(&jt->second);
+            jt = s.mx.erase(jt);
+        } else {
+            ++jt;
+        }
+    }
     cudaFree(it->second.dev);
     s.reg_bytes -= it->second.bytes;
     s.reg.erase(it);
@@ -258,6 +273,34 @@ void unknown_wdt(const DSV4QMat *m)
     abort();
 }
 
+// y = x * W^T on device buffers, through the best available kernel.
+int mmq_dev(float *dy, const float *dx, const dsv4cu_qmat *dq, int nt)
+{
+    HostState &s = S();
+    if (nt >= dsv4cu::MX_MMQ_MIN_TOKENS && dsv4cu::mx_supported(dq)) {
+        auto it = s.mx.find((uintptr_t)dq->w);
+        if (it != s.mx.end() && (it->second.q.s != dq->s || it->second.q.rows != dq->rows ||
+                                 it->second.q.cols != dq->cols || it->second.q.wdt != dq->wdt ||
+                                 it->second.q.blk_r != dq->blk_r || it->second.q.blk_c != dq->blk_c)) {
+            dsv4cu::mx_release(&it->second);
+            s.mx.erase(it);
+            it = s.mx.end();
+        }
+        if (it == s.mx.end()) {
+            dsv4cu::MxMat m;
+            int r = dsv4cu::mx_prepare(&m, dq, nullptr, s.st);
+            if (r) return r;
+            it = s.mx.emplace((uintptr_t)dq->w, m).first;
+        }
+        void *ws = nullptr;
+        int r = dsv4cu_ws_get(s.ctx, dsv4cu::mx_workspace(&it->second, nt, dsv4cu::MX_MMQ_TERMS), &ws);
+        if (r) return r;
+        return dsv4cu::mx_gemm(&it->second, dy, dx, nt, dsv4cu::MX_MMQ_TERMS, 0, 0, ws, s.ctx->sm_count, s.ctx->status,
+                               s.st);
+    }
+    return dsv4cu_mmq(s.ctx, dy, dx, dq, nt, s.st);
+}
+
 // y (host) = x (host) * W^T; returns a status instead of aborting.
 int mmq_host(float *y, const float *x, const DSV4QMat *m, int nt)
 {
@@ -272,7 +315,7 @@ int mmq_host(float *y, const float *x, const DSV4QMat *m, int nt)
     float *dx = (float *)buf(0, xb), *dy = (float *)buf(1, yb);
     if (!dx || !dy) return dsv4cu_set_error(DSV4CU_ERR_NOMEM, "staging");
     DSV4CU_CUDA_TRY(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, s.st));
-    r = dsv4cu_mmq(s.ctx, dy, dx, &dq, nt, s.st);
+    r = mmq_dev(dy, dx, &dq, nt);
     if (r) return r;
     DSV4CU_CUDA_TRY(cudaMemcpyAsync(y, dy, yb, cudaMemcpyDeviceToHost, s.st));
     DSV4CU_CUDA_TRY(cudaStreamSynchronize(s.st));
@@ -567,8 +610,8 @@ extern "C" int dsv4_prefill_vk_expert_fused(DSV4PrefillVk *v, float *y, const fl
         float *dm = (float *)buf(3, ib), *dy = (float *)buf(4, ob);
         if (!dx || !dg || !du || !dm || !dy) goto fail;
         if (cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, s.st) != cudaSuccess) goto fail;
-        if (dsv4cu_mmq(s.ctx, dg, dx, &q1, n, s.st) || dsv4cu_mmq(s.ctx, du, dx, &q3, n, s.st) ||
-            dsv4cu_swiglu(dm, dg, du, n * inter, limit, s.st) || dsv4cu_mmq(s.ctx, dy, dm, &q2, n, s.st))
+        if (mmq_dev(dg, dx, &q1, n) || mmq_dev(du, dx, &q3, n) || dsv4cu_swiglu(dm, dg, du, n * inter, limit, s.st) ||
+            mmq_dev(dy, dm, &q2, n))
             goto fail;
         if (cudaMemcpyAsync(y, dy, ob, cudaMemcpyDeviceToHost, s.st) != cudaSuccess) goto fail;
         // The CPU fill callback runs while the device is busy, until it reports

@@ -15,6 +15,7 @@
 #include "ctx.h"
 #include "gemv_core.cuh"
 #include "gemv.h"
+#include "mxgemm.h"
 #include "tma_gemv.cuh"
 #include "tmap.h"
 
@@ -299,8 +300,23 @@ int mmq_run(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *q, int
 
 using namespace dsv4cu;
 
+// Products of many tokens go to the tcgen05 GEMM; its per-matrix preparation
+// (tensor map, scale blocks) is made in the workspace for this one call.
+static bool mmq_use_mx(const dsv4cu_qmat *m, int nt) { return nt >= MX_MMQ_MIN_TOKENS && mx_supported(m); }
+
+static size_t mmq_mx_workspace(const dsv4cu_qmat *m, int nt)
+{
+    MxMat tm;
+    memset(&tm, 0, sizeof(tm));
+    tm.q = *m;
+    tm.kc = m->cols / 128;
+    tm.tiles_m = (m->rows + 127) / 128;
+    return dsv4cu_align256(mx_sfa_bytes(m)) + mx_workspace(&tm, nt, MX_MMQ_TERMS);
+}
+
 extern "C" size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt)
 {
+    if (m && nt > 0 && mmq_use_mx(m, nt)) return mmq_mx_workspace(m, nt);
     return mmq_workspace(m, nt, 148);
 }
 
@@ -319,6 +335,15 @@ extern "C" int dsv4cu_mmq(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4c
     if (m->wdt == DSV4CU_WFP4 && (m->cols & 1))
         return dsv4cu_set_error(DSV4CU_ERR_ARG, "mmq: FP4 cols must be even");
     void *ws = nullptr;
+    if (mmq_use_mx(m, nt)) {
+        int r = dsv4cu_ws_get(ctx, mmq_mx_workspace(m, nt), &ws);
+        if (r) return r;
+        MxMat tm;
+        r = mx_prepare(&tm, m, (uint8_t *)ws, (cudaStream_t)stream);
+        if (r) return r;
+        return mx_gemm(&tm, y, x, nt, MX_MMQ_TERMS, 0, 0, (char *)ws + dsv4cu_align256(mx_sfa_bytes(m)),
+                       ctx->sm_count, ctx->status, (cudaStream_t)stream);
+    }
     const size_t need = mmq_workspace(m, nt, ctx->sm_count);
     if (need) {
         int r = dsv4cu_ws_get(ctx, need, &ws);

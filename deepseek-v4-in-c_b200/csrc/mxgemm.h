@@ -26,6 +26,12 @@ struct MxTiling {
     int NB, tpt, tiles_n, KB;
 };
 
+// dsv4cu_mmq (and the reference-signature matmuls built on it) hands
+// products of at least MX_MMQ_MIN_TOKENS tokens to the tensor-core GEMM with
+// MX_MMQ_TERMS exact activation terms (results within ~1e-6 of fp32).
+constexpr int MX_MMQ_MIN_TOKENS = 1;
+constexpr int MX_MMQ_TERMS = 4;
+
 bool mx_supported(const dsv4cu_qmat *q);
 size_t mx_sfa_bytes(const dsv4cu_qmat *q);
 // sfa_buf: caller-owned block of mx_sfa_bytes(q) device bytes, or NULL to

@@ -80,9 +80,12 @@ size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt);
 
 /* y[t*rows + o] = sum_c x[t*cols + c] * W[o][c], t < nt, fp32 in and out.
  * Replaces dsv4_mmq_n (src/10_compute/dsv4_matmul.h:40) on device memory.
- * Every geometry the reference accepts is covered: fast tensor-core paths for
- * FP8 with blk_c % 16 == 0, FP4 with blk_c % 32 == 0 and BF16, and an exact
- * per-element path for every other block geometry. */
+ * Every geometry the reference accepts is covered. FP4/FP8 matrices with
+ * cols % 128 == 0 and blk_c % 32 == 0 (FP4 weights 32-byte, FP8 16-byte
+ * aligned) run on the tcgen05 block-scaled GEMM with 4 exact activation terms
+ * (results within ~1e-6 of fp32; a batch row is bit-identical to the same
+ * token computed alone); other FP8/FP4 geometries and BF16 use mma.sync
+ * kernels, and any remaining block geometry an exact per-element path. */
 int dsv4cu_mmq(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
                int nt, void *stream);
 
