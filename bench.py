@@ -1,25 +1,29 @@
-"""Benchmark of the hot path: the FP4 MoE layer decode step.
+"""Benchmark of the hot path. Default: the FP4 MoE layer decode step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|prefill|gemv]
 
-One step = one MoE layer decode for one token per GPU: router over 256
-bf16-valued logits -> top-8 of 256 HBM-resident FP4 experts (2048x4096 w1/w3,
-4096x2048 w2, 1x32 E8M0 scales) + the FP8 shared expert (128x128 E8M0) ->
-SwiGLU -> weighted k-order combine, hidden 4096. Every step routes a fresh
-token (seeded logits), and L2 is flushed (256 MiB write) before each timed step,
-so each step streams its ~132 MB of expert weights from HBM.
+decode (config 2, the headline). One step = one MoE layer decode for one
+token per GPU: router over 256 bf16-valued logits -> top-8 of 256
+HBM-resident FP4 experts (2048x4096 w1/w3, 4096x2048 w2, 1x32 E8M0 scales) +
+the FP8 shared expert (128x128 E8M0) -> SwiGLU -> weighted k-order combine,
+hidden 4096. Four such layers (13.7 GB of weights, far beyond L2) are used in
+turn with a fresh token every step and the K steps run back to back, as a
+decoder's layers do, so each step streams its ~132 MB of expert weights from
+HBM.
+prefill (config 3): 4096 tokens through the MoE layer + the FP8 QKV projection.
+gemv (config 1): FP8 7168x7168 GEMV, four matrices in turn, back to back.
 
-value  = tokens/s over all ranks, device time (CUDA events, max over ranks).
-e2e    = the same through the public C ABI (dsv4cu_moe_decode) from pinned host
-         buffers: H2D of x + logits and D2H of the output inside the timed region.
-roofline: the dominant kernel (w1/w3 + SwiGLU) timed live with CUDA events on
-         its stream; algorithmic bytes = weight bytes of the 9 experts' w1/w3
-         plus activations in/out; peak = MEASURED_PEAKS.json hbm_gbs.
-cpu_baseline: the reference's own CPU kernels (oracle/_ref, dsv4_route +
-         9 x dsv4_expert_forward + the k-order combine) on the host's cores.
+value  = the workload's metric over all ranks, device time (CUDA events, max
+         over ranks).
+e2e    = the same through the public C ABI from host buffers, with the
+         host<->device copies inside the timed region.
+roofline: the dominant kernel timed live with CUDA events on its stream;
+         peak = MEASURED_PEAKS.json.
+cpu_baseline: the reference's own CPU kernels (oracle/_ref) on the host's cores.
 --impl reference: times that reference CPU path as the reference arm.
-N > 1: every rank runs an independent replica of the layer on its own token
-         ("replicas"; the expert-parallel NCCL path is not used by this bench).
+N > 1: every rank runs an independent replica on its own tokens ("replicas";
+         the expert-parallel NCCL path is not used by this bench).
 """
 from __future__ import annotations
 
@@ -59,9 +63,9 @@ def parse():
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts resident in HBM (256 = config 2; smaller only for ncu captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv"], default="decode",
                     help="decode = config 2 (the headline); prefill = config 3 (MoE layer over 4096 tokens + "
-                         "FP8 QKV projection)")
+                         "FP8 QKV projection); gemv = config 1 (FP8 7168x7168 GEMV, HBM GB/s)")
     return ap.parse_args()
 
 
@@ -79,10 +83,10 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
-def load_traffic():
+def load_traffic(name="moe_gate_up_config2.json"):
     """dram bytes per launch of the dominant kernel from the committed ncu summary."""
     try:
-        with open(os.path.join(ROOT, "profiles", "moe_gate_up_config2.json")) as f:
+        with open(os.path.join(ROOT, "profiles", name)) as f:
             return json.load(f).get("dram_bytes_per_launch")
     except Exception:
         return None
@@ -135,14 +139,15 @@ class Clocks:
 
 
 # ----------------------------------------------------------------- our arm
-def build_layer(dev, torch, n_experts=N_EXPERTS):
-    """n_experts FP4 routed experts + 1 FP8 shared expert, N(0, 0.02) quantized on device."""
+def build_layer(dev, torch, n_experts=N_EXPERTS, layer_id=0):
+    """n_experts FP4 routed experts + 1 FP8 shared expert, N(0, 0.02) quantized
+    on device; layer_id selects distinct weights."""
     import dsv4cu
     keep = []
     src = torch.empty(INTER * HIDDEN, dtype=torch.float32, device="cuda")
 
     def mat(fmt, rows, cols, seed):
-        dev.fill_normal(src, seed, 0.0, 0.02)
+        dev.fill_normal(src, seed + 100003 * layer_id, 0.0, 0.02)
         if fmt == 3:
             W = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
             S = torch.empty(rows * cols // 32, dtype=torch.uint8, device="cuda")
@@ -176,6 +181,9 @@ def step_inputs(n, seed):
     return x, lg
 
 
+D_LAYERS = 4          # MoE layers used in turn by the decode bench: 4 x 3.4 GB of experts
+
+
 def run_ours(args, rank, local_rank, world):
     import torch
     import dsv4cu
@@ -188,21 +196,20 @@ def run_ours(args, rank, local_rank, world):
         pg = tdist
     dev = dsv4cu.Device(local_rank)
     NE = args.experts
-    layer, keep = build_layer(dev, torch, NE)
+    built = [build_layer(dev, torch, NE, l) for l in range(D_LAYERS)]
+    layers = [b[0] for b in built]
     n_steps = args.warmup + args.steps
     xs, lgs = step_inputs(n_steps, 1000 + rank)
     lgs = np.ascontiguousarray(lgs[:, :NE])
     dx = torch.from_numpy(xs).cuda()
     dl = torch.from_numpy(lgs).cuda()
-    out = torch.empty((1, HIDDEN), dtype=torch.float32, device="cuda")
-    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")   # 256 MiB > L2
-    st = torch.cuda.current_stream()
+    out = torch.empty((n_steps, HIDDEN), dtype=torch.float32, device="cuda")
 
     def step(i, ev=None):
-        dev.moe_decode(layer, out, dx[i:i + 1], dl[i:i + 1], TOPK, ROUTE_SCALE, LIMIT, 1, events=ev)
+        dev.moe_decode(layers[i % D_LAYERS], out[i:i + 1], dx[i:i + 1], dl[i:i + 1], TOPK, ROUTE_SCALE, LIMIT, 1,
+                       events=ev)
 
     for i in range(args.warmup):
-        flush.zero_()
         step(i)
     torch.cuda.synchronize()
 
@@ -210,25 +217,22 @@ def run_ours(args, rank, local_rank, world):
         if pg:
             pg.barrier()
 
-    # ---- headline: device time per step, L2 flushed before each step
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # ---- headline: K decode steps back to back, layer k % 4 at step k
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = Clocks(local_rank)
     barrier()
     torch.cuda.synchronize()
     clocks.start()
     wall0 = time.perf_counter()
+    t0.record()
     for k in range(args.steps):
-        flush.zero_()
-        starts[k].record()
         step(args.warmup + k)
-        ends[k].record()
+    t1.record()
     torch.cuda.synchronize()
     wall = time.perf_counter() - wall0
     barrier()
     clk = clocks.stop()
-    ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(ms)
+    total_ms = t0.elapsed_time(t1)
     t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
     if pg:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -241,33 +245,44 @@ def run_ours(args, rank, local_rank, world):
             ev.record()
     torch.cuda.synchronize()
     for k in range(args.steps):
-        flush.zero_()
         step(args.warmup + k, evs[k])
     torch.cuda.synchronize()
     ph = np.array([[e[i].elapsed_time(e[i + 1]) for i in range(3)] for e in evs])
     ph_ms = ph.mean(axis=0)
 
-    # ---- e2e through the public API from pinned host buffers
+    # ---- one isolated step after an L2 flush (cold launch; for reference)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")   # 256 MiB > L2
+    iso = []
+    for k in range(min(args.steps, 20)):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step(args.warmup + k)
+        b.record()
+        torch.cuda.synchronize()
+        iso.append(a.elapsed_time(b))
+    del flush
+
+    # ---- e2e through the public API from pinned host buffers, back to back
     hx = torch.from_numpy(xs).pin_memory()
     hl = torch.from_numpy(lgs).pin_memory()
-    hout = torch.empty((args.steps, HIDDEN), dtype=torch.float32).pin_memory()
-    e_s = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    e_e = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    hout = torch.empty((n_steps, HIDDEN), dtype=torch.float32).pin_memory()
     gx = torch.empty((1, HIDDEN), dtype=torch.float32, device="cuda")
     gl = torch.empty((1, NE), dtype=torch.float32, device="cuda")
+    go = torch.empty((1, HIDDEN), dtype=torch.float32, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    e0.record()
     for k in range(args.steps):
         i = args.warmup + k
-        flush.zero_()
-        e_s[k].record()
         gx.copy_(hx[i:i + 1], non_blocking=True)
         gl.copy_(hl[i:i + 1], non_blocking=True)
-        dev.moe_decode(layer, out, gx, gl, TOPK, ROUTE_SCALE, LIMIT, 1)
-        hout[k].copy_(out[0], non_blocking=True)
-        e_e[k].record()
+        dev.moe_decode(layers[i % D_LAYERS], go, gx, gl, TOPK, ROUTE_SCALE, LIMIT, 1)
+        hout[i].copy_(go[0], non_blocking=True)
+    e1.record()
     torch.cuda.synchronize()
-    e2e_ms = sum(s.elapsed_time(e) for s, e in zip(e_s, e_e))
+    e2e_ms = e0.elapsed_time(e1)
     t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
     if pg:
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
@@ -289,9 +304,12 @@ def run_ours(args, rank, local_rank, world):
         "dtype": "e2m1/e4m3 weights x e4m3 activation terms (4, exact split) -> f32 (tcgen05 kind::mxf8f6f4)",
         "data": "synthetic: weights N(0,0.02) quantized on device, x/logits N(0,1) bf16-valued, seeded",
         "config": {"workload": WORKLOAD, "global_batch": world, "parallelism": f"replicas x{world}",
-                   "l2": "flushed before every timed step (256 MiB write, untimed)",
+                   "l2": f"inputs larger than L2: {D_LAYERS} layers (each 256 FP4 experts + its FP8 shared expert, "
+                         f"13.7 GB in all) used in turn, a fresh token per step, steps back to back",
                    "algorithmic_bytes_per_step": STEP_BYTES,
                    "step_hbm_gbs": round(STEP_BYTES / (total_ms / args.steps * 1e-3) / 1e9, 1),
+                   "isolated_step_ms": round(float(np.median(iso)), 5),
+                   "isolated_step_note": "one step after a 256 MiB L2 flush, CUDA events around it",
                    "wall_s_timed_loop": round(wall, 4)},
         "roofline": {"bound": "hbm", "kernel": "mx_kernel<8,4,MoeGateUp> (tcgen05 w1/w3 GEMV of 9 experts)",
                      "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind,
@@ -313,9 +331,10 @@ def run_ours(args, rank, local_rank, world):
     if pg:
         pg.barrier()
         pg.destroy_process_group()
-    dev.moe_destroy(layer)
+    for layer in layers:
+        dev.moe_destroy(layer)
     dev.close()
-    del keep
+    del built
     return res if rank == 0 else None
 
 
@@ -664,10 +683,235 @@ def run_prefill_reference(args, rank, world):
             "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# --------------------------------------------------- config 1: FP8 GEMV
+G1_N = 7168
+G1_TERMS = 4          # the activation split dsv4_mmq uses (MX_MMQ_TERMS)
+G1_BYTES = G1_N * G1_N + (G1_N // 128) ** 2 + 2 * G1_N * 4   # e4m3 W + E8M0 128x128 scales + f32 x, y
+G1_METRIC = "GEMV HBM GB/s (FP8 e4m3 7168x7168, 128x128 E8M0 block scales, one token)"
+G1_WORKLOAD = ("config1: y = W x, W 7168x7168 e4m3 from N(0,0.02) with one E8M0 scale per 128x128 block, "
+               "x one bf16-valued N(0,1) vector, f32 accumulate and output")
+
+
+def g1_inputs(n, seed):
+    sys.path.insert(0, PKG)
+    import pack
+    rng = np.random.default_rng(seed)
+    return pack.bf16_round(rng.standard_normal((n, G1_N)).astype(np.float32))
+
+
+G1_SETS = 4          # distinct weight matrices rotated: 205 MB > L2
+
+
+def run_gemv(args, rank, local_rank, world):
+    import torch
+    import dsv4cu
+    torch.cuda.set_device(local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        pg = tdist
+    dev = dsv4cu.Device(local_rank)
+    mats, hs = [], []
+    src = torch.empty(G1_N * G1_N, dtype=torch.float32, device="cuda")
+    for j in range(G1_SETS):
+        dev.fill_normal(src, j, 0.0, 0.02)
+        W = torch.empty(G1_N * G1_N, dtype=torch.uint8, device="cuda")
+        S = torch.empty((G1_N // 128) ** 2, dtype=torch.uint8, device="cuda")
+        dev.quantize_fp8(W, S, src, G1_N, G1_N)
+        mats.append((W, S))
+        hs.append(dev.mat_create(dsv4cu.QMat(W.data_ptr(), S.data_ptr(), 2, G1_N, G1_N, 128, 128)))
+    del src
+    n_steps = args.warmup + args.steps
+    xs = g1_inputs(n_steps, 4000 + rank)
+    dx = torch.from_numpy(xs).cuda()
+    y = torch.empty((n_steps, G1_N), dtype=torch.float32, device="cuda")
+
+    def step(i, ev=None):
+        dev.mat_gemm(hs[i % G1_SETS], y[i:i + 1], dx[i:i + 1], 1, G1_TERMS, events=ev)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    # ---- headline: K GEMVs back to back, each on the next of 4 matrices
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local_rank)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record()
+    for k in range(args.steps):
+        step(args.warmup + k)
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = t0.elapsed_time(t1)
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    total_ms = t.item()
+    # ---- the GEMM kernel alone, live on its stream (events between the launches)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    for e in evs:
+        for ev in e:
+            ev.record()
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        step(args.warmup + k, evs[k])
+    torch.cuda.synchronize()
+    ph = np.array([[e[i].elapsed_time(e[i + 1]) for i in range(2)] for e in evs]).mean(axis=0)
+    # ---- one isolated GEMV after an L2 flush (cold launch; for reference)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")   # 256 MiB > L2
+    iso = []
+    for k in range(min(args.steps, 20)):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step(args.warmup + k)
+        b.record()
+        torch.cuda.synchronize()
+        iso.append(a.elapsed_time(b))
+    del flush
+    # ---- e2e: the reference's own entry point dsv4_mmq (include/dsv4_compat.h)
+    # on host buffers, back to back over the same 4 matrices (uploaded once,
+    # then resident in HBM); wall clock over the K calls.
+    import ctypes as C
+    L = dsv4cu.lib()
+    host = [(W.cpu().numpy(), S.cpu().numpy()) for W, S in mats]
+    qh = [dsv4cu.QMat(w.ctypes.data, sc.ctypes.data, 2, G1_N, G1_N, 128, 128) for w, sc in host]
+    hy = np.zeros((n_steps, G1_N), np.float32)
+    for j in range(G1_SETS):
+        L.dsv4_mmq(hy[j].ctypes.data, xs[j].ctypes.data, C.byref(qh[j]))    # upload + warm-up
+    if pg:
+        pg.barrier()
+    w0 = time.perf_counter()
+    for k in range(args.steps):
+        i = args.warmup + k
+        L.dsv4_mmq(hy[i].ctypes.data, xs[i].ctypes.data, C.byref(qh[i % G1_SETS]))
+    e2e_s = time.perf_counter() - w0
+    t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    e2e_s = t.item()
+    L.dsv4cu_host_forget_all()
+    dev.check_status()
+    peak, peak_kind = load_peaks()
+    ms = total_ms / args.steps
+    value = world * G1_BYTES / (ms * 1e-3) / 1e9
+    achieved = G1_BYTES / (ph[1] * 1e-3) / 1e9
+    res = {
+        "metric": G1_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": f"e4m3 weights x e4m3 activation terms ({G1_TERMS}, exact split) -> f32 (tcgen05 kind::mxf8f6f4)",
+        "data": "synthetic: W N(0,0.02) quantized on device, x N(0,1) bf16-valued, seeded",
+        "config": {"workload": G1_WORKLOAD, "global_batch": world, "parallelism": f"replicas x{world}",
+                   "l2": f"inputs larger than L2: {G1_SETS} distinct 7168x7168 matrices (205 MB) used in turn, "
+                         "GEMVs back to back",
+                   "algorithmic_bytes_per_step": G1_BYTES,
+                   "isolated_step_ms": round(float(np.median(iso)), 5),
+                   "isolated_step_note": "one GEMV after a 256 MiB L2 flush, CUDA events around it (includes "
+                                         "~6 us of event/launch latency an empty kernel shows the same way)"},
+        "roofline": {"bound": "hbm", "kernel": "mx_kernel<8,4,DenseMx> (tcgen05 GEMV, split-K)",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": load_traffic("gemv_fp8_config1.json"),
+                     "algorithmic_bytes": G1_BYTES,
+                     "kernel_ms": {"split": round(ph[0], 5), "gemm": round(ph[1], 5)},
+                     "step_frac": round(value / world / peak, 4)},
+        "e2e": {"value": round(world * args.steps * G1_BYTES / e2e_s / 1e9, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": G1_N * 4, "d2h_bytes_per_step": G1_N * 4,
+                "api": "dsv4_mmq (include/dsv4_compat.h, the reference's signature) on host buffers, wall clock "
+                       "over the K calls"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_gemv_baseline(args.cpu_seconds)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    for h in hs:
+        dev.mat_destroy(h)
+    dev.close()
+    return res if rank == 0 else None
+
+
+G1_CPU_SETS = 8      # host copies rotated by the CPU legs: 411 MB, beyond a server L3
+
+
+def cpu_gemv_setup():
+    sys.path.insert(0, ORACLE)
+    os.environ.setdefault("OMP_NUM_THREADS", str(cpu_threads()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import oracle
+    import pack
+    if not oracle.RefLib.available():
+        return None
+    rng = np.random.default_rng(0)
+    W, S = pack.quantize_fp8((rng.standard_normal((G1_N, G1_N), dtype=np.float32) * np.float32(0.02)))
+    keep = [(np.ascontiguousarray(np.roll(W, 7 * j, axis=0)), S) for j in range(G1_CPU_SETS)]
+    qs = [oracle.qmat(w, sc, 2, G1_N, G1_N, 128, 128) for w, sc in keep]
+    return oracle.RefLib(), qs, keep
+
+
+def cpu_gemv_time(ref, qs, xs, seconds, max_calls):
+    ref.mmq(xs[0:1], qs[0])
+    n, t0 = 0, time.perf_counter()
+    while n < max_calls and (time.perf_counter() - t0 < seconds or n < 3):
+        ref.mmq(xs[n % len(xs):n % len(xs) + 1], qs[n % len(qs)])
+        n += 1
+    return n, time.perf_counter() - t0
+
+
+def cpu_gemv_baseline(seconds):
+    st = cpu_gemv_setup()
+    if st is None:
+        return {"value": None, "unit": "GB/s", "cores": 0, "kind": "port", "sample": "oracle/_ref not built"}
+    ref, qs, keep = st
+    xs = g1_inputs(8, 77)
+    n, dt = cpu_gemv_time(ref, qs, xs, seconds, 4000)
+    return {"value": round(n * G1_BYTES / dt / 1e9, 3), "unit": "GB/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "kind": "reference", "sample": f"{n} calls of the reference's dsv4_mmq on config 1 ({dt:.2f} s), "
+                                           f"{G1_CPU_SETS} distinct host matrices (411 MB) in turn"}
+
+
+def run_gemv_reference(args, rank, world):
+    if rank != 0:
+        return None
+    st = cpu_gemv_setup()
+    if st is None:
+        return {"impl": "reference", "unavailable": "oracle/_ref/libdsv4ref.so was not built"}
+    ref, qs, keep = st
+    xs = g1_inputs(args.warmup + args.steps, 2000)
+    for i in range(args.warmup):
+        ref.mmq(xs[i:i + 1], qs[i % len(qs)])
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        i = args.warmup + k
+        ref.mmq(xs[i:i + 1], qs[i % len(qs)])
+    dt = time.perf_counter() - t0
+    v = args.steps * G1_BYTES / dt / 1e9
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    return {"impl": "reference", "metric": G1_METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3 weights x f32 (AVX2 FMA)", "data": "synthetic, seeded",
+            "config": {"workload": G1_WORKLOAD, "global_batch": 1, "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+                             "sample": f"{args.steps} calls of the reference's dsv4_mmq (src/10_compute), "
+                                       f"{cores} threads, {G1_CPU_SETS} distinct host matrices in turn"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def main():
     args = parse()
     rank, local_rank, world = dist_env()
-    if args.workload == "prefill":
+    if args.workload == "gemv":
+        res = (run_gemv_reference(args, rank, world) if args.impl == "reference"
+               else run_gemv(args, rank, local_rank, world))
+    elif args.workload == "prefill":
         res = (run_prefill_reference(args, rank, world) if args.impl == "reference"
                else run_prefill(args, rank, local_rank, world))
     elif args.impl == "reference":

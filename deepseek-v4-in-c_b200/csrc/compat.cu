@@ -293,7 +293,8 @@ int mmq_dev(float *dy, const float *dx, const dsv4cu_qmat *dq, int nt)
             it = s.mx.emplace((uintptr_t)dq->w, m).first;
         }
         void *ws = nullptr;
-        int r = dsv4cu_ws_get(s.ctx, dsv4cu::mx_workspace(&it->second, nt, dsv4cu::MX_MMQ_TERMS), &ws);
+        int r = dsv4cu_ws_get(s.ctx, dsv4cu::mx_workspace(&it->second, nt, dsv4cu::MX_MMQ_TERMS, s.ctx->sm_count),
+                              &ws);
         if (r) return r;
         return dsv4cu::mx_gemm(&it->second, dy, dx, nt, dsv4cu::MX_MMQ_TERMS, 0, 0, ws, s.ctx->sm_count, s.ctx->status,
                                s.st);

@@ -304,19 +304,19 @@ using namespace dsv4cu;
 // (tensor map, scale blocks) is made in the workspace for this one call.
 static bool mmq_use_mx(const dsv4cu_qmat *m, int nt) { return nt >= MX_MMQ_MIN_TOKENS && mx_supported(m); }
 
-static size_t mmq_mx_workspace(const dsv4cu_qmat *m, int nt)
+static size_t mmq_mx_workspace(const dsv4cu_qmat *m, int nt, int sms)
 {
     MxMat tm;
     memset(&tm, 0, sizeof(tm));
     tm.q = *m;
     tm.kc = m->cols / 128;
     tm.tiles_m = (m->rows + 127) / 128;
-    return dsv4cu_align256(mx_sfa_bytes(m)) + mx_workspace(&tm, nt, MX_MMQ_TERMS);
+    return dsv4cu_align256(mx_sfa_bytes(m)) + mx_workspace(&tm, nt, MX_MMQ_TERMS, sms);
 }
 
 extern "C" size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt)
 {
-    if (m && nt > 0 && mmq_use_mx(m, nt)) return mmq_mx_workspace(m, nt);
+    if (m && nt > 0 && mmq_use_mx(m, nt)) return mmq_mx_workspace(m, nt, mx_device_sms());
     return mmq_workspace(m, nt, 148);
 }
 
@@ -336,7 +336,7 @@ extern "C" int dsv4cu_mmq(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4c
         return dsv4cu_set_error(DSV4CU_ERR_ARG, "mmq: FP4 cols must be even");
     void *ws = nullptr;
     if (mmq_use_mx(m, nt)) {
-        int r = dsv4cu_ws_get(ctx, mmq_mx_workspace(m, nt), &ws);
+        int r = dsv4cu_ws_get(ctx, mmq_mx_workspace(m, nt, ctx->sm_count), &ws);
         if (r) return r;
         MxMat tm;
         r = mx_prepare(&tm, m, (uint8_t *)ws, (cudaStream_t)stream);

@@ -437,6 +437,8 @@ DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc,
     T.b_row = i * c.nb;
     T.k0 = 0;
     T.kc = kc;
+    T.nseg = 1;
+    T.kst = 1;
     return T;
 }
 
@@ -446,6 +448,7 @@ struct MoeGateUp {
     struct Params {
         MxMoeCommon c;
     };
+    static constexpr bool kPrefetchA = false;   // the experts come from the routing kernel
     DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * 2 * (p.c.inter >> 7); }
     DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
     DSV4CU_DEV static int terms(const Params &p) { return p.c.terms; }
@@ -461,7 +464,7 @@ struct MoeGateUp {
         T.id3 = 0;
         return T;
     }
-    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v)
+    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v, int)
     {
         if (tl < p.c.tpt && tl < p.c.ws.c_cnt[T.id0]) {
             const int slot = p.c.ws.c_slot0[T.id0] + tl;
@@ -477,6 +480,7 @@ struct MoeDown {
     struct Params {
         MxMoeCommon c;
     };
+    static constexpr bool kPrefetchA = false;   // the experts come from the routing kernel
     DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * (p.c.hidden >> 7); }
     DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
     DSV4CU_DEV static int terms(const Params &p) { return p.c.terms; }
@@ -492,7 +496,7 @@ struct MoeDown {
         T.id3 = 0;
         return T;
     }
-    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v)
+    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v, int)
     {
         if (tl < p.c.tpt && tl < p.c.ws.c_cnt[T.id0]) {
             const int slot = p.c.ws.c_slot0[T.id0] + tl;

@@ -47,6 +47,10 @@ struct MxTile {
     int b_row;               // first row of the B term buffer
     int k0;                  // first 128-wide K chunk (a K segment of a split tile)
     int kc;                  // 128-wide K chunks of this tile
+    // K segments accumulated separately, in order, each handed to the
+    // epilogue on its own: the tile's kc chunks form kst equal granules and
+    // segment s covers granules [s * kst / nseg, (s + 1) * kst / nseg).
+    int nseg, kst;
     int id0, id1, id2, id3;  // problem-specific tile coordinates
 };
 
@@ -176,6 +180,10 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accf[2], acce[2], drain;
     __shared__ uint32_t tmem_holder;
     __shared__ volatile int abort_flag;
+    // The epilogue warps' own stop decision, one slot per segment parity: a
+    // slot is written only before the named barrier of its segment and read
+    // after it, so the four warps always agree on it.
+    __shared__ volatile int epi_stop[2];
     __shared__ int epi_words[64];    // policy scratch (epilogue warps only)
     // Descriptors of this CTA's first MX_TCACHE tiles, resolved once up front
     // (a policy's tile() may chase table entries in global memory).
@@ -196,7 +204,34 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         }
         mbar_init(&drain, 1);
         abort_flag = 0;
+        epi_stop[0] = epi_stop[1] = 0;
         fence_mbar_init();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    // Stages whose A operand (weights + scale blocks) is requested before the
+    // previous kernel has finished: a policy whose A side and tile list do not
+    // depend on that kernel's output fills the first ring's worth early.
+    int pre = 0;
+    if constexpr (P::kPrefetchA) {
+        if (threadIdx.x == 0) {
+            const int nt0 = P::ntiles(p);
+            for (int t = blockIdx.x; t < nt0 && pre < STAGES; t += gridDim.x) {
+                const MxTile T = P::tile(p, t);
+                const uint32_t tx = KB * (T.a_tx + C::B_BOX + C::SFA_BOX + C::SFB_BOX);
+                const int nst = T.kc / KB;
+                for (int c = 0; c < nst && pre < STAGES; c++, pre++) {
+                    uint8_t *st = smem + pre * C::STAGE;
+                    mbar_arrive_expect_tx(&full[pre], tx);
+#pragma unroll
+                    for (int b = 0; b < KB; b++) {
+                        const int kc = T.k0 + c * KB + b;
+                        tma_load_2d(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[pre]);
+                        bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
+                                  &full[pre]);
+                    }
+                }
+            }
+        }
     }
     if (warp == 1) {
         umma::tmem_alloc(&tmem_holder, C::TMEM_COLS);
@@ -234,44 +269,55 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
                 const int nst = T.kc / KB;
                 for (int c = 0; c < nst; c++, it++) {
                     const int s = it % STAGES, r = it / STAGES;
-                    if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, err, MXE_EMPTY)) {
-                        abort_flag = 1;
-                        break;
-                    }
                     uint8_t *st = smem + s * C::STAGE;
-                    mbar_arrive_expect_tx(&full[s], tx);
+                    if (it >= pre) {
+                        if (r > 0 && !mbar_wait(&empty[s], (r - 1) & 1, err, MXE_EMPTY)) {
+                            abort_flag = 1;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+                        for (int b = 0; b < KB; b++) {
+                            const int kc = T.k0 + c * KB + b;
+                            tma_load_2d(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s]);
+                            bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
+                                      &full[s]);
+                        }
+                    }
 #pragma unroll
                     for (int b = 0; b < KB; b++) {
                         const int kc = T.k0 + c * KB + b;
-                        tma_load_2d(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s]);
                         tma_load_2d(st + C::OFF_B + b * C::B_BOX, &tb, kc * 128, T.b_row, &full[s]);
-                        bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
-                                  &full[s]);
                         bulk_load(st + C::OFF_SFB + b * C::SFB_BOX, T.sfb + (size_t)kc * C::SFB_BOX, C::SFB_BOX,
                                   &full[s]);
                     }
                 }
             }
-            // Every issued copy lands before the CTA can exit.
-            for (int j = max(0, it - STAGES); j < it; j++)
+            // Every issued copy lands before the CTA can exit. (After an abort
+            // a stage requested early may lack its B half: its bounded wait
+            // gives up long after the A copy has landed.)
+            const int hi = it > pre ? it : pre;
+            for (int j = max(0, hi - STAGES); j < hi; j++)
                 mbar_wait(&full[j % STAGES], (j / STAGES) & 1, nullptr, 0);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            int it = 0, tcount = 0;
-            for (int t = blockIdx.x; t < ntiles && !abort_flag; t += gridDim.x, tcount++) {
-                const MxTile T = tile_of(t, tcount);
-                const int nst = T.kc / KB;
+            int it = 0, tcount = 0, kt = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok && !abort_flag; t += gridDim.x, kt++) {
+                const MxTile T = tile_of(t, kt);
+                const int gs = T.kc / KB / T.kst;     // stages per granule
+                for (int sg = 0; sg < T.nseg && ok; sg++, tcount++) {
                 const int ab = tcount % C::ACC_BUFS, use = tcount / C::ACC_BUFS;
                 if (use > 0 && !mbar_wait(&acce[ab], (use - 1) & 1, err, MXE_ACC_EMPTY)) {
-                    abort_flag = 1;
+                    ok = false;
                     break;
                 }
                 umma::fence_after();
                 const uint32_t dacc = tmem + ab * NB;
-                bool ok = true;
-                for (int c = 0; c < nst; c++, it++) {
+                const int c0 = sg * T.kst / T.nseg * gs, c1 = (sg + 1) * T.kst / T.nseg * gs;
+                for (int c = c0; c < c1; c++, it++) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&full[s], (it / STAGES) & 1, err, MXE_FULL)) {
                         ok = false;
@@ -293,18 +339,16 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
                         for (int k = 0; k < 4; k++) {
                             const uint32_t id = T.idesc | ((uint32_t)k << 4) | ((uint32_t)k << 29);
                             umma::mma_mx(dacc, umma::desc_sw128(sa + 32 * k), umma::desc_sw128(sb + 32 * k), id,
-                                         (c | b | k) ? 1u : 0u, tsfa | ((uint32_t)k << 30),
+                                         ((c - c0) | b | k) ? 1u : 0u, tsfa | ((uint32_t)k << 30),
                                          tsfb | ((uint32_t)k << 30));
                         }
                     }
                     umma::commit(&empty[s]);
                 }
-                if (!ok) {
-                    abort_flag = 1;
-                    break;
+                if (ok) umma::commit(&accf[ab]);
                 }
-                umma::commit(&accf[ab]);
             }
+            if (!ok) abort_flag = 1;
             // Every MMA / copy this thread issued completes before TMEM is freed.
             umma::commit(&drain);
             mbar_wait(&drain, 0, err, MXE_DRAIN);
@@ -315,20 +359,31 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         const int q = warp & 3;             // the TMEM lane quarter this warp may read
         const int row_l = q * 32 + lane;
         const int terms = P::terms(p), tpt = P::tpt(p);
-        int tcount = 0;
-        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, tcount++) {
+        // A stopped MMA warp commits no more accumulators, so the epilogue
+        // learns of any abort through its own bounded wait.
+        int tcount = 0, kt = 0;
+        bool stop = false;
+        for (int t = blockIdx.x; t < ntiles && !stop; t += gridDim.x, kt++) {
+            const MxTile T = tile_of(t, kt);
+            for (int sg = 0; sg < T.nseg; sg++, tcount++) {
             const int ab = tcount % C::ACC_BUFS, use = tcount / C::ACC_BUFS;
             bool ok = true;
             if (lane == 0) ok = mbar_wait(&accf[ab], use & 1, err, MXE_ACC_FULL);
             ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-            if (!ok) abort_flag = 1;
+            if (!ok) {
+                epi_stop[tcount & 1] = 1;
+                abort_flag = 1;
+            }
             epi_sync();
-            if (abort_flag) break;      // every epilogue warp leaves at the same tile
+            if (epi_stop[tcount & 1]) {
+                stop = true;            // every epilogue warp leaves at the same segment
+                break;
+            }
             umma::fence_after();
-            const MxTile T = tile_of(t, tcount);
             const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * NB;
             if constexpr (NB <= 16) {
-                // Narrow tiles: all NB columns at once, then per token.
+                // Narrow tiles: all NB columns at once, then per token; the
+                // terms of token tl are columns tl, tpt + tl, 2 tpt + tl, ...
                 float v[NB];
 #pragma unroll
                 for (int c8 = 0; c8 < NB; c8 += 8) {
@@ -339,10 +394,15 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
                 }
                 for (int tl = 0; tl < tpt; tl++) {
                     float a = 0.0f;
+                    bool first = true;
 #pragma unroll
-                    for (int c = 0; c < NB; c++)
-                        if (c % tpt == tl && c / tpt < terms) a += v[c];
-                    P::store(p, T, row_l, tl, a);
+                    for (int c = 0; c < NB; c++) {
+                        if (c % tpt == tl && c / tpt < terms) {
+                            a = first ? v[c] : a + v[c];
+                            first = false;
+                        }
+                    }
+                    P::store(p, T, row_l, tl, a, sg);
                 }
             } else {
                 for (int tb = 0; tb < tpt; tb += 8) {
@@ -355,16 +415,18 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
                         for (int i = 0; i < 8; i++) acc[i] += v[i];
                     }
 #pragma unroll
-                    for (int i = 0; i < 8; i++) P::store(p, T, row_l, tb + i, acc[i]);
+                    for (int i = 0; i < 8; i++) P::store(p, T, row_l, tb + i, acc[i], sg);
                 }
             }
             // The accumulator is free once every epilogue warp has read it.
             umma::fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[ab]);
+            }
+            if (stop) break;
             P::finish(p, T, row_l, epi_words);
         }
-        if (!abort_flag) P::finish_all(p, row_l, ntiles, epi_words);
+        if (!stop) P::finish_all(p, row_l, ntiles, epi_words);
     }
 
     umma::fence_before();

@@ -52,10 +52,17 @@ __global__ void sfa_blocks_kernel(uint8_t *__restrict__ out, const uint8_t *__re
 // chunk). Column n of column tile tn holds term n / tpt of token tn * tpt +
 // n % tpt; columns past terms x tpt only feed accumulator columns that are
 // never read.
+// Also clears the ncnt split-K tile counters the GEMM after it counts with.
 __global__ void __launch_bounds__(256) xsplit_kernel(const float *__restrict__ x, int nt, int K, int ldx, int terms,
                                                      int tpt, int NB, uint8_t *__restrict__ xq,
-                                                     uint8_t *__restrict__ sfb)
+                                                     uint8_t *__restrict__ sfb, int *__restrict__ cnt, int ncnt)
 {
+    // x, the buffers written below and (on the dsv4cu_mmq path) the weight
+    // scale blocks belong to earlier kernels until they end; after that the
+    // GEMM may launch and stream weights until it needs this kernel's output.
+    pdl_wait();
+    pdl_trigger();
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < ncnt; i += (long)gridDim.x * blockDim.x) cnt[i] = 0;
     const long gw = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31, kc = K >> 7;
     if (gw >= (long)nt * kc) return;
@@ -80,25 +87,41 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const float *__restrict__ x
 }
 
 // ------------------------------------------------------------ dense policy
+// K is cut into S segments of whole granules (g = 4, 2 or 1 chunks, the
+// largest dividing kc; segment s covers granules [s * kst / S, (s + 1) * kst /
+// S) of kst = kc / g). S depends on the matrix and the SM count only, never
+// on the token count, and y = ((p_0 + p_1) + p_2) + ... over the segment
+// partials p_s in every case, so a token's result is the same bits in a
+// batch of any size. Two ways of running it:
+//   cross (few tiles): tile t = (seg * tiles_n + tn) * tiles_m + tm, one
+//     segment per tile on its own CTA, partials to part[seg]; the CTA that
+//     completes a (tm, tn) tile's last segment (a counter per tile) sums the
+//     partials in segment order into y;
+//   in-CTA (tiles fill the GPU): tile t = tn * tiles_m + tm with nseg = S;
+//     the CTA accumulates each segment separately and its epilogue adds it
+//     onto y in order (y = p_0, then y = y + p_s).
 struct DenseMx {
     struct Params {
         CUtensorMap ta;
         const uint8_t *sfa, *sfb;
-        int kc, tiles_m, tiles_n, nb, nbb;
+        int kc, gran, tiles_m, tiles_n, nb, nbb, S, cross;
         int rows, nt, tpt, terms;
-        float *y;
+        float *y;        // in-CTA or S == 1: the output; cross: partials [S][nt][ldy]
+        float *out;      // cross: the output
+        int *cnt;        // cross: completed segments per (tm, tn) tile, cleared by the split kernel
         int ldy;
         uint32_t idesc, a_tx;
         int *err;
     };
-    DSV4CU_DEV static int ntiles(const Params &p) { return p.tiles_m * p.tiles_n; }
+    static constexpr bool kPrefetchA = true;    // weights and tiles are known at launch
+    DSV4CU_DEV static int ntiles(const Params &p) { return p.tiles_m * p.tiles_n * (p.cross ? p.S : 1); }
     DSV4CU_DEV static int *err(const Params &p) { return p.err; }
     DSV4CU_DEV static int terms(const Params &p) { return p.terms; }
     DSV4CU_DEV static int tpt(const Params &p) { return p.tpt; }
     DSV4CU_DEV static MxTile tile(const Params &p, int t)
     {
         MxTile T;
-        const int tm = t % p.tiles_m, tn = t / p.tiles_m;
+        const int tm = t % p.tiles_m, rest = t / p.tiles_m, tn = rest % p.tiles_n, seg = rest / p.tiles_n;
         T.ta = &p.ta;
         T.sfa = p.sfa + (size_t)tm * p.kc * 512;
         T.sfb = p.sfb + (size_t)tn * p.kc * p.nbb * 512;
@@ -106,19 +129,57 @@ struct DenseMx {
         T.a_tx = p.a_tx;
         T.a_row = tm * 128;
         T.b_row = tn * p.nb;
-        T.k0 = 0;
-        T.kc = p.kc;
+        const int kst = p.kc / p.gran;
+        if (p.cross) {
+            const int s0 = seg * kst / p.S, s1 = (seg + 1) * kst / p.S;
+            T.k0 = s0 * p.gran;
+            T.kc = (s1 - s0) * p.gran;
+            T.nseg = 1;
+            T.kst = 1;
+        } else {
+            T.k0 = 0;
+            T.kc = p.kc;
+            T.nseg = p.S;
+            T.kst = kst;
+        }
         T.id0 = tm;
         T.id1 = tn;
-        T.id2 = 0;
+        T.id2 = p.cross ? seg : 0;
+        T.id3 = 0;
         return T;
     }
-    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v)
+    DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v, int sg)
     {
         const int row = T.id0 * 128 + row_l, tok = T.id1 * p.tpt + tl;
-        if (tl < p.tpt && row < p.rows && tok < p.nt) p.y[(size_t)tok * p.ldy + row] = v;
+        if (tl < p.tpt && row < p.rows && tok < p.nt) {
+            float *dst = p.y + ((size_t)T.id2 * p.nt + tok) * p.ldy + row;
+            // The same thread stored the previous segment's sum here.
+            *dst = sg ? __fadd_rn(*dst, v) : v;
+        }
     }
-    DSV4CU_DEV static void finish(const Params &, const MxTile &, int, int *) {}
+    // Cross mode: after its partial stores the CTA counts the segment done;
+    // the one that completes the tile sums part[0] + part[1] + ... in order.
+    DSV4CU_DEV static void finish(const Params &p, const MxTile &T, int row_l, int *words)
+    {
+        if (!p.cross) return;
+        __threadfence();
+        epi_sync();
+        if (row_l == 0) words[0] = atomicAdd(p.cnt + T.id1 * p.tiles_m + T.id0, 1) == p.S - 1;
+        epi_sync();
+        if (!words[0]) return;
+        __threadfence();
+        const int row = T.id0 * 128 + row_l;
+        if (row >= p.rows) return;
+        const size_t n = (size_t)p.nt * p.ldy;
+        for (int tl = 0; tl < p.tpt; tl++) {
+            const int tok = T.id1 * p.tpt + tl;
+            if (tok >= p.nt) break;
+            const float *src = p.y + (size_t)tok * p.ldy + row;
+            float v = __ldcg(src);
+            for (int sg = 1; sg < p.S; sg++) v = __fadd_rn(v, __ldcg(src + sg * n));
+            p.out[(size_t)tok * p.ldy + row] = v;
+        }
+    }
     DSV4CU_DEV static void finish_all(const Params &, int, int, int *) {}
 };
 
@@ -218,22 +279,66 @@ MxTiling mx_tiling(int nt, int terms, int nb_req, int kb_req, int kc)
     return t;
 }
 
-static size_t dense_ws(int K, int kc, const MxTiling &t)
+// Granule of the K segmentation: the largest of 4, 2, 1 chunks dividing kc
+// (every tiling's chunks per stage divide it).
+static int dense_gran(int kc) { return kc % 4 == 0 ? 4 : kc % 2 == 0 ? 2 : 1; }
+
+// K segments of a matrix, sized for the one-token product: S minimises the
+// longest CTA's share, ceil(tiles_m * S / sms) tiles of ceil(kst / S)
+// granules, and must beat one segment by 10 %.
+static int dense_segments(int tiles_m, int kc, int sms)
 {
-    const size_t cols = (size_t)t.tiles_n * t.NB;
-    return dsv4cu_align256(cols * K) + dsv4cu_align256((size_t)t.tiles_n * kc * ((t.NB + 127) / 128) * 512);
+    if (tiles_m >= sms) return 1;
+    const int kst = kc / dense_gran(kc);
+    int S = 1;
+    long best = kst;
+    for (int c = 2; c <= MX_MAX_SEGMENTS && c <= kst; c++) {
+        const long cost = (long)(((long)tiles_m * c + sms - 1) / sms) * ((kst + c - 1) / c);
+        if (cost * 10 < best * 9 && (S == 1 || cost < best)) {
+            best = cost;
+            S = c;
+        }
+    }
+    return S;
 }
 
-size_t mx_workspace(const MxMat *m, int nt, int terms)
+// Segments run on separate CTAs (partials + reduction) while the tiles leave SMs idle.
+static bool dense_cross(int tiles, int S, int sms) { return S > 1 && tiles < sms; }
+
+int mx_device_sms()
+{
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return 148;
+    return n;
+}
+
+// Workspace: B terms, B scale blocks, and in cross mode (S > 1) the partials
+// [S][nt][rows] and one counter per tile.
+static size_t dense_ws(int K, int kc, const MxTiling &t, int nt, int rows, int S)
+{
+    const size_t cols = (size_t)t.tiles_n * t.NB;
+    size_t b = dsv4cu_align256(cols * K) + dsv4cu_align256((size_t)t.tiles_n * kc * ((t.NB + 127) / 128) * 512);
+    if (S > 1)
+        b += dsv4cu_align256((size_t)S * nt * rows * 4) + dsv4cu_align256((size_t)((rows + 127) / 128) * t.tiles_n * 4);
+    return b;
+}
+
+size_t mx_workspace(const MxMat *m, int nt, int terms, int sms)
 {
     // The widest tiling any configuration of this call may pick.
     size_t best = 0;
     const int nbs[7] = {8, 16, 32, 64, 128, 192, 256};
     for (int i = 0; i < 7; i++) {
-        const MxTiling t = mx_tiling(nt, terms, nbs[i], 1, m->kc);
-        if (t.tpt <= 0) continue;
-        const size_t b = dense_ws(m->q.cols, m->kc, t);
-        if (b > best) best = b;
+        for (int kb = 1; kb <= 4; kb *= 2) {
+            const MxTiling t = mx_tiling(nt, terms, nbs[i], kb, m->kc);
+            if (t.tpt <= 0) continue;
+            const int S = dense_segments(m->tiles_m, m->kc, sms);
+            const int Sx = dense_cross(m->tiles_m * t.tiles_n, S, sms) ? S : 1;
+            const size_t b = dense_ws(m->q.cols, m->kc, t, nt, m->q.rows, Sx);
+            if (b > best) best = b;
+        }
     }
     return best;
 }
@@ -243,50 +348,70 @@ static int dense_launch(const CUtensorMap &tb, const DenseMx::Params &p, int sms
 {
     int r = mx_kernel_prepare<NB, KB, DenseMx>();
     if (r) return r;
-    const int tiles = p.tiles_m * p.tiles_n;
-    mx_kernel<NB, KB, DenseMx><<<tiles < sms ? tiles : sms, MX_THREADS, MxCfg<NB, KB>::SMEM, st>>>(tb, p);
-    DSV4CU_LAUNCH_CHECK();
+    const int tiles = p.tiles_m * p.tiles_n * (p.cross ? p.S : 1);
+    DSV4CU_CUDA_TRY(launch_pdl(mx_kernel<NB, KB, DenseMx>, dim3(tiles < sms ? tiles : sms), dim3(MX_THREADS),
+                               MxCfg<NB, KB>::SMEM, st, tb, p));
     return DSV4CU_OK;
 }
 
+static int dense_dispatch(const MxTiling &t, const CUtensorMap &tb, const DenseMx::Params &p, int sms,
+                          cudaStream_t st);
+
 int mx_gemm(const MxMat *m, float *y, const float *x, int nt, int terms, int nb_req, int kb_req, void *ws, int sms,
-            int *err, cudaStream_t st)
+            int *err, cudaStream_t st, cudaEvent_t *ev)
 {
     if (terms < 1 || terms > 4) return dsv4cu_set_error(DSV4CU_ERR_ARG, "mx gemm: terms must be 1..4");
     if (nt <= 0) return DSV4CU_OK;
     const MxTiling t = mx_tiling(nt, terms, nb_req, kb_req, m->kc);
     if (t.tpt <= 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "mx gemm: %d columns cannot hold %d terms", t.NB, terms);
     const int K = m->q.cols;
-    uint8_t *xq = (uint8_t *)ws;
-    uint8_t *sfb = xq + dsv4cu_align256((size_t)t.tiles_n * t.NB * K);
-    {
-        const long warps = (long)nt * (K / 128);
-        xsplit_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(x, nt, K, K, terms, t.tpt, t.NB, xq,
-                                                                           sfb);
-        DSV4CU_LAUNCH_CHECK();
-    }
-    CUtensorMap tb;
-    int r = mx_encode_kmajor(&tb, xq, false, (uint64_t)K, (uint64_t)t.tiles_n * t.NB, (uint64_t)K, (uint32_t)t.NB);
-    if (r) return r;
     DenseMx::Params p;
     memset(&p, 0, sizeof(p));
     p.ta = m->ta;
-    p.sfa = m->sfa;
-    p.sfb = sfb;
     p.kc = m->kc;
+    p.gran = dense_gran(m->kc);
     p.tiles_m = m->tiles_m;
     p.tiles_n = t.tiles_n;
     p.nb = t.NB;
     p.nbb = (t.NB + 127) / 128;
+    p.S = dense_segments(m->tiles_m, m->kc, sms);
+    p.cross = dense_cross(m->tiles_m * t.tiles_n, p.S, sms) ? 1 : 0;
     p.rows = m->q.rows;
     p.nt = nt;
     p.tpt = t.tpt;
     p.terms = terms;
-    p.y = y;
     p.ldy = m->q.rows;
     p.idesc = umma::idesc_mx(m->fp4 ? umma::FMT_E2M1 : umma::FMT_E4M3, umma::FMT_E4M3, 128, t.NB);
     p.a_tx = m->fp4 ? 128 * 64 : 128 * 128;
     p.err = err;
+    uint8_t *xq = (uint8_t *)ws;
+    uint8_t *sfb = xq + dsv4cu_align256((size_t)t.tiles_n * t.NB * K);
+    p.sfa = m->sfa;
+    p.sfb = sfb;
+    float *part = (float *)(sfb + dsv4cu_align256((size_t)t.tiles_n * m->kc * p.nbb * 512));
+    int *cnt = p.cross ? (int *)((char *)part + dsv4cu_align256((size_t)p.S * nt * m->q.rows * 4)) : nullptr;
+    const int ncnt = p.cross ? m->tiles_m * t.tiles_n : 0;
+    p.y = p.cross ? part : y;
+    p.out = y;
+    p.cnt = cnt;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
+    {
+        const long warps = (long)nt * (K / 128);
+        DSV4CU_CUDA_TRY(launch_pdl(xsplit_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st, x,
+                                   nt, K, K, terms, t.tpt, t.NB, xq, sfb, cnt, ncnt));
+    }
+    CUtensorMap tb;
+    int r = mx_encode_kmajor(&tb, xq, false, (uint64_t)K, (uint64_t)t.tiles_n * t.NB, (uint64_t)K, (uint32_t)t.NB);
+    if (r) return r;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
+    r = dense_dispatch(t, tb, p, sms, st);
+    if (r) return r;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
+    return DSV4CU_OK;
+}
+
+static int dense_dispatch(const MxTiling &t, const CUtensorMap &tb, const DenseMx::Params &p, int sms, cudaStream_t st)
+{
     switch (t.NB * 8 + t.KB) {
     case 8 * 8 + 1: return dense_launch<8, 1>(tb, p, sms, st);
     case 8 * 8 + 2: return dense_launch<8, 2>(tb, p, sms, st);
@@ -343,7 +468,7 @@ extern "C" void dsv4cu_mat_destroy(dsv4cu_mat *h)
 
 extern "C" size_t dsv4cu_mat_workspace(const dsv4cu_mat *h, int nt, int terms)
 {
-    return h ? mx_workspace(&h->m, nt, terms) : 0;
+    return h ? mx_workspace(&h->m, nt, terms, mx_device_sms()) : 0;
 }
 
 extern "C" int dsv4cu_mat_gemm_cfg(dsv4cu_ctx *ctx, const dsv4cu_mat *h, float *y, const float *x, int nt, int terms,
@@ -353,7 +478,7 @@ extern "C" int dsv4cu_mat_gemm_cfg(dsv4cu_ctx *ctx, const dsv4cu_mat *h, float *
     if (nt < 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "mat_gemm: nt < 0");
     if (nt == 0) return DSV4CU_OK;
     void *ws = nullptr;
-    int r = dsv4cu_ws_get(ctx, mx_workspace(&h->m, nt, terms), &ws);
+    int r = dsv4cu_ws_get(ctx, mx_workspace(&h->m, nt, terms, ctx->sm_count), &ws);
     if (r) return r;
     return mx_gemm(&h->m, y, x, nt, terms, nb, kb, ws, ctx->sm_count, ctx->status, (cudaStream_t)stream);
 }
@@ -362,4 +487,17 @@ extern "C" int dsv4cu_mat_gemm(dsv4cu_ctx *ctx, const dsv4cu_mat *h, float *y, c
                                void *stream)
 {
     return dsv4cu_mat_gemm_cfg(ctx, h, y, x, nt, terms, 0, 0, stream);
+}
+
+extern "C" int dsv4cu_mat_gemm_ev(dsv4cu_ctx *ctx, const dsv4cu_mat *h, float *y, const float *x, int nt, int terms,
+                                  void *stream, void **events)
+{
+    if (!ctx || !h || !y || !x || !events) return dsv4cu_set_error(DSV4CU_ERR_ARG, "mat_gemm_ev: NULL argument");
+    if (nt < 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "mat_gemm_ev: nt < 0");
+    if (nt == 0) return DSV4CU_OK;
+    void *ws = nullptr;
+    int r = dsv4cu_ws_get(ctx, mx_workspace(&h->m, nt, terms, ctx->sm_count), &ws);
+    if (r) return r;
+    return mx_gemm(&h->m, y, x, nt, terms, 0, 0, ws, ctx->sm_count, ctx->status, (cudaStream_t)stream,
+                   (cudaEvent_t *)events);
 }

@@ -41,8 +41,13 @@ void mx_release(MxMat *m);
 int mx_encode_kmajor(CUtensorMap *map, const void *base, bool fp4, uint64_t inner, uint64_t outer,
                      uint64_t row_bytes, uint32_t box_rows);
 MxTiling mx_tiling(int nt, int terms, int nb_req, int kb_req, int kc);
-size_t mx_workspace(const MxMat *m, int nt, int terms);
+// Split-K segments of one dense product: at most MX_MAX_SEGMENTS.
+constexpr int MX_MAX_SEGMENTS = 16;
+int mx_device_sms();
+size_t mx_workspace(const MxMat *m, int nt, int terms, int sms);
+// ev (optional): three events recorded before the activation split, before
+// the GEMM and after it.
 int mx_gemm(const MxMat *m, float *y, const float *x, int nt, int terms, int nb_req, int kb_req, void *ws, int sms,
-            int *err, cudaStream_t st);
+            int *err, cudaStream_t st, cudaEvent_t *ev = nullptr);
 
 }  // namespace dsv4cu

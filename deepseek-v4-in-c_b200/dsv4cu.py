@@ -76,6 +76,7 @@ def lib() -> C.CDLL:
             "dsv4cu_mat_workspace": (sz, [vp, i, i]),
             "dsv4cu_mat_gemm": (i, [vp, vp, vp, vp, i, i, vp]),
             "dsv4cu_mat_gemm_cfg": (i, [vp, vp, vp, vp, i, i, i, i, vp]),
+            "dsv4cu_mat_gemm_ev": (i, [vp, vp, vp, vp, i, i, vp, vp]),
             "dsv4cu_indexer_score": (i, [vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_indexer_score_fp8": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]),
             "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
@@ -123,6 +124,16 @@ def last_error() -> str:
 def check(rc: int, what: str = "dsv4cu") -> None:
     if rc != 0:
         raise DSV4CUError(f"{what}: status {rc}: {last_error()}")
+
+
+def _event_handles(events):
+    """cudaEvent_t handles of torch.cuda.Event objects; torch creates the
+    driver event on first record, so an unrecorded event is recorded once
+    on the current stream first."""
+    for e in events:
+        if not e.cuda_event:
+            e.record()
+    return (C.c_void_p * len(events))(*[e.cuda_event for e in events])
 
 
 def _p(a):
@@ -279,8 +290,12 @@ class Device:
     def mat_destroy(self, h):
         self.L.dsv4cu_mat_destroy(h)
 
-    def mat_gemm(self, h, y, x, nt: int, terms: int = 3, nb: int = 0, kb: int = 0):
-        if nb or kb:
+    def mat_gemm(self, h, y, x, nt: int, terms: int = 3, nb: int = 0, kb: int = 0, events=None):
+        if events is not None:
+            evp = _event_handles(events)
+            check(self.L.dsv4cu_mat_gemm_ev(self.ctx, h, self.ptr(y), self.ptr(x), nt, terms, self.stream(), evp),
+                  "dsv4cu_mat_gemm_ev")
+        elif nb or kb:
             check(self.L.dsv4cu_mat_gemm_cfg(self.ctx, h, self.ptr(y), self.ptr(x), nt, terms, nb, kb,
                                              self.stream()), "dsv4cu_mat_gemm_cfg")
         else:
@@ -315,7 +330,7 @@ class Device:
         if events is None:
             check(self.L.dsv4cu_moe_prefill(*args), "dsv4cu_moe_prefill")
         else:
-            evp = (C.c_void_p * 4)(*[e.cuda_event for e in events])
+            evp = _event_handles(events)
             check(self.L.dsv4cu_moe_prefill_ev(*args, evp), "dsv4cu_moe_prefill_ev")
 
     def moe_decode(self, layer, out, x, logits, topk, route_scale, limit, nt, idx_out=None, wts_out=None,
@@ -327,7 +342,7 @@ class Device:
         if events is None:
             check(self.L.dsv4cu_moe_decode(*args), "dsv4cu_moe_decode")
         else:
-            evp = (C.c_void_p * 4)(*[e.cuda_event for e in events])
+            evp = _event_handles(events)
             check(self.L.dsv4cu_moe_decode_ev(*args, evp), "dsv4cu_moe_decode_ev")
 
     def indexer_score(self, out, q, kv, w, n_heads, head_dim, n_pos):

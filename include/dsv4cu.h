@@ -118,6 +118,12 @@ int dsv4cu_mat_gemm(dsv4cu_ctx *ctx, const dsv4cu_mat *m, float *y, const float 
 int dsv4cu_mat_gemm_cfg(dsv4cu_ctx *ctx, const dsv4cu_mat *m, float *y, const float *x,
                         int nt, int terms, int nb, int kb, void *stream);
 
+/* dsv4cu_mat_gemm that also records events[0..2] (cudaEvent_t, created by the
+ * caller) on the stream: before the activation split, before the GEMM and
+ * after it. For timing the GEMM kernel alone. */
+int dsv4cu_mat_gemm_ev(dsv4cu_ctx *ctx, const dsv4cu_mat *m, float *y, const float *x,
+                       int nt, int terms, void *stream, void **events);
+
 /* Router for nt tokens; replaces dsv4_route (src/10_compute/dsv4_kernels.h:24).
  * logits [nt][n_experts] (read), scores/orig [nt][n_experts] (written: biased
  * selection scores and sqrt(softplus) scores, either may be NULL), idx/wts

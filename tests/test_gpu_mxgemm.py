@@ -114,3 +114,59 @@ def test_mx_tile_configs(dev, orc, cfg):
         dev.mat_destroy(h)
     want = orc.mmq(x, oracle.qmat(W, S, 3, rows, cols, 1, 32))
     assert rel_err(got, want) <= 1e-4
+
+
+@pytest.mark.parametrize("rows,cols,nt", [(7168, 7168, 1), (1536, 7168, 2), (640, 2560, 1), (7168, 7168, 3)],
+                         ids=["config1", "even", "one-stage", "config1-nt3"])
+def test_mx_split_k(dev, orc, rows, cols, nt):
+    """Few row tiles: K is split into segments (lengths differing by one
+    stage at most) whose partial products are summed in a fixed order; the
+    result is within the terms = 4 bar and identical on a second call."""
+    import oracle
+    t = __import__("torch")
+    W, S, Wd, Sd, q = _upload_qmat(dev, 2, rows, cols, 21)
+    x = pack.bf16_round(np.random.default_rng(22).standard_normal((nt, cols)).astype(np.float32))
+    h = dev.mat_create(q)
+    try:
+        xd = t.from_numpy(x).cuda()
+        y1 = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+        y2 = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+        dev.mat_gemm(h, y1, xd, nt, 4)
+        evs = [t.cuda.Event(enable_timing=True) for _ in range(3)]
+        dev.mat_gemm(h, y2, xd, nt, 4, events=evs)
+        t.cuda.synchronize()
+        got, again = y1.cpu().numpy(), y2.cpu().numpy()
+    finally:
+        dev.mat_destroy(h)
+    want = orc.mmq(x, oracle.qmat(W, S, 2, rows, cols, 128, 128))
+    e = rel_err(got, want)
+    print(f"split-k {rows}x{cols} nt={nt} max-rel={e:.3e}")
+    assert e <= 1e-4, e
+    assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+
+
+@pytest.mark.parametrize("nt", [8, 130])
+def test_mx_split_k_batch_invariant(dev, nt):
+    """The K segmentation depends on the matrix only: a token's row of a
+    batched product is the same bits as its one-token product, whether the
+    batch runs its segments on separate CTAs (nt = 8) or inside one CTA per
+    tile (nt = 130)."""
+    t = __import__("torch")
+    W, S, Wd, Sd, q = _upload_qmat(dev, 2, 7168, 7168, 23)
+    x = np.random.default_rng(24).standard_normal((nt, 7168)).astype(np.float32)
+    h = dev.mat_create(q)
+    try:
+        xd = t.from_numpy(x).cuda()
+        yb = t.empty((nt, 7168), dtype=t.float32, device="cuda")
+        dev.mat_gemm(h, yb, xd, nt, 4)
+        singles = []
+        for tok in (0, 3, nt - 1):
+            y1 = t.empty((1, 7168), dtype=t.float32, device="cuda")
+            dev.mat_gemm(h, y1, xd[tok:tok + 1], 1, 4)
+            singles.append(y1)
+        t.cuda.synchronize()
+        got = yb.cpu().numpy()
+    finally:
+        dev.mat_destroy(h)
+    for tok, y1 in zip((0, 3, nt - 1), singles):
+        assert np.array_equal(got[tok].view(np.uint32), y1.cpu().numpy()[0].view(np.uint32)), tok
