@@ -1,7 +1,7 @@
 """Benchmark of the hot path. Default: the FP4 MoE layer decode step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|prefill|gemv]
+                    [--workload decode|prefill|gemv|indexer]
 
 decode (config 2, the headline). One step = one MoE layer decode for one
 token per GPU: router over 256 bf16-valued logits -> top-8 of 256
@@ -13,6 +13,8 @@ decoder's layers do, so each step streams its ~132 MB of expert weights from
 HBM.
 prefill (config 3): 4096 tokens through the MoE layer + the FP8 QKV projection.
 gemv (config 1): FP8 7168x7168 GEMV, four matrices in turn, back to back.
+indexer (config 4): FP8 indexer score over 32768 keys, top-2048, sparse
+         attention (64 heads x 576) over the picks; four contexts in turn.
 
 value  = the workload's metric over all ranks, device time (CUDA events, max
          over ranks).
@@ -63,9 +65,10 @@ def parse():
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts resident in HBM (256 = config 2; smaller only for ncu captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["decode", "prefill", "gemv"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "indexer"], default="decode",
                     help="decode = config 2 (the headline); prefill = config 3 (MoE layer over 4096 tokens + "
-                         "FP8 QKV projection); gemv = config 1 (FP8 7168x7168 GEMV, HBM GB/s)")
+                         "FP8 QKV projection); gemv = config 1 (FP8 7168x7168 GEMV, HBM GB/s); indexer = "
+                         "config 4 (FP8 indexer score + top-2048 + sparse attention)")
     return ap.parse_args()
 
 
@@ -904,11 +907,264 @@ def run_gemv_reference(args, rank, world):
                                        f"{cores} threads, {G1_CPU_SETS} distinct host matrices in turn"},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
+# --------------------------------------------------- config 4: sparse-attention indexer
+I4_N, I4_H, I4_D, I4_TOPK = 32768, 64, 128, 2048       # keys, indexer heads, indexer dim, picks
+I4_AH, I4_AD = 64, 576                                   # attention heads, latent 512 + rope 64
+I4_CTX = 4                                               # independent contexts used in turn (> L2)
+I4_METRIC = "sparse-attention decode steps/s (FP8 indexer score over 32768 keys + top-2048 + attention)"
+I4_WORKLOAD = ("config4: indexer q 64 heads x 128 and 32768 keys, e4m3 with one power-of-two fp32 scale per row "
+               "(from N(0,1)), ReLU-weighted head sum, top-2048 (ties to the lower index), then attention with "
+               "per-head sinks of 64 heads x 576 (bf16 KV, N(0,1)) over the 2048 picked entries")
+I4_SCORE_BYTES = I4_N * (I4_D + 4) + I4_H * (I4_D + 8) + I4_N * 4          # keys + scales, q, w, scores out
+I4_TOPK_BYTES = I4_N * 4 + I4_TOPK * 4
+I4_ATTN_BYTES = I4_TOPK * (I4_AD * 2 + 4) + I4_AH * (I4_AD * 8 + 4)        # picked bf16 rows + idx, q/o, sinks
+
+
+def i4_quant_rows(a):
+    """e4m3 codes with one power-of-two fp32 scale per row."""
+    sys.path.insert(0, PKG)
+    import pack
+    amax = np.abs(a).max(axis=1)
+    f, E = np.frexp(amax)
+    e = E - 9 + (f > 0.875)
+    sc = np.ldexp(np.ones_like(amax), e).astype(np.float32)
+    v = np.ldexp(a, -e[:, None]).astype(np.float32)
+    codes = pack._rne_grid(v, pack._E4M3_POS).astype(np.uint8)
+    codes = np.where(np.signbit(v), codes | 0x80, codes).astype(np.uint8)
+    return codes, sc
+
+
+def i4_contexts(n_ctx, seed):
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n_ctx):
+        k8, ks = i4_quant_rows(rng.standard_normal((I4_N, I4_D)).astype(np.float32))
+        out.append((k8, ks))
+    return out
+
+
+def i4_queries(n, seed):
+    sys.path.insert(0, PKG)
+    import pack
+    rng = np.random.default_rng(seed)
+    q8, qs = zip(*[i4_quant_rows(rng.standard_normal((I4_H, I4_D)).astype(np.float32)) for _ in range(n)])
+    w = rng.standard_normal((n, I4_H)).astype(np.float32)
+    qa = pack.bf16_round(rng.standard_normal((n, I4_AH, I4_AD)).astype(np.float32))
+    sink = rng.standard_normal(I4_AH).astype(np.float32)
+    return np.stack(q8), np.stack(qs), w, qa, sink
+
+
+def run_indexer(args, rank, local_rank, world):
+    import torch
+    import dsv4cu
+    torch.cuda.set_device(local_rank)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        pg = tdist
+    dev = dsv4cu.Device(local_rank)
+    ctx = []
+    for j, (k8, ks) in enumerate(i4_contexts(I4_CTX, 50 + rank)):
+        kv = torch.empty(I4_N * I4_AD, dtype=torch.float32, device="cuda")
+        dev.fill_normal(kv, 600 + j, 0.0, 1.0)
+        ctx.append((torch.from_numpy(k8).cuda(), torch.from_numpy(ks).cuda(),
+                    kv.view(I4_N, I4_AD).to(torch.bfloat16)))
+        del kv
+    n_steps = args.warmup + args.steps
+    q8, qs, w, qa, sink = i4_queries(n_steps, 70 + rank)
+    dq8, dqs, dw, dqa = (torch.from_numpy(a).cuda() for a in (q8, qs, w, qa))
+    dsink = torch.from_numpy(sink).cuda()
+    scores = torch.empty(I4_N, dtype=torch.float32, device="cuda")
+    idx = torch.empty(I4_TOPK, dtype=torch.int32, device="cuda")
+    o = torch.empty((n_steps, I4_AH, I4_AD), dtype=torch.float32, device="cuda")
+    scale = float(1.0 / np.sqrt(I4_AD))
+
+    def step(i, ev=None, src=None):
+        k8, ks, kv = ctx[i % I4_CTX]
+        a8, as_, aw, aq, oo = src if src is not None else (dq8[i], dqs[i], dw[i], dqa[i], o[i])
+        if ev:
+            ev[0].record()
+        dev.indexer_score_fp8(scores, a8, as_, k8, ks, aw, I4_H, I4_D, I4_N, I4_D)
+        if ev:
+            ev[1].record()
+        dev.topk(idx, scores, I4_N, I4_TOPK)
+        if ev:
+            ev[2].record()
+        dev.sparse_attn(oo, aq, kv, 1, dsink, idx, I4_AH, I4_AD, I4_TOPK, scale)
+        if ev:
+            ev[3].record()
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local_rank)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    t0.record()
+    h0 = time.perf_counter()
+    for k in range(args.steps):
+        step(args.warmup + k)
+    host_ms = (time.perf_counter() - h0) * 1e3
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = t0.elapsed_time(t1)
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    total_ms = t.item()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for k in range(args.steps):
+        step(args.warmup + k, evs[k])
+    torch.cuda.synchronize()
+    ph = np.array([[e[i].elapsed_time(e[i + 1]) for i in range(3)] for e in evs]).mean(axis=0)
+    # e2e: query side from pinned host buffers, the step's output back to the host
+    hq8, hqs, hw, hqa = (torch.from_numpy(a).pin_memory() for a in (q8, qs, w, qa))
+    ho = torch.empty((n_steps, I4_AH, I4_AD), dtype=torch.float32).pin_memory()
+    g8, gs, gw, gq = (torch.empty_like(a[0]) for a in (dq8, dqs, dw, dqa))
+    go = torch.empty_like(o[0])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for k in range(args.steps):
+        i = args.warmup + k
+        for dst, srch in ((g8, hq8), (gs, hqs), (gw, hw), (gq, hqa)):
+            dst.copy_(srch[i], non_blocking=True)
+        step(i, src=(g8, gs, gw, gq, go))
+        ho[i].copy_(go, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    e2e_ms = t.item()
+    dev.check_status()
+    peak, peak_kind = load_peaks()
+    names = ["indexer_score_fp8", "topk", "sparse_attn"]
+    nbytes = [I4_SCORE_BYTES, I4_TOPK_BYTES, I4_ATTN_BYTES]
+    top = int(np.argmax(ph))
+    achieved = nbytes[top] / (ph[top] * 1e-3) / 1e9
+    ms = total_ms / args.steps
+    res = {
+        "metric": I4_METRIC, "value": round(world * 1e3 / ms, 1), "unit": "steps/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 indexer q/k -> f64 exact head sums; bf16 KV x f32 attention",
+        "data": "synthetic: keys/queries N(0,1) quantized per row, KV N(0,1) bf16, seeded",
+        "config": {"workload": I4_WORKLOAD, "global_batch": world, "parallelism": f"replicas x{world}",
+                   "l2": f"inputs larger than L2: {I4_CTX} independent contexts (4.3 MB keys + 37.7 MB KV each) "
+                         "used in turn, steps back to back",
+                   "host_enqueue_ms_per_step": round(host_ms / args.steps, 5)},
+        "roofline": {"bound": "hbm", "kernel": names[top], "achieved": round(achieved, 1), "peak": peak,
+                     "peak_source": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "algorithmic_bytes": nbytes[top],
+                     "kernel_ms": {n: round(v, 5) for n, v in zip(names, ph)},
+                     "kernel_gbs": {n: round(b / (v * 1e-3) / 1e9, 1) for n, b, v in zip(names, nbytes, ph)}},
+        "e2e": {"value": round(world * args.steps / (e2e_ms * 1e-3), 1), "unit": "steps/s",
+                "h2d_bytes_per_step": int(q8[0].nbytes + qs[0].nbytes + w[0].nbytes + qa[0].nbytes),
+                "d2h_bytes_per_step": int(go.numel() * 4),
+                "api": "dsv4cu_indexer_score_fp8 + dsv4cu_topk + dsv4cu_sparse_attn (include/dsv4cu.h)"},
+        "gpu_launches": 5 * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_indexer_baseline(args.cpu_seconds)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    dev.close()
+    return res if rank == 0 else None
+
+
+def cpu_indexer_setup():
+    sys.path.insert(0, ORACLE)
+    sys.path.insert(0, PKG)
+    os.environ.setdefault("OMP_NUM_THREADS", str(cpu_threads()))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    import oracle
+    import pack
+    if not oracle.RefLib.available():
+        return None
+    k8, ks = i4_contexts(1, 50)[0]
+    kf = (pack.E4M3[k8] * ks[:, None]).astype(np.float32)
+    rng = np.random.default_rng(601)
+    kv = pack.bf16_round(rng.standard_normal((I4_N, I4_AD)).astype(np.float32))
+    # The reference's dsv4_topk stops at k = 1024 (DSV4_TOPK_MAX,
+    # src/10_compute/dsv4_topk.c:79-84); config 4 picks 2048, so the CPU legs
+    # take the top-k from the restatement (oracle/dsv4_oracle.c, same heap rule).
+    return (oracle.RefLib(), oracle.Oracle()), kf, kv
+
+
+def cpu_indexer_step(ref, kf, kv, q8, qs, w, qa, sink):
+    sys.path.insert(0, PKG)
+    import pack
+    ref, port = ref
+    qf = (pack.E4M3[q8] * qs[:, None]).astype(np.float32)
+    sc = ref.indexer_score(qf, kf, w)
+    idx = port.topk(sc, I4_TOPK)
+    return ref.sparse_attn(qa, kv, sink, idx, np.float32(1.0 / np.sqrt(I4_AD)))
+
+
+def cpu_indexer_baseline(seconds):
+    st = cpu_indexer_setup()
+    if st is None:
+        return {"value": None, "unit": "steps/s", "cores": 0, "kind": "port", "sample": "oracle/_ref not built"}
+    ref, kf, kv = st
+    q8, qs, w, qa, sink = i4_queries(16, 71)
+    cpu_indexer_step(ref, kf, kv, q8[0], qs[0], w[0], qa[0], sink)
+    n, t0 = 0, time.perf_counter()
+    while n < 16 and (time.perf_counter() - t0 < seconds or n < 3):
+        cpu_indexer_step(ref, kf, kv, q8[n], qs[n], w[n], qa[n], sink)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "steps/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
+            "kind": "reference", "sample": f"{n} steps of the reference's dsv4_indexer_score + dsv4_sparse_attn and "
+                                           f"the restatement's top-2048 (the reference caps k at 1024) on config 4 "
+                                           f"({dt:.2f} s)"}
+
+
+def run_indexer_reference(args, rank, world):
+    if rank != 0:
+        return None
+    st = cpu_indexer_setup()
+    if st is None:
+        return {"impl": "reference", "unavailable": "oracle/_ref/libdsv4ref.so was not built"}
+    ref, kf, kv = st
+    n = args.warmup + args.steps
+    q8, qs, w, qa, sink = i4_queries(n, 2000)
+    for i in range(args.warmup):
+        cpu_indexer_step(ref, kf, kv, q8[i], qs[i], w[i], qa[i], sink)
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        i = args.warmup + k
+        cpu_indexer_step(ref, kf, kv, q8[i], qs[i], w[i], qa[i], sink)
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    return {"impl": "reference", "metric": I4_METRIC, "value": round(v, 3), "unit": "steps/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 indexer (dequantized e4m3) + f32 attention", "data": "synthetic, seeded",
+            "config": {"workload": I4_WORKLOAD, "global_batch": 1, "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(v, 3), "unit": "steps/s", "cores": cores, "kind": "reference",
+                             "sample": f"{args.steps} steps of dsv4_indexer_score + dsv4_sparse_attn (src/10_compute) "
+                                       f"and the restatement's top-2048 (dsv4_topk caps k at 1024), {cores} threads"},
+            "e2e": {"value": round(v, 3), "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
 
 def main():
     args = parse()
     rank, local_rank, world = dist_env()
-    if args.workload == "gemv":
+    if args.workload == "indexer":
+        res = (run_indexer_reference(args, rank, world) if args.impl == "reference"
+               else run_indexer(args, rank, local_rank, world))
+    elif args.workload == "gemv":
         res = (run_gemv_reference(args, rank, world) if args.impl == "reference"
                else run_gemv(args, rank, local_rank, world))
     elif args.workload == "prefill":

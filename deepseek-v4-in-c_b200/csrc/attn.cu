@@ -31,7 +31,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
     int topk, float scale, float *__restrict__ pm, float *__restrict__ pl, float *__restrict__ po)
 {
     extern __shared__ float smem[];
-    const int DP = D + 4;                      // padded row stride (floats)
+    const int DP = D + 8;                      // padded row stride (floats): rows 4 lanes apart miss each other's banks
     float *kvs = smem;                         // [CH][DP]
     float *qs = kvs + ATT_CH * DP;             // [HG][D]
     float *ss = qs + ATT_HG * D;               // [HG][CH] scores, then weights
@@ -68,21 +68,37 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
     }
     __syncthreads();
 
-    // Scores: thread (hh, jj) -> rows jj and jj + 16 of head hh.
+    // Scores: warp w -> heads 2w, 2w + 1; lane -> rows rp, rp + 16 (rp = lane / 2)
+    // over the 4-column groups of parity lane & 1; lane pairs add their halves.
     {
-        const int hh = tid >> 4, jj = tid & 15;
-        if (hh < nh) {
-            const float *qh = qs + hh * D, *k0 = kvs + jj * DP, *k1 = kvs + (jj + 16) * DP;
-            float a0 = 0.f, a1 = 0.f;
-            for (int c = 0; c < D; c += 4) {
-                const float4 qv = *reinterpret_cast<const float4 *>(qh + c);
+        const int hp = tid >> 5, lane = tid & 31, rp = lane >> 1, ds = lane & 1;
+        const int ha = 2 * hp, hb = 2 * hp + 1;
+        if (ha < nh) {
+            const float *qa = qs + ha * D, *qb = qs + (hb < nh ? hb : ha) * D;
+            const float *k0 = kvs + rp * DP, *k1 = kvs + (rp + 16) * DP;
+            float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
+            for (int c = 4 * ds; c < D; c += 8) {
+                const float4 x = *reinterpret_cast<const float4 *>(qa + c);
+                const float4 y = *reinterpret_cast<const float4 *>(qb + c);
                 const float4 v0 = *reinterpret_cast<const float4 *>(k0 + c);
                 const float4 v1 = *reinterpret_cast<const float4 *>(k1 + c);
-                a0 = fmaf(qv.x, v0.x, fmaf(qv.y, v0.y, fmaf(qv.z, v0.z, fmaf(qv.w, v0.w, a0))));
-                a1 = fmaf(qv.x, v1.x, fmaf(qv.y, v1.y, fmaf(qv.z, v1.z, fmaf(qv.w, v1.w, a1))));
+                a00 = fmaf(x.x, v0.x, fmaf(x.y, v0.y, fmaf(x.z, v0.z, fmaf(x.w, v0.w, a00))));
+                a01 = fmaf(x.x, v1.x, fmaf(x.y, v1.y, fmaf(x.z, v1.z, fmaf(x.w, v1.w, a01))));
+                a10 = fmaf(y.x, v0.x, fmaf(y.y, v0.y, fmaf(y.z, v0.z, fmaf(y.w, v0.w, a10))));
+                a11 = fmaf(y.x, v1.x, fmaf(y.y, v1.y, fmaf(y.z, v1.z, fmaf(y.w, v1.w, a11))));
             }
-            ss[hh * ATT_CH + jj] = a0 * scale;
-            ss[hh * ATT_CH + jj + 16] = a1 * scale;
+            a00 += __shfl_xor_sync(0xFFFFFFFFu, a00, 1);
+            a01 += __shfl_xor_sync(0xFFFFFFFFu, a01, 1);
+            a10 += __shfl_xor_sync(0xFFFFFFFFu, a10, 1);
+            a11 += __shfl_xor_sync(0xFFFFFFFFu, a11, 1);
+            if (ds == 0) {
+                ss[ha * ATT_CH + rp] = a00 * scale;
+                ss[ha * ATT_CH + rp + 16] = a01 * scale;
+                if (hb < nh) {
+                    ss[hb * ATT_CH + rp] = a10 * scale;
+                    ss[hb * ATT_CH + rp + 16] = a11 * scale;
+                }
+            }
         }
     }
     __syncthreads();
@@ -105,51 +121,99 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
         }
     }
     __syncthreads();
-    // Unnormalised chunk output: thread -> head tid/16, columns 4*(tid%16) + 64*i.
+    // Unnormalised chunk output: warp w -> heads 2w, 2w + 1; lane -> 4-column
+    // groups lane, lane + 32, ...
     {
-        const int hh = tid >> 4, cg = (tid & 15) * 4;
-        if (hh < nh) {
-            float *dst = po + ((size_t)chunk * H + h0 + hh) * D;
-            for (int c = cg; c < D; c += 64) {
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        const int hp = tid >> 5, lane = tid & 31;
+        const int ha = 2 * hp, hb = 2 * hp + 1;
+        if (ha < nh) {
+            const float *wa = ss + ha * ATT_CH, *wb = ss + (hb < nh ? hb : ha) * ATT_CH;
+            float *da = po + ((size_t)chunk * H + h0 + ha) * D, *db = po + ((size_t)chunk * H + h0 + hb) * D;
+            for (int c = 4 * lane; c < D; c += 128) {
+                float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
                 for (int j = 0; j < ATT_CH; j++) {
-                    const float w = ss[hh * ATT_CH + j];
+                    const float u = wa[j], w = wb[j];
                     const float4 v = *reinterpret_cast<const float4 *>(kvs + j * DP + c);
-                    acc.x = fmaf(w, v.x, acc.x);
-                    acc.y = fmaf(w, v.y, acc.y);
-                    acc.z = fmaf(w, v.z, acc.z);
-                    acc.w = fmaf(w, v.w, acc.w);
+                    x.x = fmaf(u, v.x, x.x);
+                    x.y = fmaf(u, v.y, x.y);
+                    x.z = fmaf(u, v.z, x.z);
+                    x.w = fmaf(u, v.w, x.w);
+                    y.x = fmaf(w, v.x, y.x);
+                    y.y = fmaf(w, v.y, y.y);
+                    y.z = fmaf(w, v.z, y.z);
+                    y.w = fmaf(w, v.w, y.w);
                 }
-                *reinterpret_cast<float4 *>(dst + c) = acc;
+                *reinterpret_cast<float4 *>(da + c) = x;
+                if (hb < nh) *reinterpret_cast<float4 *>(db + c) = y;
             }
         }
     }
 }
 
-__global__ void attn_combine_kernel(const float *__restrict__ pm, const float *__restrict__ pl,
-                                    const float *__restrict__ po, const float *__restrict__ sink, int H, int D,
-                                    int nchunks, float *__restrict__ o)
+// Block (h, column slice): the head's chunk factors f_c = exp(m_c - m) and the
+// denominator are formed once in shared memory (denominator summed in chunk
+// order, in double), then each thread combines its columns in chunk order.
+constexpr int ATT_COMB_COLS = 128;
+constexpr int ATT_MAX_CHUNKS = 1024;
+
+__global__ void __launch_bounds__(ATT_COMB_COLS) attn_combine_kernel(
+    const float *__restrict__ pm, const float *__restrict__ pl, const float *__restrict__ po,
+    const float *__restrict__ sink, int H, int D, int nchunks, float *__restrict__ o)
 {
-    const int h = blockIdx.x;
+    __shared__ float fac[ATT_MAX_CHUNKS], lsum[ATT_MAX_CHUNKS];
+    __shared__ float s_m, s_inv;
+    __shared__ float red[ATT_COMB_COLS / 32];
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     float m = -INFINITY;
-    for (int c = 0; c < nchunks; c++) m = fmaxf(m, pm[(size_t)c * H + h]);
-    double denom = 0.0;
-    for (int c = 0; c < nchunks; c++) {
+    for (int c = tid; c < nchunks; c += blockDim.x) {
         const float mc = pm[(size_t)c * H + h];
-        if (mc != -INFINITY) denom += (double)pl[(size_t)c * H + h] * (double)expf(mc - m);
+        fac[c] = mc;
+        lsum[c] = pl[(size_t)c * H + h];
+        m = fmaxf(m, mc);
     }
-    denom += (double)expf(sink[h] - m);
-    const float inv = (float)(1.0 / denom);
-    for (int col = threadIdx.x; col < D; col += blockDim.x) {
-        float acc = 0.0f;
-        for (int c = 0; c < nchunks; c++) {
-            const float mc = pm[(size_t)c * H + h];
-            if (mc == -INFINITY) continue;
-            acc = fmaf(po[((size_t)c * H + h) * D + col], expf(mc - m), acc);
-        }
-        o[(size_t)h * D + col] = acc * inv;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (tid == 0) {
+        float mm = red[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) mm = fmaxf(mm, red[w]);
+        s_m = mm;
     }
+    __syncthreads();
+    m = s_m;
+    // f_c = 0 marks a chunk without a valid row (its max is -inf).
+    for (int c = tid; c < nchunks; c += blockDim.x) {
+        const float mc = fac[c];
+        fac[c] = (mc != -INFINITY) ? expf(mc - m) : 0.0f;
+    }
+    __syncthreads();
+    // A chunk without a valid row has l = 0 and an all-zero output, so it
+    // adds exactly nothing below.
+    if (tid == 0) {
+        double denom = 0.0;
+        for (int c = 0; c < nchunks; c++) denom += (double)lsum[c] * (double)fac[c];
+        denom += (double)expf(sink[h] - m);
+        s_inv = (float)(1.0 / denom);
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    const int col = blockIdx.y * ATT_COMB_COLS + tid;
+    if (col >= D) return;
+    float acc = 0.0f;
+    const float *src = po + (size_t)h * D + col;
+    const size_t cstride = (size_t)H * D;
+    int c = 0;
+    for (; c + 16 <= nchunks; c += 16) {       // 16 loads in flight, then the fma in chunk order
+        float v[16];
+#pragma unroll
+        for (int u = 0; u < 16; u++) v[u] = __ldg(src + (size_t)(c + u) * cstride);
+#pragma unroll
+        for (int u = 0; u < 16; u++) acc = fmaf(v[u], fac[c + u], acc);
+    }
+    for (; c < nchunks; c++) acc = fmaf(__ldg(src + (size_t)c * cstride), fac[c], acc);
+    o[(size_t)h * D + col] = acc * inv;
 }
 
 size_t attn_workspace(int H, int D, int topk)
@@ -168,18 +232,22 @@ int attn_run(float *o, const float *q, const void *kv, int kv_bf16, const float 
     float *pl = (float *)p;
     p += dsv4cu_align256((size_t)nch * H * 4);
     float *po = (float *)p;
-    const size_t smem = ((size_t)ATT_CH * (D + 4) + (size_t)ATT_HG * D + ATT_HG * ATT_CH) * sizeof(float);
+    const size_t smem = ((size_t)ATT_CH * (D + 8) + (size_t)ATT_HG * D + ATT_HG * ATT_CH) * sizeof(float);
     if (smem > 220 * 1024) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "sparse_attn: head dim %d too large", D);
+    if (nch > ATT_MAX_CHUNKS)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "sparse_attn: topk %d > %d", topk, ATT_MAX_CHUNKS * ATT_CH);
     dim3 grid(nch, (H + ATT_HG - 1) / ATT_HG);
+    static SmemLimit lim_bf16, lim_f32;
     if (kv_bf16) {
-        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        DSV4CU_CUDA_TRY(smem_limit(lim_bf16, (const void *)attn_chunk_kernel<true>, (int)smem));
         attn_chunk_kernel<true><<<grid, ATT_THREADS, smem, st>>>(q, kv, idxs, H, D, topk, scale, pm, pl, po);
     } else {
-        DSV4CU_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        DSV4CU_CUDA_TRY(smem_limit(lim_f32, (const void *)attn_chunk_kernel<false>, (int)smem));
         attn_chunk_kernel<false><<<grid, ATT_THREADS, smem, st>>>(q, kv, idxs, H, D, topk, scale, pm, pl, po);
     }
     DSV4CU_LAUNCH_CHECK();
-    attn_combine_kernel<<<H, 256, 0, st>>>(pm, pl, po, sink, H, D, nch, o);
+    attn_combine_kernel<<<dim3(H, (D + ATT_COMB_COLS - 1) / ATT_COMB_COLS), ATT_COMB_COLS, 0, st>>>(
+        pm, pl, po, sink, H, D, nch, o);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
 }

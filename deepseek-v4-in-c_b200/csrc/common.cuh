@@ -163,6 +163,37 @@ namespace dsv4cu {
 DSV4CU_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 DSV4CU_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// Host-side per-device caches, so a call costs no attribute queries after
+// the first: SmemLimit (one per call site) remembers the largest dynamic
+// shared-memory limit set for a kernel on each device; device_sms() the SM
+// count of the current device.
+struct SmemLimit {
+    int set[64];
+};
+static inline cudaError_t smem_limit(SmemLimit &c, const void *kernel, int bytes)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const bool cache = dev >= 0 && dev < 64;
+    if (cache && c.set[dev] >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && cache) c.set[dev] = bytes;
+    return e;
+}
+static inline int device_sms()
+{
+    static int n[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!n[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        n[dev] = v > 0 ? v : 148;
+    }
+    return n[dev];
+}
+
 template <typename... KArgs, typename... Args>
 static inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                                      Args &&...args)

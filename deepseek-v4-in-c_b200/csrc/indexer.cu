@@ -23,12 +23,19 @@ namespace dsv4cu {
 constexpr int IDX_MAX_D = 256;       // head_dim bound (chains of <= 16 elements)
 constexpr int IDX_WARPS = 16;
 
+// load(t, i) = key element i of position t as a double; raw / rscale / val
+// split it into the global loads and the conversion, so loads can run ahead.
 struct KeysF32 {
+    using Raw = float;
     const float *kv;
     int ld;
     DSV4CU_DEV double load(int t, int i) const { return (double)__ldg(kv + (size_t)t * ld + i); }
+    DSV4CU_DEV Raw raw(int t, int i) const { return __ldg(kv + (size_t)t * ld + i); }
+    DSV4CU_DEV float rscale(int) const { return 1.0f; }
+    DSV4CU_DEV double val(Raw r, float) const { return (double)r; }
 };
 struct KeysFP8 {
+    using Raw = uint32_t;
     const uint8_t *k8;
     const float *ks;
     int ld;
@@ -37,6 +44,9 @@ struct KeysFP8 {
         const float v = __fmul_rn(e4m3_to_f32(__ldg(k8 + (size_t)t * ld + i)), __ldg(ks + t));
         return (double)v;
     }
+    DSV4CU_DEV Raw raw(int t, int i) const { return __ldg(k8 + (size_t)t * ld + i); }
+    DSV4CU_DEV float rscale(int t) const { return __ldg(ks + t); }
+    DSV4CU_DEV double val(Raw r, float sc) const { return (double)__fmul_rn(e4m3_to_f32((uint8_t)r), sc); }
 };
 
 template <class K>
@@ -81,6 +91,263 @@ __global__ void __launch_bounds__(IDX_WARPS * 32) indexer_score_kernel(
     }
 }
 
+// The same IEEE operations, arranged for throughput when head_dim = 16 J and
+// n_heads % 16 == 0. A warp covers 4 positions: half h (lanes 16h .. 16h+15)
+// takes positions 2h and 2h + 1, lane l of a half runs chain l of both, so
+// every q element read from shared memory (a broadcast to both halves) feeds
+// two fma. Heads go 16 at a time; the 16 chain values of the 16 heads are
+// folded by recursive halving over lane bits 2, 3, 0, 1: partners xor 4 and
+// xor 8 give (p_l + p_{l+4}) + (p_{l+8} + p_{l+12}) = b_{l mod 4}, partners
+// xor 1 and xor 2 give (b0 + b1) + (b2 + b3) - the reference's tree, with
+// each addition's two operands the same (IEEE addition is commutative) - and
+// each lane keeps the dot of head 8 b2 + 4 b3 + 2 b0 + b1 (b_i = bit i of l).
+// The dots go to shared memory and four lanes add the heads in order.
+constexpr int IDXF_WARPS = 12;
+
+template <int J, class K>
+__global__ void __launch_bounds__(IDXF_WARPS * 32, 1) indexer_fast_kernel(
+    float *__restrict__ out, const double *__restrict__ qd_g, const float *__restrict__ w, int H, int n_pos,
+    float scale, K keys)
+{
+    constexpr int D = 16 * J;
+    extern __shared__ double ism[];          // q [H][D], then dots [IDXF_WARPS][4][H]
+    double *qs = ism;
+    for (int i = threadIdx.x; i < H * D; i += blockDim.x) qs[i] = qd_g[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, l = lane & 15, half = lane >> 4;
+    const bool b0 = l & 1, b1 = l & 2, b2 = l & 4, b3 = l & 8;
+    const int hoff = 8 * b2 + 4 * b3 + 2 * b0 + b1;
+    double *dw = ism + H * D + warp * 4 * H;
+
+    // The next positions' key bytes are requested before this position's math.
+    typename K::Raw raw[2][J];
+    float rsc[2];
+    auto fetch = [&](int tb) {
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int t = tb + 2 * half + r;
+            const bool ok = t < n_pos;
+            rsc[r] = ok ? keys.rscale(t) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < J; j++) raw[r][j] = ok ? keys.raw(t, 16 * j + l) : (typename K::Raw)0;
+        }
+    };
+    const int tstride = gridDim.x * IDXF_WARPS * 4;
+    fetch((blockIdx.x * IDXF_WARPS + warp) * 4);
+    for (int t0 = (blockIdx.x * IDXF_WARPS + warp) * 4; t0 < n_pos; t0 += tstride) {
+        double k[2][J];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const bool ok = t0 + 2 * half + r < n_pos;
+#pragma unroll
+            for (int j = 0; j < J; j++) k[r][j] = ok ? keys.val(raw[r][j], rsc[r]) : 0.0;
+        }
+        fetch(t0 + tstride);
+        for (int hg = 0; hg < H; hg += 16) {
+            double v[2][16];
+#pragma unroll
+            for (int hh = 0; hh < 16; hh++) {
+                const double *qh = qs + (size_t)(hg + hh) * D + l;
+                double p0 = 0.0, p1 = 0.0;
+#pragma unroll
+                for (int j = 0; j < J; j++) {
+                    const double qv = qh[16 * j];
+                    p0 = __fma_rn(qv, k[0][j], p0);
+                    p1 = __fma_rn(qv, k[1][j], p1);
+                }
+                v[0][hh] = p0;
+                v[1][hh] = p1;
+            }
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                double a8[8], a4[4], a2[2];
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const double send = b2 ? v[r][i] : v[r][8 + i];
+                    a8[i] = __dadd_rn(b2 ? v[r][8 + i] : v[r][i], __shfl_xor_sync(0xFFFFFFFFu, send, 4));
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const double send = b3 ? a8[i] : a8[4 + i];
+                    a4[i] = __dadd_rn(b3 ? a8[4 + i] : a8[i], __shfl_xor_sync(0xFFFFFFFFu, send, 8));
+                }
+#pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const double send = b0 ? a4[i] : a4[2 + i];
+                    a2[i] = __dadd_rn(b0 ? a4[2 + i] : a4[i], __shfl_xor_sync(0xFFFFFFFFu, send, 1));
+                }
+                const double send = b1 ? a2[0] : a2[1];
+                dw[(2 * half + r) * H + hg + hoff] =
+                    __dadd_rn(b1 ? a2[1] : a2[0], __shfl_xor_sync(0xFFFFFFFFu, send, 2));
+            }
+        }
+        __syncwarp();
+        if (lane < 4 && t0 + lane < n_pos) {
+            const double *dd = dw + lane * H;
+            double total = 0.0;
+            for (int h = 0; h < H; h++) {
+                const double d = dd[h];
+                if (d > 0.0) total = __dadd_rn(total, __dmul_rn(d, (double)__ldg(w + h)));
+            }
+            out[t0 + lane] = __fmul_rn((float)total, scale);
+        }
+        __syncwarp();
+    }
+}
+
+
+// ------------------------------------------------------------ FP8 keys, FP64 tensor cores
+// For the FP8 cache (64 heads x 128) the dots can run on the FP64 tensor
+// core (mma.m8n8k4.f64) without changing a bit, when every scale involved
+// is a power of two 2^e with -117 <= e <= 118 (or zero): then each q and k
+// value is fl32(e4m3 x scale) = an integer below 2^18 times a quantum of
+// 2^-9 x scale, exactly, each product is an integer below 2^36 times the
+// product of the quanta, and all 128 products of a dot and every partial sum
+// are integers below 2^43 in those units - exact in double. The reference's
+// fma chains and pairwise fold therefore never round, and neither does any
+// other order: the dot is the exact value either way. The head sum
+// total = sum_h relu(dot_h) w_h stays in the reference's order, per position.
+// A warp task (16 positions) whose key scales (or the q scales) fail the
+// test is computed by the exact replay instead.
+constexpr int IDXM_WARPS = 8, IDXM_POS = 16, IDXM_H = 64, IDXM_D = 128;
+constexpr int IDXM_DSTRIDE = IDXM_H + 1;   // dot rows padded against bank conflicts
+
+DSV4CU_DEV bool idx_pow2_scale(float s)
+{
+    const uint32_t u = __float_as_uint(s) & 0x7FFFFFFFu;
+    if (u == 0u) return true;
+    const int e = (int)(u >> 23) - 127;
+    return (u & 0x7FFFFFu) == 0u && e >= -117 && e <= 118;
+}
+
+// D[8x8] += A[8x4] B[4x8] in FP64; lane: a = A[lane / 4][lane % 4],
+// b = B[lane % 4][lane / 4], d = D[lane / 4][2 (lane % 4) + {0, 1}].
+DSV4CU_DEV void dmma_884(double (&d)[2], double a, double b)
+{
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
+
+// q element (h, k) in the fragment order [k / 4][h / 8][(h % 8) * 4 + k % 4].
+DSV4CU_DEV double idxm_q(const double *qf, int h, int k)
+{
+    return qf[((k >> 2) * 8 + (h >> 3)) * 32 + (h & 7) * 4 + (k & 3)];
+}
+
+// The exact replay of one position (16 fma chains, the reference's fold),
+// two heads at a time; writes dot[h] for every head.
+DSV4CU_DEV void idxm_replay(const double *qf, const KeysFP8 &keys, int t, double *dot)
+{
+    const int lane = threadIdx.x & 31, l = lane & 15, half = lane >> 4;
+    double kr[IDXM_D / 16];
+#pragma unroll
+    for (int j = 0; j < IDXM_D / 16; j++) kr[j] = keys.load(t, 16 * j + l);
+    for (int h0 = 0; h0 < IDXM_H; h0 += 2) {
+        const int h = h0 + half;
+        double p = 0.0;
+#pragma unroll
+        for (int j = 0; j < IDXM_D / 16; j++) p = __fma_rn(idxm_q(qf, h, 16 * j + l), kr[j], p);
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 4));
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 8));
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 1));
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 2));
+        if (l == 0) dot[h] = p;
+    }
+}
+
+
+__global__ void __launch_bounds__(IDXM_WARPS * 32, 1) indexer_dmma_kernel(
+    float *__restrict__ out, const double *__restrict__ qd_g, const float *__restrict__ qscale,
+    const float *__restrict__ w, int n_pos, float scale, KeysFP8 keys)
+{
+    extern __shared__ double idxm_sm[];
+    double *qf = idxm_sm;                                  // [32][8][32] fragment order
+    double *dots = qf + IDXM_D / 4 * 8 * 32;               // [IDXM_WARPS][IDXM_POS][IDXM_DSTRIDE]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < IDXM_H * IDXM_D; i += blockDim.x) {
+        const int ks = i >> 8, mt = (i >> 5) & 7, L = i & 31;
+        qf[i] = qd_g[(mt * 8 + (L >> 2)) * IDXM_D + 4 * ks + (L & 3)];
+    }
+    const int q_ok = __syncthreads_and(tid < IDXM_H ? idx_pow2_scale(__ldg(qscale + tid)) : 1);
+    double *dw = dots + warp * IDXM_POS * IDXM_DSTRIDE;
+    const int g = lane >> 2, c = lane & 3;
+
+    for (int task = blockIdx.x * IDXM_WARPS + warp; task * IDXM_POS < n_pos; task += gridDim.x * IDXM_WARPS) {
+        const int t0 = task * IDXM_POS;
+        const int tl = t0 + (lane & 15);
+        const bool ok = __all_sync(0xFFFFFFFFu, tl >= n_pos || idx_pow2_scale(__ldg(keys.ks + tl))) && q_ok;
+        if (ok) {
+            double acc[2][8][2];
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                for (int mt = 0; mt < 8; mt++) acc[nt][mt][0] = acc[nt][mt][1] = 0.0;
+            // B: position t0 + 8 nt + g, element 4 ks + c.
+            const uint8_t *row[2];
+            float ksc[2];
+            bool live[2];
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++) {
+                const int t = t0 + 8 * nt + g;
+                live[nt] = t < n_pos;
+                row[nt] = keys.k8 + (size_t)(live[nt] ? t : 0) * keys.ld;
+                ksc[nt] = live[nt] ? __ldg(keys.ks + t) : 0.0f;
+            }
+#pragma unroll 4
+            for (int ks = 0; ks < IDXM_D / 4; ks++) {
+                double b[2];
+#pragma unroll
+                for (int nt = 0; nt < 2; nt++)
+                    b[nt] = live[nt] ? (double)__fmul_rn(e4m3_to_f32(__ldg(row[nt] + 4 * ks + c)), ksc[nt]) : 0.0;
+                const double *qa = qf + ks * 256 + lane;
+#pragma unroll
+                for (int mt = 0; mt < 8; mt++) {
+                    const double a = qa[mt * 32];
+                    dmma_884(acc[0][mt], a, b[0]);
+                    dmma_884(acc[1][mt], a, b[1]);
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 2; nt++)
+#pragma unroll
+                for (int mt = 0; mt < 8; mt++)
+#pragma unroll
+                    for (int j = 0; j < 2; j++) dw[(8 * nt + 2 * c + j) * IDXM_DSTRIDE + mt * 8 + g] = acc[nt][mt][j];
+        } else {
+            for (int p = 0; p < IDXM_POS && t0 + p < n_pos; p++) idxm_replay(qf, keys, t0 + p, dw + p * IDXM_DSTRIDE);
+        }
+        __syncwarp();
+        if (lane < IDXM_POS && t0 + lane < n_pos) {
+            const double *dd = dw + lane * IDXM_DSTRIDE;
+            double total = 0.0;
+            for (int h = 0; h < IDXM_H; h++) {
+                const double d = dd[h];
+                if (d > 0.0) total = __dadd_rn(total, __dmul_rn(d, (double)__ldg(w + h)));
+            }
+            out[t0 + lane] = __fmul_rn((float)total, scale);
+        }
+        __syncwarp();
+    }
+}
+
+static float indexer_scale(int H, int D);
+
+static int indexer_dmma_launch(float *out, const double *qd, const float *qscale, const float *w, int n_pos,
+                               KeysFP8 keys, cudaStream_t st)
+{
+    const size_t smem = ((size_t)IDXM_H * IDXM_D + (size_t)IDXM_WARPS * IDXM_POS * IDXM_DSTRIDE) * sizeof(double);
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)indexer_dmma_kernel, (int)smem));
+    int blocks = device_sms();
+    const int need = (n_pos + IDXM_WARPS * IDXM_POS - 1) / (IDXM_WARPS * IDXM_POS);
+    if (blocks > need) blocks = need;
+    indexer_dmma_kernel<<<blocks, IDXM_WARPS * 32, smem, st>>>(out, qd, qscale, w, n_pos,
+                                                               indexer_scale(IDXM_H, IDXM_D), keys);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
 // q (fp32, or e4m3 * per-head scale in float) -> double, once per call.
 __global__ void indexer_q_kernel(double *qd, const float *q, const uint8_t *q8, const float *qscale, int H, int D)
 {
@@ -97,18 +364,38 @@ static float indexer_scale(int H, int D)
     return r;
 }
 
+template <int J, class K>
+static int indexer_fast_launch(float *out, double *qd, const float *w, int H, int n_pos, K keys, cudaStream_t st)
+{
+    const size_t smem = ((size_t)H * 16 * J + (size_t)IDXF_WARPS * 4 * H) * sizeof(double);
+    auto kern = indexer_fast_kernel<J, K>;
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)kern, (int)smem));
+    int blocks = device_sms();      // one CTA per SM (its registers fill the SM)
+    const int need = (n_pos + IDXF_WARPS * 4 - 1) / (IDXF_WARPS * 4);
+    if (blocks > need) blocks = need;
+    kern<<<blocks, IDXF_WARPS * 32, smem, st>>>(out, qd, w, H, n_pos, indexer_scale(H, 16 * J), keys);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
 template <class K>
 static int indexer_launch(float *out, double *qd, const float *w, int H, int D, int n_pos, K keys,
                           cudaStream_t st)
 {
+    // Fast arrangement: whole 16-element chains, heads in groups of 16, q +
+    // dot scratch within 200 KB of shared memory.
+    if (H % 16 == 0 && ((size_t)H * D + (size_t)IDXF_WARPS * 4 * H) * sizeof(double) <= 200 * 1024) {
+        if (D == 64) return indexer_fast_launch<4>(out, qd, w, H, n_pos, keys, st);
+        if (D == 128) return indexer_fast_launch<8>(out, qd, w, H, n_pos, keys, st);
+    }
     const size_t smem = (size_t)H * D * sizeof(double);
     if (smem > 200 * 1024)
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "indexer: n_heads*head_dim too large");
     auto kern = indexer_score_kernel<K>;
-    DSV4CU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)kern, (int)smem));
+    const int sms = device_sms();
     int per_sm = 1;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, IDX_WARPS * 32, smem);
     if (per_sm < 1) per_sm = 1;
@@ -185,5 +472,7 @@ extern "C" int dsv4cu_indexer_score_fp8(float *out, const uint8_t *q8, const flo
     indexer_q_kernel<<<(n + 255) / 256, 256, 0, st>>>(qd, nullptr, q8, q_scale, n_heads, head_dim);
     DSV4CU_LAUNCH_CHECK();
     KeysFP8 k{k8, k_scale, k_stride};
+    if (n_heads == IDXM_H && head_dim == IDXM_D)
+        return indexer_dmma_launch(out, qd, q_scale, weights, n_pos, k, st);
     return indexer_launch(out, qd, weights, n_heads, head_dim, n_pos, k, st);
 }

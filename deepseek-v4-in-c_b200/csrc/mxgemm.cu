@@ -57,11 +57,13 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const float *__restrict__ x
                                                      int tpt, int NB, uint8_t *__restrict__ xq,
                                                      uint8_t *__restrict__ sfb, int *__restrict__ cnt, int ncnt)
 {
-    // x, the buffers written below and (on the dsv4cu_mmq path) the weight
-    // scale blocks belong to earlier kernels until they end; after that the
-    // GEMM may launch and stream weights until it needs this kernel's output.
-    pdl_wait();
+    // The GEMM may launch at once and stream its weights while the previous
+    // kernel finishes: weights and scale blocks were complete before this
+    // kernel could start (the kernels that write them, the scale-block
+    // preparation included, never release their dependents early). x and the
+    // buffers written below belong to the previous kernel until it ends.
     pdl_trigger();
+    pdl_wait();
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < ncnt; i += (long)gridDim.x * blockDim.x) cnt[i] = 0;
     const long gw = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31, kc = K >> 7;

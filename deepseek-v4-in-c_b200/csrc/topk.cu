@@ -7,13 +7,18 @@
 // shared-memory sort limit (TOPK_MAX_SORT).
 //
 // One CTA of 1024 threads:
-//   1. key(i) = order-preserving uint32 of score i (larger score -> larger key).
-//   2. Radix select, 4 passes of 8 bits from the top: the k-th largest key T
-//      and how many of the keys equal to T belong in the result (need_eq).
-//   3. Ordered compaction over i ascending: every key > T, and the first need_eq
-//      indices whose key == T (the lower indices win the tie).
+//   1. key(i) = order-preserving uint32 of score i (larger score -> larger key),
+//      staged in shared memory when the keys fit (n <= ~47K for k <= 2048).
+//   2. Radix select, 3 passes of 11, 11 and 10 bits from the top: the k-th
+//      largest key T and how many of the keys equal to T belong in the result
+//      (need_eq); each pass finds its digit with one block scan.
+//   3. Ordered compaction over i ascending (ballots per 32 indices): every
+//      key > T, and the first need_eq indices whose key == T (the lower
+//      indices win the tie).
 //   4. Bitonic sort of (key, ~index) descending: score descending, then index
 //      ascending - exactly the reference output order.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "ctx.h"
 
@@ -52,71 +57,125 @@ __device__ int block_exscan(int v, int *out_prefix, int *sh_warp)
     return total;
 }
 
+// Radix digits, most significant first: 11 + 11 + 10 bits.
+constexpr int TOPK_BINS = 2048;
+__device__ __constant__ int topk_shift[3] = {21, 10, 0};
+__device__ __constant__ int topk_width[3] = {11, 11, 10};
+
+template <bool SMEM_KEYS>
 __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(const float *__restrict__ scores, int n, int k,
                                                             int *__restrict__ out, int sort_n)
 {
-    __shared__ int hist[256];
+    __shared__ int hist[TOPK_BINS];
     __shared__ int sh_warp[32];
+    __shared__ int warp_gt[32], warp_eq[32];
     __shared__ uint32_t s_prefix, s_mask;
     __shared__ int s_need;
-    extern __shared__ unsigned long long sel[];   // [sort_n]
+    extern __shared__ unsigned long long sel[];   // [sort_n], then (SMEM_KEYS) keys [n]
+    uint32_t *skeys = (uint32_t *)(sel + sort_n);
 
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (SMEM_KEYS) {
+        // Several independent loads in flight per thread.
+        constexpr int U = 8;
+        for (int b = 0; b < n; b += U * TOPK_THREADS) {
+            float v[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = b + u * TOPK_THREADS + tid;
+                v[u] = i < n ? __ldg(scores + i) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = b + u * TOPK_THREADS + tid;
+                if (i < n) skeys[i] = float_order_key(v[u]);
+            }
+        }
+    }
+    auto key_at = [&](int i) -> uint32_t { return SMEM_KEYS ? skeys[i] : score_key(scores, i); };
     if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = k; }
-    __syncthreads();
 
-    // --- radix select: find T, the k-th largest key, 8 bits at a time
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+    // --- radix select: T = the k-th largest key, need = how many keys == T are taken
+    for (int pass = 0; pass < 3; pass++) {
+        const int shift = topk_shift[pass], width = topk_width[pass], nb = 1 << width;
+        for (int i = tid; i < TOPK_BINS; i += blockDim.x) hist[i] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix, mask = s_mask;
         for (int i = tid; i < n; i += blockDim.x) {
-            const uint32_t key = score_key(scores, i);
-            const bool act = (key & mask) == prefix;
-            const unsigned d = (key >> shift) & 255u;
-            // Warp-aggregated histogram update: scores cluster in a few top
-            // digits, and per-lane shared atomics on one bin would serialise.
-            const unsigned am = __activemask();
-            const unsigned peers = __match_any_sync(am, act ? d : 256u + (threadIdx.x & 31));
-            if (act && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[d], __popc(peers));
+            const uint32_t key = key_at(i);
+            if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & (nb - 1)], 1);
         }
         __syncthreads();
-        if (tid == 0) {
-            int need = s_need, d = 255;
-            for (; d > 0; d--) {
-                if (hist[d] >= need) break;
-                need -= hist[d];
-            }
-            s_need = need;   // keys with this digit still needed
+        // Digits in descending order, two per thread; the thread whose range
+        // holds the need-th key (counting from the top) picks the digit.
+        const int dA = nb - 1 - 2 * tid, dB = dA - 1;
+        const int cA = dA >= 0 ? hist[dA] : 0, cB = dB >= 0 ? hist[dB] : 0;
+        const int need = s_need;          // read before the scan's barriers; written after them
+        int above;
+        block_exscan(cA + cB, &above, sh_warp);
+        if (above < need && need <= above + cA + cB) {
+            const bool inA = need <= above + cA;
+            const int d = inA ? dA : dB;
+            s_need = need - above - (inA ? 0 : cA);
             s_prefix = prefix | ((uint32_t)d << shift);
-            s_mask = mask | (255u << shift);
+            s_mask = mask | ((uint32_t)(nb - 1) << shift);
         }
         __syncthreads();
     }
     const uint32_t T = s_prefix;
-    const int need_eq = s_need;          // how many keys == T are taken
+    const int need_eq = s_need;
 
-    // --- ordered compaction: thread tid owns a contiguous index range
-    const int per = (n + blockDim.x - 1) / blockDim.x;
-    const int i0 = min(n, tid * per), i1 = min(n, i0 + per);
+    // --- ordered compaction: warp w owns indices [w * span, (w + 1) * span),
+    // walked 32 at a time; ballots keep index order inside the warp.
+    const int nw = blockDim.x >> 5;
+    const int span = ((n + nw - 1) / nw + 31) & ~31;
+    const int w0 = min(n, warp * span), w1 = min(n, w0 + span);
     int cgt = 0, ceq = 0;
-    for (int i = i0; i < i1; i++) {
-        const uint32_t key = score_key(scores, i);
-        cgt += key > T;
-        ceq += key == T;
+    for (int b = w0; b < w1; b += 32) {
+        const int i = b + lane;
+        const uint32_t key = i < w1 ? key_at(i) : 0u;
+        cgt += __popc(__ballot_sync(0xFFFFFFFFu, i < w1 && key > T));
+        ceq += __popc(__ballot_sync(0xFFFFFFFFu, i < w1 && key == T));
     }
-    int pgt, peq;
-    const int ngt = block_exscan(cgt, &pgt, sh_warp);
-    block_exscan(ceq, &peq, sh_warp);
-    int wgt = pgt, weq = peq;
-    for (int i = i0; i < i1; i++) {
-        const uint32_t key = score_key(scores, i);
-        const unsigned long long v = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)i);
-        if (key > T) sel[wgt++] = v;
-        else if (key == T) {
-            if (weq < need_eq) sel[ngt + weq] = v;
-            weq++;
+    if (lane == 0) {
+        warp_gt[warp] = cgt;
+        warp_eq[warp] = ceq;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int g = lane < nw ? warp_gt[lane] : 0, e = lane < nw ? warp_eq[lane] : 0;
+        int gi = g, ei = e;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a = __shfl_up_sync(0xFFFFFFFFu, gi, o), c = __shfl_up_sync(0xFFFFFFFFu, ei, o);
+            if (lane >= o) {
+                gi += a;
+                ei += c;
+            }
         }
+        if (lane < nw) {
+            warp_gt[lane] = gi - g;   // exclusive
+            warp_eq[lane] = ei - e;
+        }
+        if (lane == nw - 1) s_need = gi;   // keys > T in all
+    }
+    __syncthreads();
+    const int ngt = s_need;
+    int wgt = warp_gt[warp], weq = warp_eq[warp];
+    const unsigned lt = (1u << lane) - 1u;
+    for (int b = w0; b < w1; b += 32) {
+        const int i = b + lane;
+        const uint32_t key = i < w1 ? key_at(i) : 0u;
+        const bool gt = i < w1 && key > T, eq = i < w1 && key == T;
+        const unsigned mg = __ballot_sync(0xFFFFFFFFu, gt), me = __ballot_sync(0xFFFFFFFFu, eq);
+        const unsigned long long v = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)i);
+        if (gt) sel[wgt + __popc(mg & lt)] = v;
+        if (eq) {
+            const int r = weq + __popc(me & lt);
+            if (r < need_eq) sel[ngt + r] = v;
+        }
+        wgt += __popc(mg);
+        weq += __popc(me);
     }
     for (int i = k + tid; i < sort_n; i += blockDim.x) sel[i] = 0ull;   // padding sorts last
     __syncthreads();
@@ -137,14 +196,202 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(const float *__restr
     for (int i = tid; i < k; i += blockDim.x) out[i] = (int)(0xFFFFFFFFu - (uint32_t)(sel[i] & 0xFFFFFFFFull));
 }
 
+
+// Cluster form (n up to TOPK_CL * ~40K keys): the same steps over a cluster of
+// TOPK_CL CTAs. CTA c stages keys [c * span, (c + 1) * span) in its shared
+// memory; each radix pass builds per-CTA histograms, and after a cluster
+// barrier every CTA sums all of them through distributed shared memory and
+// picks the same digit (identical inputs, identical arithmetic). The ordered
+// compaction writes (key, ~index) pairs straight into CTA 0's sort buffer at
+// offsets from the CTAs' counts; CTA 0 sorts and writes the result.
+constexpr int TOPK_CL = 8;
+namespace cg = cooperative_groups;
+
+__global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float *__restrict__ scores, int n, int k,
+                                                                    int *__restrict__ out, int sort_n, int span)
+{
+    __shared__ int hist[2][TOPK_BINS];
+    __shared__ int sh_warp[32];
+    __shared__ int warp_gt[32], warp_eq[32];
+    __shared__ int cta_cnt[2];                    // this CTA's keys > T and == T
+    __shared__ uint32_t s_prefix, s_mask;
+    __shared__ int s_need;
+    extern __shared__ unsigned long long sel[];   // [sort_n] (used in CTA 0), then keys [span]
+    uint32_t *skeys = (uint32_t *)(sel + sort_n);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g0 = min(n, rank * span), g1 = min(n, g0 + span), cnt = g1 - g0;
+
+    constexpr int U = 8;
+    for (int b = 0; b < cnt; b += U * TOPK_THREADS) {
+        float v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = b + u * TOPK_THREADS + tid;
+            v[u] = i < cnt ? __ldg(scores + g0 + i) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = b + u * TOPK_THREADS + tid;
+            if (i < cnt) skeys[i] = float_order_key(v[u]);
+        }
+    }
+    if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = k; }
+
+    for (int pass = 0; pass < 3; pass++) {
+        const int shift = topk_shift[pass], width = topk_width[pass], nb = 1 << width;
+        int *hb = hist[pass & 1];
+        for (int i = tid; i < TOPK_BINS; i += blockDim.x) hb[i] = 0;
+        __syncthreads();
+        const uint32_t prefix = s_prefix, mask = s_mask;
+        for (int i = tid; i < cnt; i += blockDim.x) {
+            const uint32_t key = skeys[i];
+            if ((key & mask) == prefix) atomicAdd(&hb[(key >> shift) & (nb - 1)], 1);
+        }
+        cluster.sync();                           // every CTA's histogram is complete
+        const int dA = nb - 1 - 2 * tid, dB = dA - 1;
+        int cA = 0, cB = 0;
+        for (int r = 0; r < TOPK_CL; r++) {
+            const int *rh = cluster.map_shared_rank(hb, r);
+            if (dA >= 0) cA += rh[dA];
+            if (dB >= 0) cB += rh[dB];
+        }
+        const int need = s_need;
+        int above;
+        block_exscan(cA + cB, &above, sh_warp);
+        if (above < need && need <= above + cA + cB) {
+            const bool inA = need <= above + cA;
+            const int d = inA ? dA : dB;
+            s_need = need - above - (inA ? 0 : cA);
+            s_prefix = prefix | ((uint32_t)d << shift);
+            s_mask = mask | ((uint32_t)(nb - 1) << shift);
+        }
+        __syncthreads();
+    }
+    const uint32_t T = s_prefix;
+    const int need_eq = s_need;
+
+    // counts of this CTA's slice, per warp in index order
+    const int nw = blockDim.x >> 5;
+    const int wspan = ((cnt + nw - 1) / nw + 31) & ~31;
+    const int w0 = min(cnt, warp * wspan), w1 = min(cnt, w0 + wspan);
+    int cgt = 0, ceq = 0;
+    for (int b = w0; b < w1; b += 32) {
+        const int i = b + lane;
+        const uint32_t key = i < w1 ? skeys[i] : 0u;
+        cgt += __popc(__ballot_sync(0xFFFFFFFFu, i < w1 && key > T));
+        ceq += __popc(__ballot_sync(0xFFFFFFFFu, i < w1 && key == T));
+    }
+    if (lane == 0) {
+        warp_gt[warp] = cgt;
+        warp_eq[warp] = ceq;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int g = lane < nw ? warp_gt[lane] : 0, e = lane < nw ? warp_eq[lane] : 0;
+        int gi = g, ei = e;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a = __shfl_up_sync(0xFFFFFFFFu, gi, o), c = __shfl_up_sync(0xFFFFFFFFu, ei, o);
+            if (lane >= o) {
+                gi += a;
+                ei += c;
+            }
+        }
+        if (lane < nw) {
+            warp_gt[lane] = gi - g;
+            warp_eq[lane] = ei - e;
+        }
+        if (lane == nw - 1) {
+            cta_cnt[0] = gi;
+            cta_cnt[1] = ei;
+        }
+    }
+    cluster.sync();                               // every CTA's counts are complete
+    int gbase = 0, ebase = 0, ngt = 0;
+    for (int r = 0; r < TOPK_CL; r++) {
+        const int *rc = cluster.map_shared_rank(cta_cnt, r);
+        const int a = rc[0], b = rc[1];
+        if (r < rank) {
+            gbase += a;
+            ebase += b;
+        }
+        ngt += a;
+    }
+    unsigned long long *sel0 = cluster.map_shared_rank(sel, 0);
+    int wgt = gbase + warp_gt[warp], weq = ebase + warp_eq[warp];
+    const unsigned lt = (1u << lane) - 1u;
+    for (int b = w0; b < w1; b += 32) {
+        const int i = b + lane;
+        const uint32_t key = i < w1 ? skeys[i] : 0u;
+        const bool gt = i < w1 && key > T, eq = i < w1 && key == T;
+        const unsigned mg = __ballot_sync(0xFFFFFFFFu, gt), me = __ballot_sync(0xFFFFFFFFu, eq);
+        const unsigned long long v = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)(g0 + i));
+        if (gt) sel0[wgt + __popc(mg & lt)] = v;
+        if (eq) {
+            const int r = weq + __popc(me & lt);
+            if (r < need_eq) sel0[ngt + r] = v;
+        }
+        wgt += __popc(mg);
+        weq += __popc(me);
+    }
+    if (rank == 0)
+        for (int i = k + tid; i < sort_n; i += blockDim.x) sel[i] = 0ull;
+    cluster.sync();                               // CTA 0 holds all k picks
+    if (rank != 0) return;
+    for (int size = 2; size <= sort_n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < (sort_n >> 1); i += blockDim.x) {
+                const int lo = 2 * i - (i & (stride - 1));
+                const int hi = lo + stride;
+                const bool desc = ((lo & size) == 0);
+                const unsigned long long a = sel[lo], b = sel[hi];
+                if ((a < b) == desc) { sel[lo] = b; sel[hi] = a; }
+            }
+            __syncthreads();
+        }
+    }
+    for (int i = tid; i < k; i += blockDim.x) out[i] = (int)(0xFFFFFFFFu - (uint32_t)(sel[i] & 0xFFFFFFFFull));
+}
+
+// Shared memory above the static arrays: the sort buffer and, when they fit,
+// the n keys.
+constexpr size_t TOPK_DYN_SMEM = 200 * 1024;
+
 int topk_run(int *idx, const float *scores, int n, int k, cudaStream_t st)
 {
     int sort_n = 1;
     while (sort_n < k) sort_n <<= 1;
     if (sort_n < 2) sort_n = 2;
-    const size_t smem = (size_t)sort_n * sizeof(unsigned long long);
-    DSV4CU_CUDA_TRY(cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    topk_kernel<<<1, TOPK_THREADS, smem, st>>>(scores, n, k, idx, sort_n);
+    const size_t sort_b = (size_t)sort_n * sizeof(unsigned long long);
+    // Cluster form when each CTA's slice fits beside the sort buffer.
+    const int span = ((n + TOPK_CL - 1) / TOPK_CL + 31) & ~31;
+    if (n >= TOPK_CL * 1024 && sort_b + (size_t)span * 4 <= TOPK_DYN_SMEM - 16 * 1024) {
+        const size_t smem = sort_b + (size_t)span * 4;
+        static SmemLimit lim_cl;
+        DSV4CU_CUDA_TRY(smem_limit(lim_cl, (const void *)topk_cluster_kernel, (int)smem));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(TOPK_CL);
+        cfg.blockDim = dim3(TOPK_THREADS);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = TOPK_CL;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        DSV4CU_CUDA_TRY(cudaLaunchKernelEx(&cfg, topk_cluster_kernel, scores, n, k, idx, sort_n, span));
+        return DSV4CU_OK;
+    }
+    const bool in_smem = sort_b + (size_t)n * 4 <= TOPK_DYN_SMEM;
+    const size_t smem = in_smem ? sort_b + (size_t)n * 4 : sort_b;
+    auto kern = in_smem ? topk_kernel<true> : topk_kernel<false>;
+    static SmemLimit lim_a, lim_b;
+    DSV4CU_CUDA_TRY(smem_limit(in_smem ? lim_a : lim_b, (const void *)kern, (int)smem));
+    kern<<<1, TOPK_THREADS, smem, st>>>(scores, n, k, idx, sort_n);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
 }

@@ -77,7 +77,8 @@ def test_indexer_kat(host):
     assert abs(out[1] / out[0] - 4) < 1e-4
 
 
-@pytest.mark.parametrize("h,d,n", [(64, 128, 4097), (3, 7, 50), (8, 48, 31), (1, 16, 1), (64, 256, 33)])
+@pytest.mark.parametrize("h,d,n", [(64, 128, 4097), (3, 7, 50), (8, 48, 31), (1, 16, 1), (64, 256, 33),
+                                   (16, 64, 5), (48, 64, 130), (32, 128, 3), (64, 128, 1)])
 def test_indexer_random_bitexact(dev, orc, h, d, n):
     rng = np.random.default_rng(h * d + n)
     q = rng.standard_normal((h, d)).astype(np.float32)
@@ -99,6 +100,30 @@ def test_config4_full_fp8_score_topk(dev, orc):
     assert np.array_equal(bits(got), bits(want))
     idx = dev_topk(dev, got, 2048)
     assert np.array_equal(idx, orc.topk(want, 2048))
+
+
+@pytest.mark.parametrize("case", ["keys-mixed", "q-nonpow2", "zero-scale"])
+def test_config4_fp8_scale_forms(dev, orc, case):
+    """The FP8 path uses FP64 tensor cores only where every scale is a power of
+    two (exact there) and replays the reference's fma chains elsewhere: both
+    must give the reference's bits, in the same launch."""
+    rng = np.random.default_rng({"keys-mixed": 31, "q-nonpow2": 32, "zero-scale": 33}[case])
+    n = 1000
+    k8, ks = quant_rows(rng.standard_normal((n, 128)).astype(np.float32))
+    q8, qs = quant_rows(rng.standard_normal((64, 128)).astype(np.float32))
+    if case == "keys-mixed":
+        bad = rng.random(n) < 0.05                     # a few 16-position tasks fall back
+        ks = np.where(bad, ks * np.float32(1.2345), ks).astype(np.float32)
+    elif case == "q-nonpow2":
+        qs = (qs * np.float32(0.7771)).astype(np.float32)
+    else:
+        ks[::7] = 0.0
+    w = rng.standard_normal(64).astype(np.float32)
+    got = dev_score8(dev, q8, qs, k8, ks, w)
+    kf = (pack.E4M3[k8] * ks[:, None]).astype(np.float32)
+    qf = (pack.E4M3[q8] * qs[:, None]).astype(np.float32)
+    want = orc.indexer_score(qf, kf, w)
+    assert np.array_equal(bits(got), bits(want))
 
 
 def test_topk_golden_and_kat(dev, host):
