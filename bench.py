@@ -15,6 +15,8 @@ prefill (config 3): 4096 tokens through the MoE layer + the FP8 QKV projection.
 gemv (config 1): FP8 7168x7168 GEMV, four matrices in turn, back to back.
 indexer (config 4): FP8 indexer score over 32768 keys, top-2048, sparse
          attention (64 heads x 576) over the picks; four contexts in turn.
+ep: the MoE layer expert-parallel over the ranks (256 / N experts each,
+         64 tokens per rank per step, NCCL all-to-all dispatch and return).
 
 value  = the workload's metric over all ranks, device time (CUDA events, max
          over ranks).
@@ -65,10 +67,11 @@ def parse():
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts resident in HBM (256 = config 2; smaller only for ncu captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "indexer"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "gemv", "indexer", "ep"], default="decode",
                     help="decode = config 2 (the headline); prefill = config 3 (MoE layer over 4096 tokens + "
                          "FP8 QKV projection); gemv = config 1 (FP8 7168x7168 GEMV, HBM GB/s); indexer = "
-                         "config 4 (FP8 indexer score + top-2048 + sparse attention)")
+                         "config 4 (FP8 indexer score + top-2048 + sparse attention); ep = the MoE layer with "
+                         "experts partitioned over the ranks (NCCL all-to-all)")
     return ap.parse_args()
 
 
@@ -1158,10 +1161,178 @@ def run_indexer_reference(args, rank, world):
             "e2e": {"value": round(v, 3), "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# --------------------------------------------------- expert-parallel MoE layer (config 5's layer)
+EP_BATCH = 64
+EP_METRIC = "expert-parallel MoE layer decode tok/s (all ranks; batch 64 per rank)"
+EP_WORKLOAD = ("ep: config-2 MoE layer (256 FP4 experts 2048x4096 / 4096x2048, top-8, FP8 shared expert, hidden "
+               "4096) with the routed experts partitioned over the ranks (256 / N each, HBM-resident) and 64 "
+               "tokens per rank per step; NCCL all-to-all dispatch and return, k-order combine on the home rank")
+
+
+def build_local_experts(dev, torch, first, count, layer_id=0):
+    """Experts first .. first + count - 1 of the config-2 layer + the FP8 shared expert."""
+    import dsv4cu
+    keep = []
+    src = torch.empty(INTER * HIDDEN, dtype=torch.float32, device="cuda")
+
+    def mat(fmt, rows, cols, seed):
+        dev.fill_normal(src, seed + 100003 * layer_id, 0.0, 0.02)
+        if fmt == 3:
+            W = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
+            S = torch.empty(rows * cols // 32, dtype=torch.uint8, device="cuda")
+            dev.quantize_fp4(W, S, src, rows, cols)
+            q = dsv4cu.QMat(W.data_ptr(), S.data_ptr(), 3, rows, cols, 1, 32)
+        else:
+            W = torch.empty(rows * cols, dtype=torch.uint8, device="cuda")
+            S = torch.empty((rows // 128) * (cols // 128), dtype=torch.uint8, device="cuda")
+            dev.quantize_fp8(W, S, src, rows, cols)
+            q = dsv4cu.QMat(W.data_ptr(), S.data_ptr(), 2, rows, cols, 128, 128)
+        keep.extend([W, S])
+        return q
+
+    experts = [dsv4cu.Expert(mat(3, INTER, HIDDEN, 10 * e + 1), mat(3, INTER, HIDDEN, 10 * e + 2),
+                             mat(3, HIDDEN, INTER, 10 * e + 3)) for e in range(first, first + count)]
+    shared = dsv4cu.Expert(mat(2, INTER, HIDDEN, 7001), mat(2, INTER, HIDDEN, 7002), mat(2, HIDDEN, INTER, 7003))
+    torch.cuda.synchronize()
+    return dev.moe_create(experts, shared, HIDDEN, INTER), keep
+
+
+def run_ep(args, rank, local_rank, world):
+    import datetime
+    import torch
+    import dsv4cu
+    from ep import DeviceOps, ExpertParallelMoE
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local_rank))
+    dev = dsv4cu.Device(local_rank)
+    epr = N_EXPERTS // world
+    layer, keep = build_local_experts(dev, torch, rank * epr, epr)
+
+    class TimedOps(DeviceOps):
+        """DeviceOps that can time the rows compute and count the experts it touched."""
+        probe = None
+
+        def rows(self, recv, ids, nrows):
+            if self.probe is None:
+                return super().rows(recv, ids, nrows)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            y = super().rows(recv, ids, nrows)
+            b.record()
+            self.probe.append((a, b, ids))
+            return y
+
+    ops = TimedOps(dev, layer, N_EXPERTS, epr, world, HIDDEN, TOPK, ROUTE_SCALE, LIMIT)
+    moe = ExpertParallelMoE(ops, rank, world)
+    n_steps = args.warmup + args.steps
+    rng = np.random.default_rng(5000 + rank)
+    sys.path.insert(0, PKG)
+    import pack
+    xs = pack.bf16_round(rng.standard_normal((n_steps, EP_BATCH, HIDDEN)).astype(np.float32))
+    lgs = pack.bf16_round(rng.standard_normal((n_steps, EP_BATCH, N_EXPERTS)).astype(np.float32))
+    dx, dl = torch.from_numpy(xs).cuda(), torch.from_numpy(lgs).cuda()
+
+    def barrier():
+        if world > 1:
+            tdist.barrier()
+
+    for i in range(args.warmup):
+        moe.forward(dx[i], dl[i])
+    torch.cuda.synchronize()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local_rank)
+    clocks.start()
+    t0.record()
+    for k in range(args.steps):
+        moe.forward(dx[args.warmup + k], dl[args.warmup + k])
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    total_ms = t0.elapsed_time(t1)
+    t = torch.tensor([total_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+    total_ms = t.item()
+    # the rows compute of every step, live on the stream, with the experts it touched
+    ops.probe = []
+    barrier()
+    for k in range(args.steps):
+        moe.forward(dx[args.warmup + k], dl[args.warmup + k])
+    torch.cuda.synchronize()
+    rows_ms, rows_bytes = [], []
+    for a, b, ids in ops.probe:
+        rows_ms.append(a.elapsed_time(b))
+        u = ids.unique().cpu().numpy()
+        rows_bytes.append(int((u < epr).sum()) * 3 * FP4_MAT + (3 * FP8_MAT if (u == epr).any() else 0))
+    ops.probe = None
+    rms, rb = float(np.mean(rows_ms)), float(np.mean(rows_bytes))
+    # e2e: own tokens from pinned host memory in, the layer output back each step
+    hx, hl = torch.from_numpy(xs).pin_memory(), torch.from_numpy(lgs).pin_memory()
+    hout = torch.empty((n_steps, EP_BATCH, HIDDEN), dtype=torch.float32).pin_memory()
+    gx, gl = torch.empty_like(dx[0]), torch.empty_like(dl[0])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for k in range(args.steps):
+        i = args.warmup + k
+        gx.copy_(hx[i], non_blocking=True)
+        gl.copy_(hl[i], non_blocking=True)
+        out, _, _ = moe.forward(gx, gl)
+        hout[i].copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+    e2e_ms = t.item()
+    dev.check_status()
+    peak, peak_kind = load_peaks()
+    achieved = rb / (rms * 1e-3) / 1e9
+    res = {
+        "metric": EP_METRIC, "value": round(world * EP_BATCH * args.steps / (total_ms * 1e-3), 1), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1/e4m3 weights x e4m3 activation terms (4, exact split) -> f32 (tcgen05 kind::mxf8f6f4)",
+        "data": "synthetic: weights N(0,0.02) quantized on device, x/logits N(0,1) bf16-valued, seeded",
+        "config": {"workload": EP_WORKLOAD, "global_batch": world * EP_BATCH, "parallelism": f"ep{world}",
+                   "experts_per_rank": epr,
+                   "l2": f"inputs larger than L2: {epr} routed experts per rank ({epr * 13.37:.0f} MB) + the shared "
+                         "expert, fresh tokens every step"},
+        "roofline": {"bound": "hbm", "kernel": "dsv4cu_moe_rows (tcgen05 grouped expert GEMMs of the rank)",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": None, "algorithmic_bytes": round(rb),
+                     "algorithmic_bytes_note": "weights of the distinct local experts the step's rows touched",
+                     "kernel_ms": round(rms, 5)},
+        "e2e": {"value": round(world * EP_BATCH * args.steps / (e2e_ms * 1e-3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": int(xs[0].nbytes + lgs[0].nbytes), "d2h_bytes_per_step": int(xs[0].nbytes),
+                "api": "ep.ExpertParallelMoE over dsv4cu_route / dsv4cu_ep_pack / dsv4cu_moe_rows / "
+                       "dsv4cu_ep_combine + NCCL all-to-all"},
+        "gpu_launches": 14 * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        tdist.barrier()
+        tdist.destroy_process_group()
+    dev.moe_destroy(layer)
+    dev.close()
+    return res if rank == 0 else None
+
+
 def main():
     args = parse()
     rank, local_rank, world = dist_env()
-    if args.workload == "indexer":
+    if args.workload == "ep":
+        res = (run_reference(args, rank, world) if args.impl == "reference"
+               else run_ep(args, rank, local_rank, world))
+    elif args.workload == "indexer":
         res = (run_indexer_reference(args, rank, world) if args.impl == "reference"
                else run_indexer(args, rank, local_rank, world))
     elif args.workload == "gemv":

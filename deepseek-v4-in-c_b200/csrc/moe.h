@@ -58,4 +58,8 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
                    int terms, int *idx_out, float *wts_out, void *ws, int *status, int sms, cudaStream_t st,
                    cudaEvent_t *ev);
 
+size_t moe_mx_rows_workspace(const dsv4cu_moe *L, int nrows);
+int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const int *ids, int nrows, float limit,
+                void *ws, int *status, int sms, cudaStream_t st);
+
 }  // namespace dsv4cu

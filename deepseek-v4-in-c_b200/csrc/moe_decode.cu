@@ -702,3 +702,24 @@ extern "C" int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, floa
     return dsv4cu_moe_prefill_ev(ctx, layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt,
                                  terms, idx_out, wts_out, stream, nullptr);
 }
+
+extern "C" size_t dsv4cu_moe_rows_workspace(const dsv4cu_moe *L, int nrows)
+{
+    return (L && L->mx_ok && nrows > 0) ? moe_mx_rows_workspace(L, nrows) : 0;
+}
+
+extern "C" int dsv4cu_moe_rows(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *y, const float *x, long ldx,
+                               const int *ids, int nrows, float limit, void *stream)
+{
+    if (!ctx || !layer || !y || !x || !ids) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_rows: NULL argument");
+    if (nrows < 1) return nrows == 0 ? DSV4CU_OK : dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_rows: nrows %d", nrows);
+    if (ldx < layer->hidden || ldx % 4)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_rows: ldx %ld (hidden %d, multiple of 4)", ldx, layer->hidden);
+    if (!layer->mx_ok)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED,
+                                "moe_rows: the layer's matrices do not qualify for the tensor-core path");
+    void *ws = nullptr;
+    int r = dsv4cu_ws_get(ctx, moe_mx_rows_workspace(layer, nrows), &ws);
+    if (r) return r;
+    return moe_mx_rows(layer, y, x, ldx, ids, nrows, limit, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream);
+}

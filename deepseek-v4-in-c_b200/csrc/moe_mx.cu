@@ -739,8 +739,25 @@ void moe_mx_release(dsv4cu_moe *L)
 
 // The four launches after the B operand of gate/up is in place: gate/up,
 // SwiGLU split, down, combine.
+// y[r] = the expert output of slot pos[r] (per-row mode of the layer, no combine).
+__global__ void __launch_bounds__(256) mxmoe_rows_out_kernel(MxMoeWs ws, int nrows, int hidden, float *__restrict__ y)
+{
+    pdl_wait();
+    pdl_trigger();
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    const int h4 = hidden >> 2;
+    if (i >= (long)nrows * h4) return;
+    const int r = (int)(i / h4), c = (int)(i - (long)r * h4) * 4;
+    const int slot = ws.pos[r];
+    const float4 v = slot >= 0 ? *reinterpret_cast<const float4 *>(ws.ypart + (size_t)slot * hidden + c)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+    *reinterpret_cast<float4 *>(y + (size_t)r * hidden + c) = v;
+}
+
+// rows_mode: out receives each row's expert output (the pairs are rows,
+// topk = 1) instead of the weighted combine.
 static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &ws, int terms, float limit,
-                       float *out, int *status, int sms, cudaStream_t st, cudaEvent_t *ev)
+                       float *out, int *status, int sms, cudaStream_t st, cudaEvent_t *ev, bool rows_mode = false)
 {
     const int RT = s.inter / 128, RTH = s.hidden / 128, nt = s.nt, topk = s.topk;
     MxMoeCommon c;
@@ -782,8 +799,12 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     while (kb2 > 1 && (s.inter / 128) % kb2) kb2 >>= 1;
     r = mxmoe_dispatch<MoeDown>(s.NB, kb2, tb2, pd, g2, st);
     if (r) return r;
-    DSV4CU_CUDA_TRY(launch_pdl(mxmoe_combine_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)), dim3(256), 0,
-                               st, ws, nt, topk, s.hidden, s.has_shared, out));
+    if (rows_mode)
+        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_rows_out_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)),
+                                   dim3(256), 0, st, ws, nt, s.hidden, out));
+    else
+        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_combine_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)),
+                                   dim3(256), 0, st, ws, nt, topk, s.hidden, s.has_shared, out));
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
     return DSV4CU_OK;
 }
@@ -984,7 +1005,7 @@ __global__ void __launch_bounds__(1024) mxpf_scatter_kernel(MxMoeWs ws, PfWs pf,
 
 // Gate/up B operand of the prefill: one warp per (column tile, slot) walks
 // the token's row chunk by chunk (the table lookups are paid once per row).
-__global__ void __launch_bounds__(256) mxpf_split_kernel(const float *__restrict__ x, int hidden, MxMoeWs ws,
+__global__ void __launch_bounds__(256) mxpf_split_kernel(const float *__restrict__ x, int hidden, long ldx, MxMoeWs ws,
                                                          int terms, int tpt, int NB, long max_tasks)
 {
     pdl_wait();
@@ -995,7 +1016,7 @@ __global__ void __launch_bounds__(256) mxpf_split_kernel(const float *__restrict
     if (i >= ws.meta[2] || tl >= ws.c_cnt[i]) return;
     const int tok = ws.b_tok[ws.c_slot0[i] + tl], nbb = (NB + 127) / 128;
     for (int c = 0; c < (hidden >> 7); c++)
-        mxmoe_split_row_chunk(x + (size_t)tok * hidden, hidden, c, i, tl, terms, tpt, NB, nbb, ws.xq1, ws.sfb1);
+        mxmoe_split_row_chunk(x + (size_t)tok * ldx, hidden, c, i, tl, terms, tpt, NB, nbb, ws.xq1, ws.sfb1);
 }
 
 static MxMoeShape mxpf_shape(const dsv4cu_moe *L, int topk, int nt, int terms)
@@ -1065,9 +1086,71 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
                                nt, s.has_shared));
     const long tasks = (long)s.max_tiles * s.tpt;
     DSV4CU_CUDA_TRY(launch_pdl(mxpf_split_kernel, dim3((unsigned)((tasks * 32 + 255) / 256)), dim3(256), 0, st, x,
-                               s.hidden, ws, terms, s.tpt, s.NB, tasks));
+                               s.hidden, (long)s.hidden, ws, terms, s.tpt, s.NB, tasks));
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
     return mxmoe_gemms(L, s, ws, terms, limit, out, status, sms, st, ev);
+}
+
+
+// ------------------------------------------------------------ per-row experts
+// Row r of x (row stride ldx) through expert ids[r] (0 .. n_experts - 1, or
+// n_experts for the shared expert), no weighting: the local compute of the
+// expert-parallel layer. The prefill bucketing runs with the shared expert as
+// one more bucket and one pair per row; each row's result is the same bits
+// as the layer's decode / prefill paths give that (token, expert) pair.
+static MxMoeShape mxrows_shape(const dsv4cu_moe *L, int nrows)
+{
+    MxMoeShape s = mxpf_shape(L, 1, nrows, MX_TERMS);
+    s.n_experts = L->n_experts + (L->has_shared ? 1 : 0);
+    s.has_shared = 0;
+    s.npairs = nrows;
+    s.nbmax = min(nrows, s.n_experts);
+    s.max_tiles = nrows / s.tpt + s.nbmax + 1;
+    return s;
+}
+
+__global__ void __launch_bounds__(256) mxrows_ids_kernel(const int *__restrict__ ids, int nrows, int n_buckets,
+                                                         MxMoeWs ws, int *status)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= nrows) return;
+    const int e = ids[r];
+    const bool ok = e >= 0 && e < n_buckets;
+    ws.idx[r] = ok ? e : -1;
+    ws.wts[r] = 1.0f;
+    if (!ok) atomicCAS(status, 0, MXE_BAD_EXPERT);
+}
+
+size_t moe_mx_rows_workspace(const dsv4cu_moe *L, int nrows)
+{
+    return mxpf_layout(mxrows_shape(L, nrows), nullptr, nullptr, nullptr);
+}
+
+int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const int *ids, int nrows, float limit,
+                void *wsp, int *status, int sms, cudaStream_t st)
+{
+    if (nrows > PF_MAX_NT * 2 || L->n_experts + 1 > PREP_MAX_EXPERTS)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_rows: %d rows / %d experts beyond %d / %d", nrows,
+                                L->n_experts, PF_MAX_NT * 2, PREP_MAX_EXPERTS - 1);
+    const MxMoeShape s = mxrows_shape(L, nrows);
+    MxMoeWs ws;
+    PfWs pf;
+    mxpf_layout(s, (char *)wsp, &ws, &pf);
+    const int nchunks = (nrows + PF_CHUNK - 1) / PF_CHUNK;
+    DSV4CU_CUDA_TRY(cudaMemsetAsync(ws.meta, 0, 64, st));
+    DSV4CU_CUDA_TRY(launch_pdl(mxrows_ids_kernel, dim3((nrows + 255) / 256), dim3(256), 0, st, ids, nrows,
+                               s.n_experts, ws, status));
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_count_kernel, dim3(nchunks), dim3(1024), 0, st, ws, pf, nrows, s.n_experts));
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_offsets_kernel, dim3(1), dim3(1024), 0, st, ws, pf, nchunks, s.n_experts, nrows, 0,
+                               s.tpt, s.max_tiles));
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_scatter_kernel, dim3(nchunks), dim3(1024), 0, st, ws, pf, nrows, s.n_experts, 1,
+                               nrows, 0));
+    const long tasks = (long)s.max_tiles * s.tpt;
+    DSV4CU_CUDA_TRY(launch_pdl(mxpf_split_kernel, dim3((unsigned)((tasks * 32 + 255) / 256)), dim3(256), 0, st, x,
+                               s.hidden, ldx, ws, MX_TERMS, s.tpt, s.NB, tasks));
+    return mxmoe_gemms(L, s, ws, MX_TERMS, limit, y, status, sms, st, nullptr, true);
 }
 
 }  // namespace dsv4cu

@@ -88,7 +88,7 @@ struct MxCfg {
     static_assert(USED <= 512, "TMEM budget");
 };
 
-enum { MXE_EMPTY = 21, MXE_FULL = 22, MXE_ACC_EMPTY = 23, MXE_ACC_FULL = 24, MXE_DRAIN = 25 };
+enum { MXE_EMPTY = 21, MXE_FULL = 22, MXE_ACC_EMPTY = 23, MXE_ACC_FULL = 24, MXE_DRAIN = 25, MXE_BAD_EXPERT = 26 };
 
 DSV4CU_DEV void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
 {

@@ -71,6 +71,11 @@ def lib() -> C.CDLL:
             "dsv4cu_moe_prefill": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, i, vp, vp, vp]),
             "dsv4cu_moe_prefill_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, i, vp, vp, vp, vp]),
             "dsv4cu_moe_decode_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp, vp]),
+            "dsv4cu_moe_rows_workspace": (sz, [vp, i]),
+            "dsv4cu_moe_rows": (i, [vp, vp, vp, vp, C.c_long, vp, i, f, vp]),
+            "dsv4cu_ep_pack": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, i, vp]),
+            "dsv4cu_ep_tail": (i, [vp, i, vp, i, i, i, vp, vp]),
+            "dsv4cu_ep_combine": (i, [vp, vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_mat_create": (i, [C.POINTER(vp), vp, vp]),
             "dsv4cu_mat_destroy": (None, [vp]),
             "dsv4cu_mat_workspace": (sz, [vp, i, i]),
@@ -344,6 +349,24 @@ class Device:
         else:
             evp = _event_handles(events)
             check(self.L.dsv4cu_moe_decode_ev(*args, evp), "dsv4cu_moe_decode_ev")
+
+    def moe_rows(self, layer, y, x, ldx, ids, nrows, limit):
+        """y[r] = expert ids[r] (n_experts = the shared expert) on row r of x (dsv4cu_moe_rows)."""
+        check(self.L.dsv4cu_moe_rows(self.ctx, layer, self.ptr(y), self.ptr(x), ldx, self.ptr(ids), nrows, limit,
+                                     self.stream()), "dsv4cu_moe_rows")
+
+    def ep_pack(self, send, counts, pair_slot, x, idx, nt, topk, hidden, experts_per_rank, n_ranks):
+        check(self.L.dsv4cu_ep_pack(self.ctx, self.ptr(send), self.ptr(counts), self.ptr(pair_slot), self.ptr(x),
+                                    self.ptr(idx), nt, topk, hidden, experts_per_rank, n_ranks, self.stream()),
+              "dsv4cu_ep_pack")
+
+    def ep_tail(self, recv, nrecv, x, nt, hidden, shared_id, ids):
+        check(self.L.dsv4cu_ep_tail(self.ptr(recv), nrecv, self.ptr(x), nt, hidden, shared_id, self.ptr(ids),
+                                    self.stream()), "dsv4cu_ep_tail")
+
+    def ep_combine(self, out, back, pair_slot, wts, shared, nt, topk, hidden):
+        check(self.L.dsv4cu_ep_combine(self.ptr(out), self.ptr(back), self.ptr(pair_slot), self.ptr(wts),
+                                       self.ptr(shared), nt, topk, hidden, self.stream()), "dsv4cu_ep_combine")
 
     def indexer_score(self, out, q, kv, w, n_heads, head_dim, n_pos):
         check(self.L.dsv4cu_indexer_score(self.ptr(out), self.ptr(q), self.ptr(kv), self.ptr(w),

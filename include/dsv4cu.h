@@ -176,6 +176,40 @@ int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
                          float route_scale, float limit, int nt, int *idx_out,
                          float *wts_out, void *stream, void **events);
 
+/* ---- expert-parallel MoE layer (no reference counterpart: it replaces the
+ * src/60_cache expert cache with HBM-resident experts spread over ranks;
+ * the per-token math is dsv4_layer_moe's, src/70_decode/dsv4_layer.c:48-117).
+ *
+ * dsv4cu_moe_rows: y[r] = expert ids[r] applied to row r of x (row stride
+ * ldx floats, a multiple of 4), no weighting; ids in 0 .. n_experts - 1 or
+ * n_experts for the layer's shared expert. An id out of range gives a zero row
+ * and the device status DSV4CU status code 26. nrows <= 32768. */
+size_t dsv4cu_moe_rows_workspace(const dsv4cu_moe *layer, int nrows);
+int dsv4cu_moe_rows(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *y, const float *x, long ldx,
+                    const int *ids, int nrows, float limit, void *stream);
+
+/* Dispatch side: the nt * topk (token, slot) pairs of idx [nt][topk] (global
+ * expert ids; rank = id / experts_per_rank) become send rows [nt * topk]
+ * [hidden + 4] grouped by rank and, inside a rank, in pair order; a row is
+ * x[t] then the rank-local expert id as a float and 3 zeros. counts [n_ranks]
+ * = rows per rank, pair_slot [nt * topk] = each pair's send row (-1 for an
+ * id out of range, which also sets the device status to 31). n_ranks <= 16. */
+int dsv4cu_ep_pack(dsv4cu_ctx *ctx, float *send, int *counts, int *pair_slot, const float *x,
+                   const int *idx, int nt, int topk, int hidden, int experts_per_rank,
+                   int n_ranks, void *stream);
+
+/* recv [nrecv + nt][hidden + 4]: ids[r] = the id column of the nrecv
+ * received rows; rows nrecv .. nrecv + nt - 1 are set to x (the own tokens)
+ * with id shared_id. */
+int dsv4cu_ep_tail(float *recv, int nrecv, const float *x, int nt, int hidden, int shared_id,
+                   int *ids, void *stream);
+
+/* out[t] = sum over k in order of wts[t][k] * back[pair_slot[t][k]] (rows of
+ * hidden floats), then + shared[t] (may be NULL): the single-device layer's
+ * float operations. */
+int dsv4cu_ep_combine(float *out, const float *back, const int *pair_slot, const float *wts,
+                      const float *shared, int nt, int topk, int hidden, void *stream);
+
 /* Indexer score with fp32 inputs, bit-identical to dsv4_indexer_score
  * (src/10_compute/dsv4_indexer.c:66-90): out[t] = (float)(sum_h relu(q_h.k_t)
  * * w_h) * d^-1/2 h^-1/2, with the reference's double reduction tree. */
