@@ -1098,6 +1098,9 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
 // expert-parallel layer. The prefill bucketing runs with the shared expert as
 // one more bucket and one pair per row; each row's result is the same bits
 // as the layer's decode / prefill paths give that (token, expert) pair.
+// Tile width from the rows per expert: a few rows per expert (decode-like
+// batches) stream weights best through the narrow decode tiles, many rows
+// (prefill-like) through 256-column tiles.
 static MxMoeShape mxrows_shape(const dsv4cu_moe *L, int nrows)
 {
     MxMoeShape s = mxpf_shape(L, 1, nrows, MX_TERMS);
@@ -1105,6 +1108,19 @@ static MxMoeShape mxrows_shape(const dsv4cu_moe *L, int nrows)
     s.has_shared = 0;
     s.npairs = nrows;
     s.nbmax = min(nrows, s.n_experts);
+    const int avg = (nrows + s.nbmax - 1) / max(1, s.nbmax);
+    if (avg <= 2) {
+        s.NB = 8;
+        s.KB = 4;
+    } else if (avg <= 4) {
+        s.NB = 16;
+        s.KB = 4;
+    } else if (avg <= 16) {
+        s.NB = 32;
+        s.KB = 2;
+    }
+    s.tpt = s.NB <= 16 ? s.NB / MX_TERMS : (s.NB / MX_TERMS) / 8 * 8;
+    s.nbb = (s.NB + 127) / 128;
     s.max_tiles = nrows / s.tpt + s.nbmax + 1;
     return s;
 }
