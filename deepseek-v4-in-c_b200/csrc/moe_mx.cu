@@ -669,8 +669,33 @@ size_t moe_mx_workspace(const dsv4cu_moe *L, int topk, int nt)
     return mxmoe_layout(mxmoe_shape(L, topk, nt, L->sms), nullptr, nullptr);
 }
 
+// Loads every tile variant the layer's calls may pick (the shared-memory
+// limit is set and the kernel loaded), so a step that first needs a variant
+// does not pay for it.
+template <class P>
+static int mxmoe_prepare_variants()
+{
+    int r = 0;
+    if (!r) r = mx_kernel_prepare<8, 4, P>();
+    if (!r) r = mx_kernel_prepare<8, 2, P>();
+    if (!r) r = mx_kernel_prepare<8, 1, P>();
+    if (!r) r = mx_kernel_prepare<16, 4, P>();
+    if (!r) r = mx_kernel_prepare<16, 2, P>();
+    if (!r) r = mx_kernel_prepare<16, 1, P>();
+    if (!r) r = mx_kernel_prepare<32, 2, P>();
+    if (!r) r = mx_kernel_prepare<32, 1, P>();
+    if (!r) r = mx_kernel_prepare<192, 1, P>();
+    if (!r) r = mx_kernel_prepare<256, 1, P>();
+    return r;
+}
+
 int moe_mx_prepare(dsv4cu_moe *L, const dsv4cu_expert *hexp)
 {
+    {
+        int r = mxmoe_prepare_variants<MoeGateUp>();
+        if (!r) r = mxmoe_prepare_variants<MoeDown>();
+        if (r) return r;
+    }
     L->mx_ok = 0;
     L->mx_block = nullptr;
     L->sms = 148;

@@ -57,6 +57,76 @@ __device__ int block_exscan(int v, int *out_prefix, int *sh_warp)
     return total;
 }
 
+// Bitonic sort of sel[0 .. sort_n) into descending order, all 1024 threads.
+// For 64 <= sort_n <= 2048, warp w holds elements 64 w + l and 64 w + 32 + l
+// in registers: stages of stride 32 compare a lane's pair, strides below 32
+// exchange with lane l ^ stride, and only strides of 64 and more go through
+// shared memory (15 barrier stages for 2048 instead of 66).
+__device__ void bitonic_desc(unsigned long long *sel, int sort_n)
+{
+    const int tid = threadIdx.x;
+    auto smem_stage = [&](int size, int stride) {
+        for (int i = tid; i < (sort_n >> 1); i += blockDim.x) {
+            const int lo = 2 * i - (i & (stride - 1));
+            const int hi = lo + stride;
+            const bool desc = ((lo & size) == 0);
+            const unsigned long long a = sel[lo], b = sel[hi];
+            if ((a < b) == desc) { sel[lo] = b; sel[hi] = a; }
+        }
+        __syncthreads();
+    };
+    if (sort_n < 64 || sort_n > 2048) {
+        for (int size = 2; size <= sort_n; size <<= 1)
+            for (int stride = size >> 1; stride > 0; stride >>= 1) smem_stage(size, stride);
+        return;
+    }
+    const int lane = tid & 31, warp = tid >> 5;
+    const bool live = warp * 64 < sort_n;
+    const int i0 = warp * 64 + lane, i1 = i0 + 32;
+    unsigned long long v0 = 0ull, v1 = 0ull;
+    if (live) {
+        v0 = sel[i0];
+        v1 = sel[i1];
+    }
+    for (int size = 2; size <= sort_n; size <<= 1) {
+        int stride = size >> 1;
+        if (stride >= 64) {
+            if (live) {
+                sel[i0] = v0;
+                sel[i1] = v1;
+            }
+            __syncthreads();
+            for (; stride >= 64; stride >>= 1) smem_stage(size, stride);
+            if (live) {
+                v0 = sel[i0];
+                v1 = sel[i1];
+            }
+        }
+        if (!live) continue;
+        for (; stride > 0; stride >>= 1) {
+            if (stride == 32) {
+                const bool desc = (i0 & size) == 0;
+                const unsigned long long hi = v0 > v1 ? v0 : v1, lo = v0 > v1 ? v1 : v0;
+                v0 = desc ? hi : lo;
+                v1 = desc ? lo : hi;
+            } else {
+                const bool lower = (lane & stride) == 0;
+                const unsigned long long o0 = __shfl_xor_sync(0xFFFFFFFFu, v0, stride);
+                const unsigned long long o1 = __shfl_xor_sync(0xFFFFFFFFu, v1, stride);
+                const bool d0 = (i0 & size) == 0, d1 = (i1 & size) == 0;
+                // the lower index of a descending pair keeps the larger value
+                v0 = (lower == d0) ? (v0 > o0 ? v0 : o0) : (v0 < o0 ? v0 : o0);
+                v1 = (lower == d1) ? (v1 > o1 ? v1 : o1) : (v1 < o1 ? v1 : o1);
+            }
+        }
+    }
+    if (live) {
+        sel[i0] = v0;
+        sel[i1] = v1;
+    }
+    __syncthreads();
+}
+
 // Radix digits, most significant first: 11 + 11 + 10 bits.
 constexpr int TOPK_BINS = 2048;
 __device__ __constant__ int topk_shift[3] = {21, 10, 0};
@@ -181,18 +251,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(const float *__restr
     __syncthreads();
 
     // --- bitonic sort, descending
-    for (int size = 2; size <= sort_n; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < (sort_n >> 1); i += blockDim.x) {
-                const int lo = 2 * i - (i & (stride - 1));
-                const int hi = lo + stride;
-                const bool desc = ((lo & size) == 0);
-                const unsigned long long a = sel[lo], b = sel[hi];
-                if ((a < b) == desc) { sel[lo] = b; sel[hi] = a; }
-            }
-            __syncthreads();
-        }
-    }
+    bitonic_desc(sel, sort_n);
     for (int i = tid; i < k; i += blockDim.x) out[i] = (int)(0xFFFFFFFFu - (uint32_t)(sel[i] & 0xFFFFFFFFull));
 }
 
@@ -251,11 +310,19 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
         }
         cluster.sync();                           // every CTA's histogram is complete
         const int dA = nb - 1 - 2 * tid, dB = dA - 1;
-        int cA = 0, cB = 0;
+        // all remote loads in flight before the sums
+        int ra[TOPK_CL], rb[TOPK_CL];
+#pragma unroll
         for (int r = 0; r < TOPK_CL; r++) {
             const int *rh = cluster.map_shared_rank(hb, r);
-            if (dA >= 0) cA += rh[dA];
-            if (dB >= 0) cB += rh[dB];
+            ra[r] = dA >= 0 ? rh[dA] : 0;
+            rb[r] = dB >= 0 ? rh[dB] : 0;
+        }
+        int cA = 0, cB = 0;
+#pragma unroll
+        for (int r = 0; r < TOPK_CL; r++) {
+            cA += ra[r];
+            cB += rb[r];
         }
         const int need = s_need;
         int above;
@@ -340,18 +407,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
         for (int i = k + tid; i < sort_n; i += blockDim.x) sel[i] = 0ull;
     cluster.sync();                               // CTA 0 holds all k picks
     if (rank != 0) return;
-    for (int size = 2; size <= sort_n; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = tid; i < (sort_n >> 1); i += blockDim.x) {
-                const int lo = 2 * i - (i & (stride - 1));
-                const int hi = lo + stride;
-                const bool desc = ((lo & size) == 0);
-                const unsigned long long a = sel[lo], b = sel[hi];
-                if ((a < b) == desc) { sel[lo] = b; sel[hi] = a; }
-            }
-            __syncthreads();
-        }
-    }
+    bitonic_desc(sel, sort_n);
     for (int i = tid; i < k; i += blockDim.x) out[i] = (int)(0xFFFFFFFFu - (uint32_t)(sel[i] & 0xFFFFFFFFull));
 }
 
