@@ -117,6 +117,7 @@ class Clocks:
                                       stdout=self.f, stderr=subprocess.DEVNULL)
         except Exception:
             self.p = None
+        time.sleep(0.3)            # the sampler is running before the timed region starts
 
     def stop(self):
         if not self.p:
@@ -269,23 +270,19 @@ def run_ours(args, rank, local_rank, world):
         iso.append(a.elapsed_time(b))
     del flush
 
-    # ---- e2e through the public API from pinned host buffers, back to back
+    # ---- e2e through the public API from pinned host buffers, back to back:
+    # dsv4cu_moe_decode_host copies x and logits in, runs the step and copies
+    # the output back, all on the stream
     hx = torch.from_numpy(xs).pin_memory()
     hl = torch.from_numpy(lgs).pin_memory()
     hout = torch.empty((n_steps, HIDDEN), dtype=torch.float32).pin_memory()
-    gx = torch.empty((1, HIDDEN), dtype=torch.float32, device="cuda")
-    gl = torch.empty((1, NE), dtype=torch.float32, device="cuda")
-    go = torch.empty((1, HIDDEN), dtype=torch.float32, device="cuda")
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     e0.record()
     for k in range(args.steps):
         i = args.warmup + k
-        gx.copy_(hx[i:i + 1], non_blocking=True)
-        gl.copy_(hl[i:i + 1], non_blocking=True)
-        dev.moe_decode(layers[i % D_LAYERS], go, gx, gl, TOPK, ROUTE_SCALE, LIMIT, 1)
-        hout[i].copy_(go[0], non_blocking=True)
+        dev.moe_decode_host(layers[i % D_LAYERS], hout[i], hx[i], hl[i], TOPK, ROUTE_SCALE, LIMIT, 1)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
@@ -326,7 +323,7 @@ def run_ours(args, rank, local_rank, world):
                      "swiglu_down_combine_gbs": round((STEP_BYTES - PHASE1_BYTES) / (ph_ms[2] * 1e-3) / 1e9, 1)},
         "e2e": {"value": round(world * args.steps / (e2e_ms * 1e-3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": (HIDDEN + NE) * 4, "d2h_bytes_per_step": HIDDEN * 4,
-                "api": "dsv4cu_moe_decode (include/dsv4cu.h)"},
+                "api": "dsv4cu_moe_decode_host (include/dsv4cu.h): host x/logits in, host output back"},
         "gpu_launches": 5 * args.steps,
         "clocks": clk,
     }
@@ -844,7 +841,7 @@ def run_gemv(args, rank, local_rank, world):
     return res if rank == 0 else None
 
 
-G1_CPU_SETS = 8      # host copies rotated by the CPU legs: 411 MB, beyond a server L3
+G1_CPU_SETS = 32     # host copies rotated by the CPU legs: 1.6 GB, beyond any host cache
 
 
 def cpu_gemv_setup():
@@ -880,7 +877,7 @@ def cpu_gemv_baseline(seconds):
     n, dt = cpu_gemv_time(ref, qs, xs, seconds, 4000)
     return {"value": round(n * G1_BYTES / dt / 1e9, 3), "unit": "GB/s", "cores": int(os.environ["OMP_NUM_THREADS"]),
             "kind": "reference", "sample": f"{n} calls of the reference's dsv4_mmq on config 1 ({dt:.2f} s), "
-                                           f"{G1_CPU_SETS} distinct host matrices (411 MB) in turn"}
+                                           f"{G1_CPU_SETS} distinct host matrices ({G1_CPU_SETS * 51.4:.0f} MB) in turn"}
 
 
 def run_gemv_reference(args, rank, world):
@@ -921,6 +918,7 @@ I4_WORKLOAD = ("config4: indexer q 64 heads x 128 and 32768 keys, e4m3 with one 
 I4_SCORE_BYTES = I4_N * (I4_D + 4) + I4_H * (I4_D + 8) + I4_N * 4          # keys + scales, q, w, scores out
 I4_TOPK_BYTES = I4_N * 4 + I4_TOPK * 4
 I4_ATTN_BYTES = I4_TOPK * (I4_AD * 2 + 4) + I4_AH * (I4_AD * 8 + 4)        # picked bf16 rows + idx, q/o, sinks
+I4_FP64_PEAK = 40.0                                      # TFLOP/s, nominal
 
 
 def i4_quant_rows(a):
@@ -1051,8 +1049,8 @@ def run_indexer(args, rank, local_rank, world):
     peak, peak_kind = load_peaks()
     names = ["indexer_score_fp8", "topk", "sparse_attn"]
     nbytes = [I4_SCORE_BYTES, I4_TOPK_BYTES, I4_ATTN_BYTES]
-    top = int(np.argmax(ph))
-    achieved = nbytes[top] / (ph[top] * 1e-3) / 1e9
+    # The score launch is FP64 tensor-core work (exact dots): 2 H D N flops.
+    score_tflops = 2.0 * I4_H * I4_D * I4_N / (ph[0] * 1e-3) / 1e12
     ms = total_ms / args.steps
     res = {
         "metric": I4_METRIC, "value": round(world * 1e3 / ms, 1), "unit": "steps/s", "n_gpus": world,
@@ -1064,11 +1062,14 @@ def run_indexer(args, rank, local_rank, world):
                    "l2": f"inputs larger than L2: {I4_CTX} independent contexts (4.3 MB keys + 37.7 MB KV each) "
                          "used in turn, steps back to back",
                    "host_enqueue_ms_per_step": round(host_ms / args.steps, 5)},
-        "roofline": {"bound": "hbm", "kernel": names[top], "achieved": round(achieved, 1), "peak": peak,
-                     "peak_source": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
-                     "algorithmic_bytes": nbytes[top],
+        "roofline": {"bound": "tensor", "kernel": "indexer_dmma_kernel (FP64 mma.m8n8k4 dots, exact)",
+                     "achieved": round(score_tflops, 2), "peak": I4_FP64_PEAK,
+                     "peak_source": "nominal B200 FP64 tensor rate (no measured FP64 figure)", "unit": "TFLOP/s",
+                     "frac": round(score_tflops / I4_FP64_PEAK, 4), "traffic": None,
+                     "algorithmic_flops": 2 * I4_H * I4_D * I4_N,
                      "kernel_ms": {n: round(v, 5) for n, v in zip(names, ph)},
-                     "kernel_gbs": {n: round(b / (v * 1e-3) / 1e9, 1) for n, b, v in zip(names, nbytes, ph)}},
+                     "kernel_gbs": {n: round(b / (v * 1e-3) / 1e9, 1) for n, b, v in zip(names, nbytes, ph)},
+                     "hbm_peak": peak},
         "e2e": {"value": round(world * args.steps / (e2e_ms * 1e-3), 1), "unit": "steps/s",
                 "h2d_bytes_per_step": int(q8[0].nbytes + qs[0].nbytes + w[0].nbytes + qa[0].nbytes),
                 "d2h_bytes_per_step": int(go.numel() * 4),

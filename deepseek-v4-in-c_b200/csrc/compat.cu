@@ -45,6 +45,7 @@ struct HostState {
     // matrices, keyed by the device weight address.
     std::map<uintptr_t, dsv4cu::MxMat> mx;
     DevBuf buf[8];
+    DevBuf pin[2];   // pinned host staging for activations in / results out
 };
 
 HostState &S()
@@ -223,6 +224,26 @@ void *buf(int i, size_t bytes)
     return b.p;
 }
 
+// Pinned host staging buffer i (grown on demand): a copy between it and the
+// device is a plain DMA, where a pageable buffer costs a driver-side staging
+// copy and synchronisation per call.
+void *pinned(int i, size_t bytes)
+{
+    DevBuf &b = S().pin[i];
+    if (bytes == 0) bytes = 16;
+    if (b.n < bytes) {
+        if (b.p) {
+            cudaStreamSynchronize(S().st);
+            cudaFreeHost(b.p);
+        }
+        b.p = nullptr;
+        b.n = 0;
+        if (cudaHostAlloc(&b.p, bytes, cudaHostAllocDefault) != cudaSuccess) return nullptr;
+        b.n = bytes;
+    }
+    return b.p;
+}
+
 void *buf_or_die(int i, size_t bytes)
 {
     void *p = buf(i, bytes);
@@ -314,12 +335,15 @@ int mmq_host(float *y, const float *x, const DSV4QMat *m, int nt)
     if (r) return r;
     const size_t xb = (size_t)nt * m->cols * 4, yb = (size_t)nt * m->rows * 4;
     float *dx = (float *)buf(0, xb), *dy = (float *)buf(1, yb);
-    if (!dx || !dy) return dsv4cu_set_error(DSV4CU_ERR_NOMEM, "staging");
-    DSV4CU_CUDA_TRY(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, s.st));
+    float *px = (float *)pinned(0, xb), *py = (float *)pinned(1, yb);
+    if (!dx || !dy || !px || !py) return dsv4cu_set_error(DSV4CU_ERR_NOMEM, "staging");
+    memcpy(px, x, xb);
+    DSV4CU_CUDA_TRY(cudaMemcpyAsync(dx, px, xb, cudaMemcpyHostToDevice, s.st));
     r = mmq_dev(dy, dx, &dq, nt);
     if (r) return r;
-    DSV4CU_CUDA_TRY(cudaMemcpyAsync(y, dy, yb, cudaMemcpyDeviceToHost, s.st));
+    DSV4CU_CUDA_TRY(cudaMemcpyAsync(py, dy, yb, cudaMemcpyDeviceToHost, s.st));
     DSV4CU_CUDA_TRY(cudaStreamSynchronize(s.st));
+    memcpy(y, py, yb);
     return DSV4CU_OK;
 }
 

@@ -723,3 +723,41 @@ extern "C" int dsv4cu_moe_rows(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *
     if (r) return r;
     return moe_mx_rows(layer, y, x, ldx, ids, nrows, limit, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream);
 }
+
+// Host buffers in and out, all on the stream: x and logits are copied into
+// staging after the step's workspace, the step runs, the output is copied
+// back. Nothing is synchronised; pinned host buffers make the copies
+// asynchronous (pageable ones work, with the driver's own staging).
+extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out_host,
+                                      const float *x_host, const float *logits_host, int topk, float route_scale,
+                                      float limit, int nt, void *stream)
+{
+    if (!ctx || !layer || !out_host || !x_host || !logits_host)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode_host: NULL argument");
+    if (nt < 1 || nt > MOE_MAX_NT) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode_host: nt %d", nt);
+    if (topk < 1 || topk > MOE_MAX_TOPK || topk > layer->n_experts)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode_host: topk %d", topk);
+    const size_t need = layer->mx_ok ? moe_mx_workspace(layer, topk, nt)
+                                     : moe_decode_workspace(nt, topk, layer->n_experts, layer->hidden, layer->inter,
+                                                            layer->has_shared);
+    const size_t xb = (size_t)nt * layer->hidden * 4, lb = (size_t)nt * layer->n_experts * 4;
+    const size_t base = dsv4cu_align256(need);
+    void *ws = nullptr;
+    int r = dsv4cu_ws_get(ctx, base + dsv4cu_align256(xb) * 2 + dsv4cu_align256(lb), &ws);
+    if (r) return r;
+    float *dx = (float *)((char *)ws + base);
+    float *dl = (float *)((char *)dx + dsv4cu_align256(xb));
+    float *dout = (float *)((char *)dl + dsv4cu_align256(lb));
+    cudaStream_t st = (cudaStream_t)stream;
+    DSV4CU_CUDA_TRY(cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, st));
+    DSV4CU_CUDA_TRY(cudaMemcpyAsync(dl, logits_host, lb, cudaMemcpyHostToDevice, st));
+    if (layer->mx_ok)
+        r = moe_mx_decode(layer, dout, dx, dl, nullptr, nullptr, nullptr, topk, route_scale, limit, nt, nullptr,
+                          nullptr, ws, ctx->counters, ctx->status, ctx->sm_count, st, nullptr);
+    else
+        r = moe_decode_run(layer, dout, dx, dl, nullptr, nullptr, nullptr, topk, route_scale, limit, nt, nullptr,
+                           nullptr, ws, ctx->counters, ctx->status, st, nullptr);
+    if (r) return r;
+    DSV4CU_CUDA_TRY(cudaMemcpyAsync(out_host, dout, xb, cudaMemcpyDeviceToHost, st));
+    return DSV4CU_OK;
+}

@@ -71,6 +71,7 @@ def lib() -> C.CDLL:
             "dsv4cu_moe_prefill": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, i, vp, vp, vp]),
             "dsv4cu_moe_prefill_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, i, vp, vp, vp, vp]),
             "dsv4cu_moe_decode_ev": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp, vp]),
+            "dsv4cu_moe_decode_host": (i, [vp, vp, vp, vp, vp, i, f, f, i, vp]),
             "dsv4cu_moe_rows_workspace": (sz, [vp, i]),
             "dsv4cu_moe_rows": (i, [vp, vp, vp, vp, C.c_long, vp, i, f, vp]),
             "dsv4cu_ep_pack": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, i, vp]),
@@ -349,6 +350,12 @@ class Device:
         else:
             evp = _event_handles(events)
             check(self.L.dsv4cu_moe_decode_ev(*args, evp), "dsv4cu_moe_decode_ev")
+
+    def moe_decode_host(self, layer, out, x, logits, topk, route_scale, limit, nt):
+        """dsv4cu_moe_decode_host on host tensors / arrays (pinned for asynchronous copies)."""
+        hp = (lambda a: a.data_ptr()) if hasattr(x, "data_ptr") else (lambda a: a.ctypes.data)
+        check(self.L.dsv4cu_moe_decode_host(self.ctx, layer, hp(out), hp(x), hp(logits), topk, route_scale, limit,
+                                            nt, self.stream()), "dsv4cu_moe_decode_host")
 
     def moe_rows(self, layer, y, x, ldx, ids, nrows, limit):
         """y[r] = expert ids[r] (n_experts = the shared expert) on row r of x (dsv4cu_moe_rows)."""

@@ -342,3 +342,21 @@ def test_moe_prefill_config3_sampled(dev, orc):
         want, _, _ = fx.oracle_out(orc, x[t_], logits[t_], 8, 1.5, 10.0)
         assert rel_err(out[t_], want) <= 1e-4, (t_, rel_err(out[t_], want))
     fx.close()
+
+
+def test_moe_decode_host_matches_device_call(dev):
+    """dsv4cu_moe_decode_host (host buffers, copies on the stream) gives the
+    same bits as dsv4cu_moe_decode on device buffers."""
+    t = __import__("torch")
+    fx = MoeFixture(dev, 16, 512, 256, shared_fmt=2, seed=91)
+    rng = np.random.default_rng(91)
+    nt = 3
+    x = pack.bf16_round(rng.standard_normal((nt, 512)).astype(np.float32))
+    lg = pack.bf16_round(rng.standard_normal((nt, 16)).astype(np.float32))
+    want, _, _ = run(dev, fx, x, lg, 4, 1.5, 10.0)
+    hx, hl = t.from_numpy(x).pin_memory(), t.from_numpy(lg).pin_memory()
+    hout = t.full((nt, 512), float("nan"), dtype=t.float32).pin_memory()
+    dev.moe_decode_host(fx.layer, hout, hx, hl, 4, 1.5, 10.0, nt)
+    t.cuda.synchronize()
+    assert np.array_equal(hout.numpy().view(np.uint32), want.view(np.uint32))
+    fx.close()
