@@ -626,43 +626,6 @@ static int mxmoe_dispatch(int NB, int KB, const CUtensorMap &tb, const typename 
     }
 }
 
-// The B-operand maps of a step depend only on the workspace address and the
-// shape: encoded once and reused (the encode is a driver call per map).
-static int cached_bmap(CUtensorMap *out, const void *base, uint64_t inner, uint64_t outer, uint32_t box)
-{
-    struct Entry {
-        const void *base;
-        uint64_t inner, outer;
-        uint32_t box;
-        int device;
-        CUtensorMap map;
-    };
-    static std::mutex mu;
-    static Entry cache[16];
-    static int next = 0;
-    int dev = 0;
-    DSV4CU_CUDA_TRY(cudaGetDevice(&dev));
-    std::lock_guard<std::mutex> lk(mu);
-    for (const Entry &e : cache)
-        if (e.base == base && e.inner == inner && e.outer == outer && e.box == box && e.device == dev) {
-            *out = e.map;
-            return DSV4CU_OK;
-        }
-    Entry &e = cache[next];
-    int r = mx_encode_kmajor(&e.map, base, false, inner, outer, inner, box);
-    if (r) {
-        e.base = nullptr;
-        return r;
-    }
-    e.base = base;
-    e.inner = inner;
-    e.outer = outer;
-    e.box = box;
-    e.device = dev;
-    next = (next + 1) % 16;
-    *out = e.map;
-    return DSV4CU_OK;
-}
 
 size_t moe_mx_workspace(const dsv4cu_moe *L, int topk, int nt)
 {
@@ -799,8 +762,8 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     const int g1 = min(sms, s.max_tiles * 2 * RT), g2 = min(sms, s.max_tiles * RTH);
 
     CUtensorMap tb1, tb2;
-    int r = cached_bmap(&tb1, ws.xq1, (uint64_t)s.hidden, (uint64_t)s.max_tiles * s.NB, (uint32_t)s.NB);
-    if (!r) r = cached_bmap(&tb2, ws.xq2, (uint64_t)s.inter, (uint64_t)s.max_tiles * s.NB, (uint32_t)s.NB);
+    int r = mx_cached_bmap(&tb1, ws.xq1, (uint64_t)s.hidden, (uint64_t)s.max_tiles * s.NB, (uint32_t)s.NB);
+    if (!r) r = mx_cached_bmap(&tb2, ws.xq2, (uint64_t)s.inter, (uint64_t)s.max_tiles * s.NB, (uint32_t)s.NB);
     if (r) return r;
 
     MoeGateUp::Params pg;

@@ -60,7 +60,10 @@ constexpr int MX_TCACHE = 32;
 // slack and 4 KB for the kernel's static shared variables.
 constexpr int MX_SMEM_BUDGET = 227 * 1024 - 1024 - 4096;
 
-template <int NB, int KB>
+// STG: ring stages (0 = as many as the shared-memory budget holds). A small
+// ring (a few stages) leaves room on the SM for the next kernel's CTA, which
+// can then fetch its first weight tiles while this kernel finishes.
+template <int NB, int KB, int STG = 0>
 struct MxCfg {
     static constexpr int NBB = (NB + 127) / 128;          // 128-column scale blocks of B
     static constexpr int A_BOX = 128 * 128;
@@ -72,7 +75,8 @@ struct MxCfg {
     static constexpr int OFF_SFA = OFF_B + KB * B_BOX;
     static constexpr int OFF_SFB = OFF_SFA + KB * SFA_BOX;
     static constexpr int STAGE = ((OFF_SFB + KB * SFB_BOX + 1023) / 1024) * 1024;
-    static constexpr int STAGES = (MX_SMEM_BUDGET / STAGE) < 16 ? (MX_SMEM_BUDGET / STAGE) : 16;
+    static constexpr int FIT = (MX_SMEM_BUDGET / STAGE) < 16 ? (MX_SMEM_BUDGET / STAGE) : 16;
+    static constexpr int STAGES = STG > 0 && STG < FIT ? STG : FIT;
     static constexpr int SMEM = STAGES * STAGE + 1024;
     static constexpr int SF_SLOTS = 2 * KB < 4 ? 4 : 2 * KB;
     static constexpr int SFB_COLS = 4 * NBB;
@@ -170,11 +174,11 @@ DSV4CU_DEV int mx_sfb_offset(int n, int kb)
     return (n >> 7) * 512 + (n & 31) * 16 + ((n & 127) >> 5) * 4 + kb;
 }
 
-template <int NB, int KB, class P>
+template <int NB, int KB, class P, int STG = 0>
 __global__ void __launch_bounds__(MX_THREADS, 1)
     mx_kernel(const __grid_constant__ CUtensorMap tb, const __grid_constant__ typename P::Params p)
 {
-    using C = MxCfg<NB, KB>;
+    using C = MxCfg<NB, KB, STG>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t mx_smem_raw[];
     __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], accf[2], acce[2], drain;
@@ -438,15 +442,15 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 }
 
 // Dynamic shared memory of mx_kernel<NB, KB, P>, set once per device.
-template <int NB, int KB, class P>
+template <int NB, int KB, class P, int STG = 0>
 static int mx_kernel_prepare()
 {
     static volatile int done[64];
     int dev = 0;
     DSV4CU_CUDA_TRY(cudaGetDevice(&dev));
     if (dev >= 0 && dev < 64 && done[dev]) return DSV4CU_OK;
-    DSV4CU_CUDA_TRY(cudaFuncSetAttribute(mx_kernel<NB, KB, P>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         MxCfg<NB, KB>::SMEM));
+    DSV4CU_CUDA_TRY(cudaFuncSetAttribute(mx_kernel<NB, KB, P, STG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         MxCfg<NB, KB, STG>::SMEM));
     if (dev >= 0 && dev < 64) done[dev] = 1;
     return DSV4CU_OK;
 }

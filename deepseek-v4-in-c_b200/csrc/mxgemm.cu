@@ -17,6 +17,7 @@
 // preparation, tensor-map encoding, column tiling) and the dense problem: a
 // grid of 128-row x NB-column tiles over one matrix.
 #include <cuda.h>
+#include <mutex>
 #include <stdlib.h>
 #include <string.h>
 
@@ -219,6 +220,44 @@ int mx_encode_kmajor(CUtensorMap *map, const void *base, bool fp4, uint64_t inne
     return DSV4CU_OK;
 }
 
+// The B-operand maps of a step depend only on the workspace address and the
+// shape: encoded once and reused (the encode is a driver call per map).
+int mx_cached_bmap(CUtensorMap *out, const void *base, uint64_t inner, uint64_t outer, uint32_t box)
+{
+    struct Entry {
+        const void *base;
+        uint64_t inner, outer;
+        uint32_t box;
+        int device;
+        CUtensorMap map;
+    };
+    static std::mutex mu;
+    static Entry cache[16];
+    static int next = 0;
+    int dev = 0;
+    DSV4CU_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    for (const Entry &e : cache)
+        if (e.base == base && e.inner == inner && e.outer == outer && e.box == box && e.device == dev) {
+            *out = e.map;
+            return DSV4CU_OK;
+        }
+    Entry &e = cache[next];
+    int r = mx_encode_kmajor(&e.map, base, false, inner, outer, inner, box);
+    if (r) {
+        e.base = nullptr;
+        return r;
+    }
+    e.base = base;
+    e.inner = inner;
+    e.outer = outer;
+    e.box = box;
+    e.device = dev;
+    next = (next + 1) % 16;
+    *out = e.map;
+    return DSV4CU_OK;
+}
+
 bool mx_supported(const dsv4cu_qmat *q)
 {
     if (!q || !q->w || !q->s || q->rows <= 0 || q->cols <= 0 || q->cols % 128) return false;
@@ -345,16 +384,22 @@ size_t mx_workspace(const MxMat *m, int nt, int terms, int sms)
     return best;
 }
 
-template <int NB, int KB>
+template <int NB, int KB, int STG = 0>
 static int dense_launch(const CUtensorMap &tb, const DenseMx::Params &p, int sms, cudaStream_t st)
 {
-    int r = mx_kernel_prepare<NB, KB, DenseMx>();
+    int r = mx_kernel_prepare<NB, KB, DenseMx, STG>();
     if (r) return r;
     const int tiles = p.tiles_m * p.tiles_n * (p.cross ? p.S : 1);
-    DSV4CU_CUDA_TRY(launch_pdl(mx_kernel<NB, KB, DenseMx>, dim3(tiles < sms ? tiles : sms), dim3(MX_THREADS),
-                               MxCfg<NB, KB>::SMEM, st, tb, p));
+    DSV4CU_CUDA_TRY(launch_pdl(mx_kernel<NB, KB, DenseMx, STG>, dim3(tiles < sms ? tiles : sms), dim3(MX_THREADS),
+                               MxCfg<NB, KB, STG>::SMEM, st, tb, p));
     return DSV4CU_OK;
 }
+
+// One- and two-token products with the automatic tiling: 8-column tiles with
+// a 5-stage ring of single K chunks (91 KB), one CTA per SM. The SM keeps
+// room for the next product's CTA, which fetches its first weight tiles
+// while this one finishes (the weights never depend on the previous kernel).
+constexpr int MX_GEMV_STAGES = 5;
 
 static int dense_dispatch(const MxTiling &t, const CUtensorMap &tb, const DenseMx::Params &p, int sms,
                           cudaStream_t st);
@@ -403,10 +448,11 @@ int mx_gemm(const MxMat *m, float *y, const float *x, int nt, int terms, int nb_
                                    nt, K, K, terms, t.tpt, t.NB, xq, sfb, cnt, ncnt));
     }
     CUtensorMap tb;
-    int r = mx_encode_kmajor(&tb, xq, false, (uint64_t)K, (uint64_t)t.tiles_n * t.NB, (uint64_t)K, (uint32_t)t.NB);
+    int r = mx_cached_bmap(&tb, xq, (uint64_t)K, (uint64_t)t.tiles_n * t.NB, (uint32_t)t.NB);
     if (r) return r;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
-    r = dense_dispatch(t, tb, p, sms, st);
+    if (t.NB == 8 && nb_req == 0 && kb_req == 0) r = dense_launch<8, 1, MX_GEMV_STAGES>(tb, p, sms, st);
+    else r = dense_dispatch(t, tb, p, sms, st);
     if (r) return r;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
     return DSV4CU_OK;

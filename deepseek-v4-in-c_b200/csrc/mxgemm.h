@@ -40,6 +40,10 @@ int mx_prepare(MxMat *m, const dsv4cu_qmat *q, uint8_t *sfa_buf, cudaStream_t st
 void mx_release(MxMat *m);
 int mx_encode_kmajor(CUtensorMap *map, const void *base, bool fp4, uint64_t inner, uint64_t outer,
                      uint64_t row_bytes, uint32_t box_rows);
+// The B-operand tensor map of an activation buffer (e4m3 rows of `inner`
+// bytes, box_rows-row boxes), from a small per-process cache keyed by
+// address, shape and device: workspace buffers repeat call after call.
+int mx_cached_bmap(CUtensorMap *out, const void *base, uint64_t inner, uint64_t outer, uint32_t box);
 MxTiling mx_tiling(int nt, int terms, int nb_req, int kb_req, int kc);
 // Split-K segments of one dense product: at most MX_MAX_SEGMENTS.
 constexpr int MX_MAX_SEGMENTS = 16;
