@@ -304,8 +304,8 @@ def run_ours(args, rank, local_rank, world):
     del flush
 
     # ---- e2e through the public API from pinned host buffers, back to back:
-    # dsv4cu_moe_decode_host copies x and logits in, runs the step and copies
-    # the output back, all on the stream
+    # dsv4cu_moe_decode_host runs the step with its kernels reading x and the
+    # logits from, and writing the output to, the page-locked host buffers
     hx = torch.from_numpy(xs).pin_memory()
     hl = torch.from_numpy(lgs).pin_memory()
     hout = torch.empty((n_steps, HIDDEN), dtype=torch.float32).pin_memory()
@@ -360,7 +360,8 @@ def run_ours(args, rank, local_rank, world):
                      "swiglu_down_combine_gbs": round((STEP_BYTES - PHASE1_BYTES) / (ph_ms[2] * 1e-3) / 1e9, 1)},
         "e2e": {"value": round(world * args.steps / (e2e_ms * 1e-3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": (HIDDEN + NE) * 4, "d2h_bytes_per_step": HIDDEN * 4,
-                "api": "dsv4cu_moe_decode_host (include/dsv4cu.h): host x/logits in, host output back"},
+                "api": "dsv4cu_moe_decode_host (include/dsv4cu.h): pinned host x/logits read and the output "
+                       "written across the bus by the step's kernels"},
         "gpu_launches": 5 * args.steps,
         "clocks": clk,
     }

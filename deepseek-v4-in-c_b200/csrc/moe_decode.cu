@@ -724,10 +724,24 @@ extern "C" int dsv4cu_moe_rows(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *
     return moe_mx_rows(layer, y, x, ldx, ids, nrows, limit, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream);
 }
 
-// Host buffers in and out, all on the stream: x and logits are copied into
-// staging after the step's workspace, the step runs, the output is copied
-// back. Nothing is synchronised; pinned host buffers make the copies
-// asynchronous (pageable ones work, with the driver's own staging).
+// Device address of a page-locked, mapped host buffer (cudaHostAlloc /
+// cudaHostRegister with unified addressing), or NULL for pageable memory.
+static const void *mapped_host(const void *p)
+{
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return (a.type == cudaMemoryTypeHost && a.devicePointer) ? a.devicePointer : nullptr;
+}
+
+// Host buffers in and out, all on the stream, nothing synchronised. With
+// page-locked host buffers on the tensor-core path the step's kernels read x
+// and the logits and write the output across the bus themselves (no copy
+// operations between the step's launches); otherwise x and logits are
+// copied into staging after the step's workspace and the output is copied
+// back.
 extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out_host,
                                       const float *x_host, const float *logits_host, int topk, float route_scale,
                                       float limit, int nt, void *stream)
@@ -741,6 +755,17 @@ extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, 
                                      : moe_decode_workspace(nt, topk, layer->n_experts, layer->hidden, layer->inter,
                                                             layer->has_shared);
     const size_t xb = (size_t)nt * layer->hidden * 4, lb = (size_t)nt * layer->n_experts * 4;
+    if (layer->mx_ok) {
+        const void *mx = mapped_host(x_host), *ml = mapped_host(logits_host), *mo = mapped_host(out_host);
+        if (mx && ml && mo) {
+            void *ws = nullptr;
+            int r = dsv4cu_ws_get(ctx, need, &ws);
+            if (r) return r;
+            return moe_mx_decode(layer, (float *)mo, (const float *)mx, (const float *)ml, nullptr, nullptr, nullptr,
+                                 topk, route_scale, limit, nt, nullptr, nullptr, ws, ctx->counters, ctx->status,
+                                 ctx->sm_count, (cudaStream_t)stream, nullptr);
+        }
+    }
     const size_t base = dsv4cu_align256(need);
     void *ws = nullptr;
     int r = dsv4cu_ws_get(ctx, base + dsv4cu_align256(xb) * 2 + dsv4cu_align256(lb), &ws);

@@ -166,11 +166,13 @@ int dsv4cu_moe_decode(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
                       float route_scale, float limit, int nt, int *idx_out,
                       float *wts_out, void *stream);
 
-/* dsv4cu_moe_decode from host buffers: x_host [nt][hidden] and logits_host
- * [nt][n_experts] are copied in, the step runs, out_host [nt][hidden] is
- * copied back - all enqueued on the stream, nothing synchronised (read
- * out_host after synchronising the stream). Pinned host buffers make the
- * copies asynchronous. No bias, hash routing or index outputs. */
+/* dsv4cu_moe_decode from host buffers x_host [nt][hidden], logits_host
+ * [nt][n_experts] and out_host [nt][hidden], enqueued on the stream, nothing
+ * synchronised (read out_host after synchronising the stream). With
+ * page-locked host buffers (cudaHostAlloc, cudaHostRegister, torch
+ * pin_memory) the step's kernels read the inputs and write the output across
+ * the bus directly; with pageable buffers they are copied through device
+ * staging. No bias, hash routing or index outputs. */
 int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out_host,
                            const float *x_host, const float *logits_host, int topk,
                            float route_scale, float limit, int nt, void *stream);
