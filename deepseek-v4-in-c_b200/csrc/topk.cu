@@ -260,9 +260,12 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(const float *__restr
 // TOPK_CL CTAs. CTA c stages keys [c * span, (c + 1) * span) in its shared
 // memory; each radix pass builds per-CTA histograms, and after a cluster
 // barrier every CTA sums all of them through distributed shared memory and
-// picks the same digit (identical inputs, identical arithmetic). The ordered
-// compaction writes (key, ~index) pairs straight into CTA 0's sort buffer at
-// offsets from the CTAs' counts; CTA 0 sorts and writes the result.
+// picks the same digit (identical inputs, identical arithmetic). The first
+// pass also cuts the picks into TOPK_CL ranges of whole top digits, about
+// k / TOPK_CL picks each; the compaction sends every (key, ~index) pick to the
+// CTA of its range, and each CTA sorts its range and writes it at the range's
+// output offset. (The unique (key, ~index) order makes the arrival order
+// within a range irrelevant.)
 constexpr int TOPK_CL = 8;
 namespace cg = cooperative_groups;
 
@@ -275,7 +278,14 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
     __shared__ int cta_cnt[2];                    // this CTA's keys > T and == T
     __shared__ uint32_t s_prefix, s_mask;
     __shared__ int s_need;
-    extern __shared__ unsigned long long sel[];   // [sort_n] (used in CTA 0), then keys [span]
+    // The picks are sorted in 8 key ranges, one per CTA: ranges of top
+    // (pass-0) digits holding about k / 8 picks each. s_owner[d] = the CTA
+    // sorting digit d's picks, s_own_off[r] = where CTA r's run starts in the
+    // output, own_cnt = picks received so far (other CTAs add remotely).
+    __shared__ uint8_t s_owner[TOPK_BINS];
+    __shared__ int s_own_off[TOPK_CL + 1];
+    __shared__ int own_cnt;
+    extern __shared__ unsigned long long sel[];   // [sort_n] (this CTA's range), then keys [span]
     uint32_t *skeys = (uint32_t *)(sel + sort_n);
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
@@ -296,7 +306,8 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
             if (i < cnt) skeys[i] = float_order_key(v[u]);
         }
     }
-    if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = k; }
+    if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = k; own_cnt = 0; }
+    if (tid <= TOPK_CL) s_own_off[tid] = k;
 
     for (int pass = 0; pass < 3; pass++) {
         const int shift = topk_shift[pass], width = topk_width[pass], nb = 1 << width;
@@ -327,6 +338,21 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
         const int need = s_need;
         int above;
         block_exscan(cA + cB, &above, sh_warp);
+        if (pass == 0) {
+            // Output positions [above, above + c) belong to digit d (keys in
+            // higher digits come first); its picks go to CTA above * 8 / k.
+            const int startB = above + cA;
+            if (dA >= 0 && cA > 0 && above < k) {
+                const int r = min(TOPK_CL - 1, (int)((long)above * TOPK_CL / k));
+                s_owner[dA] = (uint8_t)r;
+                atomicMin(&s_own_off[r], above);
+            }
+            if (dB >= 0 && cB > 0 && startB < k) {
+                const int r = min(TOPK_CL - 1, (int)((long)startB * TOPK_CL / k));
+                s_owner[dB] = (uint8_t)r;
+                atomicMin(&s_own_off[r], startB);
+            }
+        }
         if (above < need && need <= above + cA + cB) {
             const bool inA = need <= above + cA;
             const int d = inA ? dA : dB;
@@ -335,6 +361,8 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
             s_mask = mask | ((uint32_t)(nb - 1) << shift);
         }
         __syncthreads();
+        if (pass == 0 && tid == 0)
+            for (int r = TOPK_CL - 1; r >= 0; r--) s_own_off[r] = min(s_own_off[r], s_own_off[r + 1]);
     }
     const uint32_t T = s_prefix;
     const int need_eq = s_need;
@@ -376,39 +404,40 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
         }
     }
     cluster.sync();                               // every CTA's counts are complete
-    int gbase = 0, ebase = 0, ngt = 0;
-    for (int r = 0; r < TOPK_CL; r++) {
-        const int *rc = cluster.map_shared_rank(cta_cnt, r);
-        const int a = rc[0], b = rc[1];
-        if (r < rank) {
-            gbase += a;
-            ebase += b;
-        }
-        ngt += a;
-    }
-    unsigned long long *sel0 = cluster.map_shared_rank(sel, 0);
-    int wgt = gbase + warp_gt[warp], weq = ebase + warp_eq[warp];
+    int ebase = 0;
+    for (int r = 0; r < rank; r++) ebase += cluster.map_shared_rank(cta_cnt, r)[1];
+    // Every key > T and the first need_eq keys == T in index order are
+    // picked; each pick goes to the CTA that sorts its key range (a slot
+    // from that CTA's counter, one remote atomic per owner and warp).
+    int weq = ebase + warp_eq[warp];
     const unsigned lt = (1u << lane) - 1u;
     for (int b = w0; b < w1; b += 32) {
         const int i = b + lane;
         const uint32_t key = i < w1 ? skeys[i] : 0u;
         const bool gt = i < w1 && key > T, eq = i < w1 && key == T;
-        const unsigned mg = __ballot_sync(0xFFFFFFFFu, gt), me = __ballot_sync(0xFFFFFFFFu, eq);
-        const unsigned long long v = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)(g0 + i));
-        if (gt) sel0[wgt + __popc(mg & lt)] = v;
-        if (eq) {
-            const int r = weq + __popc(me & lt);
-            if (r < need_eq) sel0[ngt + r] = v;
-        }
-        wgt += __popc(mg);
+        const unsigned me = __ballot_sync(0xFFFFFFFFu, eq);
+        const bool pick = gt || (eq && weq + __popc(me & lt) < need_eq);
         weq += __popc(me);
+        const int owner = pick ? (int)s_owner[key >> 21] : -1;
+        const unsigned grp = __match_any_sync(0xFFFFFFFFu, owner);
+        const int leader = __ffs(grp) - 1, before = __popc(grp & lt);
+        int base = 0;
+        if (pick && lane == leader) base = atomicAdd(cluster.map_shared_rank(&own_cnt, owner), __popc(grp));
+        base = __shfl_sync(0xFFFFFFFFu, base, leader);
+        if (pick)
+            cluster.map_shared_rank(sel, owner)[base + before] =
+                ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)(g0 + i));
     }
-    if (rank == 0)
-        for (int i = k + tid; i < sort_n; i += blockDim.x) sel[i] = 0ull;
-    cluster.sync();                               // CTA 0 holds all k picks
-    if (rank != 0) return;
-    bitonic_desc(sel, sort_n);
-    for (int i = tid; i < k; i += blockDim.x) out[i] = (int)(0xFFFFFFFFu - (uint32_t)(sel[i] & 0xFFFFFFFFull));
+    cluster.sync();                               // every CTA holds the picks of its range
+    const int m = s_own_off[rank + 1] - s_own_off[rank];
+    if (m <= 0) return;
+    int sn = 2;
+    while (sn < m) sn <<= 1;
+    for (int i = m + tid; i < sn; i += blockDim.x) sel[i] = 0ull;   // padding sorts last
+    __syncthreads();
+    bitonic_desc(sel, sn);
+    for (int i = tid; i < m; i += blockDim.x)
+        out[s_own_off[rank] + i] = (int)(0xFFFFFFFFu - (uint32_t)(sel[i] & 0xFFFFFFFFull));
 }
 
 // Shared memory above the static arrays: the sort buffer and, when they fit,
