@@ -196,3 +196,87 @@ def test_ep_world1_without_collectives():
         torch.from_numpy(x), torch.from_numpy(lg))
     want = reference_layer(orc, experts, shared, x, lg)
     assert np.array_equal(out.numpy().view(np.uint32), want.view(np.uint32))
+
+
+# ---- failure paths (host side, gloo): a peer that fails or never arrives
+# ends the other ranks' step with an error within the process-group timeout.
+
+class _FailingOps(CpuOps):
+    """Raises on one rank after routing, before the exchange."""
+
+    def __init__(self, *a, fail_rank=1, **kw):
+        super().__init__(*a, **kw)
+        self.fail_rank, self.rank = fail_rank, a[4]
+
+    def pack(self, x, idx):
+        if self.rank == self.fail_rank:
+            raise RuntimeError("injected failure before the exchange")
+        return super().pack(x, idx)
+
+
+class _BadCountsOps(CpuOps):
+    """Claims one row more for rank 0 than it sends (a corrupt count exchange)."""
+
+    def pack(self, x, idx):
+        send, counts, pair_slot = super().pack(x, idx)
+        counts = counts.clone()
+        counts[0] += 1
+        return send, counts, pair_slot
+
+
+def _failure_rank(rank, world, port, q, mode):
+    try:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        _paths()
+        import oracle
+        from ep import ExpertParallelMoE
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=8))
+        if mode == "absent" and rank == world - 1:
+            q.put((rank, "left"))
+            return                          # joins, then never takes part in the step
+        orc = oracle.Oracle()
+        experts, shared, keep = _layer()
+        x, lg = _tokens(world)
+        mine = slice(rank * NT, (rank + 1) * NT)
+        cls = {"raise": _FailingOps, "absent": CpuOps, "counts": _BadCountsOps}[mode]
+        ops = cls(orc, experts, shared, N_EXPERTS // world, rank, world)
+        try:
+            ExpertParallelMoE(ops, rank, world).forward(torch.from_numpy(x[mine]), torch.from_numpy(lg[mine]))
+            q.put((rank, "completed"))
+        except Exception as e:      # the outcome under test
+            q.put((rank, "error:" + type(e).__name__))
+    except Exception as e:
+        q.put((rank, "setup:" + repr(e)))
+
+
+@pytest.mark.parametrize("mode", ["raise", "absent", "counts"])
+def test_ep_failures_end_with_an_error(mode):
+    """No rank hangs: the failing / absent rank's peers get an exception from
+    the exchange (gloo timeout 8 s, or a size mismatch), well inside the
+    test's bound."""
+    import multiprocessing as mp
+    import time
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failure_rank, args=(r, world, port, q, mode)) for r in range(world)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert time.time() - t0 < 120
+    if mode == "raise":
+        assert res[1].startswith("error"), res
+        assert res[0].startswith("error"), res          # the peer's exchange times out
+    elif mode == "absent":
+        assert res[1] == "left" and res[0].startswith("error"), res
+    else:
+        assert any(v.startswith("error") for v in res.values()), res
