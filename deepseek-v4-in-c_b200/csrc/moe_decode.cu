@@ -736,12 +736,26 @@ static const void *mapped_host(const void *p)
     return (a.type == cudaMemoryTypeHost && a.devicePointer) ? a.devicePointer : nullptr;
 }
 
+// x and the logits from mapped host memory into device staging in one
+// coalesced pass (every load in flight at once), after the previous kernel on
+// the stream has finished (it may have written these host buffers).
+__global__ void __launch_bounds__(1024) stage_in_kernel(float4 *__restrict__ dx, const float4 *__restrict__ hx,
+                                                        long nx4, float *__restrict__ dl,
+                                                        const float *__restrict__ hl, long nl)
+{
+    pdl_wait();
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x, stride = (long)gridDim.x * blockDim.x;
+    for (long j = i; j < nx4; j += stride) dx[j] = hx[j];
+    for (long j = i; j < nl; j += stride) dl[j] = hl[j];
+    pdl_trigger();
+}
+
 // Host buffers in and out, all on the stream, nothing synchronised. With
-// page-locked host buffers on the tensor-core path the step's kernels read x
-// and the logits and write the output across the bus themselves (no copy
-// operations between the step's launches); otherwise x and logits are
-// copied into staging after the step's workspace and the output is copied
-// back.
+// page-locked host buffers on the tensor-core path one staging kernel reads
+// x and the logits across the bus and the combine writes the output straight
+// into host memory (no copy operations between the step's launches);
+// otherwise x and logits are copied into staging after the step's workspace
+// and the output is copied back.
 extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out_host,
                                       const float *x_host, const float *logits_host, int topk, float route_scale,
                                       float limit, int nt, void *stream)
@@ -755,18 +769,25 @@ extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, 
                                      : moe_decode_workspace(nt, topk, layer->n_experts, layer->hidden, layer->inter,
                                                             layer->has_shared);
     const size_t xb = (size_t)nt * layer->hidden * 4, lb = (size_t)nt * layer->n_experts * 4;
-    if (layer->mx_ok) {
+    const size_t base = dsv4cu_align256(need);
+    if (layer->mx_ok && xb % 16 == 0) {
         const void *mx = mapped_host(x_host), *ml = mapped_host(logits_host), *mo = mapped_host(out_host);
-        if (mx && ml && mo) {
+        if (mx && ml && mo && ((uintptr_t)mx & 15u) == 0) {
             void *ws = nullptr;
-            int r = dsv4cu_ws_get(ctx, need, &ws);
+            int r = dsv4cu_ws_get(ctx, base + dsv4cu_align256(xb) + dsv4cu_align256(lb), &ws);
             if (r) return r;
-            return moe_mx_decode(layer, (float *)mo, (const float *)mx, (const float *)ml, nullptr, nullptr, nullptr,
-                                 topk, route_scale, limit, nt, nullptr, nullptr, ws, ctx->counters, ctx->status,
-                                 ctx->sm_count, (cudaStream_t)stream, nullptr);
+            float *dx = (float *)((char *)ws + base);
+            float *dl = (float *)((char *)dx + dsv4cu_align256(xb));
+            const long nx4 = (long)(xb / 16), nl = (long)(lb / 4);
+            const long work = nx4 > nl ? nx4 : nl;
+            const unsigned blocks = (unsigned)((work + 1023) / 1024 < 32 ? (work + 1023) / 1024 : 32);
+            DSV4CU_CUDA_TRY(launch_pdl(stage_in_kernel, dim3(blocks), dim3(1024), 0, (cudaStream_t)stream,
+                                       (float4 *)dx, (const float4 *)mx, nx4, dl, (const float *)ml, nl));
+            return moe_mx_decode(layer, (float *)mo, dx, dl, nullptr, nullptr, nullptr, topk, route_scale, limit, nt,
+                                 nullptr, nullptr, ws, ctx->counters, ctx->status, ctx->sm_count,
+                                 (cudaStream_t)stream, nullptr);
         }
     }
-    const size_t base = dsv4cu_align256(need);
     void *ws = nullptr;
     int r = dsv4cu_ws_get(ctx, base + dsv4cu_align256(xb) * 2 + dsv4cu_align256(lb), &ws);
     if (r) return r;

@@ -170,9 +170,10 @@ int dsv4cu_moe_decode(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
  * [nt][n_experts] and out_host [nt][hidden], enqueued on the stream, nothing
  * synchronised (read out_host after synchronising the stream). With
  * page-locked host buffers (cudaHostAlloc, cudaHostRegister, torch
- * pin_memory) the step's kernels read the inputs and write the output across
- * the bus directly; with pageable buffers they are copied through device
- * staging. No bias, hash routing or index outputs. */
+ * pin_memory) one staging kernel reads the inputs across the bus and the
+ * step writes the output into host memory directly; with pageable buffers
+ * they are copied through device staging. No bias, hash routing or index
+ * outputs. */
 int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out_host,
                            const float *x_host, const float *logits_host, int topk,
                            float route_scale, float limit, int nt, void *stream);
