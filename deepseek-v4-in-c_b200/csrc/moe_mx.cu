@@ -422,6 +422,7 @@ struct MxMoeCommon {
     MxMoeWs ws;
     int nb, nbb, tpt, terms, hidden, inter;
     int *err;
+    int max_tiles, n_mats;   // bounds of the column-tile table and of the matrix index (3 x experts)
 };
 
 DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc, const uint8_t *sfb)
@@ -480,8 +481,16 @@ struct MoeDown {
     struct Params {
         MxMoeCommon c;
     };
-    static constexpr bool kPrefetchA = false;   // the experts come from the routing kernel
-    DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * (p.c.hidden >> 7); }
+    // The tile list (the routing kernel's tables) is complete before this
+    // kernel can start (its predecessors waited for that kernel), so the first
+    // weight tiles are requested before the wait for the SwiGLU operand, while
+    // the gate/up kernel's last CTAs still run. Table entries are clamped to
+    // their bounds.
+    static constexpr bool kPrefetchA = true;
+    DSV4CU_DEV static int ntiles(const Params &p)
+    {
+        return min(p.c.ws.meta[2], p.c.max_tiles) * (p.c.hidden >> 7);
+    }
     DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
     DSV4CU_DEV static int terms(const Params &p) { return p.c.terms; }
     DSV4CU_DEV static int tpt(const Params &p) { return p.c.tpt; }
@@ -489,7 +498,8 @@ struct MoeDown {
     {
         const int RTH = p.c.hidden >> 7;
         const int i = t / RTH, rt = t - i * RTH;
-        MxTile T = mxmoe_tile(p.c, i, 3 * p.c.ws.c_expert[i] + 2, rt, p.c.inter >> 7, p.c.ws.sfb2);
+        const int m = min(3 * p.c.ws.c_expert[i] + 2, p.c.n_mats - 1);
+        MxTile T = mxmoe_tile(p.c, i, m < 0 ? 2 : m, rt, p.c.inter >> 7, p.c.ws.sfb2);
         T.id0 = i;
         T.id1 = 0;
         T.id2 = rt;
@@ -513,8 +523,10 @@ struct MoeDown {
 __global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter, int terms, int tpt, int NB,
                                                            float limit, int cpt, int max_items)
 {
-    pdl_wait();
+    // The down kernel may launch at once: it fetches weights until it needs
+    // this kernel's output.
     pdl_trigger();
+    pdl_wait();
     const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
     const int kc = inter >> 7, ntiles = ws.meta[2], groups = kc / cpt;
     if (gw >= max_items) return;
@@ -758,6 +770,8 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     c.hidden = s.hidden;
     c.inter = s.inter;
     c.err = status;
+    c.max_tiles = s.max_tiles;
+    c.n_mats = 3 * (L->n_experts + 1);
     // Persistent grids: the tile count is known only on the device.
     const int g1 = min(sms, s.max_tiles * 2 * RT), g2 = min(sms, s.max_tiles * RTH);
 
