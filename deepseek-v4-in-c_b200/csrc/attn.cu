@@ -25,16 +25,21 @@ constexpr int ATT_CH = 32;    // selected rows per CTA
 constexpr int ATT_HG = 16;    // heads per CTA
 constexpr int ATT_THREADS = 256;
 
-template <bool BF16>
+// VEC: D % 4 == 0 and q / kv aligned for 16-byte (f32) or 8-byte (bf16)
+// loads. Otherwise rows are gathered element by element into shared rows of
+// DA = D rounded up to 4 columns whose tail is zero, so the 4-column loops
+// below add exact zeros there, and the output is stored element by element.
+template <bool BF16, bool VEC>
 __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
     const float *__restrict__ q, const void *__restrict__ kvp, const int *__restrict__ idxs, int H, int D,
     int topk, float scale, float *__restrict__ pm, float *__restrict__ pl, float *__restrict__ po)
 {
     extern __shared__ float smem[];
-    const int DP = D + 8;                      // padded row stride (floats): rows 4 lanes apart miss each other's banks
+    const int DA = VEC ? D : ((D + 3) & ~3);
+    const int DP = DA + 8;                     // padded row stride (floats): rows 4 lanes apart miss each other's banks
     float *kvs = smem;                         // [CH][DP]
-    float *qs = kvs + ATT_CH * DP;             // [HG][D]
-    float *ss = qs + ATT_HG * D;               // [HG][CH] scores, then weights
+    float *qs = kvs + ATT_CH * DP;             // [HG][DA]
+    float *ss = qs + ATT_HG * DA;              // [HG][CH] scores, then weights
     __shared__ int rows[ATT_CH];
 
     const int chunk = blockIdx.x, h0 = blockIdx.y * ATT_HG, tid = threadIdx.x;
@@ -44,27 +49,47 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
         rows[tid] = (j < topk) ? idxs[j] : -1;
     }
     __syncthreads();
-    // Gather rows (D % 4 == 0) and the head group's q.
-    const int d4 = D >> 2;
-    for (int i = tid; i < ATT_CH * d4; i += ATT_THREADS) {
-        const int r = i / d4, c = (i - r * d4) * 4, src = rows[r];
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (src >= 0) {
-            if constexpr (BF16) {
-                const uint2 u = __ldg(reinterpret_cast<const uint2 *>(
-                    reinterpret_cast<const uint16_t *>(kvp) + (size_t)src * D + c));
-                v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
-                                __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
-            } else {
-                v = __ldg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(kvp) + (size_t)src * D + c));
+    // Gather rows and the head group's q.
+    if constexpr (!VEC) {
+        for (int i = tid; i < ATT_CH * DA; i += ATT_THREADS) {
+            const int r = i / DA, c = i - r * DA, src = rows[r];
+            float v = 0.0f;
+            if (src >= 0 && c < D) {
+                if constexpr (BF16)
+                    v = __uint_as_float((uint32_t)__ldg(reinterpret_cast<const unsigned short *>(kvp) +
+                                                        (size_t)src * D + c) << 16);
+                else
+                    v = __ldg(reinterpret_cast<const float *>(kvp) + (size_t)src * D + c);
             }
+            kvs[r * DP + c] = v;
         }
-        *reinterpret_cast<float4 *>(kvs + r * DP + c) = v;
+        for (int i = tid; i < nh * DA; i += ATT_THREADS) {
+            const int hh = i / DA, c = i - hh * DA;
+            qs[hh * DA + c] = (c < D) ? __ldg(q + (size_t)(h0 + hh) * D + c) : 0.0f;
+        }
     }
-    for (int i = tid; i < nh * d4; i += ATT_THREADS) {
-        const int hh = i / d4, c = (i - hh * d4) * 4;
-        *reinterpret_cast<float4 *>(qs + hh * D + c) =
-            __ldg(reinterpret_cast<const float4 *>(q + (size_t)(h0 + hh) * D + c));
+    if constexpr (VEC) {
+        const int d4 = D >> 2;
+        for (int i = tid; i < ATT_CH * d4; i += ATT_THREADS) {
+            const int r = i / d4, c = (i - r * d4) * 4, src = rows[r];
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (src >= 0) {
+                if constexpr (BF16) {
+                    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(
+                        reinterpret_cast<const uint16_t *>(kvp) + (size_t)src * D + c));
+                    v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u),
+                                    __uint_as_float(u.y << 16), __uint_as_float(u.y & 0xFFFF0000u));
+                } else {
+                    v = __ldg(reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(kvp) + (size_t)src * D + c));
+                }
+            }
+            *reinterpret_cast<float4 *>(kvs + r * DP + c) = v;
+        }
+        for (int i = tid; i < nh * d4; i += ATT_THREADS) {
+            const int hh = i / d4, c = (i - hh * d4) * 4;
+            *reinterpret_cast<float4 *>(qs + hh * D + c) =
+                __ldg(reinterpret_cast<const float4 *>(q + (size_t)(h0 + hh) * D + c));
+        }
     }
     __syncthreads();
 
@@ -74,10 +99,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
         const int hp = tid >> 5, lane = tid & 31, rp = lane >> 1, ds = lane & 1;
         const int ha = 2 * hp, hb = 2 * hp + 1;
         if (ha < nh) {
-            const float *qa = qs + ha * D, *qb = qs + (hb < nh ? hb : ha) * D;
+            const float *qa = qs + ha * DA, *qb = qs + (hb < nh ? hb : ha) * DA;
             const float *k0 = kvs + rp * DP, *k1 = kvs + (rp + 16) * DP;
             float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;
-            for (int c = 4 * ds; c < D; c += 8) {
+            for (int c = 4 * ds; c < DA; c += 8) {
                 const float4 x = *reinterpret_cast<const float4 *>(qa + c);
                 const float4 y = *reinterpret_cast<const float4 *>(qb + c);
                 const float4 v0 = *reinterpret_cast<const float4 *>(k0 + c);
@@ -129,7 +154,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
         if (ha < nh) {
             const float *wa = ss + ha * ATT_CH, *wb = ss + (hb < nh ? hb : ha) * ATT_CH;
             float *da = po + ((size_t)chunk * H + h0 + ha) * D, *db = po + ((size_t)chunk * H + h0 + hb) * D;
-            for (int c = 4 * lane; c < D; c += 128) {
+            for (int c = 4 * lane; c < DA; c += 128) {
                 float4 x = make_float4(0.f, 0.f, 0.f, 0.f), y = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
                 for (int j = 0; j < ATT_CH; j++) {
@@ -144,8 +169,22 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
                     y.z = fmaf(w, v.z, y.z);
                     y.w = fmaf(w, v.w, y.w);
                 }
-                *reinterpret_cast<float4 *>(da + c) = x;
-                if (hb < nh) *reinterpret_cast<float4 *>(db + c) = y;
+                if constexpr (VEC) {
+                    *reinterpret_cast<float4 *>(da + c) = x;
+                    if (hb < nh) *reinterpret_cast<float4 *>(db + c) = y;
+                } else {
+                    const int nk = D - c;        // >= 1
+                    da[c] = x.x;
+                    if (nk > 1) da[c + 1] = x.y;
+                    if (nk > 2) da[c + 2] = x.z;
+                    if (nk > 3) da[c + 3] = x.w;
+                    if (hb < nh) {
+                        db[c] = y.x;
+                        if (nk > 1) db[c + 1] = y.y;
+                        if (nk > 2) db[c + 2] = y.z;
+                        if (nk > 3) db[c + 3] = y.w;
+                    }
+                }
             }
         }
     }
@@ -232,19 +271,19 @@ int attn_run(float *o, const float *q, const void *kv, int kv_bf16, const float 
     float *pl = (float *)p;
     p += dsv4cu_align256((size_t)nch * H * 4);
     float *po = (float *)p;
-    const size_t smem = ((size_t)ATT_CH * (D + 8) + (size_t)ATT_HG * D + ATT_HG * ATT_CH) * sizeof(float);
+    const bool vec = D % 4 == 0 && ((uintptr_t)q & 15) == 0 && ((uintptr_t)kv & (kv_bf16 ? 7 : 15)) == 0;
+    const size_t DA = (size_t)((D + 3) & ~3);
+    const size_t smem = ((size_t)ATT_CH * (DA + 8) + (size_t)ATT_HG * DA + ATT_HG * ATT_CH) * sizeof(float);
     if (smem > 220 * 1024) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "sparse_attn: head dim %d too large", D);
     if (nch > ATT_MAX_CHUNKS)
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "sparse_attn: topk %d > %d", topk, ATT_MAX_CHUNKS * ATT_CH);
     dim3 grid(nch, (H + ATT_HG - 1) / ATT_HG);
-    static SmemLimit lim_bf16, lim_f32;
-    if (kv_bf16) {
-        DSV4CU_CUDA_TRY(smem_limit(lim_bf16, (const void *)attn_chunk_kernel<true>, (int)smem));
-        attn_chunk_kernel<true><<<grid, ATT_THREADS, smem, st>>>(q, kv, idxs, H, D, topk, scale, pm, pl, po);
-    } else {
-        DSV4CU_CUDA_TRY(smem_limit(lim_f32, (const void *)attn_chunk_kernel<false>, (int)smem));
-        attn_chunk_kernel<false><<<grid, ATT_THREADS, smem, st>>>(q, kv, idxs, H, D, topk, scale, pm, pl, po);
-    }
+    static SmemLimit lim[4];
+    void (*kern)(const float *, const void *, const int *, int, int, int, float, float *, float *, float *) =
+        kv_bf16 ? (vec ? attn_chunk_kernel<true, true> : attn_chunk_kernel<true, false>)
+                : (vec ? attn_chunk_kernel<false, true> : attn_chunk_kernel<false, false>);
+    DSV4CU_CUDA_TRY(smem_limit(lim[(kv_bf16 ? 2 : 0) + (vec ? 1 : 0)], (const void *)kern, (int)smem));
+    kern<<<grid, ATT_THREADS, smem, st>>>(q, kv, idxs, H, D, topk, scale, pm, pl, po);
     DSV4CU_LAUNCH_CHECK();
     attn_combine_kernel<<<dim3(H, (D + ATT_COMB_COLS - 1) / ATT_COMB_COLS), ATT_COMB_COLS, 0, st>>>(
         pm, pl, po, sink, H, D, nch, o);
@@ -262,7 +301,6 @@ extern "C" int dsv4cu_sparse_attn(dsv4cu_ctx *ctx, float *o, const float *q, con
 {
     if (!ctx || !o || !q || !kv || !sink) return dsv4cu_set_error(DSV4CU_ERR_ARG, "sparse_attn: NULL argument");
     if (h <= 0 || d <= 0 || topk < 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "sparse_attn: bad shape");
-    if (d % 4) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "sparse_attn: head dim must be a multiple of 4");
     cudaStream_t st = (cudaStream_t)stream;
     if (topk == 0) {
         // No slot at all: the reference output is zero (denominator = sink only).

@@ -70,8 +70,6 @@ extern "C" int dsv4cu_sparse_attn_noalloc(float *o, const float *q, const void *
 {
     if (!o || !q || !kv || !sink) return dsv4cu_set_error(DSV4CU_ERR_ARG, "sparse_attn_noalloc: NULL argument");
     if (h <= 0 || d <= 0 || topk < 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "sparse_attn_noalloc: bad shape");
-    if (d % 4)
-        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "sparse_attn_noalloc: head dim must be a multiple of 4");
     cudaStream_t st = (cudaStream_t)stream;
     if (topk == 0) {
         DSV4CU_CUDA_TRY(cudaMemsetAsync(o, 0, (size_t)h * d * sizeof(float), st));

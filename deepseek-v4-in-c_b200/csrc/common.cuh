@@ -51,6 +51,30 @@ DSV4CU_DEV float e2m1_to_f32(uint32_t nib)
 }
 
 // Two e4m3 codes (low byte = first element) -> f16x2 (first element low).
+// The float the reference's scalar FP8/FP4 matmul returns for a row whose
+// result is NaN. Its double arithmetic carries the first NaN operand it meets,
+// sign included, and its decoders give quiet NaNs: E4M3 0x7F -> 0x7FC00000,
+// E4M3 0xFF -> 0xFFC00000, E8M0 0xFF -> 0x7FC00000 (src/10_compute/
+// dsv4_quant.h:72-83 and the E4M3 table after it). The row's scale blocks are
+// scanned in order: the first NaN weight code of the first block holding one
+// gives its sign, else that block's NaN scale gives +NaN. A row with neither
+// got its NaN from the activations (inf - inf, 0 x inf), for which x86 gives
+// its default NaN 0xFFC00000; a NaN activation's own payload is not kept.
+DSV4CU_DEV float ref_row_nan(const uint8_t *w_row, const uint8_t *s_row, int cols, int blk_c, bool fp4)
+{
+    for (int c0 = 0, b = 0; c0 < cols; c0 += blk_c, b++) {
+        if (!fp4) {
+            const int n = min(blk_c, cols - c0);
+            for (int k = 0; k < n; k++) {
+                const uint32_t code = w_row[c0 + k];
+                if ((code & 0x7Fu) == 0x7Fu) return __uint_as_float(0x7FC00000u | ((code & 0x80u) << 24));
+            }
+        }
+        if (s_row[b] == 0xFFu) return __uint_as_float(0x7FC00000u);
+    }
+    return __uint_as_float(0xFFC00000u);
+}
+
 DSV4CU_DEV uint32_t cvt_e4m3x2_f16x2(uint16_t two)
 {
     uint32_t r;

@@ -1,13 +1,15 @@
 // gemv.cu - dsv4cu_mmq: the packed matmul on device memory.
 //
 // Replaces dsv4_mmq_n (src/10_compute/dsv4_matmul.c:63-73) and the per-format
-// bodies fp8_n / fp4_n / bf16_n. Two paths:
-//   * fast: the tensor-core GEMV tile of gemv_core.cuh, for FP8 (blk_c % 16),
-//     FP4 (blk_c % 32) and BF16 weights whose rows are whole 16-byte chunks.
+// bodies fp8_n / fp4_n / bf16_n. Three paths:
+//   * fast: the tensor-core GEMV tile of gemv_core.cuh, for FP8 (blk_c % 16)
+//     and FP4 (blk_c % 32) weights whose rows are whole 16-byte chunks.
 //     Activations are first split into exact hi/lo operands (xprep_kernel).
-//   * generic: every other geometry the reference accepts (any blk_r/blk_c,
-//     ragged K), one thread per output in the scalar double arithmetic of the
-//     reference's own scalar reference (tests/unit/test_matmul.c:54-176).
+//   * generic: every other FP8/FP4 geometry the reference accepts (any
+//     blk_r/blk_c, ragged K), one thread per output in the scalar double
+//     arithmetic of the reference's own scalar reference
+//     (tests/unit/test_matmul.c:54-176).
+//   * BF16: gemv_bf16.cu, the reference's double fma tree step for step.
 #include <stdio.h>
 #include <string.h>
 
@@ -22,11 +24,10 @@
 namespace dsv4cu {
 
 // ------------------------------------------------------------------ xprep
-// One warp per (token, 32-element block). F16 mode: P = 14 - floor(log2 amax)
-// so the block's magnitudes land in [2^14, 2^15); hi = f16(x 2^P), lo =
+// One warp per (token, 32-element block): P = 14 - floor(log2 amax) so the
+// block's magnitudes land in [2^14, 2^15); hi = f16(x 2^P), lo =
 // f16(x 2^P - hi), xs = 2^-P. A bf16-valued x (8 significant bits) is exact in
-// hi alone. BF16 mode (for BF16 weights): hi = bf16(x), lo = bf16(x - hi), xs = 1.
-template <bool BF16MODE>
+// hi alone.
 __global__ void xprep_kernel(const float *__restrict__ x, int cols, int ldx_in, int nt,
                              int ldx, uint16_t *__restrict__ xh, uint16_t *__restrict__ xl,
                              float *__restrict__ xs)
@@ -37,33 +38,22 @@ __global__ void xprep_kernel(const float *__restrict__ x, int cols, int ldx_in, 
     if (gw >= nt * nblk) return;
     const int t = gw / nblk, b = gw - t * nblk, k = b * 32 + lane;
     const float v = k < cols ? x[(size_t)t * ldx_in + k] : 0.0f;
-    uint16_t h, l;
-    float s = 1.0f;
-    if constexpr (BF16MODE) {
-        const __nv_bfloat16 hb = __float2bfloat16_rn(v);
-        const float hf = __bfloat162float(hb);
-        const __nv_bfloat16 lb = isfinite(hf) ? __float2bfloat16_rn(v - hf) : __float2bfloat16_rn(0.0f);
-        h = __bfloat16_as_ushort(hb);
-        l = __bfloat16_as_ushort(lb);
-    } else {
-        float a = isfinite(v) ? fabsf(v) : 0.0f;
+    float a = isfinite(v) ? fabsf(v) : 0.0f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
-        int P = 0;
-        if (a > 0.0f) {
-            int e;
-            frexpf(a, &e);          // a = f 2^e, f in [0.5, 1): floor(log2 a) = e - 1
-            P = 15 - e;
-            P = P > 125 ? 125 : (P < -125 ? -125 : P);
-        }
-        const float vs = ldexpf(v, P);
-        const __half hh = __float2half_rn(vs);
-        const float hf = __half2float(hh);
-        const __half lh = isfinite(hf) ? __float2half_rn(vs - hf) : __float2half_rn(0.0f);
-        h = __half_as_ushort(hh);
-        l = __half_as_ushort(lh);
-        s = ldexpf(1.0f, -P);
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+    int P = 0;
+    if (a > 0.0f) {
+        int e;
+        frexpf(a, &e);          // a = f 2^e, f in [0.5, 1): floor(log2 a) = e - 1
+        P = 15 - e;
+        P = P > 125 ? 125 : (P < -125 ? -125 : P);
     }
+    const float vs = ldexpf(v, P);
+    const __half hh = __float2half_rn(vs);
+    const float hf = __half2float(hh);
+    const __half lh = isfinite(hf) ? __float2half_rn(vs - hf) : __float2half_rn(0.0f);
+    const uint16_t h = __half_as_ushort(hh), l = __half_as_ushort(lh);
+    const float s = ldexpf(1.0f, -P);
     xh[(size_t)t * ldx + k] = h;
     xl[(size_t)t * ldx + k] = l;
     if (lane == 0) xs[(size_t)t * nblk + b] = s;
@@ -127,7 +117,12 @@ __global__ void __launch_bounds__(GEMV_THREADS, 3) gemv_tma_kernel(MatArgs m, co
             const int t = i / R, r = i - t * R, grp = r >> 4, rr = r & 15, row = row0 + r;
             float v = 0.0f;
             for (int p = 0; p < P; p++) v += red[grp * P + p][t][rr];
-            if (row < m.rows && t0 + t < nt) y[(size_t)(t0 + t) * m.rows + row] = v;
+            if (row < m.rows && t0 + t < nt) {
+                if (isnan(v))
+                    v = ref_row_nan(m.w + (size_t)row * m.row_bytes, m.s + (size_t)(row / m.blk_r) * m.s_cols,
+                                    m.cols, m.blk_c, FMT == DSV4CU_WFP4);
+                y[(size_t)(t0 + t) * m.rows + row] = v;
+            }
         }
         __syncthreads();
     }
@@ -144,14 +139,6 @@ __global__ void gemv_generic_kernel(const uint8_t *__restrict__ W, const uint8_t
     if (i >= (long)nt * rows) return;
     const int t = (int)(i / rows), o = (int)(i - (long)t * rows);
     const float *xt = x + (size_t)t * cols;
-    if (wdt == DSV4CU_WBF16) {
-        const uint16_t *row = reinterpret_cast<const uint16_t *>(W) + (size_t)o * cols;
-        double acc = 0.0;
-        for (int c = 0; c < cols; c++)
-            acc = __dadd_rn(acc, __dmul_rn((double)__uint_as_float((uint32_t)row[c] << 16), (double)xt[c]));
-        y[(size_t)t * rows + o] = (float)acc;
-        return;
-    }
     const int sc = (cols + blk_c - 1) / blk_c;
     const uint8_t *srow = S + (size_t)(o / blk_r) * sc;
     double total = 0.0;
@@ -174,7 +161,11 @@ __global__ void gemv_generic_kernel(const uint8_t *__restrict__ W, const uint8_t
         }
         total = __dadd_rn(total, __dmul_rn(acc, (double)e8m0_to_f32(srow[bi])));
     }
-    y[(size_t)t * rows + o] = (float)total;
+    float v = (float)total;
+    if (isnan(v))
+        v = ref_row_nan(W + (size_t)o * (wdt == DSV4CU_WFP4 ? cols / 2 : cols), srow, cols, blk_c,
+                        wdt == DSV4CU_WFP4);
+    y[(size_t)t * rows + o] = v;
 }
 
 int row_bytes_of(int wdt, int cols)
@@ -196,16 +187,13 @@ MatArgs mat_args(const dsv4cu_qmat *q)
     return m;
 }
 
-int xprep_launch(const float *x, int cols, int ldx_in, int nt, int ldx, bool bf16mode,
-                 uint16_t *xh, uint16_t *xl, float *xs, cudaStream_t st)
+int xprep_launch(const float *x, int cols, int ldx_in, int nt, int ldx, uint16_t *xh, uint16_t *xl, float *xs,
+                 cudaStream_t st)
 {
     const long warps = (long)nt * (ldx >> 5);
     const int threads = 256;
     const unsigned blocks = (unsigned)((warps * 32 + threads - 1) / threads);
-    if (bf16mode)
-        xprep_kernel<true><<<blocks, threads, 0, st>>>(x, cols, ldx_in, nt, ldx, xh, xl, xs);
-    else
-        xprep_kernel<false><<<blocks, threads, 0, st>>>(x, cols, ldx_in, nt, ldx, xh, xl, xs);
+    xprep_kernel<<<blocks, threads, 0, st>>>(x, cols, ldx_in, nt, ldx, xh, xl, xs);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
 }
@@ -252,6 +240,7 @@ static bool fast_ok(const dsv4cu_qmat *q)
 size_t mmq_workspace(const dsv4cu_qmat *q, int nt, int sm_count)
 {
     if (!q || nt <= 0) return 0;
+    if (q->wdt == DSV4CU_WBF16) return bf16_chain_workspace(q->cols, nt);
     if (!fast_ok(q)) return 0;
     const size_t ldx = (size_t)((q->cols + 31) / 32) * 32;
     size_t b = dsv4cu_align256(nt * ldx * 2) * 2 + dsv4cu_align256(nt * (ldx / 32) * 4);
@@ -261,6 +250,8 @@ size_t mmq_workspace(const dsv4cu_qmat *q, int nt, int sm_count)
 int mmq_run(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *q, int nt,
             cudaStream_t st, void *ws, int *counters)
 {
+    if (q->wdt == DSV4CU_WBF16)
+        return bf16_chain_run(y, x, (const uint16_t *)q->w, q->rows, q->cols, nt, ws, st);
     const MatArgs m = mat_args(q);
     if (!fast_ok(q)) {
         const long n = (long)nt * q->rows;
@@ -286,14 +277,11 @@ int mmq_run(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *q, int
     p += dsv4cu_align256((size_t)nt * (ldx / 32) * 4);
     (void)counters;
     int *err = ctx->status;
-    int r = xprep_launch(x, q->cols, q->cols, nt, ldx, q->wdt == DSV4CU_WBF16, xh, xl, xs, st);
+    int r = xprep_launch(x, q->cols, q->cols, nt, ldx, xh, xl, xs, st);
     if (r) return r;
     const int sms = ctx ? ctx->sm_count : 148;
-    switch (q->wdt) {
-    case DSV4CU_WFP8: return launch_fast<DSV4CU_WFP8>(q, m, xa, nt, y, sms, err, st);
-    case DSV4CU_WFP4: return launch_fast<DSV4CU_WFP4>(q, m, xa, nt, y, sms, err, st);
-    default: return launch_fast<DSV4CU_WBF16>(q, m, xa, nt, y, sms, err, st);
-    }
+    if (q->wdt == DSV4CU_WFP8) return launch_fast<DSV4CU_WFP8>(q, m, xa, nt, y, sms, err, st);
+    return launch_fast<DSV4CU_WFP4>(q, m, xa, nt, y, sms, err, st);
 }
 
 }  // namespace dsv4cu

@@ -1,0 +1,213 @@
+// gemv_bf16.cu - the BF16 matmul in the reference's own double arithmetic.
+//
+// Reference: bf16_n (src/10_compute/dsv4_matmul.c:88-113) with BLOCK_DOT_V
+// (src/10_compute/dsv4_dec_common.h:45-61). Its scalar twin BLOCK_DOT_S
+// (tests/unit/test_matmul.c:54-67) is held to the same bits by the reference's
+// own gate. Per (token, row), with w and x widened exactly to double and
+// n16 = 16 * floor(n / 16):
+//   a[c] = fma chain over i = c, c + 16, c + 32, ... < n16, from +0   (c = 0..15)
+//   b[j] = (a[j] + a[j + 4]) + (a[j + 8] + a[j + 12])                (j = 0..3)
+//   acc  = (b[0] + b[1]) + (b[2] + b[3]); acc = fma(w[i], x[i], acc) for i >= n16
+//   y    = (float)acc
+// Every step here is the same IEEE double operation in the same order, so y
+// carries the reference's bits (a NaN's payload aside: the GPU returns its
+// canonical NaN). A bf16 x fp32 product has at most 32 significant bits, so each
+// fma is the exact product plus one rounded add, as on the host.
+//
+// Work split: a warp owns 16 rows; lanes 2r and 2r + 1 own chains 0-7 and 8-15
+// of row r. Per 64-column group a lane loads four 16-byte words of its row
+// (8 bf16 each, one per 16-column step), so the warp's four loads cover 16 whole
+// 128-byte lines; the next group's words are in flight while this one computes.
+// x is widened once per call into a double copy (xd, rows of ldxd doubles) that
+// every warp reads through L1 as broadcasts. Weights are widened with integer
+// ops: a normal bf16 becomes the double whose high word is
+// sign | (exponent + 896) << 20 | mantissa << 13; a 16-byte word that holds a
+// zero, subnormal, inf or NaN takes the float conversion instead, which is exact
+// for every bf16.
+#include "common.cuh"
+#include "ctx.h"
+#include "gemv.h"
+
+namespace dsv4cu {
+
+constexpr int BFC_WARPS = 8;            // 128 rows per CTA
+constexpr int BFC_THREADS = 32 * BFC_WARPS;
+
+// x rows widened to double, zero-padded to ldxd columns.
+__global__ void bf16_xwiden_kernel(const float *__restrict__ x, int cols, int nt, int ldxd,
+                                   double *__restrict__ xd)
+{
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)nt * ldxd) return;
+    const int t = (int)(i / ldxd), k = (int)(i - (long)t * ldxd);
+    xd[i] = k < cols ? (double)x[(size_t)t * cols + k] : 0.0;
+}
+
+// All 8 bf16 of the word have an exponent field in 1..254. Per halfword with
+// exponent field E: ((E + 1) >> 1) & 0x7F is zero exactly for E = 0 and 255;
+// adding 0x7F00 then sets the halfword's top bit exactly when it is not.
+DSV4CU_DEV bool bf16x8_normal(uint4 u)
+{
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t ok = 0xFFFFFFFFu;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t g = ((w[i] & 0x7F807F80u) + 0x00800080u) & 0x7F007F00u;
+        ok &= g + 0x7F007F00u;
+    }
+    return (ok & 0x80008000u) == 0x80008000u;
+}
+
+// The normal bf16 held in bits 31..16 of u, as a double.
+DSV4CU_DEV double bf16_top_to_f64(uint32_t u)
+{
+    const uint32_t hi = ((uint32_t)((int32_t)u >> 3) & 0x8FFFE000u) + 0x38000000u;
+    return __hiloint2double((int)hi, 0);
+}
+
+DSV4CU_DEV void bf16x8_to_f64(uint4 u, bool normal, double (&w)[8])
+{
+    const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+    if (normal) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w[2 * i] = bf16_top_to_f64(q[i] << 16);
+            w[2 * i + 1] = bf16_top_to_f64(q[i]);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            w[2 * i] = (double)__uint_as_float(q[i] << 16);
+            w[2 * i + 1] = (double)__uint_as_float(q[i] & 0xFFFF0000u);
+        }
+    }
+}
+
+// The 8 bf16 of row `row` at column c (c % 8 == 0). VEC: the row's bytes are
+// 16-byte aligned, one vector load; otherwise 8 halfword loads.
+template <bool VEC>
+DSV4CU_DEV uint4 bf16x8_load(const uint16_t *__restrict__ row, int c)
+{
+    if constexpr (VEC) {
+        return __ldg(reinterpret_cast<const uint4 *>(row + c));
+    } else {
+        uint32_t q[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            q[i] = (uint32_t)__ldg(row + c + 2 * i) | ((uint32_t)__ldg(row + c + 2 * i + 1) << 16);
+        return make_uint4(q[0], q[1], q[2], q[3]);
+    }
+}
+
+// One 16-column step for the lane's 8 chains and every token of the tile.
+template <int NT>
+DSV4CU_DEV void bf16_step(uint4 u, const double *__restrict__ xs, int ldxd, int ntile, double (&a)[NT][8])
+{
+    double w[8];
+    bf16x8_to_f64(u, bf16x8_normal(u), w);
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        if (t >= ntile) break;
+        const double2 *xp = reinterpret_cast<const double2 *>(xs + (size_t)t * ldxd);
+        double2 xv[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) xv[i] = __ldg(xp + i);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            a[t][2 * i] = __fma_rn(w[2 * i], xv[i].x, a[t][2 * i]);
+            a[t][2 * i + 1] = __fma_rn(w[2 * i + 1], xv[i].y, a[t][2 * i + 1]);
+        }
+    }
+}
+
+template <int NT, bool VEC>
+__global__ void __launch_bounds__(BFC_THREADS) bf16_chain_kernel(const uint16_t *__restrict__ W, int rows, int cols,
+                                                                  const double *__restrict__ xd, int ldxd, int nt,
+                                                                  float *__restrict__ y)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = (blockIdx.x * BFC_WARPS + warp) * 16 + (lane >> 1), h = lane & 1;
+    const int t0 = blockIdx.y * NT, ntile = min(NT, nt - t0);
+    if ((blockIdx.x * BFC_WARPS + warp) * 16 >= rows) return;       // whole warp past the end
+    const uint16_t *wrow = W + (size_t)min(row, rows - 1) * cols;  // rows past the end load row rows - 1
+    const double *xt = xd + (size_t)t0 * ldxd;
+    double a[NT][8];
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int q = 0; q < 8; q++) a[t][q] = 0.0;
+
+    const int M = cols >> 4;         // whole 16-column steps
+    const int G = M >> 2;            // whole 64-column groups
+    uint4 nxt[4];
+    if (G > 0) {
+#pragma unroll
+        for (int s = 0; s < 4; s++) nxt[s] = bf16x8_load<VEC>(wrow, 16 * s + 8 * h);
+    }
+    for (int g = 0; g < G; g++) {
+        uint4 cur[4];
+#pragma unroll
+        for (int s = 0; s < 4; s++) cur[s] = nxt[s];
+        if (g + 1 < G) {
+#pragma unroll
+            for (int s = 0; s < 4; s++) nxt[s] = bf16x8_load<VEC>(wrow, 64 * (g + 1) + 16 * s + 8 * h);
+        }
+#pragma unroll
+        for (int s = 0; s < 4; s++) bf16_step<NT>(cur[s], xt + 64 * g + 16 * s + 8 * h, ldxd, ntile, a);
+    }
+    for (int m = 4 * G; m < M; m++) bf16_step<NT>(bf16x8_load<VEC>(wrow, 16 * m + 8 * h), xt + 16 * m + 8 * h,
+                                                  ldxd, ntile, a);
+
+    // Fold: lane h = 0 holds chains 0-7, h = 1 chains 8-15. Each forms
+    // a[j] + a[j + 4] on its half; the pair then adds the halves.
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        double b[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const double mine = a[t][j] + a[t][j + 4];
+            const double other = __shfl_xor_sync(0xFFFFFFFFu, mine, 1);
+            b[j] = h ? other + mine : mine + other;
+        }
+        if (t >= ntile || h) continue;
+        double acc = (b[0] + b[1]) + (b[2] + b[3]);
+        const double *xr = xt + (size_t)t * ldxd;
+        for (int i = 16 * M; i < cols; i++)
+            acc = __fma_rn((double)__uint_as_float((uint32_t)__ldg(wrow + i) << 16), xr[i], acc);
+        if (row < rows) y[(size_t)(t0 + t) * rows + row] = __double2float_rn(acc);
+    }
+}
+
+size_t bf16_chain_workspace(int cols, int nt)
+{
+    const size_t ldxd = (size_t)((cols + 15) / 16) * 16;
+    return dsv4cu_align256((size_t)nt * ldxd * sizeof(double));
+}
+
+int bf16_chain_run(float *y, const float *x, const uint16_t *W, int rows, int cols, int nt, void *ws,
+                   cudaStream_t st)
+{
+    const int ldxd = ((cols + 15) / 16) * 16;
+    double *xd = (double *)ws;
+    const long n = (long)nt * ldxd;
+    bf16_xwiden_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, cols, nt, ldxd, xd);
+    DSV4CU_LAUNCH_CHECK();
+    const bool vec = cols % 8 == 0 && ((uintptr_t)W & 15u) == 0;
+    const unsigned gx = (unsigned)((rows + 16 * BFC_WARPS - 1) / (16 * BFC_WARPS));
+    if (nt == 1) {
+        if (vec)
+            bf16_chain_kernel<1, true><<<dim3(gx, 1), BFC_THREADS, 0, st>>>(W, rows, cols, xd, ldxd, nt, y);
+        else
+            bf16_chain_kernel<1, false><<<dim3(gx, 1), BFC_THREADS, 0, st>>>(W, rows, cols, xd, ldxd, nt, y);
+    } else {
+        const unsigned gy = (unsigned)((nt + 3) / 4);
+        if (vec)
+            bf16_chain_kernel<4, true><<<dim3(gx, gy), BFC_THREADS, 0, st>>>(W, rows, cols, xd, ldxd, nt, y);
+        else
+            bf16_chain_kernel<4, false><<<dim3(gx, gy), BFC_THREADS, 0, st>>>(W, rows, cols, xd, ldxd, nt, y);
+    }
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+}  // namespace dsv4cu

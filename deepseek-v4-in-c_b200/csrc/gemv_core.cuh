@@ -53,10 +53,10 @@ template <int FMT> struct Fmt {
     static DSV4CU_DEV int elem(int b) { return FMT == DSV4CU_WFP4 ? 2 * b : (FMT == DSV4CU_WFP8 ? b : b / 2); }
 };
 
-// Host-side check that the fast path covers a geometry.
+// Host-side check that the fast path covers a geometry (BF16 weights take
+// the exact double path of gemv_bf16.cu instead).
 static inline bool fast_geometry(int wdt, int cols, int blk_r, int blk_c)
 {
-    if (wdt == DSV4CU_WBF16) return cols % 8 == 0;
     if (wdt == DSV4CU_WFP8) return cols % 16 == 0 && blk_c > 0 && blk_c % 16 == 0 && blk_r > 0;
     if (wdt == DSV4CU_WFP4) return cols % 32 == 0 && blk_c > 0 && blk_c % 32 == 0 && blk_r > 0;
     return false;

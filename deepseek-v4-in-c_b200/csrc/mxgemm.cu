@@ -115,8 +115,17 @@ struct DenseMx {
         int ldy;
         uint32_t idesc, a_tx;
         int *err;
+        // The packed matrix, read only for a NaN result (ref_row_nan).
+        const uint8_t *w, *s;
+        int cols, blk_r, blk_c, s_cols, fp4;
     };
     static constexpr bool kPrefetchA = true;    // weights and tiles are known at launch
+    DSV4CU_DEV static float final_value(const Params &p, int row, float v)
+    {
+        if (!isnan(v)) return v;
+        return ref_row_nan(p.w + (size_t)row * (p.fp4 ? p.cols / 2 : p.cols),
+                           p.s + (size_t)(row / p.blk_r) * p.s_cols, p.cols, p.blk_c, p.fp4 != 0);
+    }
     DSV4CU_DEV static int ntiles(const Params &p) { return p.tiles_m * p.tiles_n * (p.cross ? p.S : 1); }
     DSV4CU_DEV static int *err(const Params &p) { return p.err; }
     DSV4CU_DEV static int terms(const Params &p) { return p.terms; }
@@ -157,7 +166,9 @@ struct DenseMx {
         if (tl < p.tpt && row < p.rows && tok < p.nt) {
             float *dst = p.y + ((size_t)T.id2 * p.nt + tok) * p.ldy + row;
             // The same thread stored the previous segment's sum here.
-            *dst = sg ? __fadd_rn(*dst, v) : v;
+            float r = sg ? __fadd_rn(*dst, v) : v;
+            if (!p.cross && sg == p.S - 1) r = final_value(p, row, r);
+            *dst = r;
         }
     }
     // Cross mode: after its partial stores the CTA counts the segment done;
@@ -180,7 +191,7 @@ struct DenseMx {
             const float *src = p.y + (size_t)tok * p.ldy + row;
             float v = __ldcg(src);
             for (int sg = 1; sg < p.S; sg++) v = __fadd_rn(v, __ldcg(src + sg * n));
-            p.out[(size_t)tok * p.ldy + row] = v;
+            p.out[(size_t)tok * p.ldy + row] = final_value(p, row, v);
         }
     }
     DSV4CU_DEV static void finish_all(const Params &, int, int, int *) {}
@@ -431,6 +442,13 @@ int mx_gemm(const MxMat *m, float *y, const float *x, int nt, int terms, int nb_
     p.idesc = umma::idesc_mx(m->fp4 ? umma::FMT_E2M1 : umma::FMT_E4M3, umma::FMT_E4M3, 128, t.NB);
     p.a_tx = m->fp4 ? 128 * 64 : 128 * 128;
     p.err = err;
+    p.w = (const uint8_t *)m->q.w;
+    p.s = (const uint8_t *)m->q.s;
+    p.cols = K;
+    p.blk_r = m->q.blk_r;
+    p.blk_c = m->q.blk_c;
+    p.s_cols = (K + m->q.blk_c - 1) / m->q.blk_c;
+    p.fp4 = m->fp4 ? 1 : 0;
     uint8_t *xq = (uint8_t *)ws;
     uint8_t *sfb = xq + dsv4cu_align256((size_t)t.tiles_n * t.NB * K);
     p.sfa = m->sfa;

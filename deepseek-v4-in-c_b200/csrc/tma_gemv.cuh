@@ -256,7 +256,8 @@ DSV4CU_DEV void tma_gemv_streams(unsigned char *smem_raw, const Stream *streams,
                         mma_f16_16816(e[t][0], e[t][1], e[t][2], e[t][3], a0, b0, a1, b1, b.x, b.y);
                         mma_f16_16816(e[t][0], e[t][1], e[t][2], e[t][3], a2, b2, a3, b3, b.z, b.w);
                     }
-                } else if constexpr (FMT == DSV4CU_WFP8) {
+                } else {
+                    static_assert(FMT == DSV4CU_WFP8, "the TMA GEMV streams FP4 or FP8 weights");
                     uint32_t glo, ghi, hlo, hhi;
                     cvt_e4m3x4(q0[i], glo, ghi);
                     cvt_e4m3x4(q1[i], hlo, hhi);
@@ -266,16 +267,6 @@ DSV4CU_DEV void tma_gemv_streams(unsigned char *smem_raw, const Stream *streams,
                         uint2 b = make_uint2(0u, 0u);
                         if (bact && cvalid) b = __ldg(reinterpret_cast<const uint2 *>(xb[t] + 4 * i));
                         mma_f16_16816(e[t][0], e[t][1], e[t][2], e[t][3], glo, hlo, ghi, hhi, b.x, b.y);
-                    }
-                } else {
-                    if (i & 1) continue;   // BF16: words (i, i+1) hold elements 2i..2i+3
-#pragma unroll
-                    for (int t = 0; t < NT; t++) {
-                        if (t >= nvalid) break;
-                        uint2 b = make_uint2(0u, 0u);
-                        if (bact && cvalid) b = __ldg(reinterpret_cast<const uint2 *>(xb[t] + 2 * i));
-                        mma_bf16_16816(e[t][0], e[t][1], e[t][2], e[t][3], q0[i], q1[i], q0[i + 1], q1[i + 1],
-                                       b.x, b.y);
                     }
                 }
             }

@@ -169,8 +169,8 @@ int dsv4cu_moe_decode(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
 /* dsv4cu_moe_decode from host buffers x_host [nt][hidden], logits_host
  * [nt][n_experts] and out_host [nt][hidden], enqueued on the stream, nothing
  * synchronised (read out_host after synchronising the stream). With
- * page-locked host buffers (cudaHostAlloc, cudaHostRegister, torch
- * pin_memory) one staging kernel reads the inputs across the bus and the
+ * page-locked host buffers (cudaHostAlloc, cudaHostRegister, a framework's
+ * pinned allocator) one staging kernel reads the inputs across the bus and the
  * step writes the output into host memory directly; with pageable buffers
  * they are copied through device staging. No bias, hash routing or index
  * outputs. */

@@ -52,12 +52,31 @@ static double bf16_to_d(uint16_t h)
     return (double)v.f;
 }
 
+/* BF16 row dot in the reference's order: bf16_n (src/10_compute/
+ * dsv4_matmul.c:88-113) runs BLOCK_DOT_V (src/10_compute/dsv4_dec_common.h:
+ * 45-61), 16 double fma chains a[c] over columns c, c+16, ... below
+ * 16*floor(n/16), folded b[j] = (a[j]+a[j+4]) + (a[j+8]+a[j+12]),
+ * acc = (b0+b1) + (b2+b3), then the remaining columns fma'd into acc in
+ * order. Its scalar twin is BLOCK_DOT_S (tests/unit/test_matmul.c:54-67). */
+static double bf16_row_dot(const uint16_t *row, const float *x, int n)
+{
+    double a[16] = {0};
+    int i = 0;
+    for (; i + 15 < n; i += 16)
+        for (int l = 0; l < 16; l++) a[l] = fma(bf16_to_d(row[i + l]), (double)x[i + l], a[l]);
+    double b[4];
+    for (int j = 0; j < 4; j++) b[j] = (a[j] + a[j + 4]) + (a[j + 8] + a[j + 12]);
+    double acc = (b[0] + b[1]) + (b[2] + b[3]);
+    for (; i < n; i++) acc = fma(bf16_to_d(row[i]), (double)x[i], acc);
+    return acc;
+}
+
 /* ------------------------------------------------------- packed matmul ----
- * Contract: src/10_compute/dsv4_matmul.h:33-43 (y[t*rows+o]). The arithmetic
- * is the scalar double reference of tests/unit/test_matmul.c:54-176: every
- * weight decoded exactly, the block dot product in double, one multiply by the
- * block's E8M0 scale per block (as kernel.py does), totals in double, one
- * rounding to float per output. Scale grid indexing follows fp8_n/fp4_n:
+ * Contract: src/10_compute/dsv4_matmul.h:33-43 (y[t*rows+o]). BF16 rows use
+ * bf16_row_dot above. FP8/FP4 follow the scalar double reference of
+ * tests/unit/test_matmul.c:54-176: every weight decoded exactly, the block dot
+ * product in double, one multiply by the block's E8M0 scale per block (as
+ * kernel.py does), totals in double, one rounding to float per output. Scale grid indexing follows fp8_n/fp4_n:
  * srow = S + (o / blk_r) * ceil(cols / blk_c)  (dsv4_matmul_fp8.c:158-160,
  * dsv4_matmul_fp4.c:56). FP4 rows are cols/2 bytes (dsv4_weights.h:25-27). */
 int orc_mmq_n(float *y, const float *x, const OrcQMat *m, int nt)
@@ -69,11 +88,7 @@ int orc_mmq_n(float *y, const float *x, const OrcQMat *m, int nt)
         float *yt = y + (size_t)t * out;
         for (int o = 0; o < out; o++) {
             if (m->wdt == 1) {
-                const uint16_t *row = (const uint16_t *)m->w + (size_t)o * in;
-                double acc = 0.0;
-                for (int c = 0; c < in; c++)
-                    acc += bf16_to_d(row[c]) * (double)xt[c];
-                yt[o] = (float)acc;
+                yt[o] = (float)bf16_row_dot((const uint16_t *)m->w + (size_t)o * in, xt, in);
                 continue;
             }
             const int sc = (in + m->blk_c - 1) / m->blk_c;

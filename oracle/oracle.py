@@ -43,6 +43,9 @@ def build(with_ref: bool | None = None) -> None:
         with_ref = os.path.isdir(os.path.join(REF_TREE, "src", "10_compute"))
     if with_ref:
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True)
+        # the reference's own unit tests linked against the CUDA library (run only by the GPU tests)
+        if os.path.exists(os.path.join(HERE, "..", "deepseek-v4-in-c_b200", "libdsv4cu.so")):
+            subprocess.run(["make", "-s", "-C", HERE, "units", f"REF={REF_TREE}"], check=True)
 
 
 def _p(a):

@@ -176,13 +176,33 @@ def att_err(got, want):
 @pytest.mark.parametrize("case", kat.attn_kat(), ids=lambda c: c[0])
 def test_attn_kat(host, case):
     name, q, kv, sink, idxs, scale, check = case
-    # the device kernel needs head dims that are multiples of 4: pad with zeros
-    d = q.shape[1]
-    pad = (-d) % 4
-    qp = np.pad(q, ((0, 0), (0, pad)))
-    kvp = np.pad(kv, ((0, 0), (0, pad)))
-    o = host.sparse_attn(qp, kvp, sink, idxs, scale)[:, :d]
+    o = host.sparse_attn(q, kv, sink, idxs, scale)     # head dims 2 and 4, as the reference tests them
     assert check(o), (name, o)
+
+
+@pytest.mark.parametrize("d", [1, 2, 7, 130, 513])
+@pytest.mark.parametrize("bf16", [0, 1])
+def test_attn_any_head_dim(dev, orc, d, bf16):
+    """Head dims that are not multiples of 4 (dsv4_sparse_attn takes any d):
+    rows gathered element by element, tail columns stored one by one."""
+    t = __import__("torch")
+    rng = np.random.default_rng(d + 7 * bf16)
+    H, N, T = 5, 300, 70
+    kv = pack.bf16_round(rng.standard_normal((N, d)).astype(np.float32))
+    q = rng.standard_normal((H, d)).astype(np.float32)
+    sink = rng.standard_normal(H).astype(np.float32)
+    idx = rng.choice(N, T, replace=False).astype(np.int32)
+    idx[::9] = -1
+    scale = np.float32(1 / np.sqrt(d))
+    o = t.empty((H, d), dtype=t.float32, device="cuda")
+    kvd = t.from_numpy(kv).cuda()
+    if bf16:
+        kvd = kvd.to(t.bfloat16)
+    dev.sparse_attn(o, t.from_numpy(q).cuda(), kvd, bf16, t.from_numpy(sink).cuda(), t.from_numpy(idx).cuda(),
+                    H, d, T, float(scale))
+    t.cuda.synchronize()
+    want = orc.sparse_attn(q, kv, sink, idx, scale)
+    assert att_err(o.cpu().numpy(), want) <= ATT_TOL
 
 
 def test_attn_golden(host):

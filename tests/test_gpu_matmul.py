@@ -132,6 +132,8 @@ def test_matmul_vs_oracle(host, dev, orc, shape):
     m = dsv4cu.QMat(W.ctypes.data, None if S is None else S.ctypes.data, wdt, rows, cols, br, bc)
     got = host.mmq(x, m)
     assert_close(got, want, shape)
+    if wdt == 1:        # BF16 runs the reference's double fma tree: same bits
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), shape
     # native device ABI gives the same bits
     dW = torch.from_numpy(W).cuda()
     dS = None if S is None else torch.from_numpy(S).cuda()
@@ -181,6 +183,75 @@ def test_deterministic_and_cache_refresh(host):
     assert not np.array_equal(a, c)
     d = oracle.Oracle().mmq(x, oracle.qmat(W, S, 3, 1024, 2048, 1, 32))
     assert_close(c, d)
+
+
+@pytest.mark.parametrize("rows,cols,nt", [(4096, 7168, 1), (1000, 7168, 5), (300, 4104, 2), (77, 1030, 1)])
+def test_bf16_bitwise_with_specials(dev, orc, rows, cols, nt):
+    """BF16 weights with zeros, subnormals and infinities among them and
+    arbitrary fp32 activations: the reference's bits (bf16_n,
+    src/10_compute/dsv4_matmul.c:88-113), including a misaligned row start
+    (cols % 8 != 0 takes the halfword-load variant)."""
+    import torch
+    rng = np.random.default_rng(rows + cols + nt)
+    W = pack.bf16_bits((rng.standard_normal((rows, cols)) * 0.05).astype(np.float32))
+    flat = W.reshape(-1)
+    pick = rng.integers(0, flat.size, flat.size // 50)
+    flat[pick[0::3]] = 0x0000
+    flat[pick[1::3]] = 0x8000 | rng.integers(1, 0x80, pick[1::3].size).astype(np.uint16)   # -subnormal
+    flat[pick[2::3][:3]] = 0x7F80                                                      # +inf, a few rows
+    x = (rng.standard_normal((nt, cols)) * np.exp(rng.uniform(-8, 8, (nt, cols)))).astype(np.float32)
+    want = orc.mmq(x, oracle.qmat(W, None, 1, rows, cols))
+    dW = torch.from_numpy(W).cuda()
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.empty((nt, rows), dtype=torch.float32, device="cuda")
+    dev.mmq(dy, dx, dev.qmat(dW, None, 1, rows, cols), nt)
+    got = dy.cpu().numpy()
+    fin = ~np.isnan(want)
+    assert np.array_equal(np.isnan(got), ~fin)
+    assert np.array_equal(got[fin].view(np.uint32), want[fin].view(np.uint32))
+
+
+@pytest.mark.parametrize("path", ["mx", "fast", "generic", "batch"])
+def test_every_e4m3_code_keeps_reference_bits(dev, path):
+    """test_matmul.c:588-632: W[r][r] = r, x = 1, scales 2^0, so y[r] is the
+    decode of code r - NaN codes 0x7F / 0xFF included, whose bits must be the
+    reference's quiet NaNs 0x7FC00000 / 0xFFC00000. -0.0 codes give +0.0."""
+    import torch
+    N = 256
+    bc = {"fast": 48, "generic": 120}.get(path, 128)  # 48: TMA GEMV tile, 120: generic double path
+    W = np.zeros((N, N), np.uint8)
+    W[np.arange(N), np.arange(N)] = np.arange(N, dtype=np.uint8)
+    S = np.full((-(-N // 128)) * (-(-N // bc)), 127, np.uint8)
+    nt = 1 if path != "batch" else 40
+    x = np.ones((nt, N), np.float32)
+    dW, dS = torch.from_numpy(W).cuda(), torch.from_numpy(S).cuda()
+    dy = torch.empty((nt, N), dtype=torch.float32, device="cuda")
+    dev.mmq(dy, torch.from_numpy(x).cuda(), dev.qmat(dW, dS, 2, N, N, 128, bc), nt)
+    got = dy.cpu().numpy().view(np.uint32)
+    want = np.array([np.float32(kat.e4m3_value(c)) for c in range(N)], np.float32).view(np.uint32).copy()
+    want[want == 0x80000000] = 0
+    want[0x7F], want[0xFF] = 0x7FC00000, 0xFFC00000
+    for t in range(nt):
+        assert np.array_equal(got[t], want), [hex(v) for v in got[t][want != got[t]][:4]]
+
+
+def test_nan_scale_gives_positive_quiet_nan(dev):
+    """E8M0 0xFF decodes to 0x7FC00000 (dsv4_quant.h:82): rows whose scale
+    block is NaN come back with exactly those bits, on FP4 and FP8."""
+    import torch
+    rng = np.random.default_rng(17)
+    for wdt, rows, cols, br, bc in ((3, 256, 512, 1, 32), (2, 256, 512, 128, 128)):
+        W, S = make_weights(rng, wdt, rows, cols, br, bc)
+        S = S.copy()
+        S[1] = 0xFF                       # row block 0 (FP4: row 0), column block 1
+        dW, dS = torch.from_numpy(W).cuda(), torch.from_numpy(S).cuda()
+        x = np.ones((1, cols), np.float32)
+        dy = torch.empty((1, rows), dtype=torch.float32, device="cuda")
+        dev.mmq(dy, torch.from_numpy(x).cuda(), dev.qmat(dW, dS, wdt, rows, cols, br, bc), 1)
+        got = dy.cpu().numpy()[0]
+        nan_rows = 1 if wdt == 3 else 128
+        assert np.all(got[:nan_rows].view(np.uint32) == 0x7FC00000), wdt
+        assert not np.any(np.isnan(got[nan_rows:])), wdt
 
 
 def test_fp8_n_fp4_n_bf16_n_entry_points(host, orc):
