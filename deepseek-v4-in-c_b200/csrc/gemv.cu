@@ -251,7 +251,7 @@ int mmq_run(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *q, int
             cudaStream_t st, void *ws, int *counters)
 {
     if (q->wdt == DSV4CU_WBF16)
-        return bf16_chain_run(y, x, (const uint16_t *)q->w, q->rows, q->cols, nt, ws, st);
+        return bf16_chain_run(y, x, q, nt, ws, ctx->status, st);
     const MatArgs m = mat_args(q);
     if (!fast_ok(q)) {
         const long n = (long)nt * q->rows;

@@ -13,8 +13,7 @@ int xprep_launch(const float *x, int cols, int ldx_in, int nt, int ldx, uint16_t
                  cudaStream_t st);
 size_t mmq_workspace(const dsv4cu_qmat *q, int nt, int sm_count);
 size_t bf16_chain_workspace(int cols, int nt);
-int bf16_chain_run(float *y, const float *x, const uint16_t *W, int rows, int cols, int nt, void *ws,
-                   cudaStream_t st);
+int bf16_chain_run(float *y, const float *x, const dsv4cu_qmat *q, int nt, void *ws, int *err, cudaStream_t st);
 int mmq_run(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *q, int nt,
             cudaStream_t st, void *ws, int *counters);
 

@@ -14,19 +14,28 @@
 // canonical NaN). A bf16 x fp32 product has at most 32 significant bits, so each
 // fma is the exact product plus one rounded add, as on the host.
 //
-// Work split: a warp owns 16 rows; lanes 2r and 2r + 1 own chains 0-7 and 8-15
-// of row r. Per 64-column group a lane loads four 16-byte words of its row
-// (8 bf16 each, one per 16-column step), so the warp's four loads cover 16 whole
-// 128-byte lines; the next group's words are in flight while this one computes.
-// x is widened once per call into a double copy (xd, rows of ldxd doubles) that
-// every warp reads through L1 as broadcasts. Weights are widened with integer
-// ops: a normal bf16 becomes the double whose high word is
+// Work split (both kernels): lanes 2r and 2r + 1 of a warp own chains 0-7 and
+// 8-15 of row r, 16 rows per row group. x is widened once per call into a
+// double copy (xd, rows of ldxd doubles, zero-padded). Weights are widened with
+// integer ops: a normal bf16 becomes the double whose high word is
 // sign | (exponent + 896) << 20 | mantissa << 13; a 16-byte word that holds a
 // zero, subnormal, inf or NaN takes the float conversion instead, which is exact
 // for every bf16.
+//
+// bf16_chain_tma_kernel (rows of 16-byte multiples, at least 128 bytes, aligned
+// base): one producer warp streams each consumer warp's rows through a ring of
+// shared-memory stages with tensor-map TMA (16-row x 128-byte boxes, 128-byte
+// swizzle, 256 bytes of every row per stage) and the stage's 128 activation
+// columns as doubles with a bulk copy; the consumers read both from shared
+// memory (R row groups per warp share every activation load). Every wait is
+// bounded and records an error code instead of hanging.
+// bf16_chain_kernel (any other geometry): each lane loads its row's 16-byte
+// words directly, the next 64-column group in flight, and reads xd through L1.
 #include "common.cuh"
 #include "ctx.h"
 #include "gemv.h"
+#include "tma_gemv.cuh"
+#include "tmap.h"
 
 namespace dsv4cu {
 
@@ -178,20 +187,212 @@ __global__ void __launch_bounds__(BFC_THREADS) bf16_chain_kernel(const uint16_t 
     }
 }
 
-size_t bf16_chain_workspace(int cols, int nt)
+// ------------------------------------------------------- TMA-staged variant
+// Stage layout: [8 consumer warps][R row groups][2 boxes of 16 rows x 128 B]
+// of weights, then [NT][128] activation doubles. Stage sizes are multiples of
+// 1 KB, so every box stays on the 1024-byte boundary of the 128-byte swizzle.
+template <int R, int NT>
+struct BfcCfg {
+    static constexpr int STAGES = 6 / R;
+    static constexpr int STREAM = 16 * R * TMA_SB;     // weight bytes per warp per stage
+    static constexpr int WBYTES = 8 * STREAM;
+    static constexpr int XBYTES = NT * 128 * 8;
+    static constexpr int STAGE = WBYTES + XBYTES;
+    static constexpr int SMEM = 1024 + STAGES * STAGE + 2 * STAGES * 8;
+};
+constexpr int BFT_THREADS = 288;                      // 8 consumer warps + 1 producer warp
+
+DSV4CU_DEV void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
 {
-    const size_t ldxd = (size_t)((cols + 15) / 16) * 16;
-    return dsv4cu_align256((size_t)nt * ldxd * sizeof(double));
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
 }
 
-int bf16_chain_run(float *y, const float *x, const uint16_t *W, int rows, int cols, int nt, void *ws,
-                   cudaStream_t st)
+template <int R, int NT>
+__global__ void __launch_bounds__(BFT_THREADS, 1) bf16_chain_tma_kernel(
+    const __grid_constant__ CUtensorMap tw, const uint16_t *__restrict__ W, int rows, int cols,
+    const double *__restrict__ xd, int ldxd, int nt, float *__restrict__ y, int *__restrict__ err)
 {
-    const int ldxd = ((cols + 15) / 16) * 16;
+    using C = BfcCfg<R, NT>;
+    extern __shared__ __align__(128) unsigned char dsmem[];
+    unsigned char *base = reinterpret_cast<unsigned char *>(
+        (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(base + C::STAGES * C::STAGE);
+    uint64_t *empty = full + C::STAGES;
+    __shared__ int abort_flag;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int row_cta = blockIdx.x * 128 * R;
+    const int t0 = blockIdx.y * NT, ntile = min(NT, nt - t0);
+    const int M = cols >> 4;                       // chain steps; stage k holds steps 8k .. 8k + 7
+    const int nst = (M + 7) >> 3;
+    const int rb = 2 * cols;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 8);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == 8) {
+        // ---------------- producer: lane w < 8 loads warp w's boxes, lane t < ntile token t's columns
+        const int row_w = row_cta + 16 * R * lane;
+        for (int k = 0; k < nst; k++) {
+            const int s = k % C::STAGES;
+            if (k >= C::STAGES) {
+                bool ok = true;
+                if (lane == 0) ok = mbar_wait(empty + s, ((k / C::STAGES) - 1) & 1, err, 0x201);
+                ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+                if (!ok) {
+                    if (lane == 0) abort_flag = 1;
+                    break;
+                }
+            }
+            const int x0 = k * TMA_SB;
+            uint32_t bytes = lane < ntile ? 1024u : 0u;
+            if (lane < 8) {
+#pragma unroll
+                for (int g = 0; g < R; g++) {
+                    const bool in = row_w + 16 * g < rows;
+                    bytes += (in && x0 < rb ? 2048u : 0u) + (in && x0 + TMA_BOX_HALF < rb ? 2048u : 0u);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xFFFFFFFFu, bytes, o);
+            if (lane == 0) mbar_arrive_expect_tx(full + s, bytes);
+            __syncwarp();
+            unsigned char *st = base + s * C::STAGE;
+            if (lane < 8) {
+#pragma unroll
+                for (int g = 0; g < R; g++) {
+                    const int r0 = row_w + 16 * g;
+                    unsigned char *dst = st + lane * C::STREAM + g * 4096;
+                    if (r0 < rows && x0 < rb) tma_load_2d(dst, &tw, x0, r0, full + s);
+                    if (r0 < rows && x0 + TMA_BOX_HALF < rb) tma_load_2d(dst + 2048, &tw, x0 + TMA_BOX_HALF, r0, full + s);
+                }
+            }
+            if (lane < ntile)
+                bulk_copy_g2s(st + C::WBYTES + lane * 1024, xd + (size_t)(t0 + lane) * ldxd + (size_t)k * 128, 1024u,
+                              full + s);
+        }
+        return;
+    }
+
+    // ---------------- consumers: lane (r, h), rows row_cta + 16 R warp + 16 g + r
+    const int r = lane >> 1, h = lane & 1;
+    double a[NT][R][8];
+#pragma unroll
+    for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int g = 0; g < R; g++)
+#pragma unroll
+            for (int q = 0; q < 8; q++) a[t][g][q] = 0.0;
+    for (int k = 0; k < nst; k++) {
+        const int s = k % C::STAGES;
+        const bool ok = mbar_wait(full + s, (k / C::STAGES) & 1, err, 0x202);
+        if (!__all_sync(0xFFFFFFFFu, ok) || abort_flag) break;
+        const unsigned char *sw = base + s * C::STAGE + warp * C::STREAM;
+        const double *sx = reinterpret_cast<const double *>(base + s * C::STAGE + C::WBYTES);
+        const int nsteps = min(8, M - 8 * k);
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            if (i >= nsteps) break;
+            const int lb = i * 32 + 16 * h, box = lb >> 7, j = (lb & 127) >> 4;
+            double w[R][8];
+#pragma unroll
+            for (int g = 0; g < R; g++) {
+                const uint4 u = *reinterpret_cast<const uint4 *>(sw + g * 4096 + box * 2048 + r * 128 +
+                                                                 ((j ^ (r & 7)) << 4));
+                bf16x8_to_f64(u, bf16x8_normal(u), w[g]);
+            }
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t >= ntile) break;
+                const double2 *xp = reinterpret_cast<const double2 *>(sx + t * 128 + i * 16 + 8 * h);
+                double2 xv[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) xv[q] = xp[q];
+#pragma unroll
+                for (int g = 0; g < R; g++)
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        a[t][g][2 * q] = __fma_rn(w[g][2 * q], xv[q].x, a[t][g][2 * q]);
+                        a[t][g][2 * q + 1] = __fma_rn(w[g][2 * q + 1], xv[q].y, a[t][g][2 * q + 1]);
+                    }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + s);
+    }
+
+    // Fold as in bf16_chain_kernel, then the ragged tail from global memory.
+#pragma unroll
+    for (int g = 0; g < R; g++) {
+        const int row = row_cta + 16 * R * warp + 16 * g + r;
+        const uint16_t *wrow = W + (size_t)min(row, rows - 1) * cols;
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            double b[4];
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                const double mine = a[t][g][jj] + a[t][g][jj + 4];
+                const double other = __shfl_xor_sync(0xFFFFFFFFu, mine, 1);
+                b[jj] = h ? other + mine : mine + other;
+            }
+            if (t >= ntile || h || row >= rows) continue;
+            double acc = (b[0] + b[1]) + (b[2] + b[3]);
+            const double *xr = xd + (size_t)(t0 + t) * ldxd;
+            for (int i = 16 * M; i < cols; i++)
+                acc = __fma_rn((double)__uint_as_float((uint32_t)__ldg(wrow + i) << 16), xr[i], acc);
+            y[(size_t)(t0 + t) * rows + row] = __double2float_rn(acc);
+        }
+    }
+}
+
+// The activation copy: rows of ldxd doubles, ldxd a multiple of 128 columns so
+// every TMA stage's 128 columns lie inside the row.
+static int bf16_ldxd(int cols) { return ((cols + 127) / 128) * 128; }
+
+size_t bf16_chain_workspace(int cols, int nt)
+{
+    return dsv4cu_align256((size_t)nt * bf16_ldxd(cols) * sizeof(double));
+}
+
+template <int R, int NT>
+static int bf16_tma_launch(const CUtensorMap &tw, const dsv4cu_qmat *q, const double *xd, int ldxd, int nt, float *y,
+                           int *err, cudaStream_t st)
+{
+    using C = BfcCfg<R, NT>;
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)bf16_chain_tma_kernel<R, NT>, C::SMEM));
+    const dim3 grid((unsigned)((q->rows + 128 * R - 1) / (128 * R)), (unsigned)((nt + NT - 1) / NT));
+    bf16_chain_tma_kernel<R, NT><<<grid, BFT_THREADS, C::SMEM, st>>>(tw, (const uint16_t *)q->w, q->rows, q->cols, xd,
+                                                                    ldxd, nt, y, err);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+int bf16_chain_run(float *y, const float *x, const dsv4cu_qmat *q, int nt, void *ws, int *err, cudaStream_t st)
+{
+    const int rows = q->rows, cols = q->cols;
+    const uint16_t *W = (const uint16_t *)q->w;
+    const int ldxd = bf16_ldxd(cols);
     double *xd = (double *)ws;
     const long n = (long)nt * ldxd;
     bf16_xwiden_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, cols, nt, ldxd, xd);
     DSV4CU_LAUNCH_CHECK();
+    if (tmap_weights_ok(q) && cols >= 16) {
+        CUtensorMap tw;
+        int staged = 0;
+        int r = tmap_encode(q, &tw, nullptr, &staged);
+        if (r) return r;
+        return nt == 1 ? bf16_tma_launch<2, 1>(tw, q, xd, ldxd, nt, y, err, st)
+                       : bf16_tma_launch<1, 4>(tw, q, xd, ldxd, nt, y, err, st);
+    }
     const bool vec = cols % 8 == 0 && ((uintptr_t)W & 15u) == 0;
     const unsigned gx = (unsigned)((rows + 16 * BFC_WARPS - 1) / (16 * BFC_WARPS));
     if (nt == 1) {
