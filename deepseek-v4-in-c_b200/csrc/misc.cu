@@ -177,6 +177,53 @@ __global__ void round_bf16_kernel(float *x, size_t n)
     if (i < n) x[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
 }
 
+// ------------------------------------------------------------- argmax
+// Greedy pick over a row of logits, as the reference's argmax
+// (src/90_cli/dsv4_decode.c:128-133): best starts at 0 and moves to v only
+// when lg[v] > lg[best]. So a NaN at index 0 keeps 0; other NaNs are never
+// picked; -0.0 and +0.0 tie; ties go to the lower index. One CTA per row:
+// each thread keeps (order key, index) over a strided range, then the CTA
+// reduces with larger key first, lower index on a tie.
+constexpr int ARGMAX_THREADS = 1024;
+
+DSV4CU_DEV void argmax_take(uint32_t &bk, int &bi, uint32_t k, int i)
+{
+    if (k > bk || (k == bk && i < bi)) {
+        bk = k;
+        bi = i;
+    }
+}
+
+__global__ void __launch_bounds__(ARGMAX_THREADS) argmax_kernel(const float *__restrict__ logits, int n,
+                                                                 int *__restrict__ best)
+{
+    __shared__ uint32_t s_k[ARGMAX_THREADS / 32];
+    __shared__ int s_i[ARGMAX_THREADS / 32];
+    const float *lg = logits + (size_t)blockIdx.x * n;
+    uint32_t bk = 0;            // below every non-NaN key (float_order_key(-inf) = 0x007FFFFF)
+    int bi = 0x7FFFFFFF;
+    for (int v = threadIdx.x; v < n; v += blockDim.x) {
+        const float f = __ldg(lg + v);
+        if (!isnan(f)) argmax_take(bk, bi, float_order_key(f), v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint32_t k = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
+        const int i = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        argmax_take(bk, bi, k, i);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        s_k[warp] = bk;
+        s_i[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) argmax_take(bk, bi, s_k[w], s_i[w]);
+        best[blockIdx.x] = (n <= 0 || isnan(__ldg(lg)) || bi == 0x7FFFFFFF) ? 0 : bi;
+    }
+}
+
 }  // namespace dsv4cu
 
 using namespace dsv4cu;
@@ -252,4 +299,21 @@ extern "C" int dsv4cu_round_bf16(float *x, size_t n, void *stream)
     round_bf16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(x, n);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_argmax(int *best, const float *logits, int n, int nt, void *stream)
+{
+    if (!best || !logits || n <= 0 || nt <= 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "argmax: bad args");
+    argmax_kernel<<<(unsigned)nt, ARGMAX_THREADS, 0, (cudaStream_t)stream>>>(logits, n, best);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_head(dsv4cu_ctx *ctx, float *logits, int *best, const float *x, const dsv4cu_qmat *head, int nt,
+                           void *stream)
+{
+    if (!ctx || !logits || !best || !x || !head) return dsv4cu_set_error(DSV4CU_ERR_ARG, "head: NULL argument");
+    int r = dsv4cu_mmq(ctx, logits, x, head, nt, stream);
+    if (r) return r;
+    return dsv4cu_argmax(best, logits, head->rows, nt, stream);
 }

@@ -88,6 +88,8 @@ def lib() -> C.CDLL:
             "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
             "dsv4cu_sparse_attn": (i, [vp, vp, vp, vp, i, vp, vp, i, i, i, f, vp]),
             "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
+            "dsv4cu_argmax": (i, [vp, vp, i, i, vp]),
+            "dsv4cu_head": (i, [vp, vp, vp, vp, vp, i, vp]),
             "dsv4cu_quantize_fp8": (i, [vp, vp, vp, i, i, vp]),
             "dsv4cu_quantize_fp4": (i, [vp, vp, vp, i, i, vp]),
             "dsv4cu_fill_normal": (i, [vp, sz, C.c_uint64, f, f, vp]),
@@ -389,6 +391,13 @@ class Device:
     def topk(self, idx, scores, n, k):
         check(self.L.dsv4cu_topk(self.ctx, self.ptr(idx), self.ptr(scores), n, k, self.stream()),
               "dsv4cu_topk")
+
+    def argmax(self, best, logits, n: int, nt: int = 1):
+        check(self.L.dsv4cu_argmax(self.ptr(best), self.ptr(logits), n, nt, self.stream()), "argmax")
+
+    def head(self, logits, best, x, m: QMat, nt: int = 1):
+        check(self.L.dsv4cu_head(self.ctx, self.ptr(logits), self.ptr(best), self.ptr(x), C.byref(m), nt,
+                                 self.stream()), "head")
 
     def sparse_attn(self, o, q, kv, kv_bf16, sink, idxs, h, d, topk, scale):
         check(self.L.dsv4cu_sparse_attn(self.ctx, self.ptr(o), self.ptr(q), self.ptr(kv), kv_bf16,

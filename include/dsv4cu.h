@@ -295,6 +295,19 @@ int dsv4cu_sparse_attn_noalloc(float *o, const float *q, const void *kv,
  * src/10_compute/dsv4_indexer.c:92-96). */
 int dsv4cu_indexer_offset(int *idxs, int n, int offset, void *stream);
 
+/* Greedy pick per row of logits [nt][n] into best[nt], with the reference's
+ * argmax rule (src/90_cli/dsv4_decode.c:128-133): the first index of the
+ * largest value, -0.0 equal to +0.0, NaNs never picked, and 0 when row[0] is
+ * NaN. */
+int dsv4cu_argmax(int *best, const float *logits, int n, int nt, void *stream);
+
+/* Output head (dsv4_head_from_h, src/90_cli/dsv4_decode.c:138-148, from the
+ * normalised hidden state on): logits[nt][head->rows] = dsv4cu_mmq(x, head)
+ * - BF16 in the reference, so the reference's bits - then best[nt] as
+ * dsv4cu_argmax. */
+int dsv4cu_head(dsv4cu_ctx *ctx, float *logits, int *best, const float *x, const dsv4cu_qmat *head, int nt,
+                void *stream);
+
 /* --------------------------------------------------- weight packing utility
  * Quantize fp32 [rows][cols] to the reference pack layouts: FP8 e4m3 with one
  * E8M0 scale per 128x128 block, or FP4 e2m1 with one E8M0 scale per 1x32

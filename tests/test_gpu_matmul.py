@@ -254,6 +254,52 @@ def test_nan_scale_gives_positive_quiet_nan(dev):
         assert not np.any(np.isnan(got[nan_rows:])), wdt
 
 
+def ref_argmax(lg):
+    """src/90_cli/dsv4_decode.c:128-133, literally."""
+    best = 0
+    for v in range(1, len(lg)):
+        if lg[v] > lg[best]:
+            best = v
+    return best
+
+
+def test_argmax_rule(dev):
+    import torch
+    rng = np.random.default_rng(21)
+    rows = []
+    a = rng.standard_normal(129280).astype(np.float32)
+    rows.append(a)
+    b = a.copy(); b[5] = b[77777] = b.max() + 1; rows.append(b)               # tie: lower index
+    c = a.copy(); c[0] = np.nan; rows.append(c)                               # NaN first: 0
+    d = a.copy(); d[1000] = np.nan; d[2000] = np.float32(50); rows.append(d)  # NaN skipped
+    e = np.full(129280, -np.inf, np.float32); rows.append(e)                  # all -inf: 0
+    f = np.zeros(129280, np.float32); f[:10] = -0.0; f[3] = 0.0; rows.append(f)  # -0 == +0: 0
+    g = np.full(129280, np.nan, np.float32); g[9] = 1.0; g[0] = 2.0; rows.append(g)
+    lg = np.stack(rows)
+    best = torch.empty(len(rows), dtype=torch.int32, device="cuda")
+    dev.argmax(best, torch.from_numpy(lg).cuda(), lg.shape[1], len(rows))
+    got = best.cpu().numpy()
+    want = [ref_argmax(r.tolist()) for r in lg]
+    assert got.tolist() == want
+
+
+def test_head_bf16_logits_and_pick(dev, orc):
+    """The output head: BF16 logits with the reference's bits, then the pick."""
+    import torch
+    rng = np.random.default_rng(22)
+    rows, cols, nt = 12800, 4096, 2
+    W = pack.bf16_bits((rng.standard_normal((rows, cols)) * 0.05).astype(np.float32))
+    x = rng.standard_normal((nt, cols)).astype(np.float32)
+    want = orc.mmq(x, oracle.qmat(W, None, 1, rows, cols))
+    logits = torch.empty((nt, rows), dtype=torch.float32, device="cuda")
+    best = torch.empty(nt, dtype=torch.int32, device="cuda")
+    dW = torch.from_numpy(W).cuda()
+    dev.head(logits, best, torch.from_numpy(x).cuda(), dev.qmat(dW, None, 1, rows, cols), nt)
+    got = logits.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert best.cpu().numpy().tolist() == [int(np.argmax(want[t])) for t in range(nt)]
+
+
 def test_fp8_n_fp4_n_bf16_n_entry_points(host, orc):
     rng = np.random.default_rng(4)
     W8, S8 = make_weights(rng, 2, 256, 512, 128, 128)
