@@ -89,6 +89,9 @@ def lib() -> C.CDLL:
             "dsv4cu_sparse_attn": (i, [vp, vp, vp, vp, i, vp, vp, i, i, i, f, vp]),
             "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
             "dsv4cu_argmax": (i, [vp, vp, i, i, vp]),
+            "dsv4cu_experts_load": (i, [C.POINTER(vp), vp, C.c_char_p, C.c_char_p, i, i, i, i, i, vp]),
+            "dsv4cu_experts_free": (None, [vp]),
+            "dsv4cu_experts_index": (i, [C.c_char_p, C.POINTER(i), C.POINTER(i), i, i, C.POINTER(C.c_int64)]),
             "dsv4cu_head": (i, [vp, vp, vp, vp, vp, i, vp]),
             "dsv4cu_quantize_fp8": (i, [vp, vp, vp, i, i, vp]),
             "dsv4cu_quantize_fp4": (i, [vp, vp, vp, i, i, vp]),
@@ -318,6 +321,19 @@ class Device:
                                   self.ptr(token_ids), ne, topk, route_scale, nt, self.stream()),
               "dsv4cu_route")
 
+    def experts_load(self, model_dir: str, index_dir: str, layer: int, first: int, count: int, hidden: int,
+                     inter: int):
+        """Routed experts [first, first + count) of `layer` from a pack into HBM:
+        (store handle, list of Expert descriptors)."""
+        h = C.c_void_p()
+        arr = (Expert * count)()
+        check(self.L.dsv4cu_experts_load(C.byref(h), arr, model_dir.encode(), index_dir.encode(), layer, first,
+                                         count, hidden, inter, self.stream()), "experts_load")
+        return h, list(arr)
+
+    def experts_free(self, h):
+        self.L.dsv4cu_experts_free(h)
+
     def moe_create(self, experts: list, shared: Expert | None, hidden: int, inter: int):
         """Prepare a MoE layer (dsv4cu_moe_create); returns an opaque handle."""
         arr = (Expert * len(experts))(*experts)
@@ -418,3 +434,16 @@ class Device:
 
     def round_bf16(self, x):
         check(self.L.dsv4cu_round_bf16(self.ptr(x), x.numel(), self.stream()), "round_bf16")
+
+
+def experts_index(index_dir: str, layer: int = -1, expert: int = -1):
+    """Host only: (n_layers, n_experts, records) of a pack's experts.idx;
+    records = six (shard, offset, bytes) for (layer, expert), or None."""
+    L = lib()
+    nl, ne = C.c_int(), C.c_int()
+    loc = (C.c_int64 * 18)()
+    want = layer >= 0
+    check(L.dsv4cu_experts_index(index_dir.encode(), C.byref(nl), C.byref(ne), layer, expert,
+                                 loc if want else None), "experts_index")
+    recs = [tuple(loc[3 * t:3 * t + 3]) for t in range(6)] if want else None
+    return nl.value, ne.value, recs

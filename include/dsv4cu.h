@@ -31,7 +31,8 @@ enum {
     DSV4CU_ERR_CUDA = -3,         /* a CUDA runtime call or launch failed     */
     DSV4CU_ERR_NOMEM = -4,        /* device allocation failed                 */
     DSV4CU_ERR_TIMEOUT = -5,      /* a bounded device wait expired            */
-    DSV4CU_ERR_COMM = -6          /* collective / peer exchange failed        */
+    DSV4CU_ERR_COMM = -6,         /* collective / peer exchange failed        */
+    DSV4CU_ERR_IO = -7            /* pack file missing, malformed or short    */
 };
 
 /* Weight storage tags; same values as the reference enum
@@ -147,6 +148,27 @@ int dsv4cu_swiglu(float *y, const float *gate, const float *up, int n,
  * w2 [hidden][inter]; FP4 (blk_c % 32 == 0) or FP8 (blk_c % 16 == 0), 16-byte
  * aligned weights; hidden and inter multiples of 128. */
 typedef struct dsv4cu_moe dsv4cu_moe;
+
+/* Routed experts of one layer read from the reference's pack into HBM (the
+ * experts.idx written by tools/pack_trunk.py and read by
+ * src/40_io/dsv4_st.c:65-87; shards = model_dir's *.safetensors in name
+ * order). Experts first .. first + count - 1 of `layer` are read once (pread
+ * into pinned staging, copied on `stream`, synchronised before return) into
+ * one device allocation owned by *out, and experts[0 .. count - 1] receive
+ * their FP4 e2m1 1x32 E8M0 descriptors (device pointers) for
+ * dsv4cu_moe_create. Every record's size is checked against hidden / inter;
+ * a missing, malformed or short pack returns DSV4CU_ERR_IO. For expert
+ * parallelism rank r loads [r * per_rank, (r + 1) * per_rank). */
+typedef struct dsv4cu_expert_store dsv4cu_expert_store;
+int  dsv4cu_experts_load(dsv4cu_expert_store **out, dsv4cu_expert *experts, const char *model_dir,
+                         const char *index_dir, int layer, int first, int count, int hidden, int inter,
+                         void *stream);
+void dsv4cu_experts_free(dsv4cu_expert_store *store);
+/* Host only: the index's shape, and (when loc != NULL) the six records of
+ * (layer, expert) as loc[3 t + {0, 1, 2}] = shard, offset, bytes in the order
+ * w1, w1 scales, w2, w2 scales, w3, w3 scales. */
+int  dsv4cu_experts_index(const char *index_dir, int *n_layers, int *n_experts, int layer, int expert,
+                          int64_t *loc);
 int  dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts, int n_experts,
                        const dsv4cu_expert *shared, int hidden, int inter);
 void dsv4cu_moe_destroy(dsv4cu_moe *layer);
