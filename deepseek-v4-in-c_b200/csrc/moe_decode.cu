@@ -533,7 +533,9 @@ static int expert_check(const dsv4cu_expert &e, int hidden, int inter, const cha
             return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_create: %s matrix %d format %d blk %dx%d", what, i,
                                     q.wdt, q.blk_r, q.blk_c);
         if (!tmap_weights_ok(&q))
-            return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_create: %s matrix %d not 16-byte aligned", what, i);
+            return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED,
+                                    "moe_create: %s matrix %d: rows must be >= 128 bytes, a multiple of 16, on a "
+                                    "16-byte aligned base", what, i);
     }
     if (e.w1.wdt != e.w3.wdt) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_create: %s w1/w3 formats differ", what);
     return DSV4CU_OK;

@@ -17,7 +17,7 @@ import oracle
 import pack
 import packfix
 
-H, I = 256, 128
+H, I = 256, 256
 
 
 def test_index_records_and_shard_order(tmp_path):
@@ -47,13 +47,13 @@ def test_index_rejects_bad_files(tmp_path):
 
 
 def test_load_rejects_mismatched_sizes_before_touching_the_device(tmp_path):
-    """inter 256 against a pack of inter 128: every record is checked first."""
+    """inter 512 against a pack of inter 256: every record is checked first."""
     import ctypes as C
     packfix.write_pack(str(tmp_path), 1, 2, H, I)
     L = dsv4cu.lib()
     h = C.c_void_p()
     arr = (dsv4cu.Expert * 2)()
-    rc = L.dsv4cu_experts_load(C.byref(h), arr, str(tmp_path).encode(), str(tmp_path).encode(), 0, 0, 2, H, 256,
+    rc = L.dsv4cu_experts_load(C.byref(h), arr, str(tmp_path).encode(), str(tmp_path).encode(), 0, 0, 2, H, 512,
                                None)
     assert rc == -7 and "want" in dsv4cu.last_error()
     rc = L.dsv4cu_experts_load(C.byref(h), arr, str(tmp_path).encode(), str(tmp_path).encode(), 0, 1, 2, H, I, None)
