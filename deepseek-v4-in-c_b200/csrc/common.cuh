@@ -118,16 +118,6 @@ DSV4CU_DEV void mma_f16_16816(float &d0, float &d1, float &d2, float &d3,
                  : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-DSV4CU_DEV void mma_bf16_16816(float &d0, float &d1, float &d2, float &d3,
-                               uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                               uint32_t b0, uint32_t b1)
-{
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-                 "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                 : "+f"(d0), "+f"(d1), "+f"(d2), "+f"(d3)
-                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 // Streaming 16-byte load that does not allocate in L1 (weights are read once).
 DSV4CU_DEV uint4 ld_stream16(const void *p)
 {

@@ -7,7 +7,7 @@
 //     L1 allocation): lane (g, c) = (lane/4, lane%4) reads chunk c of the
 //     segment for rows g and g+8, so a warp load covers 16 rows x 64 bytes.
 //   * The chunk is widened in registers with the exact hardware converters
-//     (e4m3 / e2m1 -> f16; bf16 stays bf16) straight into mma.sync A fragments.
+//     (e4m3 / e2m1 -> f16) straight into mma.sync A fragments.
 //     K positions inside an MMA are a free permutation of a dot product, so a
 //     lane feeds its own contiguous chunk.
 //   * The activation enters as B = [hi | lo] f16 pairs (x split exactly after
@@ -35,7 +35,7 @@ struct MatArgs {
     int row_bytes;  // stored bytes per weight row (multiple of 16)
 };
 
-// Activation operand: per token row, f16 (or bf16) hi and lo halves and the
+// Activation operand: per token row, f16 hi and lo halves and the
 // per-32 power-of-two factor 2^-P that undoes the prescale.
 struct XArgs {
     const uint16_t *xh;
@@ -47,10 +47,11 @@ struct XArgs {
 
 template <int FMT> struct Fmt {
     // Logical elements in one 16-byte chunk, and MMAs (4 elements each) per chunk.
-    static constexpr int CE = FMT == DSV4CU_WFP4 ? 32 : (FMT == DSV4CU_WFP8 ? 16 : 8);
+    static_assert(FMT == DSV4CU_WFP4 || FMT == DSV4CU_WFP8, "FP4 or FP8 weights");
+    static constexpr int CE = FMT == DSV4CU_WFP4 ? 32 : 16;
     static constexpr int MMAS = CE / 4;
     // element offset of byte offset b
-    static DSV4CU_DEV int elem(int b) { return FMT == DSV4CU_WFP4 ? 2 * b : (FMT == DSV4CU_WFP8 ? b : b / 2); }
+    static DSV4CU_DEV int elem(int b) { return FMT == DSV4CU_WFP4 ? 2 * b : b; }
 };
 
 // Host-side check that the fast path covers a geometry (BF16 weights take
@@ -75,12 +76,9 @@ DSV4CU_DEV void decode_chunk(const uint4 &q, uint32_t (&lo)[Fmt<FMT>::MMAS], uin
             lo[2 * i] = h0; hi[2 * i] = h1;
             lo[2 * i + 1] = h2; hi[2 * i + 1] = h3;
         }
-    } else if constexpr (FMT == DSV4CU_WFP8) {
+    } else {
 #pragma unroll
         for (int i = 0; i < 4; i++) cvt_e4m3x4(wv[i], lo[i], hi[i]);
-    } else {
-        lo[0] = wv[0]; hi[0] = wv[1];
-        lo[1] = wv[2]; hi[1] = wv[3];
     }
 }
 
@@ -133,12 +131,9 @@ DSV4CU_DEV void gemv_tile16(const MatArgs &m, int row0, int seg_begin, int seg_e
             decode_chunk<FMT>(w0, a0, a2);
             decode_chunk<FMT>(w1, a1, a3);
 
-            float sc0 = 1.0f, sc1 = 1.0f;
-            if constexpr (FMT != DSV4CU_WBF16) {
-                const int kb = cvalid ? k0 / m.blk_c : 0;
-                sc0 = (cvalid && v0) ? e8m0_to_f32(__ldg(m.s + (size_t)sr0 * m.s_cols + kb)) : 0.0f;
-                sc1 = (cvalid && v1) ? e8m0_to_f32(__ldg(m.s + (size_t)sr1 * m.s_cols + kb)) : 0.0f;
-            }
+            const int kb = cvalid ? k0 / m.blk_c : 0;
+            const float sc0 = (cvalid && v0) ? e8m0_to_f32(__ldg(m.s + (size_t)sr0 * m.s_cols + kb)) : 0.0f;
+            const float sc1 = (cvalid && v1) ? e8m0_to_f32(__ldg(m.s + (size_t)sr1 * m.s_cols + kb)) : 0.0f;
 #pragma unroll
             for (int t = 0; t < NT; t++) {
                 if (t >= nt_valid) break;
@@ -149,10 +144,7 @@ DSV4CU_DEV void gemv_tile16(const MatArgs &m, int row0, int seg_begin, int seg_e
                 for (int j = 0; j < MM; j++) {
                     uint2 b = make_uint2(0u, 0u);
                     if (bact && cvalid) b = __ldg(reinterpret_cast<const uint2 *>(xb + 4 * j));
-                    if constexpr (FMT == DSV4CU_WBF16)
-                        mma_bf16_16816(d0, d1, d2, d3, a0[j], a1[j], a2[j], a3[j], b.x, b.y);
-                    else
-                        mma_f16_16816(d0, d1, d2, d3, a0[j], a1[j], a2[j], a3[j], b.x, b.y);
+                    mma_f16_16816(d0, d1, d2, d3, a0[j], a1[j], a2[j], a3[j], b.x, b.y);
                 }
                 const float xsv = cvalid ? __ldg(x.xs + (size_t)xr * (x.ldx >> 5) + (k0 >> 5)) : 0.0f;
                 acc[t][0] = fmaf((d0 + d1) * xsv, sc0, acc[t][0]);
