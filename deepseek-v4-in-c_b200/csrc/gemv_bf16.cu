@@ -27,8 +27,7 @@
 // shared-memory stages with tensor-map TMA (16-row x 128-byte boxes, 128-byte
 // swizzle, 256 bytes of every row per stage) and the stage's 128 activation
 // columns as doubles with a bulk copy; the consumers read both from shared
-// memory (R row groups per warp share every activation load). Every wait is
-// bounded and records an error code instead of hanging.
+// memory. Every wait is bounded and records an error code instead of hanging.
 // bf16_chain_kernel (any other geometry): each lane loads its row's 16-byte
 // words directly, the next 64-column group in flight, and reads xd through L1.
 #include "common.cuh"
@@ -188,19 +187,25 @@ __global__ void __launch_bounds__(BFC_THREADS) bf16_chain_kernel(const uint16_t 
 }
 
 // ------------------------------------------------------- TMA-staged variant
-// Stage layout: [8 consumer warps][R row groups][2 boxes of 16 rows x 128 B]
+// Stage layout: [CW consumer warps][R row groups][2 boxes of 16 rows x 128 B]
 // of weights, then [NT][128] activation doubles. Stage sizes are multiples of
 // 1 KB, so every box stays on the 1024-byte boundary of the 128-byte swizzle.
-template <int R, int NT>
+// One CTA per SM: the stages fill about 220 KB. The kernel is latency-bound
+// (dependent widening -> fma chains per lane), so CW = 16 consumer warps with
+// one row group each keep twice the warps in flight of 8 warps with two (the
+// four-token tiles hold 4x the chains per lane and use 12 warps to stay in
+// registers).
+template <int R, int NT, int CW>
 struct BfcCfg {
-    static constexpr int STAGES = 6 / R;
     static constexpr int STREAM = 16 * R * TMA_SB;     // weight bytes per warp per stage
-    static constexpr int WBYTES = 8 * STREAM;
+    static constexpr int WBYTES = CW * STREAM;
     static constexpr int XBYTES = NT * 128 * 8;
     static constexpr int STAGE = WBYTES + XBYTES;
+    static constexpr int STAGES = (220 * 1024) / STAGE < 6 ? (220 * 1024) / STAGE : 6;
     static constexpr int SMEM = 1024 + STAGES * STAGE + 2 * STAGES * 8;
+    static constexpr int THREADS = 32 * (CW + 1);      // CW consumer warps + 1 producer warp
+    static_assert(STAGES >= 2 && CW <= 32, "stage ring");
 };
-constexpr int BFT_THREADS = 288;                      // 8 consumer warps + 1 producer warp
 
 DSV4CU_DEV void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar)
 {
@@ -209,12 +214,12 @@ DSV4CU_DEV void bulk_copy_g2s(void *dst, const void *src, uint32_t bytes, uint64
                  : "memory");
 }
 
-template <int R, int NT>
-__global__ void __launch_bounds__(BFT_THREADS, 1) bf16_chain_tma_kernel(
+template <int R, int NT, int CW>
+__global__ void __launch_bounds__(BfcCfg<R, NT, CW>::THREADS, 1) bf16_chain_tma_kernel(
     const __grid_constant__ CUtensorMap tw, const uint16_t *__restrict__ W, int rows, int cols,
     const double *__restrict__ xd, int ldxd, int nt, float *__restrict__ y, int *__restrict__ err)
 {
-    using C = BfcCfg<R, NT>;
+    using C = BfcCfg<R, NT, CW>;
     extern __shared__ __align__(128) unsigned char dsmem[];
     unsigned char *base = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -222,7 +227,7 @@ __global__ void __launch_bounds__(BFT_THREADS, 1) bf16_chain_tma_kernel(
     uint64_t *empty = full + C::STAGES;
     __shared__ int abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row_cta = blockIdx.x * 128 * R;
+    const int row_cta = blockIdx.x * 16 * R * CW;
     const int t0 = blockIdx.y * NT, ntile = min(NT, nt - t0);
     const int M = cols >> 4;                       // chain steps; stage k holds steps 8k .. 8k + 7
     const int nst = (M + 7) >> 3;
@@ -231,15 +236,15 @@ __global__ void __launch_bounds__(BFT_THREADS, 1) bf16_chain_tma_kernel(
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; s++) {
             mbar_init(full + s, 1);
-            mbar_init(empty + s, 8);
+            mbar_init(empty + s, CW);
         }
         abort_flag = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == 8) {
-        // ---------------- producer: lane w < 8 loads warp w's boxes, lane t < ntile token t's columns
+    if (warp == CW) {
+        // ---------------- producer: lane w < CW loads warp w's boxes, lane t < ntile token t's columns
         const int row_w = row_cta + 16 * R * lane;
         for (int k = 0; k < nst; k++) {
             const int s = k % C::STAGES;
@@ -254,7 +259,7 @@ __global__ void __launch_bounds__(BFT_THREADS, 1) bf16_chain_tma_kernel(
             }
             const int x0 = k * TMA_SB;
             uint32_t bytes = lane < ntile ? 1024u : 0u;
-            if (lane < 8) {
+            if (lane < CW) {
 #pragma unroll
                 for (int g = 0; g < R; g++) {
                     const bool in = row_w + 16 * g < rows;
@@ -266,7 +271,7 @@ __global__ void __launch_bounds__(BFT_THREADS, 1) bf16_chain_tma_kernel(
             if (lane == 0) mbar_arrive_expect_tx(full + s, bytes);
             __syncwarp();
             unsigned char *st = base + s * C::STAGE;
-            if (lane < 8) {
+            if (lane < CW) {
 #pragma unroll
                 for (int g = 0; g < R; g++) {
                     const int r0 = row_w + 16 * g;
@@ -362,16 +367,17 @@ size_t bf16_chain_workspace(int cols, int nt)
     return dsv4cu_align256((size_t)nt * bf16_ldxd(cols) * sizeof(double));
 }
 
-template <int R, int NT>
+template <int R, int NT, int CW>
 static int bf16_tma_launch(const CUtensorMap &tw, const dsv4cu_qmat *q, const double *xd, int ldxd, int nt, float *y,
                            int *err, cudaStream_t st)
 {
-    using C = BfcCfg<R, NT>;
+    using C = BfcCfg<R, NT, CW>;
     static SmemLimit lim;
-    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)bf16_chain_tma_kernel<R, NT>, C::SMEM));
-    const dim3 grid((unsigned)((q->rows + 128 * R - 1) / (128 * R)), (unsigned)((nt + NT - 1) / NT));
-    bf16_chain_tma_kernel<R, NT><<<grid, BFT_THREADS, C::SMEM, st>>>(tw, (const uint16_t *)q->w, q->rows, q->cols, xd,
-                                                                    ldxd, nt, y, err);
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)bf16_chain_tma_kernel<R, NT, CW>, C::SMEM));
+    constexpr int ROWS = 16 * R * CW;
+    const dim3 grid((unsigned)((q->rows + ROWS - 1) / ROWS), (unsigned)((nt + NT - 1) / NT));
+    bf16_chain_tma_kernel<R, NT, CW><<<grid, C::THREADS, C::SMEM, st>>>(tw, (const uint16_t *)q->w, q->rows, q->cols,
+                                                                       xd, ldxd, nt, y, err);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
 }
@@ -390,8 +396,8 @@ int bf16_chain_run(float *y, const float *x, const dsv4cu_qmat *q, int nt, void 
         int staged = 0;
         int r = tmap_encode(q, &tw, nullptr, &staged);
         if (r) return r;
-        return nt == 1 ? bf16_tma_launch<2, 1>(tw, q, xd, ldxd, nt, y, err, st)
-                       : bf16_tma_launch<1, 4>(tw, q, xd, ldxd, nt, y, err, st);
+        return nt == 1 ? bf16_tma_launch<1, 1, 16>(tw, q, xd, ldxd, nt, y, err, st)
+                       : bf16_tma_launch<1, 4, 12>(tw, q, xd, ldxd, nt, y, err, st);   // 4-token chains: registers
     }
     const bool vec = cols % 8 == 0 && ((uintptr_t)W & 15u) == 0;
     const unsigned gx = (unsigned)((rows + 16 * BFC_WARPS - 1) / (16 * BFC_WARPS));
