@@ -177,6 +177,71 @@ __global__ void round_bf16_kernel(float *x, size_t n)
     if (i < n) x[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
 }
 
+// ------------------------------------------------------------- rmsnorm
+// dsv4_rmsnorm (src/10_compute/dsv4_ops.c:26-33): sum of x^2 in double in
+// index order, inv = (float)(1 / sqrt(sum / n + eps)), y = w * (x * inv).
+// The only rounding-order-dependent step is the sequential sum; everything
+// after it is monotone in the sum. So the CTA sums in parallel (S', within
+// (n / threads + log2 threads) ulps of the exact sum, as the sequential sum T
+// is within (n - 1) ulps), evaluates the reference's inv at both ends of an
+// interval that must hold T, and uses that inv when the two agree - then it
+// is the reference's inv whatever T's exact rounding was. When they differ
+// (a sum within about n ulps of a float rounding boundary of inv, or a
+// non-finite or tiny sum) one thread replays the reference's sequential sum.
+// Each square of a float is exact in double, so S' and T differ only by
+// the sums' roundings.
+constexpr int NORM_THREADS = 256;
+
+DSV4CU_DEV float norm_inv(double sum, int n, float eps)
+{
+    return __double2float_rn(1.0 / sqrt(__dadd_rn(__ddiv_rn(sum, (double)n), (double)eps)));
+}
+
+__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(float *__restrict__ y, const float *__restrict__ x,
+                                                               const float *__restrict__ w, int n, float eps)
+{
+    __shared__ double red[NORM_THREADS / 32];
+    __shared__ float s_inv;
+    const float *xr = x + (size_t)blockIdx.x * n;
+    float *yr = y + (size_t)blockIdx.x * n;
+    double acc = 0.0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const double v = (double)xr[i];
+        acc = __dadd_rn(acc, __dmul_rn(v, v));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xFFFFFFFFu, acc, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double s = 0.0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) s = __dadd_rn(s, red[i]);
+        // Relative bound on |T - S'|: (n - 1) + n / threads + log2(threads) + 5 unit
+        // roundoffs, doubled, plus the two roundings of the interval ends.
+        const double g = (2.0 * n + 64.0) * 0x1.0p-53;
+        bool done = false;
+        if (isfinite(s) && s > 0x1.0p-900) {
+            const float lo = norm_inv(s * (1.0 + g) * (1.0 + 0x1.0p-50), n, eps);
+            const float hi = norm_inv(s * (1.0 - g) * (1.0 - 0x1.0p-50), n, eps);
+            if (lo == hi) {
+                s_inv = lo;
+                done = true;
+            }
+        }
+        if (!done) {
+            double t = 0.0;
+            for (int i = 0; i < n; i++) {
+                const double v = (double)xr[i];
+                t = __dadd_rn(t, __dmul_rn(v, v));
+            }
+            s_inv = norm_inv(t, n, eps);
+        }
+    }
+    __syncthreads();
+    const float inv = s_inv;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fmul_rn(w[i], __fmul_rn(xr[i], inv));
+}
+
 // ------------------------------------------------------------- argmax
 // Greedy pick over a row of logits, as the reference's argmax
 // (src/90_cli/dsv4_decode.c:128-133): best starts at 0 and moves to v only
@@ -316,4 +381,12 @@ extern "C" int dsv4cu_head(dsv4cu_ctx *ctx, float *logits, int *best, const floa
     int r = dsv4cu_mmq(ctx, logits, x, head, nt, stream);
     if (r) return r;
     return dsv4cu_argmax(best, logits, head->rows, nt, stream);
+}
+
+extern "C" int dsv4cu_rmsnorm(float *y, const float *x, const float *w, int n, int nt, float eps, void *stream)
+{
+    if (!y || !x || !w || n <= 0 || nt <= 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "rmsnorm: bad args");
+    rmsnorm_kernel<<<(unsigned)nt, NORM_THREADS, 0, (cudaStream_t)stream>>>(y, x, w, n, eps);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
 }

@@ -89,6 +89,7 @@ def lib() -> C.CDLL:
             "dsv4cu_sparse_attn": (i, [vp, vp, vp, vp, i, vp, vp, i, i, i, f, vp]),
             "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
             "dsv4cu_argmax": (i, [vp, vp, i, i, vp]),
+            "dsv4cu_rmsnorm": (i, [vp, vp, vp, i, i, f, vp]),
             "dsv4cu_experts_load": (i, [C.POINTER(vp), vp, C.c_char_p, C.c_char_p, i, i, i, i, i, vp]),
             "dsv4cu_experts_free": (None, [vp]),
             "dsv4cu_experts_index": (i, [C.c_char_p, C.POINTER(i), C.POINTER(i), i, i, C.POINTER(C.c_int64)]),
@@ -407,6 +408,9 @@ class Device:
     def topk(self, idx, scores, n, k):
         check(self.L.dsv4cu_topk(self.ctx, self.ptr(idx), self.ptr(scores), n, k, self.stream()),
               "dsv4cu_topk")
+
+    def rmsnorm(self, y, x, w, n: int, nt: int = 1, eps: float = 1e-6):
+        check(self.L.dsv4cu_rmsnorm(self.ptr(y), self.ptr(x), self.ptr(w), n, nt, eps, self.stream()), "rmsnorm")
 
     def argmax(self, best, logits, n: int, nt: int = 1):
         check(self.L.dsv4cu_argmax(self.ptr(best), self.ptr(logits), n, nt, self.stream()), "argmax")

@@ -317,6 +317,14 @@ int dsv4cu_sparse_attn_noalloc(float *o, const float *q, const void *kv,
  * src/10_compute/dsv4_indexer.c:92-96). */
 int dsv4cu_indexer_offset(int *idxs, int n, int offset, void *stream);
 
+/* RMS norm of nt rows of n floats (dsv4_rmsnorm, src/10_compute/dsv4_ops.c:
+ * 26-33): y = w * (x * inv), inv = (float)(1 / sqrt(sum(x^2) / n + eps)) with
+ * the sum in double. The result has the reference's bits: the sum runs in
+ * parallel with a bound on its distance from the reference's sequential sum,
+ * and a row whose inv that bound cannot pin down is replayed in the
+ * reference's order. y may alias x. */
+int dsv4cu_rmsnorm(float *y, const float *x, const float *w, int n, int nt, float eps, void *stream);
+
 /* Greedy pick per row of logits [nt][n] into best[nt], with the reference's
  * argmax rule (src/90_cli/dsv4_decode.c:128-133): the first index of the
  * largest value, -0.0 equal to +0.0, NaNs never picked, and 0 when row[0] is

@@ -158,6 +158,18 @@ void orc_route(int *idx, float *wts, float *scores, float *orig,
 /* ---------------------------------------------------------------- SwiGLU --
  * src/10_compute/dsv4_ops.c:61-79: up clamped to [-limit, limit], gate clamped
  * from ABOVE only, silu(g) = g / (1 + expf(-g)); limit <= 0 disables both. */
+/* src/10_compute/dsv4_ops.c:26-33 (dsv4_rmsnorm): the sum of squares in
+ * double in index order, mean = sum / n, inv = (float)(1 / sqrt(mean + eps)),
+ * y = w * (x * inv) in float. */
+void orc_rmsnorm(float *y, const float *x, const float *w, int n, float eps)
+{
+    double sum = 0.0;
+    for (int i = 0; i < n; i++) sum += (double)x[i] * (double)x[i];
+    const double mean = sum / (double)n;
+    const float inv = (float)(1.0 / sqrt(mean + (double)eps));
+    for (int i = 0; i < n; i++) y[i] = w[i] * (x[i] * inv);
+}
+
 void orc_swiglu(float *y, const float *gate, const float *up, int n, float limit)
 {
     for (int i = 0; i < n; i++) {

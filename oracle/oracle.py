@@ -70,6 +70,7 @@ class _Common:
         f("sparse_attn").restype = None
         f("route").restype = None
         f("swiglu").restype = None
+        f("rmsnorm").restype = None
 
     def fn(self, name):
         return getattr(self.lib, self.pf + name)
@@ -92,6 +93,13 @@ class _Common:
         self.fn("swiglu")(_p(y), _p(np.ascontiguousarray(gate, np.float32)),
                           _p(np.ascontiguousarray(up, np.float32)), C.c_int(gate.size),
                           C.c_float(limit))
+        return y
+
+    def rmsnorm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros_like(x)
+        self.fn("rmsnorm")(_p(y), _p(x), _p(np.ascontiguousarray(w, np.float32)), C.c_int(x.size),
+                           C.c_float(eps))
         return y
 
     def indexer_score(self, q, kv, weights):

@@ -1,0 +1,62 @@
+"""dsv4cu_rmsnorm against the oracle's dsv4_rmsnorm (src/10_compute/dsv4_ops.c:26-33),
+bit for bit: ordinary rows of the engine's widths, many rows at once (the
+parallel sum with its rounding certificate), and rows that take the
+sequential replay (a zero row, NaN, inf), subnormal inputs, and y aliasing x."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(dev, x, w, eps):
+    import torch
+    nt, n = x.shape
+    dx = torch.from_numpy(np.ascontiguousarray(x)).cuda()
+    dy = torch.empty_like(dx)
+    dev.rmsnorm(dy, dx, torch.from_numpy(w).cuda(), n, nt, eps)
+    return dy.cpu().numpy(), dx
+
+
+def _want(orc, x, w, eps):
+    return np.stack([orc.rmsnorm(r, w, eps) for r in x])
+
+
+@pytest.mark.parametrize("n", [1, 7, 512, 4096, 7168])
+def test_rmsnorm_bitwise(dev, orc, n):
+    rng = np.random.default_rng(n)
+    x = (rng.standard_normal((6, n)) * np.array([1e-3, 0.1, 1, 3, 40, 1e4])[:, None]).astype(np.float32)
+    w = rng.standard_normal(n).astype(np.float32)
+    got, _ = _run(dev, x, w, 1e-6)
+    assert np.array_equal(got.view(np.uint32), _want(orc, x, w, 1e-6).view(np.uint32))
+
+
+def test_rmsnorm_many_rows(dev, orc):
+    rng = np.random.default_rng(3)
+    n, nt = 4096, 1500
+    x = (rng.standard_normal((nt, n)) * rng.uniform(0.01, 10, (nt, 1))).astype(np.float32)
+    w = (1 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    got, _ = _run(dev, x, w, 1e-6)
+    assert np.array_equal(got.view(np.uint32), _want(orc, x, w, 1e-6).view(np.uint32))
+
+
+def test_rmsnorm_replay_rows_and_alias(dev, orc):
+    import torch
+    rng = np.random.default_rng(4)
+    n = 1024
+    x = rng.standard_normal((5, n)).astype(np.float32)
+    x[0] = 0.0
+    x[1, 17] = np.nan
+    x[2, 5] = np.inf
+    x[3] *= np.float32(1e-40)          # float subnormal inputs
+    w = rng.standard_normal(n).astype(np.float32)
+    got, _ = _run(dev, x, w, 1e-6)
+    want = _want(orc, x, w, 1e-6)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    fin = ~np.isnan(want)
+    assert np.array_equal(got[fin].view(np.uint32), want[fin].view(np.uint32))
+    # in place: y aliases x
+    dx = torch.from_numpy(x[4:].copy()).cuda()
+    dev.rmsnorm(dx, dx, torch.from_numpy(w).cuda(), n, 1, 1e-6)
+    assert np.array_equal(dx.cpu().numpy().view(np.uint32), want[4:].view(np.uint32))
