@@ -177,6 +177,36 @@ __global__ void round_bf16_kernel(float *x, size_t n)
     if (i < n) x[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
 }
 
+// ------------------------------------------------------------- rope
+// dsv4_rope_apply (src/10_compute/dsv4_rope.c) over v [nt][nh][head_dim]:
+// the last rd dims of every head are (re, im) pairs rotated by table entry
+// (pos[t], i), -sin when inverse. One thread per pair, the reference's float
+// multiplies and one subtract / add, uncontracted, so the bits match.
+__global__ void rope_kernel(float *__restrict__ v, int nt, int nh, int head_dim, int rd,
+                            const float *__restrict__ cs, const float *__restrict__ sn,
+                            const int *__restrict__ pos, int table_half, int n_pos, int inverse,
+                            int *__restrict__ err)
+{
+    const int half = rd >> 1;
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)nt * nh * half) return;
+    const int j = (int)(i % half);
+    const long vh = i / half;
+    const int t = (int)(vh / nh);
+    const int p = __ldg(pos + t);
+    if (p < 0 || p >= n_pos) {
+        if (err) atomicCAS(err, 0, 41);
+        return;
+    }
+    float *tail = v + vh * head_dim + (head_dim - rd);
+    const float ci = __ldg(cs + (size_t)p * table_half + j);
+    const float s0 = __ldg(sn + (size_t)p * table_half + j);
+    const float si = inverse ? __fmul_rn(-1.0f, s0) : s0;
+    const float re = tail[2 * j], im = tail[2 * j + 1];
+    tail[2 * j] = __fsub_rn(__fmul_rn(re, ci), __fmul_rn(im, si));
+    tail[2 * j + 1] = __fadd_rn(__fmul_rn(re, si), __fmul_rn(im, ci));
+}
+
 // ------------------------------------------------------------- rmsnorm
 // dsv4_rmsnorm (src/10_compute/dsv4_ops.c:26-33): sum of x^2 in double in
 // index order, inv = (float)(1 / sqrt(sum / n + eps)), y = w * (x * inv).
@@ -387,6 +417,20 @@ extern "C" int dsv4cu_rmsnorm(float *y, const float *x, const float *w, int n, i
 {
     if (!y || !x || !w || n <= 0 || nt <= 0) return dsv4cu_set_error(DSV4CU_ERR_ARG, "rmsnorm: bad args");
     rmsnorm_kernel<<<(unsigned)nt, NORM_THREADS, 0, (cudaStream_t)stream>>>(y, x, w, n, eps);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_rope_apply(dsv4cu_ctx *ctx, float *v, int nt, int nh, int head_dim, int rd, const float *cs,
+                                 const float *sn, const int *pos, int table_half, int n_pos, int inverse,
+                                 void *stream)
+{
+    if (!v || !cs || !sn || !pos || nt <= 0 || nh <= 0 || rd <= 0 || rd % 2 || rd > head_dim ||
+        rd / 2 > table_half || n_pos <= 0)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "rope_apply: bad args");
+    const long n = (long)nt * nh * (rd / 2);
+    rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+        v, nt, nh, head_dim, rd, cs, sn, pos, table_half, n_pos, inverse, ctx ? ctx->status : nullptr);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
 }

@@ -90,6 +90,7 @@ def lib() -> C.CDLL:
             "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
             "dsv4cu_argmax": (i, [vp, vp, i, i, vp]),
             "dsv4cu_rmsnorm": (i, [vp, vp, vp, i, i, f, vp]),
+            "dsv4cu_rope_apply": (i, [vp, vp, i, i, i, i, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_experts_load": (i, [C.POINTER(vp), vp, C.c_char_p, C.c_char_p, i, i, i, i, i, vp]),
             "dsv4cu_experts_free": (None, [vp]),
             "dsv4cu_experts_index": (i, [C.c_char_p, C.POINTER(i), C.POINTER(i), i, i, C.POINTER(C.c_int64)]),
@@ -411,6 +412,12 @@ class Device:
 
     def rmsnorm(self, y, x, w, n: int, nt: int = 1, eps: float = 1e-6):
         check(self.L.dsv4cu_rmsnorm(self.ptr(y), self.ptr(x), self.ptr(w), n, nt, eps, self.stream()), "rmsnorm")
+
+    def rope_apply(self, v, nt, nh, head_dim, rd, cs, sn, pos, inverse=0):
+        """In place on v [nt][nh][head_dim]; cs / sn device [n_pos][table_half]; pos device int32 [nt]."""
+        check(self.L.dsv4cu_rope_apply(self.ctx, self.ptr(v), nt, nh, head_dim, rd, self.ptr(cs), self.ptr(sn),
+                                       self.ptr(pos), cs.shape[1], cs.shape[0], inverse, self.stream()),
+              "rope_apply")
 
     def argmax(self, best, logits, n: int, nt: int = 1):
         check(self.L.dsv4cu_argmax(self.ptr(best), self.ptr(logits), n, nt, self.stream()), "argmax")

@@ -325,6 +325,16 @@ int dsv4cu_indexer_offset(int *idxs, int n, int offset, void *stream);
  * reference's order. y may alias x. */
 int dsv4cu_rmsnorm(float *y, const float *x, const float *w, int n, int nt, float eps, void *stream);
 
+/* Rotary embedding in place (dsv4_rope_apply, src/10_compute/dsv4_rope.c)
+ * over v [nt][nh][head_dim]: the last rd dims of each head of token t are
+ * rotated by row pos[t] of the device tables cs / sn [n_pos][table_half]
+ * (built once on the host with the reference's dsv4_rope_table and copied
+ * up), with -sin when inverse. Same float operations as the reference, so the
+ * same bits. pos is a device array; a position outside [0, n_pos) leaves that
+ * token's heads unchanged and sets status code 41 (dsv4cu_ctx_status). */
+int dsv4cu_rope_apply(dsv4cu_ctx *ctx, float *v, int nt, int nh, int head_dim, int rd, const float *cs,
+                      const float *sn, const int *pos, int table_half, int n_pos, int inverse, void *stream);
+
 /* Greedy pick per row of logits [nt][n] into best[nt], with the reference's
  * argmax rule (src/90_cli/dsv4_decode.c:128-133): the first index of the
  * largest value, -0.0 equal to +0.0, NaNs never picked, and 0 when row[0] is

@@ -158,6 +158,23 @@ void orc_route(int *idx, float *wts, float *scores, float *orig,
 /* ---------------------------------------------------------------- SwiGLU --
  * src/10_compute/dsv4_ops.c:61-79: up clamped to [-limit, limit], gate clamped
  * from ABOVE only, silu(g) = g / (1 + expf(-g)); limit <= 0 disables both. */
+/* src/10_compute/dsv4_rope.c (dsv4_rope_apply): the last rd dims of v as
+ * interleaved (re, im) pairs rotated by table entry (pos, i); inverse uses
+ * -sin. Float multiplies and one add or subtract per output, uncontracted. */
+void orc_rope_apply(float *v, int head_dim, int rd, const float *cs, const float *sn, int pos, int table_half,
+                    int inverse)
+{
+    float *tail = v + (head_dim - rd);
+    const float *c = cs + (size_t)pos * table_half, *s = sn + (size_t)pos * table_half;
+    const float sgn = inverse ? -1.0f : 1.0f;
+    for (int i = 0; i < rd / 2; i++) {
+        const float re = tail[2 * i], im = tail[2 * i + 1];
+        const float ci = c[i], si = sgn * s[i];
+        tail[2 * i] = re * ci - im * si;
+        tail[2 * i + 1] = re * si + im * ci;
+    }
+}
+
 /* src/10_compute/dsv4_ops.c:26-33 (dsv4_rmsnorm): the sum of squares in
  * double in index order, mean = sum / n, inv = (float)(1 / sqrt(mean + eps)),
  * y = w * (x * inv) in float. */

@@ -44,6 +44,8 @@ int  orc_mmq_n(float *y, const float *x, const OrcQMat *m, int nt);
 void orc_route(int *idx, float *wts, float *scores, float *orig,
                const float *bias, const int64_t *tid2eid, int token_id,
                int n_experts, int topk, float route_scale);
+void orc_rope_apply(float *v, int head_dim, int rd, const float *cs, const float *sn, int pos, int table_half,
+                    int inverse);
 void orc_rmsnorm(float *y, const float *x, const float *w, int n, float eps);
 void orc_swiglu(float *y, const float *gate, const float *up, int n,
                 float limit);

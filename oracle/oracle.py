@@ -71,6 +71,7 @@ class _Common:
         f("route").restype = None
         f("swiglu").restype = None
         f("rmsnorm").restype = None
+        f("rope_apply").restype = None
 
     def fn(self, name):
         return getattr(self.lib, self.pf + name)
@@ -101,6 +102,14 @@ class _Common:
         self.fn("rmsnorm")(_p(y), _p(x), _p(np.ascontiguousarray(w, np.float32)), C.c_int(x.size),
                            C.c_float(eps))
         return y
+
+    def rope_apply(self, v, rd, cs, sn, pos, inverse=0):
+        """v [head_dim] (a copy is rotated and returned); cs / sn [positions][half]."""
+        v = np.ascontiguousarray(v, np.float32).copy()
+        cs = np.ascontiguousarray(cs, np.float32)
+        self.fn("rope_apply")(_p(v), C.c_int(v.size), C.c_int(rd), _p(cs), _p(np.ascontiguousarray(sn, np.float32)),
+                              C.c_int(pos), C.c_int(cs.shape[1]), C.c_int(inverse))
+        return v
 
     def indexer_score(self, q, kv, weights):
         h, d = q.shape
