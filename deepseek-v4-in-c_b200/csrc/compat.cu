@@ -381,6 +381,22 @@ extern "C" void fp4_n(float *y, const float *x, const uint8_t *W, const uint8_t 
 }
 
 // ====================================================== router / expert ops
+extern "C" void dsv4_rmsnorm(float *y, const float *x, const float *w, int n, float eps)
+{
+    if (n <= 0) return;
+    HostState &s = S();
+    std::lock_guard<std::recursive_mutex> lk(s.mu);
+    must(ensure_init(), "dsv4_rmsnorm");
+    DeviceScope ds;
+    const size_t b = (size_t)n * 4;
+    float *dx = (float *)buf_or_die(0, b), *dw = (float *)buf_or_die(1, b), *dy = (float *)buf_or_die(2, b);
+    must_cuda(cudaMemcpyAsync(dx, x, b, cudaMemcpyHostToDevice, s.st), "dsv4_rmsnorm");
+    must_cuda(cudaMemcpyAsync(dw, w, b, cudaMemcpyHostToDevice, s.st), "dsv4_rmsnorm");
+    must(dsv4cu_rmsnorm(dy, dx, dw, n, 1, eps, s.st), "dsv4_rmsnorm");
+    must_cuda(cudaMemcpyAsync(y, dy, b, cudaMemcpyDeviceToHost, s.st), "dsv4_rmsnorm");
+    must_cuda(cudaStreamSynchronize(s.st), "dsv4_rmsnorm");
+}
+
 extern "C" void dsv4_swiglu(float *y, const float *gate, const float *up, int n, float limit)
 {
     if (n <= 0) return;

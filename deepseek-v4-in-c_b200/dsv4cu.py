@@ -106,6 +106,7 @@ def lib() -> C.CDLL:
             "fp8_n": (None, [vp, vp, vp, vp, i, i, i, i, i]),
             "fp4_n": (None, [vp, vp, vp, vp, i, i, i, i, i]),
             "dsv4_swiglu": (None, [vp, vp, vp, i, f]),
+            "dsv4_rmsnorm": (None, [vp, vp, vp, i, f]),
             "dsv4_route": (None, [vp, vp, vp, vp, vp, vp, i, i, i, f]),
             "dsv4_expert_forward": (None, [vp, vp, vp, vp, vp, vp, i, f]),
             "dsv4_sparse_attn": (None, [vp, vp, vp, vp, vp, i, i, i, f, vp]),
@@ -200,6 +201,12 @@ class HostAPI:
         self.L.dsv4_route(_p(idx), _p(wts), _p(scores), _p(orig), _p(b), _p(t), token_id, ne,
                           topk, route_scale)
         return idx, wts, scores, orig
+
+    def rmsnorm(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros_like(x)
+        self.L.dsv4_rmsnorm(_p(y), _p(x), _p(np.ascontiguousarray(w, np.float32)), x.size, eps)
+        return y
 
     def swiglu(self, gate, up, limit):
         g = np.ascontiguousarray(gate, np.float32)

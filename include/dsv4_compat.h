@@ -69,7 +69,10 @@ void fp8_n(float *y, const float *x, const uint8_t *W, const uint8_t *S,
 void fp4_n(float *y, const float *x, const uint8_t *W, const uint8_t *S,
            int in, int out, int blk_r, int blk_c, int nt);
 
-/* ---- src/10_compute/dsv4_kernels.h:22-57 (the hot-path subset) ---- */
+/* ---- src/10_compute/dsv4_kernels.h:20-57 (the hot-path subset) ---- */
+/* src/10_compute/dsv4_kernels.h:20: with dsv4_route, dsv4_swiglu and
+ * dsv4_expert_forward, every symbol of src/10_compute/dsv4_ops.c. */
+void dsv4_rmsnorm(float *y, const float *x, const float *w, int n, float eps);
 void dsv4_swiglu(float *y, const float *gate, const float *up, int n, float limit);
 void dsv4_route(int *idx, float *wts, float *scores, float *orig,
                 const float *bias, const int64_t *tid2eid, int token_id,

@@ -43,7 +43,7 @@ def built_lib():
 def test_headers_declare_the_reference_entry_points():
     names = set(declared_functions())
     # src/10_compute/dsv4_matmul.h:40-52, dsv4_kernels.h, 80_prefill/dsv4_prefill_vk.h:31-49
-    for ref in ("dsv4_mmq_n", "dsv4_mmq", "bf16_n", "fp8_n", "fp4_n", "dsv4_route", "dsv4_swiglu",
+    for ref in ("dsv4_mmq_n", "dsv4_mmq", "bf16_n", "fp8_n", "fp4_n", "dsv4_route", "dsv4_swiglu", "dsv4_rmsnorm",
                 "dsv4_expert_forward", "dsv4_indexer_score", "dsv4_topk", "dsv4_indexer_offset",
                 "dsv4_sparse_attn", "dsv4_window_idxs", "dsv4_prefill_vk_init",
                 "dsv4_prefill_vk_free", "dsv4_prefill_vk_gemm", "dsv4_prefill_vk_expert_fused"):

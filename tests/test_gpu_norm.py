@@ -60,3 +60,12 @@ def test_rmsnorm_replay_rows_and_alias(dev, orc):
     dx = torch.from_numpy(x[4:].copy()).cuda()
     dev.rmsnorm(dx, dx, torch.from_numpy(w).cuda(), n, 1, 1e-6)
     assert np.array_equal(dx.cpu().numpy().view(np.uint32), want[4:].view(np.uint32))
+
+
+def test_rmsnorm_reference_symbol(host, orc):
+    """dsv4_rmsnorm, the reference's host-pointer symbol (src/10_compute/dsv4_kernels.h:20)."""
+    rng = np.random.default_rng(8)
+    for n in (7, 4096):
+        x = rng.standard_normal(n).astype(np.float32)
+        w = rng.standard_normal(n).astype(np.float32)
+        assert np.array_equal(host.rmsnorm(x, w, 1e-6).view(np.uint32), orc.rmsnorm(x, w, 1e-6).view(np.uint32))
