@@ -69,3 +69,20 @@ def test_binding_raises_without_library(tmp_path, monkeypatch):
     monkeypatch.setattr(dsv4cu, "_lib", None)
     with pytest.raises(dsv4cu.DSV4CUError):
         dsv4cu.lib()
+
+
+def test_reference_engine_links_against_the_library(built_lib):
+    """The reference's whole engine, linked with the CPU kernel files the library
+    replaces left out (oracle/Makefile target `engine`): every compute symbol the
+    engine uses resolves in libdsv4cu.so. Needs the reference tree (built where
+    oracle/_ref/libdsv4ref.so was built)."""
+    ref_so = os.path.join(ROOT, "oracle", "_ref", "libdsv4ref.so")
+    if not os.path.exists(ref_so):
+        pytest.skip("reference tree not available here")
+    r = subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "engine"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-2000:]
+    exe = os.path.join(ROOT, "oracle", "_ref", "dsv4-serve-cuda")
+    und = subprocess.run(["nm", "-u", exe], capture_output=True, text=True).stdout.split()
+    need = {s for s in und if s.startswith("dsv4_") or s in ("fp8_n", "fp4_n", "bf16_n")}
+    lib = ctypes.CDLL(built_lib)
+    assert need and all(hasattr(lib, s) for s in need), sorted(need)
