@@ -177,6 +177,28 @@ __global__ void round_bf16_kernel(float *x, size_t n)
     if (i < n) x[i] = __bfloat162float(__float2bfloat16_rn(x[i]));
 }
 
+// ------------------------------------------------------------- mHC post
+// dsv4_hc_post (src/10_compute/dsv4_hc.c) per token t: for copy k and dim d,
+// acc = post[k] * x[d] in double (exact), then fma(comb[j][k], residual[j][d],
+// acc) for j in order (each product exact, one rounded add, as the reference's
+// vector body and scalar tail both do), y = (float)acc. One thread per output.
+__global__ void hc_post_kernel(float *__restrict__ y, const float *__restrict__ x,
+                               const float *__restrict__ residual, const float *__restrict__ post,
+                               const float *__restrict__ comb, int nt, int hc, int hidden)
+{
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= (long)nt * hc * hidden) return;
+    const int d = (int)(i % hidden);
+    const long tk = i / hidden;
+    const int k = (int)(tk % hc), t = (int)(tk / hc);
+    const float *res = residual + (size_t)t * hc * hidden;
+    const float *cm = comb + (size_t)t * hc * hc;
+    double acc = __dmul_rn((double)__ldg(post + (size_t)t * hc + k), (double)__ldg(x + (size_t)t * hidden + d));
+    for (int j = 0; j < hc; j++)
+        acc = __fma_rn((double)__ldg(cm + j * hc + k), (double)__ldg(res + (size_t)j * hidden + d), acc);
+    y[i] = __double2float_rn(acc);
+}
+
 // ------------------------------------------------------------- rope
 // dsv4_rope_apply (src/10_compute/dsv4_rope.c) over v [nt][nh][head_dim]:
 // the last rd dims of every head are (re, im) pairs rotated by table entry
@@ -431,6 +453,18 @@ extern "C" int dsv4cu_rope_apply(dsv4cu_ctx *ctx, float *v, int nt, int nh, int 
     const long n = (long)nt * nh * (rd / 2);
     rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
         v, nt, nh, head_dim, rd, cs, sn, pos, table_half, n_pos, inverse, ctx ? ctx->status : nullptr);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_hc_post(float *y, const float *x, const float *residual, const float *post, const float *comb,
+                              int nt, int hc, int hidden, void *stream)
+{
+    if (!y || !x || !residual || !post || !comb || nt <= 0 || hc <= 0 || hidden <= 0)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "hc_post: bad args");
+    const long n = (long)nt * hc * hidden;
+    hc_post_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(y, x, residual, post, comb, nt, hc,
+                                                                                 hidden);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
 }

@@ -90,6 +90,7 @@ def lib() -> C.CDLL:
             "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
             "dsv4cu_argmax": (i, [vp, vp, i, i, vp]),
             "dsv4cu_rmsnorm": (i, [vp, vp, vp, i, i, f, vp]),
+            "dsv4cu_hc_post": (i, [vp, vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_rope_apply": (i, [vp, vp, i, i, i, i, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_experts_load": (i, [C.POINTER(vp), vp, C.c_char_p, C.c_char_p, i, i, i, i, i, vp]),
             "dsv4cu_experts_free": (None, [vp]),
@@ -425,6 +426,10 @@ class Device:
         check(self.L.dsv4cu_rope_apply(self.ctx, self.ptr(v), nt, nh, head_dim, rd, self.ptr(cs), self.ptr(sn),
                                        self.ptr(pos), cs.shape[1], cs.shape[0], inverse, self.stream()),
               "rope_apply")
+
+    def hc_post(self, y, x, residual, post, comb, nt: int, hc: int, hidden: int):
+        check(self.L.dsv4cu_hc_post(self.ptr(y), self.ptr(x), self.ptr(residual), self.ptr(post), self.ptr(comb), nt,
+                                    hc, hidden, self.stream()), "hc_post")
 
     def argmax(self, best, logits, n: int, nt: int = 1):
         check(self.L.dsv4cu_argmax(self.ptr(best), self.ptr(logits), n, nt, self.stream()), "argmax")

@@ -335,6 +335,14 @@ int dsv4cu_rmsnorm(float *y, const float *x, const float *w, int n, int nt, floa
 int dsv4cu_rope_apply(dsv4cu_ctx *ctx, float *v, int nt, int nh, int head_dim, int rd, const float *cs,
                       const float *sn, const int *pos, int table_half, int n_pos, int inverse, void *stream);
 
+/* mHC residual update (dsv4_hc_post, src/10_compute/dsv4_hc.c) for nt
+ * tokens: y [nt][hc][hidden] from the block output x [nt][hidden], the
+ * residual copies [nt][hc][hidden], post [nt][hc] and comb [nt][hc][hc], with
+ * the reference's double arithmetic in its order - the same bits. y must not
+ * alias residual. */
+int dsv4cu_hc_post(float *y, const float *x, const float *residual, const float *post, const float *comb,
+                   int nt, int hc, int hidden, void *stream);
+
 /* Greedy pick per row of logits [nt][n] into best[nt], with the reference's
  * argmax rule (src/90_cli/dsv4_decode.c:128-133): the first index of the
  * largest value, -0.0 equal to +0.0, NaNs never picked, and 0 when row[0] is

@@ -175,6 +175,20 @@ void orc_rope_apply(float *v, int head_dim, int rd, const float *cs, const float
     }
 }
 
+/* src/10_compute/dsv4_hc.c (dsv4_hc_post): for each copy k and dim d,
+ * acc = post[k] * x[d] in double, then acc += comb[j][k] * residual[j][d] for
+ * j in order (each product exact in double, one rounded add), y = (float)acc. */
+void orc_hc_post(float *y, const float *x, const float *residual, const float *post, const float *comb, int hc,
+                 int hidden)
+{
+    for (int k = 0; k < hc; k++)
+        for (int d = 0; d < hidden; d++) {
+            double acc = (double)post[k] * (double)x[d];
+            for (int j = 0; j < hc; j++) acc += (double)comb[j * hc + k] * (double)residual[(size_t)j * hidden + d];
+            y[(size_t)k * hidden + d] = (float)acc;
+        }
+}
+
 /* src/10_compute/dsv4_ops.c:26-33 (dsv4_rmsnorm): the sum of squares in
  * double in index order, mean = sum / n, inv = (float)(1 / sqrt(mean + eps)),
  * y = w * (x * inv) in float. */

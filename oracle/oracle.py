@@ -72,6 +72,7 @@ class _Common:
         f("swiglu").restype = None
         f("rmsnorm").restype = None
         f("rope_apply").restype = None
+        f("hc_post").restype = None
 
     def fn(self, name):
         return getattr(self.lib, self.pf + name)
@@ -110,6 +111,16 @@ class _Common:
         self.fn("rope_apply")(_p(v), C.c_int(v.size), C.c_int(rd), _p(cs), _p(np.ascontiguousarray(sn, np.float32)),
                               C.c_int(pos), C.c_int(cs.shape[1]), C.c_int(inverse))
         return v
+
+    def hc_post(self, x, residual, post, comb):
+        """x [hidden], residual [hc][hidden], post [hc], comb [hc][hc] -> y [hc][hidden]."""
+        residual = np.ascontiguousarray(residual, np.float32)
+        hc, hidden = residual.shape
+        y = np.zeros((hc, hidden), np.float32)
+        self.fn("hc_post")(_p(y), _p(np.ascontiguousarray(x, np.float32)), _p(residual),
+                           _p(np.ascontiguousarray(post, np.float32)), _p(np.ascontiguousarray(comb, np.float32)),
+                           C.c_int(hc), C.c_int(hidden))
+        return y
 
     def indexer_score(self, q, kv, weights):
         h, d = q.shape

@@ -1,4 +1,5 @@
-"""dsv4cu_rmsnorm against the oracle's dsv4_rmsnorm (src/10_compute/dsv4_ops.c:26-33),
+"""dsv4cu_hc_post against the oracle's dsv4_hc_post (src/10_compute/dsv4_hc.c), and
+dsv4cu_rmsnorm against the oracle's dsv4_rmsnorm (src/10_compute/dsv4_ops.c:26-33),
 bit for bit: ordinary rows of the engine's widths, many rows at once (the
 parallel sum with its rounding certificate), and rows that take the
 sequential replay (a zero row, NaN, inf), subnormal inputs, and y aliasing x."""
@@ -69,3 +70,20 @@ def test_rmsnorm_reference_symbol(host, orc):
         x = rng.standard_normal(n).astype(np.float32)
         w = rng.standard_normal(n).astype(np.float32)
         assert np.array_equal(host.rmsnorm(x, w, 1e-6).view(np.uint32), orc.rmsnorm(x, w, 1e-6).view(np.uint32))
+
+
+@pytest.mark.parametrize("hc,hidden", [(4, 4096), (4, 7), (2, 130)])
+def test_hc_post_bitwise(dev, orc, hc, hidden):
+    import torch
+    rng = np.random.default_rng(hc * 1000 + hidden)
+    nt = 3
+    x = rng.standard_normal((nt, hidden)).astype(np.float32)
+    res = rng.standard_normal((nt, hc, hidden)).astype(np.float32)
+    post = rng.uniform(0, 2, (nt, hc)).astype(np.float32)
+    comb = rng.uniform(0, 1, (nt, hc, hc)).astype(np.float32)
+    y = torch.empty((nt, hc, hidden), dtype=torch.float32, device="cuda")
+    dev.hc_post(y, *(torch.from_numpy(a).cuda() for a in (x, res, post, comb)), nt, hc, hidden)
+    got = y.cpu().numpy()
+    for t in range(nt):
+        want = orc.hc_post(x[t], res[t], post[t], comb[t])
+        assert np.array_equal(got[t].view(np.uint32), want.view(np.uint32)), t
