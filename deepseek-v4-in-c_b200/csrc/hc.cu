@@ -1,0 +1,153 @@
+// hc.cu - mHC pre-mix (dsv4_hc_pre with dsv4_hc_split_sinkhorn) on the device.
+//
+// Reference: src/10_compute/dsv4_hc.c. Per token, over the hc residual copies
+// x [hc][hidden] (hcdim = hc * hidden):
+//   sq       = dot(x, x)                     the 16-chain double tree of
+//   mixes[m] = (float)dot(fn[m], x) * rsqrt  dsv4_dot_f32d (dsv4_dot.h:20-42),
+//   rsqrt    = (float)(1 / sqrt(sq / hcdim + norm_eps))
+//   pre / post / comb = the Sinkhorn split of mixes (sigmoids, a row softmax,
+//              then iters - 1 rounds of row and column normalising, sums in
+//              double, divisors (float)sum + eps)
+//   y[d]     = (float)(sum over j in order of fma(pre[j], x[j][d]))
+// Every dot, sum, division and product is the reference's IEEE operation in
+// its order, uncontracted. The one operation that is not is expf: the
+// reference calls glibc's, which no device formula reproduces bit for bit;
+// here it is exp in double rounded once to float - the correctly rounded
+// value, which glibc's expf (accurate to about half an ulp) also returns
+// except when the exact value lies very close to a float rounding midpoint.
+//
+// One CTA per token: thread (dot m, chain c) runs chain c of dot m (m = 0 is
+// sq), 16 consecutive lanes read 16 consecutive floats; one thread folds each
+// dot; thread 0 runs the Sinkhorn split (a few hundred dependent float ops);
+// all threads then form y.
+#include "common.cuh"
+#include "ctx.h"
+
+namespace dsv4cu {
+
+constexpr int HC_MAX = 6;
+constexpr int HC_MAX_DOTS = (2 + HC_MAX) * HC_MAX + 1;
+
+DSV4CU_DEV float hc_expf(float v) { return __double2float_rn(exp((double)v)); }
+DSV4CU_DEV float hc_sigmoid(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, hc_expf(-v))); }
+
+__global__ void __launch_bounds__(1024) hc_pre_kernel(float *__restrict__ y, float *__restrict__ post,
+                                                      float *__restrict__ comb_out, float *__restrict__ mixes_out,
+                                                      const float *__restrict__ x, const float *__restrict__ fn,
+                                                      const float *__restrict__ base, const float *__restrict__ scale,
+                                                      int hc, int hidden, int iters, float norm_eps, float hc_eps)
+{
+    __shared__ double chains[HC_MAX_DOTS * 16];
+    __shared__ double dots[HC_MAX_DOTS];
+    __shared__ float s_pre[HC_MAX];
+    const int t = blockIdx.x, hcdim = hc * hidden, mix = (2 + hc) * hc, ndots = mix + 1;
+    const int n16 = hcdim & ~15;
+    const float *xt = x + (size_t)t * hcdim;
+
+    for (int task = threadIdx.x; task < ndots * 16; task += blockDim.x) {
+        const int m = task >> 4, c = task & 15;
+        const float *a = m == 0 ? xt : fn + (size_t)(m - 1) * hcdim;
+        double acc = 0.0;
+#pragma unroll 8
+        for (int i = c; i < n16; i += 16) acc = __fma_rn((double)__ldg(a + i), (double)__ldg(xt + i), acc);
+        chains[task] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x < ndots) {
+        const int m = threadIdx.x;
+        const double *ch = chains + m * 16;
+        double bb[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) bb[j] = __dadd_rn(__dadd_rn(ch[j], ch[j + 4]), __dadd_rn(ch[j + 8], ch[j + 12]));
+        double acc = __dadd_rn(__dadd_rn(bb[0], bb[1]), __dadd_rn(bb[2], bb[3]));
+        const float *a = m == 0 ? xt : fn + (size_t)(m - 1) * hcdim;
+        for (int i = n16; i < hcdim; i++) acc = __fma_rn((double)__ldg(a + i), (double)__ldg(xt + i), acc);
+        dots[m] = acc;
+    }
+    __syncthreads();
+
+    if (threadIdx.x == 0) {
+        const float rsq = __double2float_rn(
+            __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(dots[0], (double)hcdim), (double)norm_eps))));
+        float mixes[(2 + HC_MAX) * HC_MAX], pre[HC_MAX], po[HC_MAX], comb[HC_MAX * HC_MAX];
+        for (int m = 0; m < mix; m++) {
+            mixes[m] = __fmul_rn(__double2float_rn(dots[m + 1]), rsq);
+            mixes_out[(size_t)t * mix + m] = mixes[m];
+        }
+        for (int j = 0; j < hc; j++)
+            pre[j] = __fadd_rn(hc_sigmoid(__fadd_rn(__fmul_rn(mixes[j], scale[0]), base[j])), hc_eps);
+        for (int j = 0; j < hc; j++)
+            po[j] = __fmul_rn(2.0f, hc_sigmoid(__fadd_rn(__fmul_rn(mixes[j + hc], scale[1]), base[j + hc])));
+        for (int j = 0; j < hc; j++)
+            for (int k = 0; k < hc; k++) {
+                const int o = j * hc + k + 2 * hc;
+                comb[j * hc + k] = __fadd_rn(__fmul_rn(mixes[o], scale[2]), base[o]);
+            }
+        // First pass: row softmax, + eps, then a column normalise.
+        for (int j = 0; j < hc; j++) {
+            float mx = comb[j * hc];
+            for (int k = 1; k < hc; k++)
+                if (comb[j * hc + k] > mx) mx = comb[j * hc + k];
+            double sum = 0.0;
+            for (int k = 0; k < hc; k++) {
+                const float e = hc_expf(__fsub_rn(comb[j * hc + k], mx));
+                comb[j * hc + k] = e;
+                sum = __dadd_rn(sum, (double)e);
+            }
+            const float inv = __double2float_rn(__ddiv_rn(1.0, sum));
+            for (int k = 0; k < hc; k++) comb[j * hc + k] = __fadd_rn(__fmul_rn(comb[j * hc + k], inv), hc_eps);
+        }
+        for (int k = 0; k < hc; k++) {
+            double cs = 0.0;
+            for (int j = 0; j < hc; j++) cs = __dadd_rn(cs, (double)comb[j * hc + k]);
+            const float d = __fadd_rn(__double2float_rn(cs), hc_eps);
+            for (int j = 0; j < hc; j++) comb[j * hc + k] = __fdiv_rn(comb[j * hc + k], d);
+        }
+        // The remaining iters - 1 passes: rows, then columns.
+        for (int it = 0; it < iters - 1; it++) {
+            for (int j = 0; j < hc; j++) {
+                double rs = 0.0;
+                for (int k = 0; k < hc; k++) rs = __dadd_rn(rs, (double)comb[j * hc + k]);
+                const float d = __fadd_rn(__double2float_rn(rs), hc_eps);
+                for (int k = 0; k < hc; k++) comb[j * hc + k] = __fdiv_rn(comb[j * hc + k], d);
+            }
+            for (int k = 0; k < hc; k++) {
+                double cs = 0.0;
+                for (int j = 0; j < hc; j++) cs = __dadd_rn(cs, (double)comb[j * hc + k]);
+                const float d = __fadd_rn(__double2float_rn(cs), hc_eps);
+                for (int j = 0; j < hc; j++) comb[j * hc + k] = __fdiv_rn(comb[j * hc + k], d);
+            }
+        }
+        for (int j = 0; j < hc; j++) {
+            s_pre[j] = pre[j];
+            post[(size_t)t * hc + j] = po[j];
+        }
+        for (int i = 0; i < hc * hc; i++) comb_out[(size_t)t * hc * hc + i] = comb[i];
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) {
+        double acc = 0.0;
+        for (int j = 0; j < hc; j++) acc = __fma_rn((double)s_pre[j], (double)__ldg(xt + (size_t)j * hidden + d), acc);
+        y[(size_t)t * hidden + d] = __double2float_rn(acc);
+    }
+}
+
+}  // namespace dsv4cu
+
+using namespace dsv4cu;
+
+extern "C" int dsv4cu_hc_pre(float *y, float *post, float *comb, float *mixes, const float *x, const float *fn,
+                             const float *base, const float *scale, int nt, int hc, int hidden, int iters,
+                             float norm_eps, float hc_eps, void *stream)
+{
+    if (!y || !post || !comb || !mixes || !x || !fn || !base || !scale || nt <= 0 || hidden <= 0 || iters < 1)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "hc_pre: bad args");
+    if (hc < 1 || hc > HC_MAX) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "hc_pre: hc %d (1..%d)", hc, HC_MAX);
+    const int ndots = (2 + hc) * hc + 1;
+    int threads = ((ndots * 16 + 31) / 32) * 32;
+    if (threads < 256) threads = 256;
+    hc_pre_kernel<<<(unsigned)nt, threads, 0, (cudaStream_t)stream>>>(y, post, comb, mixes, x, fn, base, scale, hc,
+                                                                      hidden, iters, norm_eps, hc_eps);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}

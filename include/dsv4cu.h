@@ -335,6 +335,18 @@ int dsv4cu_rmsnorm(float *y, const float *x, const float *w, int n, int nt, floa
 int dsv4cu_rope_apply(dsv4cu_ctx *ctx, float *v, int nt, int nh, int head_dim, int rd, const float *cs,
                       const float *sn, const int *pos, int table_half, int n_pos, int inverse, void *stream);
 
+/* mHC pre-mix (dsv4_hc_pre with dsv4_hc_split_sinkhorn,
+ * src/10_compute/dsv4_hc.c) for nt tokens: from the residual copies
+ * x [nt][hc][hidden] and the block's device weights fn [(2+hc)hc][hc hidden],
+ * base [(2+hc)hc], scale [3], writes y [nt][hidden], post [nt][hc],
+ * comb [nt][hc][hc] and mixes [nt][(2+hc)hc]. The reference's double dots,
+ * sums and float arithmetic in its order; expf is exp in double rounded to
+ * float (the reference's glibc expf agrees except within a hair of a rounding
+ * midpoint). hc <= 6. */
+int dsv4cu_hc_pre(float *y, float *post, float *comb, float *mixes, const float *x, const float *fn,
+                  const float *base, const float *scale, int nt, int hc, int hidden, int iters, float norm_eps,
+                  float hc_eps, void *stream);
+
 /* mHC residual update (dsv4_hc_post, src/10_compute/dsv4_hc.c) for nt
  * tokens: y [nt][hc][hidden] from the block output x [nt][hidden], the
  * residual copies [nt][hc][hidden], post [nt][hc] and comb [nt][hc][hc], with

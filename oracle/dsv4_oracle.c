@@ -175,6 +175,76 @@ void orc_rope_apply(float *v, int head_dim, int rd, const float *cs, const float
     }
 }
 
+static float orc_sigmoidf(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+/* src/10_compute/dsv4_hc.c (dsv4_hc_split_sinkhorn): pre = sigmoid + eps,
+ * post = 2 sigmoid, comb = row softmax + eps then a column normalise, then
+ * iters - 1 rounds of row and column normalising (sums in double, divisors
+ * (float)sum + eps). */
+static void orc_hc_split_sinkhorn(float *pre, float *post, float *comb, const float *mixes, const float *scale,
+                                  const float *base, int hc, int iters, float eps)
+{
+    for (int j = 0; j < hc; j++) pre[j] = orc_sigmoidf(mixes[j] * scale[0] + base[j]) + eps;
+    for (int j = 0; j < hc; j++) post[j] = 2.0f * orc_sigmoidf(mixes[j + hc] * scale[1] + base[j + hc]);
+    for (int j = 0; j < hc; j++)
+        for (int k = 0; k < hc; k++) {
+            const int o = j * hc + k + 2 * hc;
+            comb[j * hc + k] = mixes[o] * scale[2] + base[o];
+        }
+    for (int j = 0; j < hc; j++) {
+        float mx = comb[j * hc];
+        for (int k = 1; k < hc; k++)
+            if (comb[j * hc + k] > mx) mx = comb[j * hc + k];
+        double sum = 0.0;
+        for (int k = 0; k < hc; k++) {
+            const float e = expf(comb[j * hc + k] - mx);
+            comb[j * hc + k] = e;
+            sum += (double)e;
+        }
+        const float inv = (float)(1.0 / sum);
+        for (int k = 0; k < hc; k++) comb[j * hc + k] = comb[j * hc + k] * inv + eps;
+    }
+    for (int k = 0; k < hc; k++) {
+        double cs = 0.0;
+        for (int j = 0; j < hc; j++) cs += (double)comb[j * hc + k];
+        const float d = (float)cs + eps;
+        for (int j = 0; j < hc; j++) comb[j * hc + k] /= d;
+    }
+    for (int it = 0; it < iters - 1; it++) {
+        for (int j = 0; j < hc; j++) {
+            double rs = 0.0;
+            for (int k = 0; k < hc; k++) rs += (double)comb[j * hc + k];
+            const float d = (float)rs + eps;
+            for (int k = 0; k < hc; k++) comb[j * hc + k] /= d;
+        }
+        for (int k = 0; k < hc; k++) {
+            double cs = 0.0;
+            for (int j = 0; j < hc; j++) cs += (double)comb[j * hc + k];
+            const float d = (float)cs + eps;
+            for (int j = 0; j < hc; j++) comb[j * hc + k] /= d;
+        }
+    }
+}
+
+/* src/10_compute/dsv4_hc.c (dsv4_hc_pre): RMS over the whole hc x hidden
+ * vector (norm_eps), mixes[m] = (float)dot(fn[m], x) * rsqrt, the Sinkhorn
+ * split, then y[d] = (float)(sum over j in order of fma(pre[j], x[j][d])). */
+void orc_hc_pre(float *y, float *post, float *comb, float *mixes, const float *x, const float *fn,
+                const float *base, const float *scale, int hc, int hidden, int iters, float norm_eps, float hc_eps)
+{
+    const int hcdim = hc * hidden, mix_hc = (2 + hc) * hc;
+    const double sq = orc_dot_f32d(x, x, hcdim);
+    const float rsqrt = (float)(1.0 / sqrt(sq / (double)hcdim + (double)norm_eps));
+    for (int m = 0; m < mix_hc; m++) mixes[m] = (float)orc_dot_f32d(fn + (size_t)m * hcdim, x, hcdim) * rsqrt;
+    float pre[16];
+    orc_hc_split_sinkhorn(pre, post, comb, mixes, scale, base, hc, iters, hc_eps);
+    for (int d = 0; d < hidden; d++) {
+        double acc = 0.0;
+        for (int j = 0; j < hc; j++) acc = fma((double)pre[j], (double)x[(size_t)j * hidden + d], acc);
+        y[d] = (float)acc;
+    }
+}
+
 /* src/10_compute/dsv4_hc.c (dsv4_hc_post): for each copy k and dim d,
  * acc = post[k] * x[d] in double, then acc += comb[j][k] * residual[j][d] for
  * j in order (each product exact in double, one rounded add), y = (float)acc. */

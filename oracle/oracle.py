@@ -73,6 +73,7 @@ class _Common:
         f("rmsnorm").restype = None
         f("rope_apply").restype = None
         f("hc_post").restype = None
+        f("hc_pre").restype = None
 
     def fn(self, name):
         return getattr(self.lib, self.pf + name)
@@ -111,6 +112,28 @@ class _Common:
         self.fn("rope_apply")(_p(v), C.c_int(v.size), C.c_int(rd), _p(cs), _p(np.ascontiguousarray(sn, np.float32)),
                               C.c_int(pos), C.c_int(cs.shape[1]), C.c_int(inverse))
         return v
+
+    def hc_pre(self, x, fn, base, scale, iters, norm_eps, hc_eps):
+        """x [hc][hidden], fn [(2 + hc) hc][hc hidden], base [(2 + hc) hc], scale [3]
+        -> (y [hidden], post [hc], comb [hc][hc], mixes [(2 + hc) hc])."""
+        x = np.ascontiguousarray(x, np.float32)
+        hc, hidden = x.shape
+        mix = (2 + hc) * hc
+        y = np.zeros(hidden, np.float32)
+        post = np.zeros(hc, np.float32)
+        comb = np.zeros((hc, hc), np.float32)
+        mixes = np.zeros(mix, np.float32)
+        fn = np.ascontiguousarray(fn, np.float32)
+        base = np.ascontiguousarray(base, np.float32)
+        scale = np.ascontiguousarray(scale, np.float32)
+        if self.pf == "orc_":
+            self.fn("hc_pre")(_p(y), _p(post), _p(comb), _p(mixes), _p(x), _p(fn), _p(base), _p(scale), C.c_int(hc),
+                              C.c_int(hidden), C.c_int(iters), C.c_float(norm_eps), C.c_float(hc_eps))
+        else:       # the reference takes a DSV4HcW {fn, base, scale} (src/00_base/dsv4_weights.h:116-121)
+            w = (C.c_void_p * 3)(fn.ctypes.data, base.ctypes.data, scale.ctypes.data)
+            self.fn("hc_pre")(_p(y), _p(post), _p(comb), _p(mixes), _p(x), w, C.c_int(hc), C.c_int(hidden),
+                              C.c_int(iters), C.c_float(norm_eps), C.c_float(hc_eps))
+        return y, post, comb, mixes
 
     def hc_post(self, x, residual, post, comb):
         """x [hidden], residual [hc][hidden], post [hc], comb [hc][hc] -> y [hc][hidden]."""

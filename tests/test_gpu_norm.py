@@ -1,4 +1,5 @@
-"""dsv4cu_hc_post against the oracle's dsv4_hc_post (src/10_compute/dsv4_hc.c), and
+"""dsv4cu_hc_pre / dsv4cu_hc_post against the oracle's dsv4_hc_pre / dsv4_hc_post
+(src/10_compute/dsv4_hc.c), and
 dsv4cu_rmsnorm against the oracle's dsv4_rmsnorm (src/10_compute/dsv4_ops.c:26-33),
 bit for bit: ordinary rows of the engine's widths, many rows at once (the
 parallel sum with its rounding certificate), and rows that take the
@@ -87,3 +88,35 @@ def test_hc_post_bitwise(dev, orc, hc, hidden):
     for t in range(nt):
         want = orc.hc_post(x[t], res[t], post[t], comb[t])
         assert np.array_equal(got[t].view(np.uint32), want.view(np.uint32)), t
+
+
+@pytest.mark.parametrize("hc,hidden", [(4, 4096), (4, 35), (2, 64)])
+def test_hc_pre_vs_oracle(dev, orc, hc, hidden):
+    """The dots, sums and float arithmetic are the reference's; only expf is not
+    glibc's (exp in double rounded to float), so the bar is 1e-6 relative, and
+    the test reports how many outputs match bit for bit."""
+    import torch
+    rng = np.random.default_rng(hc * 100 + hidden)
+    nt, mix = 4, (2 + hc) * hc
+    x = rng.standard_normal((nt, hc, hidden)).astype(np.float32)
+    fn = (rng.standard_normal((mix, hc * hidden)) * 0.02).astype(np.float32)
+    base = rng.standard_normal(mix).astype(np.float32)
+    scale = rng.uniform(0.5, 2, 3).astype(np.float32)
+    t = torch
+    y = t.empty((nt, hidden), dtype=t.float32, device="cuda")
+    post = t.empty((nt, hc), dtype=t.float32, device="cuda")
+    comb = t.empty((nt, hc, hc), dtype=t.float32, device="cuda")
+    mixes = t.empty((nt, mix), dtype=t.float32, device="cuda")
+    dev.hc_pre(y, post, comb, mixes, *(t.from_numpy(a).cuda() for a in (x, fn, base, scale)), nt, hc, hidden)
+    got = [a.cpu().numpy() for a in (y, post, comb, mixes)]
+    same = total = 0
+    for k in range(nt):
+        want = orc.hc_pre(x[k], fn, base, scale, 20, 1e-6, 1e-6)
+        # the dots and rsqrt do not involve expf: mixes are bit-exact
+        assert np.array_equal(got[3][k].view(np.uint32), want[3].view(np.uint32))
+        for g, w in zip(got[:3], want[:3]):
+            gk = g[k]
+            assert float(np.abs(gk - w).max()) <= 1e-6 * max(float(np.abs(w).max()), 1e-30)
+            same += int(np.sum(gk.view(np.uint32) == w.view(np.uint32)))
+            total += gk.size
+    print(f"hc_pre: {same} of {total} outputs bit-identical")
