@@ -1,4 +1,5 @@
-// hc.cu - mHC pre-mix (dsv4_hc_pre with dsv4_hc_split_sinkhorn) on the device.
+// hc.cu - mHC pre-mix (dsv4_hc_pre with dsv4_hc_split_sinkhorn, and the
+// output head's hc_head) on the device.
 //
 // Reference: src/10_compute/dsv4_hc.c. Per token, over the hc residual copies
 // x [hc][hidden] (hcdim = hc * hidden):
@@ -132,9 +133,66 @@ __global__ void __launch_bounds__(1024) hc_pre_kernel(float *__restrict__ y, flo
     }
 }
 
+// The output head's mHC (hc_head, src/90_cli/dsv4_decode.c:102-125): sq and
+// each copy's mixing dot are single sequential chains in the reference (no
+// tree), so one thread runs each, in separate warps so they run side by side;
+// then pre[j] = sigmoid(m * scale[0] + base[j]) + hc_eps and y as above (the
+// sum over copies as products then adds, which equals fma: each product is
+// exact in double).
+__global__ void __launch_bounds__(256) hc_head_kernel(float *__restrict__ y, const float *__restrict__ x,
+                                                      const float *__restrict__ fn, const float *__restrict__ base,
+                                                      const float *__restrict__ scale, int hc, int hidden,
+                                                      float norm_eps, float hc_eps)
+{
+    __shared__ double dots[HC_MAX + 1];
+    __shared__ float s_pre[HC_MAX];
+    const int t = blockIdx.x, hcdim = hc * hidden, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *xt = x + (size_t)t * hcdim;
+    if (lane == 0 && warp <= hc) {
+        double acc = 0.0;
+        if (warp == 0) {
+            for (int i = 0; i < hcdim; i++) {
+                const double v = (double)__ldg(xt + i);
+                acc = __dadd_rn(acc, __dmul_rn(v, v));
+            }
+        } else {
+            const float *row = fn + (size_t)(warp - 1) * hcdim;
+            for (int i = 0; i < hcdim; i++) acc = __fma_rn((double)__ldg(row + i), (double)__ldg(xt + i), acc);
+        }
+        dots[warp] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const float rs = __double2float_rn(
+            __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(dots[0], (double)hcdim), (double)norm_eps))));
+        for (int j = 0; j < hc; j++) {
+            const float m = __fmul_rn(__double2float_rn(dots[j + 1]), rs);
+            s_pre[j] = __fadd_rn(hc_sigmoid(__fadd_rn(__fmul_rn(m, scale[0]), base[j])), hc_eps);
+        }
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) {
+        double acc = 0.0;
+        for (int j = 0; j < hc; j++) acc = __fma_rn((double)s_pre[j], (double)__ldg(xt + (size_t)j * hidden + d), acc);
+        y[(size_t)t * hidden + d] = __double2float_rn(acc);
+    }
+}
+
 }  // namespace dsv4cu
 
 using namespace dsv4cu;
+
+extern "C" int dsv4cu_hc_head(float *y, const float *x, const float *fn, const float *base, const float *scale,
+                              int nt, int hc, int hidden, float norm_eps, float hc_eps, void *stream)
+{
+    if (!y || !x || !fn || !base || !scale || nt <= 0 || hidden <= 0)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "hc_head: bad args");
+    if (hc < 1 || hc > HC_MAX) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "hc_head: hc %d (1..%d)", hc, HC_MAX);
+    hc_head_kernel<<<(unsigned)nt, 256, 0, (cudaStream_t)stream>>>(y, x, fn, base, scale, hc, hidden, norm_eps,
+                                                                   hc_eps);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
 
 extern "C" int dsv4cu_hc_pre(float *y, float *post, float *comb, float *mixes, const float *x, const float *fn,
                              const float *base, const float *scale, int nt, int hc, int hidden, int iters,

@@ -92,6 +92,7 @@ def lib() -> C.CDLL:
             "dsv4cu_rmsnorm": (i, [vp, vp, vp, i, i, f, vp]),
             "dsv4cu_hc_post": (i, [vp, vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_hc_pre": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, f, f, vp]),
+            "dsv4cu_hc_head": (i, [vp, vp, vp, vp, vp, i, i, i, f, f, vp]),
             "dsv4cu_rope_apply": (i, [vp, vp, i, i, i, i, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_experts_load": (i, [C.POINTER(vp), vp, C.c_char_p, C.c_char_p, i, i, i, i, i, vp]),
             "dsv4cu_experts_free": (None, [vp]),
@@ -433,6 +434,11 @@ class Device:
         check(self.L.dsv4cu_hc_pre(self.ptr(y), self.ptr(post), self.ptr(comb), self.ptr(mixes), self.ptr(x),
                                    self.ptr(fn), self.ptr(base), self.ptr(scale), nt, hc, hidden, iters, norm_eps,
                                    hc_eps, self.stream()), "hc_pre")
+
+    def hc_head(self, y, x, fn, base, scale, nt: int, hc: int, hidden: int, norm_eps: float = 1e-6,
+                hc_eps: float = 1e-6):
+        check(self.L.dsv4cu_hc_head(self.ptr(y), self.ptr(x), self.ptr(fn), self.ptr(base), self.ptr(scale), nt, hc,
+                                    hidden, norm_eps, hc_eps, self.stream()), "hc_head")
 
     def hc_post(self, y, x, residual, post, comb, nt: int, hc: int, hidden: int):
         check(self.L.dsv4cu_hc_post(self.ptr(y), self.ptr(x), self.ptr(residual), self.ptr(post), self.ptr(comb), nt,

@@ -347,6 +347,14 @@ int dsv4cu_hc_pre(float *y, float *post, float *comb, float *mixes, const float 
                   const float *base, const float *scale, int nt, int hc, int hidden, int iters, float norm_eps,
                   float hc_eps, void *stream);
 
+/* The output head's mHC (hc_head, src/90_cli/dsv4_decode.c:102-125): from
+ * x [nt][hc][hidden] and the head's fn [hc][hc hidden], base [hc], scale [1],
+ * y [nt][hidden] = sum over j of pre[j] * x[j], pre the head's sigmoid mix.
+ * The reference's sequential sums and order; expf as in dsv4cu_hc_pre. Then
+ * dsv4cu_rmsnorm and dsv4cu_head complete dsv4_head_from_h. hc <= 6. */
+int dsv4cu_hc_head(float *y, const float *x, const float *fn, const float *base, const float *scale, int nt, int hc,
+                   int hidden, float norm_eps, float hc_eps, void *stream);
+
 /* mHC residual update (dsv4_hc_post, src/10_compute/dsv4_hc.c) for nt
  * tokens: y [nt][hc][hidden] from the block output x [nt][hidden], the
  * residual copies [nt][hc][hidden], post [nt][hc] and comb [nt][hc][hc], with

@@ -245,6 +245,33 @@ void orc_hc_pre(float *y, float *post, float *comb, float *mixes, const float *x
     }
 }
 
+/* src/90_cli/dsv4_decode.c:102-125 (hc_head): sq summed in index order
+ * (products then adds), rs = (float)(1 / sqrt(sq / hcdim + norm_eps)); per copy
+ * j one sequential fma chain over the whole hc x hidden vector, m = (float)acc *
+ * rs, pre[j] = 1 / (1 + expf(-(m * scale + base[j]))) + hc_eps; then
+ * y[d] = (float)(sum over j in order of pre[j] * x[j][d]). */
+void orc_hc_head(float *y, const float *x, const float *fn, const float *base, const float *scale, int hc,
+                 int hidden, float norm_eps, float hc_eps)
+{
+    const int hcdim = hc * hidden;
+    double sq = 0.0;
+    for (int i = 0; i < hcdim; i++) sq += (double)x[i] * x[i];
+    const float rs = (float)(1.0 / sqrt(sq / (double)hcdim + (double)norm_eps));
+    float pre[16];
+    for (int j = 0; j < hc; j++) {
+        const float *row = fn + (size_t)j * hcdim;
+        double acc = 0.0;
+        for (int i = 0; i < hcdim; i++) acc = fma((double)row[i], (double)x[i], acc);
+        const float m = (float)acc * rs;
+        pre[j] = 1.0f / (1.0f + expf(-(m * scale[0] + base[j]))) + hc_eps;
+    }
+    for (int d = 0; d < hidden; d++) {
+        double acc = 0.0;
+        for (int j = 0; j < hc; j++) acc += (double)pre[j] * (double)x[(size_t)j * hidden + d];
+        y[d] = (float)acc;
+    }
+}
+
 /* src/10_compute/dsv4_hc.c (dsv4_hc_post): for each copy k and dim d,
  * acc = post[k] * x[d] in double, then acc += comb[j][k] * residual[j][d] for
  * j in order (each product exact in double, one rounded add), y = (float)acc. */

@@ -135,6 +135,17 @@ class _Common:
                               C.c_int(iters), C.c_float(norm_eps), C.c_float(hc_eps))
         return y, post, comb, mixes
 
+    def hc_head(self, x, fn, base, scale, norm_eps, hc_eps):
+        """The restatement only (hc_head is static in the reference's CLI)."""
+        x = np.ascontiguousarray(x, np.float32)
+        hc, hidden = x.shape
+        y = np.zeros(hidden, np.float32)
+        self.lib.orc_hc_head.restype = None
+        self.lib.orc_hc_head(_p(y), _p(x), _p(np.ascontiguousarray(fn, np.float32)),
+                             _p(np.ascontiguousarray(base, np.float32)), _p(np.ascontiguousarray(scale, np.float32)),
+                             C.c_int(hc), C.c_int(hidden), C.c_float(norm_eps), C.c_float(hc_eps))
+        return y
+
     def hc_post(self, x, residual, post, comb):
         """x [hidden], residual [hc][hidden], post [hc], comb [hc][hc] -> y [hc][hidden]."""
         residual = np.ascontiguousarray(residual, np.float32)

@@ -120,3 +120,37 @@ def test_hc_pre_vs_oracle(dev, orc, hc, hidden):
             same += int(np.sum(gk.view(np.uint32) == w.view(np.uint32)))
             total += gk.size
     print(f"hc_pre: {same} of {total} outputs bit-identical")
+
+
+def test_head_path_hc_norm_gemv_pick(dev, orc):
+    """dsv4_head_from_h (src/90_cli/dsv4_decode.c:138-148) on the device: hc_head,
+    the final RMS norm, the BF16 head and the greedy pick, against the oracle's
+    restatements step by step (hc_head's expf aside, the same bits)."""
+    import torch
+    import oracle
+    import pack
+    rng = np.random.default_rng(31)
+    hc, hidden, vocab, nt = 4, 1024, 3000, 2
+    x = rng.standard_normal((nt, hc, hidden)).astype(np.float32)
+    fn = (rng.standard_normal((hc, hc * hidden)) * 0.02).astype(np.float32)
+    base = rng.standard_normal(hc).astype(np.float32)
+    scale = np.array([1.3], np.float32)
+    norm_w = (1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+    W = pack.bf16_bits((rng.standard_normal((vocab, hidden)) * 0.05).astype(np.float32))
+    t = torch
+    h = t.empty((nt, hidden), dtype=t.float32, device="cuda")
+    dev.hc_head(h, t.from_numpy(x).cuda(), t.from_numpy(fn).cuda(), t.from_numpy(base).cuda(),
+                t.from_numpy(scale).cuda(), nt, hc, hidden)
+    dev.rmsnorm(h, h, t.from_numpy(norm_w).cuda(), hidden, nt, 1e-6)
+    logits = t.empty((nt, vocab), dtype=t.float32, device="cuda")
+    best = t.empty(nt, dtype=t.int32, device="cuda")
+    dev.head(logits, best, h, dev.qmat(t.from_numpy(W).cuda(), None, 1, vocab, hidden), nt)
+    got_h, got_l, got_b = h.cpu().numpy(), logits.cpu().numpy(), best.cpu().numpy()
+    for k in range(nt):
+        hh = orc.hc_head(x[k], fn, base, scale, 1e-6, 1e-6)
+        hn = orc.rmsnorm(hh, norm_w, 1e-6)
+        assert float(np.abs(got_h[k] - hn).max()) <= 1e-6 * float(np.abs(hn).max())
+        want = orc.mmq(got_h[k][None], oracle.qmat(W, None, 1, vocab, hidden))[0]   # the head itself is exact
+        assert np.array_equal(got_l[k].view(np.uint32), want.view(np.uint32))
+        assert int(got_b[k]) == int(np.argmax(want))
+        print(f"head path token {k}: normalised state bit-identical: {np.array_equal(got_h[k].view(np.uint32), hn.view(np.uint32))}")
