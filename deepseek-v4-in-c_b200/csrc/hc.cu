@@ -1,5 +1,5 @@
 // hc.cu - mHC pre-mix (dsv4_hc_pre with dsv4_hc_split_sinkhorn, and the
-// output head's hc_head) on the device.
+// output head's hc_head) and the KV compressor step on the device.
 //
 // Reference: src/10_compute/dsv4_hc.c. Per token, over the hc residual copies
 // x [hc][hidden] (hcdim = hc * hidden):
@@ -178,9 +178,79 @@ __global__ void __launch_bounds__(256) hc_head_kernel(float *__restrict__ y, con
     }
 }
 
+// ------------------------------------------------------------ compressor
+// dsv4_compress_step (src/10_compute/dsv4_compress.c): the token's kv and
+// score (+ ape[pos % ratio]) go into its slot; when the window closes each
+// channel pools its slots with a softmax over the slot axis (max, then
+// e = expf(v - max) over finite slots, denominator and weighted sum in double
+// in slot order, (float)(acc / denom)). Ratio 4 overlaps the previous window:
+// slots 0..3 read the first half of each slot's channels, slots 4..7 the
+// second half, and the state then slides by one window. expf as above.
+__global__ void compress_place_kernel(float *__restrict__ kv_state, float *__restrict__ score_state,
+                                      const float *__restrict__ kv_in, const float *__restrict__ score_in,
+                                      const float *__restrict__ apr, int slot, int width)
+{
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= width) return;
+    kv_state[(size_t)slot * width + c] = kv_in[c];
+    score_state[(size_t)slot * width + c] = __fadd_rn(score_in[c], apr[c]);
+}
+
+__global__ void compress_pool_kernel(float *__restrict__ out, const float *__restrict__ kv_state,
+                                     const float *__restrict__ score_state, int ratio, int head_dim, int overlap)
+{
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= head_dim) return;
+    const int width = (1 + overlap) * head_dim, nslot = overlap ? 2 * ratio : ratio;
+    auto at = [&](int s) -> size_t { return (size_t)s * width + ((overlap && s >= ratio) ? head_dim : 0) + c; };
+    float mx = -INFINITY;
+    for (int s = 0; s < nslot; s++) {
+        const float v = score_state[at(s)];
+        if (v > mx) mx = v;
+    }
+    if (mx == -INFINITY) {
+        out[c] = 0.0f;
+        return;
+    }
+    double denom = 0.0, acc = 0.0;
+    for (int s = 0; s < nslot; s++) {
+        const float v = score_state[at(s)];
+        if (v == -INFINITY) continue;
+        const double e = (double)hc_expf(__fsub_rn(v, mx));
+        denom = __dadd_rn(denom, e);
+        acc = __dadd_rn(acc, __dmul_rn(e, (double)kv_state[at(s)]));
+    }
+    out[c] = __double2float_rn(__ddiv_rn(acc, denom));
+}
+
 }  // namespace dsv4cu
 
 using namespace dsv4cu;
+
+extern "C" int dsv4cu_compress_step(float *out, const float *kv_in, const float *score_in, const float *ape,
+                                    float *kv_state, float *score_state, int pos, int ratio, int head_dim,
+                                    void *stream)
+{
+    if (!out || !kv_in || !score_in || !ape || !kv_state || !score_state || pos < 0 || ratio <= 0 || head_dim <= 0)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "compress_step: bad args");
+    cudaStream_t st = (cudaStream_t)stream;
+    const int overlap = ratio == 4, width = (1 + overlap) * head_dim, phase = pos % ratio;
+    const int slot = overlap ? ratio + phase : phase;
+    compress_place_kernel<<<(unsigned)((width + 255) / 256), 256, 0, st>>>(kv_state, score_state, kv_in, score_in,
+                                                                          ape + (size_t)phase * width, slot, width);
+    DSV4CU_LAUNCH_CHECK();
+    if ((pos + 1) % ratio != 0) return 0;
+    compress_pool_kernel<<<(unsigned)((head_dim + 127) / 128), 128, 0, st>>>(out, kv_state, score_state, ratio,
+                                                                            head_dim, overlap);
+    DSV4CU_LAUNCH_CHECK();
+    if (overlap) {
+        const size_t b = (size_t)ratio * width * sizeof(float);
+        DSV4CU_CUDA_TRY(cudaMemcpyAsync(kv_state, kv_state + (size_t)ratio * width, b, cudaMemcpyDeviceToDevice, st));
+        DSV4CU_CUDA_TRY(
+            cudaMemcpyAsync(score_state, score_state + (size_t)ratio * width, b, cudaMemcpyDeviceToDevice, st));
+    }
+    return 1;
+}
 
 extern "C" int dsv4cu_hc_head(float *y, const float *x, const float *fn, const float *base, const float *scale,
                               int nt, int hc, int hidden, float norm_eps, float hc_eps, void *stream)

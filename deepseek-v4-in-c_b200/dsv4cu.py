@@ -93,6 +93,7 @@ def lib() -> C.CDLL:
             "dsv4cu_hc_post": (i, [vp, vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_hc_pre": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i, f, f, vp]),
             "dsv4cu_hc_head": (i, [vp, vp, vp, vp, vp, i, i, i, f, f, vp]),
+            "dsv4cu_compress_step": (i, [vp, vp, vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_rope_apply": (i, [vp, vp, i, i, i, i, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_experts_load": (i, [C.POINTER(vp), vp, C.c_char_p, C.c_char_p, i, i, i, i, i, vp]),
             "dsv4cu_experts_free": (None, [vp]),
@@ -439,6 +440,13 @@ class Device:
                 hc_eps: float = 1e-6):
         check(self.L.dsv4cu_hc_head(self.ptr(y), self.ptr(x), self.ptr(fn), self.ptr(base), self.ptr(scale), nt, hc,
                                     hidden, norm_eps, hc_eps, self.stream()), "hc_head")
+
+    def compress_step(self, out, kv_in, score_in, ape, kv_state, score_state, pos: int, ratio: int, head_dim: int):
+        r = self.L.dsv4cu_compress_step(self.ptr(out), self.ptr(kv_in), self.ptr(score_in), self.ptr(ape),
+                                        self.ptr(kv_state), self.ptr(score_state), pos, ratio, head_dim, self.stream())
+        if r < 0:
+            check(r, "compress_step")
+        return r
 
     def hc_post(self, y, x, residual, post, comb, nt: int, hc: int, hidden: int):
         check(self.L.dsv4cu_hc_post(self.ptr(y), self.ptr(x), self.ptr(residual), self.ptr(post), self.ptr(comb), nt,

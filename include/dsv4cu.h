@@ -347,6 +347,16 @@ int dsv4cu_hc_pre(float *y, float *post, float *comb, float *mixes, const float 
                   const float *base, const float *scale, int nt, int hc, int hidden, int iters, float norm_eps,
                   float hc_eps, void *stream);
 
+/* One KV compressor step (dsv4_compress_step, src/10_compute/dsv4_compress.c)
+ * on device buffers: kv_in / score_in [coff * head_dim] (coff = 2 when ratio
+ * is 4, else 1), ape [ratio][coff * head_dim], the layer's ring states
+ * kv_state / score_state [coff * ratio][coff * head_dim]. Returns 1 when the
+ * window closed and out [head_dim] was written (on the stream), 0 when not,
+ * a negative status on bad arguments - the reference's return contract. The
+ * reference's double sums in its order; expf as in dsv4cu_hc_pre. */
+int dsv4cu_compress_step(float *out, const float *kv_in, const float *score_in, const float *ape, float *kv_state,
+                         float *score_state, int pos, int ratio, int head_dim, void *stream);
+
 /* The output head's mHC (hc_head, src/90_cli/dsv4_decode.c:102-125): from
  * x [nt][hc][hidden] and the head's fn [hc][hc hidden], base [hc], scale [1],
  * y [nt][hidden] = sum over j of pre[j] * x[j], pre the head's sigmoid mix.

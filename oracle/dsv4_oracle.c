@@ -245,6 +245,63 @@ void orc_hc_pre(float *y, float *post, float *comb, float *mixes, const float *x
     }
 }
 
+/* src/10_compute/dsv4_compress.c (pool_channel): max over the slots, then
+ * e = (double)expf(v - max) over the finite slots, denominator and weighted
+ * sum in double in slot order, (float)(acc / denom); 0 when every slot is -inf. */
+static float orc_pool_channel(const float *kv, const float *sc, int slots, int kv_stride, int sc_stride, int c)
+{
+    float mx = -INFINITY;
+    for (int s = 0; s < slots; s++) {
+        const float v = sc[(size_t)s * sc_stride + c];
+        if (v > mx) mx = v;
+    }
+    if (mx == -INFINITY) return 0.0f;
+    double denom = 0.0, acc = 0.0;
+    for (int s = 0; s < slots; s++) {
+        const float v = sc[(size_t)s * sc_stride + c];
+        if (v == -INFINITY) continue;
+        const double e = (double)expf(v - mx);
+        denom += e;
+        acc += e * (double)kv[(size_t)s * kv_stride + c];
+    }
+    return (float)(acc / denom);
+}
+
+/* src/10_compute/dsv4_compress.c (dsv4_compress_step): the token goes into
+ * its slot (score + ape[pos % ratio]); when the window closes the slots are
+ * pooled per channel - ratio 4 overlaps the previous window (first half of
+ * each slot's channels) with the current one (second half), then slides. */
+int orc_compress_step(float *out, const float *kv_in, const float *score_in, const float *ape, float *kv_state,
+                      float *score_state, int pos, int ratio, int head_dim)
+{
+    const int overlap = ratio == 4, coff = 1 + overlap, width = coff * head_dim, nslot = coff * ratio;
+    const int phase = pos % ratio, slot = overlap ? ratio + phase : phase;
+    const float *apr = ape + (size_t)phase * width;
+    for (int c = 0; c < width; c++) {
+        kv_state[(size_t)slot * width + c] = kv_in[c];
+        score_state[(size_t)slot * width + c] = score_in[c] + apr[c];
+    }
+    if ((pos + 1) % ratio != 0) return 0;
+    if (!overlap) {
+        for (int c = 0; c < head_dim; c++) out[c] = orc_pool_channel(kv_state, score_state, nslot, width, width, c);
+        return 1;
+    }
+    const int d = head_dim;
+    float *gk = malloc(sizeof(float) * 2 * ratio * d), *gs = malloc(sizeof(float) * 2 * ratio * d);
+    for (int s = 0; s < ratio; s++) {
+        memcpy(gk + (size_t)s * d, kv_state + (size_t)s * width, sizeof(float) * d);
+        memcpy(gs + (size_t)s * d, score_state + (size_t)s * width, sizeof(float) * d);
+        memcpy(gk + (size_t)(ratio + s) * d, kv_state + (size_t)(ratio + s) * width + d, sizeof(float) * d);
+        memcpy(gs + (size_t)(ratio + s) * d, score_state + (size_t)(ratio + s) * width + d, sizeof(float) * d);
+    }
+    for (int c = 0; c < d; c++) out[c] = orc_pool_channel(gk, gs, 2 * ratio, d, d, c);
+    free(gk);
+    free(gs);
+    memmove(kv_state, kv_state + (size_t)ratio * width, sizeof(float) * ratio * width);
+    memmove(score_state, score_state + (size_t)ratio * width, sizeof(float) * ratio * width);
+    return 1;
+}
+
 /* src/90_cli/dsv4_decode.c:102-125 (hc_head): sq summed in index order
  * (products then adds), rs = (float)(1 / sqrt(sq / hcdim + norm_eps)); per copy
  * j one sequential fma chain over the whole hc x hidden vector, m = (float)acc *

@@ -48,6 +48,8 @@ void orc_rope_apply(float *v, int head_dim, int rd, const float *cs, const float
                     int inverse);
 void orc_hc_pre(float *y, float *post, float *comb, float *mixes, const float *x, const float *fn,
                 const float *base, const float *scale, int hc, int hidden, int iters, float norm_eps, float hc_eps);
+int orc_compress_step(float *out, const float *kv_in, const float *score_in, const float *ape, float *kv_state,
+                      float *score_state, int pos, int ratio, int head_dim);
 void orc_hc_head(float *y, const float *x, const float *fn, const float *base, const float *scale, int hc,
                  int hidden, float norm_eps, float hc_eps);
 void orc_hc_post(float *y, const float *x, const float *residual, const float *post, const float *comb, int hc,

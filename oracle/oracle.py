@@ -74,6 +74,7 @@ class _Common:
         f("rope_apply").restype = None
         f("hc_post").restype = None
         f("hc_pre").restype = None
+        f("compress_step").restype = C.c_int
 
     def fn(self, name):
         return getattr(self.lib, self.pf + name)
@@ -145,6 +146,15 @@ class _Common:
                              _p(np.ascontiguousarray(base, np.float32)), _p(np.ascontiguousarray(scale, np.float32)),
                              C.c_int(hc), C.c_int(hidden), C.c_float(norm_eps), C.c_float(hc_eps))
         return y
+
+    def compress_step(self, kv_in, score_in, ape, kv_state, score_state, pos, ratio, head_dim):
+        """Updates kv_state / score_state in place; returns (emitted, out [head_dim])."""
+        out = np.zeros(head_dim, np.float32)
+        r = self.fn("compress_step")(_p(out), _p(np.ascontiguousarray(kv_in, np.float32)),
+                                     _p(np.ascontiguousarray(score_in, np.float32)),
+                                     _p(np.ascontiguousarray(ape, np.float32)), _p(kv_state), _p(score_state),
+                                     C.c_int(pos), C.c_int(ratio), C.c_int(head_dim))
+        return r, out
 
     def hc_post(self, x, residual, post, comb):
         """x [hidden], residual [hc][hidden], post [hc], comb [hc][hc] -> y [hc][hidden]."""

@@ -154,3 +154,38 @@ def test_head_path_hc_norm_gemv_pick(dev, orc):
         assert np.array_equal(got_l[k].view(np.uint32), want.view(np.uint32))
         assert int(got_b[k]) == int(np.argmax(want))
         print(f"head path token {k}: normalised state bit-identical: {np.array_equal(got_h[k].view(np.uint32), hn.view(np.uint32))}")
+
+
+@pytest.mark.parametrize("ratio", [4, 8, 128])
+def test_compress_steps_vs_oracle(dev, orc, ratio):
+    """dsv4cu_compress_step over several windows against the oracle's
+    dsv4_compress_step (pinned live to the reference): the emit contract and the
+    ring states bit for bit, the pooled rows within 1e-6 (expf) and counted
+    bit-identical."""
+    import torch
+    rng = np.random.default_rng(ratio + 1)
+    d = 128
+    coff = 2 if ratio == 4 else 1
+    width = coff * d
+    ape = rng.standard_normal((ratio, width)).astype(np.float32)
+    ks, ss = (np.zeros((coff * ratio, width), np.float32) for _ in range(2))
+    dks, dss = (torch.zeros((coff * ratio, width), dtype=torch.float32, device="cuda") for _ in range(2))
+    dape = torch.from_numpy(ape).cuda()
+    out = torch.empty(d, dtype=torch.float32, device="cuda")
+    same = total = 0
+    for pos in range(3 * ratio):
+        kv = rng.standard_normal(width).astype(np.float32)
+        sc = rng.standard_normal(width).astype(np.float32)
+        sc[rng.integers(0, width, 2)] = -np.inf
+        r_want, o_want = orc.compress_step(kv, sc, ape, ks, ss, pos, ratio, d)
+        r_got = dev.compress_step(out, torch.from_numpy(kv).cuda(), torch.from_numpy(sc).cuda(), dape, dks, dss, pos,
+                                  ratio, d)
+        assert r_got == r_want
+        if r_got:
+            got = out.cpu().numpy()
+            assert float(np.abs(got - o_want).max()) <= 1e-6 * max(float(np.abs(o_want).max()), 1e-30)
+            same += int(np.sum(got.view(np.uint32) == o_want.view(np.uint32)))
+            total += d
+        assert np.array_equal(dks.cpu().numpy().view(np.uint32), ks.view(np.uint32))
+        assert np.array_equal(dss.cpu().numpy().view(np.uint32), ss.view(np.uint32))
+    print(f"compress ratio {ratio}: {same} of {total} pooled values bit-identical")
