@@ -1,0 +1,307 @@
+// gemv_stream.cu - the decode GEMV (1 or 2 tokens) of one packed FP8 / FP4
+// matrix on the streamed GEMV core (stream_mv.cuh).
+//
+// Reference: fp8_n / fp4_n (src/10_compute/dsv4_matmul_fp8.c:49-177,
+// dsv4_matmul_fp4.c:46-162) behind dsv4_mmq_n (src/10_compute/dsv4_matmul.c:
+// 34-73): y[t * rows + o] = sum_c x[t * cols + c] * W[o][c].
+//
+// Two launches chained by programmatic dependent launch:
+//   split   x -> the f16 hi / lo operand (one warp per token and 32-element
+//           block); it lets the GEMV launch at its start;
+//   stream  the matrix as stages of (32-row group, 1 KB row segment) in row
+//           order; CTA c of G takes the contiguous stage range
+//           [S c / G, S (c + 1) / G), so every SM streams the same number of
+//           bytes. The weights do not depend on the split, so the producer
+//           starts at once. A row group inside one CTA's range is finished by
+//           its epilogue; a row group split between CTAs leaves one partial
+//           per CTA, and the CTA whose partial arrives last (a per-row-group
+//           counter) adds them in CTA order.
+// Each output is summed in one fixed order that depends on the matrix shape
+// and the SM count only: a token's row has the same bits for nt = 1 and 2
+// and on every run.
+#include <stdio.h>
+
+#include "common.cuh"
+#include "ctx.h"
+#include "stream_mv.cuh"
+
+namespace dsv4cu {
+
+struct SmvDenseParams {
+    SmvGeom geom;
+    CUtensorMap wmap, smap;    // streamer maps of the matrix (stream_mv.cuh)
+    dsv4cu_qmat q;
+    const uint16_t *xh, *xl;   // [nt][K]
+    const float *xs;           // [nt][K / 32]
+    float *y;                  // [nt][rows]
+    float *part;               // [rows / 32][maxparts][32][NT]
+    int *cnt;                  // [rows / 32] arrivals (zero between calls)
+    int nt, K, nseg, maxparts;
+    long long stages;          // (rows / 32) * nseg
+    int *status;
+};
+
+// CTA whose range holds stage q (ranges [S c / G, S (c + 1) / G)).
+DSV4CU_DEV int smv_dense_cta(long long q, long long S, int G) { return (int)(((q + 1) * G + S - 1) / S) - 1; }
+
+// The operand (every token's x, buffer 0) after the split kernel finished.
+// Producer thread.
+template <int NT>
+DSV4CU_DEV void smv_dense_operand(uint8_t *bufs, SmvSmem<NT> &sm, const SmvDenseParams &p)
+{
+    pdl_wait();
+    int rows[NT];
+    for (int i = 0; i < NT; i++) rows[i] = i < p.nt ? i : 0;
+    smv_put_operand(bufs, p.geom.bstride, 0, sm, p.xh, p.xl, p.xs, p.K, rows, p.nt);
+}
+
+// Weights stream from the start: the first ring's worth of stages goes out
+// before the wait for the split kernel, then the operand, then the rest.
+// Producer thread; stage q = (32-row group r, segment sg) with q = r nseg + sg.
+template <int NT>
+DSV4CU_DEV void smv_dense_producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm, const SmvDenseParams &p)
+{
+    const long long S = p.stages, G = gridDim.x;
+    const long long b0 = S * blockIdx.x / G, b1 = S * (blockIdx.x + 1) / G;
+    const SmvMat m = smv_mat(p.q, &p.wmap, &p.smap);
+    SmvDrain dr = {0u, 0u};
+    int slot = 0;
+    uint32_t ph = 0;
+    SmvDesc d;
+    d.bbuf = 0;
+    d.bk = p.K;
+    d.ntok = p.nt;
+    d.combo = 0;
+    d.e3 = 1;
+    int job = 0, s0 = 0, r = (int)(b0 / p.nseg), sg = (int)(b0 - (long long)r * p.nseg);
+    bool ok = true, pend = true;
+    for (long long q = b0; q < b1 && ok; q++) {
+        const bool first = q == b0 || sg == 0, last = q == b1 - 1 || sg == p.nseg - 1;
+        if (first) s0 = sg;
+        smv_seg_fields(d, m, r * SMV_ROWS, sg);
+        d.job = job;
+        d.flags = (first ? SMV_F_FIRST : 0) | (q == b0 ? SMV_F_LOAD : 0) | (last ? SMV_F_FLUSH | SMV_F_LAST : 0);
+        d.e0 = r;
+        d.e1 = s0;
+        d.e2 = last ? sg + 1 : 0;
+        if (pend && q - b0 >= p.geom.ns) {
+            smv_dense_operand(bufs, sm, p);
+            pend = false;
+        }
+        ok = smv_slot_free(sm, slot, ph, p.status);
+        if (ok) smv_put_stage(ring, sm, dr, slot, ph, d, m, r * SMV_ROWS, sg);
+        if (++slot == p.geom.ns) {
+            slot = 0;
+            ph ^= 1u;
+        }
+        if (last) job++;
+        if (++sg == p.nseg) {
+            sg = 0;
+            r++;
+        }
+    }
+    if (pend && b1 > b0) smv_dense_operand(bufs, sm, p);
+    smv_end_marker<NT>(sm, dr, slot, ph, p.status);
+    pdl_trigger();
+}
+
+// y value with the reference's NaN bits (ref_row_nan) when the sum is NaN.
+DSV4CU_DEV float smv_dense_fix(const SmvDenseParams &p, int row, float v)
+{
+    if (!isnan(v)) return v;
+    const bool fp4 = p.q.wdt == DSV4CU_WFP4;
+    const int rb = fp4 ? p.K / 2 : p.K, s_ld = (p.K + p.q.blk_c - 1) / p.q.blk_c;
+    const uint8_t *w_row = (const uint8_t *)p.q.w + (size_t)row * rb;
+    const uint8_t *s_row = (const uint8_t *)p.q.s + (size_t)(fp4 ? row : row / p.q.blk_r) * s_ld;
+    return ref_row_nan(w_row, s_row, p.K, p.q.blk_c, fp4);
+}
+
+template <int NT>
+DSV4CU_DEV void smv_dense_epilogue(const SmvDenseParams &p, const SmvSmem<NT> &sm, int eb, const SmvEpi &e)
+{
+    const int lane = threadIdx.x & 31;
+    const int r = e.e0, s0 = e.e1, s1 = e.e2, row = r * SMV_ROWS + lane;
+    const int rows = p.q.rows;
+    if (s0 == 0 && s1 == p.nseg) {
+        for (int i = 0; i < e.ntok; i++) p.y[(size_t)i * rows + row] = smv_dense_fix(p, row, smv_job_value(sm, eb, 0, lane, i));
+        return;
+    }
+    // A part of a row group that other CTAs share: store it, count it, and
+    // the last arrival sums the parts in CTA order. The parts are the
+    // distinct owners of the group's stages (CTAs with empty ranges own none).
+    const long long S = p.stages, q0 = (long long)r * p.nseg;
+    int nparts = 0, ord = 0, prev = -1;
+    for (int k = 0; k < p.nseg; k++) {
+        const int c = smv_dense_cta(q0 + k, S, gridDim.x);
+        if (c != prev) {
+            if (c == (int)blockIdx.x) ord = nparts;
+            nparts++;
+            prev = c;
+        }
+    }
+    float *base = p.part + (size_t)r * p.maxparts * SMV_ROWS * NT;
+    for (int i = 0; i < e.ntok; i++) base[((size_t)ord * SMV_ROWS + lane) * NT + i] = smv_job_value(sm, eb, 0, lane, i);
+    __threadfence();
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) old = atomicAdd(p.cnt + r, 1);
+    old = __shfl_sync(0xFFFFFFFFu, old, 0);
+    if (old != nparts - 1) return;
+    __threadfence();
+    for (int i = 0; i < e.ntok; i++) {
+        float s = 0.0f;
+        for (int k = 0; k < nparts; k++) s += __ldcg(base + ((size_t)k * SMV_ROWS + lane) * NT + i);
+        p.y[(size_t)i * rows + row] = smv_dense_fix(p, row, s);
+    }
+    if (lane == 0) atomicExch(p.cnt + r, 0);    // zero again for the next call
+}
+
+struct SmvDensePolicy {
+    using Params = SmvDenseParams;
+    template <int NT>
+    static DSV4CU_DEV void producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm, const Params &p)
+    {
+        smv_dense_producer<NT>(ring, bufs, sm, p);
+    }
+    template <int NT>
+    static DSV4CU_DEV void epilogue(const Params &p, const SmvSmem<NT> &sm, int eb, const SmvEpi &e)
+    {
+        smv_dense_epilogue<NT>(p, sm, eb, e);
+    }
+};
+
+// x -> f16 hi / lo operand, one warp per (token, 32-element block).
+__global__ void __launch_bounds__(256) smv_split_kernel(const float *__restrict__ x, int K, int nt,
+                                                       uint16_t *__restrict__ xh, uint16_t *__restrict__ xl,
+                                                       float *__restrict__ xs)
+{
+    pdl_trigger();       // the GEMV streams weights meanwhile
+    pdl_wait();          // x may come from the previous kernel
+    const int lane = threadIdx.x & 31, nblk = K >> 5;
+    const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5);
+    if (gw >= nt * nblk) return;
+    const int t = gw / nblk, b = gw - t * nblk;
+    const size_t i = (size_t)t * K + b * 32 + lane;
+    uint16_t hi, lo;
+    float fac;
+    smv_split32(x[i], hi, lo, fac);
+    xh[i] = hi;
+    xl[i] = lo;
+    if (lane == 0) xs[(size_t)t * nblk + b] = fac;
+}
+
+struct DenseShape {
+    int nt, NT, K, nseg, maxparts, groups;
+    long long stages;
+};
+
+static DenseShape dense_shape(const dsv4cu_qmat *m, int nt)
+{
+    DenseShape s;
+    s.nt = nt;
+    s.NT = nt <= 1 ? 1 : 2;
+    s.K = m->cols;
+    const int rb = m->wdt == DSV4CU_WFP4 ? m->cols / 2 : m->cols;
+    s.nseg = (rb + SMV_SEG - 1) / SMV_SEG;
+    s.groups = m->rows / SMV_ROWS;
+    s.stages = (long long)s.groups * s.nseg;
+    s.maxparts = s.nseg;       // each part of a row group owns at least one of its stages
+    return s;
+}
+
+static size_t dense_layout(const DenseShape &s, char *base, SmvDenseParams *p)
+{
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        char *q = base ? base + off : nullptr;
+        off += dsv4cu_align256(bytes);
+        return q;
+    };
+    char *xh = take((size_t)s.nt * s.K * 2), *xl = take((size_t)s.nt * s.K * 2);
+    char *xs = take((size_t)s.nt * (s.K / 32) * 4);
+    char *part = take((size_t)s.groups * s.maxparts * SMV_ROWS * s.NT * 4);
+    if (p) {
+        p->xh = (const uint16_t *)xh;
+        p->xl = (const uint16_t *)xl;
+        p->xs = (const float *)xs;
+        p->part = (float *)part;
+    }
+    return off;
+}
+
+static bool dense_ok(const dsv4cu_qmat *m, int nt)
+{
+    return m && nt >= 1 && nt <= SMV_MAXT && m->rows / SMV_ROWS <= DSV4CU_MAX_COUNTERS &&
+           smv_ok(m->wdt, m->w, m->s, m->rows, m->cols, m->blk_r, m->blk_c);
+}
+
+template <int NT>
+static int dense_launch(SmvDenseParams &p, int sms, cudaStream_t st)
+{
+    static SmemLimit lim;
+    p.geom = smv_geometry<NT>(p.K, 1);
+    const int smem = smv_smem_bytes<NT>(p.geom);
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)smv_kernel<NT, SmvDensePolicy>, smem));
+    DSV4CU_CUDA_TRY(launch_pdl(smv_kernel<NT, SmvDensePolicy>, dim3(sms), dim3(SMV_THREADS), smem, st, p));
+    return DSV4CU_OK;
+}
+
+}  // namespace dsv4cu
+
+using namespace dsv4cu;
+
+extern "C" size_t dsv4cu_gemv_workspace(const dsv4cu_qmat *m, int nt)
+{
+    if (!dense_ok(m, nt)) return dsv4cu_mmq_workspace(m, nt);
+    return dense_layout(dense_shape(m, nt), nullptr, nullptr);
+}
+
+extern "C" int dsv4cu_gemv_ev(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m, int nt, void *stream,
+                              void **events)
+{
+    if (!ctx || !y || !x || !m) return dsv4cu_set_error(DSV4CU_ERR_ARG, "gemv: NULL argument");
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaEvent_t *ev = (cudaEvent_t *)events;
+    if (!dense_ok(m, nt)) {
+        // Shapes the streamer does not read (and nt > 2) take dsv4cu_mmq.
+        if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
+        if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
+        const int r = dsv4cu_mmq(ctx, y, x, m, nt, stream);
+        if (!r && ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
+        return r;
+    }
+    const int sms = ctx->sm_count;
+    const DenseShape s = dense_shape(m, nt);
+    void *ws = nullptr;
+    int r = dsv4cu_ws_get(ctx, dense_layout(s, nullptr, nullptr), &ws);
+    if (r) return r;
+    SmvDenseParams p;
+    dense_layout(s, (char *)ws, &p);
+    p.q = *m;
+    r = smv_encode(m, &p.wmap, &p.smap);
+    if (r) return r;
+    p.y = y;
+    p.cnt = ctx->counters;
+    p.nt = nt;
+    p.K = s.K;
+    p.nseg = s.nseg;
+    p.maxparts = s.maxparts;
+    p.stages = s.stages;
+    p.status = ctx->status;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
+    {
+        const long warps = (long)nt * (s.K / 32);
+        DSV4CU_CUDA_TRY(launch_pdl(smv_split_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, st, x, s.K, nt,
+                                   (uint16_t *)p.xh, (uint16_t *)p.xl, (float *)p.xs));
+    }
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
+    r = s.NT == 1 ? dense_launch<1>(p, sms, st) : dense_launch<2>(p, sms, st);
+    if (r) return r;
+    if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
+    return DSV4CU_OK;
+}
+
+extern "C" int dsv4cu_gemv(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m, int nt, void *stream)
+{
+    return dsv4cu_gemv_ev(ctx, y, x, m, nt, stream, nullptr);
+}

@@ -36,6 +36,13 @@ struct dsv4cu_moe {
     // Tensor-core path (mx_ok == 0 when a matrix does not qualify).
     int mx_ok;
     int sms;                        // SM count of the layer's device (sizes the tensor-core work split)
+    // Streamed decode path (moe_stream.cu): every matrix readable by the
+    // streamer (stream_mv.cuh); used for one or two tokens. smv_maps: per
+    // matrix 3e + m (m = w1, w3, w2) its weight map and FP4 scale map.
+    int smv_ok;
+    int path;                       // DSV4CU_MOE_PATH_* chosen by dsv4cu_moe_set_path
+    void *smv_block;
+    const CUtensorMap *smv_maps;
     void *mx_block;                 // maps + scale blocks + pointer table, one allocation
     dsv4cu::MoeMxDev mx;
 };
@@ -57,6 +64,13 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
                    const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
                    int terms, int *idx_out, float *wts_out, void *ws, int *status, int sms, cudaStream_t st,
                    cudaEvent_t *ev);
+
+bool smv_moe_layer_ok(const dsv4cu_expert *hexp, int n_experts, int hidden, int inter);
+int smv_moe_prepare(dsv4cu_moe *L, const dsv4cu_expert *hexp);
+size_t smv_moe_workspace(const dsv4cu_moe *L, int topk, int nt);
+int smv_moe_decode(const dsv4cu_moe *L, float *out, const float *x, const float *logits, const float *bias,
+                   const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
+                   int *idx_out, float *wts_out, void *ws, int *status, int sms, cudaStream_t st, cudaEvent_t *ev);
 
 size_t moe_mx_rows_workspace(const dsv4cu_moe *L, int nrows);
 int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const int *ids, int nrows, float limit,

@@ -32,6 +32,7 @@
 #include "gemv_core.cuh"
 #include "moe.h"
 #include "router.cuh"
+#include "stream_mv.cuh"
 #include "tma_gemv.cuh"
 #include "tmap.h"
 
@@ -545,6 +546,17 @@ static int expert_check(const dsv4cu_expert &e, int hidden, int inter, const cha
 
 using namespace dsv4cu;
 
+// Whether a decode of nt tokens takes the streamed path: chosen explicitly,
+// or by default only where the tensor-core path is missing (it is the faster
+// of the two for the layer shapes measured). Buckets of the streamed path
+// hold at most nt tokens, which hash routing (rows may repeat an expert)
+// breaks.
+static bool use_stream(const dsv4cu_moe *L, int nt, bool hash)
+{
+    if (!L->smv_ok || nt > SMV_MAXT || hash || L->path == DSV4CU_MOE_PATH_TENSOR) return false;
+    return L->path == DSV4CU_MOE_PATH_STREAM || !L->mx_ok;
+}
+
 extern "C" int dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts, int n_experts,
                                  const dsv4cu_expert *shared, int hidden, int inter)
 {
@@ -606,8 +618,21 @@ extern "C" int dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts,
     L->view.has_shared = L->has_shared;
     L->mx_ok = 0;
     L->mx_block = nullptr;
+    L->smv_ok = 0;
+    L->path = DSV4CU_MOE_PATH_AUTO;
+    L->smv_block = nullptr;
+    L->smv_maps = nullptr;
+    if (smv_moe_layer_ok(hexp.data(), n_experts, hidden, inter)) {
+        const int rs = smv_moe_prepare(L, hexp.data());
+        if (rs) {
+            cudaFree(blk);
+            delete L;
+            return rs;
+        }
+    }
     const int r = moe_mx_prepare(L, hexp.data());
     if (r && r != DSV4CU_ERR_UNSUPPORTED) {
+        cudaFree(L->smv_block);
         cudaFree(blk);
         delete L;
         return r;
@@ -616,10 +641,24 @@ extern "C" int dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts,
     return DSV4CU_OK;
 }
 
+extern "C" int dsv4cu_moe_set_path(dsv4cu_moe *L, int path)
+{
+    if (!L) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_set_path: NULL layer");
+    if (path == DSV4CU_MOE_PATH_TENSOR && !L->mx_ok)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_set_path: layer has no tensor-core path");
+    if (path == DSV4CU_MOE_PATH_STREAM && !L->smv_ok)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_set_path: layer has no streamed path");
+    if (path < DSV4CU_MOE_PATH_AUTO || path > DSV4CU_MOE_PATH_STREAM)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_set_path: path %d", path);
+    L->path = path;
+    return DSV4CU_OK;
+}
+
 extern "C" void dsv4cu_moe_destroy(dsv4cu_moe *L)
 {
     if (!L) return;
     moe_mx_release(L);
+    cudaFree(L->smv_block);
     cudaFree(L->dev_block);
     delete L;
 }
@@ -629,7 +668,8 @@ extern "C" size_t dsv4cu_moe_workspace(const dsv4cu_moe *L, int topk, int nt)
     if (!L) return 0;
     const size_t a = moe_decode_workspace(nt, topk, L->n_experts, L->hidden, L->inter, L->has_shared);
     const size_t b = L->mx_ok ? moe_mx_workspace(L, topk, nt) : 0;
-    return a > b ? a : b;
+    const size_t c = use_stream(L, nt, false) ? smv_moe_workspace(L, topk, nt) : 0;
+    return a > b ? (a > c ? a : c) : (b > c ? b : c);
 }
 
 extern "C" int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,
@@ -645,6 +685,12 @@ extern "C" int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, fl
     if (topk < 1 || topk > MOE_MAX_TOPK || topk > layer->n_experts)
         return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode: topk %d", topk);
     void *ws = nullptr;
+    if (use_stream(layer, nt, tid2eid != nullptr)) {
+        int r = dsv4cu_ws_get(ctx, smv_moe_workspace(layer, topk, nt), &ws);
+        if (r) return r;
+        return smv_moe_decode(layer, out, x, logits, bias, tid2eid, token_ids, topk, route_scale, limit, nt, idx_out,
+                              wts_out, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream, (cudaEvent_t *)events);
+    }
     if (layer->mx_ok) {
         int r = dsv4cu_ws_get(ctx, moe_mx_workspace(layer, topk, nt), &ws);
         if (r) return r;
@@ -752,12 +798,33 @@ __global__ void __launch_bounds__(1024) stage_in_kernel(float4 *__restrict__ dx,
     pdl_trigger();
 }
 
+// Workspace and launch of the decode path a layer takes for nt tokens
+// without bias, hash routing or index outputs.
+static size_t decode_plain_workspace(const dsv4cu_moe *layer, int topk, int nt)
+{
+    if (use_stream(layer, nt, false)) return smv_moe_workspace(layer, topk, nt);
+    if (layer->mx_ok) return moe_mx_workspace(layer, topk, nt);
+    return moe_decode_workspace(nt, topk, layer->n_experts, layer->hidden, layer->inter, layer->has_shared);
+}
+static int decode_plain(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x, const float *lg,
+                        int topk, float route_scale, float limit, int nt, void *ws, cudaStream_t st)
+{
+    if (use_stream(layer, nt, false))
+        return smv_moe_decode(layer, out, x, lg, nullptr, nullptr, nullptr, topk, route_scale, limit, nt, nullptr,
+                              nullptr, ws, ctx->status, ctx->sm_count, st, nullptr);
+    if (layer->mx_ok)
+        return moe_mx_decode(layer, out, x, lg, nullptr, nullptr, nullptr, topk, route_scale, limit, nt, nullptr,
+                             nullptr, ws, ctx->counters, ctx->status, ctx->sm_count, st, nullptr);
+    return moe_decode_run(layer, out, x, lg, nullptr, nullptr, nullptr, topk, route_scale, limit, nt, nullptr, nullptr,
+                          ws, ctx->counters, ctx->status, st, nullptr);
+}
+
 // Host buffers in and out, all on the stream, nothing synchronised. With
-// page-locked host buffers on the tensor-core path one staging kernel reads
-// x and the logits across the bus and the combine writes the output straight
-// into host memory (no copy operations between the step's launches);
-// otherwise x and logits are copied into staging after the step's workspace
-// and the output is copied back.
+// page-locked host buffers on the streamed or tensor-core path one staging
+// kernel reads x and the logits across the bus and the combine writes the
+// output straight into host memory (no copy operations between the step's
+// launches); otherwise x and logits are copied into staging after the step's
+// workspace and the output is copied back.
 extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out_host,
                                       const float *x_host, const float *logits_host, int topk, float route_scale,
                                       float limit, int nt, void *stream)
@@ -767,12 +834,11 @@ extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, 
     if (nt < 1 || nt > MOE_MAX_NT) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_decode_host: nt %d", nt);
     if (topk < 1 || topk > MOE_MAX_TOPK || topk > layer->n_experts)
         return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_decode_host: topk %d", topk);
-    const size_t need = layer->mx_ok ? moe_mx_workspace(layer, topk, nt)
-                                     : moe_decode_workspace(nt, topk, layer->n_experts, layer->hidden, layer->inter,
-                                                            layer->has_shared);
+    const size_t need = decode_plain_workspace(layer, topk, nt);
     const size_t xb = (size_t)nt * layer->hidden * 4, lb = (size_t)nt * layer->n_experts * 4;
     const size_t base = dsv4cu_align256(need);
-    if (layer->mx_ok && xb % 16 == 0) {
+    cudaStream_t st = (cudaStream_t)stream;
+    if ((layer->mx_ok || use_stream(layer, nt, false)) && xb % 16 == 0) {
         const void *mx = mapped_host(x_host), *ml = mapped_host(logits_host), *mo = mapped_host(out_host);
         if (mx && ml && mo && ((uintptr_t)mx & 15u) == 0) {
             void *ws = nullptr;
@@ -783,11 +849,9 @@ extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, 
             const long nx4 = (long)(xb / 16), nl = (long)(lb / 4);
             const long work = nx4 > nl ? nx4 : nl;
             const unsigned blocks = (unsigned)((work + 1023) / 1024 < 32 ? (work + 1023) / 1024 : 32);
-            DSV4CU_CUDA_TRY(launch_pdl(stage_in_kernel, dim3(blocks), dim3(1024), 0, (cudaStream_t)stream,
-                                       (float4 *)dx, (const float4 *)mx, nx4, dl, (const float *)ml, nl));
-            return moe_mx_decode(layer, (float *)mo, dx, dl, nullptr, nullptr, nullptr, topk, route_scale, limit, nt,
-                                 nullptr, nullptr, ws, ctx->counters, ctx->status, ctx->sm_count,
-                                 (cudaStream_t)stream, nullptr);
+            DSV4CU_CUDA_TRY(launch_pdl(stage_in_kernel, dim3(blocks), dim3(1024), 0, st, (float4 *)dx,
+                                       (const float4 *)mx, nx4, dl, (const float *)ml, nl));
+            return decode_plain(ctx, layer, (float *)mo, dx, dl, topk, route_scale, limit, nt, ws, st);
         }
     }
     void *ws = nullptr;
@@ -796,15 +860,9 @@ extern "C" int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, 
     float *dx = (float *)((char *)ws + base);
     float *dl = (float *)((char *)dx + dsv4cu_align256(xb));
     float *dout = (float *)((char *)dl + dsv4cu_align256(lb));
-    cudaStream_t st = (cudaStream_t)stream;
     DSV4CU_CUDA_TRY(cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, st));
     DSV4CU_CUDA_TRY(cudaMemcpyAsync(dl, logits_host, lb, cudaMemcpyHostToDevice, st));
-    if (layer->mx_ok)
-        r = moe_mx_decode(layer, dout, dx, dl, nullptr, nullptr, nullptr, topk, route_scale, limit, nt, nullptr,
-                          nullptr, ws, ctx->counters, ctx->status, ctx->sm_count, st, nullptr);
-    else
-        r = moe_decode_run(layer, dout, dx, dl, nullptr, nullptr, nullptr, topk, route_scale, limit, nt, nullptr,
-                           nullptr, ws, ctx->counters, ctx->status, st, nullptr);
+    r = decode_plain(ctx, layer, dout, dx, dl, topk, route_scale, limit, nt, ws, st);
     if (r) return r;
     DSV4CU_CUDA_TRY(cudaMemcpyAsync(out_host, dout, xb, cudaMemcpyDeviceToHost, st));
     return DSV4CU_OK;

@@ -4,6 +4,7 @@
 #include "common.cuh"
 #include "gemv.h"
 #include "tmap.h"
+#include "stream_mv.cuh"
 
 namespace dsv4cu {
 
@@ -66,6 +67,37 @@ int tmap_encode(const dsv4cu_qmat *q, CUtensorMap *wmap, CUtensorMap *smap, int 
                                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         if (r != CUDA_SUCCESS) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "cuTensorMapEncodeTiled(scales): %d", (int)r);
         *staged = 1;
+    }
+    return DSV4CU_OK;
+}
+
+// Streamed GEMV maps (stream_mv.cuh). Weights: 3-D uint8 view of
+// [rows][row_bytes] as (128-byte chunk piece, row, chunk) with strides
+// (row_bytes, 128), box 128 x 32 x min(8, chunks), 128-byte swizzle: one copy
+// moves 32 rows x up to 1 KB of row. FP4 scales of rows longer than one
+// stage: 2-D [rows][cols / 32] with 64 x 32 boxes.
+int smv_encode(const dsv4cu_qmat *q, CUtensorMap *wmap, CUtensorMap *smap)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const int rb = row_bytes_of(q->wdt, q->cols), chunks = rb / 128;
+    cuuint64_t dims[3] = {128, (cuuint64_t)q->rows, (cuuint64_t)chunks};
+    cuuint64_t strides[2] = {(cuuint64_t)rb, 128};
+    cuuint32_t box[3] = {128, SMV_ROWS, (cuuint32_t)(chunks < 8 ? chunks : 8)}, es[3] = {1, 1, 1};
+    CUresult r = enc(wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(q->w), dims, strides, box, es,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "cuTensorMapEncodeTiled(stream weights): %d", (int)r);
+    memset(smap, 0, sizeof *smap);
+    if (q->wdt == DSV4CU_WFP4 && rb > 1024) {
+        const int sl = q->cols / 32;
+        cuuint64_t sd[2] = {(cuuint64_t)sl, (cuuint64_t)q->rows};
+        cuuint64_t ss[1] = {(cuuint64_t)sl};
+        cuuint32_t sb[2] = {64, SMV_ROWS}, se[2] = {1, 1};
+        r = enc(smap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(q->s), sd, ss, sb, se,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "cuTensorMapEncodeTiled(stream scales): %d", (int)r);
     }
     return DSV4CU_OK;
 }

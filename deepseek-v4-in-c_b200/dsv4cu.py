@@ -61,10 +61,14 @@ def lib() -> C.CDLL:
             "dsv4cu_ctx_status": (i, [vp, vp, C.POINTER(i)]),
             "dsv4cu_mmq_workspace": (sz, [vp, i]),
             "dsv4cu_mmq": (i, [vp, vp, vp, vp, i, vp]),
+            "dsv4cu_gemv_workspace": (sz, [vp, i]),
+            "dsv4cu_gemv": (i, [vp, vp, vp, vp, i, vp]),
+            "dsv4cu_gemv_ev": (i, [vp, vp, vp, vp, i, vp, vp]),
             "dsv4cu_route": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, i, f, i, vp]),
             "dsv4cu_swiglu": (i, [vp, vp, vp, i, f, vp]),
             "dsv4cu_moe_create": (i, [C.POINTER(vp), vp, i, vp, i, i]),
             "dsv4cu_moe_destroy": (None, [vp]),
+            "dsv4cu_moe_set_path": (i, [vp, i]),
             "dsv4cu_moe_workspace": (sz, [vp, i, i]),
             "dsv4cu_moe_decode": (i, [vp, vp, vp, vp, vp, vp, vp, vp, i, f, f, i, vp, vp, vp]),
             "dsv4cu_moe_prefill_workspace": (sz, [vp, i, i, i]),
@@ -305,6 +309,15 @@ class Device:
         check(self.L.dsv4cu_mmq(self.ctx, self.ptr(y), self.ptr(x), C.byref(m), nt, self.stream()),
               "dsv4cu_mmq")
 
+    def gemv(self, y, x, m: QMat, nt: int, events=None):
+        """Decode GEMV (dsv4cu_gemv / dsv4cu_gemv_ev): one or two tokens streamed."""
+        if events is None:
+            check(self.L.dsv4cu_gemv(self.ctx, self.ptr(y), self.ptr(x), C.byref(m), nt, self.stream()),
+                  "dsv4cu_gemv")
+        else:
+            check(self.L.dsv4cu_gemv_ev(self.ctx, self.ptr(y), self.ptr(x), C.byref(m), nt, self.stream(),
+                                        _event_handles(events)), "dsv4cu_gemv_ev")
+
     def mat_create(self, m: QMat):
         """Prepare a packed matrix for the tensor-core GEMM (dsv4cu_mat_create)."""
         h = C.c_void_p()
@@ -355,6 +368,12 @@ class Device:
                                        None if shared is None else C.addressof(shared), hidden, inter),
               "dsv4cu_moe_create")
         return h
+
+    MOE_PATH = {"auto": 0, "tensor": 1, "stream": 2}
+
+    def moe_set_path(self, layer, path: str):
+        """Decode path of a layer (dsv4cu_moe_set_path): "auto", "tensor" or "stream"."""
+        check(self.L.dsv4cu_moe_set_path(layer, self.MOE_PATH[path]), "dsv4cu_moe_set_path")
 
     def moe_destroy(self, layer):
         self.L.dsv4cu_moe_destroy(layer)

@@ -90,6 +90,25 @@ size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt);
 int dsv4cu_mmq(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
                int nt, void *stream);
 
+/* Decode GEMV: the dsv4cu_mmq product for one or two tokens, streamed at
+ * HBM rate. Replaces fp8_n / fp4_n at decode (src/10_compute/
+ * dsv4_matmul_fp8.c:49-177, dsv4_matmul_fp4.c:46-162, behind dsv4_mmq_n,
+ * src/10_compute/dsv4_matmul.h:40). FP4 matrices with 1x32 scales and
+ * cols % 256 == 0, and FP8 matrices with blk_r % 32 == 0, blk_c % 64 == 0
+ * and cols % 128 == 0, with rows % 32 == 0, cols <= 8192 and 16-byte aligned
+ * weights (and FP4 scales), are read in 32-row x 1 KB tensor-map copies and
+ * reduced on the CUDA cores and mma.sync: results within about 1e-6 of fp32,
+ * and a token's row has the same bits for nt = 1 and 2 and on every run
+ * (they are not the bits of dsv4cu_mmq). Other shapes and nt > 2 run
+ * dsv4cu_mmq. */
+size_t dsv4cu_gemv_workspace(const dsv4cu_qmat *m, int nt);
+int dsv4cu_gemv(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
+                int nt, void *stream);
+/* dsv4cu_gemv recording events[0..2] (cudaEvent_t) on the stream: before
+ * the activation split, before the streamed GEMV and after it. */
+int dsv4cu_gemv_ev(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
+                   int nt, void *stream, void **events);
+
 /* ------------------------------------------- tensor-core (tcgen05) GEMM
  * A packed matrix prepared once for the block-scaled tensor-core GEMM: the
  * library keeps its TMA descriptor and a copy of its scale factors in the
@@ -172,6 +191,18 @@ int  dsv4cu_experts_index(const char *index_dir, int *n_layers, int *n_experts, 
 int  dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts, int n_experts,
                        const dsv4cu_expert *shared, int hidden, int inter);
 void dsv4cu_moe_destroy(dsv4cu_moe *layer);
+/* Which kernels a decode of one or two tokens takes. AUTO (the default): the
+ * tcgen05 path where every matrix qualifies for it, else the streamed path
+ * (one persistent CTA per SM over a queue of 32-row jobs, FP4/FP8 decoded in
+ * registers, mma.sync as the reduction). TENSOR / STREAM force one; a layer
+ * without that path returns DSV4CU_ERR_UNSUPPORTED. Hash routing, three or
+ * more tokens and dsv4cu_moe_prefill always take the tensor-core path. Both
+ * paths give the reference's results within the matmul tolerance; each is
+ * deterministic. */
+#define DSV4CU_MOE_PATH_AUTO   0
+#define DSV4CU_MOE_PATH_TENSOR 1
+#define DSV4CU_MOE_PATH_STREAM 2
+int  dsv4cu_moe_set_path(dsv4cu_moe *layer, int path);
 /* Workspace bytes one dsv4cu_moe_decode of this layer needs. */
 size_t dsv4cu_moe_workspace(const dsv4cu_moe *layer, int topk, int nt);
 

@@ -339,3 +339,45 @@ def test_prefill_seam(host, orc):
     for t in range(3):
         assert_close(ye[t], g["fp4_out"], "expert_fused")
     L.dsv4_prefill_vk_free(v)
+
+
+GEMV_SHAPES = [
+    # (wdt, rows, cols, blk_r, blk_c, nt): dsv4cu_gemv (streamed GEMV; other
+    # shapes take dsv4cu_mmq)
+    (2, 7168, 7168, 128, 128, 1),
+    (2, 4096, 8192, 128, 128, 2),     # wo_b, two tokens
+    (2, 1024, 4096, 128, 128, 1),     # wq_a: fewer row groups than SMs
+    (3, 2048, 4096, 1, 32, 1),        # routed w1/w3
+    (3, 4096, 2048, 1, 32, 2),        # routed w2
+    (3, 512, 8192, 1, 32, 1),         # FP4 rows wider than one 1 KB stage
+    (3, 77, 160, 1, 32, 2),           # not streamable: falls back to dsv4cu_mmq
+    (2, 129, 320, 128, 128, 1),       # not streamable: falls back to dsv4cu_mmq
+]
+
+
+@pytest.mark.parametrize("shape", GEMV_SHAPES, ids=lambda s: "w%d_%dx%d_b%dx%d_nt%d" % s)
+def test_gemv_stream_vs_oracle(dev, orc, shape):
+    """dsv4cu_gemv against the oracle (the reference's matvec within the
+    matmul tolerance), bit-identical run to run; an FP8 NaN code makes its
+    row NaN as in the reference."""
+    import torch
+    wdt, rows, cols, br, bc, nt = shape
+    rng = np.random.default_rng(rows * 7 + cols + nt)
+    W, S = make_weights(rng, wdt, rows, cols, br, bc)
+    if wdt == 2:
+        W[rows // 2, cols - 3] = 0x7F
+    x = pack.bf16_round(rng.standard_normal((nt, cols)).astype(np.float32))
+    want = orc.mmq(x, oracle.qmat(W, S, wdt, rows, cols, br, bc))
+    dW, dS, dx = (torch.from_numpy(a).cuda() for a in (W, S, x))
+    m = dev.qmat(dW, dS, wdt, rows, cols, br, bc)
+    y = torch.empty((nt, rows), dtype=torch.float32, device="cuda")
+    y2 = torch.empty_like(y)
+    dev.gemv(y, dx, m, nt)
+    dev.gemv(y2, dx, m, nt)
+    torch.cuda.synchronize()
+    dev.check_status()
+    got = y.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), y2.cpu().numpy().view(np.uint32))
+    nan = np.isnan(want)
+    assert np.array_equal(np.isnan(got), nan), shape
+    assert_close(np.where(nan, 0, got), np.where(nan, 0, want), shape)

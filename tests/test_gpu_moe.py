@@ -149,10 +149,13 @@ def test_moe_bias_hash_noshared(dev, orc):
         assert rel_err(out[t], want) <= 1e-5
 
 
-def test_moe_full_config2(dev, orc):
+@pytest.mark.parametrize("path", ["tensor", "stream"])
+def test_moe_full_config2(dev, orc, path):
     """BASELINE config 2 geometry: 256 FP4 experts 2048x4096 / 4096x2048, top-8,
-    FP8 shared expert, hidden 4096, route_scale 1.5, SwiGLU limit 10."""
+    FP8 shared expert, hidden 4096, route_scale 1.5, SwiGLU limit 10; both
+    decode paths."""
     fx = MoeFixture(dev, 256, 4096, 2048, shared_fmt=2, seed=42)
+    dev.moe_set_path(fx.layer, path)
     rng = np.random.default_rng(2)
     for trial in range(2):
         x = pack.bf16_round(rng.standard_normal((1, 4096)).astype(np.float32))
@@ -162,6 +165,33 @@ def test_moe_full_config2(dev, orc):
         assert np.array_equal(idx[0], widx)
         assert np.array_equal(wts[0].view(np.uint32), wwts.view(np.uint32))
         assert rel_err(out[0], want) <= 1e-5, rel_err(out[0], want)
+
+
+@pytest.mark.parametrize("shared_fmt,nt", [(2, 1), (3, 2), (0, 1), (0, 2)])
+def test_moe_stream_path_vs_oracle(dev, orc, shared_fmt, nt):
+    """The streamed decode path (forced) against the oracle, with an FP8, an
+    FP4 or no shared expert, one or two tokens; two runs agree bit for bit."""
+    fx = MoeFixture(dev, 16, 1024, 512, shared_fmt=shared_fmt, seed=20 + nt)
+    dev.moe_set_path(fx.layer, "stream")
+    rng = np.random.default_rng(30 + shared_fmt)
+    x = pack.bf16_round(rng.standard_normal((nt, 1024)).astype(np.float32))
+    logits = pack.bf16_round(rng.standard_normal((nt, 16)).astype(np.float32))
+    out, idx, wts = run(dev, fx, x, logits, 6, 1.5, 10.0)
+    again, _, _ = run(dev, fx, x, logits, 6, 1.5, 10.0)
+    assert np.array_equal(out.view(np.uint32), again.view(np.uint32))
+    for t in range(nt):
+        want, widx, wwts = fx.oracle_out(orc, x[t], logits[t], 6, 1.5, 10.0)
+        assert np.array_equal(idx[t], widx)
+        assert np.array_equal(wts[t].view(np.uint32), wwts.view(np.uint32))
+        assert rel_err(out[t], want) <= 1e-5, rel_err(out[t], want)
+    fx.close()
+
+
+def test_moe_set_path_rejects(dev):
+    fx = MoeFixture(dev, 4, 512, 256, shared_fmt=0, seed=3)
+    assert dev.L.dsv4cu_moe_set_path(fx.layer, 7) != 0
+    dev.moe_set_path(fx.layer, "auto")
+    fx.close()
 
 
 def test_router_bitexact_vs_reference_golden(dev):
