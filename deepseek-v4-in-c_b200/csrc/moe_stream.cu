@@ -137,67 +137,97 @@ __global__ void __launch_bounds__(256) smv_moe_prep_kernel(
         return;
     }
 
-    // CTA 0: routing, one warp per token (dsv4_route, dsv4_ops.c:117-156).
-    for (int t = warp; t < nt; t += nwarps)
-        route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0,
-                         n_experts, topk, route_scale, ws.idx + t * topk, ws.wts + t * topk, nullptr, nullptr);
-    __syncthreads();
-
-    // Buckets: per-expert counts, then ascending expert order; slots inside
-    // a bucket follow (t, k) order, so tokens ascend.
-    __shared__ int cnt[512 + 1];
-    __shared__ int boff[512 + 1];
+    // CTA 0: routing, one warp per token (dsv4_route, dsv4_ops.c:117-156),
+    // into shared memory.
+    constexpr int MAXP = SMV_MAXT * SMV_MOE_MAX_TOPK;
+    __shared__ int sidx[MAXP];
+    __shared__ float swts[MAXP];
+    __shared__ int cnt[512];
+    __shared__ int boff[512];
+    __shared__ int wtot[2][8];
     __shared__ int bad;
     const int npairs = nt * topk;
-    for (int e = threadIdx.x; e <= n_experts; e += blockDim.x) cnt[e] = 0;
+    for (int e = threadIdx.x; e < n_experts; e += blockDim.x) cnt[e] = 0;
     if (threadIdx.x == 0) bad = 0;
     for (int i = threadIdx.x; i < nbmax + 4; i += blockDim.x) ws.ctr[i] = 0;
+    for (int t = warp; t < nt; t += nwarps)
+        route_token_warp(tab, logits + (size_t)t * n_experts, bias, tid2eid, token_ids ? token_ids[t] : 0,
+                         n_experts, topk, route_scale, sidx + t * topk, swts + t * topk, nullptr, nullptr);
     __syncthreads();
+
+    // Buckets: per-expert counts, then one block scan over the experts
+    // (two per thread, n_experts <= 512) gives each expert its first slot and
+    // each touched expert its bucket, in ascending expert order; slots inside
+    // a bucket follow (t, k) order, so tokens ascend.
     for (int p = threadIdx.x; p < npairs; p += blockDim.x) {
-        const int e = ws.idx[p];
+        const int e = sidx[p];
+        ws.idx[p] = e;
+        ws.wts[p] = swts[p];
+        if (idx_out) {
+            idx_out[p] = e;
+            wts_out[p] = swts[p];
+        }
         if (e < 0 || e >= n_experts) atomicOr(&bad, 1);
         else atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int off = 0, nb = 0;
-        for (int e = 0; e < n_experts; e++) {
-            boff[e] = off;
-            if (cnt[e]) {
-                ws.b_expert[nb] = e;
-                ws.b_off[nb] = off;
-                nb++;
-            }
-            off += cnt[e];
+    const int e0 = 2 * threadIdx.x;
+    const int c0 = e0 < n_experts ? cnt[e0] : 0, c1 = e0 + 1 < n_experts ? cnt[e0 + 1] : 0;
+    const int sc = c0 + c1, sg = (c0 > 0) + (c1 > 0);
+    int ic = sc, ig = sg;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const int uc = __shfl_up_sync(0xFFFFFFFFu, ic, d), ug = __shfl_up_sync(0xFFFFFFFFu, ig, d);
+        if (lane >= d) {
+            ic += uc;
+            ig += ug;
         }
-        ws.b_off[nb] = off;
-        ws.b_off[nb + 1] = off + (has_shared ? nt : 0);
-        ws.meta[0] = nb;
+    }
+    if (lane == 31) {
+        wtot[0][warp] = ic;
+        wtot[1][warp] = ig;
+    }
+    __syncthreads();
+    int oc = ic - sc, og = ig - sg, tc = 0, tg = 0;
+    for (int w = 0; w < nwarps; w++) {
+        if (w < warp) {
+            oc += wtot[0][w];
+            og += wtot[1][w];
+        }
+        tc += wtot[0][w];
+        tg += wtot[1][w];
+    }
+    if (e0 < n_experts) boff[e0] = oc;
+    if (e0 + 1 < n_experts) boff[e0 + 1] = oc + c0;
+    if (c0) {
+        ws.b_expert[og] = e0;
+        ws.b_off[og] = oc;
+    }
+    if (c1) {
+        ws.b_expert[og + (c0 > 0)] = e0 + 1;
+        ws.b_off[og + (c0 > 0)] = oc + c0;
+    }
+    if (threadIdx.x == 0) {
+        ws.b_off[tg] = tc;
+        ws.b_off[tg + 1] = tc + (has_shared ? nt : 0);
+        ws.meta[0] = tg;
         ws.meta[1] = bad;
     }
     __syncthreads();
     for (int p = threadIdx.x; p < npairs; p += blockDim.x) {
-        const int e = ws.idx[p];
+        const int e = sidx[p];
         if (e < 0 || e >= n_experts) {
             ws.pos[p] = -1;
             continue;
         }
         int r = 0;
-        for (int q = 0; q < p; q++) r += (ws.idx[q] == e);
+        for (int q = 0; q < p; q++) r += (sidx[q] == e);
         const int slot = boff[e] + r;
         ws.pos[p] = slot;
         ws.b_tok[slot] = p / topk;
     }
-    __syncthreads();
-    if (has_shared) {
-        const int s0 = ws.b_off[ws.meta[0]];
-        for (int t = threadIdx.x; t < nt; t += blockDim.x) ws.b_tok[s0 + t] = t;
-    }
-    if (idx_out)
-        for (int p = threadIdx.x; p < npairs; p += blockDim.x) {
-            idx_out[p] = ws.idx[p];
-            wts_out[p] = ws.wts[p];
-        }
+    if (has_shared)
+        for (int t = threadIdx.x; t < nt; t += blockDim.x) ws.b_tok[tc + t] = t;
 }
 
 // ------------------------------------------------------------- the stream

@@ -47,13 +47,18 @@ DSV4CU_DEV void mbar_arrive(uint64_t *bar)
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// A waiting thread is suspended until the phase completes or the hint (ns)
+// runs out, so warps parked on a barrier leave the SM's issue slots to the
+// warps that work (a dependent grid's CTAs wait beside the primary's).
+constexpr uint32_t MBAR_SUSPEND_NS = 1000000u;
+
 DSV4CU_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity)
 {
     uint32_t ok;
     asm volatile("{\n\t.reg .pred p;\n\t"
-                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
                  "selp.u32 %0, 1, 0, p;\n\t}"
-                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "n"(MBAR_SUSPEND_NS) : "memory");
     return ok != 0;
 }
 
@@ -74,8 +79,7 @@ DSV4CU_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code)
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (;;) {
-        for (int i = 0; i < 64; i++)
-            if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait(bar, parity)) return true;
         if (globaltimer_ns() - t0 > MBAR_TIMEOUT_NS) break;
     }
     if (err) atomicCAS(err, 0, code);
