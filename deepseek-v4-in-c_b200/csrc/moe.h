@@ -72,8 +72,9 @@ int smv_moe_decode(const dsv4cu_moe *L, float *out, const float *x, const float 
                    const int64_t *tid2eid, const int *token_ids, int topk, float route_scale, float limit, int nt,
                    int *idx_out, float *wts_out, void *ws, int *status, int sms, cudaStream_t st, cudaEvent_t *ev);
 
-size_t moe_mx_rows_workspace(const dsv4cu_moe *L, int nrows);
-int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const int *ids, int nrows, float limit,
+size_t moe_mx_rows_workspace(const dsv4cu_moe *L, int nrows, int live_rows);
+int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const int *ids, int nrows, int live_rows,
+                float limit,
                 void *ws, int *status, int sms, cudaStream_t st);
 
 }  // namespace dsv4cu

@@ -753,7 +753,7 @@ extern "C" int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, floa
 
 extern "C" size_t dsv4cu_moe_rows_workspace(const dsv4cu_moe *L, int nrows)
 {
-    return (L && L->mx_ok && nrows > 0) ? moe_mx_rows_workspace(L, nrows) : 0;
+    return (L && L->mx_ok && nrows > 0) ? moe_mx_rows_workspace(L, nrows, nrows) : 0;
 }
 
 extern "C" int dsv4cu_moe_rows(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *y, const float *x, long ldx,
@@ -767,9 +767,10 @@ extern "C" int dsv4cu_moe_rows(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED,
                                 "moe_rows: the layer's matrices do not qualify for the tensor-core path");
     void *ws = nullptr;
-    int r = dsv4cu_ws_get(ctx, moe_mx_rows_workspace(layer, nrows), &ws);
+    int r = dsv4cu_ws_get(ctx, moe_mx_rows_workspace(layer, nrows, nrows), &ws);
     if (r) return r;
-    return moe_mx_rows(layer, y, x, ldx, ids, nrows, limit, ws, ctx->status, ctx->sm_count, (cudaStream_t)stream);
+    return moe_mx_rows(layer, y, x, ldx, ids, nrows, nrows, limit, ws, ctx->status, ctx->sm_count,
+                       (cudaStream_t)stream);
 }
 
 // Device address of a page-locked, mapped host buffer (cudaHostAlloc /

@@ -739,8 +739,10 @@ void moe_mx_release(dsv4cu_moe *L)
 
 // The four launches after the B operand of gate/up is in place: gate/up,
 // SwiGLU split, down, combine.
-// y[r] = the expert output of slot pos[r] (per-row mode of the layer, no combine).
-__global__ void __launch_bounds__(256) mxmoe_rows_out_kernel(MxMoeWs ws, int nrows, int hidden, float *__restrict__ y)
+// y[r] = the expert output of slot pos[r] (per-row mode of the layer, no combine);
+// rows whose caller id is -1 (skip) are left unwritten.
+__global__ void __launch_bounds__(256) mxmoe_rows_out_kernel(MxMoeWs ws, int nrows, int hidden, float *__restrict__ y,
+                                                             const int *__restrict__ ids)
 {
     pdl_wait();
     pdl_trigger();
@@ -748,6 +750,7 @@ __global__ void __launch_bounds__(256) mxmoe_rows_out_kernel(MxMoeWs ws, int nro
     const int h4 = hidden >> 2;
     if (i >= (long)nrows * h4) return;
     const int r = (int)(i / h4), c = (int)(i - (long)r * h4) * 4;
+    if (ids && ids[r] == -1) return;
     const int slot = ws.pos[r];
     const float4 v = slot >= 0 ? *reinterpret_cast<const float4 *>(ws.ypart + (size_t)slot * hidden + c)
                                : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -757,7 +760,8 @@ __global__ void __launch_bounds__(256) mxmoe_rows_out_kernel(MxMoeWs ws, int nro
 // rows_mode: out receives each row's expert output (the pairs are rows,
 // topk = 1) instead of the weighted combine.
 static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &ws, int terms, float limit,
-                       float *out, int *status, int sms, cudaStream_t st, cudaEvent_t *ev, bool rows_mode = false)
+                       float *out, int *status, int sms, cudaStream_t st, cudaEvent_t *ev, bool rows_mode = false,
+                       const int *row_ids = nullptr)
 {
     const int RT = s.inter / 128, RTH = s.hidden / 128, nt = s.nt, topk = s.topk;
     MxMoeCommon c;
@@ -803,7 +807,7 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     if (r) return r;
     if (rows_mode)
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_rows_out_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)),
-                                   dim3(256), 0, st, ws, nt, s.hidden, out));
+                                   dim3(256), 0, st, ws, nt, s.hidden, out, row_ids));
     else
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_combine_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)),
                                    dim3(256), 0, st, ws, nt, topk, s.hidden, s.has_shared, out));
@@ -1103,14 +1107,17 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
 // Tile width from the rows per expert: a few rows per expert (decode-like
 // batches) stream weights best through the narrow decode tiles, many rows
 // (prefill-like) through 256-column tiles.
-static MxMoeShape mxrows_shape(const dsv4cu_moe *L, int nrows)
+// live_rows: the rows expected to carry an expert (the rest skipped with id
+// -1); it picks the tile width, nrows bounds every buffer.
+static MxMoeShape mxrows_shape(const dsv4cu_moe *L, int nrows, int live_rows)
 {
     MxMoeShape s = mxpf_shape(L, 1, nrows, MX_TERMS);
     s.n_experts = L->n_experts + (L->has_shared ? 1 : 0);
     s.has_shared = 0;
     s.npairs = nrows;
     s.nbmax = min(nrows, s.n_experts);
-    const int avg = (nrows + s.nbmax - 1) / max(1, s.nbmax);
+    const int live = max(1, min(live_rows, nrows));
+    const int avg = (live + min(live, s.n_experts) - 1) / max(1, min(live, s.n_experts));
     if (avg <= 2) {
         s.NB = 8;
         s.KB = 4;
@@ -1138,21 +1145,21 @@ __global__ void __launch_bounds__(256) mxrows_ids_kernel(const int *__restrict__
     const bool ok = e >= 0 && e < n_buckets;
     ws.idx[r] = ok ? e : -1;
     ws.wts[r] = 1.0f;
-    if (!ok) atomicCAS(status, 0, MXE_BAD_EXPERT);
+    if (!ok && e != -1) atomicCAS(status, 0, MXE_BAD_EXPERT);     // -1: a skipped row
 }
 
-size_t moe_mx_rows_workspace(const dsv4cu_moe *L, int nrows)
+size_t moe_mx_rows_workspace(const dsv4cu_moe *L, int nrows, int live_rows)
 {
-    return mxpf_layout(mxrows_shape(L, nrows), nullptr, nullptr, nullptr);
+    return mxpf_layout(mxrows_shape(L, nrows, live_rows), nullptr, nullptr, nullptr);
 }
 
-int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const int *ids, int nrows, float limit,
-                void *wsp, int *status, int sms, cudaStream_t st)
+int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const int *ids, int nrows, int live_rows,
+                float limit, void *wsp, int *status, int sms, cudaStream_t st)
 {
     if (nrows > PF_MAX_NT * 2 || L->n_experts + 1 > PREP_MAX_EXPERTS)
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_rows: %d rows / %d experts beyond %d / %d", nrows,
                                 L->n_experts, PF_MAX_NT * 2, PREP_MAX_EXPERTS - 1);
-    const MxMoeShape s = mxrows_shape(L, nrows);
+    const MxMoeShape s = mxrows_shape(L, nrows, live_rows);
     MxMoeWs ws;
     PfWs pf;
     mxpf_layout(s, (char *)wsp, &ws, &pf);
@@ -1168,7 +1175,7 @@ int moe_mx_rows(const dsv4cu_moe *L, float *y, const float *x, long ldx, const i
     const long tasks = (long)s.max_tiles * s.tpt;
     DSV4CU_CUDA_TRY(launch_pdl(mxpf_split_kernel, dim3((unsigned)((tasks * 32 + 255) / 256)), dim3(256), 0, st, x,
                                s.hidden, ldx, ws, MX_TERMS, s.tpt, s.NB, tasks));
-    return mxmoe_gemms(L, s, ws, MX_TERMS, limit, y, status, sms, st, nullptr, true);
+    return mxmoe_gemms(L, s, ws, MX_TERMS, limit, y, status, sms, st, nullptr, true, ids);
 }
 
 }  // namespace dsv4cu

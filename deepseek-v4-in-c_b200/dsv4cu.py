@@ -81,6 +81,12 @@ def lib() -> C.CDLL:
             "dsv4cu_ep_pack": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, i, vp]),
             "dsv4cu_ep_tail": (i, [vp, i, vp, i, i, i, vp, vp]),
             "dsv4cu_ep_combine": (i, [vp, vp, vp, vp, vp, i, i, i, vp]),
+            "dsv4cu_ep_create": (i, [C.POINTER(vp), i, i, i, i, i, i]),
+            "dsv4cu_ep_handle": (i, [vp, vp]),
+            "dsv4cu_ep_connect": (i, [vp, vp]),
+            "dsv4cu_ep_workspace": (sz, [vp, vp, i]),
+            "dsv4cu_ep_forward": (i, [vp, vp, vp, vp, vp, vp, i, f, f, vp, vp, vp, vp]),
+            "dsv4cu_ep_destroy": (None, [vp]),
             "dsv4cu_mat_create": (i, [C.POINTER(vp), vp, vp]),
             "dsv4cu_mat_destroy": (None, [vp]),
             "dsv4cu_mat_workspace": (sz, [vp, i, i]),
@@ -406,6 +412,37 @@ class Device:
         hp = (lambda a: a.data_ptr()) if hasattr(x, "data_ptr") else (lambda a: a.ctypes.data)
         check(self.L.dsv4cu_moe_decode_host(self.ctx, layer, hp(out), hp(x), hp(logits), topk, route_scale, limit,
                                             nt, self.stream()), "dsv4cu_moe_decode_host")
+
+    EP_HANDLE_BYTES = 128
+
+    def ep_create(self, rank: int, world: int, nt_max: int, hidden: int, topk: int, experts_per_rank: int):
+        """Rank-local state of the peer-memory expert-parallel step (dsv4cu_ep_create)."""
+        h = C.c_void_p()
+        check(self.L.dsv4cu_ep_create(C.byref(h), rank, world, nt_max, hidden, topk, experts_per_rank),
+              "dsv4cu_ep_create")
+        return h
+
+    def ep_handle(self, ep) -> bytes:
+        """This rank's exported handle (dsv4cu_ep_handle), to be all-gathered."""
+        blob = (C.c_char * self.EP_HANDLE_BYTES)()
+        check(self.L.dsv4cu_ep_handle(ep, blob), "dsv4cu_ep_handle")
+        return bytes(blob)
+
+    def ep_connect(self, ep, handles: list):
+        """Map the peers' buffers from every rank's handle, in rank order (dsv4cu_ep_connect)."""
+        joined = b"".join(handles)
+        buf = (C.c_char * len(joined)).from_buffer_copy(joined)
+        check(self.L.dsv4cu_ep_connect(ep, buf), "dsv4cu_ep_connect")
+
+    def ep_forward(self, ep, layer, out, x, logits, nt, route_scale, limit, idx=None, wts=None, events=None):
+        """One expert-parallel layer step (dsv4cu_ep_forward); events: 7 torch.cuda.Event or None."""
+        evp = None if events is None else _event_handles(events)
+        check(self.L.dsv4cu_ep_forward(self.ctx, ep, layer, self.ptr(out), self.ptr(x), self.ptr(logits), nt,
+                                       route_scale, limit, self.ptr(idx), self.ptr(wts), self.stream(), evp),
+              "dsv4cu_ep_forward")
+
+    def ep_destroy(self, ep):
+        self.L.dsv4cu_ep_destroy(ep)
 
     def moe_rows(self, layer, y, x, ldx, ids, nrows, limit):
         """y[r] = expert ids[r] (n_experts = the shared expert) on row r of x (dsv4cu_moe_rows)."""

@@ -1,4 +1,13 @@
-"""Expert-parallel MoE layer: one process per GPU, torch.distributed (NCCL).
+"""Expert-parallel MoE layer: one process per GPU.
+
+PeerExpertParallel is the product path: one call of the library's
+dsv4cu_ep_forward per step, the rows crossing NVLink as peer stores inside
+the library's kernels (include/dsv4cu.h, csrc/ep_p2p.cu), nothing
+synchronised with the host. Python only all-gathers the ranks' handles once.
+
+ExpertParallelMoE below is the same layer with the exchange done by
+torch.distributed all-to-all (NCCL, or gloo in the CPU tests); it keeps the
+host-side logic testable without GPUs and serves as the NCCL comparison.
 
 The reference keeps every expert of a layer reachable from one process and
 streams them through a disk cache (src/60_cache); here the 256 experts of a
@@ -113,3 +122,50 @@ class ExpertParallelMoE:
         else:
             back = y[:nrecv]
         return ops.combine(back, pair_slot, wts, y[nrecv:], nt), idx, wts
+
+
+def torch_allgather(group=None):
+    """allgather(bytes) -> list of every rank's bytes in rank order, over torch.distributed."""
+    def gather(blob: bytes):
+        import torch.distributed as dist
+        if not dist.is_initialized() or dist.get_world_size(group) == 1:
+            return [blob]
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, blob, group=group)
+        return out
+    return gather
+
+
+class PeerExpertParallel:
+    """The layer step through dsv4cu_ep_* (peer memory over NVLink).
+
+    layer: this rank's dsv4cu_moe (experts_per_rank routed experts + the shared
+    expert). allgather: callable(bytes) -> list[bytes] in rank order, used
+    once to exchange the ranks' buffer handles. All ranks call forward in
+    lockstep."""
+
+    def __init__(self, dev, layer, rank: int, world: int, nt_max: int, hidden: int, topk: int,
+                 experts_per_rank: int, route_scale: float, limit: float, allgather):
+        import torch
+        self.torch, self.dev, self.layer = torch, dev, layer
+        self.hidden, self.topk = hidden, topk
+        self.route_scale, self.limit = route_scale, limit
+        self.ep = dev.ep_create(rank, world, nt_max, hidden, topk, experts_per_rank)
+        try:
+            dev.ep_connect(self.ep, allgather(dev.ep_handle(self.ep)))
+        except Exception:
+            dev.ep_destroy(self.ep)
+            self.ep = None
+            raise
+
+    def forward(self, x, logits, out=None, idx=None, wts=None, events=None):
+        nt = x.shape[0]
+        if out is None:
+            out = self.torch.empty((nt, self.hidden), dtype=self.torch.float32, device=x.device)
+        self.dev.ep_forward(self.ep, self.layer, out, x, logits, nt, self.route_scale, self.limit, idx, wts, events)
+        return out
+
+    def close(self):
+        if self.ep is not None:
+            self.dev.ep_destroy(self.ep)
+            self.ep = None

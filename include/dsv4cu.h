@@ -247,8 +247,9 @@ int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
  *
  * dsv4cu_moe_rows: y[r] = expert ids[r] applied to row r of x (row stride
  * ldx floats, a multiple of 4), no weighting; ids in 0 .. n_experts - 1 or
- * n_experts for the layer's shared expert. An id out of range gives a zero row
- * and the device status DSV4CU status code 26. nrows <= 32768. */
+ * n_experts for the layer's shared expert; id -1 skips the row (y[r] is not
+ * written). Any other id out of range gives a zero row and the device status
+ * code 26. nrows <= 32768. */
 size_t dsv4cu_moe_rows_workspace(const dsv4cu_moe *layer, int nrows);
 int dsv4cu_moe_rows(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *y, const float *x, long ldx,
                     const int *ids, int nrows, float limit, void *stream);
@@ -274,6 +275,44 @@ int dsv4cu_ep_tail(float *recv, int nrecv, const float *x, int nt, int hidden, i
  * float operations. */
 int dsv4cu_ep_combine(float *out, const float *back, const int *pair_slot, const float *wts,
                       const float *shared, int nt, int topk, int hidden, void *stream);
+
+/* ---- the expert-parallel layer step on device, ranks joined by NVLink peer
+ * memory (replaces dsv4_layer_moe's loop over the src/60_cache expert cache,
+ * src/70_decode/dsv4_layer.c:48-117, for experts spread over the GPUs of one
+ * box). Rank r holds routed experts [r * experts_per_rank, (r + 1) *
+ * experts_per_rank) and the shared expert as one dsv4cu_moe; every rank is the
+ * home of its own nt <= nt_max tokens.
+ *
+ * Set-up, once per rank: dsv4cu_ep_create; dsv4cu_ep_handle writes this
+ * rank's DSV4CU_EP_HANDLE_BYTES-byte handle; the caller all-gathers the
+ * handles over any transport (MPI, a TCP key-value store, NCCL) into
+ * world * DSV4CU_EP_HANDLE_BYTES bytes in rank order and passes them to
+ * dsv4cu_ep_connect, which maps the peers' buffers (CUDA IPC; the GPUs must
+ * have peer access). Handles of a different geometry are refused with
+ * DSV4CU_ERR_COMM.
+ *
+ * dsv4cu_ep_forward: route the home tokens (logits over experts_per_rank *
+ * world experts), store each (token, k) row into its owner's inbox over
+ * NVLink, run every received row through its expert and the home tokens
+ * through the shared expert on the tensor cores, store the results back,
+ * and combine in k order. All ranks call it in lockstep (same number of
+ * calls, any nt per rank). It is enqueued on the stream with nothing
+ * synchronised (graph-capturable); the cross-rank waits are bounded (2 s) and
+ * report through dsv4cu_ctx_status (codes 61 dispatch, 62 return, 63 expert
+ * id). out equals the single-device layer bit for bit. events (7 cudaEvent_t
+ * or NULL) are recorded around route+plan, dispatch, gather, the expert
+ * GEMMs, return and combine. */
+#define DSV4CU_EP_HANDLE_BYTES 128
+typedef struct dsv4cu_ep dsv4cu_ep;
+int  dsv4cu_ep_create(dsv4cu_ep **out, int rank, int world, int nt_max, int hidden, int topk,
+                      int experts_per_rank);
+int  dsv4cu_ep_handle(const dsv4cu_ep *ep, void *blob);
+int  dsv4cu_ep_connect(dsv4cu_ep *ep, const void *blobs);
+size_t dsv4cu_ep_workspace(const dsv4cu_ep *ep, const dsv4cu_moe *layer, int nt);
+int  dsv4cu_ep_forward(dsv4cu_ctx *ctx, dsv4cu_ep *ep, const dsv4cu_moe *layer, float *out,
+                       const float *x, const float *logits, int nt, float route_scale, float limit,
+                       int *idx_out, float *wts_out, void *stream, void **events);
+void dsv4cu_ep_destroy(dsv4cu_ep *ep);
 
 /* Indexer score with fp32 inputs, bit-identical to dsv4_indexer_score
  * (src/10_compute/dsv4_indexer.c:66-90): out[t] = (float)(sum_h relu(q_h.k_t)

@@ -1,6 +1,8 @@
 """Expert-parallel MoE on the GPU: the per-row expert entry (dsv4cu_moe_rows)
 against the oracle, the EP layer at world 1 against the single-device decode
-layer, and (with 2 or more GPUs) the NCCL exchange against world 1, bitwise."""
+layer, the peer-memory step (dsv4cu_ep_forward) against the NCCL-exchange
+layer bitwise, and (with 2 or more GPUs) both exchanges at world N against
+world 1, bitwise."""
 from __future__ import annotations
 
 import os
@@ -87,6 +89,47 @@ def test_ep_world1_matches_decode(dev):
     fx.close()
 
 
+def test_ep_peer_world1_matches_exchange_layer(dev):
+    """dsv4cu_ep_forward at world 1: the same bits as the all-to-all layer over
+    dsv4cu_moe_rows, over several steps (epochs), with skipped capacity rows,
+    any nt up to nt_max, and routing outputs equal to the decode layer's."""
+    t = __import__("torch")
+    from ep import ExpertParallelMoE, PeerExpertParallel
+    from test_gpu_moe import run
+    fx = MoeFixture(dev, E, H, I, shared_fmt=2, seed=45)
+    topk, nt_max = 4, 48
+    pe = PeerExpertParallel(dev, fx.layer, 0, 1, nt_max, H, topk, E, 1.5, 10.0, lambda b: [b])
+    rng = np.random.default_rng(45)
+    for step, nt in enumerate((48, 5, 1, 48, 17)):
+        x = pack.bf16_round(rng.standard_normal((nt, H)).astype(np.float32))
+        lg = pack.bf16_round(rng.standard_normal((nt, E)).astype(np.float32))
+        dx, dl = t.from_numpy(x).cuda(), t.from_numpy(lg).cuda()
+        idx = t.empty((nt, topk), dtype=t.int32, device="cuda")
+        wts = t.empty((nt, topk), dtype=t.float32, device="cuda")
+        got = pe.forward(dx, dl, idx=idx, wts=wts).cpu().numpy()
+        ref, ridx, rwts = ExpertParallelMoE(_device_ops(dev, fx.layer, E, E, 1, topk), 0, 1).forward(dx, dl)
+        dev.check_status()
+        assert np.array_equal(idx.cpu().numpy(), ridx.cpu().numpy()), step
+        assert np.array_equal(wts.cpu().numpy().view(np.uint32), rwts.cpu().numpy().view(np.uint32)), step
+        assert np.array_equal(got.view(np.uint32), ref.cpu().numpy().view(np.uint32)), step
+        outd, _, _ = run(dev, fx, x, lg, topk, 1.5, 10.0)
+        assert max(rel_err(got[i], outd[i].astype(np.float64)) for i in range(nt)) <= 1e-5
+    with pytest.raises(Exception):
+        pe.forward(t.zeros((nt_max + 1, H), device="cuda"), t.zeros((nt_max + 1, E), device="cuda"))
+    pe.close()
+    fx.close()
+
+
+def test_ep_peer_rejects_mismatched_handles(dev):
+    import dsv4cu
+    a = dev.ep_create(0, 1, 8, H, 4, E)
+    b = dev.ep_create(0, 1, 16, H, 4, E)
+    with pytest.raises(dsv4cu.DSV4CUError):
+        dev.ep_connect(a, [dev.ep_handle(b)])
+    dev.ep_destroy(a)
+    dev.ep_destroy(b)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -117,8 +160,14 @@ def _ep_rank(rank, world, port, q):
         dx, dl = torch.from_numpy(x).cuda(), torch.from_numpy(lg).cuda()
         out, _, _ = ExpertParallelMoE(_device_ops(dev, local, E, epr, world, topk), rank, world).forward(dx, dl)
         ref, _, _ = ExpertParallelMoE(_device_ops(dev, fx.layer, E, E, 1, topk), 0, 1).forward(dx, dl)
+        from ep import PeerExpertParallel, torch_allgather
+        pe = PeerExpertParallel(dev, local, rank, world, nt, H, topk, epr, 1.5, 10.0, torch_allgather())
+        peer = [pe.forward(dx, dl).cpu().numpy() for _ in range(3)]
         dev.check_status()
         ok = np.array_equal(out.cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32))
+        ok = ok and all(np.array_equal(p.view(np.uint32), ref.cpu().numpy().view(np.uint32)) for p in peer)
+        dist.barrier()
+        pe.close()
         dist.barrier()
         dist.destroy_process_group()
         dev.moe_destroy(local)
@@ -129,7 +178,7 @@ def _ep_rank(rank, world, port, q):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_ep_nccl_matches_world1(world):
+def test_ep_nccl_and_peer_match_world1(world):
     t = __import__("torch")
     if t.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
