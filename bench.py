@@ -1470,11 +1470,14 @@ def run_ep(args, rank, local_rank, world):
     del keep
     if not bit_all:
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            res["error"] = "expert-parallel output differs from the single-device layer"
+            sys.stdout.flush()
+            os.write(JSON_FD[0], (json.dumps(res) + "\n").encode())
         sys.exit(1)
     return res if rank == 0 else None
 
 
+JSON_FD = [1]        # where the JSON line goes (main() moves other stdout to stderr)
 SECONDARY = (("config1", "gemv"), ("config3", "prefill"), ("config4", "indexer"))
 
 
@@ -1500,6 +1503,12 @@ def secondary_block(args, rank, local_rank, world):
 def main():
     args = parse()
     rank, local_rank, world = dist_env()
+    # stdout carries the one JSON line only: what libraries print there (NCCL
+    # announces its version on rank 0) goes to stderr.
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    JSON_FD[0] = json_fd
+    os.dup2(2, 1)
     wl = args.workload
     if wl == "auto":
         wl = "decode" if world == 1 else "ep"
@@ -1522,7 +1531,8 @@ def main():
         if args.workload == "auto" and world == 1 and res is not None:
             res["secondary"] = secondary_block(args, rank, local_rank, world)
     if res is not None and rank == 0:
-        print(json.dumps(res), flush=True)
+        sys.stdout.flush()
+        os.write(json_fd, (json.dumps(res) + "\n").encode())
 
 
 if __name__ == "__main__":

@@ -8,8 +8,8 @@
 // and every rank is the home of its own tokens. One call, all on the stream,
 // nothing synchronised with the host (the step can be captured in a graph):
 //
-//   plan      (1 CTA)  route the home tokens (route_token_warp = dsv4_route),
-//                      give every (token t, slot k) pair its owner d = e / epr
+//   route     (grid)   one warp per home token (route_token_warp = dsv4_route).
+//   plan      (1 CTA)  give every (token t, slot k) pair its owner d = e / epr
 //                      and a row pos in the owner's inbox slab for this rank,
 //                      in pair order (warp match + per-warp count scan).
 //   dispatch  (grid)   each pair's x[t] row is stored straight into the
@@ -96,6 +96,7 @@ struct EppLocal {
     int *idx;             // [cap]: routed expert of each pair
     float *wts;           // [cap]
     int *send_count;      // [world]
+    int *recv_count;      // [world]: rows received from each source this step
     int *ids;             // [(world + 1) * cap]
     float *y;             // [(world + 1) * cap][hidden]
 };
@@ -129,30 +130,38 @@ DSV4CU_DEV bool epp_wait_flag(const unsigned *flag, unsigned epoch)
     }
 }
 
-// ------------------------------------------------------------------ plan
-__global__ void __launch_bounds__(EPP_MAX_PAIRS) epp_plan_kernel(const float *__restrict__ tab, const float *__restrict__ logits,
-                                                        int nt, int n_total, float route_scale, EppShape sh,
-                                                        EppLocal loc, int *status, int *__restrict__ idx_out,
-                                                        float *__restrict__ wts_out)
+// ----------------------------------------------------------------- route
+__global__ void __launch_bounds__(256) epp_route_kernel(const float *__restrict__ tab, const float *__restrict__ logits,
+                                                        int nt, int n_total, int topk, float route_scale, EppLocal loc)
 {
-    __shared__ int s_idx[EPP_MAX_PAIRS];
-    __shared__ float s_wts[EPP_MAX_PAIRS];
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= nt) return;
+    route_token_warp(tab, logits + (size_t)t * n_total, nullptr, nullptr, 0, n_total, topk, route_scale,
+                     loc.idx + t * topk, loc.wts + t * topk, nullptr, nullptr);
+}
+
+// ------------------------------------------------------------------ plan
+__global__ void __launch_bounds__(EPP_MAX_PAIRS) epp_plan_kernel(int nt, EppShape sh, EppLocal loc, int *status,
+                                                                 int *__restrict__ idx_out,
+                                                                 float *__restrict__ wts_out)
+{
     constexpr int NW = EPP_MAX_PAIRS / 32;
     __shared__ int s_wc[NW][EPP_MAX_RANKS];
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int topk = sh.topk, npairs = nt * topk;
+    const int npairs = nt * sh.topk;
     if (tid == 0) loc.epoch[0] = loc.epoch[0] + 1u;
     for (int i = tid; i < NW * EPP_MAX_RANKS; i += blockDim.x) (&s_wc[0][0])[i] = 0;
-    for (int t = warp; t < nt; t += NW)
-        route_token_warp(tab, logits + (size_t)t * n_total, nullptr, nullptr, 0, n_total, topk, route_scale,
-                         s_idx + t * topk, s_wts + t * topk, nullptr, nullptr);
     __syncthreads();
     const int p = tid;
     int e = -1, d = -2;
     if (p < npairs) {
-        e = s_idx[p];
+        e = loc.idx[p];
         d = (e >= 0 && e < sh.epr * sh.world) ? e / sh.epr : -1;
         if (d < 0) atomicCAS(status, 0, EPP_E_EXPERT);
+        if (idx_out) {
+            idx_out[p] = e;
+            wts_out[p] = loc.wts[p];
+        }
     }
     // Rows of one owner keep the pair order: rank inside the warp, then the
     // owner's count over the lower warps.
@@ -172,23 +181,7 @@ __global__ void __launch_bounds__(EPP_MAX_PAIRS) epp_plan_kernel(const float *__
         loc.send_count[tid] = run;
     }
     __syncthreads();
-    if (p < npairs) {
-        loc.pair_slot[p] = d >= 0 ? d * sh.cap + s_wc[warp][d] + wrank : -1;
-        loc.idx[p] = e;
-        loc.wts[p] = s_wts[p];
-        if (idx_out) {
-            idx_out[p] = e;
-            wts_out[p] = s_wts[p];
-        }
-    }
-}
-
-// Warp w of the grid copies rows w, w + nwarps, ... (hidden floats each).
-DSV4CU_DEV void epp_copy_row(float *__restrict__ dst, const float *__restrict__ src, int h4, int lane)
-{
-    const float4 *s4 = reinterpret_cast<const float4 *>(src);
-    float4 *d4 = reinterpret_cast<float4 *>(dst);
-    for (int c = lane; c < h4; c += 32) d4[c] = s4[c];
+    if (p < npairs) loc.pair_slot[p] = d >= 0 ? d * sh.cap + s_wc[warp][d] + wrank : -1;
 }
 
 // Last CTA of the grid to finish (after every CTA's system fence) returns true.
@@ -204,30 +197,57 @@ DSV4CU_DEV bool epp_last_cta(int *ticket)
     return last;
 }
 
+// Row copies spread over every thread of the grid, 16 bytes an item and
+// EPP_UNROLL independent loads in flight per thread before the stores.
+constexpr int EPP_UNROLL = 4;
+
 // -------------------------------------------------------------- dispatch
+// Rows 0 .. npairs - 1: pair r's x[t] to its owner's inbox; rows npairs ..
+// + nt - 1: the home tokens to the local shared-expert slab.
+DSV4CU_DEV float4 *epp_dispatch_dst(const EppShape &sh, const EppLocal &loc, const EppPeers &peers, int npairs, int r,
+                                    const float *x, const float4 **src)
+{
+    const size_t row_b = (size_t)(sh.hidden + 4) * 4;
+    if (r < npairs) {
+        const int slot = loc.pair_slot[r];
+        if (slot < 0) return nullptr;
+        const int d = slot / sh.cap, pos = slot - d * sh.cap;
+        *src = reinterpret_cast<const float4 *>(x + (size_t)(r / sh.topk) * sh.hidden);
+        return reinterpret_cast<float4 *>(peers.box[d] + sh.lay.inbox + ((size_t)sh.rank * sh.cap + pos) * row_b);
+    }
+    const int t = r - npairs;
+    *src = reinterpret_cast<const float4 *>(x + (size_t)t * sh.hidden);
+    return reinterpret_cast<float4 *>(peers.box[sh.rank] + sh.lay.inbox + ((size_t)sh.world * sh.cap + t) * row_b);
+}
+
 __global__ void __launch_bounds__(256) epp_dispatch_kernel(const float *__restrict__ x, int nt, EppShape sh,
                                                            EppLocal loc, EppPeers peers)
 {
-    const int lane = threadIdx.x & 31;
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
     const int npairs = nt * sh.topk, h4 = sh.hidden >> 2;
-    const size_t row_b = (size_t)(sh.hidden + 4) * 4;
-    for (int r = gw; r < npairs + nt; r += nw) {
-        if (r < npairs) {
-            const int slot = loc.pair_slot[r];
-            if (slot < 0) continue;
-            const int d = slot / sh.cap, pos = slot - d * sh.cap;
-            char *box = peers.box[d];
-            float *dst = reinterpret_cast<float *>(box + sh.lay.inbox + ((size_t)sh.rank * sh.cap + pos) * row_b);
-            epp_copy_row(dst, x + (size_t)(r / sh.topk) * sh.hidden, h4, lane);
-            if (lane == 0)
-                reinterpret_cast<int *>(box + sh.lay.meta)[(size_t)sh.rank * sh.cap + pos] = loc.idx[r] % sh.epr;
-        } else {
-            const int t = r - npairs;
-            float *dst = reinterpret_cast<float *>(peers.box[sh.rank] + sh.lay.inbox +
-                                                   ((size_t)sh.world * sh.cap + t) * row_b);
-            epp_copy_row(dst, x + (size_t)t * sh.hidden, h4, lane);
+    const long items = (long)(npairs + nt) * h4, stride = (long)gridDim.x * blockDim.x;
+    for (long i0 = blockIdx.x * (long)blockDim.x + threadIdx.x; i0 < items; i0 += stride * EPP_UNROLL) {
+        float4 v[EPP_UNROLL];
+        float4 *dst[EPP_UNROLL];
+#pragma unroll
+        for (int u = 0; u < EPP_UNROLL; u++) {
+            const long i = i0 + u * stride;
+            dst[u] = nullptr;
+            if (i >= items) continue;
+            const int r = (int)(i / h4), c = (int)(i - (long)r * h4);
+            const float4 *src;
+            float4 *d = epp_dispatch_dst(sh, loc, peers, npairs, r, x, &src);
+            if (!d) continue;
+            v[u] = src[c];
+            dst[u] = d + c;
+            if (c == 0 && r < npairs) {
+                const int slot = loc.pair_slot[r], o = slot / sh.cap;
+                reinterpret_cast<int *>(peers.box[o] + sh.lay.meta)[(size_t)sh.rank * sh.cap + slot - o * sh.cap] =
+                    loc.idx[r] % sh.epr;
+            }
         }
+#pragma unroll
+        for (int u = 0; u < EPP_UNROLL; u++)
+            if (dst[u]) *dst[u] = v[u];
     }
     if (epp_last_cta(loc.done) && threadIdx.x == 0) {
         const unsigned epoch = loc.epoch[0];
@@ -251,6 +271,7 @@ __global__ void __launch_bounds__(1024) epp_gather_kernel(int nt, EppShape sh, E
         if (!ok) atomicCAS(status, 0, EPP_E_DISPATCH);
         const int n = reinterpret_cast<const volatile int *>(box + sh.lay.dcount)[tid];
         s_n[tid] = ok ? min(max(n, 0), sh.cap) : 0;
+        loc.recv_count[tid] = s_n[tid];
     }
     __syncthreads();
     const int *meta = reinterpret_cast<const int *>(box + sh.lay.meta);
@@ -273,16 +294,41 @@ __global__ void __launch_bounds__(1024) epp_gather_kernel(int nt, EppShape sh, E
 }
 
 // ---------------------------------------------------------------- return
+// The received rows are the first recv_count[s] rows of each source slab s:
+// item j walks them in order (a prefix over the <= 16 sources finds the slab).
 __global__ void __launch_bounds__(256) epp_return_kernel(EppShape sh, EppLocal loc, EppPeers peers)
 {
-    const int lane = threadIdx.x & 31;
-    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, nw = (gridDim.x * blockDim.x) >> 5;
+    __shared__ int s_pre[EPP_MAX_RANKS + 1];
+    if (threadIdx.x == 0) {
+        int run = 0;
+        for (int q = 0; q < sh.world; q++) {
+            s_pre[q] = run;
+            run += loc.recv_count[q];
+        }
+        s_pre[sh.world] = run;
+    }
+    __syncthreads();
     const int h4 = sh.hidden >> 2;
-    for (int r = gw; r < sh.world * sh.cap; r += nw) {
-        if (loc.ids[r] < 0) continue;
-        const int s = r / sh.cap, i = r - s * sh.cap;
-        float *dst = reinterpret_cast<float *>(peers.box[s] + sh.lay.outbox) + ((size_t)sh.rank * sh.cap + i) * sh.hidden;
-        epp_copy_row(dst, loc.y + (size_t)r * sh.hidden, h4, lane);
+    const long items = (long)s_pre[sh.world] * h4, stride = (long)gridDim.x * blockDim.x;
+    for (long i0 = blockIdx.x * (long)blockDim.x + threadIdx.x; i0 < items; i0 += stride * EPP_UNROLL) {
+        float4 v[EPP_UNROLL];
+        float4 *dst[EPP_UNROLL];
+#pragma unroll
+        for (int u = 0; u < EPP_UNROLL; u++) {
+            const long i = i0 + u * stride;
+            dst[u] = nullptr;
+            if (i >= items) continue;
+            const int j = (int)(i / h4), c = (int)(i - (long)j * h4);
+            int q = 0;
+            while (q + 1 < sh.world && j >= s_pre[q + 1]) q++;
+            const int row = j - s_pre[q];
+            v[u] = reinterpret_cast<const float4 *>(loc.y + ((size_t)q * sh.cap + row) * sh.hidden)[c];
+            dst[u] = reinterpret_cast<float4 *>(peers.box[q] + sh.lay.outbox) +
+                     ((size_t)sh.rank * sh.cap + row) * h4 + c;
+        }
+#pragma unroll
+        for (int u = 0; u < EPP_UNROLL; u++)
+            if (dst[u]) *dst[u] = v[u];
     }
     if (epp_last_cta(loc.done + 1) && threadIdx.x == 0) {
         const unsigned epoch = loc.epoch[0];
@@ -395,7 +441,7 @@ extern "C" int dsv4cu_ep_create(dsv4cu_ep **out, int rank, int world, int nt_max
         return o;
     };
     const size_t o_epoch = take(64), o_pair = take((size_t)cap * 4), o_idx = take((size_t)cap * 4),
-                 o_wts = take((size_t)cap * 4), o_cnt = take((size_t)world * 4), o_ids = take((size_t)rows * 4),
+                 o_wts = take((size_t)cap * 4), o_cnt = take((size_t)world * 8), o_ids = take((size_t)rows * 4),
                  o_y = take((size_t)rows * hidden * 4);
     if (cudaMalloc(&ep->local_block, off) != cudaSuccess) return fail(DSV4CU_ERR_NOMEM, "local state");
     char *b = (char *)ep->local_block;
@@ -406,6 +452,7 @@ extern "C" int dsv4cu_ep_create(dsv4cu_ep **out, int rank, int world, int nt_max
     ep->loc.idx = (int *)(b + o_idx);
     ep->loc.wts = (float *)(b + o_wts);
     ep->loc.send_count = (int *)(b + o_cnt);
+    ep->loc.recv_count = (int *)(b + o_cnt) + world;
     ep->loc.ids = (int *)(b + o_ids);
     ep->loc.y = (float *)(b + o_y);
     for (int r = 0; r < EPP_MAX_RANKS; r++) ep->peers.box[r] = nullptr;
@@ -509,8 +556,10 @@ extern "C" int dsv4cu_ep_forward(dsv4cu_ctx *ctx, dsv4cu_ep *ep, const dsv4cu_mo
     if (r) return r;
     const int grid = ctx->sm_count * 2;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
-    epp_plan_kernel<<<1, EPP_MAX_PAIRS, 0, st>>>(tab, logits, nt, ep->epr * ep->world, route_scale, sh, ep->loc, ctx->status,
-                                        idx_out, wts_out);
+    epp_route_kernel<<<(nt + 7) / 8, 256, 0, st>>>(tab, logits, nt, ep->epr * ep->world, ep->topk, route_scale,
+                                                   ep->loc);
+    DSV4CU_LAUNCH_CHECK();
+    epp_plan_kernel<<<1, EPP_MAX_PAIRS, 0, st>>>(nt, sh, ep->loc, ctx->status, idx_out, wts_out);
     DSV4CU_LAUNCH_CHECK();
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
     epp_dispatch_kernel<<<grid, 256, 0, st>>>(x, nt, sh, ep->loc, ep->peers);
