@@ -107,23 +107,39 @@ struct DeviceScope {
     }
 };
 
+// Content check of a mirrored host buffer. Sampled (the default): the first
+// and last 64 bytes and the first 8-byte word of every 4 KiB page, so any two
+// different experts (which differ almost everywhere) are told apart, but a
+// rewrite confined to unsampled bytes is not seen - such a caller must call
+// dsv4cu_host_forget, or switch to full checking (dsv4cu_host_verify(1):
+// every word hashed on every call, exact but a pass over the weights per call).
+static int g_verify_full = 0;
+
 uint64_t fingerprint(const void *p, size_t bytes)
 {
-    // FNV-1a over the size and 32 evenly spaced 8-byte samples (or all bytes
-    // of a small buffer). Detects a refilled cache slot at the same address.
     const unsigned char *b = (const unsigned char *)p;
-    uint64_t h = 1469598103934665603ull ^ (uint64_t)bytes;
-    auto mix = [&](const unsigned char *q, size_t n) {
-        for (size_t i = 0; i < n; i++) h = (h ^ q[i]) * 1099511628211ull;
+    uint64_t h = 0x9E3779B97F4A7C15ull ^ (uint64_t)bytes ^ (g_verify_full ? 1ull : 0ull);
+    auto mix = [&](uint64_t w) {
+        h ^= w;
+        h *= 0xFF51AFD7ED558CCDull;
+        h ^= h >> 32;
     };
-    if (bytes <= 256) {
-        mix(b, bytes);
+    auto word = [&](size_t off) {
+        uint64_t w;
+        memcpy(&w, b + off, 8);
+        mix(w);
+    };
+    if (g_verify_full || bytes <= 256) {
+        size_t i = 0;
+        for (; i + 8 <= bytes; i += 8) word(i);
+        for (; i < bytes; i++) mix(b[i]);
         return h;
     }
-    for (int i = 0; i < 32; i++) {
-        size_t off = (bytes - 8) * (size_t)i / 31;
-        mix(b + off, 8);
+    for (size_t i = 0; i < 64; i += 8) {
+        word(i);
+        word(bytes - 64 + i);
     }
+    for (size_t pg = 4096; pg + 8 <= bytes; pg += 4096) word(pg);
     return h;
 }
 
@@ -676,6 +692,12 @@ extern "C" void dsv4cu_host_forget(const void *host_ptr)
     std::lock_guard<std::recursive_mutex> lk(s.mu);
     auto it = s.reg.find((uintptr_t)host_ptr);
     if (it != s.reg.end()) reg_drop(it);
+}
+
+extern "C" void dsv4cu_host_verify(int full)
+{
+    std::lock_guard<std::recursive_mutex> lk(S().mu);
+    g_verify_full = full ? 1 : 0;
 }
 
 extern "C" void dsv4cu_host_forget_all(void)

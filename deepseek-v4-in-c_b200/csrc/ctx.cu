@@ -97,12 +97,23 @@ extern "C" size_t dsv4cu_ctx_workspace_bytes(const dsv4cu_ctx *c)
     return c ? c->ws_bytes : 0;
 }
 
+extern "C" int dsv4cu_ctx_inject(dsv4cu_ctx *c, int what)
+{
+    if (!c) return dsv4cu_set_error(DSV4CU_ERR_ARG, "ctx_inject: NULL context");
+    if (what != 0 && what != DSV4CU_INJECT_WITHHOLD_STAGE)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "ctx_inject: unknown fault %d", what);
+    c->inject = what;
+    return DSV4CU_OK;
+}
+
 extern "C" int dsv4cu_ctx_status(dsv4cu_ctx *c, void *stream, int *code)
 {
     if (!c || !code) return dsv4cu_set_error(DSV4CU_ERR_ARG, "ctx_status: NULL argument");
     DSV4CU_CUDA_TRY(cudaStreamSynchronize((cudaStream_t)stream));
     DSV4CU_CUDA_TRY(cudaMemcpy(code, c->status, sizeof(int), cudaMemcpyDeviceToHost));
     if (*code) {
+        // A kernel that gave up may have left its last-arriver counts behind.
+        DSV4CU_CUDA_TRY(cudaMemset(c->counters, 0, DSV4CU_MAX_COUNTERS * sizeof(int)));
         DSV4CU_CUDA_TRY(cudaMemset(c->status, 0, sizeof(int)));
         return dsv4cu_set_error(DSV4CU_ERR_TIMEOUT, "a bounded device wait timed out (code 0x%x)", *code);
     }

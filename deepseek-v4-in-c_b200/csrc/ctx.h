@@ -15,6 +15,7 @@ struct dsv4cu_ctx {
     size_t ws_bytes;
     int   *counters;    // [DSV4CU_MAX_COUNTERS], zero between calls
     int   *status;      // device word: first bounded-wait timeout code, 0 = none
+    int    inject;      // one-shot test fault for the next dsv4cu_gemv (DSV4CU_INJECT_*), 0 = none
 };
 
 // Returns a workspace of at least `bytes` (grows the buffer if needed).

@@ -39,6 +39,7 @@ struct SmvDenseParams {
     int nt, K, nseg, maxparts;
     long long stages;          // (rows / 32) * nseg
     int *status;
+    int withhold;              // test fault: CTA 0 skips its stage 2 (dsv4cu_ctx_inject), 0 = none
 };
 
 // CTA whose range holds stage q (ranges [S c / G, S (c + 1) / G)).
@@ -89,7 +90,8 @@ DSV4CU_DEV void smv_dense_producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm
             pend = false;
         }
         ok = smv_slot_free(sm, slot, ph, p.status);
-        if (ok) smv_put_stage(ring, sm, dr, slot, ph, d, m, r * SMV_ROWS, sg);
+        const bool skip = p.withhold && blockIdx.x == 0 && q - b0 == 2;
+        if (ok && !skip) smv_put_stage(ring, sm, dr, slot, ph, d, m, r * SMV_ROWS, sg);
         if (++slot == p.geom.ns) {
             slot = 0;
             ph ^= 1u;
@@ -288,6 +290,8 @@ extern "C" int dsv4cu_gemv_ev(dsv4cu_ctx *ctx, float *y, const float *x, const d
     p.maxparts = s.maxparts;
     p.stages = s.stages;
     p.status = ctx->status;
+    p.withhold = ctx->inject == DSV4CU_INJECT_WITHHOLD_STAGE;
+    ctx->inject = 0;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
     {
         const long warps = (long)nt * (s.K / 32);

@@ -59,6 +59,7 @@ def lib() -> C.CDLL:
             "dsv4cu_ctx_reserve": (i, [vp, sz]),
             "dsv4cu_ctx_workspace_bytes": (sz, [vp]),
             "dsv4cu_ctx_status": (i, [vp, vp, C.POINTER(i)]),
+            "dsv4cu_ctx_inject": (i, [vp, i]),
             "dsv4cu_mmq_workspace": (sz, [vp, i]),
             "dsv4cu_mmq": (i, [vp, vp, vp, vp, i, vp]),
             "dsv4cu_gemv_workspace": (sz, [vp, i]),
@@ -134,6 +135,7 @@ def lib() -> C.CDLL:
             "dsv4_prefill_vk_expert_fused": (i, [vp, vp, vp, vp, vp, vp, i, i, f, vp, vp]),
             "dsv4cu_host_forget": (None, [vp]),
             "dsv4cu_host_forget_all": (None, []),
+            "dsv4cu_host_verify": (None, [i]),
             "dsv4cu_host_registry_count": (sz, []),
             "dsv4cu_host_registry_bytes": (sz, []),
         }
@@ -276,6 +278,13 @@ class HostAPI:
     def forget_all(self):
         self.L.dsv4cu_host_forget_all()
 
+    def forget(self, host_ptr: int):
+        self.L.dsv4cu_host_forget(host_ptr)
+
+    def verify(self, full: bool):
+        """Exact (every byte per call) or sampled content check of mirrored weights."""
+        self.L.dsv4cu_host_verify(1 if full else 0)
+
 
 # ---------------------------------------------------------------- device ABI
 class Device:
@@ -298,6 +307,18 @@ class Device:
 
     def stream(self):
         return self.torch.cuda.current_stream(self.device).cuda_stream
+
+    INJECT_WITHHOLD_STAGE = 1
+
+    def inject(self, what: int):
+        """Arm a test-only fault for the next dsv4cu_gemv (dsv4cu_ctx_inject)."""
+        check(self.L.dsv4cu_ctx_inject(self.ctx, what), "dsv4cu_ctx_inject")
+
+    def status_code(self) -> int:
+        """Synchronise and return (and clear) the context's device status word."""
+        code = C.c_int(0)
+        self.L.dsv4cu_ctx_status(self.ctx, self.stream(), C.byref(code))
+        return code.value
 
     def check_status(self):
         """Raise if a kernel of this context hit a bounded-wait timeout."""

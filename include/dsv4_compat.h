@@ -8,9 +8,12 @@
  * from the GPU itself:
  *
  *   - Weights (DSV4QMat.w / .s) are uploaded once per host buffer and kept in
- *     HBM, keyed by host address, byte size and a sampled content fingerprint,
- *     so a cache slot that is refilled with another expert is re-uploaded.
- *     dsv4cu_host_forget() drops one entry, dsv4cu_host_forget_all() all.
+ *     HBM, keyed by host address, byte size and a sampled content fingerprint
+ *     (both ends and one word per 4 KiB page), so a cache slot that is
+ *     refilled with another expert is re-uploaded. The check is sampled: a
+ *     rewrite confined to unsampled bytes is NOT seen unless the caller calls
+ *     dsv4cu_host_forget() (one entry) / dsv4cu_host_forget_all(), or turns on
+ *     exact checking with dsv4cu_host_verify(1) (every byte hashed per call).
  *   - Activations and results are copied per call.
  *
  * Error behaviour mirrors the reference: an unknown weight format prints the
@@ -104,6 +107,9 @@ int  dsv4_prefill_vk_expert_fused(DSV4PrefillVk *v, float *y, const float *x,
 /* Drop the HBM copy kept for a host weight buffer / for all of them. */
 void dsv4cu_host_forget(const void *host_ptr);
 void dsv4cu_host_forget_all(void);
+/* 0 (default): sampled content check of mirrored weights; 1: every byte of a
+ * mirrored buffer hashed on every call (exact; one pass over the weights). */
+void dsv4cu_host_verify(int full);
 /* Number of weight buffers currently mirrored in HBM, and their bytes. */
 size_t dsv4cu_host_registry_count(void);
 size_t dsv4cu_host_registry_bytes(void);

@@ -72,9 +72,18 @@ void dsv4cu_ctx_destroy(dsv4cu_ctx *ctx);
 int  dsv4cu_ctx_reserve(dsv4cu_ctx *ctx, size_t bytes);
 size_t dsv4cu_ctx_workspace_bytes(const dsv4cu_ctx *ctx);
 /* Synchronise `stream` and report whether any kernel of this context hit a
- * bounded-wait timeout since the last check (*code = 0: none; the call then
- * returns DSV4CU_ERR_TIMEOUT and clears the word). */
+ * bounded-wait timeout since the last check (*code = 0: none; otherwise the
+ * call returns DSV4CU_ERR_TIMEOUT, clears the word and resets the context's
+ * cross-CTA counters, so the next call runs normally). */
 int  dsv4cu_ctx_status(dsv4cu_ctx *ctx, void *stream, int *code);
+/* Test-only fault, consumed by the next dsv4cu_gemv call on the streamed
+ * path: WITHHOLD_STAGE makes its first CTA skip its third weight stage (no
+ * copy is issued and nothing arrives on the stage's barrier), so that CTA's
+ * consumers' bounded wait expires after 2 s; every role then stops through
+ * bounded waits, the call's output is undefined and dsv4cu_ctx_status reports
+ * the timeout. 0 cancels. Nothing faults and the context stays usable. */
+#define DSV4CU_INJECT_WITHHOLD_STAGE 1
+int  dsv4cu_ctx_inject(dsv4cu_ctx *ctx, int what);
 
 /* Workspace bytes a dsv4cu_mmq call of this shape needs. */
 size_t dsv4cu_mmq_workspace(const dsv4cu_qmat *m, int nt);

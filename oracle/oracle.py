@@ -23,7 +23,9 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libdsv4ref.so")
-REF_TREE = os.environ.get("DSV4_REFERENCE_TREE", "/root/reference")
+# The reference source tree: set by the caller (DSV4_REFERENCE_TREE or build(ref_tree=...));
+# without it only the restatement is built.
+REF_TREE = os.environ.get("DSV4_REFERENCE_TREE")
 
 WF32, WBF16, WFP8, WFP4 = 0, 1, 2, 3
 
@@ -35,17 +37,17 @@ class QMat(C.Structure):
                 ("blk_r", C.c_int), ("blk_c", C.c_int)]
 
 
-def build(with_ref: bool | None = None) -> None:
-    """Compile the restatement (always) and the reference library (when the
-    reference tree is present). Builds the checkers; does not run them."""
+def build(ref_tree: str | None = None) -> None:
+    """Compile the restatement (always) and, given the reference source tree
+    (ref_tree or DSV4_REFERENCE_TREE), the reference library and its unit
+    tests. Builds the checkers; does not run them."""
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
-    if with_ref is None:
-        with_ref = os.path.isdir(os.path.join(REF_TREE, "src", "10_compute"))
-    if with_ref:
-        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={REF_TREE}"], check=True)
+    tree = ref_tree or REF_TREE
+    if tree and os.path.isdir(os.path.join(tree, "src", "10_compute")):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={tree}"], check=True)
         # the reference's own unit tests linked against the CUDA library (run only by the GPU tests)
         if os.path.exists(os.path.join(HERE, "..", "deepseek-v4-in-c_b200", "libdsv4cu.so")):
-            subprocess.run(["make", "-s", "-C", HERE, "units", f"REF={REF_TREE}"], check=True)
+            subprocess.run(["make", "-s", "-C", HERE, "units", f"REF={tree}"], check=True)
 
 
 def _p(a):

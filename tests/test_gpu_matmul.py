@@ -381,3 +381,45 @@ def test_gemv_stream_vs_oracle(dev, orc, shape):
     nan = np.isnan(want)
     assert np.array_equal(np.isnan(got), nan), shape
     assert_close(np.where(nan, 0, got), np.where(nan, 0, want), shape)
+
+
+def test_registry_refill_in_unsampled_bytes(host):
+    """The host-pointer registry's content check. A refill confined to bytes
+    the sampled fingerprint skips keeps the old HBM mirror (the documented
+    limit); dsv4cu_host_forget or exact checking (dsv4cu_host_verify(1)) make
+    the new bytes count. A refill that touches a sampled word is re-uploaded."""
+    import dsv4cu
+    rng = np.random.default_rng(11)
+    rows, cols = 64, 1024                    # 64 KiB of e4m3: 16 pages
+    W, S = make_weights(rng, 2, rows, cols, 128, 128)
+    x = pack.bf16_round(rng.standard_normal((1, cols)).astype(np.float32))
+    m = dsv4cu.QMat(W.ctypes.data, S.ctypes.data, 2, rows, cols, 128, 128)
+    y0 = host.mmq(x, m)
+
+    def bump(off):
+        r, c = divmod(off, cols)
+        W[r, c] = W[r, c] ^ 0x01 if (W[r, c] ^ 0x01) & 0x7F != 0x7F else W[r, c] ^ 0x02
+        return r
+
+    r1 = bump(2 * 4096 + 100)                # inside page 2, not a sampled word
+    assert np.array_equal(host.mmq(x, m), y0)             # stale mirror: the documented limit
+    host.forget(W.ctypes.data)
+    y1 = host.mmq(x, m)
+    assert y1[0, r1] != y0[0, r1]
+    assert_close(y1, orc_mmq(W, S, x))
+    host.verify(True)
+    try:
+        r2 = bump(5 * 4096 + 300)
+        y2 = host.mmq(x, m)
+        assert y2[0, r2] != y1[0, r2]
+        assert_close(y2, orc_mmq(W, S, x))
+    finally:
+        host.verify(False)
+    r3 = bump(7 * 4096)                      # a sampled word: seen without help
+    y3 = host.mmq(x, m)
+    assert y3[0, r3] != y2[0, r3]
+    assert_close(y3, orc_mmq(W, S, x))
+
+
+def orc_mmq(W, S, x):
+    return oracle.Oracle().mmq(x, oracle.qmat(W, S, 2, W.shape[0], W.shape[1], 128, 128))
