@@ -40,8 +40,11 @@ int attn_run(float *o, const float *q, const void *kv, int kv_bf16, const float 
 
 static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[DSV4CU_ATTN_NOALLOC_BYTES];
 
-// Device address of g_attn_noalloc_scratch on `device`, looked up once per
-// device with that device current.
+// Device address of g_attn_noalloc_scratch on `device`, looked up on every
+// call (cheap once the module is loaded) so that a module reloaded after a
+// device reset or a new primary context is followed. The last address found
+// is kept only for a lookup that fails (e.g. one the runtime refuses during a
+// stream capture); then the device must not have been reset since.
 static int attn_noalloc_scratch(int device, void **out)
 {
     static std::mutex mu;
@@ -49,13 +52,15 @@ static int attn_noalloc_scratch(int device, void **out)
     if (device < 0 || device >= DSV4CU_NOALLOC_MAX_DEVICES)
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "sparse_attn_noalloc: device %d out of range", device);
     std::lock_guard<std::mutex> lk(mu);
-    if (!addr[device]) {
-        void *p = nullptr;
-        cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
-        if (e != cudaSuccess)
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e == cudaSuccess) {
+        addr[device] = p;
+    } else {
+        cudaGetLastError();
+        if (!addr[device])
             return dsv4cu_set_error(DSV4CU_ERR_CUDA, "sparse_attn_noalloc: cudaGetSymbolAddress: %s",
                                     cudaGetErrorString(e));
-        addr[device] = p;
     }
     *out = addr[device];
     return DSV4CU_OK;

@@ -161,15 +161,20 @@ def test_compress_steps_vs_oracle(dev, orc, ratio):
     """dsv4cu_compress_step over several windows against the oracle's
     dsv4_compress_step (pinned live to the reference): the emit contract and the
     ring states bit for bit, the pooled rows within 1e-6 (expf) and counted
-    bit-identical."""
+    bit-identical. The score ring starts at -inf as the reference requires, so
+    the first windows pool over unfilled slots; in the second window every
+    score is -inf, so with no overlap (ratio 8, 128) its emitted row is 0."""
     import torch
     rng = np.random.default_rng(ratio + 1)
     d = 128
     coff = 2 if ratio == 4 else 1
     width = coff * d
     ape = rng.standard_normal((ratio, width)).astype(np.float32)
-    ks, ss = (np.zeros((coff * ratio, width), np.float32) for _ in range(2))
-    dks, dss = (torch.zeros((coff * ratio, width), dtype=torch.float32, device="cuda") for _ in range(2))
+    ks = np.zeros((coff * ratio, width), np.float32)
+    ss = np.full((coff * ratio, width), -np.inf, np.float32)
+    dks = torch.zeros((coff * ratio, width), dtype=torch.float32, device="cuda")
+    dss = torch.full((coff * ratio, width), float("-inf"), dtype=torch.float32, device="cuda")
+    zero_rows = 0
     dape = torch.from_numpy(ape).cuda()
     out = torch.empty(d, dtype=torch.float32, device="cuda")
     same = total = 0
@@ -177,6 +182,8 @@ def test_compress_steps_vs_oracle(dev, orc, ratio):
         kv = rng.standard_normal(width).astype(np.float32)
         sc = rng.standard_normal(width).astype(np.float32)
         sc[rng.integers(0, width, 2)] = -np.inf
+        if ratio <= pos < 2 * ratio:
+            sc[:] = -np.inf
         r_want, o_want = orc.compress_step(kv, sc, ape, ks, ss, pos, ratio, d)
         r_got = dev.compress_step(out, torch.from_numpy(kv).cuda(), torch.from_numpy(sc).cuda(), dape, dks, dss, pos,
                                   ratio, d)
@@ -186,6 +193,10 @@ def test_compress_steps_vs_oracle(dev, orc, ratio):
             assert float(np.abs(got - o_want).max()) <= 1e-6 * max(float(np.abs(o_want).max()), 1e-30)
             same += int(np.sum(got.view(np.uint32) == o_want.view(np.uint32)))
             total += d
+            if coff == 1 and pos == 2 * ratio - 1:
+                assert not np.any(got) and not np.any(o_want)
+                zero_rows += 1
         assert np.array_equal(dks.cpu().numpy().view(np.uint32), ks.view(np.uint32))
         assert np.array_equal(dss.cpu().numpy().view(np.uint32), ss.view(np.uint32))
+    assert zero_rows == (1 if coff == 1 else 0)
     print(f"compress ratio {ratio}: {same} of {total} pooled values bit-identical")
