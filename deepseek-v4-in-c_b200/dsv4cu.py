@@ -50,7 +50,10 @@ def lib() -> C.CDLL:
     if _lib is None:
         if not os.path.exists(LIB_PATH):
             raise DSV4CUError(f"{LIB_PATH} is missing; build with make -C {HERE}")
-        L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
+        # RTLD_LOCAL: the library exports the reference's own symbol names
+        # (dsv4_mmq_n, ...); loaded globally they would take the place of the
+        # reference's kernels inside any reference library loaded afterwards.
+        L = C.CDLL(LIB_PATH, mode=C.RTLD_LOCAL)
         vp, i, f, sz = C.c_void_p, C.c_int, C.c_float, C.c_size_t
         sig = {
             "dsv4cu_last_error": (C.c_char_p, []),
@@ -88,6 +91,11 @@ def lib() -> C.CDLL:
             "dsv4cu_ep_workspace": (sz, [vp, vp, i]),
             "dsv4cu_ep_forward": (i, [vp, vp, vp, vp, vp, vp, i, f, f, vp, vp, vp, vp]),
             "dsv4cu_ep_destroy": (None, [vp]),
+            "dsv4cu_attn_create": (i, [C.POINTER(vp), vp, vp]),
+            "dsv4cu_attn_destroy": (None, [vp]),
+            "dsv4cu_attn_step": (i, [vp, vp, vp, vp, i, vp]),
+            "dsv4cu_attn_block": (i, [vp, vp, vp, i, vp]),
+            "dsv4cu_attn_n_compressed": (i, [vp]),
             "dsv4cu_mat_create": (i, [C.POINTER(vp), vp, vp]),
             "dsv4cu_mat_destroy": (None, [vp]),
             "dsv4cu_mat_workspace": (sz, [vp, i, i]),
@@ -287,6 +295,22 @@ class HostAPI:
 
 
 # ---------------------------------------------------------------- device ABI
+class AttnCfg(C.Structure):
+    """dsv4cu_attn_cfg (include/dsv4cu.h)."""
+    _fields_ = [(n, C.c_int) for n in ("hidden", "n_heads", "head_dim", "q_lora", "o_lora", "o_groups", "qk_rope",
+                                       "sliding_window", "index_n_heads", "index_head_dim", "index_topk", "hc_mult",
+                                       "hc_sinkhorn_iters")] + \
+               [("rms_eps", C.c_float), ("hc_eps", C.c_float), ("compress_ratio", C.c_int), ("max_pos", C.c_int)]
+
+
+class AttnWeights(C.Structure):
+    """dsv4cu_attn_weights (include/dsv4cu.h): device pointers."""
+    _fields_ = [(n, QMat) for n in ("wq_a", "wq_b", "wkv", "wo_a", "wo_b", "comp_wkv", "comp_wgate", "idx_wq_b",
+                                    "idx_wproj")] + \
+               [(n, C.c_void_p) for n in ("q_norm", "kv_norm", "sink", "comp_ape", "comp_norm", "attn_norm", "hc_fn",
+                                          "hc_base", "hc_scale", "cs", "sn")]
+
+
 class Device:
     """The native dsv4cu_* entry points on one CUDA device."""
 
@@ -433,6 +457,22 @@ class Device:
         hp = (lambda a: a.data_ptr()) if hasattr(x, "data_ptr") else (lambda a: a.ctypes.data)
         check(self.L.dsv4cu_moe_decode_host(self.ctx, layer, hp(out), hp(x), hp(logits), topk, route_scale, limit,
                                             nt, self.stream()), "dsv4cu_moe_decode_host")
+
+    def attn_create(self, cfg: AttnCfg, weights: AttnWeights):
+        """One layer's device attention (dsv4cu_attn_create); weights stay referenced."""
+        h = C.c_void_p()
+        check(self.L.dsv4cu_attn_create(C.byref(h), C.byref(cfg), C.byref(weights)), "dsv4cu_attn_create")
+        return h
+
+    def attn_step(self, a, out, x, pos: int):
+        check(self.L.dsv4cu_attn_step(self.ctx, a, self.ptr(out), self.ptr(x), pos, self.stream()),
+              "dsv4cu_attn_step")
+
+    def attn_block(self, a, h, pos: int):
+        check(self.L.dsv4cu_attn_block(self.ctx, a, self.ptr(h), pos, self.stream()), "dsv4cu_attn_block")
+
+    def attn_destroy(self, a):
+        self.L.dsv4cu_attn_destroy(a)
 
     EP_HANDLE_BYTES = 128
 

@@ -285,6 +285,44 @@ int dsv4cu_ep_tail(float *recv, int nrecv, const float *x, int nt, int hidden, i
 int dsv4cu_ep_combine(float *out, const float *back, const int *pair_slot, const float *wts,
                       const float *shared, int nt, int topk, int hidden, void *stream);
 
+/* ---- one decoder layer's attention on the device (dsv4_layer_attention,
+ * src/70_decode/dsv4_layer_attn.c:12-107, and the attention half of
+ * dsv4_layer_forward, src/70_decode/dsv4_layer.c:24-36): projections, q / kv
+ * norms, RoPE, the KV ring, the compressor, the indexer (ratio 4) with its
+ * top-k, sparse attention, the inverse RoPE and the grouped wo_a (one launch)
+ * + wo_b, for one token, each step the library's device op. Weights are
+ * device pointers kept by reference; dsv4cu_attn_create allocates the
+ * layer's state (KV ring + compressed rows, the compressor's ring with its
+ * scores at -inf) and scratch. Tokens come in order pos = 0, 1, ...;
+ * nothing is synchronised. */
+typedef struct {
+    int hidden, n_heads, head_dim, q_lora, o_lora, o_groups, qk_rope, sliding_window;
+    int index_n_heads, index_head_dim, index_topk;   /* used when compress_ratio == 4 */
+    int hc_mult, hc_sinkhorn_iters;                  /* used by dsv4cu_attn_block */
+    float rms_eps, hc_eps;
+    int compress_ratio;                              /* 0, 4 (compressor + indexer) or another ratio */
+    int max_pos;                                     /* rows of the RoPE table; bounds the state */
+} dsv4cu_attn_cfg;
+
+typedef struct {
+    dsv4cu_qmat wq_a, wq_b, wkv, wo_a, wo_b;         /* FP8 (any dsv4cu_mmq format) */
+    dsv4cu_qmat comp_wkv, comp_wgate;                /* compress_ratio != 0 */
+    dsv4cu_qmat idx_wq_b, idx_wproj;                 /* compress_ratio == 4 */
+    const float *q_norm, *kv_norm, *sink, *comp_ape, *comp_norm;
+    const float *attn_norm, *hc_fn, *hc_base, *hc_scale;   /* dsv4cu_attn_block only */
+    const float *cs, *sn;                            /* RoPE table [max_pos][qk_rope / 2] */
+} dsv4cu_attn_weights;
+
+typedef struct dsv4cu_attn dsv4cu_attn;
+int  dsv4cu_attn_create(dsv4cu_attn **out, const dsv4cu_attn_cfg *cfg, const dsv4cu_attn_weights *w);
+void dsv4cu_attn_destroy(dsv4cu_attn *a);
+/* out [hidden] = the attention of x [hidden] at position pos. */
+int  dsv4cu_attn_step(dsv4cu_ctx *ctx, dsv4cu_attn *a, float *out, const float *x, int pos, void *stream);
+/* h [hc_mult][hidden] in place: mHC pre-mix, attn_norm, attention, mHC update. */
+int  dsv4cu_attn_block(dsv4cu_ctx *ctx, dsv4cu_attn *a, float *h, int pos, void *stream);
+int  dsv4cu_attn_n_compressed(const dsv4cu_attn *a);
+const float *dsv4cu_attn_kv_cache(const dsv4cu_attn *a);
+
 /* ---- the expert-parallel layer step on device, ranks joined by NVLink peer
  * memory (replaces dsv4_layer_moe's loop over the src/60_cache expert cache,
  * src/70_decode/dsv4_layer.c:48-117, for experts spread over the GPUs of one

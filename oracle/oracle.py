@@ -23,6 +23,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libdsv4ref.so")
+LAYER_SO = os.path.join(HERE, "_ref", "libdsv4layer.so")
 # The reference source tree: set by the caller (DSV4_REFERENCE_TREE or build(ref_tree=...));
 # without it only the restatement is built.
 REF_TREE = os.environ.get("DSV4_REFERENCE_TREE")
@@ -319,3 +320,80 @@ class RefLib(_Common):
                                   C.c_int(d), C.c_int(len(idxs)), C.c_float(scale),
                                   _p(scratch))
         return o
+
+
+class RefLayer:
+    """The reference's attention block on its own CPU kernels (oracle/_ref/
+    libdsv4layer.so: src/70_decode/dsv4_layer_attn.c behind layer_ref.c), one
+    layer with seeded random weights. Test infrastructure only.
+
+    dims: hidden, n_heads, head_dim, q_lora, o_lora, o_groups, qk_rope,
+    sliding_window, index_n_heads, index_head_dim, index_topk, hc_mult."""
+
+    MATS = ("wq_a", "wq_b", "wkv", "wo_a", "wo_b", "comp_wkv", "comp_wgate", "idx_wq_b", "idx_wproj")
+    VECS = ("q_norm", "kv_norm", "sink", "comp_ape", "comp_norm", "attn_norm", "hc_fn", "hc_base", "hc_scale",
+            "cs", "sn")
+
+    def __init__(self, dims, ratio: int, max_pos: int, seed: int, path: str = LAYER_SO):
+        self.lib = L = C.CDLL(path)
+        L.lr_create.restype = C.c_void_p
+        L.lr_create.argtypes = [C.POINTER(C.c_int), C.c_int, C.c_int, C.c_ulonglong]
+        L.lr_free.argtypes = [C.c_void_p]
+        L.lr_qmat.argtypes = [C.c_void_p, C.c_int, C.POINTER(QMat)]
+        L.lr_vec.restype = C.POINTER(C.c_float)
+        L.lr_vec.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_int)]
+        L.lr_attention.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+        L.lr_attn_block.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        L.lr_n_compressed.argtypes = [C.c_void_p]
+        L.lr_kv_cache.restype = C.POINTER(C.c_float)
+        L.lr_kv_cache.argtypes = [C.c_void_p]
+        self.dims = list(dims)
+        L.lr_trap_crashes()
+        arr = (C.c_int * 12)(*self.dims)
+        self.h = L.lr_create(arr, ratio, max_pos, seed)
+        if not self.h:
+            raise RuntimeError("lr_create failed")
+        self.ratio, self.max_pos = ratio, max_pos
+
+    @staticmethod
+    def available(path: str = LAYER_SO) -> bool:
+        return os.path.exists(path)
+
+    def close(self):
+        if self.h:
+            self.lib.lr_free(self.h)
+            self.h = None
+
+    def qmat(self, name):
+        """(QMat with host pointers, weight bytes, scale bytes or None) of a matrix, or None."""
+        m = QMat()
+        if not self.lib.lr_qmat(self.h, self.MATS.index(name), C.byref(m)):
+            return None
+        esz = {WBF16: 2, WFP8: 1}[m.wdt]
+        w = np.ctypeslib.as_array(C.cast(m.w, C.POINTER(C.c_uint8)), shape=(m.rows * m.cols * esz,))
+        s = None
+        if m.s:
+            n = ((m.rows + m.blk_r - 1) // m.blk_r) * ((m.cols + m.blk_c - 1) // m.blk_c)
+            s = np.ctypeslib.as_array(C.cast(m.s, C.POINTER(C.c_uint8)), shape=(n,))
+        return m, w, s
+
+    def vec(self, name):
+        n = C.c_int(0)
+        p = self.lib.lr_vec(self.h, self.VECS.index(name), C.byref(n))
+        if not p or n.value == 0:
+            return None
+        return np.ctypeslib.as_array(p, shape=(n.value,))
+
+    def attention(self, x, pos: int):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros(self.dims[0], np.float32)
+        self.lib.lr_attention(self.h, _p(out), _p(x), pos)
+        return out
+
+    def attn_block(self, h, pos: int):
+        h = np.ascontiguousarray(h, np.float32).copy()
+        self.lib.lr_attn_block(self.h, _p(h), pos)
+        return h
+
+    def n_compressed(self) -> int:
+        return self.lib.lr_n_compressed(self.h)
