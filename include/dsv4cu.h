@@ -323,6 +323,28 @@ int  dsv4cu_attn_block(dsv4cu_ctx *ctx, dsv4cu_attn *a, float *h, int pos, void 
 int  dsv4cu_attn_n_compressed(const dsv4cu_attn *a);
 const float *dsv4cu_attn_kv_cache(const dsv4cu_attn *a);
 
+/* ---- the FFN half of a decoder layer and the whole layer for one token
+ * (dsv4_layer_forward, src/70_decode/dsv4_layer.c:18-46): the FFN's mHC
+ * pre-mix, ffn_norm, the BF16 router GEMV, the MoE step of dsv4_layer_moe
+ * (dsv4cu_moe_decode) and the mHC update; dsv4cu_layer_step runs
+ * dsv4cu_attn_block then this on h [hc_mult][hidden] in place. Device
+ * pointers, kept by reference. */
+typedef struct {
+    const dsv4cu_moe *moe;        /* the layer's routed experts + shared expert */
+    dsv4cu_qmat gate;             /* router [n_experts][hidden], BF16 in the engine */
+    const float *bias;            /* selection bias [n_experts] or NULL */
+    const int64_t *tid2eid;       /* hash layers: [vocab][topk], or NULL */
+    const float *ffn_norm, *hc_fn, *hc_base, *hc_scale;
+    int hidden, hc_mult, hc_sinkhorn_iters, n_experts, topk;
+    float rms_eps, hc_eps, route_scale, swiglu_limit;
+} dsv4cu_ffn_desc;
+typedef struct dsv4cu_ffn dsv4cu_ffn;
+int  dsv4cu_ffn_create(dsv4cu_ffn **out, const dsv4cu_ffn_desc *desc);
+void dsv4cu_ffn_destroy(dsv4cu_ffn *f);
+int  dsv4cu_ffn_block(dsv4cu_ctx *ctx, dsv4cu_ffn *f, float *h, int token_id, void *stream);
+int  dsv4cu_layer_step(dsv4cu_ctx *ctx, dsv4cu_attn *a, dsv4cu_ffn *f, float *h, int pos, int token_id,
+                       void *stream);
+
 /* ---- the expert-parallel layer step on device, ranks joined by NVLink peer
  * memory (replaces dsv4_layer_moe's loop over the src/60_cache expert cache,
  * src/70_decode/dsv4_layer.c:48-117, for experts spread over the GPUs of one

@@ -38,6 +38,15 @@ typedef struct {
     int vec_n[LR_NVEC];
     void *arena;                   /* scratch floats */
     int *idxs;
+    /* FFN half: n_experts routed FP4 experts + one FP8 shared expert, BF16 gate. */
+    int n_experts, topk, inter;
+    float route_scale, limit;
+    DSV4ExpertW *experts;          /* [n_experts + 1], the shared expert last */
+    void **ebuf;                   /* their packed bytes, to free */
+    int n_ebuf;
+    DSV4QMat gate;
+    float *bias, *ffn_norm, *hcf_fn, *hcf_base, *hcf_scale;
+    float *macc;                   /* [topk + 1][hidden] expert outputs */
 } LR;
 
 static uint64_t lr_next(uint64_t *x)
@@ -250,9 +259,180 @@ LR *lr_create(const int *dims, int ratio, int max_pos, unsigned long long seed)
     return L;
 }
 
+void lr_attn_block(LR *L, float *h, int pos);
+
+static void lr_keep(LR *L, void *p)
+{
+    L->ebuf = (void **)realloc(L->ebuf, (size_t)(L->n_ebuf + 1) * sizeof(void *));
+    L->ebuf[L->n_ebuf++] = p;
+}
+
+/* FP4 e2m1 codes (any byte), 1x32 E8M0 scales 2^-8 .. 2^-5. */
+static void lr_fp4(LR *L, DSV4QMat *m, int rows, int cols, uint64_t *rng)
+{
+    const size_t n = (size_t)rows * cols / 2, ns = (size_t)rows * cols / 32;
+    unsigned char *w = (unsigned char *)malloc(n), *s = (unsigned char *)malloc(ns);
+    for (size_t i = 0; i < n; i++) w[i] = (unsigned char)lr_next(rng);
+    for (size_t i = 0; i < ns; i++) s[i] = (unsigned char)(119 + lr_next(rng) % 4);
+    *m = (DSV4QMat){w, s, DSV4_WFP4, rows, cols, 1, 32};
+    lr_keep(L, w);
+    lr_keep(L, s);
+}
+
+static void lr_fp8k(LR *L, DSV4QMat *m, int rows, int cols, uint64_t *rng)
+{
+    const size_t n = (size_t)rows * cols;
+    const int sr = (rows + 127) / 128, sc = (cols + 127) / 128;
+    unsigned char *w = (unsigned char *)malloc(n), *s = (unsigned char *)malloc((size_t)sr * sc);
+    for (size_t i = 0; i < n; i++) {
+        unsigned char b = (unsigned char)lr_next(rng);
+        if ((b & 0x7F) == 0x7F) b ^= 1;
+        w[i] = b;
+    }
+    for (int i = 0; i < sr * sc; i++) s[i] = (unsigned char)(112 + lr_next(rng) % 6);
+    *m = (DSV4QMat){w, s, DSV4_WFP8, rows, cols, 128, 128};
+    lr_keep(L, w);
+    lr_keep(L, s);
+}
+
+/* The FFN half's weights: a BF16 gate, optional selection bias, n_experts FP4
+ * experts of inter, the FP8 shared expert, ffn_norm and the FFN's mHC set. */
+int lr_ffn_create(LR *L, int n_experts, int topk, int inter, float route_scale, float limit, int with_bias,
+                  unsigned long long seed)
+{
+    uint64_t rng = seed * 0xD1B54A32D192ED03ull + 7;
+    const int d = L->c.hidden, hc = L->c.hc_mult, mix = (2 + hc) * hc;
+    L->n_experts = n_experts;
+    L->topk = topk;
+    L->inter = inter;
+    L->route_scale = route_scale;
+    L->limit = limit;
+    L->experts = (DSV4ExpertW *)calloc((size_t)n_experts + 1, sizeof(DSV4ExpertW));
+    for (int e = 0; e < n_experts; e++) {
+        lr_fp4(L, &L->experts[e].w1, inter, d, &rng);
+        lr_fp4(L, &L->experts[e].w3, inter, d, &rng);
+        lr_fp4(L, &L->experts[e].w2, d, inter, &rng);
+    }
+    lr_fp8k(L, &L->experts[n_experts].w1, inter, d, &rng);
+    lr_fp8k(L, &L->experts[n_experts].w3, inter, d, &rng);
+    lr_fp8k(L, &L->experts[n_experts].w2, d, inter, &rng);
+    uint16_t *g = (uint16_t *)malloc((size_t)n_experts * d * 2);
+    for (size_t i = 0; i < (size_t)n_experts * d; i++) {
+        const float v = lr_bf16(0.05f * lr_normal(&rng));
+        uint32_t u;
+        memcpy(&u, &v, 4);
+        g[i] = (uint16_t)(u >> 16);
+    }
+    lr_keep(L, g);
+    L->gate = (DSV4QMat){g, NULL, DSV4_WBF16, n_experts, d, 0, 0};
+    L->bias = NULL;
+    if (with_bias) {
+        L->bias = (float *)malloc((size_t)n_experts * sizeof(float));
+        for (int e = 0; e < n_experts; e++) L->bias[e] = 0.25f * lr_normal(&rng);
+        lr_keep(L, L->bias);
+    }
+    L->ffn_norm = (float *)malloc((size_t)d * sizeof(float));
+    for (int i = 0; i < d; i++) L->ffn_norm[i] = lr_bf16(1.0f + 0.1f * lr_normal(&rng));
+    lr_keep(L, L->ffn_norm);
+    L->hcf_fn = (float *)malloc((size_t)mix * hc * d * sizeof(float));
+    for (size_t i = 0; i < (size_t)mix * hc * d; i++) L->hcf_fn[i] = 0.02f * lr_normal(&rng);
+    lr_keep(L, L->hcf_fn);
+    L->hcf_base = (float *)malloc((size_t)mix * sizeof(float));
+    for (int i = 0; i < mix; i++) L->hcf_base[i] = 0.1f * lr_normal(&rng);
+    lr_keep(L, L->hcf_base);
+    L->hcf_scale = (float *)malloc(3 * sizeof(float));
+    for (int i = 0; i < 3; i++) L->hcf_scale[i] = 0.5f + 0.1f * lr_normal(&rng);
+    lr_keep(L, L->hcf_scale);
+    L->macc = (float *)calloc((size_t)(topk + 1) * d, sizeof(float));
+    lr_keep(L, L->macc);
+    return 0;
+}
+
+/* Matrix m (0 w1, 1 w3, 2 w2) of expert e (e == n_experts: the shared one); e = -1: the gate. */
+int lr_expert_qmat(LR *L, int e, int m, DSV4QMat *out)
+{
+    if (e == -1) {
+        *out = L->gate;
+        return 1;
+    }
+    if (!L->experts || e < 0 || e > L->n_experts || m < 0 || m > 2) return 0;
+    const DSV4ExpertW *x = &L->experts[e];
+    *out = m == 0 ? x->w1 : (m == 1 ? x->w3 : x->w2);
+    return 1;
+}
+
+const float *lr_ffn_vec(LR *L, int which, int *n)
+{
+    const int d = L->c.hidden, hc = L->c.hc_mult, mix = (2 + hc) * hc;
+    switch (which) {
+    case 0: *n = L->bias ? L->n_experts : 0; return L->bias;
+    case 1: *n = d; return L->ffn_norm;
+    case 2: *n = mix * hc * d; return L->hcf_fn;
+    case 3: *n = mix; return L->hcf_base;
+    case 4: *n = 3; return L->hcf_scale;
+    }
+    *n = 0;
+    return NULL;
+}
+
+/* dsv4_layer_moe (src/70_decode/dsv4_layer.c:48-117) with the routed experts
+ * in memory: the gate GEMV, dsv4_route, dsv4_expert_forward per k and for the
+ * shared expert (the reference's own functions), then the k-order weighted
+ * sum and the shared expert added unweighted, as the reference writes them. */
+static void lr_moe(LR *L, float *out, const float *x)
+{
+    const int d = L->c.hidden, topk = L->topk;
+    float *scores = (float *)malloc((size_t)L->n_experts * 2 * sizeof(float));
+    float *mid = (float *)malloc((size_t)L->inter * 3 * sizeof(float));
+    int idx[DSV4_MAX_TOPK];
+    float wts[DSV4_MAX_TOPK];
+    dsv4_mmq(scores, x, &L->gate);
+    dsv4_route(idx, wts, scores, scores + L->n_experts, L->bias, NULL, 0, L->n_experts, topk, L->route_scale);
+    for (int i = 0; i < d; i++) out[i] = 0.0f;
+    for (int k = 0; k < topk; k++)
+        dsv4_expert_forward(L->macc + (size_t)k * d, x, &L->experts[idx[k]], mid, mid + L->inter,
+                            mid + 2 * L->inter, L->inter, L->limit);
+    dsv4_expert_forward(L->macc + (size_t)topk * d, x, &L->experts[L->n_experts], mid, mid + L->inter,
+                        mid + 2 * L->inter, L->inter, L->limit);
+    for (int k = 0; k < topk; k++) {
+        const float *acc = L->macc + (size_t)k * d;
+        const float wk = wts[k];
+        for (int i = 0; i < d; i++) out[i] += wk * acc[i];
+    }
+    for (int i = 0; i < d; i++) out[i] += L->macc[(size_t)topk * d + i];
+    free(scores);
+    free(mid);
+}
+
+/* The FFN half of dsv4_layer_forward (src/70_decode/dsv4_layer.c:38-46) on h in place. */
+void lr_ffn_block(LR *L, float *h)
+{
+    const DSV4Cfg *c = &L->c;
+    const int hc = c->hc_mult, d = c->hidden;
+    DSV4Scratch *s = &L->s;
+    DSV4HcW hw = {L->hcf_fn, L->hcf_base, L->hcf_scale};
+    memcpy(s->resid, h, (size_t)hc * d * sizeof(float));
+    dsv4_hc_pre(s->x1, s->post, s->comb, s->mixes, h, &hw, hc, d, c->hc_sinkhorn_iters, c->rms_eps, c->hc_eps);
+    dsv4_rmsnorm(s->x1, s->x1, L->ffn_norm, d, c->rms_eps);
+    float *out = (float *)malloc((size_t)d * sizeof(float));
+    lr_moe(L, out, s->x1);
+    dsv4_hc_post(h, out, s->resid, s->post, s->comb, hc, d);
+    free(out);
+}
+
+/* One whole decoder layer (dsv4_layer_forward) on h in place. */
+void lr_layer(LR *L, float *h, int pos)
+{
+    lr_attn_block(L, h, pos);
+    lr_ffn_block(L, h);
+}
+
 void lr_free(LR *L)
 {
     if (!L) return;
+    for (int i = 0; i < L->n_ebuf; i++) free(L->ebuf[i]);
+    free(L->ebuf);
+    free(L->experts);
     for (int k = 0; k < LR_NMAT; k++) {
         free(L->mat_w[k]);
         free(L->mat_s[k]);

@@ -397,3 +397,48 @@ class RefLayer:
 
     def n_compressed(self) -> int:
         return self.lib.lr_n_compressed(self.h)
+
+    def ffn_create(self, n_experts: int, topk: int, inter: int, route_scale: float, limit: float, bias: bool,
+                   seed: int):
+        """The FFN half's weights (BF16 gate, FP4 experts, FP8 shared expert, ffn_norm, mHC)."""
+        L = self.lib
+        L.lr_ffn_create.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_float, C.c_int,
+                                    C.c_ulonglong]
+        L.lr_expert_qmat.argtypes = [C.c_void_p, C.c_int, C.c_int, C.POINTER(QMat)]
+        L.lr_ffn_vec.restype = C.POINTER(C.c_float)
+        L.lr_ffn_vec.argtypes = [C.c_void_p, C.c_int, C.POINTER(C.c_int)]
+        L.lr_ffn_block.argtypes = [C.c_void_p, C.c_void_p]
+        L.lr_layer.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+        L.lr_ffn_create(self.h, n_experts, topk, inter, route_scale, limit, 1 if bias else 0, seed)
+        self.n_experts, self.topk, self.inter = n_experts, topk, inter
+
+    def expert_qmat(self, e: int, m: int):
+        """(QMat, weight bytes, scale bytes or None) of matrix m of expert e (n_experts: shared; -1: gate)."""
+        q = QMat()
+        if not self.lib.lr_expert_qmat(self.h, e, m, C.byref(q)):
+            return None
+        nb = {WBF16: q.rows * q.cols * 2, WFP8: q.rows * q.cols, WFP4: q.rows * q.cols // 2}[q.wdt]
+        w = np.ctypeslib.as_array(C.cast(q.w, C.POINTER(C.c_uint8)), shape=(nb,))
+        s = None
+        if q.s:
+            n = ((q.rows + q.blk_r - 1) // q.blk_r) * ((q.cols + q.blk_c - 1) // q.blk_c)
+            s = np.ctypeslib.as_array(C.cast(q.s, C.POINTER(C.c_uint8)), shape=(n,))
+        return q, w, s
+
+    def ffn_vec(self, which: str):
+        n = C.c_int(0)
+        p = self.lib.lr_ffn_vec(self.h, ("bias", "ffn_norm", "hc_fn", "hc_base", "hc_scale").index(which),
+                                C.byref(n))
+        if not p or n.value == 0:
+            return None
+        return np.ctypeslib.as_array(p, shape=(n.value,))
+
+    def ffn_block(self, h):
+        h = np.ascontiguousarray(h, np.float32).copy()
+        self.lib.lr_ffn_block(self.h, _p(h))
+        return h
+
+    def layer(self, h, pos: int):
+        h = np.ascontiguousarray(h, np.float32).copy()
+        self.lib.lr_layer(self.h, _p(h), pos)
+        return h

@@ -122,3 +122,68 @@ def test_attn_rejects_out_of_order_position(dev, need_layer_ref):
         dev.attn_step(a, out, x, 3)
     dev.attn_destroy(a)
     ref.close()
+
+
+def _device_ffn(dev, ref, dims, keep):
+    """Upload the harness's FFN weights and build the device FFN half."""
+    import torch
+    import dsv4cu
+
+    def up(e, m):
+        q, wb, sb = ref.expert_qmat(e, m)
+        tw = torch.from_numpy(wb.copy()).cuda()
+        ts = None if sb is None else torch.from_numpy(sb.copy()).cuda()
+        keep.extend([tw, ts])
+        return dsv4cu.QMat(tw.data_ptr(), None if ts is None else ts.data_ptr(), q.wdt, q.rows, q.cols,
+                           q.blk_r, q.blk_c)
+
+    experts = [dsv4cu.Expert(up(e, 0), up(e, 1), up(e, 2)) for e in range(ref.n_experts)]
+    shared = dsv4cu.Expert(up(ref.n_experts, 0), up(ref.n_experts, 1), up(ref.n_experts, 2))
+    moe = dev.moe_create(experts, shared, dims[0], ref.inter)
+    vec = {}
+    for name in ("bias", "ffn_norm", "hc_fn", "hc_base", "hc_scale"):
+        v = ref.ffn_vec(name)
+        vec[name] = None if v is None else torch.from_numpy(v.copy()).cuda()
+        keep.append(vec[name])
+    d = dsv4cu.FfnDesc()
+    d.moe = moe
+    d.gate = up(-1, 0)
+    d.bias = None if vec["bias"] is None else vec["bias"].data_ptr()
+    d.tid2eid = None
+    d.ffn_norm, d.hc_fn = vec["ffn_norm"].data_ptr(), vec["hc_fn"].data_ptr()
+    d.hc_base, d.hc_scale = vec["hc_base"].data_ptr(), vec["hc_scale"].data_ptr()
+    d.hidden, d.hc_mult, d.hc_sinkhorn_iters, d.n_experts, d.topk = dims[0], dims[11], 20, ref.n_experts, ref.topk
+    d.rms_eps, d.hc_eps, d.route_scale, d.swiglu_limit = 1e-6, 1e-6, 1.5, 10.0
+    return dev.ffn_create(d), moe
+
+
+@pytest.mark.parametrize("dims,ratio,experts,inter,topk,steps", [
+    (SMALL, 4, 16, 256, 4, 12), (FLASH, 4, 32, 2048, 6, 6), (FLASH, 128, 32, 2048, 6, 4)],
+    ids=["small-r4", "flash-r4", "flash-r128"])
+def test_layer_step_matches_reference(dev, need_layer_ref, dims, ratio, experts, inter, topk, steps):
+    """The whole decoder layer (dsv4_layer_forward: attention half, then the
+    FFN half with the reference's dsv4_layer_moe) token after token: the
+    residual streams h [hc][hidden] after every layer step."""
+    import torch
+    ref = oracle.RefLayer(dims, ratio, 64, seed=21 + ratio)
+    ref.ffn_create(experts, topk, inter, 1.5, 10.0, True, 22)
+    a, keep = _device_layer(dev, ref, dims, ratio, 64)
+    f, moe = _device_ffn(dev, ref, dims, keep)
+    rng = np.random.default_rng(9)
+    hc, d = dims[11], dims[0]
+    worst = 0.0
+    for pos in range(steps):
+        h = rng.standard_normal((hc, d)).astype(np.float32)
+        want = ref.layer(h, pos)
+        dh = torch.from_numpy(h).cuda()
+        dev.layer_step(a, f, dh, pos)
+        got = dh.cpu().numpy()
+        dev.check_status()
+        e = _rel(got, want)
+        worst = max(worst, e)
+        assert e <= TOL, (pos, e)
+    print(f"layer {dims[0]} ratio {ratio}, {experts} experts top-{topk}: {steps} tokens, worst rel {worst:.2e}")
+    dev.ffn_destroy(f)
+    dev.moe_destroy(moe)
+    dev.attn_destroy(a)
+    ref.close()
