@@ -74,7 +74,10 @@ def parse():
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts resident in HBM (256 = config 2; smaller only for ncu captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--workload", choices=["auto", "decode", "prefill", "gemv", "indexer", "ep"], default="auto",
+    ap.add_argument("--batch", type=int, default=1, help="stack: decode batch per rank")
+    ap.add_argument("--layers", type=int, default=43, help="stack: decoder layers (43 = config 5)")
+    ap.add_argument("--workload", choices=["auto", "decode", "prefill", "gemv", "indexer", "ep", "stack"],
+                    default="auto",
                     help="auto = decode + configs 1/3/4 at N = 1, ep at N > 1; decode = config 2; prefill = config 3 (MoE layer over 4096 tokens + "
                          "FP8 QKV projection); gemv = config 1 (FP8 7168x7168 GEMV, HBM GB/s); indexer = "
                          "config 4 (FP8 indexer score + top-2048 + sparse attention); ep = the MoE layer with "
@@ -1477,6 +1480,243 @@ def run_ep(args, rank, local_rank, world):
     return res if rank == 0 else None
 
 
+# --------------------------------------------------- config 5: the layer stack
+S5_RATIOS = [0, 0] + [4, 128] * 20 + [4]          # dsv4_cfg.c flash_compress_ratios, 43 decoder layers
+S5_CTX = 8192
+S5_D = dict(hidden=4096, n_heads=64, head_dim=512, q_lora=1024, o_lora=1024, o_groups=8, qk_rope=64,
+            window=128, ih=64, ihd=128, itopk=512, hc=4)
+S5_TOPK = 6
+S5_METRIC = "decode tok/s, 43-layer DeepSeek-V4-Flash stack (config 5) at context 8192, all ranks"
+
+
+def s5_layer_bytes(ratio, epr, touched):
+    """Weight bytes one decode token reads in one layer on one rank: the
+    attention projections (FP8 + BF16 compressor / indexer), the router, the
+    shared expert and `touched` routed experts (FP4 + 1x32 scales)."""
+    d = S5_D
+    fp8 = lambda r, c: r * c + ((r + 127) // 128) * ((c + 127) // 128)
+    b = (fp8(d["q_lora"], d["hidden"]) + fp8(d["n_heads"] * d["head_dim"], d["q_lora"]) +
+         fp8(d["head_dim"], d["hidden"]) + fp8(d["o_lora"] * d["o_groups"], d["n_heads"] * d["head_dim"] // d["o_groups"]) +
+         fp8(d["hidden"], d["o_lora"] * d["o_groups"]))
+    if ratio:
+        coff = 2 if ratio == 4 else 1
+        b += 2 * coff * d["head_dim"] * d["hidden"] * 2
+    if ratio == 4:
+        b += fp8(d["ih"] * d["ihd"], d["q_lora"]) + d["ih"] * d["hidden"] * 2
+    b += 256 * d["hidden"] * 2 + 3 * FP8_MAT + touched * 3 * FP4_MAT
+    return b
+
+
+def run_stack(args, rank, local_rank, world):
+    """Config 5: every decoder layer of the Flash model on the device
+    (dsv4cu_attn_block per sequence + dsv4cu_ffn_block over the batch), weights
+    seeded random bytes of the real shapes, each layer's attention state filled
+    with a synthetic 8192-token context; the MoE's 256 experts per layer split
+    over the ranks (dsv4cu_ep_forward) when N > 1. K consecutive decode steps
+    are captured in one CUDA graph and timed as one replay, max over ranks."""
+    import datetime
+    import torch
+    import dsv4cu
+    torch.cuda.set_device(local_rank)
+    pg = None
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                 device_id=torch.device("cuda", local_rank))
+        pg = tdist
+    dev = dsv4cu.Device(local_rank)
+    B, L = args.batch, args.layers
+    d = S5_D
+    H, hd, hc, hid = d["n_heads"], d["head_dim"], d["hc"], d["hidden"]
+    epr = N_EXPERTS // world
+    max_pos = S5_CTX + args.warmup + args.steps + 8
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1234 + rank)
+    keep = []
+
+    def u8(n, lo=0, hi=256):
+        t = torch.randint(lo, hi, (n,), dtype=torch.uint8, device="cuda", generator=g)
+        keep.append(t)
+        return t
+
+    def fp8(rows, cols):
+        w = u8(rows * cols)
+        w[(w & 0x7F) == 0x7F] ^= 1
+        s = u8(((rows + 127) // 128) * ((cols + 127) // 128), 112, 118)
+        return dsv4cu.QMat(w.data_ptr(), s.data_ptr(), 2, rows, cols, 128, 128)
+
+    def bf16(rows, cols):
+        t = (torch.randn(rows * cols, device="cuda", generator=g) * 0.05).to(torch.bfloat16)
+        keep.append(t)
+        return dsv4cu.QMat(t.data_ptr(), None, 1, rows, cols, 0, 0)
+
+    def vec(n, mean=0.0, sd=1.0):
+        t = torch.randn(n, device="cuda", generator=g) * sd + mean
+        keep.append(t)
+        return t.data_ptr()
+
+    def rope(theta):
+        half = d["qk_rope"] // 2
+        inv = 1.0 / (theta ** (np.arange(half) * 2.0 / d["qk_rope"]))
+        ang = np.outer(np.arange(max_pos), inv)
+        cs, sn = (torch.from_numpy(f(ang).astype(np.float32)).cuda() for f in (np.cos, np.sin))
+        keep.extend([cs, sn])
+        return cs.data_ptr(), sn.data_ptr()
+
+    plain, comp = rope(10000.0), rope(160000.0)
+    ep = None
+    if world > 1:
+        from ep import torch_allgather
+        ep = dev.ep_create(rank, world, B, hid, S5_TOPK, epr)
+        dev.ep_connect(ep, torch_allgather()(dev.ep_handle(ep)))
+    attns, ffns, moes = [], [], []
+    for l in range(L):
+        ratio = S5_RATIOS[l]
+        w = dsv4cu.AttnWeights()
+        w.wq_a, w.wq_b, w.wkv = fp8(d["q_lora"], hid), fp8(H * hd, d["q_lora"]), fp8(hd, hid)
+        w.wo_a = fp8(d["o_lora"] * d["o_groups"], H * hd // d["o_groups"])
+        w.wo_b = fp8(hid, d["o_lora"] * d["o_groups"])
+        if ratio:
+            coff = 2 if ratio == 4 else 1
+            w.comp_wkv, w.comp_wgate = bf16(coff * hd, hid), bf16(coff * hd, hid)
+            w.comp_ape, w.comp_norm = vec(ratio * coff * hd, 0, 0.1), vec(hd, 1, 0.1)
+        if ratio == 4:
+            w.idx_wq_b, w.idx_wproj = fp8(d["ih"] * d["ihd"], d["q_lora"]), bf16(d["ih"], hid)
+        w.q_norm, w.kv_norm, w.sink = vec(d["q_lora"], 1, 0.1), vec(hd, 1, 0.1), vec(H)
+        w.attn_norm = vec(hid, 1, 0.1)
+        w.hc_fn, w.hc_base, w.hc_scale = vec((2 + hc) * hc * hc * hid, 0, 0.02), vec((2 + hc) * hc, 0, 0.1), vec(3, 0.5, 0.1)
+        w.cs, w.sn = comp if ratio else plain
+        cfg = dsv4cu.AttnCfg(hid, H, hd, d["q_lora"], d["o_lora"], d["o_groups"], d["qk_rope"], d["window"],
+                             d["ih"], d["ihd"], d["itopk"], hc, 20, 1e-6, 1e-6, ratio, max_pos)
+        row = []
+        for b in range(B):
+            a = dev.attn_create(cfg, w)
+            dev.attn_fill_context(a, S5_CTX, 7919 * l + b + 100003 * rank)
+            row.append(a)
+        attns.append(row)
+        # FFN: this rank's routed experts (FP4, one buffer per layer), the FP8 shared expert, BF16 router
+        n4 = INTER * HIDDEN // 2
+        wbuf, sbuf = u8(epr * 3 * n4), u8(epr * 3 * (n4 // 16), 119, 123)
+        experts = []
+        for e in range(epr):
+            q = [dsv4cu.QMat(wbuf.data_ptr() + (3 * e + m) * n4, sbuf.data_ptr() + (3 * e + m) * (n4 // 16), 3,
+                             *((INTER, HIDDEN) if m < 2 else (HIDDEN, INTER)), 1, 32) for m in range(3)]
+            experts.append(dsv4cu.Expert(*q))
+        shared = dsv4cu.Expert(fp8(INTER, HIDDEN), fp8(INTER, HIDDEN), fp8(HIDDEN, INTER))
+        moe = dev.moe_create(experts, shared, HIDDEN, INTER)
+        moes.append(moe)
+        fd = dsv4cu.FfnDesc()
+        fd.moe, fd.gate, fd.bias, fd.tid2eid = moe, bf16(N_EXPERTS, hid), None, None
+        fd.ffn_norm, fd.hc_fn = vec(hid, 1, 0.1), vec((2 + hc) * hc * hc * hid, 0, 0.02)
+        fd.hc_base, fd.hc_scale = vec((2 + hc) * hc, 0, 0.1), vec(3, 0.5, 0.1)
+        fd.hidden, fd.hc_mult, fd.hc_sinkhorn_iters, fd.n_experts, fd.topk, fd.nt_max = hid, hc, 20, N_EXPERTS, S5_TOPK, B
+        fd.rms_eps, fd.hc_eps, fd.route_scale, fd.swiglu_limit = 1e-6, 1e-6, 1.5, 10.0
+        fd.ep = ep
+        ffns.append(dev.ffn_create(fd))
+    torch.cuda.synchronize()
+    h = torch.randn((B, hc, hid), device="cuda", generator=g)
+
+    def step(pos):
+        for l in range(L):
+            for b in range(B):
+                dev.attn_block(attns[l][b], h[b], pos)
+            dev.ffn_block(ffns[l], h, B)
+
+    def barrier():
+        if pg:
+            pg.barrier()
+
+    pos = S5_CTX
+    for _ in range(args.warmup):
+        step(pos)
+        pos += 1
+    torch.cuda.synchronize()
+    dev.check_status()
+    barrier()
+    graph_ms, graph_err = None, None
+    clocks = Clocks(local_rank)
+    clocks.start()
+    try:
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph):
+            for k in range(args.steps):
+                step(pos + k)
+        barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        gph.replay()
+        a1.record()
+        torch.cuda.synchronize()
+        graph_ms = a0.elapsed_time(a1)
+        del gph
+    except Exception as e:        # reported in the line
+        graph_err = f"{type(e).__name__}: {e}"[:200]
+        torch.cuda.synchronize()
+    clk = clocks.stop()
+    pos += args.steps
+    if graph_ms is None:
+        barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        for k in range(args.steps):
+            step(pos + k)
+        a1.record()
+        torch.cuda.synchronize()
+        graph_ms = a0.elapsed_time(a1)
+    dev.check_status()
+    t = torch.tensor([graph_ms], dtype=torch.float64, device="cuda")
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    ms = t.item()
+    assert bool(torch.isfinite(h).all()), "non-finite residual stream"
+    peak, peak_kind = load_peaks()
+    # bytes per token step per rank: the batch's distinct experts are unknown here; bound with all
+    # min(B * topk, epr) touched (the stream of weights a step needs at least)
+    touched = min(epr, max(1, (B * world * S5_TOPK) // world))
+    step_bytes = sum(s5_layer_bytes(S5_RATIOS[l], epr, touched) for l in range(L))
+    res = {
+        "metric": S5_METRIC, "value": round(world * B * args.steps / (ms * 1e-3), 2), "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "FP8 / FP4 / BF16 weights, f32 activations (the reference's formats)",
+        "data": "synthetic: seeded random weight bytes of the real shapes, seeded synthetic 8192-token context "
+                "in every layer's KV ring, compressed rows and compressor ring, random residual streams",
+        "config": {"workload": f"config5: {L} decoder layers (compress ratios of dsv4_cfg.c), hidden 4096, 64 "
+                               f"heads x 512, q_lora 1024, 8 wo_a groups, window 128, indexer 64 x 128 top-512, "
+                               f"mHC 4, MoE 256 x 2048 top-6 + shared, decode batch {B} per rank, context {S5_CTX}",
+                   "global_batch": world * B, "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                   "timing": "CUDA graph of the K consecutive decode steps" if graph_err is None else
+                             f"stream launches (graph capture failed: {graph_err})",
+                   "note": "routing without bias or hash tables in every layer (the cost is the same); no "
+                           "embedding / head (outside the layer stack)"},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": round(step_bytes / (ms / args.steps * 1e-3) / 1e9, 1),
+                     "peak": peak, "peak_source": peak_kind, "unit": "GB/s",
+                     "frac": round(step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4), "traffic": None,
+                     "algorithmic_bytes": step_bytes,
+                     "algorithmic_bytes_note": "per rank per step: every layer's attention weights, router, shared "
+                                               "expert and min(batch x top-6, experts per rank) routed experts"},
+        "gpu_launches": None,
+        "clocks": clk,
+    }
+    barrier()
+    for row in attns:
+        for a in row:
+            dev.attn_destroy(a)
+    for f in ffns:
+        dev.ffn_destroy(f)
+    for m in moes:
+        dev.moe_destroy(m)
+    if ep is not None:
+        dev.ep_destroy(ep)
+    if pg:
+        pg.destroy_process_group()
+    dev.close()
+    del keep
+    return res if rank == 0 else None
+
+
 JSON_FD = [1]        # where the JSON line goes (main() moves other stdout to stderr)
 SECONDARY = (("config1", "gemv"), ("config3", "prefill"), ("config4", "indexer"))
 
@@ -1512,7 +1752,11 @@ def main():
     wl = args.workload
     if wl == "auto":
         wl = "decode" if world == 1 else "ep"
-    if wl == "ep":
+    if wl == "stack":
+        res = ({"impl": "reference", "unavailable": "the reference's 43-layer CPU decode at context 8192 takes "
+                "seconds per token and needs its whole engine; the per-layer reference runs in tests/test_gpu_layer.py"}
+               if args.impl == "reference" else run_stack(args, rank, local_rank, world))
+    elif wl == "ep":
         res = (run_reference(args, rank, world, EP_METRIC, "tok/s", EP_WORKLOAD) if args.impl == "reference"
                else run_ep(args, rank, local_rank, world))
     elif wl == "indexer":

@@ -215,6 +215,43 @@ extern "C" void dsv4cu_attn_destroy(dsv4cu_attn *a)
 
 extern "C" int dsv4cu_attn_n_compressed(const dsv4cu_attn *a) { return a ? a->n_compressed : -1; }
 
+namespace {
+
+// Seeded values in [-1, 1) (splitmix64 of the element index).
+__global__ void epl_synth_kernel(float *__restrict__ p, long n, unsigned long long seed)
+{
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    unsigned long long z = seed + 0x9E3779B97F4A7C15ull * (unsigned long long)(i + 1);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    p[i] = (float)((double)(z >> 11) * (2.0 / 9007199254740992.0) - 1.0);
+}
+
+}  // namespace
+
+extern "C" int dsv4cu_attn_fill_context(dsv4cu_attn *a, int pos, unsigned long long seed, void *stream)
+{
+    if (!a || pos < 0 || pos >= a->c.max_pos) return dsv4cu_set_error(DSV4CU_ERR_ARG, "attn_fill_context: pos %d", pos);
+    const dsv4cu_attn_cfg &c = a->c;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int ratio = c.compress_ratio, ncomp = ratio ? pos / ratio : 0;
+    if (ncomp > a->ncomp_max) return dsv4cu_set_error(DSV4CU_ERR_ARG, "attn_fill_context: beyond the state");
+    const long rows = (long)c.sliding_window + ncomp, n = rows * c.head_dim;
+    epl_synth_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a->kv_cache, n, seed);
+    DSV4CU_LAUNCH_CHECK();
+    if (ratio) {
+        const long cs = (long)a->coff * ratio * a->coff * c.head_dim;
+        epl_synth_kernel<<<(unsigned)((cs + 255) / 256), 256, 0, st>>>(a->comp_kv, cs, seed ^ 0x5151ull);
+        epl_synth_kernel<<<(unsigned)((cs + 255) / 256), 256, 0, st>>>(a->comp_score, cs, seed ^ 0xA2A2ull);
+        DSV4CU_LAUNCH_CHECK();
+    }
+    a->n_compressed = ncomp;
+    a->next_pos = pos;
+    return DSV4CU_OK;
+}
+
 extern "C" const float *dsv4cu_attn_kv_cache(const dsv4cu_attn *a) { return a ? a->kv_cache : nullptr; }
 
 extern "C" int dsv4cu_attn_step(dsv4cu_ctx *ctx, dsv4cu_attn *a, float *out, const float *x, int pos, void *stream)

@@ -358,6 +358,35 @@ __global__ void __launch_bounds__(BfcCfg<R, NT, CW>::THREADS, 1) bf16_chain_tma_
     }
 }
 
+// One token, a matrix of few rows (the router, the compressor and indexer
+// projections): a half-warp per row, lane c of it runs chain c over columns
+// c, c + 16, ... in order, then the same fold (((c0 + c4) + (c8 + c12)) for
+// each of c = 0..3, paired (b0 + b1) + (b2 + b3)) and the ragged tail in
+// order - the BLOCK_DOT_V operations - spread over 8x more CTAs than the
+// 256-row stages of the streaming kernel give such a matrix.
+__global__ void __launch_bounds__(256) bf16_chain_small_kernel(const uint16_t *__restrict__ W, int rows, int cols,
+                                                               const double *__restrict__ xd, float *__restrict__ y)
+{
+    const int lane = threadIdx.x & 31, c = lane & 15, half = lane >> 4;
+    const int row = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * 2 + half;
+    const int M = cols >> 4;
+    const uint16_t *wrow = W + (size_t)min(row, rows - 1) * cols;
+    double acc = 0.0;
+#pragma unroll 32
+    for (int i = 0; i < M; i++) {
+        const int k = 16 * i + c;
+        acc = __fma_rn((double)__uint_as_float((uint32_t)__ldg(wrow + k) << 16), __ldg(xd + k), acc);
+    }
+    double v = acc + __shfl_down_sync(0xFFFFFFFFu, acc, 4);   // c in 0..3, 8..11: c_j + c_j+4, c_8+j + c_12+j
+    v = v + __shfl_down_sync(0xFFFFFFFFu, v, 8);              // c in 0..3: b_c
+    v = v + __shfl_down_sync(0xFFFFFFFFu, v, 1);              // c = 0: b0 + b1, c = 2: b2 + b3
+    v = v + __shfl_down_sync(0xFFFFFFFFu, v, 2);              // c = 0: (b0 + b1) + (b2 + b3)
+    if (c != 0 || row >= rows) return;
+    for (int i = 16 * M; i < cols; i++)
+        v = __fma_rn((double)__uint_as_float((uint32_t)__ldg(wrow + i) << 16), xd[i], v);
+    y[row] = __double2float_rn(v);
+}
+
 // The activation copy: rows of ldxd doubles, ldxd a multiple of 128 columns so
 // every TMA stage's 128 columns lie inside the row.
 static int bf16_ldxd(int cols) { return ((cols + 127) / 128) * 128; }
@@ -391,6 +420,12 @@ int bf16_chain_run(float *y, const float *x, const dsv4cu_qmat *q, int nt, void 
     const long n = (long)nt * ldxd;
     bf16_xwiden_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, cols, nt, ldxd, xd);
     DSV4CU_LAUNCH_CHECK();
+    if (nt == 1 && rows <= 8192) {
+        const unsigned grid = (unsigned)((rows + 15) / 16);     // 8 warps x 2 rows per CTA
+        bf16_chain_small_kernel<<<grid, 256, 0, st>>>(W, rows, cols, xd, y);
+        DSV4CU_LAUNCH_CHECK();
+        return DSV4CU_OK;
+    }
     if (tmap_weights_ok(q) && cols >= 16) {
         CUtensorMap tw;
         int staged = 0;

@@ -27,52 +27,171 @@
 namespace dsv4cu {
 
 constexpr int HC_MAX = 6;
-constexpr int HC_MAX_DOTS = (2 + HC_MAX) * HC_MAX + 1;
 
 DSV4CU_DEV float hc_expf(float v) { return __double2float_rn(exp((double)v)); }
 DSV4CU_DEV float hc_sigmoid(float v) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, hc_expf(-v))); }
 
-__global__ void __launch_bounds__(1024) hc_pre_kernel(float *__restrict__ y, float *__restrict__ post,
-                                                      float *__restrict__ comb_out, float *__restrict__ mixes_out,
-                                                      const float *__restrict__ x, const float *__restrict__ fn,
-                                                      const float *__restrict__ base, const float *__restrict__ scale,
-                                                      int hc, int hidden, int iters, float norm_eps, float hc_eps)
+// The dots of dsv4_hc_pre: dot 0 = x.x, dot m = fn[m - 1].x (m = 1 .. mix), each
+// the reference's 16-chain tree (dsv4_dot_f32d): chain c sums elements c, c +
+// 16, ... in order, one double fma each, then the fixed fold. One CTA per
+// (dot, token): its row and x are staged in shared memory by the whole CTA
+// (every load in flight at once), then 16 threads run the chains from there.
+// The reference uses dot 0 in double and rounds the others to float before
+// anything else, so the float dots go to mixes (scaled in place by the second
+// kernel) and dot 0's two 32-bit halves to post[t][0] and comb[t][0]; the
+// second kernel reads them before it writes those outputs.
+__global__ void __launch_bounds__(256) hc_pre_dots_kernel(float *__restrict__ post, float *__restrict__ comb,
+                                                          float *__restrict__ mixes, const float *__restrict__ x,
+                                                          const float *__restrict__ fn, int hc, int hidden)
 {
-    __shared__ double chains[HC_MAX_DOTS * 16];
-    __shared__ double dots[HC_MAX_DOTS];
-    __shared__ float s_pre[HC_MAX];
-    const int t = blockIdx.x, hcdim = hc * hidden, mix = (2 + hc) * hc, ndots = mix + 1;
-    const int n16 = hcdim & ~15;
+    extern __shared__ float hc_stage[];
+    const int m = blockIdx.x, t = blockIdx.y, hcdim = hc * hidden, n16 = hcdim & ~15;
     const float *xt = x + (size_t)t * hcdim;
-
-    for (int task = threadIdx.x; task < ndots * 16; task += blockDim.x) {
-        const int m = task >> 4, c = task & 15;
-        const float *a = m == 0 ? xt : fn + (size_t)(m - 1) * hcdim;
-        double acc = 0.0;
-#pragma unroll 8
-        for (int i = c; i < n16; i += 16) acc = __fma_rn((double)__ldg(a + i), (double)__ldg(xt + i), acc);
-        chains[task] = acc;
+    const float *a = m == 0 ? xt : fn + (size_t)(m - 1) * hcdim;
+    float *sx = hc_stage, *sa = hc_stage + hcdim;
+    if ((hcdim & 3) == 0 && ((uintptr_t)xt & 15) == 0 && ((uintptr_t)a & 15) == 0) {
+        const int n4 = hcdim >> 2;
+        const float4 *x4 = reinterpret_cast<const float4 *>(xt), *a4 = reinterpret_cast<const float4 *>(a);
+        float4 *sx4 = reinterpret_cast<float4 *>(sx), *sa4 = reinterpret_cast<float4 *>(sa);
+#pragma unroll 4
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+            sx4[i] = __ldg(x4 + i);
+            sa4[i] = __ldg(a4 + i);
+        }
+    } else {
+        for (int i = threadIdx.x; i < hcdim; i += blockDim.x) {
+            sx[i] = __ldg(xt + i);
+            sa[i] = __ldg(a + i);
+        }
     }
     __syncthreads();
-    if (threadIdx.x < ndots) {
-        const int m = threadIdx.x;
-        const double *ch = chains + m * 16;
+    __shared__ double chains[16];
+    if (threadIdx.x < 16) {
+        const int c = threadIdx.x;
+        double acc = 0.0;
+#pragma unroll 8
+        for (int i = c; i < n16; i += 16) acc = __fma_rn((double)sa[i], (double)sx[i], acc);
+        chains[c] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
         double bb[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) bb[j] = __dadd_rn(__dadd_rn(ch[j], ch[j + 4]), __dadd_rn(ch[j + 8], ch[j + 12]));
+        for (int j = 0; j < 4; j++)
+            bb[j] = __dadd_rn(__dadd_rn(chains[j], chains[j + 4]), __dadd_rn(chains[j + 8], chains[j + 12]));
         double acc = __dadd_rn(__dadd_rn(bb[0], bb[1]), __dadd_rn(bb[2], bb[3]));
-        const float *a = m == 0 ? xt : fn + (size_t)(m - 1) * hcdim;
-        for (int i = n16; i < hcdim; i++) acc = __fma_rn((double)__ldg(a + i), (double)__ldg(xt + i), acc);
-        dots[m] = acc;
+        for (int i = n16; i < hcdim; i++) acc = __fma_rn((double)sa[i], (double)sx[i], acc);
+        if (m == 0) {
+            const unsigned long long b = (unsigned long long)__double_as_longlong(acc);
+            post[(size_t)t * hc] = __uint_as_float((unsigned)b);
+            comb[(size_t)t * hc * hc] = __uint_as_float((unsigned)(b >> 32));
+        } else {
+            mixes[(size_t)t * (2 + hc) * hc + m - 1] = __double2float_rn(acc);
+        }
     }
+}
+
+// dsv4_hc_pre's tail for hc = 4 (the model's value) in one warp: lane e < 16
+// owns comb[e / 4][e % 4]; each row or column sum gathers its four values by
+// shuffles and adds them in the reference's order (0, 1, 2, 3), so every lane
+// computes the same rounding the sequential loop does; the 20 Sinkhorn
+// passes then cost a few shuffles and one division per lane each.
+__global__ void __launch_bounds__(256) hc_pre4_kernel(float *__restrict__ y, float *__restrict__ post,
+                                                      float *__restrict__ comb_out, float *__restrict__ mixes_out,
+                                                      const float *__restrict__ x, const float *__restrict__ base,
+                                                      const float *__restrict__ scale, int hidden, int iters,
+                                                      float norm_eps, float hc_eps)
+{
+    constexpr int HC = 4, MIX = (2 + HC) * HC;
+    __shared__ float s_pre[HC];
+    const int t = blockIdx.x, hcdim = HC * hidden;
+    const float *xt = x + (size_t)t * hcdim;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x, k = lane & 3;
+        const double dot0 = __longlong_as_double(
+            (long long)(((unsigned long long)__float_as_uint(comb_out[(size_t)t * HC * HC]) << 32) |
+                        __float_as_uint(post[(size_t)t * HC])));
+        const float rsq = __double2float_rn(
+            __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(dot0, (double)hcdim), (double)norm_eps))));
+        __syncwarp();
+        static_assert(MIX <= 32, "one mixing value per lane");
+        const float mix_a = __fmul_rn(mixes_out[(size_t)t * MIX + lane % MIX], rsq);    // lane < MIX: mixes[lane]
+        __syncwarp();
+        if (lane < MIX) mixes_out[(size_t)t * MIX + lane] = mix_a;
+        // pre[j] from mixes[j], post[j] from mixes[4 + j], comb from mixes[8 + e]
+        const float m_pre = __shfl_sync(0xFFFFFFFFu, mix_a, lane & 3);
+        const float m_post = __shfl_sync(0xFFFFFFFFu, mix_a, 4 + (lane & 3));
+        const float m_comb = __shfl_sync(0xFFFFFFFFu, mix_a, 8 + (lane & 15));
+        if (lane < HC) {
+            s_pre[lane] = __fadd_rn(hc_sigmoid(__fadd_rn(__fmul_rn(m_pre, scale[0]), base[lane])), hc_eps);
+            post[(size_t)t * HC + lane] =
+                __fmul_rn(2.0f, hc_sigmoid(__fadd_rn(__fmul_rn(m_post, scale[1]), base[lane + HC])));
+        }
+        const int e = lane & 15;
+        float c = __fadd_rn(__fmul_rn(m_comb, scale[2]), base[2 * HC + e]);
+        auto row_val = [&](float v, int kk) { return __shfl_sync(0xFFFFFFFFu, v, (lane & ~3) + kk); };
+        auto col_val = [&](float v, int jj) { return __shfl_sync(0xFFFFFFFFu, v, (lane & 16) + 4 * jj + k); };
+        // First pass: row softmax (max over k with '>' in order), + eps, then a column normalise.
+        {
+            float mx = row_val(c, 0);
+            for (int kk = 1; kk < HC; kk++) {
+                const float v = row_val(c, kk);
+                if (v > mx) mx = v;
+            }
+            const float ex = hc_expf(__fsub_rn(c, mx));
+            double sum = 0.0;
+            for (int kk = 0; kk < HC; kk++) sum = __dadd_rn(sum, (double)row_val(ex, kk));
+            const float inv = __double2float_rn(__ddiv_rn(1.0, sum));
+            c = __fadd_rn(__fmul_rn(ex, inv), hc_eps);
+        }
+        {
+            double cs = 0.0;
+            for (int jj = 0; jj < HC; jj++) cs = __dadd_rn(cs, (double)col_val(c, jj));
+            c = __fdiv_rn(c, __fadd_rn(__double2float_rn(cs), hc_eps));
+        }
+        for (int it = 0; it < iters - 1; it++) {
+            double rs = 0.0;
+            for (int kk = 0; kk < HC; kk++) rs = __dadd_rn(rs, (double)row_val(c, kk));
+            c = __fdiv_rn(c, __fadd_rn(__double2float_rn(rs), hc_eps));
+            double cs = 0.0;
+            for (int jj = 0; jj < HC; jj++) cs = __dadd_rn(cs, (double)col_val(c, jj));
+            c = __fdiv_rn(c, __fadd_rn(__double2float_rn(cs), hc_eps));
+        }
+        if (lane < HC * HC) comb_out[(size_t)t * HC * HC + lane] = c;
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hidden; d += blockDim.x) {
+        double acc = 0.0;
+#pragma unroll
+        for (int jj = 0; jj < HC; jj++)
+            acc = __fma_rn((double)s_pre[jj], (double)__ldg(xt + (size_t)jj * hidden + d), acc);
+        y[(size_t)t * hidden + d] = __double2float_rn(acc);
+    }
+}
+
+// The rest of dsv4_hc_pre for token blockIdx.x, from the dots hc_pre_dots_kernel
+// left in its outputs.
+__global__ void __launch_bounds__(256) hc_pre_kernel(float *__restrict__ y, float *__restrict__ post,
+                                                     float *__restrict__ comb_out, float *__restrict__ mixes_out,
+                                                     const float *__restrict__ x, const float *__restrict__ base,
+                                                     const float *__restrict__ scale, int hc, int hidden, int iters,
+                                                     float norm_eps, float hc_eps)
+{
+    __shared__ double dot0;
+    __shared__ float s_pre[HC_MAX];
+    const int t = blockIdx.x, hcdim = hc * hidden, mix = (2 + hc) * hc;
+    const float *xt = x + (size_t)t * hcdim;
+    if (threadIdx.x == 0)
+        dot0 = __longlong_as_double((long long)(((unsigned long long)__float_as_uint(comb_out[(size_t)t * hc * hc]) << 32) |
+                                                __float_as_uint(post[(size_t)t * hc])));
     __syncthreads();
 
     if (threadIdx.x == 0) {
         const float rsq = __double2float_rn(
-            __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(dots[0], (double)hcdim), (double)norm_eps))));
+            __ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(__ddiv_rn(dot0, (double)hcdim), (double)norm_eps))));
         float mixes[(2 + HC_MAX) * HC_MAX], pre[HC_MAX], po[HC_MAX], comb[HC_MAX * HC_MAX];
         for (int m = 0; m < mix; m++) {
-            mixes[m] = __fmul_rn(__double2float_rn(dots[m + 1]), rsq);
+            mixes[m] = __fmul_rn(mixes_out[(size_t)t * mix + m], rsq);
             mixes_out[(size_t)t * mix + m] = mixes[m];
         }
         for (int j = 0; j < hc; j++)
@@ -272,9 +391,17 @@ extern "C" int dsv4cu_hc_pre(float *y, float *post, float *comb, float *mixes, c
         return dsv4cu_set_error(DSV4CU_ERR_ARG, "hc_pre: bad args");
     if (hc < 1 || hc > HC_MAX) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "hc_pre: hc %d (1..%d)", hc, HC_MAX);
     const int ndots = (2 + hc) * hc + 1;
-    int threads = ((ndots * 16 + 31) / 32) * 32;
-    if (threads < 256) threads = 256;
-    hc_pre_kernel<<<(unsigned)nt, threads, 0, (cudaStream_t)stream>>>(y, post, comb, mixes, x, fn, base, scale, hc,
+    const size_t smem = (size_t)2 * hc * hidden * sizeof(float);
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)hc_pre_dots_kernel, (int)smem));
+    hc_pre_dots_kernel<<<dim3((unsigned)ndots, (unsigned)nt), 256, smem, (cudaStream_t)stream>>>(post, comb, mixes, x,
+                                                                                               fn, hc, hidden);
+    DSV4CU_LAUNCH_CHECK();
+    if (hc == 4)
+        hc_pre4_kernel<<<(unsigned)nt, 256, 0, (cudaStream_t)stream>>>(y, post, comb, mixes, x, base, scale, hidden,
+                                                                       iters, norm_eps, hc_eps);
+    else
+        hc_pre_kernel<<<(unsigned)nt, 256, 0, (cudaStream_t)stream>>>(y, post, comb, mixes, x, base, scale, hc,
                                                                       hidden, iters, norm_eps, hc_eps);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;

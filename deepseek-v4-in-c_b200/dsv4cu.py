@@ -96,9 +96,10 @@ def lib() -> C.CDLL:
             "dsv4cu_attn_step": (i, [vp, vp, vp, vp, i, vp]),
             "dsv4cu_attn_block": (i, [vp, vp, vp, i, vp]),
             "dsv4cu_attn_n_compressed": (i, [vp]),
+            "dsv4cu_attn_fill_context": (i, [vp, i, C.c_ulonglong, vp]),
             "dsv4cu_ffn_create": (i, [C.POINTER(vp), vp]),
             "dsv4cu_ffn_destroy": (None, [vp]),
-            "dsv4cu_ffn_block": (i, [vp, vp, vp, i, vp]),
+            "dsv4cu_ffn_block": (i, [vp, vp, vp, i, vp, vp]),
             "dsv4cu_layer_step": (i, [vp, vp, vp, vp, i, i, vp]),
             "dsv4cu_mat_create": (i, [C.POINTER(vp), vp, vp]),
             "dsv4cu_mat_destroy": (None, [vp]),
@@ -319,8 +320,9 @@ class FfnDesc(C.Structure):
     """dsv4cu_ffn_desc (include/dsv4cu.h): device pointers."""
     _fields_ = [("moe", C.c_void_p), ("gate", QMat), ("bias", C.c_void_p), ("tid2eid", C.c_void_p),
                 ("ffn_norm", C.c_void_p), ("hc_fn", C.c_void_p), ("hc_base", C.c_void_p), ("hc_scale", C.c_void_p)] + \
-               [(n, C.c_int) for n in ("hidden", "hc_mult", "hc_sinkhorn_iters", "n_experts", "topk")] + \
-               [(n, C.c_float) for n in ("rms_eps", "hc_eps", "route_scale", "swiglu_limit")]
+               [(n, C.c_int) for n in ("hidden", "hc_mult", "hc_sinkhorn_iters", "n_experts", "topk", "nt_max")] + \
+               [(n, C.c_float) for n in ("rms_eps", "hc_eps", "route_scale", "swiglu_limit")] + \
+               [("ep", C.c_void_p)]
 
 
 class Device:
@@ -483,6 +485,9 @@ class Device:
     def attn_block(self, a, h, pos: int):
         check(self.L.dsv4cu_attn_block(self.ctx, a, self.ptr(h), pos, self.stream()), "dsv4cu_attn_block")
 
+    def attn_fill_context(self, a, pos: int, seed: int):
+        check(self.L.dsv4cu_attn_fill_context(a, pos, seed, self.stream()), "dsv4cu_attn_fill_context")
+
     def attn_destroy(self, a):
         self.L.dsv4cu_attn_destroy(a)
 
@@ -491,8 +496,9 @@ class Device:
         check(self.L.dsv4cu_ffn_create(C.byref(h), C.byref(desc)), "dsv4cu_ffn_create")
         return h
 
-    def ffn_block(self, f, h, token_id: int = 0):
-        check(self.L.dsv4cu_ffn_block(self.ctx, f, self.ptr(h), token_id, self.stream()), "dsv4cu_ffn_block")
+    def ffn_block(self, f, h, nt: int = 1, token_ids=None):
+        check(self.L.dsv4cu_ffn_block(self.ctx, f, self.ptr(h), nt, self.ptr(token_ids), self.stream()),
+              "dsv4cu_ffn_block")
 
     def layer_step(self, a, f, h, pos: int, token_id: int = 0):
         check(self.L.dsv4cu_layer_step(self.ctx, a, f, self.ptr(h), pos, token_id, self.stream()),

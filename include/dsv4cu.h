@@ -322,26 +322,35 @@ int  dsv4cu_attn_step(dsv4cu_ctx *ctx, dsv4cu_attn *a, float *out, const float *
 int  dsv4cu_attn_block(dsv4cu_ctx *ctx, dsv4cu_attn *a, float *h, int pos, void *stream);
 int  dsv4cu_attn_n_compressed(const dsv4cu_attn *a);
 const float *dsv4cu_attn_kv_cache(const dsv4cu_attn *a);
+/* Benchmarking and tests: put the layer at position pos with a synthetic
+ * context (seeded values in [-1, 1) in the KV ring, the pos / ratio
+ * compressed rows and the compressor's ring), so the next step is pos. */
+int  dsv4cu_attn_fill_context(dsv4cu_attn *a, int pos, unsigned long long seed, void *stream);
 
-/* ---- the FFN half of a decoder layer and the whole layer for one token
- * (dsv4_layer_forward, src/70_decode/dsv4_layer.c:18-46): the FFN's mHC
- * pre-mix, ffn_norm, the BF16 router GEMV, the MoE step of dsv4_layer_moe
- * (dsv4cu_moe_decode) and the mHC update; dsv4cu_layer_step runs
- * dsv4cu_attn_block then this on h [hc_mult][hidden] in place. Device
- * pointers, kept by reference. */
+/* ---- the FFN half of a decoder layer and the whole layer (dsv4_layer_forward,
+ * src/70_decode/dsv4_layer.c:18-46): the FFN's mHC pre-mix, ffn_norm, the
+ * BF16 router GEMV, the MoE step of dsv4_layer_moe (dsv4cu_moe_decode, or
+ * with `ep` set the expert-parallel step dsv4cu_ep_forward over the ranks,
+ * whose routing takes no bias or hash table) and the mHC update, for nt <=
+ * nt_max tokens (a decode batch: h [nt][hc_mult][hidden] in place;
+ * token_ids: device [nt], hash layers only). dsv4cu_layer_step runs
+ * dsv4cu_attn_block then the FFN half for one token. Device pointers, kept by
+ * reference. */
+typedef struct dsv4cu_ep dsv4cu_ep;
 typedef struct {
-    const dsv4cu_moe *moe;        /* the layer's routed experts + shared expert */
+    const dsv4cu_moe *moe;        /* the layer's routed experts + shared expert (this rank's, with ep) */
     dsv4cu_qmat gate;             /* router [n_experts][hidden], BF16 in the engine */
     const float *bias;            /* selection bias [n_experts] or NULL */
     const int64_t *tid2eid;       /* hash layers: [vocab][topk], or NULL */
     const float *ffn_norm, *hc_fn, *hc_base, *hc_scale;
-    int hidden, hc_mult, hc_sinkhorn_iters, n_experts, topk;
+    int hidden, hc_mult, hc_sinkhorn_iters, n_experts, topk, nt_max;
     float rms_eps, hc_eps, route_scale, swiglu_limit;
+    dsv4cu_ep *ep;                /* NULL: all experts on this GPU */
 } dsv4cu_ffn_desc;
 typedef struct dsv4cu_ffn dsv4cu_ffn;
 int  dsv4cu_ffn_create(dsv4cu_ffn **out, const dsv4cu_ffn_desc *desc);
 void dsv4cu_ffn_destroy(dsv4cu_ffn *f);
-int  dsv4cu_ffn_block(dsv4cu_ctx *ctx, dsv4cu_ffn *f, float *h, int token_id, void *stream);
+int  dsv4cu_ffn_block(dsv4cu_ctx *ctx, dsv4cu_ffn *f, float *h, int nt, const int *token_ids, void *stream);
 int  dsv4cu_layer_step(dsv4cu_ctx *ctx, dsv4cu_attn *a, dsv4cu_ffn *f, float *h, int pos, int token_id,
                        void *stream);
 
@@ -372,7 +381,6 @@ int  dsv4cu_layer_step(dsv4cu_ctx *ctx, dsv4cu_attn *a, dsv4cu_ffn *f, float *h,
  * or NULL) are recorded around route+plan, dispatch, gather, the expert
  * GEMMs, return and combine. */
 #define DSV4CU_EP_HANDLE_BYTES 128
-typedef struct dsv4cu_ep dsv4cu_ep;
 int  dsv4cu_ep_create(dsv4cu_ep **out, int rank, int world, int nt_max, int hidden, int topk,
                       int experts_per_rank);
 int  dsv4cu_ep_handle(const dsv4cu_ep *ep, void *blob);

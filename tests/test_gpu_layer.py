@@ -153,6 +153,7 @@ def _device_ffn(dev, ref, dims, keep):
     d.ffn_norm, d.hc_fn = vec["ffn_norm"].data_ptr(), vec["hc_fn"].data_ptr()
     d.hc_base, d.hc_scale = vec["hc_base"].data_ptr(), vec["hc_scale"].data_ptr()
     d.hidden, d.hc_mult, d.hc_sinkhorn_iters, d.n_experts, d.topk = dims[0], dims[11], 20, ref.n_experts, ref.topk
+    d.nt_max = 8
     d.rms_eps, d.hc_eps, d.route_scale, d.swiglu_limit = 1e-6, 1e-6, 1.5, 10.0
     return dev.ffn_create(d), moe
 

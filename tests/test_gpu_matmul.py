@@ -185,7 +185,8 @@ def test_deterministic_and_cache_refresh(host):
     assert_close(c, d)
 
 
-@pytest.mark.parametrize("rows,cols,nt", [(4096, 7168, 1), (1000, 7168, 5), (300, 4104, 2), (77, 1030, 1)])
+@pytest.mark.parametrize("rows,cols,nt", [(4096, 7168, 1), (1000, 7168, 5), (300, 4104, 2), (77, 1030, 1),
+                                         (1024, 4096, 1), (16384, 4096, 1), (3, 17, 1)])
 def test_bf16_bitwise_with_specials(dev, orc, rows, cols, nt):
     """BF16 weights with zeros, subnormals and infinities among them and
     arbitrary fp32 activations: the reference's bits (bf16_n,
