@@ -40,28 +40,69 @@ struct SmvDenseParams {
     long long stages;          // (rows / 32) * nseg
     int *status;
     int withhold;              // test fault: CTA 0 skips its stage 2 (dsv4cu_ctx_inject), 0 = none
+    const float *x;            // [nt][K] fp32 activations, split by the consumer warps
 };
 
 // CTA whose range holds stage q (ranges [S c / G, S (c + 1) / G)).
 DSV4CU_DEV int smv_dense_cta(long long q, long long S, int G) { return (int)(((q + 1) * G + S - 1) / S) - 1; }
 
-// The operand (every token's x, buffer 0) after the split kernel finished.
-// Producer thread.
+// The operand built in shared memory by the consumer warps (every token's x,
+// buffer 0): after the dependency wait (x may come from the previous kernel)
+// each warp splits blocks warp, warp + 16, ... of 32 values into the f16 hi /
+// lo pair and the block's power-of-two factor, the layout smv_consume reads.
 template <int NT>
-DSV4CU_DEV void smv_dense_operand(uint8_t *bufs, SmvSmem<NT> &sm, const SmvDenseParams &p)
+DSV4CU_DEV bool smv_dense_split(uint8_t *bufs, const SmvDenseParams &p, int bstride)
 {
     pdl_wait();
-    int rows[NT];
-    for (int i = 0; i < NT; i++) rows[i] = i < p.nt ? i : 0;
-    smv_put_operand(bufs, p.geom.bstride, 0, sm, p.xh, p.xl, p.xs, p.K, rows, p.nt);
+    constexpr int PER = SMV_MAXK / 32 / SMV_CW;     // blocks per warp per token at most
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nblk = p.K >> 5;
+    for (int i = 0; i < p.nt; i++) {
+        uint8_t *b = bufs + (size_t)i * bstride;
+        uint16_t *hi = reinterpret_cast<uint16_t *>(b), *lo = reinterpret_cast<uint16_t *>(b + 2 * (size_t)p.K);
+        float *fac = reinterpret_cast<float *>(b + 4 * (size_t)p.K);
+        // Every load of this warp's blocks in flight first, then the splits,
+        // eight side by side.
+        constexpr int G = 8;
+        static_assert(PER % G == 0, "split groups");
+        float v[PER];
+#pragma unroll
+        for (int j = 0; j < PER; j++) {
+            const int k = warp + j * SMV_CW;
+            v[j] = k < nblk ? __ldg(p.x + (size_t)i * p.K + k * 32 + lane) : 0.0f;
+        }
+#pragma unroll
+        for (int g0 = 0; g0 < PER; g0 += G) {
+            float vg[G], f[G];
+            bool live[G];
+            uint16_t h[G], l[G];
+#pragma unroll
+            for (int j = 0; j < G; j++) {
+                vg[j] = v[g0 + j];
+                live[j] = warp + (g0 + j) * SMV_CW < nblk;
+            }
+            smv_split32_n<G>(vg, live, h, l, f);
+#pragma unroll
+            for (int j = 0; j < G; j++) {
+                const int k = warp + (g0 + j) * SMV_CW;
+                if (!live[j]) continue;
+                hi[k * 32 + lane] = h[j];
+                lo[k * 32 + lane] = l[j];
+                if (lane == 0) fac[k] = f[j];
+            }
+        }
+    }
+    return true;
 }
 
-// Weights stream from the start: the first ring's worth of stages goes out
-// before the wait for the split kernel, then the operand, then the rest.
-// Producer thread; stage q = (32-row group r, segment sg) with q = r nseg + sg.
+// Weights only: no dependency on the previous kernel, so the stages stream
+// from the start and the next kernel may launch at once (it waits for this
+// one before it reads anything this one writes). Producer thread; stage q =
+// (32-row group r, segment sg) with q = r nseg + sg.
 template <int NT>
 DSV4CU_DEV void smv_dense_producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm, const SmvDenseParams &p)
 {
+    (void)bufs;
+    pdl_trigger();
     const long long S = p.stages, G = gridDim.x;
     const long long b0 = S * blockIdx.x / G, b1 = S * (blockIdx.x + 1) / G;
     const SmvMat m = smv_mat(p.q, &p.wmap, &p.smap);
@@ -75,20 +116,16 @@ DSV4CU_DEV void smv_dense_producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm
     d.combo = 0;
     d.e3 = 1;
     int job = 0, s0 = 0, r = (int)(b0 / p.nseg), sg = (int)(b0 - (long long)r * p.nseg);
-    bool ok = true, pend = true;
+    bool ok = true;
     for (long long q = b0; q < b1 && ok; q++) {
         const bool first = q == b0 || sg == 0, last = q == b1 - 1 || sg == p.nseg - 1;
         if (first) s0 = sg;
         smv_seg_fields(d, m, r * SMV_ROWS, sg);
         d.job = job;
-        d.flags = (first ? SMV_F_FIRST : 0) | (q == b0 ? SMV_F_LOAD : 0) | (last ? SMV_F_FLUSH | SMV_F_LAST : 0);
+        d.flags = (first ? SMV_F_FIRST : 0) | (last ? SMV_F_FLUSH | SMV_F_LAST : 0);
         d.e0 = r;
         d.e1 = s0;
         d.e2 = last ? sg + 1 : 0;
-        if (pend && q - b0 >= p.geom.ns) {
-            smv_dense_operand(bufs, sm, p);
-            pend = false;
-        }
         ok = smv_slot_free(sm, slot, ph, p.status);
         const bool skip = p.withhold && blockIdx.x == 0 && q - b0 == 2;
         if (ok && !skip) smv_put_stage(ring, sm, dr, slot, ph, d, m, r * SMV_ROWS, sg);
@@ -102,9 +139,7 @@ DSV4CU_DEV void smv_dense_producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm
             r++;
         }
     }
-    if (pend && b1 > b0) smv_dense_operand(bufs, sm, p);
     smv_end_marker<NT>(sm, dr, slot, ph, p.status);
-    pdl_trigger();
 }
 
 // y value with the reference's NaN bits (ref_row_nan) when the sum is NaN.
@@ -161,6 +196,11 @@ DSV4CU_DEV void smv_dense_epilogue(const SmvDenseParams &p, const SmvSmem<NT> &s
 struct SmvDensePolicy {
     using Params = SmvDenseParams;
     template <int NT>
+    static DSV4CU_DEV bool consumer_prologue(uint8_t *bufs, SmvSmem<NT> &, const Params &p)
+    {
+        return smv_dense_split<NT>(bufs, p, p.geom.bstride);
+    }
+    template <int NT>
     static DSV4CU_DEV void producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm, const Params &p)
     {
         smv_dense_producer<NT>(ring, bufs, sm, p);
@@ -172,25 +212,6 @@ struct SmvDensePolicy {
     }
 };
 
-// x -> f16 hi / lo operand, one warp per (token, 32-element block).
-__global__ void __launch_bounds__(256) smv_split_kernel(const float *__restrict__ x, int K, int nt,
-                                                       uint16_t *__restrict__ xh, uint16_t *__restrict__ xl,
-                                                       float *__restrict__ xs)
-{
-    pdl_trigger();       // the GEMV streams weights meanwhile
-    pdl_wait();          // x may come from the previous kernel
-    const int lane = threadIdx.x & 31, nblk = K >> 5;
-    const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5);
-    if (gw >= nt * nblk) return;
-    const int t = gw / nblk, b = gw - t * nblk;
-    const size_t i = (size_t)t * K + b * 32 + lane;
-    uint16_t hi, lo;
-    float fac;
-    smv_split32(x[i], hi, lo, fac);
-    xh[i] = hi;
-    xl[i] = lo;
-    if (lane == 0) xs[(size_t)t * nblk + b] = fac;
-}
 
 struct DenseShape {
     int nt, NT, K, nseg, maxparts, groups;
@@ -292,12 +313,8 @@ extern "C" int dsv4cu_gemv_ev(dsv4cu_ctx *ctx, float *y, const float *x, const d
     p.status = ctx->status;
     p.withhold = ctx->inject == DSV4CU_INJECT_WITHHOLD_STAGE;
     ctx->inject = 0;
+    p.x = x;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[0], st));
-    {
-        const long warps = (long)nt * (s.K / 32);
-        DSV4CU_CUDA_TRY(launch_pdl(smv_split_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, st, x, s.K, nt,
-                                   (uint16_t *)p.xh, (uint16_t *)p.xl, (float *)p.xs));
-    }
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
     r = s.NT == 1 ? dense_launch<1>(p, sms, st) : dense_launch<2>(p, sms, st);
     if (r) return r;

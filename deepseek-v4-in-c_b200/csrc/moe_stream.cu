@@ -516,6 +516,11 @@ DSV4CU_DEV void smv_moe_epilogue(const SmvMoeParams &p, const SmvSmem<NT> &sm, i
 struct SmvMoePolicy {
     using Params = SmvMoeParams;
     template <int NT>
+    static DSV4CU_DEV bool consumer_prologue(uint8_t *, SmvSmem<NT> &, const Params &)
+    {
+        return false;    // operands come by bulk copy (smv_moe_operand)
+    }
+    template <int NT>
     static DSV4CU_DEV void producer(uint8_t *ring, uint8_t *bufs, SmvSmem<NT> &sm, const Params &p)
     {
         smv_moe_producer<NT>(ring, bufs, sm, p);

@@ -91,7 +91,9 @@ struct __align__(16) SmvDesc {
     const uint8_t *s8;             // FP8: scale row of this stage's 32 rows
     int bbuf, bk;                  // activation buffer and its row length (K)
     int ntok, e0, e1, e2;          // tokens; policy job coordinates (epilogue)
-    int e3, pad0, pad1, pad2;
+    int e3;
+    int sc_ok;                     // FP8 with 128-column blocks: sc holds the stage's scales
+    uint32_t sc[2];                // byte c: E8M0 scale of 128-column chunk c of the segment
 };
 enum { SMV_F_FLUSH = 1, SMV_F_LAST = 2, SMV_F_FIRST = 4, SMV_F_LOAD = 8 };
 // SMV_F_LOAD on a job's first stage: the job copied its activation operand
@@ -245,7 +247,8 @@ DSV4CU_DEV void smv_consume(uint32_t wsm, uint32_t ssm, uint32_t bsm, uint32_t z
     const int c = boff >> 7, u = (boff >> 4) & 7;
     const int K = d.bk, ntok = d.ntok;
     float fp8s = 0.0f;
-    if constexpr (!FP4) fp8s = e8m0_to_f32(__ldg(d.s8 + kc / d.blk_c));
+    if constexpr (!FP4)
+        fp8s = e8m0_to_f32(d.sc_ok ? (uint8_t)(d.sc[c >> 2] >> (8 * (c & 3))) : __ldg(d.s8 + kc / d.blk_c));
     // Activation of every token of the job for this lane's chunk: one token
     // is loaded once for both tiles, two tokens per tile (the 96-register
     // budget of 576 threads).
@@ -302,19 +305,56 @@ DSV4CU_DEV void smv_split32(float v, uint16_t &hi, uint16_t &lo, float &fac)
     float a = isfinite(v) ? fabsf(v) : 0.0f;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+    // P = 15 - e with a = m 2^e, m in [0.5, 1) (frexp's exponent, read from
+    // the bits: a subnormal a counts its leading zeros), clamped to +-125, so
+    // that 2^P and 2^-P are normal floats and the scalings below are exact
+    // (a product that lands below the normal range rounds as ldexp does).
     int P = 0;
     if (a > 0.0f) {
-        int e;
-        frexpf(a, &e);
+        const uint32_t b = __float_as_uint(a), ef = b >> 23;
+        const int e = ef ? (int)ef - 126 : -117 - __clz((int)(b & 0x7FFFFFu));
         P = min(125, max(-125, 15 - e));
     }
-    const float vs = ldexpf(v, P);
+    const float vs = __fmul_rn(v, __uint_as_float((uint32_t)(P + 127) << 23));
     const __half hh = __float2half_rn(vs);
     const float hf = __half2float(hh);
     const __half lh = isfinite(hf) ? __float2half_rn(vs - hf) : __float2half_rn(0.0f);
     hi = __half_as_ushort(hh);
     lo = __half_as_ushort(lh);
-    fac = ldexpf(1.0f, -P);
+    fac = __uint_as_float((uint32_t)(127 - P) << 23);
+}
+
+// smv_split32 for N blocks of a warp at once (lane holds element `lane` of
+// block j in v[j]; live[j] false: skipped): the N max reductions run side by
+// side, every other step is smv_split32's.
+template <int N>
+DSV4CU_DEV void smv_split32_n(const float (&v)[N], const bool (&live)[N], uint16_t (&hi)[N], uint16_t (&lo)[N],
+                              float (&fac)[N])
+{
+    float a[N];
+#pragma unroll
+    for (int j = 0; j < N; j++) a[j] = isfinite(v[j]) ? fabsf(v[j]) : 0.0f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int j = 0; j < N; j++) a[j] = fmaxf(a[j], __shfl_xor_sync(0xFFFFFFFFu, a[j], o));
+#pragma unroll
+    for (int j = 0; j < N; j++) {
+        if (!live[j]) continue;
+        int P = 0;
+        if (a[j] > 0.0f) {
+            const uint32_t b = __float_as_uint(a[j]), ef = b >> 23;
+            const int e = ef ? (int)ef - 126 : -117 - __clz((int)(b & 0x7FFFFFu));
+            P = min(125, max(-125, 15 - e));
+        }
+        const float vs = __fmul_rn(v[j], __uint_as_float((uint32_t)(P + 127) << 23));
+        const __half hh = __float2half_rn(vs);
+        const float hf = __half2float(hh);
+        const __half lh = isfinite(hf) ? __float2half_rn(vs - hf) : __float2half_rn(0.0f);
+        hi[j] = __half_as_ushort(hh);
+        lo[j] = __half_as_ushort(lh);
+        fac[j] = __uint_as_float((uint32_t)(127 - P) << 23);
+    }
 }
 
 // ---------------------------------------------------------------- producer
@@ -328,6 +368,23 @@ DSV4CU_DEV void smv_seg_fields(SmvDesc &d, const SmvMat &m, int row0, int seg)
     d.blk_c = m.blk_c;
     d.sstr = m.row_bytes <= SMV_SEG ? m.s_ld : SMV_SEG / 16;
     d.s8 = m.fp4 ? nullptr : m.s + (size_t)(row0 / m.blk_r) * m.s_ld;
+    // FP8 scales of the segment's (at most 8) 128-column chunks, loaded by the
+    // producer before it waits for the slot, so the consumers read them from
+    // the descriptor instead of each stage starting with a global load.
+    d.sc_ok = !m.fp4 && m.blk_c == 128;
+    if (d.sc_ok) {
+        const uint8_t *sp = d.s8 + d.kseg0 / 128;
+        const int nc = d.segbytes >> 7;
+        uint32_t lo = 0u, hi = 0u;
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            const uint32_t b = c < nc ? (uint32_t)__ldg(sp + c) : 0u;
+            if (c < 4) lo |= b << (8 * c);
+            else hi |= b << (8 * (c - 4));
+        }
+        d.sc[0] = lo;
+        d.sc[1] = hi;
+    }
 }
 
 // Wait (bounded) for a ring slot to be free; the producer thread, which then
@@ -671,6 +728,9 @@ __global__ void __launch_bounds__(SMV_THREADS, 1) smv_kernel(const __grid_consta
     } else if (warp == SMV_CW + 1) {
         smv_epilogue_loop<NT, P>(sm, p);
     } else {
+        // The policy may build the activation operand in shared memory here
+        // (after its dependency wait); the consumer warps then sync once.
+        if (P::template consumer_prologue<NT>(bufs, sm, p)) asm volatile("bar.sync 1, %0;" ::"n"(SMV_CW * 32) : "memory");
         smv_consumers<NT, P>(ring, bufs, sm, p);
     }
     // Normally the consumers waited for every stage and operand the producer

@@ -113,8 +113,9 @@ int dsv4cu_mmq(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
 size_t dsv4cu_gemv_workspace(const dsv4cu_qmat *m, int nt);
 int dsv4cu_gemv(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
                 int nt, void *stream);
-/* dsv4cu_gemv recording events[0..2] (cudaEvent_t) on the stream: before
- * the activation split, before the streamed GEMV and after it. */
+/* dsv4cu_gemv recording events[0..2] (cudaEvent_t) on the stream: [0] and
+ * [1] before the streamed GEMV (which splits the activations itself), [2]
+ * after it. */
 int dsv4cu_gemv_ev(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m,
                    int nt, void *stream, void **events);
 
