@@ -190,6 +190,282 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
     }
 }
 
+// ---------------------------------------------------------------- tensor-core chunks
+// bf16 KV, head_dim % 64 == 0, n_heads % 16 == 0: the same chunk outputs from
+// the bf16 tensor cores (mma.sync m16n8k16, fp32 accumulation). CTA (chunk of
+// ATM_ROWS selected rows, 16 heads), 8 warps:
+//   gather   the chunk's KV rows into shared memory with cp.async (16-byte
+//            pieces, three commit groups over the columns so the score loop
+//            starts on the first third while the rest arrives); masked or
+//            missing slots are zero rows.
+//   scores   S[16 heads x ROWS] = Q K^T, warp w taking rows [ROWS/8 w, ..).
+//            Q is fp32: it enters as three bf16 terms q = hi + mid + lo, which
+//            carry all 24 significand bits, and KV is bf16 already, so the
+//            products are those of fp32 and only the fp32 accumulation
+//            rounds, as in the fp32 kernel.
+//   softmax  chunk max and exp-sum per head (warp partials through shared
+//            memory); P = exp(S - m) as three bf16 terms again.
+//   output   O[16 x D] = P V, warp w taking columns [D/8 w, ..); V is the same
+//            shared rows read transposed (ldmatrix.trans).
+constexpr int ATM_ROWS = 64;
+static int g_attn_mma = 1;        // 0: the fp32 chunk kernel for every shape (dsv4cu_sparse_attn_set_path)
+constexpr int ATM_HEADS = 16;
+constexpr int ATM_THREADS = 256;
+
+DSV4CU_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+DSV4CU_DEV void cp_async16(void *dst, const void *src)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+DSV4CU_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+DSV4CU_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+DSV4CU_DEV void ldsm_x4(uint32_t (&r)[4], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+DSV4CU_DEV void ldsm_x2(uint32_t (&r)[2], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+DSV4CU_DEV void ldsm_x4_t(uint32_t (&r)[4], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+DSV4CU_DEV void ldsm_x2_t(uint32_t (&r)[2], const void *p)
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(smem_u32(p)));
+}
+
+// D[16x8] += A[16x16] B[16x8], bf16 inputs, fp32 accumulators.
+DSV4CU_DEV void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+                 "{%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Three bf16 terms of an fp32 value, x = t0 + t1 + t2: each term takes the
+// next 8 significand bits of the remainder (the subtractions are exact).
+constexpr int ATM_TERMS = 3;
+DSV4CU_DEV void split3_bf16(float x, uint16_t (&t)[ATM_TERMS])
+{
+    float r = x;
+#pragma unroll
+    for (int i = 0; i < ATM_TERMS; i++) {
+        const __nv_bfloat16 b = __float2bfloat16_rn(r);
+        t[i] = __bfloat16_as_ushort(b);
+        r -= __bfloat162float(b);
+    }
+}
+// Term i of two values as one bf16x2 word.
+DSV4CU_DEV void split3_bf16x2(float x, float y, uint32_t (&w)[ATM_TERMS])
+{
+    uint16_t a[ATM_TERMS], b[ATM_TERMS];
+    split3_bf16(x, a);
+    split3_bf16(y, b);
+#pragma unroll
+    for (int i = 0; i < ATM_TERMS; i++) w[i] = (uint32_t)a[i] | ((uint32_t)b[i] << 16);
+}
+
+template <int D>
+__global__ void __launch_bounds__(ATM_THREADS, 1) attn_mma_kernel(
+    const float *__restrict__ q, const uint16_t *__restrict__ kv, const int *__restrict__ idxs, int H, int topk,
+    float scale, float *__restrict__ pm, float *__restrict__ pl, float *__restrict__ po)
+{
+    constexpr int KS = D + 8;                 // shared row stride in bf16 (odd multiple of 16 bytes)
+    constexpr int PS = ATM_ROWS + 8;
+    constexpr int NW = ATM_THREADS / 32;
+    constexpr int SN = ATM_ROWS / 8 / NW;     // score n tiles per warp
+    constexpr int ON = D / 8 / NW;            // output n tiles per warp
+    static_assert(D % 64 == 0 && SN >= 1 && ON >= 1, "shape");
+    extern __shared__ __align__(16) uint16_t atm_sm[];
+    uint16_t *ks = atm_sm;                            // [ROWS][KS]
+    uint16_t *qt = ks + ATM_ROWS * KS;                // [TERMS][16][KS]
+    uint16_t *pt = qt + ATM_TERMS * ATM_HEADS * KS;   // [TERMS][16][PS]
+    __shared__ int rows[ATM_ROWS];
+    __shared__ float red[NW][ATM_HEADS];
+    __shared__ float s_m[ATM_HEADS];
+
+    const int chunk = blockIdx.x, h0 = blockIdx.y * ATM_HEADS, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, c = lane & 3;
+    if (tid < ATM_ROWS) {
+        const int j = chunk * ATM_ROWS + tid;
+        rows[tid] = j < topk ? __ldg(idxs + j) : -1;
+    }
+    __syncthreads();
+    // gather: three column groups, each one commit group
+    constexpr int P16 = D / 8;                // 16-byte pieces per row
+#pragma unroll
+    for (int grp = 0; grp < 3; grp++) {
+        const int p0 = grp * P16 / 3, p1 = (grp + 1) * P16 / 3, np = p1 - p0;
+        for (int i = tid; i < ATM_ROWS * np; i += ATM_THREADS) {
+            const int r = i / np, p = p0 + (i - r * np), src = rows[r];
+            uint16_t *dst = ks + r * KS + 8 * p;
+            if (src >= 0)
+                cp_async16(dst, kv + (size_t)src * D + 8 * p);
+            else
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        cp_async_commit();
+    }
+    // q (fp32) -> three bf16 terms
+    for (int i = tid; i < ATM_HEADS * D / 2; i += ATM_THREADS) {
+        const int hh = i / (D / 2), cc = 2 * (i - hh * (D / 2));
+        const float2 v = __ldg(reinterpret_cast<const float2 *>(q + (size_t)(h0 + hh) * D + cc));
+        uint32_t w[ATM_TERMS];
+        split3_bf16x2(v.x, v.y, w);
+#pragma unroll
+        for (int t = 0; t < ATM_TERMS; t++)
+            *reinterpret_cast<uint32_t *>(qt + (t * ATM_HEADS + hh) * KS + cc) = w[t];
+    }
+
+    // ---- scores
+    float sacc[SN][4];
+#pragma unroll
+    for (int n = 0; n < SN; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.0f;
+    const int arow = (lane & 7) + 8 * ((lane >> 3) & 1), acol = 8 * (lane >> 4);   // A (x4) lane address
+    const int brow = lane & 7, bcol = 8 * ((lane >> 3) & 1);                       // B (x2) lane address
+    const int r0 = warp * SN * 8;
+    auto score_steps = [&](int k0, int k1) {
+        for (int kk = k0; kk < k1; kk++) {
+            uint32_t a[ATM_TERMS][4];
+#pragma unroll
+            for (int t = 0; t < ATM_TERMS; t++) ldsm_x4(a[t], qt + (t * ATM_HEADS + arow) * KS + 16 * kk + acol);
+#pragma unroll
+            for (int n = 0; n < SN; n++) {
+                uint32_t b[2];
+                ldsm_x2(b, ks + (r0 + 8 * n + brow) * KS + 16 * kk + bcol);
+#pragma unroll
+                for (int t = ATM_TERMS - 1; t >= 0; t--) mma_bf16_16816(sacc[n], a[t], b[0], b[1]);
+            }
+        }
+    };
+    // k steps whose 16 columns lie inside the groups that have arrived
+    constexpr int KST = D / 16;
+    cp_async_wait<2>();
+    __syncthreads();
+    score_steps(0, (P16 / 3) / 2);
+    cp_async_wait<1>();
+    __syncthreads();
+    score_steps((P16 / 3) / 2, (2 * P16 / 3) / 2);
+    cp_async_wait<0>();
+    __syncthreads();
+    score_steps((2 * P16 / 3) / 2, KST);
+
+    // ---- softmax over the chunk: lane holds heads g, g + 8 x rows r0 + 8n + 2c + {0, 1}
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < SN; n++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int r = r0 + 8 * n + 2 * c + (i & 1);
+            const float s = rows[r] >= 0 ? sacc[n][i] * scale : -INFINITY;
+            sacc[n][i] = s;
+            mx[i >> 1] = fmaxf(mx[i >> 1], s);
+        }
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xFFFFFFFFu, mx[j], 1));
+        mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xFFFFFFFFu, mx[j], 2));
+    }
+    if (c == 0) {
+        red[warp][g] = mx[0];
+        red[warp][g + 8] = mx[1];
+    }
+    __syncthreads();
+    if (tid < ATM_HEADS) {
+        float m = red[0][tid];
+#pragma unroll
+        for (int w = 1; w < NW; w++) m = fmaxf(m, red[w][tid]);
+        s_m[tid] = m;
+    }
+    __syncthreads();
+    const float m0 = s_m[g], m1 = s_m[g + 8];
+    float sum[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int n = 0; n < SN; n++) {
+        float e[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float m = (i >> 1) ? m1 : m0;
+            e[i] = (sacc[n][i] != -INFINITY) ? expf(sacc[n][i] - m) : 0.0f;
+            sum[i >> 1] += e[i];
+        }
+        const int col = r0 + 8 * n + 2 * c;
+        uint32_t w0[ATM_TERMS], w1[ATM_TERMS];
+        split3_bf16x2(e[0], e[1], w0);
+        split3_bf16x2(e[2], e[3], w1);
+#pragma unroll
+        for (int t = 0; t < ATM_TERMS; t++) {
+            *reinterpret_cast<uint32_t *>(pt + (t * ATM_HEADS + g) * PS + col) = w0[t];
+            *reinterpret_cast<uint32_t *>(pt + (t * ATM_HEADS + g + 8) * PS + col) = w1[t];
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+        sum[j] += __shfl_xor_sync(0xFFFFFFFFu, sum[j], 1);
+        sum[j] += __shfl_xor_sync(0xFFFFFFFFu, sum[j], 2);
+    }
+    if (c == 0) {
+        red[warp][g] = sum[0];
+        red[warp][g + 8] = sum[1];
+    }
+    __syncthreads();
+    if (tid < ATM_HEADS) {
+        float l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) l += red[w][tid];
+        pm[(size_t)chunk * H + h0 + tid] = s_m[tid];
+        pl[(size_t)chunk * H + h0 + tid] = l;
+    }
+
+    // ---- output: warp w -> columns [8 ON w, 8 ON (w + 1))
+    float oacc[ON][4];
+#pragma unroll
+    for (int n = 0; n < ON; n++) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.0f;
+    const int c0 = warp * ON * 8;
+    const int vrow = (lane & 7) + 8 * ((lane >> 3) & 1), vcol = 8 * (lane >> 4);   // V (x4.trans) lane address
+#pragma unroll
+    for (int kk = 0; kk < ATM_ROWS / 16; kk++) {
+        uint32_t a[ATM_TERMS][4];
+#pragma unroll
+        for (int t = 0; t < ATM_TERMS; t++) ldsm_x4(a[t], pt + (t * ATM_HEADS + arow) * PS + 16 * kk + acol);
+#pragma unroll
+        for (int n = 0; n + 1 < ON; n += 2) {
+            uint32_t b[4];
+            ldsm_x4_t(b, ks + (16 * kk + vrow) * KS + c0 + 8 * n + vcol);
+#pragma unroll
+            for (int t = ATM_TERMS - 1; t >= 0; t--) {
+                mma_bf16_16816(oacc[n], a[t], b[0], b[1]);
+                mma_bf16_16816(oacc[n + 1], a[t], b[2], b[3]);
+            }
+        }
+        if (ON & 1) {
+            uint32_t b[2];
+            ldsm_x2_t(b, ks + (16 * kk + vrow) * KS + c0 + 8 * (ON - 1));
+#pragma unroll
+            for (int t = ATM_TERMS - 1; t >= 0; t--) mma_bf16_16816(oacc[ON - 1], a[t], b[0], b[1]);
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < ON; n++) {
+        const int col = c0 + 8 * n + 2 * c;
+        *reinterpret_cast<float2 *>(po + ((size_t)chunk * H + h0 + g) * D + col) = make_float2(oacc[n][0], oacc[n][1]);
+        *reinterpret_cast<float2 *>(po + ((size_t)chunk * H + h0 + g + 8) * D + col) =
+            make_float2(oacc[n][2], oacc[n][3]);
+    }
+}
+
 // Block (h, column slice): the head's chunk factors f_c = exp(m_c - m) and the
 // denominator are formed once in shared memory (denominator summed in chunk
 // order, in double), then each thread combines its columns in chunk order.
@@ -271,6 +547,23 @@ int attn_run(float *o, const float *q, const void *kv, int kv_bf16, const float 
     float *pl = (float *)p;
     p += dsv4cu_align256((size_t)nch * H * 4);
     float *po = (float *)p;
+    // Tensor-core chunks for the bf16 cache at the model's head widths.
+    if (kv_bf16 && (D == 576 || D == 512) && H % ATM_HEADS == 0 && ((uintptr_t)q & 15) == 0 &&
+        ((uintptr_t)kv & 15) == 0 && g_attn_mma) {
+        const int nc = (topk + ATM_ROWS - 1) / ATM_ROWS;
+        const size_t smem =
+            ((size_t)ATM_ROWS * (D + 8) + (size_t)ATM_TERMS * ATM_HEADS * (D + 8 + ATM_ROWS + 8)) * 2;
+        auto kern = D == 576 ? attn_mma_kernel<576> : attn_mma_kernel<512>;
+        static SmemLimit lim_m[2];
+        DSV4CU_CUDA_TRY(smem_limit(lim_m[D == 576], (const void *)kern, (int)smem));
+        kern<<<dim3(nc, H / ATM_HEADS), ATM_THREADS, smem, st>>>(q, (const uint16_t *)kv, idxs, H, topk, scale, pm,
+                                                                   pl, po);
+        DSV4CU_LAUNCH_CHECK();
+        attn_combine_kernel<<<dim3(H, (D + ATT_COMB_COLS - 1) / ATT_COMB_COLS), ATT_COMB_COLS, 0, st>>>(
+            pm, pl, po, sink, H, D, nc, o);
+        DSV4CU_LAUNCH_CHECK();
+        return DSV4CU_OK;
+    }
     const bool vec = D % 4 == 0 && ((uintptr_t)q & 15) == 0 && ((uintptr_t)kv & (kv_bf16 ? 7 : 15)) == 0;
     const size_t DA = (size_t)((D + 3) & ~3);
     const size_t smem = ((size_t)ATT_CH * (DA + 8) + (size_t)ATT_HG * DA + ATT_HG * ATT_CH) * sizeof(float);
@@ -294,6 +587,14 @@ int attn_run(float *o, const float *q, const void *kv, int kv_bf16, const float 
 }  // namespace dsv4cu
 
 using namespace dsv4cu;
+
+extern "C" int dsv4cu_sparse_attn_set_path(int path)
+{
+    if (path != DSV4CU_ATTN_AUTO && path != DSV4CU_ATTN_FP32)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "sparse_attn_set_path: unknown path %d", path);
+    g_attn_mma = path == DSV4CU_ATTN_AUTO;
+    return DSV4CU_OK;
+}
 
 extern "C" int dsv4cu_sparse_attn(dsv4cu_ctx *ctx, float *o, const float *q, const void *kv, int kv_bf16,
                                   const float *sink, const int *idxs, int h, int d, int topk, float scale,

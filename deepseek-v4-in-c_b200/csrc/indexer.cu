@@ -348,6 +348,266 @@ static int indexer_dmma_launch(float *out, const double *qd, const float *qscale
     return DSV4CU_OK;
 }
 
+// ------------------------------------------------------------ FP8 keys, int8 tensor cores
+// The same exact dots (every scale a power of two), computed in integers on
+// the int8 tensor cores (mma.sync m16n8k32 s8 -> s32). With q = e4m3 x 2^eq
+// and k = e4m3 x 2^ek, each element is an integer I below 2^18 in units of
+// 2^-9 times its scale; written as three signed base-128 digits
+// I = d0 + 128 d1 + 16384 d2 (|d0|, |d1| <= 127, |d2| <= 14, all with the
+// sign of I), the dot is
+//   sum_k Iq Ik = sum over digit pairs (a, b) of 128^(a+b) D_ab,
+//   D_ab = sum_k dq_a dk_b           (one int8 GEMM per digit pair).
+// The five weights 128^L are folded in two int32 accumulators by Horner's
+// rule: hi = D_(L=2) + 128 (D_(L=3) + 128 D_(L=4)) and lo = D_(L=0) + 128
+// D_(L=1); with 128 elements |hi| < 4.8e8 and |lo| < 2^30, and the dot
+// 16384 hi + lo < 2^43 is an exact double, scaled by 2^(eq + ek - 18).
+// Integer sums do not depend on the order of the terms, so the k order
+// inside a fragment is free: lane c of a quad takes the 32 contiguous
+// elements [32c, 32c + 32) of each row, two 16-byte loads. The head sum per
+// position, the NaN handling (a NaN byte in q or in a 16-position task sends
+// it to the exact replay, whose NaN dots fail "dot > 0" as in the reference)
+// and the output rounding are those of the other kernels.
+constexpr int IDXL_WARPS = 16;
+constexpr int IDXL_ZERO = -100000;   // exponent marker of a zero scale
+static int g_idx_limbs = 1;          // 0: the FP64 tensor-core kernel (dsv4cu_indexer_set_path)
+
+// The e4m3 byte b as digits (bytes 0-2 of the word, int8 each).
+DSV4CU_DEV uint32_t idxl_digits(uint32_t b)
+{
+    const uint32_t E = (b >> 3) & 15u, m = b & 7u;
+    uint32_t I = E ? (8u + m) << (E - 1u) : m;
+    if ((b & 0x7Fu) == 0x7Fu) I = 0u;   // NaN: never used (the task is replayed)
+    int d0 = (int)(I & 127u), d1 = (int)((I >> 7) & 127u), d2 = (int)(I >> 14);
+    if (b & 0x80u) {
+        d0 = -d0;
+        d1 = -d1;
+        d2 = -d2;
+    }
+    return ((uint32_t)d0 & 0xFFu) | (((uint32_t)d1 & 0xFFu) << 8) | (((uint32_t)d2 & 0xFFu) << 16);
+}
+
+DSV4CU_DEV bool idxl_has_nan(uint32_t w) { return __vcmpeq4(w & 0x7F7F7F7Fu, 0x7F7F7F7Fu) != 0u; }
+
+// Four e4m3 bytes -> digit words l0, l1, l2 (byte i of l_a = digit a of byte i).
+DSV4CU_DEV void idxl_split(const uint32_t *tbl, uint32_t w, uint32_t &l0, uint32_t &l1, uint32_t &l2)
+{
+    const uint32_t t0 = tbl[w & 0xFFu], t1 = tbl[(w >> 8) & 0xFFu], t2 = tbl[(w >> 16) & 0xFFu], t3 = tbl[w >> 24];
+    const uint32_t x = __byte_perm(t0, t1, 0x5140), y = __byte_perm(t2, t3, 0x5140);
+    l0 = __byte_perm(x, y, 0x5410);
+    l1 = __byte_perm(x, y, 0x7632);
+    l2 = __byte_perm(__byte_perm(t0, t1, 0x0062), __byte_perm(t2, t3, 0x0062), 0x5410);
+}
+
+// D[16x8] += A[16x32] B[32x8] in int8 -> int32; lane (g = lane / 4, c = lane % 4):
+// a = rows g, g + 8 x k {4c..4c+3, 16+4c..16+4c+3}, b = k {4c.., 16+4c..} x column g,
+// d = rows g, g + 8 x columns 2c, 2c + 1.
+DSV4CU_DEV void imma_16832(int (&d)[4], const uint32_t (&a)[4], uint2 b)
+{
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+
+DSV4CU_DEV int idxl_exp(float s)
+{
+    const uint32_t u = __float_as_uint(s) & 0x7FFFFFFFu;
+    return u ? (int)(u >> 23) - 127 : IDXL_ZERO;
+}
+
+// The exact replay of one position with q read from its e4m3 bytes.
+DSV4CU_DEV void idxl_replay(const uint8_t *q8, const float *qscale, const KeysFP8 &keys, int t, double *dot)
+{
+    const int lane = threadIdx.x & 31, l = lane & 15, half = lane >> 4;
+    double kr[IDXM_D / 16];
+#pragma unroll
+    for (int j = 0; j < IDXM_D / 16; j++) kr[j] = keys.load(t, 16 * j + l);
+    for (int h0 = 0; h0 < IDXM_H; h0 += 2) {
+        const int h = h0 + half;
+        const float qs = __ldg(qscale + h);
+        double p = 0.0;
+#pragma unroll
+        for (int j = 0; j < IDXM_D / 16; j++)
+            p = __fma_rn((double)__fmul_rn(e4m3_to_f32(__ldg(q8 + h * IDXM_D + 16 * j + l)), qs), kr[j], p);
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 4));
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 8));
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 1));
+        p = __dadd_rn(p, __shfl_down_sync(0xFFFFFFFFu, p, 2));
+        if (l == 0) dot[h] = p;
+    }
+}
+
+__global__ void __launch_bounds__(IDXL_WARPS * 32, 1) indexer_limb_kernel(
+    float *__restrict__ out, const uint8_t *__restrict__ q8, const float *__restrict__ qscale,
+    const float *__restrict__ w, int n_pos, float scale, KeysFP8 keys)
+{
+    extern __shared__ __align__(16) unsigned char idxl_sm[];
+    // q digits in fragment order: entry ((a * 4 + s) * 8 + nt) * 32 + L holds
+    // digit a of head 8 nt + L / 4, elements 32 (L % 4) + 8 s + {0..3 | 4..7}.
+    uint2 *qfrag = reinterpret_cast<uint2 *>(idxl_sm);
+    double *dots = reinterpret_cast<double *>(idxl_sm + 3 * 4 * 8 * 32 * sizeof(uint2));
+    __shared__ uint32_t tbl[256];
+    __shared__ int qexp[IDXM_H];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < 256; i += blockDim.x) tbl[i] = idxl_digits((uint32_t)i);
+    int okq = 1;
+    if (tid < IDXM_H) {
+        const float s = __ldg(qscale + tid);
+        okq = idx_pow2_scale(s);
+        qexp[tid] = idxl_exp(s);
+    }
+    __syncthreads();
+    for (int i = tid; i < 4 * 8 * 32; i += blockDim.x) {
+        const int L = i & 31, nt = (i >> 5) & 7, s = i >> 8;
+        const uint8_t *src = q8 + (8 * nt + (L >> 2)) * IDXM_D + 32 * (L & 3) + 8 * s;
+        uint32_t v[2];
+#pragma unroll
+        for (int hw = 0; hw < 2; hw++)
+            v[hw] = (uint32_t)__ldg(src + 4 * hw) | ((uint32_t)__ldg(src + 4 * hw + 1) << 8) |
+                    ((uint32_t)__ldg(src + 4 * hw + 2) << 16) | ((uint32_t)__ldg(src + 4 * hw + 3) << 24);
+        okq &= !idxl_has_nan(v[0]) && !idxl_has_nan(v[1]);
+        uint32_t a[3], b[3];
+        idxl_split(tbl, v[0], a[0], a[1], a[2]);
+        idxl_split(tbl, v[1], b[0], b[1], b[2]);
+#pragma unroll
+        for (int d = 0; d < 3; d++) qfrag[(d * 4 + s) * 256 + nt * 32 + L] = make_uint2(a[d], b[d]);
+    }
+    const int q_ok = __syncthreads_and(okq);
+    double *dw = dots + warp * IDXM_POS * IDXM_DSTRIDE;
+    const int g = lane >> 2, c = lane & 3;
+
+    for (int task = blockIdx.x * IDXL_WARPS + warp; task * IDXM_POS < n_pos; task += gridDim.x * IDXL_WARPS) {
+        const int t0 = task * IDXM_POS;
+        const int tl = t0 + (lane & 15);
+        // rows g and g + 8 of the task, elements [32c, 32c + 32)
+        uint4 kw[2][2];
+        bool bad = false;
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int t = t0 + g + 8 * r;
+            if (t < n_pos) {
+                const uint4 *p = reinterpret_cast<const uint4 *>(keys.k8 + (size_t)t * keys.ld + 32 * c);
+                kw[r][0] = __ldg(p);
+                kw[r][1] = __ldg(p + 1);
+            } else {
+                kw[r][0] = kw[r][1] = make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++)
+                bad |= idxl_has_nan(kw[r][hh].x) | idxl_has_nan(kw[r][hh].y) | idxl_has_nan(kw[r][hh].z) |
+                       idxl_has_nan(kw[r][hh].w);
+        }
+        const bool ok = q_ok && !__any_sync(0xFFFFFFFFu, bad) &&
+                        __all_sync(0xFFFFFFFFu, tl >= n_pos || idx_pow2_scale(__ldg(keys.ks + tl)));
+        if (ok) {
+            // A[digit][k step][register]: k step s takes words 2s (registers 0, 1)
+            // and 2s + 1 (registers 2, 3) of rows g (0, 2) and g + 8 (1, 3).
+            uint32_t A[3][4][4];
+#pragma unroll
+            for (int r = 0; r < 2; r++)
+#pragma unroll
+                for (int q = 0; q < 8; q++) {
+                    const uint4 v = kw[r][q >> 2];
+                    const uint32_t word = (q & 3) == 0 ? v.x : (q & 3) == 1 ? v.y : (q & 3) == 2 ? v.z : v.w;
+                    const int s = q >> 1, reg = r + 2 * (q & 1);
+                    idxl_split(tbl, word, A[0][s][reg], A[1][s][reg], A[2][s][reg]);
+                }
+            int ek[2];
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const int t = t0 + g + 8 * r;
+                ek[r] = t < n_pos ? idxl_exp(__ldg(keys.ks + t)) : IDXL_ZERO;
+            }
+            // Heads in two halves of 32 (n tiles 4 hb .. 4 hb + 3): 16 accumulators.
+#pragma unroll 1
+            for (int hb = 0; hb < 2; hb++) {
+                const uint2 *qb = qfrag + hb * 4 * 32 + lane;
+                int acc[4][4];
+                auto zero = [&]() {
+#pragma unroll
+                    for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) acc[nt][i] = 0;
+                };
+                auto times128 = [&]() {
+#pragma unroll
+                    for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) acc[nt][i] *= 128;
+                };
+                auto mac = [&](int ka, int qa) {   // acc += (key digit ka) x (q digit qa), all 128 elements
+#pragma unroll
+                    for (int s = 0; s < 4; s++)
+#pragma unroll
+                        for (int nt = 0; nt < 4; nt++) imma_16832(acc[nt], A[ka][s], qb[(qa * 4 + s) * 256 + nt * 32]);
+                };
+                zero();
+                mac(2, 2);
+                times128();
+                mac(1, 2);
+                mac(2, 1);
+                times128();
+                mac(0, 2);
+                mac(1, 1);
+                mac(2, 0);
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        dw[(g + 8 * (i >> 1)) * IDXM_DSTRIDE + 32 * hb + 8 * nt + 2 * c + (i & 1)] =
+                            (double)acc[nt][i] * 16384.0;
+                zero();
+                mac(0, 1);
+                mac(1, 0);
+                times128();
+                mac(0, 0);
+#pragma unroll
+                for (int nt = 0; nt < 4; nt++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int h = 32 * hb + 8 * nt + 2 * c + (i & 1);
+                        double *slot = dw + (g + 8 * (i >> 1)) * IDXM_DSTRIDE + h;
+                        const int eq = qexp[h], e = ek[i >> 1];
+                        const double v = __dadd_rn(*slot, (double)acc[nt][i]);   // 16384 hi + lo, exact
+                        *slot = (eq == IDXL_ZERO || e == IDXL_ZERO)
+                                    ? 0.0
+                                    : v * __hiloint2double((eq + e - 18 + 1023) << 20, 0);
+                    }
+            }
+        } else {
+            for (int p = 0; p < IDXM_POS && t0 + p < n_pos; p++)
+                idxl_replay(q8, qscale, keys, t0 + p, dw + p * IDXM_DSTRIDE);
+        }
+        __syncwarp();
+        if (lane < IDXM_POS && t0 + lane < n_pos) {
+            const double *dd = dw + lane * IDXM_DSTRIDE;
+            double total = 0.0;
+            for (int h = 0; h < IDXM_H; h++) {
+                const double d = dd[h];
+                if (d > 0.0) total = __dadd_rn(total, __dmul_rn(d, (double)__ldg(w + h)));
+            }
+            out[t0 + lane] = __fmul_rn((float)total, scale);
+        }
+        __syncwarp();
+    }
+}
+
+static int indexer_limb_launch(float *out, const uint8_t *q8, const float *qscale, const float *w, int n_pos,
+                               KeysFP8 keys, cudaStream_t st)
+{
+    const size_t smem = (size_t)3 * 4 * 8 * 32 * sizeof(uint2) +
+                        (size_t)IDXL_WARPS * IDXM_POS * IDXM_DSTRIDE * sizeof(double);
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)indexer_limb_kernel, (int)smem));
+    int blocks = device_sms();
+    const int need = (n_pos + IDXL_WARPS * IDXM_POS - 1) / (IDXL_WARPS * IDXM_POS);
+    if (blocks > need) blocks = need;
+    indexer_limb_kernel<<<blocks, IDXL_WARPS * 32, smem, st>>>(out, q8, qscale, w, n_pos,
+                                                               indexer_scale(IDXM_H, IDXM_D), keys);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}
+
 // q (fp32, or e4m3 * per-head scale in float) -> double, once per call.
 __global__ void indexer_q_kernel(double *qd, const float *q, const uint8_t *q8, const float *qscale, int H, int D)
 {
@@ -457,6 +717,14 @@ extern "C" int dsv4cu_indexer_score(float *out, const float *q, const float *kv,
     return indexer_launch(out, qd, weights, n_heads, head_dim, n_pos, k, st);
 }
 
+extern "C" int dsv4cu_indexer_set_path(int path)
+{
+    if (path != DSV4CU_INDEXER_AUTO && path != DSV4CU_INDEXER_FP64)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "indexer_set_path: unknown path %d", path);
+    g_idx_limbs = path == DSV4CU_INDEXER_AUTO;
+    return DSV4CU_OK;
+}
+
 extern "C" int dsv4cu_indexer_score_fp8(float *out, const uint8_t *q8, const float *q_scale, const uint8_t *k8,
                                         const float *k_scale, const float *weights, int n_heads, int head_dim,
                                         int n_pos, int k_stride, void *stream)
@@ -465,13 +733,17 @@ extern "C" int dsv4cu_indexer_score_fp8(float *out, const uint8_t *q8, const flo
     if (r) return r;
     if (k_stride < head_dim) return dsv4cu_set_error(DSV4CU_ERR_ARG, "indexer_fp8: k_stride < head_dim");
     if (n_pos == 0) return DSV4CU_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    KeysFP8 k{k8, k_scale, k_stride};
+    // int8 tensor-core dots where the key rows allow 16-byte loads.
+    if (n_heads == IDXM_H && head_dim == IDXM_D && k_stride % 16 == 0 && ((uintptr_t)k8 & 15u) == 0u &&
+        g_idx_limbs)
+        return indexer_limb_launch(out, q8, q_scale, weights, n_pos, k, st);
     double *qd = idx_qbuf((size_t)n_heads * head_dim);
     if (!qd) return dsv4cu_set_error(DSV4CU_ERR_NOMEM, "indexer: q buffer");
-    cudaStream_t st = (cudaStream_t)stream;
     const int n = n_heads * head_dim;
     indexer_q_kernel<<<(n + 255) / 256, 256, 0, st>>>(qd, nullptr, q8, q_scale, n_heads, head_dim);
     DSV4CU_LAUNCH_CHECK();
-    KeysFP8 k{k8, k_scale, k_stride};
     if (n_heads == IDXM_H && head_dim == IDXM_D)
         return indexer_dmma_launch(out, qd, q_scale, weights, n_pos, k, st);
     return indexer_launch(out, qd, weights, n_heads, head_dim, n_pos, k, st);

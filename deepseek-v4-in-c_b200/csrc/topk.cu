@@ -3,10 +3,10 @@
 // Reference: dsv4_topk (src/10_compute/dsv4_topk.c:76-112), whose definition is
 // the scan topk_ref in tests/unit/test_indexer.c:20-34. Scores compare as
 // floats, so -0.0 and +0.0 tie; k is clamped to n. The reference aborts above
-// k = 1024 (dsv4_topk.c:80-84); this kernel has no such bound below its
-// shared-memory sort limit (TOPK_MAX_SORT).
+// k = 1024 (dsv4_topk.c:80-84); these kernels have no such bound below
+// TOPK_MAX_SORT.
 //
-// One CTA of 1024 threads:
+// Small n (below TOPK_CL x 1024 keys), one CTA of 1024 threads:
 //   1. key(i) = order-preserving uint32 of score i (larger score -> larger key),
 //      staged in shared memory when the keys fit (n <= ~47K for k <= 2048).
 //   2. Radix select, 3 passes of 11, 11 and 10 bits from the top: the k-th
@@ -17,6 +17,7 @@
 //      indices win the tie).
 //   4. Bitonic sort of (key, ~index) descending: score descending, then index
 //      ascending - exactly the reference output order.
+// Large n: the cluster select and the rank kernel further down.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -256,37 +257,40 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(const float *__restr
 }
 
 
-// Cluster form (n up to TOPK_CL * ~40K keys): the same steps over a cluster of
-// TOPK_CL CTAs. CTA c stages keys [c * span, (c + 1) * span) in its shared
-// memory; each radix pass builds per-CTA histograms, and after a cluster
-// barrier every CTA sums all of them through distributed shared memory and
-// picks the same digit (identical inputs, identical arithmetic). The first
-// pass also cuts the picks into TOPK_CL ranges of whole top digits, about
-// k / TOPK_CL picks each; the compaction sends every (key, ~index) pick to the
-// CTA of its range, and each CTA sorts its range and writes it at the range's
-// output offset. (The unique (key, ~index) order makes the arrival order
-// within a range irrelevant.)
+// Cluster form for large n (TOPK_CL CTAs, n up to TOPK_CL x ~50K keys), two
+// launches:
+//  select  CTA c of the cluster stages keys [c * span, (c + 1) * span) in its
+//          shared memory. Radix select over 8-bit digits from the top: each
+//          pass builds per-CTA histograms (one shared atomic per distinct
+//          digit and warp), and after a cluster barrier every CTA sums the
+//          TOPK_CL histograms through distributed shared memory and picks the
+//          same digit (identical inputs, identical arithmetic). The passes
+//          stop early once the digit's whole bucket is taken. Every key whose
+//          selected prefix is above the threshold is picked, and of those
+//          equal to it the first `need` in index order (the reference's tie
+//          rule); the k picks (key, ~index) go to a workspace in any order.
+//  rank    k / 32 CTAs: pick p's output position is the number of picks
+//          whose (key, ~index) is larger - score descending, then index
+//          ascending, exactly the reference order. Each CTA ranks 32 picks,
+//          its 32 warps each counting over k / 32 of the others, so the
+//          ordering runs on most of the GPU instead of on one cluster.
 constexpr int TOPK_CL = 8;
+constexpr int TOPK_RANK_PICKS = 32;
 namespace cg = cooperative_groups;
 
-__global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float *__restrict__ scores, int n, int k,
-                                                                    int *__restrict__ out, int sort_n, int span)
+DSV4CU_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+DSV4CU_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+__global__ void __launch_bounds__(TOPK_THREADS) topk_select_kernel(const float *__restrict__ scores, int n, int k,
+                                                                   unsigned long long *__restrict__ picks, int span)
 {
-    __shared__ int hist[2][TOPK_BINS];
+    __shared__ int hist[2][256];
     __shared__ int sh_warp[32];
     __shared__ int warp_gt[32], warp_eq[32];
-    __shared__ int cta_cnt[2];                    // this CTA's keys > T and == T
+    __shared__ int cta_cnt[2];                    // this CTA's keys above / equal to the threshold
     __shared__ uint32_t s_prefix, s_mask;
-    __shared__ int s_need;
-    // The picks are sorted in 8 key ranges, one per CTA: ranges of top
-    // (pass-0) digits holding about k / 8 picks each. s_owner[d] = the CTA
-    // sorting digit d's picks, s_own_off[r] = where CTA r's run starts in the
-    // output, own_cnt = picks received so far (other CTAs add remotely).
-    __shared__ uint8_t s_owner[TOPK_BINS];
-    __shared__ int s_own_off[TOPK_CL + 1];
-    __shared__ int own_cnt;
-    extern __shared__ unsigned long long sel[];   // [sort_n] (this CTA's range), then keys [span]
-    uint32_t *skeys = (uint32_t *)(sel + sort_n);
+    __shared__ int s_need, s_done;
+    extern __shared__ uint32_t skeys[];           // [span]
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = (int)cluster.block_rank();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -306,65 +310,47 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
             if (i < cnt) skeys[i] = float_order_key(v[u]);
         }
     }
-    if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = k; own_cnt = 0; }
-    if (tid <= TOPK_CL) s_own_off[tid] = k;
+    if (tid == 0) { s_prefix = 0u; s_mask = 0u; s_need = k; s_done = 0; }
 
-    for (int pass = 0; pass < 3; pass++) {
-        const int shift = topk_shift[pass], width = topk_width[pass], nb = 1 << width;
+    for (int pass = 0; pass < 4; pass++) {
+        const int shift = 24 - 8 * pass;
         int *hb = hist[pass & 1];
-        for (int i = tid; i < TOPK_BINS; i += blockDim.x) hb[i] = 0;
+        if (tid < 256) hb[tid] = 0;
         __syncthreads();
         const uint32_t prefix = s_prefix, mask = s_mask;
-        for (int i = tid; i < cnt; i += blockDim.x) {
-            const uint32_t key = skeys[i];
-            if ((key & mask) == prefix) atomicAdd(&hb[(key >> shift) & (nb - 1)], 1);
+        for (int b = 0; b < cnt; b += TOPK_THREADS) {
+            const int i = b + tid;
+            int bin = -1;
+            if (i < cnt) {
+                const uint32_t key = skeys[i];
+                if ((key & mask) == prefix) bin = (int)((key >> shift) & 255u);
+            }
+            const unsigned grp = __match_any_sync(0xFFFFFFFFu, bin);
+            if (bin >= 0 && lane == __ffs(grp) - 1) atomicAdd(&hb[bin], __popc(grp));
         }
         cluster.sync();                           // every CTA's histogram is complete
-        const int dA = nb - 1 - 2 * tid, dB = dA - 1;
-        // all remote loads in flight before the sums
-        int ra[TOPK_CL], rb[TOPK_CL];
+        // thread t < 256 holds digit 255 - t: the scan runs from the top digit down
+        int cd = 0;
+        if (tid < 256) {
+            int rv[TOPK_CL];
 #pragma unroll
-        for (int r = 0; r < TOPK_CL; r++) {
-            const int *rh = cluster.map_shared_rank(hb, r);
-            ra[r] = dA >= 0 ? rh[dA] : 0;
-            rb[r] = dB >= 0 ? rh[dB] : 0;
-        }
-        int cA = 0, cB = 0;
+            for (int r = 0; r < TOPK_CL; r++) rv[r] = cluster.map_shared_rank(hb, r)[255 - tid];
 #pragma unroll
-        for (int r = 0; r < TOPK_CL; r++) {
-            cA += ra[r];
-            cB += rb[r];
+            for (int r = 0; r < TOPK_CL; r++) cd += rv[r];
         }
-        const int need = s_need;
+        const int need = s_need;                  // read before the scan's barriers; written after them
         int above;
-        block_exscan(cA + cB, &above, sh_warp);
-        if (pass == 0) {
-            // Output positions [above, above + c) belong to digit d (keys in
-            // higher digits come first); its picks go to CTA above * 8 / k.
-            const int startB = above + cA;
-            if (dA >= 0 && cA > 0 && above < k) {
-                const int r = min(TOPK_CL - 1, (int)((long)above * TOPK_CL / k));
-                s_owner[dA] = (uint8_t)r;
-                atomicMin(&s_own_off[r], above);
-            }
-            if (dB >= 0 && cB > 0 && startB < k) {
-                const int r = min(TOPK_CL - 1, (int)((long)startB * TOPK_CL / k));
-                s_owner[dB] = (uint8_t)r;
-                atomicMin(&s_own_off[r], startB);
-            }
-        }
-        if (above < need && need <= above + cA + cB) {
-            const bool inA = need <= above + cA;
-            const int d = inA ? dA : dB;
-            s_need = need - above - (inA ? 0 : cA);
-            s_prefix = prefix | ((uint32_t)d << shift);
-            s_mask = mask | ((uint32_t)(nb - 1) << shift);
+        block_exscan(cd, &above, sh_warp);
+        if (cd > 0 && above < need && need <= above + cd) {
+            s_need = need - above;
+            s_prefix = prefix | ((uint32_t)(255 - tid) << shift);
+            s_mask = mask | (0xFFu << shift);
+            s_done = need - above == cd;          // the whole bucket is taken
         }
         __syncthreads();
-        if (pass == 0 && tid == 0)
-            for (int r = TOPK_CL - 1; r >= 0; r--) s_own_off[r] = min(s_own_off[r], s_own_off[r + 1]);
+        if (s_done) break;                        // same decision in every CTA of the cluster
     }
-    const uint32_t T = s_prefix;
+    const uint32_t T = s_prefix, M = s_mask;
     const int need_eq = s_need;
 
     // counts of this CTA's slice, per warp in index order
@@ -374,7 +360,7 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
     int cgt = 0, ceq = 0;
     for (int b = w0; b < w1; b += 32) {
         const int i = b + lane;
-        const uint32_t key = i < w1 ? skeys[i] : 0u;
+        const uint32_t key = i < w1 ? (skeys[i] & M) : 0u;
         cgt += __popc(__ballot_sync(0xFFFFFFFFu, i < w1 && key > T));
         ceq += __popc(__ballot_sync(0xFFFFFFFFu, i < w1 && key == T));
     }
@@ -404,58 +390,86 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_cluster_kernel(const float 
         }
     }
     cluster.sync();                               // every CTA's counts are complete
-    int ebase = 0;
-    for (int r = 0; r < rank; r++) ebase += cluster.map_shared_rank(cta_cnt, r)[1];
-    // Every key > T and the first need_eq keys == T in index order are
-    // picked; each pick goes to the CTA that sorts its key range (a slot
-    // from that CTA's counter, one remote atomic per owner and warp).
-    int weq = ebase + warp_eq[warp];
+    int gbase = 0, ebase = 0;
+    for (int r = 0; r < rank; r++) {
+        const int *rc = cluster.map_shared_rank(cta_cnt, r);
+        gbase += rc[0];
+        ebase += rc[1];
+    }
+    cluster_arrive();                             // remote reads done; the wait comes before exit
+    // Picks above the threshold fill [0, k - need_eq) in index order; the
+    // first need_eq equal ones fill [k - need_eq, k).
+    int wgt = gbase + warp_gt[warp], weq = ebase + warp_eq[warp];
     const unsigned lt = (1u << lane) - 1u;
     for (int b = w0; b < w1; b += 32) {
         const int i = b + lane;
-        const uint32_t key = i < w1 ? skeys[i] : 0u;
+        const uint32_t full = i < w1 ? skeys[i] : 0u, key = full & M;
         const bool gt = i < w1 && key > T, eq = i < w1 && key == T;
-        const unsigned me = __ballot_sync(0xFFFFFFFFu, eq);
-        const bool pick = gt || (eq && weq + __popc(me & lt) < need_eq);
+        const unsigned mg = __ballot_sync(0xFFFFFFFFu, gt), me = __ballot_sync(0xFFFFFFFFu, eq);
+        const unsigned long long v = ((unsigned long long)full << 32) | (0xFFFFFFFFu - (uint32_t)(g0 + i));
+        if (gt) picks[wgt + __popc(mg & lt)] = v;
+        if (eq) {
+            const int r = weq + __popc(me & lt);
+            if (r < need_eq) picks[k - need_eq + r] = v;
+        }
+        wgt += __popc(mg);
         weq += __popc(me);
-        const int owner = pick ? (int)s_owner[key >> 21] : -1;
-        const unsigned grp = __match_any_sync(0xFFFFFFFFu, owner);
-        const int leader = __ffs(grp) - 1, before = __popc(grp & lt);
-        int base = 0;
-        if (pick && lane == leader) base = atomicAdd(cluster.map_shared_rank(&own_cnt, owner), __popc(grp));
-        base = __shfl_sync(0xFFFFFFFFu, base, leader);
-        if (pick)
-            cluster.map_shared_rank(sel, owner)[base + before] =
-                ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)(g0 + i));
     }
-    cluster.sync();                               // every CTA holds the picks of its range
-    const int m = s_own_off[rank + 1] - s_own_off[rank];
-    if (m <= 0) return;
-    int sn = 2;
-    while (sn < m) sn <<= 1;
-    for (int i = m + tid; i < sn; i += blockDim.x) sel[i] = 0ull;   // padding sorts last
+    pdl_trigger();
+    cluster_wait();
+}
+
+__global__ void __launch_bounds__(TOPK_THREADS) topk_rank_kernel(const unsigned long long *__restrict__ picks, int k,
+                                                                 int *__restrict__ out)
+{
+    extern __shared__ unsigned long long pv[];   // [k]
+    __shared__ int part[32][33];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    pdl_wait();
+    for (int i = tid; i < k; i += blockDim.x) pv[i] = picks[i];
     __syncthreads();
-    bitonic_desc(sel, sn);
-    for (int i = tid; i < m; i += blockDim.x)
-        out[s_own_off[rank] + i] = (int)(0xFFFFFFFFu - (uint32_t)(sel[i] & 0xFFFFFFFFull));
+    const int p = blockIdx.x * TOPK_RANK_PICKS + lane;
+    const unsigned long long v = p < k ? pv[p] : ~0ull;
+    const int qs = (k + 31) / 32, q0 = min(k, warp * qs), q1 = min(k, q0 + qs);
+    int c0 = 0, c1 = 0, c2 = 0, c3 = 0;
+    int q = q0;
+    for (; q + 4 <= q1; q += 4) {
+        c0 += pv[q] > v;
+        c1 += pv[q + 1] > v;
+        c2 += pv[q + 2] > v;
+        c3 += pv[q + 3] > v;
+    }
+    for (; q < q1; q++) c0 += pv[q] > v;
+    part[warp][lane] = (c0 + c1) + (c2 + c3);
+    __syncthreads();
+    if (warp == 0 && p < k) {
+        int r = 0;
+#pragma unroll 8
+        for (int w = 0; w < 32; w++) r += part[w][lane];
+        out[r] = (int)(0xFFFFFFFFu - (uint32_t)(v & 0xFFFFFFFFull));
+    }
 }
 
 // Shared memory above the static arrays: the sort buffer and, when they fit,
 // the n keys.
 constexpr size_t TOPK_DYN_SMEM = 200 * 1024;
 
-int topk_run(int *idx, const float *scores, int n, int k, cudaStream_t st)
+int topk_run(dsv4cu_ctx *ctx, int *idx, const float *scores, int n, int k, cudaStream_t st)
 {
     int sort_n = 1;
     while (sort_n < k) sort_n <<= 1;
     if (sort_n < 2) sort_n = 2;
     const size_t sort_b = (size_t)sort_n * sizeof(unsigned long long);
-    // Cluster form when each CTA's slice fits beside the sort buffer.
+    // Cluster form when each CTA's slice fits in shared memory.
     const int span = ((n + TOPK_CL - 1) / TOPK_CL + 31) & ~31;
-    if (n >= TOPK_CL * 1024 && sort_b + (size_t)span * 4 <= TOPK_DYN_SMEM - 16 * 1024) {
-        const size_t smem = sort_b + (size_t)span * 4;
-        static SmemLimit lim_cl;
-        DSV4CU_CUDA_TRY(smem_limit(lim_cl, (const void *)topk_cluster_kernel, (int)smem));
+    if (ctx && n >= TOPK_CL * 1024 && (size_t)span * 4 <= TOPK_DYN_SMEM) {
+        void *ws = nullptr;
+        int r = dsv4cu_ws_get(ctx, (size_t)k * sizeof(unsigned long long), &ws);
+        if (r) return r;
+        unsigned long long *picks = (unsigned long long *)ws;
+        const size_t smem = (size_t)span * 4;
+        static SmemLimit lim_sel, lim_rank;
+        DSV4CU_CUDA_TRY(smem_limit(lim_sel, (const void *)topk_select_kernel, (int)smem));
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(TOPK_CL);
         cfg.blockDim = dim3(TOPK_THREADS);
@@ -468,7 +482,20 @@ int topk_run(int *idx, const float *scores, int n, int k, cudaStream_t st)
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        DSV4CU_CUDA_TRY(cudaLaunchKernelEx(&cfg, topk_cluster_kernel, scores, n, k, idx, sort_n, span));
+        DSV4CU_CUDA_TRY(cudaLaunchKernelEx(&cfg, topk_select_kernel, scores, n, k, picks, span));
+        const size_t rsmem = (size_t)k * sizeof(unsigned long long);
+        DSV4CU_CUDA_TRY(smem_limit(lim_rank, (const void *)topk_rank_kernel, (int)rsmem));
+        cudaLaunchConfig_t rc = {};
+        rc.gridDim = dim3((k + TOPK_RANK_PICKS - 1) / TOPK_RANK_PICKS);
+        rc.blockDim = dim3(TOPK_THREADS);
+        rc.dynamicSmemBytes = rsmem;
+        rc.stream = st;
+        cudaLaunchAttribute ra[1];
+        ra[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        ra[0].val.programmaticStreamSerializationAllowed = 1;
+        rc.attrs = ra;
+        rc.numAttrs = 1;
+        DSV4CU_CUDA_TRY(cudaLaunchKernelEx(&rc, topk_rank_kernel, (const unsigned long long *)picks, k, idx));
         return DSV4CU_OK;
     }
     const bool in_smem = sort_b + (size_t)n * 4 <= TOPK_DYN_SMEM;
@@ -487,10 +514,9 @@ using namespace dsv4cu;
 
 extern "C" int dsv4cu_topk(dsv4cu_ctx *ctx, int *idx, const float *scores, int n, int k, void *stream)
 {
-    (void)ctx;
     if (k > n) k = n;
     if (k <= 0 || n <= 0) return DSV4CU_OK;
     if (!idx || !scores) return dsv4cu_set_error(DSV4CU_ERR_ARG, "topk: NULL argument");
     if (k > TOPK_MAX_SORT) return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "topk: k=%d exceeds %d", k, TOPK_MAX_SORT);
-    return topk_run(idx, scores, n, k, (cudaStream_t)stream);
+    return topk_run(ctx, idx, scores, n, k, (cudaStream_t)stream);
 }

@@ -109,6 +109,8 @@ def lib() -> C.CDLL:
             "dsv4cu_mat_gemm_ev": (i, [vp, vp, vp, vp, i, i, vp, vp]),
             "dsv4cu_indexer_score": (i, [vp, vp, vp, vp, i, i, i, vp]),
             "dsv4cu_indexer_score_fp8": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]),
+            "dsv4cu_indexer_set_path": (i, [i]),
+            "dsv4cu_sparse_attn_set_path": (i, [i]),
             "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
             "dsv4cu_sparse_attn": (i, [vp, vp, vp, vp, i, vp, vp, i, i, i, f, vp]),
             "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
@@ -566,6 +568,20 @@ class Device:
                                               self.ptr(k8), self.ptr(ks), self.ptr(w), n_heads,
                                               head_dim, n_pos, k_stride, self.stream()),
               "dsv4cu_indexer_score_fp8")
+
+    INDEXER_PATH = {"auto": 0, "fp64": 1}
+
+    def indexer_set_path(self, path: str):
+        """Kernel of the exact FP8 score (dsv4cu_indexer_set_path): "auto" (int8
+        tensor-core digits) or "fp64" (FP64 tensor cores)."""
+        check(self.L.dsv4cu_indexer_set_path(self.INDEXER_PATH[path]), "dsv4cu_indexer_set_path")
+
+    ATTN_PATH = {"auto": 0, "fp32": 1}
+
+    def sparse_attn_set_path(self, path: str):
+        """Chunk kernel of the sparse attention (dsv4cu_sparse_attn_set_path):
+        "auto" (bf16 tensor cores where the shape allows) or "fp32"."""
+        check(self.L.dsv4cu_sparse_attn_set_path(self.ATTN_PATH[path]), "dsv4cu_sparse_attn_set_path")
 
     def topk(self, idx, scores, n, k):
         check(self.L.dsv4cu_topk(self.ctx, self.ptr(idx), self.ptr(scores), n, k, self.stream()),

@@ -408,6 +408,14 @@ int dsv4cu_indexer_score_fp8(float *out, const uint8_t *q8, const float *q_scale
                              const float *weights, int n_heads, int head_dim,
                              int n_pos, int k_stride, void *stream);
 
+/* Which kernel dsv4cu_indexer_score_fp8 uses for 64 heads x 128 when every
+ * scale is a power of two (both give the same bits): AUTO = exact integer
+ * dots on the int8 tensor cores (key rows 16-byte aligned), FP64 = exact
+ * dots on the FP64 tensor cores. Process-wide; for comparisons. */
+#define DSV4CU_INDEXER_AUTO 0
+#define DSV4CU_INDEXER_FP64 1
+int dsv4cu_indexer_set_path(int path);
+
 /* The MoE layer over nt tokens at once (prefill, up to 16384 tokens): the
  * reference's prefill union path (src/80_prefill/dsv4_prefill_union.c:30-66,
  * dsv4_prefill_experts.c:23-77, dsv4_prefill_union_run.c:109-121, shared
@@ -443,6 +451,14 @@ int dsv4cu_topk(dsv4cu_ctx *ctx, int *idx, const float *scores, int n, int k,
 int dsv4cu_sparse_attn(dsv4cu_ctx *ctx, float *o, const float *q, const void *kv,
                        int kv_bf16, const float *sink, const int *idxs, int h,
                        int d, int topk, float scale, void *stream);
+
+/* Chunk kernel of dsv4cu_sparse_attn: AUTO = bf16 tensor cores (mma.sync,
+ * q and the weights as three bf16 terms each) for a bf16 cache with head_dim
+ * 512 or 576 and n_heads % 16 == 0, the fp32 kernel otherwise; FP32 = the
+ * fp32 kernel always. Process-wide; for comparisons. */
+#define DSV4CU_ATTN_AUTO 0
+#define DSV4CU_ATTN_FP32 1
+int dsv4cu_sparse_attn_set_path(int path);
 
 /* dsv4cu_sparse_attn without a context and without any allocation. No
  * counterpart in the reference (whose dsv4_sparse_attn takes a caller scratch

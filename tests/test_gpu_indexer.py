@@ -102,28 +102,65 @@ def test_config4_full_fp8_score_topk(dev, orc):
     assert np.array_equal(idx, orc.topk(want, 2048))
 
 
-@pytest.mark.parametrize("case", ["keys-mixed", "q-nonpow2", "zero-scale"])
-def test_config4_fp8_scale_forms(dev, orc, case):
-    """The FP8 path uses FP64 tensor cores only where every scale is a power of
-    two (exact there) and replays the reference's fma chains elsewhere: both
-    must give the reference's bits, in the same launch."""
-    rng = np.random.default_rng({"keys-mixed": 31, "q-nonpow2": 32, "zero-scale": 33}[case])
+@pytest.mark.parametrize("path", ["auto", "fp64"])
+@pytest.mark.parametrize("case", ["keys-mixed", "q-nonpow2", "zero-scale", "nan-key", "nan-q", "stride-144",
+                                  "stride-136"])
+def test_config4_fp8_scale_forms(dev, orc, case, path):
+    """The FP8 path computes exact dots on tensor cores (int8 digit GEMMs, or
+    FP64) only where every scale is a power of two and no byte is NaN, and
+    replays the reference's fma chains elsewhere; key rows that are not 16-byte
+    aligned take the FP64 kernel. All must give the reference's bits, in the
+    same launch."""
+    rng = np.random.default_rng(31 + ["keys-mixed", "q-nonpow2", "zero-scale", "nan-key", "nan-q", "stride-144",
+                                      "stride-136"].index(case))
     n = 1000
     k8, ks = quant_rows(rng.standard_normal((n, 128)).astype(np.float32))
     q8, qs = quant_rows(rng.standard_normal((64, 128)).astype(np.float32))
+    stride = None
     if case == "keys-mixed":
         bad = rng.random(n) < 0.05                     # a few 16-position tasks fall back
         ks = np.where(bad, ks * np.float32(1.2345), ks).astype(np.float32)
     elif case == "q-nonpow2":
         qs = (qs * np.float32(0.7771)).astype(np.float32)
-    else:
+    elif case == "zero-scale":
         ks[::7] = 0.0
+    elif case == "nan-key":
+        k8[rng.integers(0, n, 6), rng.integers(0, 128, 6)] = np.uint8(0x7F)
+        k8[rng.integers(0, n, 3), rng.integers(0, 128, 3)] = np.uint8(0xFF)
+    elif case == "nan-q":
+        q8[5, 77] = np.uint8(0xFF)
     w = rng.standard_normal(64).astype(np.float32)
-    got = dev_score8(dev, q8, qs, k8, ks, w)
     kf = (pack.E4M3[k8] * ks[:, None]).astype(np.float32)
     qf = (pack.E4M3[q8] * qs[:, None]).astype(np.float32)
+    if case.startswith("stride-"):
+        stride = int(case[7:])
+        padded = rng.integers(0, 256, (n, stride)).astype(np.uint8)   # garbage beyond head_dim
+        padded[:, :128] = k8
+        k8 = padded
+    dev.indexer_set_path(path)
+    try:
+        got = dev_score8(dev, q8, qs, k8, ks, w, stride)
+    finally:
+        dev.indexer_set_path("auto")
     want = orc.indexer_score(qf, kf, w)
     assert np.array_equal(bits(got), bits(want))
+
+
+def test_config4_int8_and_fp64_kernels_agree(dev):
+    """Full config-4 size: the int8-digit kernel and the FP64 tensor-core
+    kernel compute the same exact dots, hence the same score bits."""
+    rng = np.random.default_rng(77)
+    k8, ks = quant_rows(rng.standard_normal((32768, 128)).astype(np.float32) * 3.0)
+    q8, qs = quant_rows(rng.standard_normal((64, 128)).astype(np.float32))
+    w = rng.standard_normal(64).astype(np.float32)
+    a = dev_score8(dev, q8, qs, k8, ks, w)
+    dev.indexer_set_path("fp64")
+    try:
+        b = dev_score8(dev, q8, qs, k8, ks, w)
+    finally:
+        dev.indexer_set_path("auto")
+    assert np.array_equal(bits(a), bits(b))
+    assert np.count_nonzero(a) > 1000
 
 
 def test_topk_golden_and_kat(dev, host):
@@ -232,3 +269,37 @@ def test_attn_config4_full(dev, orc, bf16):
     t.cuda.synchronize()
     want = orc.sparse_attn(q, kv, sink, idx, scale)
     assert att_err(o.cpu().numpy(), want) <= ATT_TOL
+
+
+@pytest.mark.parametrize("D,H,T,qscale", [(576, 64, 2048, 1.0), (576, 16, 1000, 3.0), (512, 32, 2176, 1.0),
+                                          (576, 64, 64, 0.3)])
+@pytest.mark.parametrize("path", ["auto", "fp32"])
+def test_attn_tensor_core_chunks(dev, orc, D, H, T, qscale, path):
+    """The bf16 tensor-core chunk kernel (fp32 q and weights as two bf16 terms
+    each) against the reference: fp32 q off the bf16 grid, peaky softmax
+    (qscale 3), a ragged last chunk, a fully masked 64-slot chunk and scattered
+    masked slots; the fp32 kernel on the same inputs."""
+    t = __import__("torch")
+    rng = np.random.default_rng(D + H + T)
+    N = 8192
+    kv = pack.bf16_round(rng.standard_normal((N, D)).astype(np.float32))
+    q = (rng.standard_normal((H, D)) * qscale).astype(np.float32)
+    sink = rng.standard_normal(H).astype(np.float32)
+    idx = rng.choice(N, T, replace=False).astype(np.int32)
+    idx[::13] = -1
+    if T >= 256:
+        idx[128:192] = -1
+    scale = np.float32(1 / np.sqrt(D))
+    o = t.empty((H, D), dtype=t.float32, device="cuda")
+    kvd = t.from_numpy(kv).cuda().to(t.bfloat16)
+    dev.sparse_attn_set_path(path)
+    try:
+        dev.sparse_attn(o, t.from_numpy(q).cuda(), kvd, 1, t.from_numpy(sink).cuda(), t.from_numpy(idx).cuda(),
+                        H, D, T, float(scale))
+        t.cuda.synchronize()
+    finally:
+        dev.sparse_attn_set_path("auto")
+    want = orc.sparse_attn(q, kv, sink, idx, scale)
+    got = o.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert att_err(got, want) <= ATT_TOL
