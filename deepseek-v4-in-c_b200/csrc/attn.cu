@@ -16,10 +16,13 @@
 // contract is a relative-error tolerance, not bit identity.
 #include <math.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "ctx.h"
 
 namespace dsv4cu {
+namespace cg = cooperative_groups;
 
 constexpr int ATT_CH = 32;    // selected rows per CTA
 constexpr int ATT_HG = 16;    // heads per CTA
@@ -191,26 +194,36 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
 }
 
 // ---------------------------------------------------------------- tensor-core chunks
-// bf16 KV, head_dim % 64 == 0, n_heads % 16 == 0: the same chunk outputs from
-// the bf16 tensor cores (mma.sync m16n8k16, fp32 accumulation). CTA (chunk of
-// ATM_ROWS selected rows, 16 heads), 8 warps:
-//   gather   the chunk's KV rows into shared memory with cp.async (16-byte
-//            pieces, three commit groups over the columns so the score loop
-//            starts on the first third while the rest arrives); masked or
-//            missing slots are zero rows.
-//   scores   S[16 heads x ROWS] = Q K^T, warp w taking rows [ROWS/8 w, ..).
-//            Q is fp32: it enters as three bf16 terms q = hi + mid + lo, which
-//            carry all 24 significand bits, and KV is bf16 already, so the
-//            products are those of fp32 and only the fp32 accumulation
-//            rounds, as in the fp32 kernel.
-//   softmax  chunk max and exp-sum per head (warp partials through shared
-//            memory); P = exp(S - m) as three bf16 terms again.
-//   output   O[16 x D] = P V, warp w taking columns [D/8 w, ..); V is the same
+// bf16 KV, head_dim 512 or 576, n_heads % 16 == 0: the whole attention on the
+// bf16 tensor cores (mma.sync m16n8k16, fp32 accumulation), one thread-block
+// cluster of CL CTAs per group of 16 heads, 8 warps per CTA:
+//   gather   CTA r of the cluster takes the 64-row sub-chunks r, r + CL, ...
+//            of the selected rows; each is copied into shared memory with
+//            cp.async (16-byte pieces), the next one while the current one is
+//            used; masked or missing slots are zero rows.
+//   scores   S[16 heads x 64 rows] = Q K^T split over k: warp w takes the
+//            k steps w, w + 8, ... for all 64 rows, its slice of Q held in
+//            registers as mma fragments for the whole kernel; the 8 partial
+//            tiles are added in warp order through shared memory. Q is fp32:
+//            it enters as three bf16 terms q = hi + mid + lo, which carry all
+//            24 significand bits, and KV is bf16 already, so the products are
+//            those of fp32 and only the fp32 accumulation rounds, as in the
+//            fp32 kernel.
+//   softmax  online over the CTA's sub-chunks, 16 threads per head: running
+//            max and exp-sum, the running output rescaled by exp(m_old -
+//            m_new); the weights P = exp(S - m) as three bf16 terms again.
+//   output   O[16 x D] += P V, warp w taking columns [D/8 w, ..); V is the same
 //            shared rows read transposed (ldmatrix.trans).
+//   combine  every CTA stores its partial output columns and (max, exp-sum)
+//            straight into the shared memory of the CTA that owns those
+//            columns (CTA r owns [D/CL r, D/CL (r + 1))); after one cluster
+//            barrier each CTA forms the global max, the denominator with the
+//            sink (in double, rank order) and writes its columns - no remote
+//            loads, no partials in global memory.
 constexpr int ATM_ROWS = 64;
-static int g_attn_mma = 1;        // 0: the fp32 chunk kernel for every shape (dsv4cu_sparse_attn_set_path)
 constexpr int ATM_HEADS = 16;
 constexpr int ATM_THREADS = 256;
+static int g_attn_mma = 1;        // 0: fp32 kernel always, 2: 8-CTA clusters (dsv4cu_sparse_attn_set_path)
 
 DSV4CU_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -277,192 +290,258 @@ DSV4CU_DEV void split3_bf16x2(float x, float y, uint32_t (&w)[ATM_TERMS])
     for (int i = 0; i < ATM_TERMS; i++) w[i] = (uint32_t)a[i] | ((uint32_t)b[i] << 16);
 }
 
-template <int D>
+template <int D, int CL>
 __global__ void __launch_bounds__(ATM_THREADS, 1) attn_mma_kernel(
-    const float *__restrict__ q, const uint16_t *__restrict__ kv, const int *__restrict__ idxs, int H, int topk,
-    float scale, float *__restrict__ pm, float *__restrict__ pl, float *__restrict__ po)
+    const float *__restrict__ q, const uint16_t *__restrict__ kv, const int *__restrict__ idxs,
+    const float *__restrict__ sink, int H, int topk, float scale, float *__restrict__ o)
 {
     constexpr int KS = D + 8;                 // shared row stride in bf16 (odd multiple of 16 bytes)
     constexpr int PS = ATM_ROWS + 8;
     constexpr int NW = ATM_THREADS / 32;
-    constexpr int SN = ATM_ROWS / 8 / NW;     // score n tiles per warp
+    constexpr int KST = D / 16;               // k steps
+    constexpr int KPW = (KST + NW - 1) / NW;  // k steps per warp (the last ones may be missing)
     constexpr int ON = D / 8 / NW;            // output n tiles per warp
-    static_assert(D % 64 == 0 && SN >= 1 && ON >= 1, "shape");
-    extern __shared__ __align__(16) uint16_t atm_sm[];
-    uint16_t *ks = atm_sm;                            // [ROWS][KS]
-    uint16_t *qt = ks + ATM_ROWS * KS;                // [TERMS][16][KS]
-    uint16_t *pt = qt + ATM_TERMS * ATM_HEADS * KS;   // [TERMS][16][PS]
-    __shared__ int rows[ATM_ROWS];
-    __shared__ float red[NW][ATM_HEADS];
-    __shared__ float s_m[ATM_HEADS];
-
-    const int chunk = blockIdx.x, h0 = blockIdx.y * ATM_HEADS, tid = threadIdx.x;
-    const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, c = lane & 3;
-    if (tid < ATM_ROWS) {
-        const int j = chunk * ATM_ROWS + tid;
-        rows[tid] = j < topk ? __ldg(idxs + j) : -1;
-    }
-    __syncthreads();
-    // gather: three column groups, each one commit group
     constexpr int P16 = D / 8;                // 16-byte pieces per row
-#pragma unroll
-    for (int grp = 0; grp < 3; grp++) {
-        const int p0 = grp * P16 / 3, p1 = (grp + 1) * P16 / 3, np = p1 - p0;
-        for (int i = tid; i < ATM_ROWS * np; i += ATM_THREADS) {
-            const int r = i / np, p = p0 + (i - r * np), src = rows[r];
-            uint16_t *dst = ks + r * KS + 8 * p;
+    constexpr int OC = D / CL;                // output columns owned by each rank
+    static_assert(D % 64 == 0 && ATM_ROWS == 64 && ON >= 1 && OC % 2 == 0, "shape");
+    extern __shared__ __align__(16) uint16_t atm_sm[];
+    uint16_t *kb = atm_sm;                                              // [2][ROWS][KS] row buffers
+    float *spart = reinterpret_cast<float *>(kb + 2 * ATM_ROWS * KS);   // [NW][16][ROWS] partial scores
+    uint16_t *pt = reinterpret_cast<uint16_t *>(spart);                // [TERMS][16][PS] weights (after the sum)
+    float *stage = spart + NW * ATM_HEADS * ATM_ROWS;                   // [CL][16][OC] pushed partial outputs
+    __shared__ int rows[2][ATM_ROWS];
+    __shared__ float run_m[ATM_HEADS], run_l[ATM_HEADS], s_alpha[ATM_HEADS];
+    __shared__ float st_m[CL][ATM_HEADS], st_l[CL][ATM_HEADS], fac[CL][ATM_HEADS], s_inv[ATM_HEADS];
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int h0 = blockIdx.y * ATM_HEADS, tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5, g = lane >> 2, c = lane & 3;
+    const int nsub = (topk + ATM_ROWS - 1) / ATM_ROWS;
+    const int nmine = rank < nsub ? (nsub - 1 - rank) / CL + 1 : 0;
+
+    auto load_rows = [&](int it) {            // row indices of sub-chunk `it` into rows[it & 1]
+        if (tid < ATM_ROWS) {
+            const int jj = (rank + CL * it) * ATM_ROWS + tid;
+            rows[it & 1][tid] = jj < topk ? __ldg(idxs + jj) : -1;
+        }
+    };
+    auto gather = [&](int it) {               // needs rows[it & 1] behind a barrier
+        const int buf = it & 1;
+        uint16_t *dstb = kb + buf * ATM_ROWS * KS;
+        for (int i = tid; i < ATM_ROWS * P16; i += ATM_THREADS) {
+            const int r = i / P16, p = i - r * P16, src = rows[buf][r];
+            uint16_t *dst = dstb + r * KS + 8 * p;
             if (src >= 0)
                 cp_async16(dst, kv + (size_t)src * D + 8 * p);
             else
                 *reinterpret_cast<uint4 *>(dst) = make_uint4(0u, 0u, 0u, 0u);
         }
         cp_async_commit();
+    };
+    if (nmine > 0) load_rows(0);
+    if (nmine > 1) load_rows(1);
+    if (tid < ATM_HEADS) {
+        run_m[tid] = -INFINITY;
+        run_l[tid] = 0.0f;
     }
-    // q (fp32) -> three bf16 terms
-    for (int i = tid; i < ATM_HEADS * D / 2; i += ATM_THREADS) {
-        const int hh = i / (D / 2), cc = 2 * (i - hh * (D / 2));
-        const float2 v = __ldg(reinterpret_cast<const float2 *>(q + (size_t)(h0 + hh) * D + cc));
-        uint32_t w[ATM_TERMS];
-        split3_bf16x2(v.x, v.y, w);
+    // this warp's Q slice as A fragments, three bf16 terms: k step w + 8j,
+    // registers (row g, k 2c), (row g + 8, k 2c), (row g, k 2c + 8), (row g + 8, k 2c + 8)
+    uint32_t qa[KPW][ATM_TERMS][4];
+    {
+        float2 v[KPW][4];
 #pragma unroll
-        for (int t = 0; t < ATM_TERMS; t++)
-            *reinterpret_cast<uint32_t *>(qt + (t * ATM_HEADS + hh) * KS + cc) = w[t];
-    }
-
-    // ---- scores
-    float sacc[SN][4];
+        for (int j = 0; j < KPW; j++) {
+            const int kk = warp + NW * j;
 #pragma unroll
-    for (int n = 0; n < SN; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.0f;
-    const int arow = (lane & 7) + 8 * ((lane >> 3) & 1), acol = 8 * (lane >> 4);   // A (x4) lane address
-    const int brow = lane & 7, bcol = 8 * ((lane >> 3) & 1);                       // B (x2) lane address
-    const int r0 = warp * SN * 8;
-    auto score_steps = [&](int k0, int k1) {
-        for (int kk = k0; kk < k1; kk++) {
-            uint32_t a[ATM_TERMS][4];
-#pragma unroll
-            for (int t = 0; t < ATM_TERMS; t++) ldsm_x4(a[t], qt + (t * ATM_HEADS + arow) * KS + 16 * kk + acol);
-#pragma unroll
-            for (int n = 0; n < SN; n++) {
-                uint32_t b[2];
-                ldsm_x2(b, ks + (r0 + 8 * n + brow) * KS + 16 * kk + bcol);
-#pragma unroll
-                for (int t = ATM_TERMS - 1; t >= 0; t--) mma_bf16_16816(sacc[n], a[t], b[0], b[1]);
+            for (int rr = 0; rr < 4; rr++) {
+                const int hh = g + 8 * (rr & 1), col = 16 * kk + 2 * c + 8 * (rr >> 1);
+                v[j][rr] = kk < KST ? __ldg(reinterpret_cast<const float2 *>(q + (size_t)(h0 + hh) * D + col))
+                                    : make_float2(0.f, 0.f);
             }
         }
-    };
-    // k steps whose 16 columns lie inside the groups that have arrived
-    constexpr int KST = D / 16;
-    cp_async_wait<2>();
+#pragma unroll
+        for (int j = 0; j < KPW; j++)
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++) {
+                uint32_t w[ATM_TERMS];
+                split3_bf16x2(v[j][rr].x, v[j][rr].y, w);
+#pragma unroll
+                for (int t = 0; t < ATM_TERMS; t++) qa[j][t][rr] = w[t];
+            }
+    }
     __syncthreads();
-    score_steps(0, (P16 / 3) / 2);
-    cp_async_wait<1>();
-    __syncthreads();
-    score_steps((P16 / 3) / 2, (2 * P16 / 3) / 2);
-    cp_async_wait<0>();
-    __syncthreads();
-    score_steps((2 * P16 / 3) / 2, KST);
+    if (nmine > 0) gather(0);
 
-    // ---- softmax over the chunk: lane holds heads g, g + 8 x rows r0 + 8n + 2c + {0, 1}
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int n = 0; n < SN; n++)
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int r = r0 + 8 * n + 2 * c + (i & 1);
-            const float s = rows[r] >= 0 ? sacc[n][i] * scale : -INFINITY;
-            sacc[n][i] = s;
-            mx[i >> 1] = fmaxf(mx[i >> 1], s);
-        }
-#pragma unroll
-    for (int j = 0; j < 2; j++) {
-        mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xFFFFFFFFu, mx[j], 1));
-        mx[j] = fmaxf(mx[j], __shfl_xor_sync(0xFFFFFFFFu, mx[j], 2));
-    }
-    if (c == 0) {
-        red[warp][g] = mx[0];
-        red[warp][g + 8] = mx[1];
-    }
-    __syncthreads();
-    if (tid < ATM_HEADS) {
-        float m = red[0][tid];
-#pragma unroll
-        for (int w = 1; w < NW; w++) m = fmaxf(m, red[w][tid]);
-        s_m[tid] = m;
-    }
-    __syncthreads();
-    const float m0 = s_m[g], m1 = s_m[g + 8];
-    float sum[2] = {0.0f, 0.0f};
-#pragma unroll
-    for (int n = 0; n < SN; n++) {
-        float e[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float m = (i >> 1) ? m1 : m0;
-            e[i] = (sacc[n][i] != -INFINITY) ? expf(sacc[n][i] - m) : 0.0f;
-            sum[i >> 1] += e[i];
-        }
-        const int col = r0 + 8 * n + 2 * c;
-        uint32_t w0[ATM_TERMS], w1[ATM_TERMS];
-        split3_bf16x2(e[0], e[1], w0);
-        split3_bf16x2(e[2], e[3], w1);
-#pragma unroll
-        for (int t = 0; t < ATM_TERMS; t++) {
-            *reinterpret_cast<uint32_t *>(pt + (t * ATM_HEADS + g) * PS + col) = w0[t];
-            *reinterpret_cast<uint32_t *>(pt + (t * ATM_HEADS + g + 8) * PS + col) = w1[t];
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < 2; j++) {
-        sum[j] += __shfl_xor_sync(0xFFFFFFFFu, sum[j], 1);
-        sum[j] += __shfl_xor_sync(0xFFFFFFFFu, sum[j], 2);
-    }
-    if (c == 0) {
-        red[warp][g] = sum[0];
-        red[warp][g + 8] = sum[1];
-    }
-    __syncthreads();
-    if (tid < ATM_HEADS) {
-        float l = 0.0f;
-#pragma unroll
-        for (int w = 0; w < NW; w++) l += red[w][tid];
-        pm[(size_t)chunk * H + h0 + tid] = s_m[tid];
-        pl[(size_t)chunk * H + h0 + tid] = l;
-    }
-
-    // ---- output: warp w -> columns [8 ON w, 8 ON (w + 1))
     float oacc[ON][4];
 #pragma unroll
     for (int n = 0; n < ON; n++) oacc[n][0] = oacc[n][1] = oacc[n][2] = oacc[n][3] = 0.0f;
+    const int arow = (lane & 7) + 8 * ((lane >> 3) & 1), acol = 8 * (lane >> 4);   // A (x4) / V (x4.trans)
+    const int brow = (lane & 7) + 8 * (lane >> 4), bcol = 8 * ((lane >> 3) & 1);   // B (x4, two n tiles)
     const int c0 = warp * ON * 8;
-    const int vrow = (lane & 7) + 8 * ((lane >> 3) & 1), vcol = 8 * (lane >> 4);   // V (x4.trans) lane address
+    const int rh = tid >> 4, rr0 = (tid & 15) * 4;                                 // softmax: head, 4 rows
+
+    for (int it = 0; it < nmine; it++) {
+        const int buf = it & 1;
+        const uint16_t *kbuf = kb + buf * ATM_ROWS * KS;
+        if (it + 1 < nmine) {
+            gather(it + 1);                   // into the buffer the previous sub-chunk used
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        // ---- partial scores over this warp's k steps, all 64 rows
+        {
+            float sacc[8][4];
 #pragma unroll
-    for (int kk = 0; kk < ATM_ROWS / 16; kk++) {
-        uint32_t a[ATM_TERMS][4];
+            for (int n = 0; n < 8; n++) sacc[n][0] = sacc[n][1] = sacc[n][2] = sacc[n][3] = 0.0f;
 #pragma unroll
-        for (int t = 0; t < ATM_TERMS; t++) ldsm_x4(a[t], pt + (t * ATM_HEADS + arow) * PS + 16 * kk + acol);
+            for (int j = 0; j < KPW; j++) {
+                const int kk = warp + NW * j;
+                if (kk < KST) {
 #pragma unroll
-        for (int n = 0; n + 1 < ON; n += 2) {
-            uint32_t b[4];
-            ldsm_x4_t(b, ks + (16 * kk + vrow) * KS + c0 + 8 * n + vcol);
+                    for (int np = 0; np < 4; np++) {
+                        uint32_t b[4];
+                        ldsm_x4(b, kbuf + (16 * np + brow) * KS + 16 * kk + bcol);
 #pragma unroll
-            for (int t = ATM_TERMS - 1; t >= 0; t--) {
-                mma_bf16_16816(oacc[n], a[t], b[0], b[1]);
-                mma_bf16_16816(oacc[n + 1], a[t], b[2], b[3]);
+                        for (int t = ATM_TERMS - 1; t >= 0; t--) {
+                            mma_bf16_16816(sacc[2 * np], qa[j][t], b[0], b[1]);
+                            mma_bf16_16816(sacc[2 * np + 1], qa[j][t], b[2], b[3]);
+                        }
+                    }
+                }
+            }
+            float *sw = spart + warp * ATM_HEADS * ATM_ROWS;
+#pragma unroll
+            for (int n = 0; n < 8; n++) {
+                *reinterpret_cast<float2 *>(sw + g * ATM_ROWS + 8 * n + 2 * c) = make_float2(sacc[n][0], sacc[n][1]);
+                *reinterpret_cast<float2 *>(sw + (g + 8) * ATM_ROWS + 8 * n + 2 * c) =
+                    make_float2(sacc[n][2], sacc[n][3]);
             }
         }
-        if (ON & 1) {
-            uint32_t b[2];
-            ldsm_x2_t(b, ks + (16 * kk + vrow) * KS + c0 + 8 * (ON - 1));
+        __syncthreads();
+        // ---- scores (warp order), online softmax: thread -> head rh, rows rr0 .. rr0 + 3
+        float sv[4];
+        {
+            float4 acc4 = *reinterpret_cast<const float4 *>(spart + rh * ATM_ROWS + rr0);
 #pragma unroll
-            for (int t = ATM_TERMS - 1; t >= 0; t--) mma_bf16_16816(oacc[ON - 1], a[t], b[0], b[1]);
+            for (int w = 1; w < NW; w++) {
+                const float4 x = *reinterpret_cast<const float4 *>(spart + (w * ATM_HEADS + rh) * ATM_ROWS + rr0);
+                acc4.x += x.x;
+                acc4.y += x.y;
+                acc4.z += x.z;
+                acc4.w += x.w;
+            }
+            sv[0] = acc4.x;
+            sv[1] = acc4.y;
+            sv[2] = acc4.z;
+            sv[3] = acc4.w;
         }
+        float cm = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            sv[i] = rows[buf][rr0 + i] >= 0 ? sv[i] * scale : -INFINITY;
+            cm = fmaxf(cm, sv[i]);
+        }
+#pragma unroll
+        for (int o2 = 1; o2 < 16; o2 <<= 1) cm = fmaxf(cm, __shfl_xor_sync(0xFFFFFFFFu, cm, o2));
+        const float old = run_m[rh], nm = fmaxf(old, cm);
+        const float alpha = old == -INFINITY ? 0.0f : expf(old - nm);
+        float e[4], ls = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            e[i] = sv[i] != -INFINITY ? expf(sv[i] - nm) : 0.0f;
+            ls += e[i];
+        }
+#pragma unroll
+        for (int o2 = 1; o2 < 16; o2 <<= 1) ls += __shfl_xor_sync(0xFFFFFFFFu, ls, o2);
+        if (it + 2 < nmine) load_rows(it + 2);   // rows[buf]'s masks are read
+        __syncthreads();                      // partial scores and run_m read: the weights overwrite them
+        if ((tid & 15) == 0) {
+            run_m[rh] = nm;
+            run_l[rh] = run_l[rh] * alpha + ls;
+            s_alpha[rh] = alpha;
+        }
+        {
+            uint32_t w0[ATM_TERMS], w1[ATM_TERMS];
+            split3_bf16x2(e[0], e[1], w0);
+            split3_bf16x2(e[2], e[3], w1);
+#pragma unroll
+            for (int t = 0; t < ATM_TERMS; t++)
+                *reinterpret_cast<uint2 *>(pt + (t * ATM_HEADS + rh) * PS + rr0) = make_uint2(w0[t], w1[t]);
+        }
+        __syncthreads();
+        // ---- output: rescale, then += P V over the 64 rows
+        const float al0 = s_alpha[g], al1 = s_alpha[g + 8];
+#pragma unroll
+        for (int n = 0; n < ON; n++) {
+            oacc[n][0] *= al0;
+            oacc[n][1] *= al0;
+            oacc[n][2] *= al1;
+            oacc[n][3] *= al1;
+        }
+#pragma unroll
+        for (int kk = 0; kk < ATM_ROWS / 16; kk++) {
+            uint32_t a[ATM_TERMS][4];
+#pragma unroll
+            for (int t = 0; t < ATM_TERMS; t++) ldsm_x4(a[t], pt + (t * ATM_HEADS + arow) * PS + 16 * kk + acol);
+#pragma unroll
+            for (int n = 0; n + 1 < ON; n += 2) {
+                uint32_t b[4];
+                ldsm_x4_t(b, kbuf + (16 * kk + arow) * KS + c0 + 8 * n + acol);
+#pragma unroll
+                for (int t = ATM_TERMS - 1; t >= 0; t--) {
+                    mma_bf16_16816(oacc[n], a[t], b[0], b[1]);
+                    mma_bf16_16816(oacc[n + 1], a[t], b[2], b[3]);
+                }
+            }
+            if (ON & 1) {
+                uint32_t b[2];
+                ldsm_x2_t(b, kbuf + (16 * kk + arow) * KS + c0 + 8 * (ON - 1));
+#pragma unroll
+                for (int t = ATM_TERMS - 1; t >= 0; t--) mma_bf16_16816(oacc[ON - 1], a[t], b[0], b[1]);
+            }
+        }
+        __syncthreads();                      // this buffer and the weights are free again
     }
+
+    // ---- combine: push the partial columns and statistics to their owners
 #pragma unroll
     for (int n = 0; n < ON; n++) {
-        const int col = c0 + 8 * n + 2 * c;
-        *reinterpret_cast<float2 *>(po + ((size_t)chunk * H + h0 + g) * D + col) = make_float2(oacc[n][0], oacc[n][1]);
-        *reinterpret_cast<float2 *>(po + ((size_t)chunk * H + h0 + g + 8) * D + col) =
-            make_float2(oacc[n][2], oacc[n][3]);
+        const int col = c0 + 8 * n + 2 * c, d = col / OC, lc = col - d * OC;
+        float *dst = cluster.map_shared_rank(stage, d) + (rank * ATM_HEADS + g) * OC + lc;
+        *reinterpret_cast<float2 *>(dst) = make_float2(oacc[n][0], oacc[n][1]);
+        *reinterpret_cast<float2 *>(dst + 8 * OC) = make_float2(oacc[n][2], oacc[n][3]);
+    }
+    if (tid < CL * ATM_HEADS) {
+        const int d = tid / ATM_HEADS, hh = tid % ATM_HEADS;
+        cluster.map_shared_rank(&st_m[0][0], d)[rank * ATM_HEADS + hh] = run_m[hh];
+        cluster.map_shared_rank(&st_l[0][0], d)[rank * ATM_HEADS + hh] = run_l[hh];
+    }
+    cluster.sync();                           // every rank's pushes have landed
+    if (tid < ATM_HEADS) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < CL; r++) m = fmaxf(m, st_m[r][tid]);
+        double denom = 0.0;
+#pragma unroll
+        for (int r = 0; r < CL; r++) {
+            const float mr = st_m[r][tid];
+            const float f = mr != -INFINITY ? expf(mr - m) : 0.0f;   // no valid row there: nothing
+            fac[r][tid] = f;
+            denom += (double)st_l[r][tid] * (double)f;
+        }
+        denom += (double)expf(__ldg(sink + h0 + tid) - m);   // m = -inf (no valid row at all): o = 0
+        s_inv[tid] = (float)(1.0 / denom);
+    }
+    __syncthreads();
+    for (int i = tid; i < ATM_HEADS * OC; i += ATM_THREADS) {
+        const int hh = i / OC, lc = i - hh * OC;
+        float acc = 0.0f;
+#pragma unroll
+        for (int r = 0; r < CL; r++) acc = fmaf(stage[(r * ATM_HEADS + hh) * OC + lc], fac[r][hh], acc);
+        o[(size_t)(h0 + hh) * D + rank * OC + lc] = acc * s_inv[hh];
     }
 }
 
@@ -531,6 +610,58 @@ __global__ void __launch_bounds__(ATT_COMB_COLS) attn_combine_kernel(
     o[(size_t)h * D + col] = acc * inv;
 }
 
+// Cluster of 16 CTAs (one per SM: ~208 KB of shared memory each) where the
+// device can co-schedule one per head group, else 8.
+template <int D, int CL>
+static int attn_mma_launch(float *o, const float *q, const void *kv, const float *sink, const int *idxs, int H,
+                           int topk, float scale, cudaStream_t st, bool probe, int *fits)
+{
+    const size_t smem = (size_t)2 * ATM_ROWS * (D + 8) * 2 + (size_t)(ATM_THREADS / 32) * ATM_HEADS * ATM_ROWS * 4 +
+                        (size_t)ATM_HEADS * D * 4;
+    auto kern = attn_mma_kernel<D, CL>;
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)kern, (int)smem));
+    if (CL > 8) DSV4CU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CL, H / ATM_HEADS);
+    cfg.blockDim = dim3(ATM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = CL;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (probe) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (const void *)kern, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            n = 0;
+        }
+        *fits = n;
+        return DSV4CU_OK;
+    }
+    DSV4CU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, q, (const uint16_t *)kv, idxs, sink, H, topk, scale, o));
+    return DSV4CU_OK;
+}
+
+template <int D>
+static int attn_mma_run(float *o, const float *q, const void *kv, const float *sink, const int *idxs, int H,
+                        int topk, float scale, cudaStream_t st)
+{
+    static int clusters16 = -1;   // how many 16-CTA clusters the device co-schedules
+    if (clusters16 < 0) {
+        int n = 0;
+        int r = attn_mma_launch<D, 16>(o, q, kv, sink, idxs, H, topk, scale, st, true, &n);
+        clusters16 = r ? 0 : n;
+    }
+    if (clusters16 >= H / ATM_HEADS && g_attn_mma != 2)
+        return attn_mma_launch<D, 16>(o, q, kv, sink, idxs, H, topk, scale, st, false, nullptr);
+    return attn_mma_launch<D, 8>(o, q, kv, sink, idxs, H, topk, scale, st, false, nullptr);
+}
+
 size_t attn_workspace(int H, int D, int topk)
 {
     const size_t nch = (size_t)(topk + ATT_CH - 1) / ATT_CH;
@@ -547,23 +678,12 @@ int attn_run(float *o, const float *q, const void *kv, int kv_bf16, const float 
     float *pl = (float *)p;
     p += dsv4cu_align256((size_t)nch * H * 4);
     float *po = (float *)p;
-    // Tensor-core chunks for the bf16 cache at the model's head widths.
+    // One cluster per 16 heads on the tensor cores for the bf16 cache at the
+    // model's head widths.
     if (kv_bf16 && (D == 576 || D == 512) && H % ATM_HEADS == 0 && ((uintptr_t)q & 15) == 0 &&
-        ((uintptr_t)kv & 15) == 0 && g_attn_mma) {
-        const int nc = (topk + ATM_ROWS - 1) / ATM_ROWS;
-        const size_t smem =
-            ((size_t)ATM_ROWS * (D + 8) + (size_t)ATM_TERMS * ATM_HEADS * (D + 8 + ATM_ROWS + 8)) * 2;
-        auto kern = D == 576 ? attn_mma_kernel<576> : attn_mma_kernel<512>;
-        static SmemLimit lim_m[2];
-        DSV4CU_CUDA_TRY(smem_limit(lim_m[D == 576], (const void *)kern, (int)smem));
-        kern<<<dim3(nc, H / ATM_HEADS), ATM_THREADS, smem, st>>>(q, (const uint16_t *)kv, idxs, H, topk, scale, pm,
-                                                                   pl, po);
-        DSV4CU_LAUNCH_CHECK();
-        attn_combine_kernel<<<dim3(H, (D + ATT_COMB_COLS - 1) / ATT_COMB_COLS), ATT_COMB_COLS, 0, st>>>(
-            pm, pl, po, sink, H, D, nc, o);
-        DSV4CU_LAUNCH_CHECK();
-        return DSV4CU_OK;
-    }
+        ((uintptr_t)kv & 15) == 0 && g_attn_mma)
+        return D == 576 ? attn_mma_run<576>(o, q, kv, sink, idxs, H, topk, scale, st)
+                        : attn_mma_run<512>(o, q, kv, sink, idxs, H, topk, scale, st);
     const bool vec = D % 4 == 0 && ((uintptr_t)q & 15) == 0 && ((uintptr_t)kv & (kv_bf16 ? 7 : 15)) == 0;
     const size_t DA = (size_t)((D + 3) & ~3);
     const size_t smem = ((size_t)ATT_CH * (DA + 8) + (size_t)ATT_HG * DA + ATT_HG * ATT_CH) * sizeof(float);
@@ -590,9 +710,9 @@ using namespace dsv4cu;
 
 extern "C" int dsv4cu_sparse_attn_set_path(int path)
 {
-    if (path != DSV4CU_ATTN_AUTO && path != DSV4CU_ATTN_FP32)
+    if (path != DSV4CU_ATTN_AUTO && path != DSV4CU_ATTN_FP32 && path != DSV4CU_ATTN_CLUSTER8)
         return dsv4cu_set_error(DSV4CU_ERR_ARG, "sparse_attn_set_path: unknown path %d", path);
-    g_attn_mma = path == DSV4CU_ATTN_AUTO;
+    g_attn_mma = path == DSV4CU_ATTN_AUTO ? 1 : path == DSV4CU_ATTN_CLUSTER8 ? 2 : 0;
     return DSV4CU_OK;
 }
 

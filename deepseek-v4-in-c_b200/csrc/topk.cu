@@ -391,10 +391,20 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_select_kernel(const float *
     }
     cluster.sync();                               // every CTA's counts are complete
     int gbase = 0, ebase = 0;
-    for (int r = 0; r < rank; r++) {
-        const int *rc = cluster.map_shared_rank(cta_cnt, r);
-        gbase += rc[0];
-        ebase += rc[1];
+    {
+        int rg[TOPK_CL], re[TOPK_CL];             // all remote loads in flight, then the sums
+#pragma unroll
+        for (int r = 0; r < TOPK_CL; r++) {
+            const int *rc = cluster.map_shared_rank(cta_cnt, r);
+            rg[r] = rc[0];
+            re[r] = rc[1];
+        }
+#pragma unroll
+        for (int r = 0; r < TOPK_CL; r++)
+            if (r < rank) {
+                gbase += rg[r];
+                ebase += re[r];
+            }
     }
     cluster_arrive();                             // remote reads done; the wait comes before exit
     // Picks above the threshold fill [0, k - need_eq) in index order; the

@@ -576,11 +576,12 @@ class Device:
         tensor-core digits) or "fp64" (FP64 tensor cores)."""
         check(self.L.dsv4cu_indexer_set_path(self.INDEXER_PATH[path]), "dsv4cu_indexer_set_path")
 
-    ATTN_PATH = {"auto": 0, "fp32": 1}
+    ATTN_PATH = {"auto": 0, "fp32": 1, "cluster8": 2}
 
     def sparse_attn_set_path(self, path: str):
         """Chunk kernel of the sparse attention (dsv4cu_sparse_attn_set_path):
-        "auto" (bf16 tensor cores where the shape allows) or "fp32"."""
+        "auto" (bf16 tensor cores where the shape allows), "fp32" or "cluster8"
+        (the tensor-core kernel in 8-CTA clusters)."""
         check(self.L.dsv4cu_sparse_attn_set_path(self.ATTN_PATH[path]), "dsv4cu_sparse_attn_set_path")
 
     def topk(self, idx, scores, n, k):

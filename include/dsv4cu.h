@@ -452,12 +452,16 @@ int dsv4cu_sparse_attn(dsv4cu_ctx *ctx, float *o, const float *q, const void *kv
                        int kv_bf16, const float *sink, const int *idxs, int h,
                        int d, int topk, float scale, void *stream);
 
-/* Chunk kernel of dsv4cu_sparse_attn: AUTO = bf16 tensor cores (mma.sync,
- * q and the weights as three bf16 terms each) for a bf16 cache with head_dim
- * 512 or 576 and n_heads % 16 == 0, the fp32 kernel otherwise; FP32 = the
- * fp32 kernel always. Process-wide; for comparisons. */
+/* Kernel of dsv4cu_sparse_attn: AUTO = one thread-block cluster per 16 heads
+ * on the bf16 tensor cores (mma.sync; q and the weights as three bf16 terms
+ * each, so only the fp32 accumulation rounds) for a bf16 cache with head_dim
+ * 512 or 576 and n_heads % 16 == 0 - 16-CTA clusters where the device fits
+ * one per head group, else 8 - and the fp32 chunk kernels otherwise;
+ * FP32 = the fp32 chunk kernels always; CLUSTER8 = AUTO with 8-CTA clusters.
+ * Process-wide; for comparisons. */
 #define DSV4CU_ATTN_AUTO 0
 #define DSV4CU_ATTN_FP32 1
+#define DSV4CU_ATTN_CLUSTER8 2
 int dsv4cu_sparse_attn_set_path(int path);
 
 /* dsv4cu_sparse_attn without a context and without any allocation. No

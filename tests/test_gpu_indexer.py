@@ -272,13 +272,15 @@ def test_attn_config4_full(dev, orc, bf16):
 
 
 @pytest.mark.parametrize("D,H,T,qscale", [(576, 64, 2048, 1.0), (576, 16, 1000, 3.0), (512, 32, 2176, 1.0),
-                                          (576, 64, 64, 0.3)])
-@pytest.mark.parametrize("path", ["auto", "fp32"])
+                                          (576, 64, 64, 0.3), (576, 64, 5000, 1.0)])
+@pytest.mark.parametrize("path", ["auto", "cluster8", "fp32"])
 def test_attn_tensor_core_chunks(dev, orc, D, H, T, qscale, path):
-    """The bf16 tensor-core chunk kernel (fp32 q and weights as two bf16 terms
-    each) against the reference: fp32 q off the bf16 grid, peaky softmax
-    (qscale 3), a ragged last chunk, a fully masked 64-slot chunk and scattered
-    masked slots; the fp32 kernel on the same inputs."""
+    """The bf16 tensor-core cluster kernel (fp32 q and weights as three bf16
+    terms each, online softmax over each CTA's 64-row sub-chunks, combine in
+    distributed shared memory) against the reference: fp32 q off the bf16
+    grid, peaky softmax (qscale 3), a ragged last sub-chunk, a fully masked
+    64-slot sub-chunk, scattered masked slots and fewer sub-chunks than CTAs
+    (T = 64); 16- and 8-CTA clusters and the fp32 kernel on the same inputs."""
     t = __import__("torch")
     rng = np.random.default_rng(D + H + T)
     N = 8192
@@ -303,3 +305,23 @@ def test_attn_tensor_core_chunks(dev, orc, D, H, T, qscale, path):
     got = o.cpu().numpy()
     assert np.isfinite(got).all()
     assert att_err(got, want) <= ATT_TOL
+
+
+@pytest.mark.parametrize("path", ["auto", "cluster8"])
+def test_attn_tensor_core_all_masked(dev, path):
+    """Every slot masked: the reference output is zero (denominator = sink
+    only), with no NaN from the empty sub-chunks."""
+    t = __import__("torch")
+    H, D, T = 32, 576, 300
+    q = t.randn((H, D), dtype=t.float32, device="cuda")
+    kv = t.randn((1000, D), dtype=t.float32, device="cuda").to(t.bfloat16)
+    sink = t.randn(H, dtype=t.float32, device="cuda")
+    idx = t.full((T,), -1, dtype=t.int32, device="cuda")
+    o = t.full((H, D), 7.0, dtype=t.float32, device="cuda")
+    dev.sparse_attn_set_path(path)
+    try:
+        dev.sparse_attn(o, q, kv, 1, sink, idx, H, D, T, 0.05)
+        t.cuda.synchronize()
+    finally:
+        dev.sparse_attn_set_path("auto")
+    assert t.count_nonzero(o).item() == 0
