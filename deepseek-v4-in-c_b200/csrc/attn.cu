@@ -218,8 +218,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_chunk_kernel(
 //            straight into the shared memory of the CTA that owns those
 //            columns (CTA r owns [D/CL r, D/CL (r + 1))); after one cluster
 //            barrier each CTA forms the global max, the denominator with the
-//            sink (in double, rank order) and writes its columns - no remote
-//            loads, no partials in global memory.
+//            sink (in double) and writes its columns - no remote loads, no
+//            partials in global memory.
 constexpr int ATM_ROWS = 64;
 constexpr int ATM_HEADS = 16;
 constexpr int ATM_THREADS = 256;
@@ -345,6 +345,8 @@ __global__ void __launch_bounds__(ATM_THREADS, 1) attn_mma_kernel(
         run_m[tid] = -INFINITY;
         run_l[tid] = 0.0f;
     }
+    __syncthreads();
+    if (nmine > 0) gather(0);                 // the first rows arrive while Q is split
     // this warp's Q slice as A fragments, three bf16 terms: k step w + 8j,
     // registers (row g, k 2c), (row g + 8, k 2c), (row g, k 2c + 8), (row g + 8, k 2c + 8)
     uint32_t qa[KPW][ATM_TERMS][4];
@@ -370,8 +372,6 @@ __global__ void __launch_bounds__(ATM_THREADS, 1) attn_mma_kernel(
                 for (int t = 0; t < ATM_TERMS; t++) qa[j][t][rr] = w[t];
             }
     }
-    __syncthreads();
-    if (nmine > 0) gather(0);
 
     float oacc[ON][4];
 #pragma unroll
@@ -520,20 +520,23 @@ __global__ void __launch_bounds__(ATM_THREADS, 1) attn_mma_kernel(
         cluster.map_shared_rank(&st_l[0][0], d)[rank * ATM_HEADS + hh] = run_l[hh];
     }
     cluster.sync();                           // every rank's pushes have landed
-    if (tid < ATM_HEADS) {
-        float m = -INFINITY;
+    // thread (head hh, rank r) for r < CL: the global max and the rank's factor
+    // by shuffles over the CL lanes of a head, the denominator in double in a
+    // fixed tree order
+    static_assert(ATM_HEADS * CL <= ATM_THREADS && 32 % CL == 0, "combine layout");
+    if (tid < ATM_HEADS * CL) {
+        const int hh = tid / CL, r = tid % CL;
+        const float mr = st_m[r][hh];
+        float m = mr;
 #pragma unroll
-        for (int r = 0; r < CL; r++) m = fmaxf(m, st_m[r][tid]);
-        double denom = 0.0;
+        for (int o2 = 1; o2 < CL; o2 <<= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o2));
+        const float f = mr != -INFINITY ? expf(mr - m) : 0.0f;   // no valid row there: nothing
+        fac[r][hh] = f;
+        double dsum = (double)st_l[r][hh] * (double)f;
 #pragma unroll
-        for (int r = 0; r < CL; r++) {
-            const float mr = st_m[r][tid];
-            const float f = mr != -INFINITY ? expf(mr - m) : 0.0f;   // no valid row there: nothing
-            fac[r][tid] = f;
-            denom += (double)st_l[r][tid] * (double)f;
-        }
-        denom += (double)expf(__ldg(sink + h0 + tid) - m);   // m = -inf (no valid row at all): o = 0
-        s_inv[tid] = (float)(1.0 / denom);
+        for (int o2 = 1; o2 < CL; o2 <<= 1) dsum += __shfl_xor_sync(0xFFFFFFFFu, dsum, o2);
+        if (r == 0)   // m = -inf (no valid row at all): the sink term is inf and o = 0
+            s_inv[hh] = (float)(1.0 / (dsum + (double)expf(__ldg(sink + h0 + hh) - m)));
     }
     __syncthreads();
     for (int i = tid; i < ATM_HEADS * OC; i += ATM_THREADS) {

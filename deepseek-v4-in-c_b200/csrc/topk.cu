@@ -261,8 +261,8 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_kernel(const float *__restr
 // launches:
 //  select  CTA c of the cluster stages keys [c * span, (c + 1) * span) in its
 //          shared memory. Radix select over 8-bit digits from the top: each
-//          pass builds per-CTA histograms (one shared atomic per distinct
-//          digit and warp), and after a cluster barrier every CTA sums the
+//          pass builds per-CTA histograms (the first one with one shared
+//          atomic per distinct digit and warp), and after a cluster barrier every CTA sums the
 //          TOPK_CL histograms through distributed shared memory and picks the
 //          same digit (identical inputs, identical arithmetic). The passes
 //          stop early once the digit's whole bucket is taken. Every key whose
@@ -325,8 +325,12 @@ __global__ void __launch_bounds__(TOPK_THREADS) topk_select_kernel(const float *
                 const uint32_t key = skeys[i];
                 if ((key & mask) == prefix) bin = (int)((key >> shift) & 255u);
             }
-            const unsigned grp = __match_any_sync(0xFFFFFFFFu, bin);
-            if (bin >= 0 && lane == __ffs(grp) - 1) atomicAdd(&hb[bin], __popc(grp));
+            if (pass == 0) {                      // few distinct top digits: one atomic per digit and warp
+                const unsigned grp = __match_any_sync(0xFFFFFFFFu, bin);
+                if (bin >= 0 && lane == __ffs(grp) - 1) atomicAdd(&hb[bin], __popc(grp));
+            } else if (bin >= 0) {                // inside one bucket the digits spread out
+                atomicAdd(&hb[bin], 1);
+            }
         }
         cluster.sync();                           // every CTA's histogram is complete
         // thread t < 256 holds digit 255 - t: the scan runs from the top digit down
