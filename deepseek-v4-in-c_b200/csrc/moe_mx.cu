@@ -1034,7 +1034,7 @@ static MxMoeShape mxpf_shape(const dsv4cu_moe *L, int topk, int nt, int terms)
     s.hidden = L->hidden;
     s.inter = L->inter;
     s.has_shared = L->has_shared;
-    s.NB = terms == 3 ? 192 : 256;
+    s.NB = terms == 3 ? 192 : 256;         // 64 tokens per tile at 3 and 4 terms, 128 at 2, 256 at 1
     s.KB = 1;
     s.tpt = (s.NB / terms) / 8 * 8;
     s.nbb = (s.NB + 127) / 128;
@@ -1073,7 +1073,7 @@ int moe_mx_prefill(const dsv4cu_moe *L, float *out, const float *x, const float 
     if (nt > PF_MAX_NT || topk > MXMOE_MAX_TOPK || L->n_experts > PREP_MAX_EXPERTS)
         return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "moe_prefill: nt %d / topk %d / experts %d beyond %d / 16 / 512",
                                 nt, topk, L->n_experts, PF_MAX_NT);
-    if (terms != 3 && terms != 4) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: terms must be 3 or 4");
+    if (terms < 1 || terms > 4) return dsv4cu_set_error(DSV4CU_ERR_ARG, "moe_prefill: terms must be 1 .. 4");
     const MxMoeShape s = mxpf_shape(L, topk, nt, terms);
     MxMoeWs ws;
     PfWs pf;

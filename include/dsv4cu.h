@@ -422,8 +422,10 @@ int dsv4cu_indexer_set_path(int path);
  * expert dsv4_prefill_moe.c:40-59) with the same arguments as
  * dsv4cu_moe_decode. Tokens are bucketed by expert (tokens ascending inside a
  * bucket) and every bucket runs as tcgen05 block-scaled GEMMs; the fp32
- * activations enter the tensor core as `terms` (3 or 4) exact e4m3 terms
- * (3: max-rel error ~1e-5, 4: ~1e-6). Needs a layer whose matrices all
+ * activations enter the tensor core as `terms` (1 .. 4) e4m3 terms with
+ * per-32 E8M0 scales (4: max-rel error ~1e-6, 3: ~1e-5, 2: ~1e-3; 1 is the
+ * plain MXFP8 product, the single-term mode: 64 tokens per 192/256-column
+ * tile at 3 / 4 terms, 128 at 2, 256 at 1). Needs a layer whose matrices all
  * qualify for the tensor-core path (FP4/FP8, dims multiples of 128). */
 size_t dsv4cu_moe_prefill_workspace(const dsv4cu_moe *layer, int topk, int nt, int terms);
 int dsv4cu_moe_prefill(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out, const float *x,

@@ -170,3 +170,79 @@ def test_mx_split_k_batch_invariant(dev, nt):
         dev.mat_destroy(h)
     for tok, y1 in zip((0, 3, nt - 1), singles):
         assert np.array_equal(got[tok].view(np.uint32), y1.cpu().numpy()[0].view(np.uint32)), tok
+
+
+def mx_quant_terms1(x):
+    """The activation as the single-term MX mode feeds it to the tensor core
+    (mx_split128 with terms = 1): per 32-block along K the smallest power of
+    two s = 2^e with max|x| <= 448 s, then each value rounded to nearest-even
+    on the e4m3 grid of x / s. Returns the dequantized values q * s."""
+    nt, K = x.shape
+    xb = x.reshape(nt, K // 32, 32).astype(np.float32)
+    a = np.abs(np.where(np.isfinite(xb), xb, 0.0)).max(axis=2)
+    f, E = np.frexp(a)
+    e0 = np.where(a > 0, np.clip(E - 9 + (f > 0.875), -127, 127), 0).astype(np.int64)
+    v = np.ldexp(xb, -e0[..., None]).astype(np.float32)
+    codes = pack._rne_grid(np.abs(v), pack._E4M3_POS).astype(np.int64)
+    q = pack.E4M3[codes].astype(np.float64) * np.where(np.signbit(v), -1.0, 1.0)
+    return np.ldexp(q, e0[..., None]).astype(np.float32).reshape(nt, K)
+
+
+@pytest.mark.parametrize("wdt", [3, 2], ids=["fp4", "fp8"])
+@pytest.mark.parametrize("rows,cols,nt,xscale", [(256, 512, 8, 1.0), (2048, 4096, 64, 1.0), (640, 2560, 3, 37.0),
+                                                 (1024, 1024, 130, 1e-3)])
+def test_mx_single_term_mode(dev, orc, wdt, rows, cols, nt, xscale):
+    """Single-term MX mode (dsv4cu_mat_gemm with terms = 1: one e4m3 term per
+    activation with a per-32 E8M0 scale, the plain MXFP8 x MXFP4/MXFP8
+    product) against the oracle fed the SAME quantized activations: only the
+    fp32 accumulation differs, so the bar is 1e-5, not the 1e-3 matmul bar."""
+    import oracle
+    t = __import__("torch")
+    W, S, Wd, Sd, q = _upload_qmat(dev, wdt, rows, cols, rows + cols + nt)
+    rng = np.random.default_rng(rows * 3 + nt)
+    x = (rng.standard_normal((nt, cols)) * xscale).astype(np.float32)
+    x[:, 5::97] *= 50.0                               # uneven blocks
+    h = dev.mat_create(q)
+    try:
+        y = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+        dev.mat_gemm(h, y, t.from_numpy(x).cuda(), nt, 1)
+        t.cuda.synchronize()
+        got = y.cpu().numpy()
+    finally:
+        dev.mat_destroy(h)
+    qm = oracle.qmat(W, S, wdt, rows, cols, q.blk_r, q.blk_c)
+    want = orc.mmq(mx_quant_terms1(x), qm)
+    e = rel_err(got, want)
+    print(f"wdt={wdt} {rows}x{cols} nt={nt} single-term vs quantized-x oracle: max-rel={e:.3e}")
+    assert np.isfinite(got).all()
+    assert e <= 1e-5, e
+
+
+def test_qkv_full_shape(dev, orc):
+    """The config-3 QKV projection at full shape: FP8 6144 x 4096 (128 x 128
+    E8M0 scales) over 4096 tokens, terms 3 (the matmul bar 1e-3) and the
+    single-term mode (1e-5 against the oracle on the quantized activations),
+    checked on 48 sampled tokens across the whole batch."""
+    import oracle
+    t = __import__("torch")
+    rows, cols, nt = 6144, 4096, 4096
+    W, S, Wd, Sd, q = _upload_qmat(dev, 2, rows, cols, 6144)
+    rng = np.random.default_rng(4096)
+    x = pack.bf16_round(rng.standard_normal((nt, cols)).astype(np.float32))
+    xd = t.from_numpy(x).cuda()
+    pick = np.sort(np.concatenate([[0, nt - 1], rng.choice(np.arange(1, nt - 1), 46, replace=False)]))
+    qm = oracle.qmat(W, S, 2, rows, cols, q.blk_r, q.blk_c)
+    h = dev.mat_create(q)
+    try:
+        for terms, bar in ((3, 1e-3), (1, 1e-5)):
+            y = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+            dev.mat_gemm(h, y, xd, nt, terms)
+            t.cuda.synchronize()
+            got = y.cpu().numpy()
+            assert np.isfinite(got).all(), terms
+            xs = x[pick] if terms == 3 else mx_quant_terms1(x)[pick]
+            e = rel_err(got[pick], orc.mmq(xs, qm))
+            print(f"QKV 6144x4096 @ 4096 tokens, terms={terms}: max-rel={e:.3e} over {len(pick)} tokens")
+            assert e <= bar, (terms, e)
+    finally:
+        dev.mat_destroy(h)
