@@ -175,7 +175,9 @@ DSV4CU_DEV void mxmoe_split_row_chunk(const float *__restrict__ src, int K, int 
 // of tpt slots - all in shared memory, identically in every CTA. CTA 0
 // publishes the tables; then all CTAs write their share of the gate/up B
 // operand: one warp per (column tile, column, 32-wide K block).
-__global__ void __launch_bounds__(1024) mxmoe_prep_kernel(
+constexpr int PREP_THREADS = 512;     // 128 registers a thread: the tables stay out of local memory
+
+__global__ void __launch_bounds__(PREP_THREADS) mxmoe_prep_kernel(
     const float *__restrict__ tab, const float *__restrict__ x, const float *__restrict__ logits,
     const float *__restrict__ bias, const int64_t *__restrict__ tid2eid, const int *__restrict__ token_ids,
     int n_experts, int topk, float route_scale, int nt, int hidden, int has_shared, int terms, int tpt, int NB,
@@ -221,6 +223,7 @@ __global__ void __launch_bounds__(1024) mxmoe_prep_kernel(
             if (act) {
                 const float v = r_s[threadIdx.x], *row = r_s + t * n_experts;
                 int r = 0;
+#pragma unroll 8
                 for (int q = 0; q < n_experts; q++) {
                     const float w = row[q];
                     r += (w > v) || (w == v && q < e);
@@ -834,8 +837,8 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     {
         // Every SM takes part in the split; each CTA repeats the (cheap) routing.
         const long tasks = (long)s.max_tiles * s.tpt * (s.hidden / 128);
-        const int grid = (int)min((long)sms, max(1L, (tasks + 31) / 32));
-        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_prep_kernel, dim3(grid), dim3(1024), 0, st, tab, x, logits, bias, tid2eid,
+        const int grid = (int)min((long)sms, max(1L, (tasks + PREP_THREADS / 32 - 1) / (PREP_THREADS / 32)));
+        DSV4CU_CUDA_TRY(launch_pdl(mxmoe_prep_kernel, dim3(grid), dim3(PREP_THREADS), 0, st, tab, x, logits, bias, tid2eid,
                                    token_ids, s.n_experts, topk, route_scale, nt, s.hidden, s.has_shared, MX_TERMS,
                                    s.tpt, s.NB, ws, idx_out, wts_out));
     }

@@ -216,6 +216,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     // previous kernel has finished: a policy whose A side and tile list do not
     // depend on that kernel's output fills the first ring's worth early.
     int pre = 0;
+    const uint64_t wpol = l2_evict_first();   // weights stream through L2 once
     if constexpr (P::kPrefetchA) {
         if (threadIdx.x == 0) {
             const int nt0 = P::ntiles(p);
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 #pragma unroll
                     for (int b = 0; b < KB; b++) {
                         const int kc = T.k0 + c * KB + b;
-                        tma_load_2d(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[pre]);
+                        tma_load_2d_hint(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[pre], wpol);
                         bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
                                   &full[pre]);
                     }
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 #pragma unroll
                         for (int b = 0; b < KB; b++) {
                             const int kc = T.k0 + c * KB + b;
-                            tma_load_2d(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s]);
+                            tma_load_2d_hint(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s], wpol);
                             bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
                                       &full[s]);
                         }

@@ -162,18 +162,19 @@ DSV4CU_DEV void smv_bulk_load(uint32_t dst, const void *src, uint32_t bytes, uin
 
 // Tensor-map copies (no multicast); the innermost coordinate is 0 or a
 // multiple of 64 bytes.
-DSV4CU_DEV void smv_tma_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint32_t bar)
+// Weights stream with the L2 evict-first policy (l2_evict_first).
+DSV4CU_DEV void smv_tma_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint32_t bar, uint64_t pol)
 {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3, %4}], [%5];"
-                 ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+                 " [%0], [%1, {%2, %3, %4}], [%5], %6;"
+                 ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar), "l"(pol)
                  : "memory");
 }
-DSV4CU_DEV void smv_tma_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar)
+DSV4CU_DEV void smv_tma_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar, uint64_t pol)
 {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3}], [%4];"
-                 ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+                 " [%0], [%1, {%2, %3}], [%4], %5;"
+                 ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar), "l"(pol)
                  : "memory");
 }
 
@@ -437,10 +438,11 @@ DSV4CU_DEV void smv_put_stage(uint8_t *ring, SmvSmem<NT> &sm, SmvDrain &dr, int 
     const uint32_t sbytes = !m.fp4 ? 0u : (m.row_bytes <= SMV_SEG ? (uint32_t)(SMV_ROWS * m.s_ld) : SMV_ROWS * 64u);
     mbar_arrive_expect_tx(&sm.full[slot], SMV_ROWS * 128u * (uint32_t)boxc + sbytes);
     const uint32_t base = smem_u32(ring + (size_t)slot * SMV_SLOT), bar = smem_u32(&sm.full[slot]);
-    smv_tma_3d(base, m.wmap, 0, row0, seg * 8, bar);
+    const uint64_t pol = l2_evict_first();
+    smv_tma_3d(base, m.wmap, 0, row0, seg * 8, bar, pol);
     if (m.fp4) {
         if (m.row_bytes <= SMV_SEG) smv_bulk_load(base + SMV_WBYTES, m.s + (size_t)row0 * m.s_ld, sbytes, bar);
-        else smv_tma_2d(base + SMV_WBYTES, m.smap, seg * 64, row0, bar);
+        else smv_tma_2d(base + SMV_WBYTES, m.smap, seg * 64, row0, bar, pol);
     }
 }
 

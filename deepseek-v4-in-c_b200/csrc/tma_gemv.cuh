@@ -86,6 +86,26 @@ DSV4CU_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code)
     return false;
 }
 
+// L2 policy for streamed weights: evict first. Weights are read once per
+// step and exceed the L2, so under the default policy they push out what
+// the next kernels reuse (their code, routing tables, activations, partial
+// buffers); with this hint those stay resident.
+DSV4CU_DEV uint64_t l2_evict_first()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// 2-D tensor-map load with an L2 cache policy (l2_evict_first). No multicast.
+DSV4CU_DEV void tma_load_2d_hint(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar, uint64_t pol)
+{
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+                 " [%0], [%1, {%2, %3}], [%4], %5;"
+                 ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+                 : "memory");
+}
+
 // 2-D tensor-map load of one box into shared memory; completion counted in
 // bytes on `bar`. x (bytes) is always a multiple of 16. No multicast.
 DSV4CU_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar)
