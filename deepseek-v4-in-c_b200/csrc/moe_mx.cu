@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(PREP_THREADS) mxmoe_prep_kernel(
     __shared__ float s_wts[PREP_MAX_PAIRS];
     __shared__ int s_pos[PREP_MAX_PAIRS];
     // Scratch: router scores first (2 x 1024 floats), then per-expert tables.
-    __shared__ int s_scratch[2048];
+    __shared__ __align__(16) int s_scratch[2048];
     __shared__ int s_cnt[PREP_MAX_EXPERTS + 2];
     __shared__ int s_bexp[PREP_MAX_EXPERTS + 2], s_boff[PREP_MAX_EXPERTS + 3];
     __shared__ int s_btok[PREP_MAX_SLOTS];
@@ -220,15 +220,33 @@ __global__ void __launch_bounds__(PREP_THREADS) mxmoe_prep_kernel(
         }
         warp_route = __syncthreads_or(nan);
         if (!warp_route) {
-            if (act) {
-                const float v = r_s[threadIdx.x], *row = r_s + t * n_experts;
+            // Rank of (t, e) among its token's scores, `per` adjacent threads
+            // counting a quarter / half of the experts each (4-wide loads).
+            const int items = nt * n_experts;
+            int per = 1;
+            while (per < 4 && items * per * 2 <= (int)blockDim.x && n_experts % (8 * per) == 0) per *= 2;
+            const int item = threadIdx.x / per, part = threadIdx.x % per;
+            if (item < items) {
+                const int ti = item / n_experts, ei = item - ti * n_experts, span = n_experts / per;
+                const float v = r_s[item];
+                const float *row = r_s + ti * n_experts + part * span;
+                const int q0 = part * span;
                 int r = 0;
-#pragma unroll 8
-                for (int q = 0; q < n_experts; q++) {
-                    const float w = row[q];
-                    r += (w > v) || (w == v && q < e);
+                if (span % 4 == 0) {
+#pragma unroll 2
+                    for (int q = 0; q < span; q += 4) {
+                        const float4 w = *reinterpret_cast<const float4 *>(row + q);
+                        const int qq = q0 + q;
+                        r += (w.x > v) || (w.x == v && qq < ei);
+                        r += (w.y > v) || (w.y == v && qq + 1 < ei);
+                        r += (w.z > v) || (w.z == v && qq + 2 < ei);
+                        r += (w.w > v) || (w.w == v && qq + 3 < ei);
+                    }
+                } else {
+                    for (int q = 0; q < span; q++) r += (row[q] > v) || (row[q] == v && q0 + q < ei);
                 }
-                if (r < topk) s_idx[t * topk + r] = e;
+                for (int o2 = 1; o2 < per; o2 <<= 1) r += __shfl_xor_sync(__activemask(), r, o2);
+                if (part == 0 && r < topk) s_idx[ti * topk + r] = ei;
             }
             __syncthreads();
             if ((int)threadIdx.x < nt) {
@@ -262,9 +280,10 @@ __global__ void __launch_bounds__(PREP_THREADS) mxmoe_prep_kernel(
             const bool ok = live && e0 >= 0 && e0 < n_experts;
             const int key = ok ? e0 : 0x7FFFFFFF;
             int rank = 0;
-            for (int q = 0; q < 32; q++) {
+#pragma unroll 1
+            for (int q = 0; q < npairs; q++) {      // a short loop: this code runs once per launch
                 const int kq = __shfl_sync(0xFFFFFFFFu, key, q);
-                rank += (q < npairs) && (kq < key || (kq == key && q < p));
+                rank += kq < key || (kq == key && q < p);
             }
             const int routed = __popc(__ballot_sync(0xFFFFFFFFu, ok));
             const bool bad = __any_sync(0xFFFFFFFFu, live && !ok);
