@@ -445,6 +445,7 @@ struct MxMoeCommon {
     int nb, nbb, tpt, terms, hidden, inter;
     int *err;
     int max_tiles, n_mats;   // bounds of the column-tile table and of the matrix index (3 x experts)
+    int once;                // every bucket fits one column tile: each weight tile is read once
 };
 
 DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc, const uint8_t *sfb)
@@ -462,6 +463,7 @@ DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc,
     T.kc = kc;
     T.nseg = 1;
     T.kst = 1;
+    T.once = c.once;
     return T;
 }
 
@@ -798,6 +800,7 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     c.err = status;
     c.max_tiles = s.max_tiles;
     c.n_mats = 3 * (L->n_experts + 1);
+    c.once = s.nt <= s.tpt;   // a bucket holds at most nt slots
     // Persistent grids: the tile count is known only on the device.
     const int g1 = min(sms, s.max_tiles * 2 * RT), g2 = min(sms, s.max_tiles * RTH);
 

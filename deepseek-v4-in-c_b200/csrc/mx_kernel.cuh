@@ -52,6 +52,7 @@ struct MxTile {
     // segment s covers granules [s * kst / nseg, (s + 1) * kst / nseg).
     int nseg, kst;
     int id0, id1, id2, id3;  // problem-specific tile coordinates
+    int once;                // 1: no other tile reads these weights (they stream with L2 evict-first)
 };
 
 constexpr int MX_THREADS = 192;
@@ -216,7 +217,9 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     // previous kernel has finished: a policy whose A side and tile list do not
     // depend on that kernel's output fills the first ring's worth early.
     int pre = 0;
-    const uint64_t wpol = l2_evict_first();   // weights stream through L2 once
+    // Weights read by one tile only stream with L2 evict-first; weights that
+    // several column tiles share keep the normal policy (they are re-read).
+    const uint64_t pol_once = l2_evict_first(), pol_shared = l2_evict_normal();
     if constexpr (P::kPrefetchA) {
         if (threadIdx.x == 0) {
             const int nt0 = P::ntiles(p);
@@ -230,7 +233,8 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 #pragma unroll
                     for (int b = 0; b < KB; b++) {
                         const int kc = T.k0 + c * KB + b;
-                        tma_load_2d_hint(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[pre], wpol);
+                        tma_load_2d_hint(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[pre],
+                                         T.once ? pol_once : pol_shared);
                         bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
                                   &full[pre]);
                     }
@@ -284,7 +288,8 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 #pragma unroll
                         for (int b = 0; b < KB; b++) {
                             const int kc = T.k0 + c * KB + b;
-                            tma_load_2d_hint(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s], wpol);
+                            tma_load_2d_hint(st + b * C::A_BOX, T.ta, kc * 128, T.a_row, &full[s],
+                                             T.once ? pol_once : pol_shared);
                             bulk_load(st + C::OFF_SFA + b * C::SFA_BOX, T.sfa + (size_t)kc * C::SFA_BOX, C::SFA_BOX,
                                       &full[s]);
                         }

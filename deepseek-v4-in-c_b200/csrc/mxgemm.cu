@@ -158,6 +158,7 @@ struct DenseMx {
         T.id1 = tn;
         T.id2 = p.cross ? seg : 0;
         T.id3 = 0;
+        T.once = p.tiles_n == 1;   // one column tile: these weights are read by this tile only
         return T;
     }
     DSV4CU_DEV static void store(const Params &p, const MxTile &T, int row_l, int tl, float v, int sg)

@@ -97,7 +97,14 @@ DSV4CU_DEV uint64_t l2_evict_first()
     return p;
 }
 
-// 2-D tensor-map load with an L2 cache policy (l2_evict_first). No multicast.
+DSV4CU_DEV uint64_t l2_evict_normal()
+{
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// 2-D tensor-map load with an L2 cache policy (l2_evict_first / l2_evict_normal). No multicast.
 DSV4CU_DEV void tma_load_2d_hint(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar, uint64_t pol)
 {
     asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"

@@ -7,6 +7,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+import canary
 import kat
 import pack
 from conftest import golden
@@ -30,9 +31,9 @@ def dev_score(dev, q, kv, w):
     t = __import__("torch")
     h, d = q.shape
     n = kv.shape[0]
-    out = t.empty(n, dtype=t.float32, device="cuda")
+    out = canary.guarded_empty(n)
     dev.indexer_score(out, t.from_numpy(q).cuda(), t.from_numpy(kv).cuda(), t.from_numpy(w).cuda(), h, d, n)
-    t.cuda.synchronize()
+    canary.check(out, "indexer_score")
     return out.cpu().numpy()
 
 
@@ -41,19 +42,20 @@ def dev_score8(dev, q8, qs, k8, ks, w, stride=None):
     h, d = q8.shape
     n = k8.shape[0]
     stride = stride or k8.shape[1]
-    out = t.empty(n, dtype=t.float32, device="cuda")
+    out = canary.guarded_empty(n)
     dev.indexer_score_fp8(out, t.from_numpy(q8).cuda(), t.from_numpy(qs).cuda(), t.from_numpy(k8).cuda(),
                           t.from_numpy(ks).cuda(), t.from_numpy(w).cuda(), h, d, n, stride)
-    t.cuda.synchronize()
+    canary.check(out, "indexer_score_fp8")
     return out.cpu().numpy()
 
 
 def dev_topk(dev, s, k):
     t = __import__("torch")
     kk = max(0, min(k, s.size))
-    out = t.full((max(kk, 1),), -7, dtype=t.int32, device="cuda")
+    out = canary.guarded_empty(max(kk, 1), t.int32)
+    out.fill_(-7)
     dev.topk(out, t.from_numpy(np.ascontiguousarray(s, np.float32)).cuda(), s.size, k)
-    t.cuda.synchronize()
+    canary.check(out, "topk")
     return out.cpu().numpy()[:kk]
 
 
@@ -231,13 +233,13 @@ def test_attn_any_head_dim(dev, orc, d, bf16):
     idx = rng.choice(N, T, replace=False).astype(np.int32)
     idx[::9] = -1
     scale = np.float32(1 / np.sqrt(d))
-    o = t.empty((H, d), dtype=t.float32, device="cuda")
+    o = canary.guarded_empty((H, d))
     kvd = t.from_numpy(kv).cuda()
     if bf16:
         kvd = kvd.to(t.bfloat16)
     dev.sparse_attn(o, t.from_numpy(q).cuda(), kvd, bf16, t.from_numpy(sink).cuda(), t.from_numpy(idx).cuda(),
                     H, d, T, float(scale))
-    t.cuda.synchronize()
+    canary.check(o, "sparse_attn")
     want = orc.sparse_attn(q, kv, sink, idx, scale)
     assert att_err(o.cpu().numpy(), want) <= ATT_TOL
 
@@ -260,13 +262,13 @@ def test_attn_config4_full(dev, orc, bf16):
     idx = rng.choice(N, T, replace=False).astype(np.int32)
     idx[2048 + 100:] = -1
     scale = np.float32(1 / np.sqrt(D))
-    o = t.empty((H, D), dtype=t.float32, device="cuda")
+    o = canary.guarded_empty((H, D))
     kvd = t.from_numpy(kv).cuda()
     if bf16:
         kvd = kvd.to(t.bfloat16)
     dev.sparse_attn(o, t.from_numpy(q).cuda(), kvd, bf16, t.from_numpy(sink).cuda(), t.from_numpy(idx).cuda(),
                     H, D, T, float(scale))
-    t.cuda.synchronize()
+    canary.check(o, "sparse_attn")
     want = orc.sparse_attn(q, kv, sink, idx, scale)
     assert att_err(o.cpu().numpy(), want) <= ATT_TOL
 
@@ -292,7 +294,7 @@ def test_attn_tensor_core_chunks(dev, orc, D, H, T, qscale, path):
     if T >= 256:
         idx[128:192] = -1
     scale = np.float32(1 / np.sqrt(D))
-    o = t.empty((H, D), dtype=t.float32, device="cuda")
+    o = canary.guarded_empty((H, D))
     kvd = t.from_numpy(kv).cuda().to(t.bfloat16)
     dev.sparse_attn_set_path(path)
     try:
@@ -301,6 +303,7 @@ def test_attn_tensor_core_chunks(dev, orc, D, H, T, qscale, path):
         t.cuda.synchronize()
     finally:
         dev.sparse_attn_set_path("auto")
+    canary.check(o, "sparse_attn (tensor-core cluster)")
     want = orc.sparse_attn(q, kv, sink, idx, scale)
     got = o.cpu().numpy()
     assert np.isfinite(got).all()

@@ -12,6 +12,7 @@ import math
 import numpy as np
 import pytest
 
+import canary
 import kat
 import oracle
 import pack
@@ -138,9 +139,9 @@ def test_matmul_vs_oracle(host, dev, orc, shape):
     dW = torch.from_numpy(W).cuda()
     dS = None if S is None else torch.from_numpy(S).cuda()
     dx = torch.from_numpy(x).cuda()
-    dy = torch.empty((nt, rows), dtype=torch.float32, device="cuda")
+    dy = canary.guarded_empty((nt, rows))
     dev.mmq(dy, dx, dev.qmat(dW, dS, wdt, rows, cols, br, bc), nt)
-    torch.cuda.synchronize()
+    canary.check(dy, "mmq")
     assert np.array_equal(dy.cpu().numpy().view(np.uint32), got.view(np.uint32))
 
 
@@ -204,8 +205,9 @@ def test_bf16_bitwise_with_specials(dev, orc, rows, cols, nt):
     want = orc.mmq(x, oracle.qmat(W, None, 1, rows, cols))
     dW = torch.from_numpy(W).cuda()
     dx = torch.from_numpy(x).cuda()
-    dy = torch.empty((nt, rows), dtype=torch.float32, device="cuda")
+    dy = canary.guarded_empty((nt, rows))
     dev.mmq(dy, dx, dev.qmat(dW, None, 1, rows, cols), nt)
+    canary.check(dy, "mmq bf16")
     got = dy.cpu().numpy()
     fin = ~np.isnan(want)
     assert np.array_equal(np.isnan(got), ~fin)

@@ -8,6 +8,7 @@ import ctypes as C
 import numpy as np
 import pytest
 
+import canary
 import oracle
 import pack
 
@@ -102,14 +103,15 @@ def run(dev, fx, x, logits, topk, scale, limit, bias=None, tid2eid=None, token_i
     nt = x.shape[0]
     dx = t.from_numpy(x).cuda()
     dl = t.from_numpy(logits).cuda()
-    out = t.empty((nt, fx.H), dtype=t.float32, device="cuda")
-    idx = t.empty((nt, topk), dtype=t.int32, device="cuda")
-    wts = t.empty((nt, topk), dtype=t.float32, device="cuda")
+    out = canary.guarded_empty((nt, fx.H))
+    idx = canary.guarded_empty((nt, topk), t.int32)
+    wts = canary.guarded_empty((nt, topk))
     db = None if bias is None else t.from_numpy(bias).cuda()
     dt = None if tid2eid is None else t.from_numpy(tid2eid).cuda()
     dtok = None if token_ids is None else t.from_numpy(token_ids).cuda()
     dev.moe_decode(fx.layer, out, dx, dl, topk, scale, limit, nt, idx, wts, db, dt, dtok)
-    t.cuda.synchronize()
+    for buf, what in ((out, "moe_decode out"), (idx, "moe_decode idx"), (wts, "moe_decode wts")):
+        canary.check(buf, what)
     return out.cpu().numpy(), idx.cpu().numpy(), wts.cpu().numpy()
 
 
@@ -311,12 +313,13 @@ def _oracle_batch(fx, orc, x, logits, topk, scale, limit):
 def _prefill(dev, fx, x, logits, topk, scale, limit, terms):
     t = fx.torch
     nt = x.shape[0]
-    out = t.empty((nt, fx.H), dtype=t.float32, device="cuda")
-    idx = t.empty((nt, topk), dtype=t.int32, device="cuda")
-    wts = t.empty((nt, topk), dtype=t.float32, device="cuda")
+    out = canary.guarded_empty((nt, fx.H))
+    idx = canary.guarded_empty((nt, topk), t.int32)
+    wts = canary.guarded_empty((nt, topk))
     dev.moe_prefill(fx.layer, out, t.from_numpy(x).cuda(), t.from_numpy(logits).cuda(), topk, scale, limit, nt,
                     terms, idx, wts)
-    t.cuda.synchronize()
+    for buf, what in ((out, "moe_prefill out"), (idx, "moe_prefill idx"), (wts, "moe_prefill wts")):
+        canary.check(buf, what)
     return out.cpu().numpy(), idx.cpu().numpy(), wts.cpu().numpy()
 
 

@@ -9,6 +9,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+import canary
 import pack
 
 pytestmark = pytest.mark.gpu
@@ -43,9 +44,10 @@ def _run(dev, orc, wdt, rows, cols, nt, terms, seed=0, xscale=1.0):
     x = (rng.standard_normal((nt, cols)) * xscale).astype(np.float32)
     h = dev.mat_create(q)
     try:
-        y = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+        y = canary.guarded_empty((nt, rows))
+        y.fill_(float("nan"))
         dev.mat_gemm(h, y, t.from_numpy(x).cuda(), nt, terms)
-        t.cuda.synchronize()
+        canary.check(y, "mat_gemm")
         got = y.cpu().numpy()
     finally:
         dev.mat_destroy(h)
@@ -204,9 +206,10 @@ def test_mx_single_term_mode(dev, orc, wdt, rows, cols, nt, xscale):
     x[:, 5::97] *= 50.0                               # uneven blocks
     h = dev.mat_create(q)
     try:
-        y = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+        y = canary.guarded_empty((nt, rows))
+        y.fill_(float("nan"))
         dev.mat_gemm(h, y, t.from_numpy(x).cuda(), nt, 1)
-        t.cuda.synchronize()
+        canary.check(y, "mat_gemm single-term")
         got = y.cpu().numpy()
     finally:
         dev.mat_destroy(h)
@@ -235,9 +238,10 @@ def test_qkv_full_shape(dev, orc):
     h = dev.mat_create(q)
     try:
         for terms, bar in ((3, 1e-3), (1, 1e-5)):
-            y = t.full((nt, rows), float("nan"), dtype=t.float32, device="cuda")
+            y = canary.guarded_empty((nt, rows))
+            y.fill_(float("nan"))
             dev.mat_gemm(h, y, xd, nt, terms)
-            t.cuda.synchronize()
+            canary.check(y, "QKV mat_gemm")
             got = y.cpu().numpy()
             assert np.isfinite(got).all(), terms
             xs = x[pick] if terms == 3 else mx_quant_terms1(x)[pick]
