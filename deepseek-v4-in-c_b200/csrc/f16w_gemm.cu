@@ -1,0 +1,407 @@
+// f16w_gemm.cu - exact-weight GEMM on the bf16 tensor cores (tcgen05 kind::f16).
+//
+// y[t][o] = sum_c x[t][c] * W[o][c] for a packed FP8 (e4m3) or FP4 (e2m1)
+// matrix with E8M0 block scales, the prefill GEMM of the reference's Vulkan
+// seam (src/80_prefill/dsv4_prefill_vk_gemm.c:63-137, shaders gemm_fp8.comp /
+// gemm_fp4.comp) in its exact-weight form: every weight w * 2^e is a bf16
+// value exactly (e4m3 and e2m1 carry at most 4 significant bits and the scale
+// is a power of two), so the tensor core multiplies the reference's own
+// dequantized weights. The activations enter as one bf16 term (x rounded to
+// nearest: each activation off by up to 2^-9 of itself, so the max-rel error
+// against fp32 activations sits near 2^-9 / sqrt(3) ~ 1.1e-3 on Gaussian data)
+// or as two (hi + lo, 16 significand bits, ~1e-5 - inside the 1e-3 matmul
+// bar; each token then takes two B rows). Apart from that rounding the result
+// is fp32 accumulation.
+//
+// Tile: 128 weight rows (MMA M) x 256 tokens (N), K in 64-element chunks (one
+// 128-byte bf16 row per operand row, 128-byte swizzle). Roles, 448 threads,
+// one CTA per SM, persistent over tiles (tile t = row tile t % tiles_m, token
+// tile t / tiles_m):
+//   warp 0       TMA of the bf16 activation chunk (256 rows x 128 bytes);
+//   warp 1       TMEM (two 256-column fp32 accumulators) and the single MMA
+//                thread: four K = 16 MMAs per chunk, tcgen05.commit frees the
+//                stage, the tile's last commit hands the accumulator over;
+//   warps 2-9    converters: each warp dequantizes 16 weight rows of the chunk
+//                straight from the packed matrix (lane = row, half chunk),
+//                cvt to f16, times the block scale, to bf16 (all exact), and
+//                writes them swizzled into the stage; fence.proxy.async, arrive;
+//   warps 10-13  epilogue: tcgen05.ld of the accumulator (TMEM lane = weight
+//                row), y stored token by token (32 consecutive rows per store).
+// Every wait is bounded (2 s): a role that times out records an error code in
+// the context status word and leaves its loop; the others run into their own
+// bounded waits; TMEM is freed after the MMAs in flight have drained.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "ctx.h"
+#include "tma_gemv.cuh"
+#include "tmap.h"
+#include "umma.cuh"
+
+namespace dsv4cu {
+
+constexpr int FW_M = 128;                 // weight rows per tile
+constexpr int FW_N = 256;                 // tokens per tile
+constexpr int FW_KC = 64;                 // K elements per stage
+constexpr int FW_STAGES = 4;
+constexpr int FW_CONV_WARPS = 8;
+constexpr int FW_EPI_WARPS = 4;
+constexpr int FW_THREADS = 32 * (2 + FW_CONV_WARPS + FW_EPI_WARPS);
+constexpr int FW_A_BYTES = FW_M * 128;
+constexpr int FW_B_BYTES = FW_N * 128;
+constexpr int FW_STAGE = FW_A_BYTES + FW_B_BYTES;
+constexpr int FW_SMEM = FW_STAGES * FW_STAGE + 1024;
+
+enum { FWE_EMPTY = 41, FWE_AFULL = 42, FWE_BFULL = 43, FWE_ACCF = 44, FWE_ACCE = 45, FWE_DRAIN = 46 };
+
+struct FwParams {
+    const uint8_t *w;        // packed weights [rows][row_bytes]
+    const uint8_t *s;        // E8M0 scales [ceil(rows / blk_r)][s_cols]; blk_r, blk_c powers of two
+    int rows, cols, fp4, blk_r_log2, blk_c_log2, s_cols, row_bytes;
+    int tiles_m, tiles_n, nt, terms;   // terms: bf16 activation terms per token (1 or 2), B rows per token
+    float *y;                // [nt][rows]
+    int *err;
+};
+
+// Instruction descriptor of kind::f16: fp32 accumulator (bits 4-5 = 1), A and
+// B bf16 (bits 7-9 and 10-12 = 1), both K-major, N >> 3 in bits 17-22, M >> 4
+// in bits 24-28.
+__host__ __device__ constexpr uint32_t fw_idesc(int M, int N)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+DSV4CU_DEV void fw_mma(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile("{\n\t.reg .pred p;\n\t"
+                 "setp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+                 ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+                 : "memory");
+}
+
+// Two fp32 -> one bf16x2 word (round to nearest; exact for these values).
+DSV4CU_DEV uint32_t fw_bf2(float a, float b)
+{
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// f16x2 word times a power of two -> bf16x2 word.
+DSV4CU_DEV uint32_t fw_scale_bf2(uint32_t h2, float sc)
+{
+    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h2));
+    return fw_bf2(f.x * sc, f.y * sc);
+}
+
+// Activation rows as bf16 terms. terms = 1: xb[t][c] = RN_bf16(x[t][c]);
+// terms = 2: rows 2t and 2t + 1 hold hi = RN_bf16(x) and lo = RN_bf16(x - hi)
+// (x - hi is exact in fp32; hi + lo carries 16 significand bits).
+__global__ void fw_xbf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ xb, int cols, long n4,
+                                int terms)
+{
+    const int c4 = cols / 4;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
+        uint2 hi;
+        hi.x = fw_bf2(v.x, v.y);
+        hi.y = fw_bf2(v.z, v.w);
+        if (terms == 1) {
+            reinterpret_cast<uint2 *>(xb)[i] = hi;
+            continue;
+        }
+        const long t = i / c4, c = i - t * c4;
+        const float2 h01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&hi.x));
+        const float2 h23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&hi.y));
+        uint2 lo;
+        lo.x = fw_bf2(v.x - h01.x, v.y - h01.y);
+        lo.y = fw_bf2(v.z - h23.x, v.w - h23.y);
+        reinterpret_cast<uint2 *>(xb)[(2 * t) * c4 + c] = hi;
+        reinterpret_cast<uint2 *>(xb)[(2 * t + 1) * c4 + c] = lo;
+    }
+}
+
+__global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant__ CUtensorMap tb, const FwParams p)
+{
+    extern __shared__ uint8_t fw_raw[];
+    __shared__ __align__(8) uint64_t a_full[FW_STAGES], b_full[FW_STAGES], empty[FW_STAGES], accf[2], acce[2],
+        drain;
+    __shared__ uint32_t tmem_holder;
+    uint8_t *smem = (uint8_t *)(((uintptr_t)fw_raw + 1023) & ~(uintptr_t)1023);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kch = p.cols / FW_KC, ntiles = p.tiles_m * p.tiles_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < FW_STAGES; s++) {
+            mbar_init(&a_full[s], FW_CONV_WARPS);
+            mbar_init(&b_full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&accf[i], 1);
+            mbar_init(&acce[i], FW_EPI_WARPS);
+        }
+        mbar_init(&drain, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        umma::tmem_alloc(&tmem_holder, 512);
+        umma::tmem_relinquish();
+    }
+    umma::fence_before();
+    __syncthreads();
+    umma::fence_after();
+    const uint32_t tmem = tmem_holder;
+
+    if (warp == 0) {
+        // ------------------------------------------------ activation chunks
+        if (lane == 0) {
+            int g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int tn = t / p.tiles_m;
+                for (int kc = 0; kc < kch; kc++, g++) {
+                    const int s = g % FW_STAGES, u = g / FW_STAGES;
+                    if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1, p.err, FWE_EMPTY)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&b_full[s], FW_B_BYTES);
+                    tma_load_2d(smem + s * FW_STAGE + FW_A_BYTES, &tb, kc * FW_KC, tn * FW_N, &b_full[s]);
+                }
+            }
+            // every issued copy lands before the CTA can exit
+            for (int j = max(0, g - FW_STAGES); j < g; j++)
+                mbar_wait(&b_full[j % FW_STAGES], (j / FW_STAGES) & 1, nullptr, 0);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = fw_idesc(FW_M, FW_N);
+            int g = 0, tc = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, tc++) {
+                const int ab = tc & 1, use = tc >> 1;
+                if (use > 0 && !mbar_wait(&acce[ab], (use - 1) & 1, p.err, FWE_ACCE)) break;
+                umma::fence_after();
+                const uint32_t d = tmem + ab * FW_N;
+                for (int kc = 0; kc < kch; kc++, g++) {
+                    const int s = g % FW_STAGES, u = g / FW_STAGES;
+                    if (!mbar_wait(&a_full[s], u & 1, p.err, FWE_AFULL) ||
+                        !mbar_wait(&b_full[s], u & 1, p.err, FWE_BFULL)) {
+                        ok = false;
+                        break;
+                    }
+                    umma::fence_after();
+                    const uint8_t *st = smem + s * FW_STAGE;
+#pragma unroll
+                    for (int k = 0; k < FW_KC / 16; k++)
+                        fw_mma(d, umma::desc_sw128(st + 32 * k), umma::desc_sw128(st + FW_A_BYTES + 32 * k), idesc,
+                               (kc > 0 || k > 0) ? 1u : 0u);
+                    umma::commit(&empty[s]);
+                }
+                if (ok) umma::commit(&accf[ab]);
+            }
+            // the MMAs in flight complete before TMEM is released
+            umma::commit(&drain);
+            mbar_wait(&drain, 0, p.err, FWE_DRAIN);
+        }
+    } else if (warp < 2 + FW_CONV_WARPS) {
+        // ------------------------------------------------ weight converters
+        // The CTA's (tile, chunk) steps in order; the packed bytes and the
+        // scale of the next two steps are in flight while this step waits for
+        // its stage and converts, so the L2 round trip overlaps the work.
+        // Positions advance incrementally (one division per tile).
+        const int cw = warp - 2, r = 16 * cw + (lane >> 1), h = lane & 1;
+        struct Pos {
+            int t, kc;
+            const uint8_t *wrow, *srow;
+        };
+        auto set_tile = [&](Pos &q) {
+            q.wrow = nullptr;
+            if (q.t >= ntiles) return;
+            const int row = (q.t % p.tiles_m) * FW_M + r;
+            if (row >= p.rows) return;
+            q.wrow = p.w + (size_t)row * p.row_bytes;
+            q.srow = p.s + (size_t)(row >> p.blk_r_log2) * p.s_cols;
+        };
+        auto advance = [&](Pos &q) {
+            if (++q.kc == kch) {
+                q.kc = 0;
+                q.t += gridDim.x;
+                set_tile(q);
+            }
+        };
+        auto fetch = [&](const Pos &q, uint4 &r0, uint4 &r1, float &sc) {
+            r0 = make_uint4(0u, 0u, 0u, 0u);
+            r1 = r0;
+            sc = 0.0f;
+            if (!q.wrow) return;
+            const int c0 = q.kc * FW_KC + 32 * h;          // this lane's 32 elements (one scale block)
+            if (p.fp4) {
+                r0 = __ldg(reinterpret_cast<const uint4 *>(q.wrow + c0 / 2));
+            } else {
+                r0 = __ldg(reinterpret_cast<const uint4 *>(q.wrow + c0));
+                r1 = __ldg(reinterpret_cast<const uint4 *>(q.wrow + c0 + 16));
+            }
+            sc = e8m0_to_f32(__ldg(q.srow + (c0 >> p.blk_c_log2)));
+        };
+        const int total = (blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0) * kch;
+        Pos pf{(int)blockIdx.x, 0, nullptr, nullptr};
+        set_tile(pf);
+        uint4 a0, a1, b0, b1;
+        float as, bs;
+        fetch(pf, a0, a1, as);                              // step 0
+        advance(pf);
+        fetch(pf, b0, b1, bs);                              // step 1
+        advance(pf);
+        for (int g = 0; g < total; g++) {
+            const int s = g % FW_STAGES, u = g / FW_STAGES;
+            const uint4 raw0 = a0, raw1 = a1;
+            const float sc = as;
+            a0 = b0;
+            a1 = b1;
+            as = bs;
+            fetch(pf, b0, b1, bs);                          // step g + 2
+            advance(pf);
+            bool free_ok = true;
+            if (lane == 0 && u > 0) free_ok = mbar_wait(&empty[s], (u - 1) & 1, p.err, FWE_EMPTY);
+            if (!__shfl_sync(0xFFFFFFFFu, free_ok, 0)) break;
+            uint32_t o[16];                                     // 32 bf16 values
+            if (p.fp4) {
+                const uint32_t wv[4] = {raw0.x, raw0.y, raw0.z, raw0.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    uint32_t h0, h1, h2, h3;
+                    cvt_e2m1x8(wv[i], h0, h1, h2, h3);
+                    o[4 * i] = fw_scale_bf2(h0, sc);
+                    o[4 * i + 1] = fw_scale_bf2(h1, sc);
+                    o[4 * i + 2] = fw_scale_bf2(h2, sc);
+                    o[4 * i + 3] = fw_scale_bf2(h3, sc);
+                }
+            } else {
+                const uint32_t wv[8] = {raw0.x, raw0.y, raw0.z, raw0.w, raw1.x, raw1.y, raw1.z, raw1.w};
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    uint32_t lo, hi;
+                    cvt_e4m3x4(wv[i], lo, hi);
+                    o[2 * i] = fw_scale_bf2(lo, sc);
+                    o[2 * i + 1] = fw_scale_bf2(hi, sc);
+                }
+            }
+            // 16-byte chunks 4h .. 4h + 3 of row r, 128-byte swizzle
+            uint8_t *arow = smem + s * FW_STAGE + r * 128;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int cchunk = (4 * h + j) ^ (r & 7);
+                *reinterpret_cast<uint4 *>(arow + 16 * cchunk) =
+                    make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[s]);
+        }
+    } else {
+        // ------------------------------------------------ epilogue
+        const int q = warp & 3;
+        int tc = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, tc++) {
+            const int ab = tc & 1, use = tc >> 1;
+            bool ok = true;
+            if (lane == 0) ok = mbar_wait(&accf[ab], use & 1, p.err, FWE_ACCF);
+            if (!__shfl_sync(0xFFFFFFFFu, ok, 0)) break;
+            umma::fence_after();
+            const int tm = t % p.tiles_m, tn = t / p.tiles_m;
+            const int row = tm * FW_M + q * 32 + lane;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + ab * FW_N;
+            for (int c8 = 0; c8 < FW_N; c8 += 8) {
+                float v[8];
+                umma::ld_x8(tbase + c8, v);
+                if (row >= p.rows) continue;
+                if (p.terms == 1) {
+                    const int t0 = tn * FW_N + c8;
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        if (t0 + i < p.nt) p.y[(size_t)(t0 + i) * p.rows + row] = v[i];
+                } else {                            // columns 2j, 2j + 1: hi and lo term of one token
+                    const int t0 = (tn * FW_N + c8) / 2;
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        if (t0 + i < p.nt) p.y[(size_t)(t0 + i) * p.rows + row] = v[2 * i] + v[2 * i + 1];
+                }
+            }
+            umma::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[ab]);
+        }
+    }
+    umma::fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        umma::fence_after();
+        umma::tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace dsv4cu
+
+using namespace dsv4cu;
+
+extern "C" size_t dsv4cu_gemm_bf16w_workspace(const dsv4cu_qmat *m, int nt, int terms)
+{
+    if (!m || nt <= 0 || terms < 1 || terms > 2) return 0;
+    return dsv4cu_align256((size_t)nt * terms * m->cols * 2);
+}
+
+extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m, int nt, int terms,
+                                 void *stream)
+{
+    if (terms < 1 || terms > 2) return dsv4cu_set_error(DSV4CU_ERR_ARG, "gemm_bf16w: terms %d (1 or 2)", terms);
+    if (!ctx || !y || !x || !m || !m->w || !m->s) return dsv4cu_set_error(DSV4CU_ERR_ARG, "gemm_bf16w: NULL argument");
+    if (nt <= 0) return DSV4CU_OK;
+    const bool fp4 = m->wdt == DSV4CU_WFP4;
+    if (!fp4 && m->wdt != DSV4CU_WFP8)
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED, "gemm_bf16w: FP8 or FP4 weights only");
+    const int row_bytes = fp4 ? m->cols / 2 : m->cols;
+    const auto pow2 = [](int v) { return v > 0 && (v & (v - 1)) == 0; };
+    if (m->rows <= 0 || m->cols <= 0 || m->cols % FW_KC || !pow2(m->blk_r) || !pow2(m->blk_c) || m->blk_c < 32 ||
+        ((uintptr_t)m->w & 15u) || row_bytes % 16 || ((uintptr_t)x & 15u))
+        return dsv4cu_set_error(DSV4CU_ERR_UNSUPPORTED,
+                                "gemm_bf16w: needs cols %% 64 == 0, power-of-two blocks with blk_c >= 32, 16-byte "
+                                "aligned weights and x (rows %d cols %d blk %dx%d)", m->rows, m->cols, m->blk_r,
+                                m->blk_c);
+    cudaStream_t st = (cudaStream_t)stream;
+    void *ws = nullptr;
+    int r = dsv4cu_ws_get(ctx, dsv4cu_gemm_bf16w_workspace(m, nt, terms), &ws);
+    if (r) return r;
+    __nv_bfloat16 *xb = (__nv_bfloat16 *)ws;
+    const long n4 = (long)nt * m->cols / 4;
+    fw_xbf16_kernel<<<(int)min(4096L, (n4 + 255) / 256), 256, 0, st>>>(x, xb, m->cols, n4, terms);
+    DSV4CU_LAUNCH_CHECK();
+    CUtensorMap tb;
+    if ((r = tmap_encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, (uint64_t)m->cols, (uint64_t)nt * terms,
+                            (uint64_t)m->cols * 2, FW_KC, FW_N, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return r;
+    FwParams p;
+    p.w = (const uint8_t *)m->w;
+    p.s = (const uint8_t *)m->s;
+    p.rows = m->rows;
+    p.cols = m->cols;
+    p.fp4 = fp4;
+    p.blk_r_log2 = __builtin_ctz((unsigned)m->blk_r);
+    p.blk_c_log2 = __builtin_ctz((unsigned)m->blk_c);
+    p.s_cols = (m->cols + m->blk_c - 1) / m->blk_c;
+    p.row_bytes = row_bytes;
+    p.tiles_m = (m->rows + FW_M - 1) / FW_M;
+    p.tiles_n = (nt * terms + FW_N - 1) / FW_N;
+    p.nt = nt;
+    p.terms = terms;
+    p.y = y;
+    p.err = ctx->status;
+    static SmemLimit lim;
+    DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)fw_kernel, FW_SMEM));
+    const int grid = min(ctx->sm_count, p.tiles_m * p.tiles_n);
+    fw_kernel<<<grid, FW_THREADS, FW_SMEM, st>>>(tb, p);
+    DSV4CU_LAUNCH_CHECK();
+    return DSV4CU_OK;
+}

@@ -28,6 +28,21 @@ static EncodeTiledFn encode_fn()
     return fn;
 }
 
+int tmap_encode_2d(CUtensorMap *map, CUtensorMapDataType type, const void *base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle)
+{
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {box_inner, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, type, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return dsv4cu_set_error(DSV4CU_ERR_CUDA, "cuTensorMapEncodeTiled(2-D): %d", (int)r);
+    return DSV4CU_OK;
+}
+
 bool tmap_weights_ok(const dsv4cu_qmat *q)
 {
     const int rb = row_bytes_of(q->wdt, q->cols);

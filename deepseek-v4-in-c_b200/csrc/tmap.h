@@ -24,4 +24,10 @@ bool tmap_scales_stageable(const dsv4cu_qmat *q);
 // DSV4CU_* status; *staged tells whether the scale map was written.
 int tmap_encode(const dsv4cu_qmat *q, CUtensorMap *wmap, CUtensorMap *smap, int *staged);
 
+// A 2-D map of any element type: `inner` elements per row, `outer` rows of
+// `row_bytes`, boxes of box_inner x box_rows, the given swizzle, zero fill
+// outside the tensor.
+int tmap_encode_2d(CUtensorMap *map, CUtensorMapDataType type, const void *base, uint64_t inner, uint64_t outer,
+                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swizzle);
+
 }  // namespace dsv4cu

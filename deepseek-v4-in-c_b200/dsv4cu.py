@@ -65,6 +65,8 @@ def lib() -> C.CDLL:
             "dsv4cu_ctx_inject": (i, [vp, i]),
             "dsv4cu_mmq_workspace": (sz, [vp, i]),
             "dsv4cu_mmq": (i, [vp, vp, vp, vp, i, vp]),
+            "dsv4cu_gemm_bf16w": (i, [vp, vp, vp, vp, i, i, vp]),
+            "dsv4cu_gemm_bf16w_workspace": (sz, [vp, i, i]),
             "dsv4cu_gemv_workspace": (sz, [vp, i]),
             "dsv4cu_gemv": (i, [vp, vp, vp, vp, i, vp]),
             "dsv4cu_gemv_ev": (i, [vp, vp, vp, vp, i, vp, vp]),
@@ -375,6 +377,11 @@ class Device:
     def mmq(self, y, x, m: QMat, nt: int):
         check(self.L.dsv4cu_mmq(self.ctx, self.ptr(y), self.ptr(x), C.byref(m), nt, self.stream()),
               "dsv4cu_mmq")
+
+    def gemm_bf16w(self, y, x, m: QMat, nt: int, terms: int = 1):
+        """Exact-weight GEMM on the bf16 tensor cores (dsv4cu_gemm_bf16w), 1 or 2 bf16 activation terms."""
+        check(self.L.dsv4cu_gemm_bf16w(self.ctx, self.ptr(y), self.ptr(x), C.byref(m), nt, terms, self.stream()),
+              "dsv4cu_gemm_bf16w")
 
     def gemv(self, y, x, m: QMat, nt: int, events=None):
         """Decode GEMV (dsv4cu_gemv / dsv4cu_gemv_ev): one or two tokens streamed."""

@@ -140,6 +140,19 @@ size_t dsv4cu_mat_workspace(const dsv4cu_mat *m, int nt, int terms);
 int dsv4cu_mat_gemm(dsv4cu_ctx *ctx, const dsv4cu_mat *m, float *y, const float *x,
                     int nt, int terms, void *stream);
 
+/* Exact-weight GEMM on the bf16 tensor cores (tcgen05 kind::f16): the
+ * prefill GEMM's other numerics mode. Every weight w * 2^e of an FP8 or FP4
+ * matrix is a bf16 value exactly and is used as such; the activations enter
+ * as `terms` bf16 terms: 1 = x rounded to nearest (max-rel ~1.1e-3 against
+ * fp32 activations on Gaussian data, 2^-9 per activation), 2 = hi + lo
+ * (~1e-5; twice the MMA work). Apart from that rounding the result is fp32
+ * accumulation: against the reference fed the same rounded activations the
+ * difference is ~1e-7. Needs cols % 64 == 0, power-of-two scale blocks with
+ * blk_c >= 32, 16-byte aligned weights and x. y [nt][rows] fp32. */
+size_t dsv4cu_gemm_bf16w_workspace(const dsv4cu_qmat *m, int nt, int terms);
+int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m, int nt, int terms,
+                      void *stream);
+
 /* dsv4cu_mat_gemm with an explicit tile configuration: nb B columns per tile
  * (8, 16, 32, 64, 128, 192 or 256; terms x tokens per tile) and kb 128-wide K
  * chunks per pipeline stage (1, 2 or 4; lowered until it divides cols/128).
