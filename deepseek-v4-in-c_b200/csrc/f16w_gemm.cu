@@ -14,18 +14,21 @@
 // is fp32 accumulation.
 //
 // Tile: 128 weight rows (MMA M) x 256 tokens (N), K in 64-element chunks (one
-// 128-byte bf16 row per operand row, 128-byte swizzle). Roles, 448 threads,
+// 128-byte bf16 row per operand row, 128-byte swizzle). Roles, 704 threads,
 // one CTA per SM, persistent over tiles (tile t = row tile t % tiles_m, token
 // tile t / tiles_m):
-//   warp 0       TMA of the bf16 activation chunk (256 rows x 128 bytes);
+//   warp 0       TMA of the stage's bf16 activation chunk (256 rows x 128
+//                bytes) and of its packed weights (128 rows x 64 or 32 bytes),
+//                both counted on one barrier;
 //   warp 1       TMEM (two 256-column fp32 accumulators) and the single MMA
 //                thread: four K = 16 MMAs per chunk, tcgen05.commit frees the
 //                stage, the tile's last commit hands the accumulator over;
-//   warps 2-9    converters: each warp dequantizes 16 weight rows of the chunk
-//                straight from the packed matrix (lane = row, half chunk),
+//   warps 2-17   converters: each warp dequantizes 8 weight rows of the chunk
+//                from the packed box in shared memory (4 lanes per row, 16
+//                elements each; the E8M0 scales two steps ahead from L2),
 //                cvt to f16, times the block scale, to bf16 (all exact), and
 //                writes them swizzled into the stage; fence.proxy.async, arrive;
-//   warps 10-13  epilogue: tcgen05.ld of the accumulator (TMEM lane = weight
+//   warps 18-21  epilogue: tcgen05.ld of the accumulator (TMEM lane = weight
 //                row), y stored token by token (32 consecutive rows per store).
 // Every wait is bounded (2 s): a role that times out records an error code in
 // the context status word and leaves its loop; the others run into their own
@@ -44,13 +47,19 @@ constexpr int FW_M = 128;                 // weight rows per tile
 constexpr int FW_N = 256;                 // tokens per tile
 constexpr int FW_KC = 64;                 // K elements per stage
 constexpr int FW_STAGES = 4;
-constexpr int FW_CONV_WARPS = 8;
+constexpr int FW_CONV_WARPS = 16;
+constexpr int FW_RPW = FW_M / FW_CONV_WARPS;   // weight rows per converter warp
+constexpr int FW_LPR = 32 / FW_RPW;            // lanes per row
+constexpr int FW_EPL = FW_KC / FW_LPR;         // elements per lane and chunk (16 or 32: inside one scale block)
+constexpr int FW_CPL = FW_EPL / 8;             // 16-byte bf16 pieces per lane
+static_assert(FW_EPL == 16 || FW_EPL == 32, "converter lane layout");
 constexpr int FW_EPI_WARPS = 4;
 constexpr int FW_THREADS = 32 * (2 + FW_CONV_WARPS + FW_EPI_WARPS);
 constexpr int FW_A_BYTES = FW_M * 128;
 constexpr int FW_B_BYTES = FW_N * 128;
 constexpr int FW_STAGE = FW_A_BYTES + FW_B_BYTES;
-constexpr int FW_SMEM = FW_STAGES * FW_STAGE + 1024;
+constexpr int FW_RAW = FW_M * 64;          // packed weight box of a stage (FP8: 64 B rows, FP4: 32 B rows)
+constexpr int FW_SMEM = FW_STAGES * (FW_STAGE + FW_RAW) + 1024;
 
 enum { FWE_EMPTY = 41, FWE_AFULL = 42, FWE_BFULL = 43, FWE_ACCF = 44, FWE_ACCE = 45, FWE_DRAIN = 46 };
 
@@ -78,6 +87,29 @@ DSV4CU_DEV void fw_mma(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t ides
                  "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
                  ::"r"(d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
                  : "memory");
+}
+
+// Bounded wait without the suspend hint, for the single-thread roles (the MMA
+// issuer, the copy issuer): they poll, so a completed phase is seen at once.
+DSV4CU_DEV bool fw_spin(uint64_t *bar, uint32_t parity, int *err, int code)
+{
+    const uint32_t a = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; i++) {
+        uint32_t ok;
+        asm volatile("{\n\t.reg .pred p;\n\t"
+                     "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                     "selp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(ok) : "r"(a), "r"(parity) : "memory");
+        if (ok) return true;
+        if ((i & 255u) == 0u) {
+            const uint64_t now = globaltimer_ns();
+            if (i == 0) t0 = now;
+            else if (now - t0 > MBAR_TIMEOUT_NS) break;
+        }
+    }
+    if (err) atomicCAS(err, 0, code);
+    return false;
 }
 
 // Two fp32 -> one bf16x2 word (round to nearest; exact for these values).
@@ -121,7 +153,8 @@ __global__ void fw_xbf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__re
     }
 }
 
-__global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant__ CUtensorMap tb, const FwParams p)
+__global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant__ CUtensorMap tb,
+                                                           const __grid_constant__ CUtensorMap tw, const FwParams p)
 {
     extern __shared__ uint8_t fw_raw[];
     __shared__ __align__(8) uint64_t a_full[FW_STAGES], b_full[FW_STAGES], empty[FW_STAGES], accf[2], acce[2],
@@ -159,15 +192,19 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
             int g = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int tn = t / p.tiles_m;
+                const int tn = t / p.tiles_m, tm = t - tn * p.tiles_m;
+                const int wbox = p.fp4 ? FW_KC / 2 : FW_KC;    // packed bytes of a chunk row
                 for (int kc = 0; kc < kch; kc++, g++) {
                     const int s = g % FW_STAGES, u = g / FW_STAGES;
-                    if (u > 0 && !mbar_wait(&empty[s], (u - 1) & 1, p.err, FWE_EMPTY)) {
+                    if (u > 0 && !fw_spin(&empty[s], (u - 1) & 1, p.err, FWE_EMPTY)) {
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&b_full[s], FW_B_BYTES);
+                    // one barrier for both boxes: the converters wait on it for
+                    // the packed weights, the MMA for the activations
+                    mbar_arrive_expect_tx(&b_full[s], FW_B_BYTES + FW_M * wbox);
                     tma_load_2d(smem + s * FW_STAGE + FW_A_BYTES, &tb, kc * FW_KC, tn * FW_N, &b_full[s]);
+                    tma_load_2d(smem + FW_STAGES * FW_STAGE + s * FW_RAW, &tw, kc * wbox, tm * FW_M, &b_full[s]);
                 }
             }
             // every issued copy lands before the CTA can exit
@@ -182,13 +219,13 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, tc++) {
                 const int ab = tc & 1, use = tc >> 1;
-                if (use > 0 && !mbar_wait(&acce[ab], (use - 1) & 1, p.err, FWE_ACCE)) break;
+                if (use > 0 && !fw_spin(&acce[ab], (use - 1) & 1, p.err, FWE_ACCE)) break;
                 umma::fence_after();
                 const uint32_t d = tmem + ab * FW_N;
                 for (int kc = 0; kc < kch; kc++, g++) {
                     const int s = g % FW_STAGES, u = g / FW_STAGES;
-                    if (!mbar_wait(&a_full[s], u & 1, p.err, FWE_AFULL) ||
-                        !mbar_wait(&b_full[s], u & 1, p.err, FWE_BFULL)) {
+                    if (!fw_spin(&a_full[s], u & 1, p.err, FWE_AFULL) ||
+                        !fw_spin(&b_full[s], u & 1, p.err, FWE_BFULL)) {
                         ok = false;
                         break;
                     }
@@ -212,7 +249,7 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
         // scale of the next two steps are in flight while this step waits for
         // its stage and converts, so the L2 round trip overlaps the work.
         // Positions advance incrementally (one division per tile).
-        const int cw = warp - 2, r = 16 * cw + (lane >> 1), h = lane & 1;
+        const int cw = warp - 2, r = FW_RPW * cw + lane / FW_LPR, h = lane % FW_LPR;
         struct Pos {
             int t, kc;
             const uint8_t *wrow, *srow;
@@ -232,46 +269,51 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
                 set_tile(q);
             }
         };
-        auto fetch = [&](const Pos &q, uint4 &r0, uint4 &r1, float &sc) {
-            r0 = make_uint4(0u, 0u, 0u, 0u);
-            r1 = r0;
+        auto fetch = [&](const Pos &q, float &sc) {
             sc = 0.0f;
             if (!q.wrow) return;
-            const int c0 = q.kc * FW_KC + 32 * h;          // this lane's 32 elements (one scale block)
-            if (p.fp4) {
-                r0 = __ldg(reinterpret_cast<const uint4 *>(q.wrow + c0 / 2));
-            } else {
-                r0 = __ldg(reinterpret_cast<const uint4 *>(q.wrow + c0));
-                r1 = __ldg(reinterpret_cast<const uint4 *>(q.wrow + c0 + 16));
-            }
+            const int c0 = q.kc * FW_KC + FW_EPL * h;      // this lane's elements (one scale block)
             sc = e8m0_to_f32(__ldg(q.srow + (c0 >> p.blk_c_log2)));
         };
+        const int wbox = p.fp4 ? FW_KC / 2 : FW_KC;
         const int total = (blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0) * kch;
         Pos pf{(int)blockIdx.x, 0, nullptr, nullptr};
         set_tile(pf);
-        uint4 a0, a1, b0, b1;
         float as, bs;
-        fetch(pf, a0, a1, as);                              // step 0
+        fetch(pf, as);                                      // step 0
         advance(pf);
-        fetch(pf, b0, b1, bs);                              // step 1
+        fetch(pf, bs);                                      // step 1
         advance(pf);
         for (int g = 0; g < total; g++) {
             const int s = g % FW_STAGES, u = g / FW_STAGES;
-            const uint4 raw0 = a0, raw1 = a1;
             const float sc = as;
-            a0 = b0;
-            a1 = b1;
             as = bs;
-            fetch(pf, b0, b1, bs);                          // step g + 2
+            fetch(pf, bs);                                  // step g + 2
             advance(pf);
-            bool free_ok = true;
-            if (lane == 0 && u > 0) free_ok = mbar_wait(&empty[s], (u - 1) & 1, p.err, FWE_EMPTY);
-            if (!__shfl_sync(0xFFFFFFFFu, free_ok, 0)) break;
-            uint32_t o[16];                                     // 32 bf16 values
+            // the packed box of this stage has landed (so the MMAs of the
+            // stage's previous use are done: the copy waited for them)
+            bool full_ok = true;
+            if (lane == 0) full_ok = mbar_wait(&b_full[s], u & 1, p.err, FWE_BFULL);
+            if (!__shfl_sync(0xFFFFFFFFu, full_ok, 0)) break;
+            const uint8_t *rb = smem + FW_STAGES * FW_STAGE + s * FW_RAW + r * wbox;
+            uint4 raw0 = make_uint4(0u, 0u, 0u, 0u), raw1 = raw0;
+            if (p.fp4) {
+                if constexpr (FW_EPL == 32) {
+                    raw0 = *reinterpret_cast<const uint4 *>(rb + FW_EPL / 2 * h);
+                } else {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(rb + FW_EPL / 2 * h);
+                    raw0.x = v.x;
+                    raw0.y = v.y;
+                }
+            } else {
+                raw0 = *reinterpret_cast<const uint4 *>(rb + FW_EPL * h);
+                if constexpr (FW_EPL == 32) raw1 = *reinterpret_cast<const uint4 *>(rb + FW_EPL * h + 16);
+            }
+            uint32_t o[FW_EPL / 2];                             // FW_EPL bf16 values
             if (p.fp4) {
                 const uint32_t wv[4] = {raw0.x, raw0.y, raw0.z, raw0.w};
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
+                for (int i = 0; i < FW_EPL / 8; i++) {
                     uint32_t h0, h1, h2, h3;
                     cvt_e2m1x8(wv[i], h0, h1, h2, h3);
                     o[4 * i] = fw_scale_bf2(h0, sc);
@@ -282,18 +324,18 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
             } else {
                 const uint32_t wv[8] = {raw0.x, raw0.y, raw0.z, raw0.w, raw1.x, raw1.y, raw1.z, raw1.w};
 #pragma unroll
-                for (int i = 0; i < 8; i++) {
+                for (int i = 0; i < FW_EPL / 4; i++) {
                     uint32_t lo, hi;
                     cvt_e4m3x4(wv[i], lo, hi);
                     o[2 * i] = fw_scale_bf2(lo, sc);
                     o[2 * i + 1] = fw_scale_bf2(hi, sc);
                 }
             }
-            // 16-byte chunks 4h .. 4h + 3 of row r, 128-byte swizzle
+            // 16-byte pieces FW_CPL h .. FW_CPL (h + 1) - 1 of row r, 128-byte swizzle
             uint8_t *arow = smem + s * FW_STAGE + r * 128;
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int cchunk = (4 * h + j) ^ (r & 7);
+            for (int j = 0; j < FW_CPL; j++) {
+                const int cchunk = (FW_CPL * h + j) ^ (r & 7);
                 *reinterpret_cast<uint4 *>(arow + 16 * cchunk) =
                     make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
             }
@@ -382,6 +424,10 @@ extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, cons
     if ((r = tmap_encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, (uint64_t)m->cols, (uint64_t)nt * terms,
                             (uint64_t)m->cols * 2, FW_KC, FW_N, CU_TENSOR_MAP_SWIZZLE_128B)))
         return r;
+    CUtensorMap tw;   // packed weights: 128 rows x one chunk (64 elements) per box, rows past the end read as 0
+    if ((r = tmap_encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, m->w, (uint64_t)row_bytes, (uint64_t)m->rows,
+                            (uint64_t)row_bytes, fp4 ? FW_KC / 2 : FW_KC, FW_M, CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return r;
     FwParams p;
     p.w = (const uint8_t *)m->w;
     p.s = (const uint8_t *)m->s;
@@ -401,7 +447,7 @@ extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, cons
     static SmemLimit lim;
     DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)fw_kernel, FW_SMEM));
     const int grid = min(ctx->sm_count, p.tiles_m * p.tiles_n);
-    fw_kernel<<<grid, FW_THREADS, FW_SMEM, st>>>(tb, p);
+    fw_kernel<<<grid, FW_THREADS, FW_SMEM, st>>>(tb, tw, p);
     DSV4CU_LAUNCH_CHECK();
     return DSV4CU_OK;
 }
