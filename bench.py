@@ -600,7 +600,8 @@ def run_prefill(args, rank, local_rank, world):
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
         pg = tdist
     dev = dsv4cu.Device(local_rank)
-    layer, keep = build_layer(dev, torch, N_EXPERTS)
+    NE = args.experts                          # 256 = config 3; fewer only for ncu captures
+    layer, keep = build_layer(dev, torch, NE)
     src = torch.empty(QKV_OUT * HIDDEN, dtype=torch.float32, device="cuda")
     dev.fill_normal(src, 9001, 0.0, 0.02)
     Wq = torch.empty(QKV_OUT * HIDDEN, dtype=torch.uint8, device="cuda")
@@ -612,6 +613,7 @@ def run_prefill(args, rank, local_rank, world):
     # terms (max-rel ~5e-6): faster than the MX path at 3 terms on this shape
     qm = dsv4cu.QMat(Wq.data_ptr(), Sq.data_ptr(), 2, QKV_OUT, HIDDEN, 128, 128)
     x, lg = pf_inputs(3000 + rank)
+    lg = np.ascontiguousarray(lg[:, :NE])
     dx, dl = torch.from_numpy(x).cuda(), torch.from_numpy(lg).cuda()
     out = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32, device="cuda")
     yq = torch.empty((PF_TOKENS, QKV_OUT), dtype=torch.float32, device="cuda")
