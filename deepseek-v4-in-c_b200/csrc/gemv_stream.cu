@@ -50,10 +50,10 @@ DSV4CU_DEV int smv_dense_cta(long long q, long long S, int G) { return (int)(((q
 // buffer 0): after the dependency wait (x may come from the previous kernel)
 // each warp splits blocks warp, warp + 16, ... of 32 values into the f16 hi /
 // lo pair and the block's power-of-two factor, the layout smv_consume reads.
+// The split of all nt tokens into bufs (hi, lo, per-block factor):
 template <int NT>
-DSV4CU_DEV bool smv_dense_split(uint8_t *bufs, const SmvDenseParams &p, int bstride)
+DSV4CU_DEV void smv_dense_split_run(uint8_t *bufs, const SmvDenseParams &p, int bstride)
 {
-    pdl_wait();
     constexpr int PER = SMV_MAXK / 32 / SMV_CW;     // blocks per warp per token at most
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nblk = p.K >> 5;
     for (int i = 0; i < p.nt; i++) {
@@ -91,6 +91,15 @@ DSV4CU_DEV bool smv_dense_split(uint8_t *bufs, const SmvDenseParams &p, int bstr
             }
         }
     }
+}
+
+// The consumers' prologue: the dependency wait (x may come from the previous
+// kernel), then the split.
+template <int NT>
+DSV4CU_DEV bool smv_dense_split(uint8_t *bufs, const SmvDenseParams &p, int bstride)
+{
+    pdl_wait();
+    smv_dense_split_run<NT>(bufs, p, bstride);
     return true;
 }
 

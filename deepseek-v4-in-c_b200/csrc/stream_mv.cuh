@@ -303,9 +303,9 @@ DSV4CU_DEV void smv_consume(uint32_t wsm, uint32_t ssm, uint32_t bsm, uint32_t z
 // with its power-of-two factor.
 DSV4CU_DEV void smv_split32(float v, uint16_t &hi, uint16_t &lo, float &fac)
 {
-    float a = isfinite(v) ? fabsf(v) : 0.0f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, o));
+    // block maximum of |v| as an unsigned warp max of the bit patterns
+    const float a =
+        __uint_as_float(__reduce_max_sync(0xFFFFFFFFu, __float_as_uint(isfinite(v) ? fabsf(v) : 0.0f)));
     // P = 15 - e with a = m 2^e, m in [0.5, 1) (frexp's exponent, read from
     // the bits: a subnormal a counts its leading zeros), clamped to +-125, so
     // that 2^P and 2^-P are normal floats and the scalings below are exact
@@ -326,19 +326,19 @@ DSV4CU_DEV void smv_split32(float v, uint16_t &hi, uint16_t &lo, float &fac)
 }
 
 // smv_split32 for N blocks of a warp at once (lane holds element `lane` of
-// block j in v[j]; live[j] false: skipped): the N max reductions run side by
-// side, every other step is smv_split32's.
+// block j in v[j]; live[j] false: skipped), every step as in smv_split32.
 template <int N>
 DSV4CU_DEV void smv_split32_n(const float (&v)[N], const bool (&live)[N], uint16_t (&hi)[N], uint16_t (&lo)[N],
                               float (&fac)[N])
 {
+    // Block maxima of |v|: non-negative floats order like their bit patterns,
+    // so one unsigned warp max (redux.sync) per block gives the same value as
+    // a shuffle tree.
     float a[N];
 #pragma unroll
-    for (int j = 0; j < N; j++) a[j] = isfinite(v[j]) ? fabsf(v[j]) : 0.0f;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int j = 0; j < N; j++) a[j] = fmaxf(a[j], __shfl_xor_sync(0xFFFFFFFFu, a[j], o));
+    for (int j = 0; j < N; j++)
+        a[j] = __uint_as_float(
+            __reduce_max_sync(0xFFFFFFFFu, __float_as_uint(isfinite(v[j]) ? fabsf(v[j]) : 0.0f)));
 #pragma unroll
     for (int j = 0; j < N; j++) {
         if (!live[j]) continue;
