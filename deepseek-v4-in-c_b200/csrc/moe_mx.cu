@@ -40,6 +40,7 @@ namespace dsv4cu {
 constexpr int MX_TERMS = 4;         // activation terms (results within ~1e-6 of fp32)
 constexpr int MXMOE_MAX_NT = 64;
 constexpr int MXMOE_MAX_TOPK = 16;
+constexpr int MXMOE_FUSE_COMBINE_NT = 4;   // tokens a fused-combine thread loops over at most
 
 // Workspace of one step.
 struct MxMoeWs {
@@ -55,6 +56,11 @@ struct MxMoeWs {
     uint8_t *xq2, *sfb2; // down B operand and its scale blocks
     float *gu;           // [npairs][2][inter] gate (w1) and up (w3) rows of each slot
     float *ypart;        // [npairs][hidden] down projection of each slot
+    // Arrival counters of the fused epilogues, zeroed by the decode prep
+    // kernel: [max_tiles][inter / 128] gate/up pairs (w1 and w3 tile of one
+    // column tile and row tile), then [hidden / 128] down row tiles.
+    int *pcnt;
+    int npcnt;
 };
 
 struct MxMoeShape {
@@ -110,6 +116,8 @@ static size_t mxmoe_layout(const MxMoeShape &s, char *base, MxMoeWs *w)
     t.sfb2 = (uint8_t *)take((size_t)s.max_tiles * (s.inter / 128) * s.nbb * 512);
     t.gu = (float *)take((size_t)s.npairs * 2 * s.inter * 4);
     t.ypart = (float *)take((size_t)s.npairs * s.hidden * 4);
+    t.npcnt = s.max_tiles * (s.inter / 128) + s.hidden / 128;
+    t.pcnt = (int *)take((size_t)t.npcnt * 4);
     if (w) *w = t;
     return off;
 }
@@ -422,6 +430,7 @@ __global__ void __launch_bounds__(PREP_THREADS) mxmoe_prep_kernel(
             ws.meta[1] = s_bad;
             ws.meta[2] = ntiles;
         }
+        for (int i = threadIdx.x; i < ws.npcnt; i += blockDim.x) ws.pcnt[i] = 0;
     }
 
     // Gate/up B operand: one warp per (column tile, slot, 128-wide K chunk)
@@ -446,7 +455,64 @@ struct MxMoeCommon {
     int *err;
     int max_tiles, n_mats;   // bounds of the column-tile table and of the matrix index (3 x experts)
     int once;                // every bucket fits one column tile: each weight tile is read once
+    // Fused epilogues (decode): the CTA that completes a (column tile, row
+    // tile) pair of w1 / w3 applies SwiGLU and writes the down B operand; the
+    // one that completes a down row tile over all column tiles combines it.
+    int fuse_swiglu, fuse_combine;
+    float limit;
+    int nt, topk, has_shared;
+    float *out;
 };
+
+// SwiGLU (dsv4_ops.c:61-79: up clamped both ways, gate from above only) of
+// rows [128 c, 128 c + 128) of one slot, split into e4m3 terms (mx_split128)
+// as column tl of column tile i of the down projection's B operand. Whole
+// warp; lane l takes rows 4 l .. 4 l + 3. The gate/up rows are read from L2.
+DSV4CU_DEV void mxmoe_swiglu_chunk(const MxMoeWs &ws, int slot, int i, int tl, int c, int inter, int terms, int tpt,
+                                   int NB, float limit)
+{
+    const int lane = threadIdx.x & 31, kc = inter >> 7, nbb = (NB + 127) / 128;
+    const float *g = ws.gu + (size_t)slot * 2 * inter + c * 128 + 4 * lane, *u = g + inter;
+    const float4 g4 = __ldcg(reinterpret_cast<const float4 *>(g)), u4 = __ldcg(reinterpret_cast<const float4 *>(u));
+    const float gv[4] = {g4.x, g4.y, g4.z, g4.w}, uv[4] = {u4.x, u4.y, u4.z, u4.w};
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        float gg = gv[k], uu = uv[k];
+        if (limit > 0.0f) {
+            uu = fminf(fmaxf(uu, -limit), limit);
+            gg = fminf(gg, limit);
+        }
+        v[k] = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.0f, expf(-gg))), uu);
+    }
+    uint32_t q[4];
+    uint8_t sb[4];
+    mx_split128(v, terms, q, sb);
+    uint8_t *row[4], *sf[4];
+    int step[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int n = j * tpt + tl;
+        row[j] = ws.xq2 + ((size_t)i * NB + n) * inter + c * 128;
+        sf[j] = ws.sfb2 + ((size_t)i * kc + c) * nbb * 512 + mx_sfb_offset(n, 0);
+        step[j] = 1;
+    }
+    mx_store128(q, sb, terms, row, sf, step);
+}
+
+// Output row `row` of token t: the routed pairs IN k ORDER with the routing
+// weights (dsv4_layer.c:109-113), then the shared expert unweighted (:115).
+// The slot rows are read from L2.
+DSV4CU_DEV float mxmoe_combine_one(const MxMoeWs &ws, int t, int topk, int hidden, int has_shared, int row)
+{
+    float o = 0.0f;
+    for (int k = 0; k < topk; k++) {
+        const int slot = ws.pos[t * topk + k];
+        if (slot >= 0) o = __fadd_rn(o, __fmul_rn(ws.wts[t * topk + k], __ldcg(ws.ypart + (size_t)slot * hidden + row)));
+    }
+    if (has_shared) o = __fadd_rn(o, __ldcg(ws.ypart + (size_t)(ws.b_off[ws.meta[0]] + t) * hidden + row));
+    return o;
+}
 
 DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc, const uint8_t *sfb)
 {
@@ -496,7 +562,22 @@ struct MoeGateUp {
             p.c.ws.gu[((size_t)slot * 2 + T.id1) * p.c.inter + T.id2 * 128 + row_l] = v;
         }
     }
-    DSV4CU_DEV static void finish(const Params &, const MxTile &, int, int *) {}
+    // Fused SwiGLU: the second of the (w1, w3) tiles of a column tile and row
+    // tile to finish turns their rows into the down operand's chunk T.id2.
+    DSV4CU_DEV static void finish(const Params &p, const MxTile &T, int row_l, int *words)
+    {
+        if (!p.c.fuse_swiglu) return;
+        __threadfence();
+        epi_sync();
+        if (row_l == 0) words[0] = atomicAdd(p.c.ws.pcnt + T.id0 * (p.c.inter >> 7) + T.id2, 1) == 1;
+        epi_sync();
+        if (!words[0]) return;
+        __threadfence();
+        const int i = T.id0, n = min(p.c.tpt, p.c.ws.c_cnt[i]);
+        for (int tl = row_l >> 5; tl < n; tl += 4)
+            mxmoe_swiglu_chunk(p.c.ws, p.c.ws.c_slot0[i] + tl, i, tl, T.id2, p.c.inter, p.c.terms, p.c.tpt, p.c.nb,
+                               p.c.limit);
+    }
     DSV4CU_DEV static void finish_all(const Params &, int, int, int *) {}
 };
 
@@ -537,13 +618,30 @@ struct MoeDown {
             p.c.ws.ypart[(size_t)slot * p.c.hidden + T.id2 * 128 + row_l] = v;
         }
     }
-    DSV4CU_DEV static void finish(const Params &, const MxTile &, int, int *) {}
+    // Fused combine: the last column tile to finish row tile T.id2 writes
+    // those output rows of every token.
+    DSV4CU_DEV static void finish(const Params &p, const MxTile &T, int row_l, int *words)
+    {
+        if (!p.c.fuse_combine) return;
+        __threadfence();
+        epi_sync();
+        if (row_l == 0) {
+            const int cols = min(p.c.ws.meta[2], p.c.max_tiles);
+            words[0] = atomicAdd(p.c.ws.pcnt + p.c.max_tiles * (p.c.inter >> 7) + T.id2, 1) == cols - 1;
+        }
+        epi_sync();
+        if (!words[0]) return;
+        __threadfence();
+        const int row = T.id2 * 128 + row_l;
+        for (int t = 0; t < p.c.nt; t++)
+            p.c.out[(size_t)t * p.c.hidden + row] = mxmoe_combine_one(p.c.ws, t, p.c.topk, p.c.hidden, p.c.has_shared, row);
+    }
     DSV4CU_DEV static void finish_all(const Params &, int, int, int *) {}
 };
 
-// SwiGLU (dsv4_ops.c:61-79: up clamped both ways, gate from above only) of
-// every slot, split into e4m3 terms (mx_split128) for the down projection's B
-// operand: one warp per (column tile, slot, group of cpt 128-wide chunks).
+// SwiGLU of every slot (mxmoe_swiglu_chunk) as its own launch, for the steps
+// whose gate/up epilogue does not fuse it: one warp per (column tile, slot,
+// group of cpt 128-wide chunks).
 __global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter, int terms, int tpt, int NB,
                                                            float limit, int cpt, int max_items)
 {
@@ -551,38 +649,13 @@ __global__ void __launch_bounds__(256) mxmoe_swiglu_kernel(MxMoeWs ws, int inter
     // this kernel's output.
     pdl_trigger();
     pdl_wait();
-    const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    const int gw = (int)((blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5);
     const int kc = inter >> 7, ntiles = ws.meta[2], groups = kc / cpt;
     if (gw >= max_items) return;
     const int it = gw / groups, grp = gw - it * groups, i = it / tpt, tl = it - i * tpt;
     if (i >= ntiles || tl >= ws.c_cnt[i]) return;
-    const int slot = ws.c_slot0[i] + tl, nbb = (NB + 127) / 128;
-    for (int c = grp * cpt; c < (grp + 1) * cpt; c++) {
-        const float *g = ws.gu + (size_t)slot * 2 * inter + c * 128 + 4 * lane, *u = g + inter;
-        float v[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            float gg = g[k], uu = u[k];
-            if (limit > 0.0f) {
-                uu = fminf(fmaxf(uu, -limit), limit);
-                gg = fminf(gg, limit);
-            }
-            v[k] = __fmul_rn(__fdiv_rn(gg, __fadd_rn(1.0f, expf(-gg))), uu);
-        }
-        uint32_t q[4];
-        uint8_t sb[4];
-        mx_split128(v, terms, q, sb);
-        uint8_t *row[4], *sf[4];
-        int step[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int n = j * tpt + tl;
-            row[j] = ws.xq2 + ((size_t)i * NB + n) * inter + c * 128;
-            sf[j] = ws.sfb2 + ((size_t)i * kc + c) * nbb * 512 + mx_sfb_offset(n, 0);
-            step[j] = 1;
-        }
-        mx_store128(q, sb, terms, row, sf, step);
-    }
+    const int slot = ws.c_slot0[i] + tl;
+    for (int c = grp * cpt; c < (grp + 1) * cpt; c++) mxmoe_swiglu_chunk(ws, slot, i, tl, c, inter, terms, tpt, NB, limit);
 }
 
 // Output rows: per token the routed pairs IN k ORDER with the routing
@@ -785,7 +858,7 @@ __global__ void __launch_bounds__(256) mxmoe_rows_out_kernel(MxMoeWs ws, int nro
 // topk = 1) instead of the weighted combine.
 static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &ws, int terms, float limit,
                        float *out, int *status, int sms, cudaStream_t st, cudaEvent_t *ev, bool rows_mode = false,
-                       const int *row_ids = nullptr)
+                       const int *row_ids = nullptr, bool fused = false)
 {
     const int RT = s.inter / 128, RTH = s.hidden / 128, nt = s.nt, topk = s.topk;
     MxMoeCommon c;
@@ -801,6 +874,16 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     c.max_tiles = s.max_tiles;
     c.n_mats = 3 * (L->n_experts + 1);
     c.once = s.nt <= s.tpt;   // a bucket holds at most nt slots
+    // Decode (the prep kernel zeroes the arrival counters): SwiGLU in the
+    // gate/up epilogue; the combine in the down epilogue while one thread's
+    // loop over the tokens stays short.
+    c.fuse_swiglu = fused && !rows_mode;
+    c.fuse_combine = c.fuse_swiglu && nt <= MXMOE_FUSE_COMBINE_NT;
+    c.limit = limit;
+    c.nt = nt;
+    c.topk = topk;
+    c.has_shared = s.has_shared;
+    c.out = out;
     // Persistent grids: the tile count is known only on the device.
     const int g1 = min(sms, s.max_tiles * 2 * RT), g2 = min(sms, s.max_tiles * RTH);
 
@@ -816,7 +899,7 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     r = mxmoe_dispatch<MoeGateUp>(s.NB, kb1, tb1, pg, g1, st);
     if (r) return r;
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[2], st));
-    {
+    if (!c.fuse_swiglu) {
         // Few slots (decode): one chunk per warp; many (prefill): whole rows.
         const int cpt = s.npairs > 1024 ? s.inter / 128 : 1;
         const int items = s.max_tiles * s.tpt * (s.inter / 128 / cpt);
@@ -833,7 +916,7 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     if (rows_mode)
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_rows_out_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)),
                                    dim3(256), 0, st, ws, nt, s.hidden, out, row_ids));
-    else
+    else if (!c.fuse_combine)   // else the down kernel's epilogue writes out
         DSV4CU_CUDA_TRY(launch_pdl(mxmoe_combine_kernel, dim3((unsigned)(((long)nt * (s.hidden / 4) + 255) / 256)),
                                    dim3(256), 0, st, ws, nt, topk, s.hidden, s.has_shared, out));
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[3], st));
@@ -866,7 +949,7 @@ int moe_mx_decode(const dsv4cu_moe *L, float *out, const float *x, const float *
     }
     if (ev) DSV4CU_CUDA_TRY(cudaEventRecord(ev[1], st));
 
-    return mxmoe_gemms(L, s, ws, MX_TERMS, limit, out, status, sms, st, ev);
+    return mxmoe_gemms(L, s, ws, MX_TERMS, limit, out, status, sms, st, ev, false, nullptr, true);
 }
 
 
