@@ -68,6 +68,7 @@ struct FwParams {
     const uint8_t *s;        // E8M0 scales [ceil(rows / blk_r)][s_cols]; blk_r, blk_c powers of two
     int rows, cols, fp4, blk_r_log2, blk_c_log2, s_cols, row_bytes;
     int tiles_m, tiles_n, nt, terms;   // terms: bf16 activation terms per token (1 or 2), B rows per token
+    int pre;                 // 1: the weights were dequantized to bf16 beforehand; tw maps them, no converters
     float *y;                // [nt][rows]
     int *err;
 };
@@ -153,6 +154,44 @@ __global__ void fw_xbf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__re
     }
 }
 
+// Whole matrix to bf16 once (pre-dequantized mode): the same exact
+// conversion as the converter warps, 16 elements of one row per thread
+// (inside one scale block, blk_c >= 32).
+__global__ void __launch_bounds__(256) fw_dequant_kernel(const FwParams p, uint4 *__restrict__ wb)
+{
+    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x, per_row = p.cols / 16;
+    if (i >= (long)p.rows * per_row) return;
+    const int row = (int)(i / per_row), c0 = (int)(i - (long)row * per_row) * 16;
+    const float sc = e8m0_to_f32(__ldg(p.s + (size_t)(row >> p.blk_r_log2) * p.s_cols + (c0 >> p.blk_c_log2)));
+    uint32_t o[8];
+    if (p.fp4) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2 *>(p.w + (size_t)row * p.row_bytes + c0 / 2));
+        const uint32_t wv[2] = {v.x, v.y};
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            uint32_t h0, h1, h2, h3;
+            cvt_e2m1x8(wv[j], h0, h1, h2, h3);
+            o[4 * j] = fw_scale_bf2(h0, sc);
+            o[4 * j + 1] = fw_scale_bf2(h1, sc);
+            o[4 * j + 2] = fw_scale_bf2(h2, sc);
+            o[4 * j + 3] = fw_scale_bf2(h3, sc);
+        }
+    } else {
+        const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p.w + (size_t)row * p.row_bytes + c0));
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint32_t lo, hi;
+            cvt_e4m3x4(wv[j], lo, hi);
+            o[2 * j] = fw_scale_bf2(lo, sc);
+            o[2 * j + 1] = fw_scale_bf2(hi, sc);
+        }
+    }
+    uint4 *dst = wb + (size_t)row * (p.cols / 8) + c0 / 8;
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
 __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant__ CUtensorMap tb,
                                                            const __grid_constant__ CUtensorMap tw, const FwParams p)
 {
@@ -201,10 +240,16 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
                         break;
                     }
                     // one barrier for both boxes: the converters wait on it for
-                    // the packed weights, the MMA for the activations
-                    mbar_arrive_expect_tx(&b_full[s], FW_B_BYTES + FW_M * wbox);
+                    // the packed weights, the MMA for the activations (and, in
+                    // the pre-dequantized mode, for the bf16 weight box too)
+                    if (p.pre) {
+                        mbar_arrive_expect_tx(&b_full[s], FW_B_BYTES + FW_A_BYTES);
+                        tma_load_2d(smem + s * FW_STAGE, &tw, kc * FW_KC, tm * FW_M, &b_full[s]);
+                    } else {
+                        mbar_arrive_expect_tx(&b_full[s], FW_B_BYTES + FW_M * wbox);
+                        tma_load_2d(smem + FW_STAGES * FW_STAGE + s * FW_RAW, &tw, kc * wbox, tm * FW_M, &b_full[s]);
+                    }
                     tma_load_2d(smem + s * FW_STAGE + FW_A_BYTES, &tb, kc * FW_KC, tn * FW_N, &b_full[s]);
-                    tma_load_2d(smem + FW_STAGES * FW_STAGE + s * FW_RAW, &tw, kc * wbox, tm * FW_M, &b_full[s]);
                 }
             }
             // every issued copy lands before the CTA can exit
@@ -224,7 +269,7 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
                 const uint32_t d = tmem + ab * FW_N;
                 for (int kc = 0; kc < kch; kc++, g++) {
                     const int s = g % FW_STAGES, u = g / FW_STAGES;
-                    if (!fw_spin(&a_full[s], u & 1, p.err, FWE_AFULL) ||
+                    if ((!p.pre && !fw_spin(&a_full[s], u & 1, p.err, FWE_AFULL)) ||
                         !fw_spin(&b_full[s], u & 1, p.err, FWE_BFULL)) {
                         ok = false;
                         break;
@@ -276,7 +321,7 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
             sc = e8m0_to_f32(__ldg(q.srow + (c0 >> p.blk_c_log2)));
         };
         const int wbox = p.fp4 ? FW_KC / 2 : FW_KC;
-        const int total = (blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0) * kch;
+        const int total = p.pre ? 0 : (blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0) * kch;
         Pos pf{(int)blockIdx.x, 0, nullptr, nullptr};
         set_tile(pf);
         float as, bs;
@@ -389,10 +434,32 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
 
 using namespace dsv4cu;
 
+// Weight conversion: in the converter warps (every 256-token tile converts
+// the weights again) or once per call into a bf16 copy in the workspace.
+static int g_fw_path = DSV4CU_BF16W_AUTO;
+
+extern "C" int dsv4cu_gemm_bf16w_set_path(int path)
+{
+    if (path != DSV4CU_BF16W_AUTO && path != DSV4CU_BF16W_CONVERT && path != DSV4CU_BF16W_PREDEQUANT)
+        return dsv4cu_set_error(DSV4CU_ERR_ARG, "gemm_bf16w_set_path: unknown path %d", path);
+    g_fw_path = path;
+    return DSV4CU_OK;
+}
+
+// Pre-dequantized when the call has more than one token tile (the weights
+// would otherwise be converted once per tile).
+static bool fw_use_pre(int nt, int terms)
+{
+    if (g_fw_path != DSV4CU_BF16W_AUTO) return g_fw_path == DSV4CU_BF16W_PREDEQUANT;
+    return (long)nt * terms > FW_N;
+}
+
 extern "C" size_t dsv4cu_gemm_bf16w_workspace(const dsv4cu_qmat *m, int nt, int terms)
 {
     if (!m || nt <= 0 || terms < 1 || terms > 2) return 0;
-    return dsv4cu_align256((size_t)nt * terms * m->cols * 2);
+    size_t b = dsv4cu_align256((size_t)nt * terms * m->cols * 2);
+    if (fw_use_pre(nt, terms)) b += dsv4cu_align256((size_t)m->rows * m->cols * 2);
+    return b;
 }
 
 extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m, int nt, int terms,
@@ -424,10 +491,6 @@ extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, cons
     if ((r = tmap_encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, (uint64_t)m->cols, (uint64_t)nt * terms,
                             (uint64_t)m->cols * 2, FW_KC, FW_N, CU_TENSOR_MAP_SWIZZLE_128B)))
         return r;
-    CUtensorMap tw;   // packed weights: 128 rows x one chunk (64 elements) per box, rows past the end read as 0
-    if ((r = tmap_encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, m->w, (uint64_t)row_bytes, (uint64_t)m->rows,
-                            (uint64_t)row_bytes, fp4 ? FW_KC / 2 : FW_KC, FW_M, CU_TENSOR_MAP_SWIZZLE_NONE)))
-        return r;
     FwParams p;
     p.w = (const uint8_t *)m->w;
     p.s = (const uint8_t *)m->s;
@@ -444,6 +507,23 @@ extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, cons
     p.terms = terms;
     p.y = y;
     p.err = ctx->status;
+    p.pre = fw_use_pre(nt, terms);
+    CUtensorMap tw;
+    if (p.pre) {
+        // bf16 copy of the weights after the activation rows; 128 rows x one
+        // chunk per box with the 128-byte swizzle (the converters' layout)
+        uint4 *wb = (uint4 *)((char *)ws + dsv4cu_align256((size_t)nt * terms * m->cols * 2));
+        const long n16 = (long)m->rows * (m->cols / 16);
+        fw_dequant_kernel<<<(unsigned)((n16 + 255) / 256), 256, 0, st>>>(p, wb);
+        DSV4CU_LAUNCH_CHECK();
+        if ((r = tmap_encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, wb, (uint64_t)m->cols, (uint64_t)m->rows,
+                                (uint64_t)m->cols * 2, FW_KC, FW_M, CU_TENSOR_MAP_SWIZZLE_128B)))
+            return r;
+    } else if ((r = tmap_encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, m->w, (uint64_t)row_bytes, (uint64_t)m->rows,
+                                   (uint64_t)row_bytes, fp4 ? FW_KC / 2 : FW_KC, FW_M, CU_TENSOR_MAP_SWIZZLE_NONE))) {
+        // packed weights: 128 rows x one chunk (64 elements) per box, rows past the end read as 0
+        return r;
+    }
     static SmemLimit lim;
     DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)fw_kernel, FW_SMEM));
     const int grid = min(ctx->sm_count, p.tiles_m * p.tiles_n);

@@ -113,6 +113,7 @@ def lib() -> C.CDLL:
             "dsv4cu_indexer_score_fp8": (i, [vp, vp, vp, vp, vp, vp, i, i, i, i, vp]),
             "dsv4cu_indexer_set_path": (i, [i]),
             "dsv4cu_sparse_attn_set_path": (i, [i]),
+            "dsv4cu_gemm_bf16w_set_path": (i, [i]),
             "dsv4cu_topk": (i, [vp, vp, vp, i, i, vp]),
             "dsv4cu_sparse_attn": (i, [vp, vp, vp, vp, i, vp, vp, i, i, i, f, vp]),
             "dsv4cu_indexer_offset": (i, [vp, i, i, vp]),
@@ -584,6 +585,14 @@ class Device:
         check(self.L.dsv4cu_indexer_set_path(self.INDEXER_PATH[path]), "dsv4cu_indexer_set_path")
 
     ATTN_PATH = {"auto": 0, "fp32": 1, "cluster8": 2}
+
+    BF16W_PATH = {"auto": 0, "convert": 1, "predequant": 2}
+
+    def gemm_bf16w_set_path(self, path: str):
+        """Where the exact-weight GEMM dequantizes (dsv4cu_gemm_bf16w_set_path):
+        "auto", "convert" (converter warps per token tile) or "predequant" (one
+        bf16 copy of the matrix per call); the results are the same bits."""
+        check(self.L.dsv4cu_gemm_bf16w_set_path(self.BF16W_PATH[path]), "dsv4cu_gemm_bf16w_set_path")
 
     def sparse_attn_set_path(self, path: str):
         """Chunk kernel of the sparse attention (dsv4cu_sparse_attn_set_path):

@@ -153,6 +153,15 @@ size_t dsv4cu_gemm_bf16w_workspace(const dsv4cu_qmat *m, int nt, int terms);
 int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, const dsv4cu_qmat *m, int nt, int terms,
                       void *stream);
 
+/* Where dsv4cu_gemm_bf16w dequantizes the weights (process-wide switch; the
+ * results are bit-identical either way). CONVERT: converter warps inside the
+ * GEMM, once per 256-token tile. PREDEQUANT: one pass writes the bf16 matrix
+ * into the workspace (rows x cols x 2 bytes more), then the GEMM loads it by
+ * TMA. AUTO (default): PREDEQUANT when nt x terms > 256. Set it before
+ * sizing the workspace. */
+enum { DSV4CU_BF16W_AUTO = 0, DSV4CU_BF16W_CONVERT = 1, DSV4CU_BF16W_PREDEQUANT = 2 };
+int dsv4cu_gemm_bf16w_set_path(int path);
+
 /* dsv4cu_mat_gemm with an explicit tile configuration: nb B columns per tile
  * (8, 16, 32, 64, 128, 192 or 256; terms x tokens per tile) and kb 128-wide K
  * chunks per pipeline stage (1, 2 or 4; lowered until it divides cols/128).

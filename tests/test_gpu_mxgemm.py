@@ -293,6 +293,32 @@ def test_bf16w_exact_weight_mode(dev, orc, wdt, rows, cols, nt, terms):
         assert e_fp32 <= (1e-3 if terms == 2 else 3e-3), e_fp32
 
 
+@pytest.mark.parametrize("wdt", [2, 3], ids=["fp8", "fp4"])
+@pytest.mark.parametrize("rows,cols,nt,terms", [(200, 1024, 300, 1), (1000, 2048, 700, 2), (6144, 4096, 4096, 1)])
+def test_bf16w_paths_bit_identical(dev, wdt, rows, cols, nt, terms):
+    """The exact-weight GEMM's two dequantization paths (converter warps per
+    token tile; one bf16 copy of the matrix loaded by TMA) feed the tensor
+    cores the same bf16 operands in the same order: the outputs are the same
+    bits, ragged rows and token counts included, up to the config-3 QKV
+    shape."""
+    t = __import__("torch")
+    W, S, Wd, Sd, q = _upload_qmat(dev, wdt, rows, cols, rows + 3 * nt + wdt)
+    x = t.from_numpy(np.random.default_rng(nt + terms).standard_normal((nt, cols)).astype(np.float32)).cuda()
+    out = {}
+    try:
+        for path in ("convert", "predequant"):
+            dev.gemm_bf16w_set_path(path)
+            y = canary.guarded_empty((nt, rows))
+            y.fill_(float("nan"))
+            dev.gemm_bf16w(y, x, q, nt, terms)
+            canary.check(y, "gemm_bf16w " + path)
+            out[path] = y.cpu().numpy()
+    finally:
+        dev.gemm_bf16w_set_path("auto")
+    assert np.isfinite(out["convert"]).all()
+    assert np.array_equal(out["convert"].view(np.uint32), out["predequant"].view(np.uint32))
+
+
 def test_bf16w_qkv_full_shape(dev, orc):
     """The config-3 QKV projection (FP8 6144 x 4096, 4096 tokens) in the
     exact-weight mode, one and two bf16 activation terms, 48 sampled tokens
