@@ -130,11 +130,12 @@ DSV4CU_DEV uint32_t fw_scale_bf2(uint32_t h2, float sc)
 // Activation rows as bf16 terms. terms = 1: xb[t][c] = RN_bf16(x[t][c]);
 // terms = 2: rows 2t and 2t + 1 hold hi = RN_bf16(x) and lo = RN_bf16(x - hi)
 // (x - hi is exact in fp32; hi + lo carries 16 significand bits).
-__global__ void fw_xbf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ xb, int cols, long n4,
-                                int terms)
+// Blocks blk = 0 .. nblk - 1 of a grid-stride pass.
+DSV4CU_DEV void fw_xbf16_part(const float *__restrict__ x, __nv_bfloat16 *__restrict__ xb, int cols, long n4,
+                              int terms, int blk, int nblk)
 {
     const int c4 = cols / 4;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    for (long i = blk * (long)blockDim.x + threadIdx.x; i < n4; i += (long)nblk * blockDim.x) {
         const float4 v = __ldg(reinterpret_cast<const float4 *>(x) + i);
         uint2 hi;
         hi.x = fw_bf2(v.x, v.y);
@@ -157,9 +158,9 @@ __global__ void fw_xbf16_kernel(const float *__restrict__ x, __nv_bfloat16 *__re
 // Whole matrix to bf16 once (pre-dequantized mode): the same exact
 // conversion as the converter warps, 16 elements of one row per thread
 // (inside one scale block, blk_c >= 32).
-__global__ void __launch_bounds__(256) fw_dequant_kernel(const FwParams p, uint4 *__restrict__ wb)
+DSV4CU_DEV void fw_dequant_part(const FwParams &p, uint4 *__restrict__ wb, int blk)
 {
-    const long i = blockIdx.x * (long)blockDim.x + threadIdx.x, per_row = p.cols / 16;
+    const long i = blk * (long)blockDim.x + threadIdx.x, per_row = p.cols / 16;
     if (i >= (long)p.rows * per_row) return;
     const int row = (int)(i / per_row), c0 = (int)(i - (long)row * per_row) * 16;
     const float sc = e8m0_to_f32(__ldg(p.s + (size_t)(row >> p.blk_r_log2) * p.s_cols + (c0 >> p.blk_c_log2)));
@@ -190,6 +191,20 @@ __global__ void __launch_bounds__(256) fw_dequant_kernel(const FwParams p, uint4
     uint4 *dst = wb + (size_t)row * (p.cols / 8) + c0 / 8;
     dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
     dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
+// The GEMM's operands in one launch: blocks [0, xblocks) write the activation
+// terms, the rest (pre-dequantized mode) the bf16 weights. The GEMM is
+// launched programmatically behind it and sets up while this runs.
+__global__ void __launch_bounds__(256) fw_prep_kernel(const float *__restrict__ x, __nv_bfloat16 *__restrict__ xb,
+                                                      int cols, long n4, int terms, int xblocks, const FwParams p,
+                                                      uint4 *__restrict__ wb)
+{
+    pdl_trigger();
+    if ((int)blockIdx.x < xblocks)
+        fw_xbf16_part(x, xb, cols, n4, terms, blockIdx.x, xblocks);
+    else
+        fw_dequant_part(p, wb, blockIdx.x - xblocks);
 }
 
 __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant__ CUtensorMap tb,
@@ -224,6 +239,8 @@ __global__ void __launch_bounds__(FW_THREADS, 1) fw_kernel(const __grid_constant
     __syncthreads();
     umma::fence_after();
     const uint32_t tmem = tmem_holder;
+    // Set-up above overlaps the operand pass; its outputs are read below.
+    pdl_wait();
 
     if (warp == 0) {
         // ------------------------------------------------ activation chunks
@@ -485,8 +502,6 @@ extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, cons
     if (r) return r;
     __nv_bfloat16 *xb = (__nv_bfloat16 *)ws;
     const long n4 = (long)nt * m->cols / 4;
-    fw_xbf16_kernel<<<(int)min(4096L, (n4 + 255) / 256), 256, 0, st>>>(x, xb, m->cols, n4, terms);
-    DSV4CU_LAUNCH_CHECK();
     CUtensorMap tb;
     if ((r = tmap_encode_2d(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, xb, (uint64_t)m->cols, (uint64_t)nt * terms,
                             (uint64_t)m->cols * 2, FW_KC, FW_N, CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -509,13 +524,17 @@ extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, cons
     p.err = ctx->status;
     p.pre = fw_use_pre(nt, terms);
     CUtensorMap tw;
-    if (p.pre) {
-        // bf16 copy of the weights after the activation rows; 128 rows x one
-        // chunk per box with the 128-byte swizzle (the converters' layout)
-        uint4 *wb = (uint4 *)((char *)ws + dsv4cu_align256((size_t)nt * terms * m->cols * 2));
-        const long n16 = (long)m->rows * (m->cols / 16);
-        fw_dequant_kernel<<<(unsigned)((n16 + 255) / 256), 256, 0, st>>>(p, wb);
+    // bf16 copy of the weights (pre-dequantized mode) after the activation
+    // rows; 128 rows x one chunk per box with the 128-byte swizzle (the
+    // converters' layout)
+    uint4 *wb = (uint4 *)((char *)ws + dsv4cu_align256((size_t)nt * terms * m->cols * 2));
+    {
+        const int xblocks = (int)min(4096L, (n4 + 255) / 256);
+        const long wblocks = p.pre ? ((long)m->rows * (m->cols / 16) + 255) / 256 : 0;
+        fw_prep_kernel<<<(unsigned)(xblocks + wblocks), 256, 0, st>>>(x, xb, m->cols, n4, terms, xblocks, p, wb);
         DSV4CU_LAUNCH_CHECK();
+    }
+    if (p.pre) {
         if ((r = tmap_encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, wb, (uint64_t)m->cols, (uint64_t)m->rows,
                                 (uint64_t)m->cols * 2, FW_KC, FW_M, CU_TENSOR_MAP_SWIZZLE_128B)))
             return r;
@@ -527,7 +546,6 @@ extern "C" int dsv4cu_gemm_bf16w(dsv4cu_ctx *ctx, float *y, const float *x, cons
     static SmemLimit lim;
     DSV4CU_CUDA_TRY(smem_limit(lim, (const void *)fw_kernel, FW_SMEM));
     const int grid = min(ctx->sm_count, p.tiles_m * p.tiles_n);
-    fw_kernel<<<grid, FW_THREADS, FW_SMEM, st>>>(tb, tw, p);
-    DSV4CU_LAUNCH_CHECK();
+    DSV4CU_CUDA_TRY(launch_pdl(fw_kernel, dim3(grid), dim3(FW_THREADS), FW_SMEM, st, tb, tw, p));
     return DSV4CU_OK;
 }
