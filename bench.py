@@ -74,6 +74,8 @@ def parse():
     ap.add_argument("--experts", type=int, default=256,
                     help="routed experts resident in HBM (256 = config 2; smaller only for ncu captures)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--bf16w-path", choices=["auto", "convert", "predequant"], default="auto",
+                    help="prefill: where the exact-weight QKV GEMM dequantizes in the step (for captures)")
     ap.add_argument("--batch", type=int, default=1, help="stack: decode batch per rank")
     ap.add_argument("--layers", type=int, default=43, help="stack: decoder layers (43 = config 5)")
     ap.add_argument("--workload", choices=["auto", "decode", "prefill", "gemv", "indexer", "ep", "stack"],
@@ -620,6 +622,8 @@ def run_prefill(args, rank, local_rank, world):
     out = torch.empty((PF_TOKENS, HIDDEN), dtype=torch.float32, device="cuda")
     yq = torch.empty((PF_TOKENS, QKV_OUT), dtype=torch.float32, device="cuda")
 
+    dev.gemm_bf16w_set_path(args.bf16w_path)
+
     def step(ev=None):
         dev.moe_prefill(layer, out, dx, dl, TOPK, ROUTE_SCALE, LIMIT, PF_TOKENS, PF_TERMS, events=ev)
         dev.gemm_bf16w(yq, dx, qm, PF_TOKENS, 2)
@@ -746,7 +750,7 @@ def run_prefill(args, rank, local_rank, world):
         modes.append({"qkv_mode": label, "qkv_ms": round(q_ms, 4), "qkv_useful_tflops": round(tf, 1),
                       "frac_of_peak": round(tf / pk, 4), "peak": round(pk, 1), "peak_is": pk_name,
                       "max_rel_err_vs_fp32_x": err})
-    dev.gemm_bf16w_set_path("auto")
+    dev.gemm_bf16w_set_path(args.bf16w_path)
     dev.check_status()
     ms = total_ms / args.steps
     res = {
