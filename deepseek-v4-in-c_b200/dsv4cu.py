@@ -41,6 +41,13 @@ class Expert(C.Structure):
     _fields_ = [("w1", QMat), ("w3", QMat), ("w2", QMat)]
 
 
+class TrunkTensor(C.Structure):
+    """DSV4TrunkTensor / dsv4cu_trunk_tensor (src/50_loader/dsv4_trunk.h:20-27)."""
+    _fields_ = [("slot", C.c_int32), ("dtype", C.c_int32), ("rows", C.c_int32), ("cols", C.c_int32),
+                ("wdt", C.c_int32), ("blk_r", C.c_int32), ("blk_c", C.c_int32),
+                ("off", C.c_int64), ("nbytes", C.c_int64)]
+
+
 _lib = None
 
 
@@ -127,6 +134,14 @@ def lib() -> C.CDLL:
             "dsv4cu_experts_load": (i, [C.POINTER(vp), vp, C.c_char_p, C.c_char_p, i, i, i, i, i, vp]),
             "dsv4cu_experts_free": (None, [vp]),
             "dsv4cu_experts_index": (i, [C.c_char_p, C.POINTER(i), C.POINTER(i), i, i, C.POINTER(C.c_int64)]),
+            "dsv4cu_trunk_manifest": (i, [C.c_char_p, C.POINTER(i), i, C.POINTER(C.c_int64), C.POINTER(i),
+                                          C.POINTER(TrunkTensor), i]),
+            "dsv4cu_trunk_load": (i, [C.POINTER(vp), C.c_char_p, i, i, vp]),
+            "dsv4cu_trunk_slot": (i, [vp, i, i, C.POINTER(TrunkTensor), C.POINTER(vp)]),
+            "dsv4cu_trunk_qmat": (i, [vp, i, i, C.POINTER(QMat)]),
+            "dsv4cu_trunk_widen": (i, [vp, i, i, vp, vp]),
+            "dsv4cu_trunk_resident_bytes": (C.c_int64, [vp]),
+            "dsv4cu_trunk_free": (None, [vp]),
             "dsv4cu_head": (i, [vp, vp, vp, vp, vp, i, vp]),
             "dsv4cu_quantize_fp8": (i, [vp, vp, vp, i, i, vp]),
             "dsv4cu_quantize_fp4": (i, [vp, vp, vp, i, i, vp]),
@@ -435,6 +450,35 @@ class Device:
     def experts_free(self, h):
         self.L.dsv4cu_experts_free(h)
 
+    def trunk_load(self, pack_dir: str, first: int = 0, count: int = 0):
+        """Layers [first, first + count) (count 0: to the last) of trunk.bin into
+        HBM (dsv4cu_trunk_load); returns an opaque handle."""
+        h = C.c_void_p()
+        check(self.L.dsv4cu_trunk_load(C.byref(h), pack_dir.encode(), first, count, self.stream()), "trunk_load")
+        return h
+
+    def trunk_slot(self, h, layer: int, slot: int):
+        """(record, device address) of a resident tensor (dsv4cu_trunk_slot)."""
+        d, p = TrunkTensor(), C.c_void_p()
+        check(self.L.dsv4cu_trunk_slot(h, layer, slot, C.byref(d), C.byref(p)), "trunk_slot")
+        return d, p.value
+
+    def trunk_qmat(self, h, layer: int, slot: int) -> QMat:
+        """Device descriptor of a packed matrix and its scales (dsv4cu_trunk_qmat)."""
+        q = QMat()
+        check(self.L.dsv4cu_trunk_qmat(h, layer, slot, C.byref(q)), "trunk_qmat")
+        return q
+
+    def trunk_widen(self, h, layer: int, slot: int, dst):
+        """A vector widened to f32 into the device tensor dst (dsv4cu_trunk_widen)."""
+        check(self.L.dsv4cu_trunk_widen(h, layer, slot, self.ptr(dst), self.stream()), "trunk_widen")
+
+    def trunk_resident_bytes(self, h) -> int:
+        return int(self.L.dsv4cu_trunk_resident_bytes(h))
+
+    def trunk_free(self, h):
+        self.L.dsv4cu_trunk_free(h)
+
     def moe_create(self, experts: list, shared: Expert | None, hidden: int, inter: int):
         """Prepare a MoE layer (dsv4cu_moe_create); returns an opaque handle."""
         arr = (Expert * len(experts))(*experts)
@@ -661,6 +705,23 @@ class Device:
 
     def round_bf16(self, x):
         check(self.L.dsv4cu_round_bf16(self.ptr(x), x.numel(), self.stream()), "round_bf16")
+
+
+def trunk_manifest(pack_dir: str, layer: int = -1):
+    """Host only: (n_layers, run, records) of a pack's trunk.idx; for layer >= 0
+    run = (file offset, bytes, widened bytes) and records its TrunkTensor list,
+    else both None."""
+    L = lib()
+    nl, nt = C.c_int(), C.c_int()
+    run = (C.c_int64 * 3)()
+    if layer < 0:
+        check(L.dsv4cu_trunk_manifest(pack_dir.encode(), C.byref(nl), -1, None, None, None, 0), "trunk_manifest")
+        return nl.value, None, None
+    check(L.dsv4cu_trunk_manifest(pack_dir.encode(), C.byref(nl), layer, run, C.byref(nt), None, 0), "trunk_manifest")
+    arr = (TrunkTensor * max(1, nt.value))()
+    check(L.dsv4cu_trunk_manifest(pack_dir.encode(), C.byref(nl), layer, run, C.byref(nt), arr, nt.value),
+          "trunk_manifest")
+    return nl.value, tuple(run), [arr[i] for i in range(nt.value)]
 
 
 def experts_index(index_dir: str, layer: int = -1, expert: int = -1):

@@ -220,6 +220,47 @@ void dsv4cu_experts_free(dsv4cu_expert_store *store);
  * w1, w1 scales, w2, w2 scales, w3, w3 scales. */
 int  dsv4cu_experts_index(const char *index_dir, int *n_layers, int *n_experts, int layer, int expert,
                           int64_t *loc);
+
+/* Dense trunk from the reference's pack into HBM (replaces dsv4_trunk_open,
+ * src/50_loader/dsv4_trunk.c:37-131, which reads trunk.bin into host memory;
+ * manifest format of src/50_loader/dsv4_trunk_manifest.c:24-110). A tensor
+ * record mirrors DSV4TrunkTensor (src/50_loader/dsv4_trunk.h:20-27): off is
+ * the byte offset within its layer's run, dtype the safetensors code
+ * (1 u8, 2 bf16, 3 f16, 4 f32, 5 e4m3, 6 e8m0, 7 i8, 8 i64), wdt DSV4CU_W*. */
+typedef struct {
+    int32_t slot;
+    int32_t dtype;
+    int32_t rows, cols;
+    int32_t wdt, blk_r, blk_c;
+    int64_t off;
+    int64_t nbytes;
+} dsv4cu_trunk_tensor;
+typedef struct dsv4cu_trunk dsv4cu_trunk;
+/* Host only: trunk.idx of `dir`. n_layers always; for layer >= 0 also
+ * run[0..2] = file offset, bytes, widened-vector bytes of that layer, its
+ * tensor count and up to cap tensor records. A missing or malformed index
+ * returns DSV4CU_ERR_IO (bad magic / version, n_layers, layout, layer or
+ * tensor line, dtype or format code, a tensor outside its run). */
+int  dsv4cu_trunk_manifest(const char *dir, int *n_layers, int layer, int64_t *run, int *n_tensors,
+                           dsv4cu_trunk_tensor *tensors, int cap);
+/* Layers first .. first + count - 1 (count <= 0: to the last) of trunk.bin
+ * into one device arena owned by *out (each run 4 KiB aligned; read in
+ * 64 MiB pieces through two pinned buffers, copied on `stream`, synchronised
+ * before return). A short read returns DSV4CU_ERR_IO. */
+int  dsv4cu_trunk_load(dsv4cu_trunk **out, const char *dir, int first, int count, void *stream);
+/* Device address and record of (layer, slot); DSV4CU_ERR_ARG when the layer
+ * is not resident or has no such slot. */
+int  dsv4cu_trunk_slot(const dsv4cu_trunk *trunk, int layer, int slot, dsv4cu_trunk_tensor *desc, void **dev);
+/* A packed matrix's device descriptor: weights from `slot`, shape and format
+ * from its record, scales (FP8 / FP4) from slot + 1 (the pack's X / X_S
+ * pairing, src/50_loader/dsv4_bind_layer.c:12-23). */
+int  dsv4cu_trunk_qmat(const dsv4cu_trunk *trunk, int layer, int slot, dsv4cu_qmat *q);
+/* A vector widened to f32 into dst on `stream`, as the reference's bind
+ * does (dsv4_widen_f32, src/40_io/dsv4_st.h:117-134): f32 copied, bf16
+ * widened exactly, other dtypes DSV4CU_ERR_UNSUPPORTED. */
+int  dsv4cu_trunk_widen(const dsv4cu_trunk *trunk, int layer, int slot, float *dst, void *stream);
+int64_t dsv4cu_trunk_resident_bytes(const dsv4cu_trunk *trunk);
+void dsv4cu_trunk_free(dsv4cu_trunk *trunk);
 int  dsv4cu_moe_create(dsv4cu_moe **out, const dsv4cu_expert *experts, int n_experts,
                        const dsv4cu_expert *shared, int hidden, int inter);
 void dsv4cu_moe_destroy(dsv4cu_moe *layer);
