@@ -459,6 +459,7 @@ struct MxMoeCommon {
     // tile) pair of w1 / w3 applies SwiGLU and writes the down B operand; the
     // one that completes a down row tile over all column tiles combines it.
     int fuse_swiglu, fuse_combine;
+    int shared_first;        // the shared expert is exactly the last column tile: its gate/up tiles go first
     float limit;
     int nt, topk, has_shared;
     float *out;
@@ -535,19 +536,39 @@ DSV4CU_DEV MxTile mxmoe_tile(const MxMoeCommon &c, int i, int m, int rt, int kc,
 
 // Gate/up tiles, t = (i * RT + rt) * 2 + mat: column tile i, 128-row tile rt
 // of w1 (mat 0) or w3 (mat 1). Results go to the per-slot gate/up rows.
+// When the shared expert fills exactly one column tile (the last), its 2 RT
+// tiles come first: their weights do not depend on the routing, so a CTA
+// whose first tile is one of them fills its stage ring before the wait for
+// the routing kernel (kPrefetchA), while that kernel still runs.
 struct MoeGateUp {
     struct Params {
         MxMoeCommon c;
     };
-    static constexpr bool kPrefetchA = false;   // the experts come from the routing kernel
+    static constexpr bool kPrefetchA = true;
+    DSV4CU_DEV static int shared_first(const Params &p) { return p.c.shared_first ? 2 * (p.c.inter >> 7) : 0; }
+    DSV4CU_DEV static int ntiles_pre(const Params &p) { return shared_first(p); }
+    DSV4CU_DEV static MxTile tile_pre(const Params &p, int t)   // A side only (column tile unknown yet)
+    {
+        return mxmoe_tile(p.c, 0, p.c.n_mats - 3 + (t & 1), t >> 1, p.c.hidden >> 7, p.c.ws.sfb1);
+    }
     DSV4CU_DEV static int ntiles(const Params &p) { return p.c.ws.meta[2] * 2 * (p.c.inter >> 7); }
     DSV4CU_DEV static int *err(const Params &p) { return p.c.err; }
     DSV4CU_DEV static int terms(const Params &p) { return p.c.terms; }
     DSV4CU_DEV static int tpt(const Params &p) { return p.c.tpt; }
     DSV4CU_DEV static MxTile tile(const Params &p, int t)
     {
-        const int RT = p.c.inter >> 7;
-        const int mat = t & 1, pr = t >> 1, i = pr / RT, rt = pr - i * RT;
+        const int RT = p.c.inter >> 7, sh = shared_first(p);
+        int mat, i, rt;
+        if (t < sh) {                       // the shared expert's column tile, the last one
+            mat = t & 1;
+            rt = t >> 1;
+            i = p.c.ws.meta[2] - 1;
+        } else {
+            const int u = t - sh, pr = u >> 1;
+            mat = u & 1;
+            i = pr / RT;
+            rt = pr - i * RT;
+        }
         MxTile T = mxmoe_tile(p.c, i, 3 * p.c.ws.c_expert[i] + mat, rt, p.c.hidden >> 7, p.c.ws.sfb1);
         T.id0 = i;
         T.id1 = mat;
@@ -592,6 +613,8 @@ struct MoeDown {
     // the gate/up kernel's last CTAs still run. Table entries are clamped to
     // their bounds.
     static constexpr bool kPrefetchA = true;
+    DSV4CU_DEV static int ntiles_pre(const Params &p) { return ntiles(p); }
+    DSV4CU_DEV static MxTile tile_pre(const Params &p, int t) { return tile(p, t); }
     DSV4CU_DEV static int ntiles(const Params &p)
     {
         return min(p.c.ws.meta[2], p.c.max_tiles) * (p.c.hidden >> 7);
@@ -879,6 +902,7 @@ static int mxmoe_gemms(const dsv4cu_moe *L, const MxMoeShape &s, const MxMoeWs &
     // loop over the tokens stays short.
     c.fuse_swiglu = fused && !rows_mode;
     c.fuse_combine = c.fuse_swiglu && nt <= MXMOE_FUSE_COMBINE_NT;
+    c.shared_first = fused && s.has_shared && s.nt <= s.tpt;
     c.limit = limit;
     c.nt = nt;
     c.topk = topk;

@@ -222,9 +222,9 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     const uint64_t pol_once = l2_evict_first(), pol_shared = l2_evict_normal();
     if constexpr (P::kPrefetchA) {
         if (threadIdx.x == 0) {
-            const int nt0 = P::ntiles(p);
+            const int nt0 = P::ntiles_pre(p);   // tiles whose A side is known before the wait
             for (int t = blockIdx.x; t < nt0 && pre < STAGES; t += gridDim.x) {
-                const MxTile T = P::tile(p, t);
+                const MxTile T = P::tile_pre(p, t);
                 const uint32_t tx = KB * (T.a_tx + C::B_BOX + C::SFA_BOX + C::SFB_BOX);
                 const int nst = T.kc / KB;
                 for (int c = 0; c < nst && pre < STAGES; c++, pre++) {

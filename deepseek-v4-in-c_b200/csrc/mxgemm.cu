@@ -120,6 +120,8 @@ struct DenseMx {
         int cols, blk_r, blk_c, s_cols, fp4;
     };
     static constexpr bool kPrefetchA = true;    // weights and tiles are known at launch
+    DSV4CU_DEV static int ntiles_pre(const Params &p) { return ntiles(p); }
+    DSV4CU_DEV static MxTile tile_pre(const Params &p, int t) { return tile(p, t); }
     DSV4CU_DEV static float final_value(const Params &p, int row, float v)
     {
         if (!isnan(v)) return v;
