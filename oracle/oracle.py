@@ -24,6 +24,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libdsv4ref.so")
 LAYER_SO = os.path.join(HERE, "_ref", "libdsv4layer.so")
+TRUNK_SO = os.path.join(HERE, "_ref", "libdsv4trunk.so")
 # The reference source tree: set by the caller (DSV4_REFERENCE_TREE or build(ref_tree=...));
 # without it only the restatement is built.
 REF_TREE = os.environ.get("DSV4_REFERENCE_TREE")
@@ -442,3 +443,36 @@ class RefLayer:
         h = np.ascontiguousarray(h, np.float32).copy()
         self.lib.lr_layer(self.h, _p(h), pos)
         return h
+
+
+class RefTrunkTensor(C.Structure):
+    """The record trunk_ref.c fills (the reference's DSV4TrunkTensor fields)."""
+    _fields_ = [("slot", C.c_int32), ("dtype", C.c_int32), ("rows", C.c_int32), ("cols", C.c_int32),
+                ("wdt", C.c_int32), ("blk_r", C.c_int32), ("blk_c", C.c_int32),
+                ("off", C.c_int64), ("nbytes", C.c_int64)]
+
+
+def ref_trunk_available(path: str = TRUNK_SO) -> bool:
+    return os.path.exists(path)
+
+
+def ref_trunk_manifest(pack_dir: str, layer: int = -1, path: str = TRUNK_SO):
+    """The reference's own trunk.idx reader (src/50_loader/dsv4_trunk_manifest.c:
+    24-110 behind oracle/trunk_ref.c): None when it rejects the index, else
+    (n_layers, run, records) as tuples, run / records None for layer < 0."""
+    lib = C.CDLL(path)
+    f = lib.ref_trunk_manifest
+    f.restype = C.c_int
+    f.argtypes = [C.c_char_p, C.POINTER(C.c_int), C.c_int, C.POINTER(C.c_int64), C.POINTER(C.c_int),
+                  C.POINTER(RefTrunkTensor), C.c_int]
+    nl, nt = C.c_int(), C.c_int()
+    run = (C.c_int64 * 3)()
+    if f(pack_dir.encode(), C.byref(nl), layer, run, C.byref(nt), None, 0) != 0:
+        return None
+    if layer < 0:
+        return nl.value, None, None
+    arr = (RefTrunkTensor * max(1, nt.value))()
+    f(pack_dir.encode(), C.byref(nl), layer, run, C.byref(nt), arr, nt.value)
+    recs = [(t.slot, t.off, t.nbytes, t.dtype, t.rows, t.cols, t.wdt, t.blk_r, t.blk_c)
+            for t in arr[:nt.value]]
+    return nl.value, tuple(run), recs

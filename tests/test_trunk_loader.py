@@ -87,6 +87,58 @@ def test_manifest_rejects_malformed(tmp_path, edit):
         dsv4cu.trunk_manifest(root)
 
 
+def _ours(root, L):
+    nl, run, recs = dsv4cu.trunk_manifest(root, L)
+    return nl, run, [(r.slot, r.off, r.nbytes, r.dtype, r.rows, r.cols, r.wdt, r.blk_r, r.blk_c) for r in recs]
+
+
+_ref_trunk = pytest.mark.skipif(not __import__("oracle").ref_trunk_available(),
+                                reason="oracle/_ref/libdsv4trunk.so not built (needs the reference tree)")
+
+
+@_ref_trunk
+def test_manifest_matches_reference_reader(tmp_path):
+    """The library's trunk.idx reader against the reference's own
+    (dsv4_trunk_load_manifest, compiled into oracle/_ref): the same layers,
+    runs and records in order, blank lines and an empty layer included."""
+    import oracle
+    root = str(tmp_path)
+    trunkfix.write_trunk(root, 4, empty_layers=(2,), seed=11)
+    assert oracle.ref_trunk_manifest(root)[0] == dsv4cu.trunk_manifest(root)[0] == 4
+    for L in range(4):
+        assert oracle.ref_trunk_manifest(root, L) == _ours(root, L), L
+
+
+@_ref_trunk
+@pytest.mark.parametrize("edit", ["magic", "version", "n_layers", "layout", "layer_index", "tensor_fields",
+                                  "dtype", "wdt", "missing"])
+def test_manifest_rejections_match_reference(tmp_path, edit):
+    """Every malformed index the reference's reader rejects, the library's
+    rejects too. (The library also rejects a tensor lying outside its layer's
+    run, which the reference accepts: its device copy of the run would not
+    hold that tensor.)"""
+    import oracle
+    root = str(tmp_path)
+    trunkfix.write_trunk(root, 2, seed=12)
+    lines = _ix_lines(root)
+    first_slot = next(i for i, s in enumerate(lines) if s.startswith("slot "))
+    f = lines[first_slot].split()
+    edits = {"magic": (0, "DSV4TRUNX 2"), "version": (0, "DSV4TRUNK 1"), "n_layers": (1, "n_layers 0"),
+             "layout": (2, "layout 2"), "layer_index": (3, lines[3].replace("layer 0", "layer 1", 1)),
+             "tensor_fields": (first_slot, " ".join(f[:-1])),
+             "dtype": (first_slot, " ".join(f[:4] + ["9"] + f[5:])),
+             "wdt": (first_slot, " ".join(f[:7] + ["4"] + f[8:]))}
+    if edit == "missing":
+        os.remove(os.path.join(root, "trunk.idx"))
+    else:
+        i, v = edits[edit]
+        lines[i] = v
+        _write_ix(root, lines)
+    assert oracle.ref_trunk_manifest(root) is None
+    with pytest.raises(dsv4cu.DSV4CUError):
+        dsv4cu.trunk_manifest(root)
+
+
 @pytest.mark.gpu
 def test_trunk_upload_slots_and_widen(tmp_path, dev):
     import torch
