@@ -306,7 +306,8 @@ int dsv4cu_moe_decode_host(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out_
 
 /* dsv4cu_moe_decode with CUDA events (cudaEvent_t) recorded around its three
  * launches: events[0] before the router/bucketing prologue, [1] after it,
- * [2] after the w1/w3 + SwiGLU kernel, [3] after the w2 + combine kernel.
+ * [2] after the w1/w3 kernel (SwiGLU in its epilogue), [3] after the w2
+ * kernel (the combine in its epilogue, up to 4 tokens; else a combine kernel).
  * events may be NULL. Used to time each kernel live on the launching stream. */
 int dsv4cu_moe_decode_ev(dsv4cu_ctx *ctx, const dsv4cu_moe *layer, float *out,
                          const float *x, const float *logits, const float *bias,
