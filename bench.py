@@ -1,7 +1,7 @@
 """Benchmark of the hot path. Default: the FP4 MoE layer decode step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload auto|decode|prefill|gemv|indexer|ep]
+                    [--workload auto|decode|prefill|gemv|indexer|ep|stack]
 
 auto (the default): N = 1 runs decode and adds configs 1, 3 and 4 as a
 "secondary" block of the same line; N > 1 runs ep.
