@@ -89,3 +89,31 @@ def test_reference_engine_links_against_the_library(built_lib):
     need = {s for s in und if s.startswith("dsv4_") or s in ("fp8_n", "fp4_n", "bf16_n")}
     lib = ctypes.CDLL(built_lib)
     assert need and all(hasattr(lib, s) for s in need), sorted(need)
+
+
+def test_bf16w_workspace_follows_the_dequantization_path(built_lib):
+    """Host logic only: the exact-weight GEMM's workspace holds the bf16
+    activation rows, plus a bf16 copy of the matrix when the call takes the
+    pre-dequantized path (automatic above 256 token rows, or forced); bad
+    path codes are rejected and the automatic choice is restored."""
+    import sys
+    sys.path.insert(0, PKG)
+    import dsv4cu
+    L = dsv4cu.lib()
+    q = dsv4cu.QMat(None, None, 2, 6144, 4096, 128, 128)
+    ws = lambda nt, terms: L.dsv4cu_gemm_bf16w_workspace(ctypes.byref(q), nt, terms)
+    x_bytes = lambda nt, terms: -(-nt * terms * 4096 * 2 // 256) * 256
+    copy = 6144 * 4096 * 2
+    try:
+        assert L.dsv4cu_gemm_bf16w_set_path(0) == 0
+        assert ws(128, 2) == x_bytes(128, 2)                 # one 256-row token tile: converters
+        assert ws(129, 2) == x_bytes(129, 2) + copy          # more: one bf16 copy per call
+        assert ws(4096, 1) == x_bytes(4096, 1) + copy
+        assert L.dsv4cu_gemm_bf16w_set_path(1) == 0
+        assert ws(4096, 1) == x_bytes(4096, 1)
+        assert L.dsv4cu_gemm_bf16w_set_path(2) == 0
+        assert ws(8, 1) == x_bytes(8, 1) + copy
+        assert L.dsv4cu_gemm_bf16w_set_path(3) != 0
+        assert ws(0, 1) == 0 and ws(8, 3) == 0
+    finally:
+        L.dsv4cu_gemm_bf16w_set_path(0)
